@@ -1,0 +1,206 @@
+/*
+ * libjxb200 -- C ABI of the B200 (sm_100a) decode/prefill path that stands in for jaxml's
+ * JAX/XLA compute.  Every entry point takes plain device pointers, sizes and a cudaStream_t passed as
+ * void*, launches asynchronously on that stream and returns a status code (0 = JX_OK).  Nothing here
+ * allocates device memory: scratch buffers are passed in by the caller.  Device-side failures (index
+ * out of range, a bounded wait that ran out) are reported through an int status word in device
+ * memory that the caller reads after synchronising.
+ *
+ * The reference has no native code: each entry point replaces a piece of the Flax/XLA program named
+ * in its comment (paths relative to the reference's src/jaxml/).
+ */
+#ifndef JXB200_H_
+#define JXB200_H_
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ---- */
+#define JX_OK 0
+#define JX_ERR_ARG 1          /* bad pointer / alignment / workspace size */
+#define JX_ERR_SHAPE 2        /* unsupported or inconsistent sizes */
+#define JX_ERR_DTYPE 3        /* unsupported dtype */
+#define JX_ERR_RANGE 4        /* token id / position / cache slot out of range (device status) */
+#define JX_ERR_TIMEOUT 5      /* a bounded device wait ran out (device status) */
+#define JX_ERR_CUDA 6         /* a CUDA runtime call failed; see jx_last_error() */
+#define JX_ERR_UNSUPPORTED 7
+
+/* ---- enums ---- */
+#define JX_F32 0
+#define JX_BF16 1
+
+#define JX_NORM_NONE 0
+#define JX_NORM_RMS 1         /* nn/norms.py:83-117 */
+#define JX_NORM_GEMMA 2       /* models/gemma3.py:89-106 */
+#define JX_NORM_LAYER 3       /* nn/norms.py:120-168 */
+
+#define JX_EPI_STORE 0            /* out = dtype(acc) (+ bias)                              nn/linear.py:161-182 */
+#define JX_EPI_RESID 1            /* out = dtype(dtype(acc) + res)                          models/llama.py:133,137 */
+#define JX_EPI_GLU_SILU 2         /* out = dtype(silu(gate) * up), K128 output              models/llama.py:82-88 */
+#define JX_EPI_GLU_GELU_TANH 3    /* out = dtype(gelu_tanh(gate) * up), K128 output         models/gemma3.py:80-86 */
+#define JX_EPI_ACT_GELU_ERF 4     /* out = dtype(gelu_erf(acc + b))                         models/gpt_neox.py:75-80 */
+#define JX_EPI_RESID2 5           /* out = dtype(dtype(acc + res2) + res)  (parallel resid.) models/gpt_neox.py:126-129 */
+
+/* Fused epilogue of a projection.  Output column n of a plain output lives at out[m*ldo + n]; a K128
+ * output (out_rp > 0) is the tiled layout described in jx_pack_k128. */
+typedef struct jx_epilogue {
+  int kind;
+  int M;                 /* valid output rows */
+  int N;                 /* valid output columns (GLU: F) */
+  int _pad0;
+  const void* bias;      /* per packed weight row, model dtype, or NULL */
+  void* out;
+  long long ldo;
+  long long out_rp;      /* > 0: K128 output with this row padding */
+  const void* res;       /* RESID/RESID2 residual (may alias out) */
+  long long ldr;
+  const void* res2;      /* RESID2 second addend */
+  long long ldr2;
+} jx_epilogue;
+
+/* Row-wise embedding gather / residual add / normalisation (one launch per call). */
+typedef struct jx_norm_args {
+  int M, d;
+  float eps;
+  int kind;              /* JX_NORM_* of the main norm */
+  int kind_pre;          /* JX_NORM_* applied to `a` before it is added into h (NONE: plain add) */
+  int vocab;
+  const int* ids;        /* embedding ids [M] or NULL */
+  const void* table;     /* embedding table [vocab, d] */
+  float embed_scale;     /* multiply gathered rows by this (0: none) */
+  int _pad0;
+  const int* row_map;    /* read h[row_map[m]] instead of h[m] (no write back) */
+  const void* a;
+  long long lda;
+  void* h;
+  long long ldh;
+  const void* w_pre;
+  const void* b_pre;
+  const void* w;
+  const void* b;
+  void* out;
+  long long ldo, out_rp;
+  const void* w2;
+  const void* b2;
+  void* out2;
+  long long ldo2, out2_rp;
+  int* status;
+} jx_norm_args;
+
+typedef struct jx_qkv_args {
+  int M, S;              /* token rows, tokens per sequence (rows are b*S + s) */
+  int Hq, Hkv, hd, rd;   /* heads, head dim, rotary dim */
+  const void* qkv;       /* [M, (Hq + 2 Hkv) hd] projection output */
+  long long ld_qkv;
+  const void* qn_w;      /* [hd] QK-norm weights (Gemma3) or NULL */
+  const void* kn_w;
+  float eps;
+  int max_pos;           /* rows of the rotary tables */
+  const void* cos;       /* [max_pos, rd] in the model dtype */
+  const void* sin;
+  const int* pos_id;     /* decode: [B] last valid cache slot */
+  int decode;
+  int T;                 /* cache slots */
+  void* q_out;           /* [M, Hq, hd] */
+  void* k_cache;         /* [B, T, Hkv, hd] */
+  void* v_cache;
+  int* status;
+} jx_qkv_args;
+
+typedef struct jx_attn_args {
+  int B, S, Hq, Hkv, hd;
+  int T;                 /* key slots in the cache buffer */
+  const void* q;         /* [B*S, Hq, hd] */
+  const void* k;         /* [B, T, Hkv, hd] */
+  const void* v;
+  const int* len_ptr;    /* [B]: keys j < len_ptr[b] + len_add are valid (prefix mask) */
+  int len_add;
+  int causal;            /* 1 for prefill with S > 1 */
+  int window;            /* sliding window, 0 = none */
+  float scale;           /* attn_scale (rounded to the model dtype inside) */
+  void* out;             /* [B*S, Hq*hd]; K128 when out_rp > 0 */
+  long long ldo, out_rp;
+  int* status;
+} jx_attn_args;
+
+typedef struct jx_sample_args {
+  int B, V;              /* rows, local vocabulary columns */
+  const void* logits;
+  long long ld;
+  int dtype;
+  int greedy;
+  float temp;
+  int chunk;             /* columns per CTA */
+  long long vocab_offset;
+  long long vocab_total;
+  unsigned int* rng;     /* [4] device: key[2], subkey[2] */
+  const float* gumbel_tab; /* [256] bfloat16 Gumbel values (as float) */
+  unsigned long long* ws;  /* [B * ceil(V/chunk)] */
+  unsigned long long* row_best; /* [B] when finalize == 0 */
+  int* counters;         /* [B + 1], zero-initialised once */
+  int finalize;
+  int ld_tok;
+  int* tokens_out;       /* [B, ld_tok], column = *step */
+  int* step;
+  int* next_ids;         /* [B] */
+  int* pos_id;           /* [B] */
+  unsigned char* mask;   /* [B, T_mask] */
+  int T_mask;
+  int update_pos;
+  int advance_rng;
+  int _pad0;
+  int* status;
+} jx_sample_args;
+
+/* ---- library ---- */
+const char* jx_version(void);
+const char* jx_last_error(void);
+int jx_device_sm_count(int* out);
+
+/* ---- layout ----
+ * K128 tiled layout of a [rows, cols] matrix padded to [rp, cp] (rp % 8 == 0, cp % 128 == 0):
+ * element (r, k) at ((k/128)*(rp/8) + r/8)*1024 + ((k%128)/8)*64 + (r%8)*8 + k%8.
+ * Packs the reference's DenseGeneral kernels ([in, out], nn/linear.py:150-157) and activations into the
+ * operand layout of the projection kernels.  transposed = 1 reads src as [cols, rows] (kernel layout). */
+int jx_pack_k128(const void* src, int src_dtype, long long rows, long long cols, long long src_ld, int transposed,
+                 void* dst, long long rp, long long cp, void* stream);
+int jx_unpack_k128(const void* src, long long rows, long long cols, long long rp, void* dst, int dst_dtype,
+                   long long dst_ld, void* stream);
+
+/* ---- compute ---- */
+/* Embed (nn/embedding.py:60-111) + residual add + RMSNorm/LayerNorm (nn/norms.py:83-168, gemma3.py:89-106). */
+int jx_norm(const jx_norm_args* args, int dtype, int pdl, void* stream);
+
+/* Decode projection (M <= 64): DenseGeneral (nn/linear.py:119-182) with fused epilogue.  W and X are
+ * bfloat16 K128 ([Np, Kp] and [16*ceil(M/16) (or 64), Kp]); workspace from jx_linear_decode_workspace. */
+int jx_linear_decode_workspace(int grid, int M, long long* floats_out);
+int jx_linear_decode(const void* W, const void* X, long long Np, long long Kp, int M, const jx_epilogue* epi,
+                     float* ws, long long ws_floats, int* counters, int* status, int grid, int pdl, void* stream);
+
+/* Prefill projection (any M): bfloat16 K128 operands X [Mp, Kp], W [Np, Kp] (Mp, Np multiples of 128). */
+int jx_linear_prefill(const void* X, const void* W, long long Mp, long long Np, long long Kp, const jx_epilogue* epi,
+                      int* status, int pdl, void* stream);
+
+/* float32 projection: X [M, K] (row stride ldx) times the reference's kernel layout W [K, N]. */
+int jx_linear_f32(const float* X, long long ldx, const float* W, int M, int N, int K, const jx_epilogue* epi, int pdl,
+                  void* stream);
+
+/* QK-norm + RoPE (nn/position.py:78-141) + KV-cache append (cache.py:183-243). */
+int jx_qkv_rope_append(const jx_qkv_args* args, int dtype, int pdl, void* stream);
+
+/* Attention.mha (nn/attention.py:321-400) on the cache, any head size (CUDA cores). */
+int jx_attention(const jx_attn_args* args, int dtype, int pdl, void* stream);
+
+/* greedy_fn / categorical sampling (inference_engine/sampling.py:75-188) + end-of-step bookkeeping. */
+int jx_sample(const jx_sample_args* args, int pdl, void* stream);
+int jx_sample_finalize(const jx_sample_args* args, const unsigned long long* gathered, int n_shards, void* stream);
+
+/* Clear the split-K counters after an error (they are self-resetting otherwise). */
+int jx_memset_async(void* ptr, int value, long long bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* JXB200_H_ */

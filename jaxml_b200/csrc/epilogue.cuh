@@ -1,0 +1,75 @@
+// Fused GEMM epilogues shared by the decode GEMV, the prefill GEMM and the float32 GEMM.
+//
+// A finished output tile arrives as float32 accumulators indexed by (row m, packed weight row n).
+// Each epilogue reproduces the reference's rounding points: the projection result is rounded to the
+// model dtype before the bias / residual / activation ops, each of which rounds again
+// (nn/linear.py:161-182 for the bias, models/llama.py:133-137 for the residual adds,
+// models/llama.py:82-88 / gemma3.py:80-86 / gpt_neox.py:75-80 for the activations).
+#pragma once
+#include "common.cuh"
+
+namespace jxb {
+
+typedef jx_epilogue EpiParams;
+
+template <typename T>
+__device__ __forceinline__ float bias_at(const EpiParams& e, long long n) {
+  return e.bias ? to_f(reinterpret_cast<const T*>(e.bias)[n]) : 0.0f;
+}
+
+// tile(m, j) for m in [0, rows), j in [0, cols); n0 = packed weight row of column 0 (a multiple of 64).
+template <typename T, typename TileFn>
+__device__ __forceinline__ void run_epilogue(const EpiParams& e, long long m0, int rows, long long n0, int cols,
+                                             TileFn tile, int tid, int nthreads) {
+  if (e.kind == JX_EPI_GLU_SILU || e.kind == JX_EPI_GLU_GELU_TANH) {
+    // Packed weight rows come in groups of 64: 32 gate rows, then the 32 up rows of the same columns.
+    const int half = cols >> 1;
+    for (int idx = tid; idx < rows * half; idx += nthreads) {
+      const int m = idx / half, jj = idx - m * half;
+      const int grp = jj >> 5, j = jj & 31;
+      const long long row = m0 + m;
+      const long long ng = n0 + grp * 64 + j;
+      const long long col = ((n0 >> 6) + grp) * 32 + j;
+      if (row >= e.M || col >= e.N) continue;
+      const float g = rnd<T>(rnd<T>(tile(m, grp * 64 + j)) + bias_at<T>(e, ng));
+      const float u = rnd<T>(rnd<T>(tile(m, grp * 64 + 32 + j)) + bias_at<T>(e, ng + 32));
+      const float a = rnd<T>(e.kind == JX_EPI_GLU_SILU ? silu_f(g) : gelu_tanh_f(g));
+      const long long o = e.out_rp > 0 ? k128_offset(row, col, e.out_rp) : row * e.ldo + col;
+      reinterpret_cast<T*>(e.out)[o] = from_f<T>(a * u);
+    }
+    return;
+  }
+  for (int idx = tid; idx < rows * cols; idx += nthreads) {
+    const int m = idx / cols, j = idx - m * cols;
+    const long long row = m0 + m, n = n0 + j;
+    if (row >= e.M || n >= e.N) continue;
+    float v = rnd<T>(tile(m, j));
+    if (e.bias) v = rnd<T>(v + bias_at<T>(e, n));
+    switch (e.kind) {
+      case JX_EPI_STORE:
+        reinterpret_cast<T*>(e.out)[row * e.ldo + n] = from_f<T>(v);
+        break;
+      case JX_EPI_RESID: {
+        const float r = to_f(reinterpret_cast<const T*>(e.res)[row * e.ldr + n]);
+        reinterpret_cast<T*>(e.out)[row * e.ldo + n] = from_f<T>(v + r);
+        break;
+      }
+      case JX_EPI_RESID2: {
+        const float r2 = to_f(reinterpret_cast<const T*>(e.res2)[row * e.ldr2 + n]);
+        const float r = to_f(reinterpret_cast<const T*>(e.res)[row * e.ldr + n]);
+        reinterpret_cast<T*>(e.out)[row * e.ldo + n] = from_f<T>(rnd<T>(v + r2) + r);
+        break;
+      }
+      case JX_EPI_ACT_GELU_ERF:
+        if (e.out_rp > 0)
+          reinterpret_cast<T*>(e.out)[k128_offset(row, n, e.out_rp)] = from_f<T>(gelu_erf_f(v));
+        else
+          reinterpret_cast<T*>(e.out)[row * e.ldo + n] = from_f<T>(gelu_erf_f(v));
+        break;
+      default:
+        break;
+    }
+  }
+}
+
+}  // namespace jxb

@@ -1,0 +1,276 @@
+// Decode projection kernel: Y[M, N] = X[M, K] . W[N, K]^T for M <= 64 (one decode step of B <= 64
+// sequences), bfloat16 operands in the K128 tiled layout, float32 accumulation.
+//
+// At decode batch sizes the projection is a weight stream: every weight byte is read once from HBM
+// and used M times.  The kernel is persistent (one CTA per SM) and splits the flat iteration space
+// (64-row weight block x 128-wide K chunk) evenly across CTAs ("stream-K"), so every SM streams the
+// same number of bytes whatever N and K are.  A producer warp feeds a ring of shared-memory stages
+// with 1-D TMA bulk copies (16 KB of weights + the matching activation chunk per stage); four consumer
+// warps each own 16 of the 64 rows and run mma.sync m16n8k16 over the stage.  A weight block that is
+// split across CTAs is finished by whichever CTA arrives last: the partial tiles are summed in CTA
+// order (deterministic) and the fused epilogue runs once.
+#include "common.cuh"
+#include "epilogue.cuh"
+
+namespace jxb {
+
+constexpr int kGemvThreads = 160;   // warp 0: producer, warps 1..4: consumers
+constexpr int kGemvBN = 64;
+constexpr int kGemvBK = 128;
+constexpr int kTileLd = 68;         // padded float32 row stride of the staging tile
+
+template <int MT>
+struct GemvCfg {
+  static constexpr int kStages = MT == 1 ? 8 : (MT == 2 ? 6 : 4);
+  static constexpr int kWBytes = kGemvBN * kGemvBK * 2;   // 16 KB
+  static constexpr int kXBytes = MT * 16 * kGemvBK * 2;   // 4 KB per m16 tile
+  static constexpr int kStageBytes = kWBytes + kXBytes;
+  static constexpr int kTileBytes = MT * 16 * kTileLd * 4;
+  static constexpr int kSmem = kStages * kStageBytes + kTileBytes + 2 * kStages * 8 + 16;
+};
+
+__device__ __forceinline__ long long it_begin(long long total, int G, int c) { return total * c / G; }
+__device__ __forceinline__ int cta_of(long long it, long long total, int G) {
+  return (int)(((it + 1) * G + total - 1) / total) - 1;
+}
+
+template <int MT>
+__global__ void __launch_bounds__(kGemvThreads, 1)
+    gemv_k128_kernel(const bf16* __restrict__ W, const bf16* __restrict__ X, long long Np, long long Kp,
+                     EpiParams e, float* __restrict__ ws, int* __restrict__ counters, int* status) {
+  using C = GemvCfg<MT>;
+  extern __shared__ __align__(128) uint8_t smem[];
+  float* tile = reinterpret_cast<float*>(smem + C::kStages * C::kStageBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes + C::kTileBytes);
+  uint64_t* empty = full + C::kStages;
+  volatile int* sh = reinterpret_cast<volatile int*>(empty + C::kStages);  // [0]: dead flag, [1]: last-arriver flag
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_blocks = (int)(Np / kGemvBN), kc = (int)(Kp / kGemvBK);
+  const long long total = (long long)n_blocks * kc;
+  const int G = gridDim.x, c = blockIdx.x;
+  const long long it0 = it_begin(total, G, c), it1 = it_begin(total, G, c + 1);
+  const int n_it = (int)(it1 - it0);
+  const long long Mp = MT * 16;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 4);
+    }
+    sh[0] = 0;
+    sh[1] = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  pdl_trigger();
+
+  if (warp == 0) {
+    // ---------------- producer ----------------
+    if (lane == 0 && n_it > 0) {
+      const int pre = n_it < C::kStages ? n_it : C::kStages;
+      auto wsrc = [&](long long it) {
+        const long long nb = it / kc, kk = it - nb * kc;
+        return W + ((kk * (Np >> 3) + nb * 8) << 10);
+      };
+      auto xsrc = [&](long long it) {
+        const long long kk = it % kc;
+        return X + ((kk * (Mp >> 3)) << 10);
+      };
+      // Weights do not depend on the previous kernel: start streaming them before waiting on it.
+      for (int i = 0; i < pre; ++i) {
+        mbar_arrive_expect_tx(&full[i], C::kStageBytes);
+        bulk_g2s(smem + i * C::kStageBytes, wsrc(it0 + i), C::kWBytes, &full[i]);
+      }
+      pdl_wait();
+      for (int i = 0; i < pre; ++i)
+        bulk_g2s(smem + i * C::kStageBytes + C::kWBytes, xsrc(it0 + i), C::kXBytes, &full[i]);
+      int issued = pre;
+      for (int i = pre; i < n_it; ++i) {
+        const int s = i % C::kStages;
+        const uint32_t round = i / C::kStages;
+        if (!mbar_wait_bounded(&empty[s], (round - 1) & 1)) {
+          set_status(status, JX_ERR_TIMEOUT);
+          sh[0] = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(&full[s], C::kStageBytes);
+        bulk_g2s(smem + s * C::kStageBytes, wsrc(it0 + i), C::kWBytes, &full[s]);
+        bulk_g2s(smem + s * C::kStageBytes + C::kWBytes, xsrc(it0 + i), C::kXBytes, &full[s]);
+        issued = i + 1;
+      }
+      // Drain: every issued copy must land before this CTA's shared memory is released.
+      for (int i = (issued > C::kStages ? issued - C::kStages : 0); i < issued; ++i) {
+        const int s = i % C::kStages;
+        if (!mbar_wait_bounded(&full[s], (i / C::kStages) & 1)) {
+          set_status(status, JX_ERR_TIMEOUT);
+          break;
+        }
+      }
+    }
+    return;
+  }
+
+  // ---------------- consumers ----------------
+  pdl_wait();
+  const int cw = warp - 1;             // owns weight rows [cw*16, cw*16+16) of each 64-row block
+  const int tid = threadIdx.x - 32;    // 0..127
+  float acc[MT][2][4];
+  bool dead = false;
+
+  long long cur_nb = -1;
+  bool started_at_zero = false;
+
+  for (int i = 0; i < n_it; ++i) {
+    const long long it = it0 + i;
+    const long long nb = it / kc, kk = it - nb * kc;
+    if (nb != cur_nb) {
+      cur_nb = nb;
+      started_at_zero = (kk == 0);
+#pragma unroll
+      for (int a = 0; a < MT; ++a)
+#pragma unroll
+        for (int b = 0; b < 2; ++b)
+#pragma unroll
+          for (int q = 0; q < 4; ++q) acc[a][b][q] = 0.f;
+    }
+    const int s = i % C::kStages;
+    if (!dead) {
+      if (sh[0] || !mbar_wait_bounded(&full[s], (i / C::kStages) & 1)) {
+        dead = true;
+        sh[0] = 1;
+        set_status(status, JX_ERR_TIMEOUT);
+      }
+    }
+    if (!dead) {
+      const uint32_t sW = smem_u32(smem + s * C::kStageBytes);
+      const uint32_t sX = sW + C::kWBytes;
+      const int mi = lane >> 3, r8 = lane & 7;
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        uint32_t b0, b1, b2, b3;
+        {
+          const int rg = cw * 2 + (mi >> 1), kcore = ks * 2 + (mi & 1);
+          ldsm_x4(sW + (uint32_t)((rg * 1024 + kcore * 64 + r8 * 8) * 2), b0, b1, b2, b3);
+        }
+#pragma unroll
+        for (int mt = 0; mt < MT; ++mt) {
+          uint32_t a0, a1, a2, a3;
+          const int rg = mt * 2 + (mi & 1), kcore = ks * 2 + (mi >> 1);
+          ldsm_x4(sX + (uint32_t)((rg * 1024 + kcore * 64 + r8 * 8) * 2), a0, a1, a2, a3);
+          mma_bf16(acc[mt][0], a0, a1, a2, a3, b0, b1);
+          mma_bf16(acc[mt][1], a0, a1, a2, a3, b2, b3);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+
+    const bool block_end = (kk == kc - 1) || (i == n_it - 1);
+    if (!block_end) continue;
+
+    // ---- this CTA's share of weight block nb is done: stage the tile in shared memory ----
+#pragma unroll
+    for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        const int r = mt * 16 + (lane >> 2);
+        const int col = cw * 16 + nt * 8 + (lane & 3) * 2;
+        tile[r * kTileLd + col] = acc[mt][nt][0];
+        tile[r * kTileLd + col + 1] = acc[mt][nt][1];
+        tile[(r + 8) * kTileLd + col] = acc[mt][nt][2];
+        tile[(r + 8) * kTileLd + col + 1] = acc[mt][nt][3];
+      }
+    named_bar_sync(1, 128);
+
+    const bool whole = started_at_zero && (kk == kc - 1);
+    bool do_epi = whole;
+    if (!whole) {
+      const long long blk_first_it = nb * kc, blk_last_it = nb * kc + kc - 1;
+      const int c_first = cta_of(blk_first_it, total, G), c_last = cta_of(blk_last_it, total, G);
+      auto slot_of = [&](int cc) {
+        const int nbf = (int)(it_begin(total, G, cc) / kc);
+        return cc * 2 + (nb == nbf ? 0 : 1);
+      };
+      float* my = ws + (long long)slot_of(c) * Mp * kGemvBN;
+      for (int idx = tid; idx < Mp * kGemvBN; idx += 128) my[idx] = tile[(idx >> 6) * kTileLd + (idx & 63)];
+      __threadfence();
+      named_bar_sync(1, 128);
+      if (tid == 0) {
+        const int prev = atomicAdd(&counters[nb], 1);
+        sh[1] = (prev == c_last - c_first) ? 1 : 0;
+      }
+      named_bar_sync(1, 128);
+      do_epi = sh[1] != 0;
+      if (do_epi) {
+        __threadfence();
+        for (int idx = tid; idx < Mp * kGemvBN; idx += 128) {
+          float sum = 0.f;
+          for (int cc = c_first; cc <= c_last; ++cc) {
+            float v;
+            if (cc == c) {
+              v = tile[(idx >> 6) * kTileLd + (idx & 63)];
+            } else {
+              v = __ldcg(ws + (long long)slot_of(cc) * Mp * kGemvBN + idx);
+            }
+            sum = (cc == c_first) ? v : sum + v;
+          }
+          tile[(idx >> 6) * kTileLd + (idx & 63)] = sum;
+        }
+        if (tid == 0) counters[nb] = 0;
+        named_bar_sync(1, 128);
+      }
+    }
+    if (do_epi && !dead) {
+      run_epilogue<bf16>(e, 0, (int)Mp, nb * kGemvBN, kGemvBN,
+                         [&](int m, int j) { return tile[m * kTileLd + j]; }, tid, 128);
+    }
+    named_bar_sync(1, 128);
+  }
+}
+
+template <int MT>
+static int launch_gemv(const bf16* W, const bf16* X, long long Np, long long Kp, const EpiParams& e, float* ws,
+                       int* counters, int* status, int grid, bool pdl, cudaStream_t stream) {
+  using C = GemvCfg<MT>;
+  static bool configured = false;
+  if (!configured) {
+    if (cudaFuncSetAttribute(gemv_k128_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) !=
+        cudaSuccess)
+      return JX_ERR_CUDA;
+    configured = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kGemvThreads);
+  cfg.dynamicSmemBytes = C::kSmem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cudaError_t err = cudaLaunchKernelEx(&cfg, gemv_k128_kernel<MT>, W, X, Np, Kp, e, ws, counters, status);
+  return err == cudaSuccess ? JX_OK : JX_ERR_CUDA;
+}
+
+int gemv_workspace_floats(int grid, int mt) { return grid * 2 * mt * 16 * kGemvBN; }
+
+int run_gemv(const bf16* W, const bf16* X, long long Np, long long Kp, int M, const EpiParams& e, float* ws,
+             long long ws_floats, int* counters, int* status, int grid, bool pdl, cudaStream_t stream) {
+  if (M <= 0 || M > 64) return JX_ERR_SHAPE;
+  if (Np % kGemvBN || Kp % kGemvBK || Np <= 0 || Kp <= 0) return JX_ERR_SHAPE;
+  const int mt = M <= 16 ? 1 : (M <= 32 ? 2 : 4);
+  const long long total = (Np / kGemvBN) * (Kp / kGemvBK);
+  if (grid <= 0) grid = 148;
+  if (grid > total) grid = (int)total;
+  if ((long long)gemv_workspace_floats(grid, mt) > ws_floats) return JX_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(W) | reinterpret_cast<uintptr_t>(X)) & 15) return JX_ERR_ARG;
+  switch (mt) {
+    case 1: return launch_gemv<1>(W, X, Np, Kp, e, ws, counters, status, grid, pdl, stream);
+    case 2: return launch_gemv<2>(W, X, Np, Kp, e, ws, counters, status, grid, pdl, stream);
+    default: return launch_gemv<4>(W, X, Np, Kp, e, ws, counters, status, grid, pdl, stream);
+  }
+}
+
+}  // namespace jxb

@@ -1,0 +1,178 @@
+// Fused embedding / residual-add / normalisation kernel (one CTA per token row).
+//
+// Per row m it can, in order:
+//   1. gather the embedding row of ids[m] (ids < 0 read row 0, models/llama.py:188) and scale it by the
+//      bfloat16-rounded sqrt(d) for Gemma3 (gemma3.py:245);
+//   2. add a second input into the residual stream h, optionally normalising that input first
+//      (Gemma3's post-attention / post-feedforward norms, gemma3.py:166-173) and store h back;
+//   3. normalise h with RMSNorm (norms.py:110-117), Gemma RMSNorm (gemma3.py:94-106) or LayerNorm
+//      (norms.py:157-168) into one or two outputs (two for GPT-NeoX's parallel residual, which feeds
+//      ln1(h) to attention and ln2(h) to the MLP).  bfloat16 outputs can be written in the K128 tiled
+//      layout that the projection kernels read.
+#include "common.cuh"
+
+namespace jxb {
+
+typedef jx_norm_args NormArgs;
+
+template <int NT>
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = 0.f;
+  if (threadIdx.x < 32) {
+    t = threadIdx.x < NT / 32 ? red[threadIdx.x] : 0.f;
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (threadIdx.x == 0) red[NT / 32] = t;
+  }
+  __syncthreads();
+  return red[NT / 32];
+}
+
+// Normalise x (float32 copy of a row of model-dtype values, in shared memory) in place into y (float
+// values already rounded to T).
+template <typename T, int NT>
+__device__ void normalize_row(const float* x, float* y, int d, int kind, float eps, const T* w, const T* b,
+                              float* red) {
+  if (kind == JX_NORM_LAYER) {
+    float s = 0.f;
+    for (int j = threadIdx.x; j < d; j += NT) s += x[j];
+    const float mean = block_sum<NT>(s, red) / (float)d;
+    float v = 0.f;
+    for (int j = threadIdx.x; j < d; j += NT) {
+      const float t = x[j] - mean;
+      v += t * t;
+    }
+    const float var = block_sum<NT>(v, red) / (float)d;
+    const float den = sqrtf(var + eps);
+    for (int j = threadIdx.x; j < d; j += NT) {
+      float o = (x[j] - mean) / den * to_f(w[j]);
+      if (b) o += to_f(b[j]);
+      y[j] = rnd<T>(o);
+    }
+    return;
+  }
+  float s = 0.f;
+  for (int j = threadIdx.x; j < d; j += NT) s += x[j] * x[j];
+  const float ms = block_sum<NT>(s, red) / (float)d;
+  const float den = sqrtf(ms + eps);
+  if (kind == JX_NORM_RMS) {
+    for (int j = threadIdx.x; j < d; j += NT) y[j] = rnd<T>(to_f(w[j]) * rnd<T>(x[j] / den));
+  } else {  // JX_NORM_GEMMA
+    const float inv = 1.0f / den;
+    for (int j = threadIdx.x; j < d; j += NT) y[j] = rnd<T>((to_f(w[j]) + 1.0f) * (x[j] * inv));
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void store_row(const float* y, int d, long long m, void* out, long long ldo,
+                                          long long out_rp, int NT) {
+  T* o = reinterpret_cast<T*>(out);
+  for (int j = threadIdx.x; j < d; j += NT) {
+    const long long off = out_rp > 0 ? k128_offset(m, j, out_rp) : m * ldo + j;
+    o[off] = from_f<T>(y[j]);
+  }
+}
+
+template <typename T, int NT>
+__global__ void __launch_bounds__(NT) norm_kernel(NormArgs p) {
+  extern __shared__ float sm[];
+  float* x = sm;            // [d]
+  float* y = sm + p.d;      // [d]
+  float* red = sm + 2 * p.d;  // [NT/32 + 1]
+  const long long m = blockIdx.x;
+  const int d = p.d;
+  pdl_wait();
+  pdl_trigger();
+  T* h = reinterpret_cast<T*>(p.h);
+
+  if (p.ids) {
+    int id = p.ids[m];
+    if (id < 0) id = 0;
+    if (id >= p.vocab) {
+      set_status(p.status, JX_ERR_RANGE);
+      id = 0;
+    }
+    const T* row = reinterpret_cast<const T*>(p.table) + (long long)id * d;
+    const float sc = p.embed_scale;
+    for (int j = threadIdx.x; j < d; j += NT) {
+      float v = to_f(row[j]);
+      if (sc != 0.f) v = rnd<T>(v * sc);
+      x[j] = v;
+      h[m * p.ldh + j] = from_f<T>(v);
+    }
+    __syncthreads();
+  } else {
+    const long long src = p.row_map ? (long long)p.row_map[m] : m;
+    for (int j = threadIdx.x; j < d; j += NT) x[j] = to_f(h[src * p.ldh + j]);
+    __syncthreads();
+  }
+
+  if (p.a) {
+    const T* a = reinterpret_cast<const T*>(p.a);
+    if (p.kind_pre != JX_NORM_NONE) {
+      for (int j = threadIdx.x; j < d; j += NT) y[j] = to_f(a[m * p.lda + j]);
+      __syncthreads();
+      // normalise y in place: copy to a temp in the output half first
+      float* t = y;
+      normalize_row<T, NT>(t, t, d, p.kind_pre, p.eps, reinterpret_cast<const T*>(p.w_pre),
+                           reinterpret_cast<const T*>(p.b_pre), red);
+      __syncthreads();
+      for (int j = threadIdx.x; j < d; j += NT) x[j] = rnd<T>(x[j] + t[j]);
+    } else {
+      for (int j = threadIdx.x; j < d; j += NT) x[j] = rnd<T>(x[j] + to_f(a[m * p.lda + j]));
+    }
+    __syncthreads();
+    for (int j = threadIdx.x; j < d; j += NT) h[m * p.ldh + j] = from_f<T>(x[j]);
+    __syncthreads();
+  }
+
+  if (p.out) {
+    normalize_row<T, NT>(x, y, d, p.kind, p.eps, reinterpret_cast<const T*>(p.w), reinterpret_cast<const T*>(p.b),
+                         red);
+    __syncthreads();
+    store_row<T>(y, d, m, p.out, p.ldo, p.out_rp, NT);
+    __syncthreads();
+  }
+  if (p.out2) {
+    normalize_row<T, NT>(x, y, d, p.kind, p.eps, reinterpret_cast<const T*>(p.w2),
+                         reinterpret_cast<const T*>(p.b2), red);
+    __syncthreads();
+    store_row<T>(y, d, m, p.out2, p.ldo2, p.out2_rp, NT);
+  }
+}
+
+int run_norm(int dtype, const NormArgs& p, bool pdl, cudaStream_t stream) {
+  if (p.M <= 0 || p.d <= 0) return JX_ERR_SHAPE;
+  constexpr int NT = 256;
+  const size_t smem = (size_t)(2 * p.d + NT / 32 + 1) * sizeof(float);
+  if (smem > 200 * 1024) return JX_ERR_SHAPE;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.M);
+  cfg.blockDim = dim3(NT);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cudaError_t err;
+  if (dtype == JX_BF16) {
+    if (smem > 48 * 1024)
+      cudaFuncSetAttribute(norm_kernel<bf16, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    err = cudaLaunchKernelEx(&cfg, norm_kernel<bf16, NT>, p);
+  } else if (dtype == JX_F32) {
+    if (smem > 48 * 1024)
+      cudaFuncSetAttribute(norm_kernel<float, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    err = cudaLaunchKernelEx(&cfg, norm_kernel<float, NT>, p);
+  } else {
+    return JX_ERR_DTYPE;
+  }
+  return err == cudaSuccess ? JX_OK : JX_ERR_CUDA;
+}
+
+}  // namespace jxb

@@ -1,0 +1,99 @@
+// Attention prologue after the fused QKV projection: optional per-head QK RMSNorm (Gemma3,
+// nn/attention.py:274-276 with gemma3.py:89-106), rotary embedding on the first rotary_dim dims
+// (nn/position.py:78-141, half-split "rotate_half" form, applied in the model dtype), and the KV-cache
+// append (cache.py:183-243): k and v of token row m are written into the cache slot of that token.
+//
+// Positions: in prefill (decode == 0) row m = b*S + s sits at position s and cache slot s; in decode
+// (S == 1) row b sits at pos_id[b] + 1, the slot after the last valid one.
+#include "common.cuh"
+
+namespace jxb {
+
+typedef jx_qkv_args QkvArgs;
+
+template <typename T>
+__global__ void __launch_bounds__(256) qkv_rope_append_kernel(QkvArgs p) {
+  extern __shared__ float buf[];  // [8 warps][hd]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* v = buf + warp * p.hd;
+  const long long m = blockIdx.x;
+  pdl_wait();
+  pdl_trigger();
+  const int b = (int)(m / p.S), s = (int)(m % p.S);
+  int pos = s;
+  if (p.decode) pos = p.pos_id[b] + 1;
+  if (pos < 0 || pos >= p.max_pos || pos >= p.T) {
+    set_status(p.status, JX_ERR_RANGE);
+    return;
+  }
+  const T* row = reinterpret_cast<const T*>(p.qkv) + m * p.ld_qkv;
+  const T* cos = reinterpret_cast<const T*>(p.cos) + (long long)pos * p.rd;
+  const T* sin = reinterpret_cast<const T*>(p.sin) + (long long)pos * p.rd;
+  const int n_heads = p.Hq + 2 * p.Hkv;
+  const int half = p.rd >> 1;
+  for (int head = warp; head < n_heads; head += 8) {
+    const bool is_q = head < p.Hq, is_k = !is_q && head < p.Hq + p.Hkv;
+    const T* src = row + (long long)head * p.hd;
+    for (int j = lane; j < p.hd; j += 32) v[j] = to_f(src[j]);
+    __syncwarp();
+    const T* nw = is_q ? reinterpret_cast<const T*>(p.qn_w) : (is_k ? reinterpret_cast<const T*>(p.kn_w) : nullptr);
+    if (nw) {
+      float ss = 0.f;
+      for (int j = lane; j < p.hd; j += 32) ss += v[j] * v[j];
+      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      const float inv = 1.0f / sqrtf(ss / (float)p.hd + p.eps);
+      __syncwarp();
+      for (int j = lane; j < p.hd; j += 32) v[j] = rnd<T>((to_f(nw[j]) + 1.0f) * (v[j] * inv));
+      __syncwarp();
+    }
+    float outv[8];
+    int cnt = 0;
+    for (int j = lane; j < p.hd; j += 32, ++cnt) {
+      float o = v[j];
+      if ((is_q || is_k) && j < p.rd) {
+        const float rot = j < half ? -v[j + half] : v[j - half];
+        const float a = rnd<T>(v[j] * to_f(cos[j]));
+        const float c = rnd<T>(rot * to_f(sin[j]));
+        o = rnd<T>(a + c);
+      }
+      outv[cnt] = o;
+    }
+    __syncwarp();
+    cnt = 0;
+    for (int j = lane; j < p.hd; j += 32, ++cnt) {
+      if (is_q) {
+        reinterpret_cast<T*>(p.q_out)[(m * p.Hq + head) * p.hd + j] = from_f<T>(outv[cnt]);
+      } else {
+        const int kvh = is_k ? head - p.Hq : head - p.Hq - p.Hkv;
+        T* cache = reinterpret_cast<T*>(is_k ? p.k_cache : p.v_cache);
+        cache[(((long long)b * p.T + pos) * p.Hkv + kvh) * p.hd + j] = from_f<T>(outv[cnt]);
+      }
+    }
+    __syncwarp();
+  }
+}
+
+int run_qkv_rope_append(int dtype, const QkvArgs& p, bool pdl, cudaStream_t stream) {
+  if (p.M <= 0 || p.S <= 0 || p.hd <= 0 || p.hd > 256 || p.rd < 0 || p.rd > p.hd || (p.rd & 1)) return JX_ERR_SHAPE;
+  if (p.decode && p.S != 1) return JX_ERR_SHAPE;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.M);
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = 8 * p.hd * sizeof(float);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cudaError_t err;
+  if (dtype == JX_BF16)
+    err = cudaLaunchKernelEx(&cfg, qkv_rope_append_kernel<bf16>, p);
+  else if (dtype == JX_F32)
+    err = cudaLaunchKernelEx(&cfg, qkv_rope_append_kernel<float>, p);
+  else
+    return JX_ERR_DTYPE;
+  return err == cudaSuccess ? JX_OK : JX_ERR_CUDA;
+}
+
+}  // namespace jxb
