@@ -1,0 +1,248 @@
+"""``InferenceConfig`` and ``Engine``: the reference's generation entry point (inference_engine/engine.py).
+
+Argument checks and error messages follow ``engine.py:59-610`` and ``_generate.py:218-330``.  The
+difference is where the work runs: ``init_params`` packs the parameter tree into the GPU layout of this
+process's tensor-parallel rank, and ``generate`` runs prefill + decode on the GPU (CUDA-graph replay per
+token) instead of jit-compiled XLA programs.  One process drives one GPU; with ``tp_size > 1`` the
+processes of a ``torch.distributed`` group (NCCL) each hold 1/tp of the heads, FFN columns and
+vocabulary.  ``dp_size`` replicas are independent process groups (no cross-replica traffic in
+inference), so each Engine instance serves the batch it is given.
+"""
+from __future__ import annotations
+
+import logging
+import os
+from collections.abc import Mapping
+from dataclasses import dataclass
+from typing import Any, Optional
+
+import numpy as np
+import torch
+
+from ._checks import normalize_bool, normalize_count, normalize_dtype
+from .models import _DecoderWithHead
+from .sampling import SamplingMethod, normalize_sampling_params
+
+logger = logging.getLogger(__name__)
+
+
+@dataclass(frozen=True)
+class InferenceConfig:
+    tp_size: int = 1
+    dp_size: int = 1
+
+    def __post_init__(self):
+        tp = normalize_count("tp_size", self.tp_size)
+        dp = normalize_count("dp_size", self.dp_size)
+        object.__setattr__(self, "tp_size", tp)
+        object.__setattr__(self, "dp_size", dp)
+        if tp <= 0:
+            raise ValueError(f"tp_size must be positive, got {tp}.")
+        if dp <= 0:
+            raise ValueError(f"dp_size must be positive, got {dp}.")
+
+
+class TPComm:
+    """Collectives of one tensor-parallel group over NCCL (torch.distributed)."""
+
+    def __init__(self, group=None):
+        import torch.distributed as dist
+
+        self.dist = dist
+        self.group = group
+        self.size = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self._gather = None
+
+    def all_reduce(self, t: torch.Tensor):
+        self.dist.all_reduce(t, group=self.group)
+
+    def all_gather_keys(self, keys: torch.Tensor) -> torch.Tensor:
+        if self._gather is None or self._gather.shape[1] != keys.numel():
+            self._gather = torch.empty(self.size, keys.numel(), dtype=keys.dtype, device=keys.device)
+        self.dist.all_gather_into_tensor(self._gather, keys, group=self.group)
+        return self._gather
+
+
+def _device_count() -> int:
+    import torch.distributed as dist
+
+    if dist.is_available() and dist.is_initialized():
+        return dist.get_world_size()
+    return max(torch.cuda.device_count(), 1)
+
+
+class Engine:
+    """Wraps a model class for autoregressive generation on the GPU."""
+
+    def __init__(self, model, config: InferenceConfig, params, dtype: Any = torch.float32, cache_stride: int = 256):
+        if not isinstance(config, InferenceConfig):
+            raise TypeError(f"config must be an InferenceConfig, got {type(config)}.")
+        dtype = normalize_dtype("dtype", dtype)
+        cache_stride = normalize_count("cache_stride", cache_stride)
+        if cache_stride <= 0:
+            raise ValueError(f"cache_stride must be positive, got {cache_stride}.")
+        required = config.tp_size * config.dp_size
+        available = _device_count()
+        if required > available:
+            raise ValueError(
+                f"InferenceConfig requires {required} devices "
+                f"(tp_size={config.tp_size}, dp_size={config.dp_size}), but only {available} are available."
+            )
+        self.model = model
+        self.config = config
+        self.params = params
+        self.dtype = dtype
+        self.cache_stride = cache_stride
+        self._weights = None
+        self._runtime = None
+        self._comm = None
+
+    # -- parameters ------------------------------------------------------------------------------------
+    @staticmethod
+    def _validate_param_weights(weights):
+        if not isinstance(weights, Mapping):
+            raise TypeError(f"weights must be a mapping, got {type(weights)}.")
+        if "params" not in weights:
+            raise ValueError(f"The key 'params' was not found in weights. Got keys: {weights.keys()}.")
+        if not isinstance(weights["params"], Mapping):
+            raise TypeError(f"weights['params'] must be a mapping, got {type(weights['params'])}.")
+
+    def _device(self) -> torch.device:
+        idx = int(os.environ.get("LOCAL_RANK", torch.cuda.current_device() if torch.cuda.is_available() else 0))
+        return torch.device("cuda", idx)
+
+    def init_params(self, weights=None, use_tpu: bool = False, reinit_weight: bool = False, tp_group=None):
+        """Packs the parameters for this process's GPU (and tensor-parallel rank).
+
+        ``use_tpu`` is accepted for signature compatibility and has no effect: the packed weights always go
+        to the GPU of this process.  ``reinit_weight=True`` draws a fresh random tree first.
+        """
+        normalize_bool("use_tpu", use_tpu)
+        reinit_weight = normalize_bool("reinit_weight", reinit_weight)
+        if reinit_weight:
+            weights = self.model.init(0)
+        if weights is None:
+            weights = self.params
+        self._validate_param_weights(weights)
+        from .runtime import ModelWeights
+
+        tp = self.config.tp_size
+        rank = 0
+        if tp > 1:
+            import torch.distributed as dist
+
+            if not (dist.is_available() and dist.is_initialized()):
+                raise RuntimeError("tp_size > 1 needs torch.distributed initialised (one process per GPU).")
+            self._comm = TPComm(tp_group)
+            if self._comm.size != tp:
+                raise ValueError(f"tensor-parallel group has {self._comm.size} ranks, expected tp_size={tp}.")
+            rank = self._comm.rank
+        if not isinstance(self.model, _DecoderWithHead):
+            raise TypeError(f"model must be one of the *ModelWithHead classes, got {type(self.model)}.")
+        self.params = weights
+        self._weights = ModelWeights(self.model.family, self.model.config, weights, self.model.dtype,
+                                     self._device(), tp_rank=rank, tp_size=tp)
+        self._runtime = None
+
+    # -- inputs ----------------------------------------------------------------------------------------
+    @staticmethod
+    def _as_int_tensor(x, name: str) -> torch.Tensor:
+        if isinstance(x, torch.Tensor):
+            t = x.detach()
+        else:
+            t = torch.as_tensor(np.asarray(x))
+        return t
+
+    def _prepare_generation_inputs(self, prompt_tokens, attention_mask):
+        prompt = self._as_int_tensor(prompt_tokens, "prompt_tokens")
+        if prompt.ndim == 1:
+            prompt = prompt[None]
+        elif prompt.ndim != 2:
+            raise ValueError(f"prompt_tokens must be a 1D or 2D array, got shape {tuple(prompt.shape)}.")
+        if prompt.dtype.is_floating_point or prompt.dtype == torch.bool or prompt.dtype.is_complex:
+            raise TypeError(f"prompt_tokens must contain integer token ids, got dtype {prompt.dtype}.")
+        if prompt.shape[0] == 0:
+            raise ValueError("prompt_tokens must contain at least one batch row.")
+        if prompt.shape[1] == 0:
+            raise ValueError("prompt_tokens must contain at least one token.")
+        if attention_mask is None:
+            return prompt, None
+        mask = self._as_int_tensor(attention_mask, "attention_mask")
+        if mask.ndim == 1:
+            mask = mask[None]
+        elif mask.ndim != 2:
+            raise ValueError(f"attention_mask must be a 1D or 2D array, got shape {tuple(mask.shape)}.")
+        if mask.dtype.is_floating_point or mask.dtype.is_complex:
+            raise TypeError(f"attention_mask must be boolean or integer, got dtype {mask.dtype}.")
+        if tuple(mask.shape) != tuple(prompt.shape):
+            raise ValueError(
+                f"attention_mask shape must match prompt_tokens shape; got {tuple(mask.shape)} and {tuple(prompt.shape)}."
+            )
+        if mask.dtype != torch.bool and bool(((mask != 0) & (mask != 1)).any()):
+            raise ValueError("attention_mask integer values must be 0 or 1.")
+        mask = mask.to(torch.bool)
+        if not bool(mask.any(dim=1).all()):
+            raise ValueError("attention_mask must contain at least one valid token per batch row.")
+        if mask.shape[1] > 1 and bool((mask[:, :-1].to(torch.int8) < mask[:, 1:].to(torch.int8)).any()):
+            raise ValueError("mask must be right padded: valid tokens cannot appear after masked positions.")
+        return prompt, mask
+
+    def buffer_length(self, prompt_len: int, max_new_tokens: int) -> int:
+        """Cache slots the reference's chunk loop ends with: (P // stride + 1) * stride, grown by stride
+        until prompt + new tokens fit (engine.py:543-557)."""
+        t = (prompt_len // self.cache_stride + 1) * self.cache_stride
+        while t < prompt_len + max_new_tokens:
+            t += self.cache_stride
+        return t
+
+    def _runtime_for(self, B: int, T: int):
+        from .runtime import DecoderRuntime
+
+        if self._weights is None:
+            self.init_params()
+        rt = self._runtime
+        if rt is None or rt.B != B or rt.T < T:
+            self._runtime = None
+            torch.cuda.empty_cache()
+            rt = DecoderRuntime(self._weights, B, T, comm=self._comm)
+            self._runtime = rt
+        return rt
+
+    # -- generation ------------------------------------------------------------------------------------
+    def generate(self, prompt_tokens, attention_mask=None, seed: int = 0, max_new_tokens: int = 10, top_k: int = 0,
+                 top_p: float = 1.0, min_p: float = 0.0, temperature: float = 1.0, fuse_decoding: bool = False,
+                 include_prompt: bool = True):
+        """Greedy / temperature generation on the GPU; returns int32 tokens ``[B, P*include_prompt + N]``
+        on the host.  ``fuse_decoding`` is accepted: every decode step is already one CUDA-graph replay."""
+        seed = normalize_count("seed", seed)
+        max_new_tokens = normalize_count("max_new_tokens", max_new_tokens)
+        if max_new_tokens < 0:
+            raise ValueError(f"max_new_tokens must be non-negative, got {max_new_tokens}.")
+        normalize_bool("fuse_decoding", fuse_decoding)
+        include_prompt = normalize_bool("include_prompt", include_prompt)
+        prompt, mask = self._prepare_generation_inputs(prompt_tokens, attention_mask)
+        vocab = self.model.config.vocab_size
+        if bool(((prompt < 0) | (prompt >= vocab)).any()):
+            raise ValueError(f"prompt_tokens token ids must be within [0, {vocab}).")
+        sp = normalize_sampling_params(top_k=top_k, top_p=top_p, min_p=min_p, temp=temperature)
+        method = SamplingMethod.from_values(top_k=sp.top_k, top_p=sp.top_p, min_p=sp.min_p, temp=sp.temp)
+        logger.info("Given the parameters top_k=%.2f, top_p=%.2f, min_p=%.2f, temperature=%.2f, "
+                    "the sampling method is determined as follows: %s.", sp.top_k, sp.top_p, sp.min_p, sp.temp, method)
+        prompt = prompt.to(torch.int32)
+        B, P = prompt.shape
+        if max_new_tokens == 0:
+            return prompt.clone() if include_prompt else prompt[:, :0].clone()
+        method.require_device_support()
+        rt = self._runtime_for(B, self.buffer_length(P, max_new_tokens))
+        dev = self._weights.device
+        pin = prompt.pin_memory() if not prompt.is_cuda else prompt
+        ids_d = pin.to(dev, non_blocking=True)
+        mask_d = (torch.ones(B, P, dtype=torch.bool) if mask is None else mask).pin_memory().to(dev, non_blocking=True)
+        toks = rt.generate(ids_d, mask_d, max_new_tokens, method.use_greedy, sp.temp, seed)
+        out = toks.to("cpu")
+        rt.check_status()
+        self.last_rng = rt.rng_key()
+        if include_prompt:
+            return torch.cat([prompt, out], dim=1)
+        return out

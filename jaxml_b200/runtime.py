@@ -305,6 +305,8 @@ class DecoderRuntime:
         self.row_best = torch.zeros(B, dtype=torch.int64, device=dev)
         self.row_map = (torch.arange(B, dtype=torch.int32, device=dev))
         self.graph = None
+        self._launches = 0
+        self.launches_last_step = 0
 
     # -- buffers ------------------------------------------------------------------------------------
     def _alloc_acts(self, M: int, Mp: int) -> dict:
@@ -366,6 +368,7 @@ class DecoderRuntime:
             args.ldo2 = W.d
             args.out2_rp = oa["Mp"] if W.bf16 else 0
         args.status = ptr(self.status)
+        self._launches += 1
         N.check(N.load().jx_norm(args, W.jdt, 1, self.stream_ptr()), "jx_norm")
 
     def _linear(self, acts, w_t, Np, Kp, x_key, kind, *, N_valid, bias=None, out=None, ldo=0, out_rp=0, res=None,
@@ -376,6 +379,7 @@ class DecoderRuntime:
         e.bias, e.out, e.ldo, e.out_rp = ptr(bias), ptr(out), ldo, out_rp
         e.res, e.ldr, e.res2, e.ldr2 = ptr(res), ldr, ptr(res2), ldr2
         lib = N.load()
+        self._launches += 1
         if not W.bf16:
             rc = lib.jx_linear_f32(ptr(acts[x_key]), K_logical, ptr(w_t), acts["M"], N_cols, K_logical, e, 1,
                                    self.stream_ptr())
@@ -416,6 +420,7 @@ class DecoderRuntime:
             qa.pos_id, qa.decode, qa.T = ptr(self.pos_id), 1 if decode else 0, self.T
             qa.q_out, qa.k_cache, qa.v_cache = ptr(acts["q"]), ptr(self.k_cache[li]), ptr(self.v_cache[li])
             qa.status = ptr(self.status)
+            self._launches += 1
             N.check(lib.jx_qkv_rope_append(qa, W.jdt, 1, self.stream_ptr()), "jx_qkv_rope_append")
             at = N.JxAttnArgs()
             at.B, at.S, at.Hq, at.Hkv, at.hd, at.T = self.B, S, W.Hq, W.Hkv, hd, self.T
@@ -428,6 +433,7 @@ class DecoderRuntime:
             at.ldo = W.Hq * hd
             at.out_rp = Mp if W.bf16 else 0
             at.status = ptr(self.status)
+            self._launches += 1
             N.check(lib.jx_attention(at, W.jdt, 1, self.stream_ptr()), "jx_attention")
             parallel = fam == "neox" and cfg.use_parallel_residual
             if fam == "gemma3" or parallel or tp:
@@ -540,8 +546,10 @@ class DecoderRuntime:
         s.update_pos = 1 if update_pos else 0
         s.advance_rng = 1
         s.status = ptr(self.status)
+        self._launches += 1
         N.check(N.load().jx_sample(s, 1, self.stream_ptr()), "jx_sample")
         if tp:
+            self._launches += 1
             gathered = self.comm.all_gather_keys(self.row_best)
             N.check(N.load().jx_sample_finalize(s, ptr(gathered), self.comm.size, self.stream_ptr()), "jx_sample_finalize")
 
@@ -577,11 +585,17 @@ class DecoderRuntime:
         self._sample(greedy, temp, update_pos=False)
 
     def decode_step(self, greedy: bool, temp: float):
+        self._launches = 0
         acts = self.dec
         self._input_norm(acts, self.w.layers[0], ids=self.next_ids)
         self._layers(acts, 1, decode=True)
         self._head(acts, self.row_map)
         self._sample(greedy, temp, update_pos=True)
+        self.launches_last_step = self._launches
+
+    def count_launches_per_decode_step(self) -> int:
+        """libjxb200 kernel launches in one decode step (counted while the step was issued)."""
+        return self.launches_last_step
 
     def capture_decode(self, greedy: bool, temp: float):
         """Captures one decode step in a CUDA graph (run one eager step first to warm up)."""
