@@ -124,6 +124,27 @@ typedef struct jx_attn_args {
   int* status;
 } jx_attn_args;
 
+/* Decode attention on tensor cores: one query token per batch row, head_dim 64/128/256, n_rep <= 16. */
+typedef struct jx_dattn_args {
+  int B, Hq, Hkv, hd;
+  int T;                 /* cache slots per row */
+  int window;            /* sliding window, 0 = none */
+  long long cache_rows;  /* rows of the whole cache allocation viewed as [cache_rows, Hkv*hd] */
+  long long layer_row0;  /* first row of this layer (layer * B * T) */
+  const void* q;         /* [B, Hq, hd] */
+  const void* k_base;    /* cache allocation base (row 0) */
+  const void* v_base;
+  const int* len_ptr;    /* [B]: valid keys = len_ptr[b] + len_add */
+  int len_add;
+  float scale;
+  void* out;             /* K128 output [out_rp rows, Hq*hd] */
+  long long out_rp;
+  void* ws;              /* scratch, jx_decode_attention_workspace bytes */
+  long long ws_bytes;
+  int* counters;         /* [B * Hkv], zero-initialised once, self-resetting */
+  int* status;
+} jx_dattn_args;
+
 typedef struct jx_sample_args {
   int B, V;              /* rows, local vocabulary columns */
   const void* logits;
@@ -191,6 +212,11 @@ int jx_qkv_rope_append(const jx_qkv_args* args, int dtype, int pdl, void* stream
 
 /* Attention.mha (nn/attention.py:321-400) on the cache, any head size (CUDA cores). */
 int jx_attention(const jx_attn_args* args, int dtype, int pdl, void* stream);
+
+/* Attention.mha decode branch (nn/attention.py:321-400) for bf16 caches on tensor cores: split over
+ * the valid keys, TMA-staged K/V tiles, exact reference rounding (see csrc/attention_decode.cu). */
+int jx_decode_attention_workspace(int B, int Hq, int hd, int T, int window, long long* bytes_out);
+int jx_decode_attention(const jx_dattn_args* args, int pdl, void* stream);
 
 /* greedy_fn / categorical sampling (inference_engine/sampling.py:75-188) + end-of-step bookkeeping. */
 int jx_sample(const jx_sample_args* args, int pdl, void* stream);

@@ -53,6 +53,13 @@ class JxAttnArgs(ctypes.Structure):
                 ("ldo", LL), ("out_rp", LL), ("status", P)]
 
 
+class JxDAttnArgs(ctypes.Structure):
+    _fields_ = [("B", I), ("Hq", I), ("Hkv", I), ("hd", I), ("T", I), ("window", I), ("cache_rows", LL),
+                ("layer_row0", LL), ("q", P), ("k_base", P), ("v_base", P), ("len_ptr", P), ("len_add", I),
+                ("scale", F), ("out", P), ("out_rp", LL), ("ws", P), ("ws_bytes", LL), ("counters", P),
+                ("status", P)]
+
+
 class JxSampleArgs(ctypes.Structure):
     _fields_ = [("B", I), ("V", I), ("logits", P), ("ld", LL), ("dtype", I), ("greedy", I), ("temp", F),
                 ("chunk", I), ("vocab_offset", LL), ("vocab_total", LL), ("rng", P), ("gumbel_tab", P), ("ws", P),
@@ -75,6 +82,8 @@ _PROTOS = {
     "jx_linear_f32": (I, [P, LL, P, I, I, I, ctypes.POINTER(JxEpilogue), I, P]),
     "jx_qkv_rope_append": (I, [ctypes.POINTER(JxQkvArgs), I, I, P]),
     "jx_attention": (I, [ctypes.POINTER(JxAttnArgs), I, I, P]),
+    "jx_decode_attention_workspace": (I, [I, I, I, I, I, ctypes.POINTER(LL)]),
+    "jx_decode_attention": (I, [ctypes.POINTER(JxDAttnArgs), I, P]),
     "jx_sample": (I, [ctypes.POINTER(JxSampleArgs), I, P]),
     "jx_sample_finalize": (I, [ctypes.POINTER(JxSampleArgs), P, I, P]),
 }

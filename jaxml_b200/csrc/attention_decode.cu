@@ -1,0 +1,432 @@
+// GQA decode attention on tensor cores (bfloat16, head_dim 64 / 128 / 256), split over the key axis.
+//
+// Reproduces Attention.mha for one query token per row (nn/attention.py:321-400, decode branch): for
+// the n_rep = Hq/Hkv query heads of one KV head (repeat_kv by indexing, :294-319)
+//   s_t = bf16(bf16(q . k_t) * bf16(attn_scale))                      (einsum output and scale in dtype)
+//   keys: t < len (prefix padding mask) and, for sliding-window layers, t >= len - window
+//   p_t = bf16(exp(s_t - max) / sum exp(s - max))                     (float32 softmax, cast to dtype)
+//   o   = bf16(sum_t p_t v_t)                                          (float32 accumulation)
+// Only the valid (or in-window) keys are read, not the whole padded buffer.
+//
+// Two kernels per layer, each a grid of (key split, KV head, batch row) CTAs of 128 keys:
+//   scores: K tiles arrive by TMA (2-D tensor map over the [L*B*T, Hkv*hd] cache, 128-byte swizzle);
+//           Q.K^T on mma.sync; the rounded scores go to a float32 workspace with per-split (max, sum).
+//   pv:     combines the split statistics into the exact softmax normaliser, forms the bf16
+//           probabilities, P.V on mma.sync with V tiles by TMA, and the last CTA of a head group sums
+//           the split partials in split order (deterministic) into the bf16 output (K128 layout).
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+
+namespace jxb {
+
+constexpr int kDaKeys = 128;        // keys per CTA
+constexpr int kDaTile = 64;         // keys per TMA tile
+
+struct DAttnParams {
+  int B, Hq, Hkv, n_rep, T, n_splits;
+  long long layer_row0;
+  const bf16* q;         // [B, Hq, HD]
+  const int* len_ptr;
+  int len_add, window;
+  float scale_bf16;      // attn_scale rounded to bf16
+  bf16* out;
+  long long out_rp;
+  float* sc;             // [B, Hq, T]
+  float* stats;          // [B, Hq, n_splits, 2]
+  float* opart;          // [B, Hq, n_splits, HD]
+  int* counters;         // [B * Hkv]
+  int* status;
+};
+
+// Address of the 16-byte chunk `c` (8 bf16 columns) of row r in a [rows x 64] block stored with the
+// 128-byte swizzle (chunk index XOR row % 8), the layout TMA writes with CU_TENSOR_MAP_SWIZZLE_128B.
+__device__ __forceinline__ uint32_t swz(uint32_t block_base, int r, int c) {
+  return block_base + r * 128 + ((c ^ (r & 7)) << 4);
+}
+
+__device__ __forceinline__ void key_range(const DAttnParams& p, int b, int& lo, int& valid) {
+  valid = p.len_ptr[b] + p.len_add;
+  if (valid > p.T) {
+    set_status(p.status, JX_ERR_RANGE);
+    valid = p.T;
+  }
+  lo = (p.window > 0 && valid > p.window) ? valid - p.window : 0;
+}
+
+template <int HD>
+__global__ void __launch_bounds__(128) dattn_scores_kernel(const __grid_constant__ CUtensorMap kmap, DAttnParams p) {
+  constexpr int NB = HD / 64;                 // 64-column blocks per head
+  constexpr int TILE_BYTES = kDaTile * HD * 2;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* ktile = smem;                                   // 2 tiles, each NB blocks of [64 x 64]
+  uint8_t* qs = smem + 2 * TILE_BYTES;                     // NB blocks of [16 x 64]
+  uint64_t* bar = reinterpret_cast<uint64_t*>(qs + NB * 2048);
+  float* red = reinterpret_cast<float*>(bar + 2);          // [4 warps][16 rows]
+
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_wait();
+  pdl_trigger();
+  int lo, valid;
+  key_range(p, b, lo, valid);
+  const int t0 = lo + split * kDaKeys;
+  if (t0 >= valid) return;
+  const int t1 = min(t0 + kDaKeys, valid);
+  const int n_tiles = (t1 - t0 + kDaTile - 1) / kDaTile;
+  if (threadIdx.x == 0) {
+    prefetch_tmap(&kmap);
+    mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
+    fence_barrier_init();
+    for (int i = 0; i < n_tiles; ++i) {
+      mbar_arrive_expect_tx(&bar[i], TILE_BYTES);
+      const int y = (int)(p.layer_row0 + (long long)b * p.T + t0 + i * kDaTile);
+#pragma unroll
+      for (int c = 0; c < NB; ++c) tma_load_2d(ktile + i * TILE_BYTES + c * 8192, &kmap, kvh * HD + c * 64, y, &bar[i]);
+    }
+  }
+  // Q rows of this head group (rows >= n_rep are zero) into the swizzled layout.
+  for (int idx = threadIdx.x; idx < 16 * (HD / 8); idx += 128) {
+    const int r = idx / (HD / 8), cg = idx % (HD / 8);
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (r < p.n_rep)
+      v = *reinterpret_cast<const uint4*>(p.q + ((long long)b * p.Hq + kvh * p.n_rep + r) * HD + cg * 8);
+    const uint32_t a = swz(smem_u32(qs + (cg >> 3) * 2048), r, cg & 7);
+    asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w));
+  }
+  __syncthreads();
+
+  const int mi = lane >> 3, r8 = lane & 7;
+  float s[2][2][4];          // [tile][n8 tile][frag]
+  float mrow[2] = {-INFINITY, -INFINITY};   // rows lane/4 and lane/4 + 8
+  bool ok = true;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) s[i][nt][e] = -INFINITY;
+    if (i >= n_tiles || !ok) continue;
+    if (!mbar_wait_bounded(&bar[i], 0)) {
+      set_status(p.status, JX_ERR_TIMEOUT);
+      ok = false;
+      continue;
+    }
+    float acc[2][4] = {};
+    const uint32_t kb = smem_u32(ktile + i * TILE_BYTES);
+#pragma unroll
+    for (int ks = 0; ks < HD / 16; ++ks) {
+      uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
+      {
+        const int row = (mi & 1) * 8 + r8, ch = ks * 2 + (mi >> 1);
+        ldsm_x4(swz(smem_u32(qs + (ch >> 3) * 2048), row, ch & 7), a0, a1, a2, a3);
+      }
+      {
+        const int row = warp * 16 + (mi >> 1) * 8 + r8, ch = ks * 2 + (mi & 1);
+        ldsm_x4(swz(kb + (ch >> 3) * 8192, row, ch & 7), b0, b1, b2, b3);
+      }
+      mma_bf16(acc[0], a0, a1, a2, a3, b0, b1);
+      mma_bf16(acc[1], a0, a1, a2, a3, b2, b3);
+    }
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int t = t0 + i * kDaTile + warp * 16 + nt * 8 + (lane & 3) * 2 + (e & 1);
+        if (t < t1) {
+          const float v = rnd<bf16>(rnd<bf16>(acc[nt][e]) * p.scale_bf16);
+          s[i][nt][e] = v;
+          mrow[e >> 1] = fmaxf(mrow[e >> 1], v);
+        }
+      }
+  }
+  if (!__syncthreads_and(ok)) return;
+  // row maxima over the CTA
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    mrow[h] = fmaxf(mrow[h], __shfl_xor_sync(0xffffffffu, mrow[h], 1));
+    mrow[h] = fmaxf(mrow[h], __shfl_xor_sync(0xffffffffu, mrow[h], 2));
+  }
+  if ((lane & 3) == 0) {
+    red[warp * 16 + (lane >> 2)] = mrow[0];
+    red[warp * 16 + (lane >> 2) + 8] = mrow[1];
+  }
+  __syncthreads();
+  float m[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int row = (lane >> 2) + h * 8;
+    m[h] = fmaxf(fmaxf(red[row], red[16 + row]), fmaxf(red[32 + row], red[48 + row]));
+  }
+  __syncthreads();
+  float l[2] = {0.f, 0.f};
+  const long long sc_row = ((long long)b * p.Hq + kvh * p.n_rep) * p.T;
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int row = (lane >> 2) + (e >> 1) * 8;
+        const int t = t0 + i * kDaTile + warp * 16 + nt * 8 + (lane & 3) * 2 + (e & 1);
+        if (t < t1 && row < p.n_rep) {
+          const float v = s[i][nt][e];
+          p.sc[sc_row + (long long)row * p.T + t] = v;
+          l[e >> 1] += expf(v - m[e >> 1]);
+        }
+      }
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    l[h] += __shfl_xor_sync(0xffffffffu, l[h], 1);
+    l[h] += __shfl_xor_sync(0xffffffffu, l[h], 2);
+  }
+  if ((lane & 3) == 0) {
+    red[warp * 16 + (lane >> 2)] = l[0];
+    red[warp * 16 + (lane >> 2) + 8] = l[1];
+  }
+  __syncthreads();
+  // (max, sum) of this split for each query row: warp 0's lanes with lane % 4 == 0 own rows lane/4, +8
+  if (warp == 0 && (lane & 3) == 0) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int row = (lane >> 2) + h * 8;
+      if (row < p.n_rep) {
+        float* st = p.stats + (((long long)b * p.Hq + kvh * p.n_rep + row) * p.n_splits + split) * 2;
+        st[0] = m[h];
+        st[1] = (red[row] + red[16 + row]) + (red[32 + row] + red[48 + row]);
+      }
+    }
+  }
+}
+
+template <int HD>
+__global__ void __launch_bounds__(128) dattn_pv_kernel(const __grid_constant__ CUtensorMap vmap, DAttnParams p) {
+  constexpr int NB = HD / 64;
+  constexpr int TILE_BYTES = kDaTile * HD * 2;
+  constexpr int WCOLS = HD / 4;             // output columns per warp
+  constexpr int NT = WCOLS / 8;             // n8 tiles per warp
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* vtile = smem;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + 2 * TILE_BYTES);
+  float* Ms = reinterpret_cast<float*>(bar + 2);   // [16]
+  float* Ls = Ms + 16;                             // [16]
+  __shared__ int last_flag;
+
+  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_wait();
+  pdl_trigger();
+  int lo, valid;
+  key_range(p, b, lo, valid);
+  const int t0 = lo + split * kDaKeys;
+  const int n_active = (valid - lo + kDaKeys - 1) / kDaKeys;
+  if (t0 >= valid) return;
+  const int t1 = min(t0 + kDaKeys, valid);
+  const int n_tiles = (t1 - t0 + kDaTile - 1) / kDaTile;
+  if (threadIdx.x == 0) {
+    prefetch_tmap(&vmap);
+    mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
+    fence_barrier_init();
+    for (int i = 0; i < n_tiles; ++i) {
+      mbar_arrive_expect_tx(&bar[i], TILE_BYTES);
+      const int y = (int)(p.layer_row0 + (long long)b * p.T + t0 + i * kDaTile);
+#pragma unroll
+      for (int c = 0; c < NB; ++c) tma_load_2d(vtile + i * TILE_BYTES + c * 8192, &vmap, kvh * HD + c * 64, y, &bar[i]);
+    }
+  }
+  // exact softmax normaliser of each row from the split statistics
+  if (threadIdx.x < 16) {
+    const int row = threadIdx.x;
+    float M = -INFINITY, L = 0.f;
+    if (row < p.n_rep) {
+      const float* st = p.stats + ((long long)b * p.Hq + kvh * p.n_rep + row) * p.n_splits * 2;
+      for (int s2 = 0; s2 < n_active; ++s2) M = fmaxf(M, st[s2 * 2]);
+      for (int s2 = 0; s2 < n_active; ++s2) L += st[s2 * 2 + 1] * expf(st[s2 * 2] - M);
+    }
+    Ms[row] = M;
+    Ls[row] = L;
+  }
+  __syncthreads();
+
+  const int mi = lane >> 3, r8 = lane & 7;
+  const int r_lo = lane >> 2, r_hi = r_lo + 8;
+  const float M0 = Ms[r_lo], L0 = Ls[r_lo], M1 = Ms[r_hi], L1 = Ls[r_hi];
+  const float* sc0 = p.sc + ((long long)b * p.Hq + kvh * p.n_rep + r_lo) * p.T;
+  const float* sc1 = p.sc + ((long long)b * p.Hq + kvh * p.n_rep + r_hi) * p.T;
+  auto prob = [&](const float* sc, int row, float M, float L, int t) -> float {
+    if (row >= p.n_rep || t >= t1) return 0.f;
+    return rnd<bf16>(expf(__ldcg(sc + t) - M) / L);
+  };
+  float acc[NT][4] = {};
+  bool ok = true;
+  for (int i = 0; i < n_tiles && ok; ++i) {
+    if (!mbar_wait_bounded(&bar[i], 0)) {
+      set_status(p.status, JX_ERR_TIMEOUT);
+      ok = false;
+      continue;
+    }
+    const uint32_t vb = smem_u32(vtile + i * TILE_BYTES);
+#pragma unroll
+    for (int kk = 0; kk < kDaTile / 16; ++kk) {
+      const int tb = t0 + i * kDaTile + kk * 16 + (lane & 3) * 2;
+      const uint32_t a0 = pack_bf16x2(prob(sc0, r_lo, M0, L0, tb), prob(sc0, r_lo, M0, L0, tb + 1));
+      const uint32_t a1 = pack_bf16x2(prob(sc1, r_hi, M1, L1, tb), prob(sc1, r_hi, M1, L1, tb + 1));
+      const uint32_t a2 = pack_bf16x2(prob(sc0, r_lo, M0, L0, tb + 8), prob(sc0, r_lo, M0, L0, tb + 9));
+      const uint32_t a3 = pack_bf16x2(prob(sc1, r_hi, M1, L1, tb + 8), prob(sc1, r_hi, M1, L1, tb + 9));
+#pragma unroll
+      for (int n16 = 0; n16 < NT / 2; ++n16) {
+        uint32_t b0, b1, b2, b3;
+        const int row = kk * 16 + (mi & 1) * 8 + r8;
+        const int ch = (warp * WCOLS) / 8 + n16 * 2 + (mi >> 1);
+        ldsm_x4_t(swz(vb + (ch >> 3) * 8192, row, ch & 7), b0, b1, b2, b3);
+        mma_bf16(acc[n16 * 2], a0, a1, a2, a3, b0, b1);
+        mma_bf16(acc[n16 * 2 + 1], a0, a1, a2, a3, b2, b3);
+      }
+    }
+  }
+  if (!__syncthreads_and(ok)) return;
+  // split partial -> workspace
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int row = (e >> 1) ? r_hi : r_lo;
+      const int col = warp * WCOLS + nt * 8 + (lane & 3) * 2 + (e & 1);
+      if (row < p.n_rep)
+        p.opart[(((long long)b * p.Hq + kvh * p.n_rep + row) * p.n_splits + split) * HD + col] = acc[nt][e];
+    }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const int prev = atomicAdd(&p.counters[b * p.Hkv + kvh], 1);
+    last_flag = (prev == n_active - 1);
+  }
+  __syncthreads();
+  if (!last_flag) return;
+  __threadfence();
+  for (int idx = threadIdx.x; idx < p.n_rep * HD; idx += 128) {
+    const int row = idx / HD, col = idx % HD;
+    const float* src = p.opart + (((long long)b * p.Hq + kvh * p.n_rep + row) * p.n_splits) * HD + col;
+    float sum = 0.f;
+    for (int s2 = 0; s2 < n_active; ++s2) sum += __ldcg(src + (long long)s2 * HD);
+    const long long ocol = (long long)(kvh * p.n_rep + row) * HD + col;
+    p.out[k128_offset(b, ocol, p.out_rp)] = __float2bfloat16_rn(sum);
+  }
+  if (threadIdx.x == 0) p.counters[b * p.Hkv + kvh] = 0;
+}
+
+// ------------------------------------------------------------------------------------------------
+// host side
+// ------------------------------------------------------------------------------------------------
+static PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+// 2-D bf16 tensor map over a row-major [rows, cols] matrix with a 64x64 box and 128-byte swizzle.
+int make_tmap_2d_bf16(CUtensorMap* map, const void* base, long long rows, long long cols, long long row_stride_elems) {
+  auto enc = tmap_encoder();
+  if (!enc) return JX_ERR_CUDA;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || ((row_stride_elems * 2) & 15) || cols % 64) return JX_ERR_ARG;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(row_stride_elems * 2)};
+  cuuint32_t box[2] = {64, 64};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? JX_OK : JX_ERR_ARG;
+}
+
+long long dattn_workspace_bytes(int B, int Hq, int T, int hd, int n_splits) {
+  const long long sc = (long long)B * Hq * T;
+  const long long st = (long long)B * Hq * n_splits * 2;
+  const long long op = (long long)B * Hq * n_splits * hd;
+  return (sc + st + op) * 4;
+}
+
+int dattn_n_splits(int T, int window) {
+  const int range = (window > 0 && window < T) ? window : T;
+  return (range + kDaKeys - 1) / kDaKeys;
+}
+
+template <int HD>
+static int launch_dattn(const CUtensorMap& km, const CUtensorMap& vm, const DAttnParams& p, bool pdl, cudaStream_t s) {
+  const int smem_a = 1024 + 2 * kDaTile * HD * 2 + (HD / 64) * 2048 + 16 + 4 * 16 * 4;
+  const int smem_b = 1024 + 2 * kDaTile * HD * 2 + 16 + 32 * 4;
+  static bool configured = false;
+  if (!configured) {
+    if (cudaFuncSetAttribute(dattn_scores_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_a) != cudaSuccess ||
+        cudaFuncSetAttribute(dattn_pv_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_b) != cudaSuccess)
+      return JX_ERR_CUDA;
+    configured = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.n_splits, p.Hkv, p.B);
+  cfg.blockDim = dim3(128);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cfg.dynamicSmemBytes = smem_a;
+  if (cudaLaunchKernelEx(&cfg, dattn_scores_kernel<HD>, km, p) != cudaSuccess) return JX_ERR_CUDA;
+  cfg.dynamicSmemBytes = smem_b;
+  if (cudaLaunchKernelEx(&cfg, dattn_pv_kernel<HD>, vm, p) != cudaSuccess) return JX_ERR_CUDA;
+  return JX_OK;
+}
+
+int run_decode_attention(const jx_dattn_args& a, bool pdl, cudaStream_t stream) {
+  if (a.B <= 0 || a.Hkv <= 0 || a.Hq % a.Hkv || a.T <= 0) return JX_ERR_SHAPE;
+  const int n_rep = a.Hq / a.Hkv;
+  if (n_rep > 16) return JX_ERR_SHAPE;
+  if (a.hd != 64 && a.hd != 128 && a.hd != 256) return JX_ERR_SHAPE;
+  const int n_splits = dattn_n_splits(a.T, a.window);
+  if (dattn_workspace_bytes(a.B, a.Hq, a.T, a.hd, n_splits) > a.ws_bytes) return JX_ERR_ARG;
+  if (reinterpret_cast<uintptr_t>(a.q) & 15) return JX_ERR_ARG;
+  CUtensorMap km, vm;
+  const long long cols = (long long)a.Hkv * a.hd;
+  int rc = make_tmap_2d_bf16(&km, a.k_base, a.cache_rows, cols, cols);
+  if (rc == JX_OK) rc = make_tmap_2d_bf16(&vm, a.v_base, a.cache_rows, cols, cols);
+  if (rc != JX_OK) return rc;
+  DAttnParams p;
+  p.B = a.B;
+  p.Hq = a.Hq;
+  p.Hkv = a.Hkv;
+  p.n_rep = n_rep;
+  p.T = a.T;
+  p.n_splits = n_splits;
+  p.layer_row0 = a.layer_row0;
+  p.q = reinterpret_cast<const bf16*>(a.q);
+  p.len_ptr = a.len_ptr;
+  p.len_add = a.len_add;
+  p.window = a.window;
+  p.scale_bf16 = __bfloat162float(__float2bfloat16_rn(a.scale));
+  p.out = reinterpret_cast<bf16*>(a.out);
+  p.out_rp = a.out_rp;
+  float* ws = reinterpret_cast<float*>(a.ws);
+  p.sc = ws;
+  p.stats = p.sc + (long long)a.B * a.Hq * a.T;
+  p.opart = p.stats + (long long)a.B * a.Hq * n_splits * 2;
+  p.counters = a.counters;
+  p.status = a.status;
+  switch (a.hd) {
+    case 64: return launch_dattn<64>(km, vm, p, pdl, stream);
+    case 128: return launch_dattn<128>(km, vm, p, pdl, stream);
+    default: return launch_dattn<256>(km, vm, p, pdl, stream);
+  }
+}
+
+}  // namespace jxb

@@ -16,6 +16,9 @@ int run_gemm_f32(const float* X, long long ldx, const float* W, int M, int N, in
 int run_qkv_rope_append(int dtype, const jx_qkv_args& p, bool pdl, cudaStream_t stream);
 int run_attention_generic(int dtype, const jx_attn_args& p, bool pdl, cudaStream_t stream);
 int run_sample(const jx_sample_args& p, bool pdl, cudaStream_t stream);
+int run_decode_attention(const jx_dattn_args& a, bool pdl, cudaStream_t stream);
+long long dattn_workspace_bytes(int B, int Hq, int T, int hd, int n_splits);
+int dattn_n_splits(int T, int window);
 int run_sample_finalize(const jx_sample_args& p, const unsigned long long* gathered, int n_shards,
                         cudaStream_t stream);
 
@@ -184,6 +187,23 @@ int jx_attention(const jx_attn_args* args, int dtype, int pdl, void* stream) {
   const int rc = run_attention_generic(dtype, *args, pdl != 0, (cudaStream_t)stream);
   if (rc == JX_ERR_CUDA) return note_cuda("jx_attention");
   if (rc != JX_OK) return fail(rc, "jx_attention: unsupported sizes or dtype");
+  return JX_OK;
+}
+
+int jx_decode_attention_workspace(int B, int Hq, int hd, int T, int window, long long* bytes_out) {
+  if (!bytes_out || B <= 0 || Hq <= 0 || hd <= 0 || T <= 0) return fail(JX_ERR_SHAPE, "jx_decode_attention_workspace: bad sizes");
+  *bytes_out = dattn_workspace_bytes(B, Hq, T, hd, dattn_n_splits(T, window));
+  return JX_OK;
+}
+
+int jx_decode_attention(const jx_dattn_args* args, int pdl, void* stream) {
+  if (!args || !args->q || !args->k_base || !args->v_base || !args->out || !args->ws || !args->counters || !args->len_ptr)
+    return fail(JX_ERR_ARG, "jx_decode_attention: null pointer");
+  const int rc = run_decode_attention(*args, pdl != 0, (cudaStream_t)stream);
+  if (rc == JX_ERR_CUDA) return note_cuda("jx_decode_attention");
+  if (rc != JX_OK)
+    return fail(rc, "jx_decode_attention: head_dim must be 64/128/256, Hq/Hkv <= 16, workspace large enough, "
+                    "16-byte aligned q/cache");
   return JX_OK;
 }
 

@@ -304,6 +304,13 @@ class DecoderRuntime:
         self.sample_counters = torch.zeros(B + 1, dtype=torch.int32, device=dev)
         self.row_best = torch.zeros(B, dtype=torch.int64, device=dev)
         self.row_map = (torch.arange(B, dtype=torch.int32, device=dev))
+        # tensor-core decode attention: bf16, head_dim 64/128/256, up to 16 query heads per KV head
+        self.fast_attn = w.bf16 and w.hd in (64, 128, 256) and (w.Hq // w.Hkv) <= 16
+        if self.fast_attn:
+            nb = N.LL()
+            N.check(N.load().jx_decode_attention_workspace(B, w.Hq, w.hd, T, 0, nb), "attention workspace")
+            self.attn_ws = torch.zeros((nb.value + 3) // 4, dtype=torch.float32, device=dev)
+            self.attn_counters = torch.zeros(B * w.Hkv, dtype=torch.int32, device=dev)
         self.graph = None
         self._launches = 0
         self.launches_last_step = 0
@@ -400,100 +407,128 @@ class DecoderRuntime:
 
     # -- one pass over the stack -----------------------------------------------------------------------
     def _layers(self, acts, S: int, decode: bool):
-        W, cfg = self.w, self.w.cfg
-        M, Mp = acts["M"], acts["Mp"]
-        d, hd = W.d, W.hd
-        tp = self.comm is not None
-        fam = W.family
-        lib = N.load()
+        W = self.w
         for li, lw in enumerate(W.layers):
             nx = W.layers[li + 1] if li + 1 < len(W.layers) else None
-            # ---- attention block ----
             self._linear(acts, lw.wqkv, W.Np_qkv, W.Kp_d, "xn", N.JX_EPI_STORE, N_valid=W.nqkv, bias=lw.bqkv,
-                         out=acts["qkv"], ldo=W.nqkv, K_logical=d, N_cols=W.nqkv)
-            qa = N.JxQkvArgs()
-            qa.M, qa.S, qa.Hq, qa.Hkv, qa.hd, qa.rd = M, S, W.Hq, W.Hkv, hd, W.rd
-            qa.qkv, qa.ld_qkv = ptr(acts["qkv"]), W.nqkv
-            qa.qn_w, qa.kn_w, qa.eps = ptr(lw.qn), ptr(lw.kn), cfg.norm_eps
-            cos, sin = (W.cos_l, W.sin_l) if lw.local_rope else (W.cos, W.sin)
-            qa.max_pos, qa.cos, qa.sin = cfg.max_position_embeddings, ptr(cos), ptr(sin)
-            qa.pos_id, qa.decode, qa.T = ptr(self.pos_id), 1 if decode else 0, self.T
-            qa.q_out, qa.k_cache, qa.v_cache = ptr(acts["q"]), ptr(self.k_cache[li]), ptr(self.v_cache[li])
-            qa.status = ptr(self.status)
-            self._launches += 1
-            N.check(lib.jx_qkv_rope_append(qa, W.jdt, 1, self.stream_ptr()), "jx_qkv_rope_append")
-            at = N.JxAttnArgs()
-            at.B, at.S, at.Hq, at.Hkv, at.hd, at.T = self.B, S, W.Hq, W.Hkv, hd, self.T
-            at.q, at.k, at.v = ptr(acts["q"]), ptr(self.k_cache[li]), ptr(self.v_cache[li])
-            at.len_ptr, at.len_add = ptr(self.pos_id), 2 if decode else 1
-            at.causal = 0 if (decode or S == 1) else 1
-            at.window = cfg.sliding_window if lw.sliding else 0
-            at.scale = cfg.attn_scale
-            at.out = ptr(acts["attn"])
-            at.ldo = W.Hq * hd
-            at.out_rp = Mp if W.bf16 else 0
-            at.status = ptr(self.status)
-            self._launches += 1
-            N.check(lib.jx_attention(at, W.jdt, 1, self.stream_ptr()), "jx_attention")
-            parallel = fam == "neox" and cfg.use_parallel_residual
-            if fam == "gemma3" or parallel or tp:
-                # o_proj result kept apart: Gemma normalises it, NeoX's parallel residual adds it with the
-                # MLP output, and under tensor parallelism it is a partial sum to all-reduce first.
-                self._linear(acts, lw.wo, W.Np_d, W.Kp_o, "attn", N.JX_EPI_STORE, N_valid=d, bias=lw.bo,
-                             out=acts["tmp"], ldo=d, K_logical=W.Hq * hd, N_cols=d)
-                if not parallel:
-                    self._allreduce(acts["tmp"], M)
+                         out=acts["qkv"], ldo=W.nqkv, K_logical=W.d, N_cols=W.nqkv)
+            self._qkv_rope_append(acts, li, lw, S, decode)
+            if decode and self.fast_attn:
+                self._decode_attention(acts, li, lw)
             else:
-                self._linear(acts, lw.wo, W.Np_d, W.Kp_o, "attn", N.JX_EPI_RESID, N_valid=d, bias=lw.bo,
-                             out=acts["h"], ldo=d, res=acts["h"], ldr=d, K_logical=W.Hq * hd, N_cols=d)
-            # ---- MLP input ----
+                self._generic_attention(acts, li, lw, S, decode)
+            self._o_and_mlp(acts, lw, nx)
+
+    def _qkv_rope_append(self, acts, li, lw, S, decode):
+        W, cfg = self.w, self.w.cfg
+        qa = N.JxQkvArgs()
+        qa.M, qa.S, qa.Hq, qa.Hkv, qa.hd, qa.rd = acts["M"], S, W.Hq, W.Hkv, W.hd, W.rd
+        qa.qkv, qa.ld_qkv = ptr(acts["qkv"]), W.nqkv
+        qa.qn_w, qa.kn_w, qa.eps = ptr(lw.qn), ptr(lw.kn), cfg.norm_eps
+        cos, sin = (W.cos_l, W.sin_l) if lw.local_rope else (W.cos, W.sin)
+        qa.max_pos, qa.cos, qa.sin = cfg.max_position_embeddings, ptr(cos), ptr(sin)
+        qa.pos_id, qa.decode, qa.T = ptr(self.pos_id), 1 if decode else 0, self.T
+        qa.q_out, qa.k_cache, qa.v_cache = ptr(acts["q"]), ptr(self.k_cache[li]), ptr(self.v_cache[li])
+        qa.status = ptr(self.status)
+        self._launches += 1
+        N.check(N.load().jx_qkv_rope_append(qa, W.jdt, 1, self.stream_ptr()), "jx_qkv_rope_append")
+
+    def _generic_attention(self, acts, li, lw, S, decode):
+        W, cfg = self.w, self.w.cfg
+        at = N.JxAttnArgs()
+        at.B, at.S, at.Hq, at.Hkv, at.hd, at.T = self.B, S, W.Hq, W.Hkv, W.hd, self.T
+        at.q, at.k, at.v = ptr(acts["q"]), ptr(self.k_cache[li]), ptr(self.v_cache[li])
+        at.len_ptr, at.len_add = ptr(self.pos_id), 2 if decode else 1
+        at.causal = 0 if (decode or S == 1) else 1
+        at.window = cfg.sliding_window if lw.sliding else 0
+        at.scale = cfg.attn_scale
+        at.out = ptr(acts["attn"])
+        at.ldo = W.Hq * W.hd
+        at.out_rp = acts["Mp"] if W.bf16 else 0
+        at.status = ptr(self.status)
+        self._launches += 1
+        N.check(N.load().jx_attention(at, W.jdt, 1, self.stream_ptr()), "jx_attention")
+
+    def _decode_attention(self, acts, li, lw):
+        W, cfg = self.w, self.w.cfg
+        a = N.JxDAttnArgs()
+        a.B, a.Hq, a.Hkv, a.hd, a.T = self.B, W.Hq, W.Hkv, W.hd, self.T
+        a.window = cfg.sliding_window if lw.sliding else 0
+        a.cache_rows = self.k_cache.shape[0] * self.B * self.T
+        a.layer_row0 = li * self.B * self.T
+        a.q, a.k_base, a.v_base = ptr(acts["q"]), ptr(self.k_cache), ptr(self.v_cache)
+        a.len_ptr, a.len_add = ptr(self.pos_id), 2
+        a.scale = cfg.attn_scale
+        a.out, a.out_rp = ptr(acts["attn"]), acts["Mp"]
+        a.ws, a.ws_bytes = ptr(self.attn_ws), self.attn_ws.numel() * 4
+        a.counters, a.status = ptr(self.attn_counters), ptr(self.status)
+        self._launches += 2
+        N.check(N.load().jx_decode_attention(a, 1, self.stream_ptr()), "jx_decode_attention")
+
+    def _o_and_mlp(self, acts, lw, nx):
+        """o_proj, residual / post-attention norm, MLP, residual and the next layer's input norm."""
+        W, cfg, fam = self.w, self.w.cfg, self.w.family
+        M, Mp, d, hd = acts["M"], acts["Mp"], W.d, W.hd
+        tp = self.comm is not None
+        parallel = fam == "neox" and cfg.use_parallel_residual
+        if fam == "gemma3" or parallel or tp:
+            # o_proj result kept apart: Gemma normalises it, NeoX's parallel residual adds it with the
+            # MLP output, and under tensor parallelism it is a partial sum to all-reduce first.
+            self._linear(acts, lw.wo, W.Np_d, W.Kp_o, "attn", N.JX_EPI_STORE, N_valid=d, bias=lw.bo,
+                         out=acts["tmp"], ldo=d, K_logical=W.Hq * hd, N_cols=d)
+            if not parallel:
+                self._allreduce(acts["tmp"], M)
+        else:
+            self._linear(acts, lw.wo, W.Np_d, W.Kp_o, "attn", N.JX_EPI_RESID, N_valid=d, bias=lw.bo,
+                         out=acts["h"], ldo=d, res=acts["h"], ldr=d, K_logical=W.Hq * hd, N_cols=d)
+        # ---- MLP input ----
+        if fam == "gemma3":
+            pa = lw.norms["post_attention_layernorm"]
+            pf = lw.norms["pre_feedforward_layernorm"]
+            self._norm(acts, a=acts["tmp"], kind_pre=N.JX_NORM_GEMMA, w_pre=pa[0], b_pre=pa[1], w=pf[0], b=pf[1])
+            mlp_in = "xn"
+        elif parallel:
+            mlp_in = "xn2"      # ln2(h) was produced together with ln1(h)
+        else:
+            pn = lw.norms["post_attention_layernorm"]
+            if tp:
+                self._norm(acts, a=acts["tmp"], w=pn[0], b=pn[1])
+            else:
+                self._norm(acts, w=pn[0], b=pn[1])
+            mlp_in = "xn"
+        # ---- MLP ----
+        if W.glu:
+            kind = N.JX_EPI_GLU_SILU if fam == "llama" else N.JX_EPI_GLU_GELU_TANH
+            self._linear(acts, lw.wgu, W.Np_gu, W.Kp_d, mlp_in, kind, N_valid=W.F, bias=lw.bgu,
+                         out=acts["act"], ldo=W.F32, out_rp=Mp if W.bf16 else 0, K_logical=d, N_cols=2 * W.F32)
+        else:
+            self._linear(acts, lw.wgu, W.Np_gu, W.Kp_d, mlp_in, N.JX_EPI_ACT_GELU_ERF, N_valid=W.F, bias=lw.bgu,
+                         out=acts["act"], ldo=W.F, out_rp=Mp if W.bf16 else 0, K_logical=d, N_cols=W.F)
+        Fk = W.F32 if (W.glu and not W.bf16) else W.F
+        down_kw = dict(N_valid=d, bias=lw.bd, K_logical=Fk, N_cols=d)
+        if parallel and tp:
+            # tmp = attn_partial + mlp_partial, all-reduced once; h += tmp in the next norm.
+            self._linear(acts, lw.wd, W.Np_d, W.Kp_f, "act", N.JX_EPI_RESID, out=acts["tmp"], ldo=d,
+                         res=acts["tmp"], ldr=d, **down_kw)
+            self._allreduce(acts["tmp"], M)
+        elif fam == "gemma3" or tp:
+            self._linear(acts, lw.wd, W.Np_d, W.Kp_f, "act", N.JX_EPI_STORE, out=acts["tmp"], ldo=d, **down_kw)
+            self._allreduce(acts["tmp"], M)
+        elif parallel:
+            self._linear(acts, lw.wd, W.Np_d, W.Kp_f, "act", N.JX_EPI_RESID2, out=acts["h"], ldo=d,
+                         res=acts["h"], ldr=d, res2=acts["tmp"], ldr2=d, **down_kw)
+        else:
+            self._linear(acts, lw.wd, W.Np_d, W.Kp_f, "act", N.JX_EPI_RESID, out=acts["h"], ldo=d,
+                         res=acts["h"], ldr=d, **down_kw)
+        # ---- next layer's input norm (the final norm is done by the caller) ----
+        if nx is None:
             if fam == "gemma3":
-                pa = lw.norms["post_attention_layernorm"]
-                pf = lw.norms["pre_feedforward_layernorm"]
-                self._norm(acts, a=acts["tmp"], kind_pre=N.JX_NORM_GEMMA, w_pre=pa[0], b_pre=pa[1], w=pf[0], b=pf[1])
-                mlp_in = "xn"
-            elif parallel:
-                mlp_in = "xn2"      # ln2(h) was produced together with ln1(h)
-            else:
-                pn = lw.norms["post_attention_layernorm"]
-                if tp:
-                    self._norm(acts, a=acts["tmp"], w=pn[0], b=pn[1])
-                else:
-                    self._norm(acts, w=pn[0], b=pn[1])
-                mlp_in = "xn"
-            # ---- MLP ----
-            if W.glu:
-                kind = N.JX_EPI_GLU_SILU if fam == "llama" else N.JX_EPI_GLU_GELU_TANH
-                self._linear(acts, lw.wgu, W.Np_gu, W.Kp_d, mlp_in, kind, N_valid=W.F, bias=lw.bgu,
-                             out=acts["act"], ldo=W.F32, out_rp=Mp if W.bf16 else 0, K_logical=d, N_cols=2 * W.F32)
-            else:
-                self._linear(acts, lw.wgu, W.Np_gu, W.Kp_d, mlp_in, N.JX_EPI_ACT_GELU_ERF, N_valid=W.F, bias=lw.bgu,
-                             out=acts["act"], ldo=W.F, out_rp=Mp if W.bf16 else 0, K_logical=d, N_cols=W.F)
-            Fk = W.F32 if (W.glu and not W.bf16) else W.F
-            down_kw = dict(N_valid=d, bias=lw.bd, K_logical=Fk, N_cols=d)
-            if parallel and tp:
-                # tmp = attn_partial + mlp_partial, all-reduced once; h += tmp in the next norm.
-                self._linear(acts, lw.wd, W.Np_d, W.Kp_f, "act", N.JX_EPI_RESID, out=acts["tmp"], ldo=d,
-                             res=acts["tmp"], ldr=d, **down_kw)
-                self._allreduce(acts["tmp"], M)
-            elif fam == "gemma3" or tp:
-                self._linear(acts, lw.wd, W.Np_d, W.Kp_f, "act", N.JX_EPI_STORE, out=acts["tmp"], ldo=d, **down_kw)
-                self._allreduce(acts["tmp"], M)
-            elif parallel:
-                self._linear(acts, lw.wd, W.Np_d, W.Kp_f, "act", N.JX_EPI_RESID2, out=acts["h"], ldo=d,
-                             res=acts["h"], ldr=d, res2=acts["tmp"], ldr2=d, **down_kw)
-            else:
-                self._linear(acts, lw.wd, W.Np_d, W.Kp_f, "act", N.JX_EPI_RESID, out=acts["h"], ldo=d,
-                             res=acts["h"], ldr=d, **down_kw)
-            # ---- next layer's input norm (the final norm is done by the caller) ----
-            if nx is None:
-                if fam == "gemma3":
-                    pf = lw.norms["post_feedforward_layernorm"]
-                    self._norm(acts, out_key=None, a=acts["tmp"], kind_pre=N.JX_NORM_GEMMA, w_pre=pf[0], b_pre=pf[1])
-                elif tp:
-                    self._norm(acts, out_key=None, a=acts["tmp"], kind=N.JX_NORM_NONE)
-                continue
-            self._input_norm(acts, nx, after=lw)
+                pf = lw.norms["post_feedforward_layernorm"]
+                self._norm(acts, out_key=None, a=acts["tmp"], kind_pre=N.JX_NORM_GEMMA, w_pre=pf[0], b_pre=pf[1])
+            elif tp:
+                self._norm(acts, out_key=None, a=acts["tmp"], kind=N.JX_NORM_NONE)
+            return
+        self._input_norm(acts, nx, after=lw)
 
     def _input_norm(self, acts, lw: LayerWeights, after: Optional[LayerWeights] = None, ids=None):
         W, fam, cfg = self.w, self.w.family, self.w.cfg
