@@ -51,6 +51,9 @@ def parse():
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--micro", choices=["gemv", "attn"], default=None,
+                    help="single-kernel microbenchmark on Llama-3-8B layer shapes instead of the decode step")
+    ap.add_argument("--ctx", type=int, default=4096, help="context length of --micro attn")
     return ap.parse_args()
 
 
@@ -349,8 +352,94 @@ def gpu_arm(args):
         dist.destroy_process_group()
 
 
+def micro(args):
+    """Single-kernel microbenchmarks on Llama-3-8B layer shapes (bf16, N(0,1) activations, N(0,0.02)
+    weights): `gemv` = the decode projection on the gate/up weights of 8 distinct layers (1.9 GB, larger
+    than L2); `attn` = decode attention over a [B, ctx] cache.  Prints one JSON line."""
+    import torch
+
+    from jaxml_b200 import _native as N
+
+    N.load()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    s = torch.cuda.current_stream().cuda_stream
+    B = args.batch
+    rup = lambda x, m: (x + m - 1) // m * m
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if args.micro == "gemv":
+        Nn, K, copies = 2 * 14336, 4096, 8
+        Mp = 16 if B <= 16 else (32 if B <= 32 else 64)
+        Np, Kp = rup(Nn, 128), rup(K, 128)
+        ws = [torch.empty(Np * Kp, dtype=torch.bfloat16, device=dev).normal_(0, 0.02) for _ in range(copies)]
+        x = torch.randn(Mp * Kp, device=dev).to(torch.bfloat16)
+        out = torch.zeros(Mp * rup(Nn // 2, 128), dtype=torch.bfloat16, device=dev)
+        wsp = torch.zeros(148 * 2 * 64 * 64, dtype=torch.float32, device=dev)
+        cnt = torch.zeros(Np // 64 + 1, dtype=torch.int32, device=dev)
+        e = N.JxEpilogue()
+        e.kind, e.M, e.N, e.out, e.out_rp = N.JX_EPI_GLU_SILU, B, Nn // 2, out.data_ptr(), Mp
+
+        def run(w):
+            N.call("jx_linear_decode", w.data_ptr(), x.data_ptr(), Np, Kp, B, e, wsp.data_ptr(), wsp.numel(),
+                   cnt.data_ptr(), None, 148, 1, s)
+        for w in ws:
+            run(w)
+        reps = 5
+        torch.cuda.synchronize()
+        start.record()
+        for _ in range(reps):
+            for w in ws:
+                run(w)
+        end.record()
+        torch.cuda.synchronize()
+        ms = start.elapsed_time(end) / (reps * copies)
+        nbytes = 2 * Np * Kp + 2 * Mp * Kp + 2 * B * Nn // 2
+        line = {"micro": "gemv", "shape": f"M={B} N={Nn} K={K}", "us": ms * 1e3, "gbs": nbytes / ms / 1e6}
+    else:
+        ctx, L = args.ctx, 8
+        Hq, Hkv, hd = 32, 8, 128
+        T = rup(ctx + 1, 256)
+        kc = torch.randn(L, B, T, Hkv, hd, device=dev).to(torch.bfloat16)
+        vc = torch.randn_like(kc)
+        q = torch.randn(16 * ((B + 15) // 16), Hq * hd, device=dev).to(torch.bfloat16)
+        pos = torch.full((B,), ctx - 2, dtype=torch.int32, device=dev)
+        Mp = 16 * ((B + 15) // 16) if B <= 32 else 64
+        out = torch.zeros(max(Mp, rup(B, 16)) * Hq * hd, dtype=torch.bfloat16, device=dev)
+        nb = N.LL()
+        N.check(N.load().jx_decode_attention_workspace(B, Hq, hd, T, 0, nb), "ws")
+        wsp = torch.zeros(nb.value // 4 + 1, dtype=torch.float32, device=dev)
+        cnt = torch.zeros(B * Hkv, dtype=torch.int32, device=dev)
+        a = N.JxDAttnArgs()
+        a.B, a.Hq, a.Hkv, a.hd, a.T, a.window, a.cache_rows = B, Hq, Hkv, hd, T, 0, L * B * T
+        a.q, a.k_base, a.v_base, a.len_ptr, a.len_add, a.scale = (q.data_ptr(), kc.data_ptr(), vc.data_ptr(),
+                                                                  pos.data_ptr(), 2, hd ** -0.5)
+        a.out, a.out_rp, a.ws, a.ws_bytes, a.counters = out.data_ptr(), max(Mp, rup(B, 16)), wsp.data_ptr(), wsp.numel() * 4, cnt.data_ptr()
+
+        def run(layer):
+            a.layer_row0 = layer * B * T
+            N.call("jx_decode_attention", a, 1, s)
+        for l in range(L):
+            run(l)
+        reps = 5
+        torch.cuda.synchronize()
+        start.record()
+        for _ in range(reps):
+            for l in range(L):
+                run(l)
+        end.record()
+        torch.cuda.synchronize()
+        ms = start.elapsed_time(end) / (reps * L)
+        nbytes = B * ctx * 2 * Hkv * hd * 2
+        line = {"micro": "attn", "shape": f"B={B} ctx={ctx} Hq={Hq} Hkv={Hkv} hd={hd}", "us": ms * 1e3,
+                "gbs": nbytes / ms / 1e6}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
+    if args.micro:
+        micro(args)
+        return
     if args.impl == "reference":
         reference_arm(args)
         return

@@ -158,7 +158,10 @@ def mha(q, k, v, attention_mask, causal: bool, sliding_window: Optional[int], at
     x = x.masked_fill(neg, float("-inf"))
     all_masked = torch.isneginf(x).all(-1, keepdim=True)
     x = torch.where(all_masked, torch.zeros_like(x), x)
-    p = torch.softmax(x, dim=-1).to(dtype)
+    # jax.nn.softmax: exp(x - max) / sum(exp(x - max)) with a true division (torch's CPU softmax
+    # multiplies by the reciprocal, which rounds differently)
+    e = torch.exp(x - x.max(-1, keepdim=True).values)
+    p = (e / e.sum(-1, keepdim=True)).to(dtype)
     out = torch.einsum("bhst,bthn->bshn", _f32(p), _f32(v)).to(dtype)
     return (out, p) if return_weights else out
 
