@@ -5,8 +5,8 @@
 // and used M times.  The kernel is persistent (one CTA per SM) and splits the flat iteration space
 // (64-row weight block x 128-wide K chunk) evenly across CTAs ("stream-K"), so every SM streams the
 // same number of bytes whatever N and K are.  A producer warp feeds a ring of shared-memory stages
-// with 1-D TMA bulk copies (16 KB of weights + the matching activation chunk per stage); four consumer
-// warps each own 16 of the 64 rows and run mma.sync m16n8k16 over the stage.  A weight block that is
+// with 1-D TMA bulk copies (16 KB of weights + the matching activation chunk per stage); eight consumer
+// warps (16 rows x half the K steps each) run mma.sync m16n8k16 over the stage.  A weight block that is
 // split across CTAs is finished by whichever CTA arrives last: the partial tiles are summed in CTA
 // order (deterministic) and the fused epilogue runs once.
 #include "common.cuh"
@@ -14,7 +14,11 @@
 
 namespace jxb {
 
-constexpr int kGemvThreads = 160;   // warp 0: producer, warps 1..4: consumers
+// warp 0: producer; warps 1..8: consumers.  Consumer warp c owns weight rows [(c%4)*16, +16) of each
+// 64-row block and the K steps [(c/4)*4, +4) of each 128-wide chunk: two warps per SM sub-partition
+// keep enough independent ldmatrix / mma instructions in flight to follow the memory stream.
+constexpr int kGemvConsumers = 256;
+constexpr int kGemvThreads = 32 + kGemvConsumers;
 constexpr int kGemvBN = 64;
 constexpr int kGemvBK = 128;
 constexpr int kTileLd = 68;         // padded float32 row stride of the staging tile
@@ -56,7 +60,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 4);
+      mbar_init(&empty[s], kGemvConsumers / 32);
     }
     sh[0] = 0;
     sh[1] = 0;
@@ -113,8 +117,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
 
   // ---------------- consumers ----------------
   pdl_wait();
-  const int cw = warp - 1;             // owns weight rows [cw*16, cw*16+16) of each 64-row block
-  const int tid = threadIdx.x - 32;    // 0..127
+  const int cw = (warp - 1) & 3;       // owns weight rows [cw*16, cw*16+16) of each 64-row block
+  const int khalf = (warp - 1) >> 2;   // and K steps [khalf*4, khalf*4+4) of each chunk
+  const int tid = threadIdx.x - 32;    // 0..255
   float acc[MT][2][4];
   bool dead = false;
 
@@ -147,7 +152,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
       const uint32_t sX = sW + C::kWBytes;
       const int mi = lane >> 3, r8 = lane & 7;
 #pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
+      for (int kq = 0; kq < 4; ++kq) {
+        const int ks = khalf * 4 + kq;
         uint32_t b0, b1, b2, b3;
         {
           const int rg = cw * 2 + (mi >> 1), kcore = ks * 2 + (mi & 1);
@@ -170,18 +176,33 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
     if (!block_end) continue;
 
     // ---- this CTA's share of weight block nb is done: stage the tile in shared memory ----
+    // (the K-half 0 warps store, then the K-half 1 warps add: a fixed summation order)
 #pragma unroll
-    for (int mt = 0; mt < MT; ++mt)
+    for (int half = 0; half < 2; ++half) {
+      if (khalf == half) {
 #pragma unroll
-      for (int nt = 0; nt < 2; ++nt) {
-        const int r = mt * 16 + (lane >> 2);
-        const int col = cw * 16 + nt * 8 + (lane & 3) * 2;
-        tile[r * kTileLd + col] = acc[mt][nt][0];
-        tile[r * kTileLd + col + 1] = acc[mt][nt][1];
-        tile[(r + 8) * kTileLd + col] = acc[mt][nt][2];
-        tile[(r + 8) * kTileLd + col + 1] = acc[mt][nt][3];
+        for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt) {
+            const int r = mt * 16 + (lane >> 2);
+            const int col = cw * 16 + nt * 8 + (lane & 3) * 2;
+            float* t0 = tile + r * kTileLd + col;
+            float* t1 = tile + (r + 8) * kTileLd + col;
+            if (half == 0) {
+              t0[0] = acc[mt][nt][0];
+              t0[1] = acc[mt][nt][1];
+              t1[0] = acc[mt][nt][2];
+              t1[1] = acc[mt][nt][3];
+            } else {
+              t0[0] += acc[mt][nt][0];
+              t0[1] += acc[mt][nt][1];
+              t1[0] += acc[mt][nt][2];
+              t1[1] += acc[mt][nt][3];
+            }
+          }
       }
-    named_bar_sync(1, 128);
+      named_bar_sync(1, kGemvConsumers);
+    }
 
     const bool whole = started_at_zero && (kk == kc - 1);
     bool do_epi = whole;
@@ -193,18 +214,18 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
         return cc * 2 + (nb == nbf ? 0 : 1);
       };
       float* my = ws + (long long)slot_of(c) * Mp * kGemvBN;
-      for (int idx = tid; idx < Mp * kGemvBN; idx += 128) my[idx] = tile[(idx >> 6) * kTileLd + (idx & 63)];
+      for (int idx = tid; idx < Mp * kGemvBN; idx += kGemvConsumers) my[idx] = tile[(idx >> 6) * kTileLd + (idx & 63)];
       __threadfence();
-      named_bar_sync(1, 128);
+      named_bar_sync(1, kGemvConsumers);
       if (tid == 0) {
         const int prev = atomicAdd(&counters[nb], 1);
         sh[1] = (prev == c_last - c_first) ? 1 : 0;
       }
-      named_bar_sync(1, 128);
+      named_bar_sync(1, kGemvConsumers);
       do_epi = sh[1] != 0;
       if (do_epi) {
         __threadfence();
-        for (int idx = tid; idx < Mp * kGemvBN; idx += 128) {
+        for (int idx = tid; idx < Mp * kGemvBN; idx += kGemvConsumers) {
           float sum = 0.f;
           for (int cc = c_first; cc <= c_last; ++cc) {
             float v;
@@ -218,14 +239,14 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
           tile[(idx >> 6) * kTileLd + (idx & 63)] = sum;
         }
         if (tid == 0) counters[nb] = 0;
-        named_bar_sync(1, 128);
+        named_bar_sync(1, kGemvConsumers);
       }
     }
     if (do_epi && !dead) {
       run_epilogue<bf16>(e, 0, (int)Mp, nb * kGemvBN, kGemvBN,
-                         [&](int m, int j) { return tile[m * kTileLd + j]; }, tid, 128);
+                         [&](int m, int j) { return tile[m * kTileLd + j]; }, tid, kGemvConsumers);
     }
-    named_bar_sync(1, 128);
+    named_bar_sync(1, kGemvConsumers);
   }
 }
 
