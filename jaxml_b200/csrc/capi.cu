@@ -17,6 +17,7 @@ int run_qkv_rope_append(int dtype, const jx_qkv_args& p, bool pdl, cudaStream_t 
 int run_attention_generic(int dtype, const jx_attn_args& p, bool pdl, cudaStream_t stream);
 int run_sample(const jx_sample_args& p, bool pdl, cudaStream_t stream);
 int run_decode_attention(const jx_dattn_args& a, bool pdl, cudaStream_t stream);
+void set_gemv_impl(int impl);
 long long dattn_workspace_bytes(int B, int Hq, int T, int hd, int n_splits);
 int dattn_n_splits(int T, int window);
 int run_sample_finalize(const jx_sample_args& p, const unsigned long long* gathered, int n_shards,
@@ -133,6 +134,12 @@ int jx_norm(const jx_norm_args* args, int dtype, int pdl, void* stream) {
     return fail(JX_ERR_DTYPE, "jx_norm: K128 outputs are bfloat16 only");
   const int rc = run_norm(dtype, *args, pdl != 0, (cudaStream_t)stream);
   if (rc != JX_OK) return rc == JX_ERR_CUDA ? note_cuda("jx_norm") : fail(rc, "jx_norm: unsupported sizes or dtype");
+  return JX_OK;
+}
+
+int jx_set_decode_linear_impl(int impl) {
+  if (impl != 0 && impl != 1) return fail(JX_ERR_ARG, "jx_set_decode_linear_impl: 0 (tcgen05) or 1 (mma.sync)");
+  set_gemv_impl(impl);
   return JX_OK;
 }
 

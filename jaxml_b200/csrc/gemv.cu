@@ -275,10 +275,21 @@ static int launch_gemv(const bf16* W, const bf16* X, long long Np, long long Kp,
   return err == cudaSuccess ? JX_OK : JX_ERR_CUDA;
 }
 
-int gemv_workspace_floats(int grid, int mt) { return grid * 2 * mt * 16 * kGemvBN; }
+// Split-K partial tiles: two slots per CTA of (16 * mt) rows x 128 columns (the larger of the two
+// kernels' weight blocks).
+int gemv_workspace_floats(int grid, int mt) { return grid * 2 * mt * 16 * 128; }
+
+int run_gemv_tc(const bf16* W, const bf16* X, long long Np, long long Kp, int M, const EpiParams& e, float* ws,
+                long long ws_floats, int* counters, int* status, int grid, bool pdl, cudaStream_t stream);
+
+// 0: tcgen05 kernel (default), 1: mma.sync kernel
+static int g_gemv_impl = 0;
+void set_gemv_impl(int impl) { g_gemv_impl = impl; }
 
 int run_gemv(const bf16* W, const bf16* X, long long Np, long long Kp, int M, const EpiParams& e, float* ws,
              long long ws_floats, int* counters, int* status, int grid, bool pdl, cudaStream_t stream) {
+  if (g_gemv_impl == 0 && Np % 128 == 0)
+    return run_gemv_tc(W, X, Np, Kp, M, e, ws, ws_floats, counters, status, grid, pdl, stream);
   if (M <= 0 || M > 64) return JX_ERR_SHAPE;
   if (Np % kGemvBN || Kp % kGemvBK || Np <= 0 || Kp <= 0) return JX_ERR_SHAPE;
   const int mt = M <= 16 ? 1 : (M <= 32 ? 2 : 4);

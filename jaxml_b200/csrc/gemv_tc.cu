@@ -1,0 +1,293 @@
+// Decode projection on the 5th-generation tensor cores (tcgen05 + TMEM): Y[M, N] = X[M, K] . W[N, K]^T
+// for M <= 64 token rows, bfloat16 operands in the K128 tiled layout, float32 accumulation in TMEM.
+//
+// Same work split as gemv.cu (persistent, stream-K over 128-row weight blocks x 128-wide K chunks,
+// deterministic last-arriver fix-up of split blocks, fused epilogue), but the contraction runs as
+// tcgen05.mma with the weight tile as A (M = 128 rows) and the activations as B (N = 16/32/64 tokens),
+// reading both operands straight from shared memory (the K128 layout is the canonical K-major
+// no-swizzle operand layout).  One thread issues all MMAs, so the SM's issue slots stay free and the
+// kernel follows the TMA weight stream.  Warp roles: 0 = TMA producer, 1 = MMA issuer (and TMEM
+// owner), 2..5 = epilogue (one TMEM lane quadrant each).  The accumulator is double-buffered in TMEM so
+// the epilogue of one block overlaps the MMAs of the next.
+#include "common.cuh"
+#include "epilogue.cuh"
+
+namespace jxb {
+
+constexpr int kTcThreads = 192;
+constexpr int kTcBN = 128;
+constexpr int kTcBK = 128;
+
+template <int MT>
+struct TcCfg {
+  static constexpr int N = MT * 16;                       // tokens = MMA N
+  static constexpr int kWBytes = kTcBN * kTcBK * 2;        // 32 KB
+  static constexpr int kXBytes = N * kTcBK * 2;            // 4 / 8 / 16 KB
+  static constexpr int kStageBytes = kWBytes + kXBytes;
+  static constexpr int kStages = MT == 1 ? 6 : (MT == 2 ? 5 : 4);
+  static constexpr int kLd = kTcBN + 4;                    // staging tile [N][128 rows] float32
+  static constexpr int kTileBytes = N * kLd * 4;
+  static constexpr int kBars = 2 * kStages + 4;
+  static constexpr int kSmem = kStages * kStageBytes + kTileBytes + kBars * 8 + 32;
+  static constexpr uint32_t kTmemCols = N <= 16 ? 32 : (N <= 32 ? 64 : 128);
+};
+
+__device__ __forceinline__ long long tc_it_begin(long long total, int G, int c) { return total * c / G; }
+__device__ __forceinline__ int tc_cta_of(long long it, long long total, int G) {
+  return (int)(((it + 1) * G + total - 1) / total) - 1;
+}
+
+template <int MT>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    gemv_tc_kernel(const bf16* __restrict__ W, const bf16* __restrict__ X, long long Np, long long Kp, EpiParams e,
+                   float* __restrict__ ws, int* __restrict__ counters, int* status) {
+  using C = TcCfg<MT>;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  float* tile = reinterpret_cast<float*>(smem + C::kStages * C::kStageBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes + C::kTileBytes);
+  uint64_t* empty = full + C::kStages;
+  uint64_t* accf = empty + C::kStages;      // [2] accumulator ready
+  uint64_t* acce = accf + 2;                // [2] accumulator drained
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce + 2);
+  volatile int* sh = reinterpret_cast<volatile int*>(tmem_slot + 1);   // [0] dead, [1] last-arriver
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_blocks = (int)(Np / kTcBN), kc = (int)(Kp / kTcBK);
+  const long long total = (long long)n_blocks * kc;
+  const int G = gridDim.x, c = blockIdx.x;
+  const long long it0 = tc_it_begin(total, G, c), it1 = tc_it_begin(total, G, c + 1);
+  const int n_it = (int)(it1 - it0);
+  constexpr long long Np8 = 0;  // (unused) keeps the layout formula below explicit
+  (void)Np8;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&accf[b], 1);
+      mbar_init(&acce[b], 4);
+    }
+    sh[0] = 0;
+    sh[1] = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  pdl_trigger();
+
+  if (warp == 0) {
+    // ---------------- TMA producer ----------------
+    if (lane == 0 && n_it > 0) {
+      auto wsrc = [&](long long it) {
+        const long long nb = it / kc, kk = it - nb * kc;
+        return W + ((kk * (Np >> 3) + nb * (kTcBN / 8)) << 10);
+      };
+      auto xsrc = [&](long long it) { return X + (((it % kc) * (C::N >> 3)) << 10); };
+      const int pre = n_it < C::kStages ? n_it : C::kStages;
+      for (int i = 0; i < pre; ++i) {
+        mbar_arrive_expect_tx(&full[i], C::kStageBytes);
+        bulk_g2s(smem + i * C::kStageBytes, wsrc(it0 + i), C::kWBytes, &full[i]);
+      }
+      pdl_wait();
+      for (int i = 0; i < pre; ++i)
+        bulk_g2s(smem + i * C::kStageBytes + C::kWBytes, xsrc(it0 + i), C::kXBytes, &full[i]);
+      int issued = pre;
+      for (int i = pre; i < n_it; ++i) {
+        const int s = i % C::kStages;
+        if (sh[0] || !mbar_wait_bounded(&empty[s], ((i / C::kStages) - 1) & 1)) {
+          set_status(status, JX_ERR_TIMEOUT);
+          sh[0] = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(&full[s], C::kStageBytes);
+        bulk_g2s(smem + s * C::kStageBytes, wsrc(it0 + i), C::kWBytes, &full[s]);
+        bulk_g2s(smem + s * C::kStageBytes + C::kWBytes, xsrc(it0 + i), C::kXBytes, &full[s]);
+        issued = i + 1;
+      }
+      for (int i = (issued > C::kStages ? issued - C::kStages : 0); i < issued; ++i)
+        if (!mbar_wait_bounded(&full[i % C::kStages], (i / C::kStages) & 1)) break;
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0 && n_it > 0) {
+      constexpr uint32_t idesc = umma_idesc_bf16_f32(kTcBN, C::N);
+      long long cur_nb = -1;
+      int blk = -1;
+      uint32_t dcol = 0;
+      bool first = true;
+      for (int i = 0; i < n_it && !sh[0]; ++i) {
+        const long long it = it0 + i;
+        const long long nb = it / kc, kk = it - nb * kc;
+        if (nb != cur_nb) {
+          cur_nb = nb;
+          ++blk;
+          const int buf = blk & 1;
+          if (blk >= 2 && !mbar_wait_bounded(&acce[buf], ((blk >> 1) - 1) & 1)) {
+            set_status(status, JX_ERR_TIMEOUT);
+            sh[0] = 1;
+            break;
+          }
+          tc_fence_after();
+          dcol = (uint32_t)(buf * C::N);
+          first = true;
+        }
+        const int s = i % C::kStages;
+        if (!mbar_wait_bounded(&full[s], (i / C::kStages) & 1)) {
+          set_status(status, JX_ERR_TIMEOUT);
+          sh[0] = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sw = smem_u32(smem + s * C::kStageBytes);
+        const uint32_t sx = sw + C::kWBytes;
+#pragma unroll
+        for (int ks = 0; ks < kTcBK / 16; ++ks) {
+          const uint64_t ad = umma_desc_kmajor(sw + ks * 256, 128, 2048);
+          const uint64_t bd = umma_desc_kmajor(sx + ks * 256, 128, 2048);
+          umma_bf16(tmem + dcol, ad, bd, idesc, (first && ks == 0) ? 0u : 1u);
+        }
+        first = false;
+        umma_commit(&empty[s]);
+        const bool block_end = (kk == kc - 1) || (i == n_it - 1);
+        if (block_end) umma_commit(&accf[blk & 1]);
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 2..5, 128 threads) ----------------
+    pdl_wait();
+    const int tid = threadIdx.x - 64;
+    const int quad = warp & 3;                 // TMEM lane quadrant this warp may read
+    const int row = quad * 32 + lane;          // weight row within the block
+    const long long Mp = C::N;
+    long long cur_nb = -1;
+    int blk = -1;
+    bool started_at_zero = false;
+    for (int i = 0; i < n_it; ++i) {
+      const long long it = it0 + i;
+      const long long nb = it / kc, kk = it - nb * kc;
+      if (nb != cur_nb) {
+        cur_nb = nb;
+        ++blk;
+        started_at_zero = (kk == 0);
+      }
+      const bool block_end = (kk == kc - 1) || (i == n_it - 1);
+      if (!block_end) continue;
+      const int buf = blk & 1;
+      bool ok = !sh[0] && mbar_wait_bounded(&accf[buf], (blk >> 1) & 1);
+      if (!ok) {
+        set_status(status, JX_ERR_TIMEOUT);
+        sh[0] = 1;
+      }
+      tc_fence_after();
+      if (ok) {
+#pragma unroll
+        for (int c0 = 0; c0 < C::N; c0 += 16) {
+          float v[16];
+          tmem_ld16(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(buf * C::N + c0), v);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) tile[(c0 + j) * C::kLd + row] = v[j];
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acce[buf]);
+      named_bar_sync(1, 128);
+
+      const bool whole = started_at_zero && (kk == kc - 1);
+      bool do_epi = whole;
+      if (!whole) {
+        const int c_first = tc_cta_of(nb * kc, total, G), c_last = tc_cta_of(nb * kc + kc - 1, total, G);
+        auto slot_of = [&](int cc) {
+          const int nbf = (int)(tc_it_begin(total, G, cc) / kc);
+          return cc * 2 + (nb == nbf ? 0 : 1);
+        };
+        float* my = ws + (long long)slot_of(c) * Mp * kTcBN;
+        for (int idx = tid; idx < Mp * kTcBN; idx += 128) my[idx] = tile[(idx >> 7) * C::kLd + (idx & 127)];
+        __threadfence();
+        named_bar_sync(1, 128);
+        if (tid == 0) {
+          const int prev = atomicAdd(&counters[nb], 1);
+          sh[1] = (prev == c_last - c_first) ? 1 : 0;
+        }
+        named_bar_sync(1, 128);
+        do_epi = sh[1] != 0;
+        if (do_epi) {
+          __threadfence();
+          for (int idx = tid; idx < Mp * kTcBN; idx += 128) {
+            float sum = 0.f;
+            for (int cc = c_first; cc <= c_last; ++cc) {
+              const float v = (cc == c) ? tile[(idx >> 7) * C::kLd + (idx & 127)]
+                                        : __ldcg(ws + (long long)slot_of(cc) * Mp * kTcBN + idx);
+              sum = (cc == c_first) ? v : sum + v;
+            }
+            tile[(idx >> 7) * C::kLd + (idx & 127)] = sum;
+          }
+          if (tid == 0) counters[nb] = 0;
+          named_bar_sync(1, 128);
+        }
+      }
+      if (do_epi && !sh[0])
+        run_epilogue<bf16>(e, 0, (int)Mp, nb * kTcBN, kTcBN, [&](int m, int j) { return tile[m * C::kLd + j]; },
+                           tid, 128);
+      named_bar_sync(1, 128);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::kTmemCols);
+  }
+}
+
+template <int MT>
+static int launch_gemv_tc(const bf16* W, const bf16* X, long long Np, long long Kp, const EpiParams& e, float* ws,
+                          int* counters, int* status, int grid, bool pdl, cudaStream_t stream) {
+  using C = TcCfg<MT>;
+  static bool configured = false;
+  if (!configured) {
+    if (cudaFuncSetAttribute(gemv_tc_kernel<MT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) != cudaSuccess)
+      return JX_ERR_CUDA;
+    configured = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kTcThreads);
+  cfg.dynamicSmemBytes = C::kSmem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, gemv_tc_kernel<MT>, W, X, Np, Kp, e, ws, counters, status) == cudaSuccess
+             ? JX_OK
+             : JX_ERR_CUDA;
+}
+
+int run_gemv_tc(const bf16* W, const bf16* X, long long Np, long long Kp, int M, const EpiParams& e, float* ws,
+                long long ws_floats, int* counters, int* status, int grid, bool pdl, cudaStream_t stream) {
+  if (M <= 0 || M > 64) return JX_ERR_SHAPE;
+  if (Np % kTcBN || Kp % kTcBK || Np <= 0 || Kp <= 0) return JX_ERR_SHAPE;
+  const int mt = M <= 16 ? 1 : (M <= 32 ? 2 : 4);
+  const long long total = (Np / kTcBN) * (Kp / kTcBK);
+  if (grid <= 0) grid = 148;
+  if (grid > total) grid = (int)total;
+  if ((long long)grid * 2 * mt * 16 * kTcBN > ws_floats) return JX_ERR_ARG;
+  if ((reinterpret_cast<uintptr_t>(W) | reinterpret_cast<uintptr_t>(X)) & 15) return JX_ERR_ARG;
+  switch (mt) {
+    case 1: return launch_gemv_tc<1>(W, X, Np, Kp, e, ws, counters, status, grid, pdl, stream);
+    case 2: return launch_gemv_tc<2>(W, X, Np, Kp, e, ws, counters, status, grid, pdl, stream);
+    default: return launch_gemv_tc<4>(W, X, Np, Kp, e, ws, counters, status, grid, pdl, stream);
+  }
+}
+
+}  // namespace jxb

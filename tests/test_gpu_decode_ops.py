@@ -1,0 +1,147 @@
+"""GPU tests of the decode-step kernels through the C ABI: both decode projection kernels (tcgen05 and
+mma.sync) with their fused epilogues, and the tensor-core decode attention."""
+import pytest
+import torch
+
+from tests.test_gpu_kernels import _assert_rounded_dot, _epi, _n, _pack, _rup, _stream
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(params=[0, 1], ids=["tcgen05", "mma_sync"])
+def impl(request):
+    N = _n()
+    N.call("jx_set_decode_linear_impl", request.param)
+    yield request.param
+    N.call("jx_set_decode_linear_impl", 0)
+
+
+def _ws(N, Np):
+    n = N.LL()
+    N.check(N.load().jx_linear_decode_workspace(148, 64, n), "ws")
+    return (torch.zeros(n.value, dtype=torch.float32, device="cuda"),
+            torch.zeros(Np // 64 + 1, dtype=torch.int32, device="cuda"))
+
+
+@pytest.mark.parametrize("M,Nn,K", [(1, 6144, 4096), (16, 6144, 4096), (16, 4096, 14336), (16, 28672, 4096),
+                                    (33, 512, 1024), (64, 1000, 384), (5, 100, 48), (16, 128256, 4096)])
+def test_linear_decode_store(impl, M, Nn, K):
+    N = _n()
+    torch.manual_seed(0)
+    x = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+    w = (torch.randn(Nn, K, device="cuda") * 0.02).to(torch.bfloat16)
+    Mp = 16 if M <= 16 else (32 if M <= 32 else 64)
+    Np, Kp = _rup(Nn, 128), _rup(K, 128)
+    xp, wp = _pack(N, x, Mp, Kp), _pack(N, w, Np, Kp)
+    out = torch.zeros(M, Nn, dtype=torch.bfloat16, device="cuda")
+    ws, cnt = _ws(N, Np)
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    e = _epi(N, N.JX_EPI_STORE, M, Nn, out, Nn)
+    for grid in (148, 13):
+        out.zero_()
+        N.call("jx_linear_decode", wp.data_ptr(), xp.data_ptr(), Np, Kp, M, e, ws.data_ptr(), ws.numel(),
+               cnt.data_ptr(), status.data_ptr(), grid, 1, _stream())
+        torch.cuda.synchronize()
+        assert int(status.item()) == 0
+        assert int(cnt.abs().sum().item()) == 0
+        _assert_rounded_dot(out, x, w)
+
+
+@pytest.mark.parametrize("M", [3, 16, 40])
+def test_linear_decode_glu_resid_bias(impl, M):
+    """GLU (SiLU) into a K128 output, then a residual projection with bias, both fused."""
+    N = _n()
+    torch.manual_seed(1)
+    F, K, D = 200, 256, 384
+    Mp = 16 if M <= 16 else (32 if M <= 32 else 64)
+    x = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+    g = (torch.randn(F, K, device="cuda") * 0.05).to(torch.bfloat16)
+    u = (torch.randn(F, K, device="cuda") * 0.05).to(torch.bfloat16)
+    F32 = _rup(F, 32)
+    gp = torch.zeros(F32, K, dtype=torch.bfloat16, device="cuda")
+    up = torch.zeros_like(gp)
+    gp[:F], up[:F] = g, u
+    wgu = torch.stack([gp.reshape(-1, 32, K), up.reshape(-1, 32, K)], 1).reshape(2 * F32, K)
+    Kp, Np = _rup(K, 128), _rup(2 * F32, 128)
+    xp, wp = _pack(N, x, Mp, Kp), _pack(N, wgu, Np, Kp)
+    act = torch.zeros(Mp * _rup(F, 128), dtype=torch.bfloat16, device="cuda")
+    ws, cnt = _ws(N, max(Np, 4096))
+    e = _epi(N, N.JX_EPI_GLU_SILU, M, F, act, 0, out_rp=Mp)
+    N.call("jx_linear_decode", wp.data_ptr(), xp.data_ptr(), Np, Kp, M, e, ws.data_ptr(), ws.numel(),
+           cnt.data_ptr(), None, 148, 1, _stream())
+    got = torch.empty(M, F, dtype=torch.bfloat16, device="cuda")
+    N.call("jx_unpack_k128", act.data_ptr(), M, F, Mp, got.data_ptr(), N.JX_BF16, F, _stream())
+    gg = (x.double() @ g.double().T).to(torch.bfloat16).double()
+    uu = (x.double() @ u.double().T).to(torch.bfloat16).double()
+    a = (gg * torch.sigmoid(gg)).to(torch.bfloat16).double()
+    ref = (a * uu).to(torch.bfloat16).double()
+    # inputs of the activation may differ by one bf16 ulp (accumulation order)
+    assert (got.double() - ref).abs().max().item() <= 0.03 * ref.abs().max().item()
+    # down projection with bias and residual, reading the K128 activations
+    wd = (torch.randn(D, F, device="cuda") * 0.05).to(torch.bfloat16)
+    bias = (torch.randn(_rup(D, 128), device="cuda") * 0.1).to(torch.bfloat16)
+    h = torch.randn(M, D, device="cuda").to(torch.bfloat16)
+    h0 = h.clone()
+    Npd, Kpd = _rup(D, 128), _rup(F, 128)
+    wdp = _pack(N, wd, Npd, Kpd)
+    e2 = _epi(N, N.JX_EPI_RESID, M, D, h, D, res=h, ldr=D, bias=bias)
+    N.call("jx_linear_decode", wdp.data_ptr(), act.data_ptr(), Npd, Kpd, M, e2, ws.data_ptr(), ws.numel(),
+           cnt.data_ptr(), None, 148, 1, _stream())
+    torch.cuda.synchronize()
+    y = (got.double() @ wd.double().T).to(torch.bfloat16).double()
+    y = (y + bias[:D].double()).to(torch.bfloat16).double()
+    ref2 = (y + h0.double()).to(torch.bfloat16).double()
+    assert (h.double() - ref2).abs().max().item() <= 0.05 * ref2.abs().max().item()
+
+
+@pytest.mark.parametrize("hd,Hq,Hkv,window", [(128, 32, 8, 0), (256, 16, 8, 0), (256, 16, 8, 100), (64, 8, 8, 0),
+                                               (128, 16, 1, 0), (128, 64, 8, 0)])
+def test_decode_attention_matches_oracle(hd, Hq, Hkv, window):
+    """Tensor-core decode attention vs the oracle's Attention.mha on a padded cache.
+
+    The kernel rounds at the reference's points (scores, scale, probabilities, output), so results agree
+    to about one bf16 ulp.  A q.k accumulated in a different order can round to the neighbouring bf16
+    value (|q.k| ~ 40 here, where one ulp is 0.25), which moves that key's probability by a few percent;
+    such flips are rare, so the bound is one ulp for 99% of the outputs and 2e-3 absolute for all."""
+    from oracle import jaxml_oracle as O
+
+    N = _n()
+    torch.manual_seed(5)
+    B, T, L = 3, 768, 2
+    lens = torch.tensor([513, 200, 767], dtype=torch.int32)      # valid keys after the append
+    kc = torch.randn(L, B, T, Hkv, hd).to(torch.bfloat16)
+    vc = torch.randn(L, B, T, Hkv, hd).to(torch.bfloat16)
+    q = torch.randn(B, Hq, hd).to(torch.bfloat16)
+    scale = hd ** -0.5
+    layer = 1
+    kd, vd, qd = kc.cuda(), vc.cuda(), q.cuda()
+    pos = (lens - 2).cuda()
+    Mp = 16
+    Kp = _rup(Hq * hd, 128)
+    out = torch.zeros(Mp * Kp, dtype=torch.bfloat16, device="cuda")
+    nb = N.LL()
+    N.check(N.load().jx_decode_attention_workspace(B, Hq, hd, T, window, nb), "ws")
+    ws = torch.zeros(nb.value // 4 + 1, dtype=torch.float32, device="cuda")
+    cnt = torch.zeros(B * Hkv, dtype=torch.int32, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    a = N.JxDAttnArgs()
+    a.B, a.Hq, a.Hkv, a.hd, a.T, a.window = B, Hq, Hkv, hd, T, window
+    a.cache_rows, a.layer_row0 = L * B * T, layer * B * T
+    a.q, a.k_base, a.v_base = qd.data_ptr(), kd.data_ptr(), vd.data_ptr()
+    a.len_ptr, a.len_add, a.scale = pos.data_ptr(), 2, scale
+    a.out, a.out_rp = out.data_ptr(), Mp
+    a.ws, a.ws_bytes, a.counters, a.status = ws.data_ptr(), ws.numel() * 4, cnt.data_ptr(), status.data_ptr()
+    mask = torch.arange(T)[None, :] < lens[:, None]
+    want = O.mha(q[:, None], O.repeat_kv(kc[layer], Hq // Hkv), O.repeat_kv(vc[layer], Hq // Hkv), mask, True,
+                 window if window else None, scale)[:, 0].float()
+    ulp = torch.exp2(torch.floor(torch.log2(want.abs().clamp_min(1e-30))) - 7)
+    for _ in range(2):   # twice: the split counters must reset themselves
+        N.call("jx_decode_attention", a, 1, _stream())
+        torch.cuda.synchronize()
+        assert int(status.item()) == 0 and int(cnt.abs().sum().item()) == 0
+        got = torch.empty(B, Hq * hd, dtype=torch.bfloat16, device="cuda")
+        N.call("jx_unpack_k128", out.data_ptr(), B, Hq * hd, Mp, got.data_ptr(), N.JX_BF16, Hq * hd, _stream())
+        got = got.float().cpu().reshape(B, Hq, hd)
+        err = (got - want).abs()
+        assert err.max().item() <= 2e-3, err.max().item()
+        assert (err <= ulp + 1e-6).float().mean().item() >= 0.99
