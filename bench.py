@@ -54,6 +54,8 @@ def parse():
     ap.add_argument("--micro", choices=["gemv", "attn"], default=None,
                     help="single-kernel microbenchmark on Llama-3-8B layer shapes instead of the decode step")
     ap.add_argument("--ctx", type=int, default=4096, help="context length of --micro attn")
+    ap.add_argument("--shape", default="28672,4096", help="N,K of --micro gemv (default: fused gate/up)")
+    ap.add_argument("--gemv-impl", type=int, default=0, help="--micro gemv kernel: 0 by shape, 1 mma.sync, 2 tcgen05")
     return ap.parse_args()
 
 
@@ -368,16 +370,24 @@ def micro(args):
     rup = lambda x, m: (x + m - 1) // m * m
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if args.micro == "gemv":
-        Nn, K, copies = 2 * 14336, 4096, 8
+        Nn, K = (int(v) for v in args.shape.split(","))
+        glu = Nn == 2 * 14336 and K == 4096
+        copies = max(2, min(64, int(2e9 // (Nn * K * 2))))       # distinct weight copies: > L2 in total
+        N.call("jx_set_decode_linear_impl", args.gemv_impl)
         Mp = 16 if B <= 16 else (32 if B <= 32 else 64)
         Np, Kp = rup(Nn, 128), rup(K, 128)
         ws = [torch.empty(Np * Kp, dtype=torch.bfloat16, device=dev).normal_(0, 0.02) for _ in range(copies)]
         x = torch.randn(Mp * Kp, device=dev).to(torch.bfloat16)
-        out = torch.zeros(Mp * rup(Nn // 2, 128), dtype=torch.bfloat16, device=dev)
-        wsp = torch.zeros(148 * 2 * 64 * 64, dtype=torch.float32, device=dev)
+        out = torch.zeros(Mp * rup(Nn, 128), dtype=torch.bfloat16, device=dev)
+        nws = N.LL()
+        N.check(N.load().jx_linear_decode_workspace(148, B, nws), "ws")
+        wsp = torch.zeros(nws.value, dtype=torch.float32, device=dev)
         cnt = torch.zeros(Np // 64 + 1, dtype=torch.int32, device=dev)
         e = N.JxEpilogue()
-        e.kind, e.M, e.N, e.out, e.out_rp = N.JX_EPI_GLU_SILU, B, Nn // 2, out.data_ptr(), Mp
+        if glu:
+            e.kind, e.M, e.N, e.out, e.out_rp = N.JX_EPI_GLU_SILU, B, Nn // 2, out.data_ptr(), Mp
+        else:
+            e.kind, e.M, e.N, e.out, e.ldo = N.JX_EPI_STORE, B, Nn, out.data_ptr(), Nn
 
         def run(w):
             N.call("jx_linear_decode", w.data_ptr(), x.data_ptr(), Np, Kp, B, e, wsp.data_ptr(), wsp.numel(),
@@ -393,8 +403,9 @@ def micro(args):
         end.record()
         torch.cuda.synchronize()
         ms = start.elapsed_time(end) / (reps * copies)
-        nbytes = 2 * Np * Kp + 2 * Mp * Kp + 2 * B * Nn // 2
-        line = {"micro": "gemv", "shape": f"M={B} N={Nn} K={K}", "us": ms * 1e3, "gbs": nbytes / ms / 1e6}
+        nbytes = 2 * Nn * K + 2 * B * K + 2 * B * (Nn // 2 if glu else Nn)
+        line = {"micro": "gemv", "impl": ["by-shape", "mma.sync", "tcgen05"][args.gemv_impl], "shape": f"M={B} N={Nn} K={K}",
+                "us": ms * 1e3, "gbs": nbytes / ms / 1e6}
     else:
         ctx, L = args.ctx, 8
         Hq, Hkv, hd = 32, 8, 128

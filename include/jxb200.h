@@ -196,7 +196,8 @@ int jx_norm(const jx_norm_args* args, int dtype, int pdl, void* stream);
 /* Decode projection (M <= 64): DenseGeneral (nn/linear.py:119-182) with fused epilogue.  W and X are
  * bfloat16 K128 ([Np, Kp] and [16*ceil(M/16) (or 64), Kp]); workspace from jx_linear_decode_workspace. */
 int jx_linear_decode_workspace(int grid, int M, long long* floats_out);
-/* Kernel behind jx_linear_decode: 0 = tcgen05/TMEM (default, needs Np % 128 == 0), 1 = mma.sync. */
+/* Kernel behind jx_linear_decode: 0 = by shape (default: tcgen05/TMEM when Np/128 >= grid), 1 = mma.sync,
+ * 2 = tcgen05/TMEM (needs Np % 128 == 0). */
 int jx_set_decode_linear_impl(int impl);
 int jx_linear_decode(const void* W, const void* X, long long Np, long long Kp, int M, const jx_epilogue* epi,
                      float* ws, long long ws_floats, int* counters, int* status, int grid, int pdl, void* stream);

@@ -138,7 +138,7 @@ int jx_norm(const jx_norm_args* args, int dtype, int pdl, void* stream) {
 }
 
 int jx_set_decode_linear_impl(int impl) {
-  if (impl != 0 && impl != 1) return fail(JX_ERR_ARG, "jx_set_decode_linear_impl: 0 (tcgen05) or 1 (mma.sync)");
+  if (impl < 0 || impl > 2) return fail(JX_ERR_ARG, "jx_set_decode_linear_impl: 0 (by shape), 1 (mma.sync), 2 (tcgen05)");
   set_gemv_impl(impl);
   return JX_OK;
 }

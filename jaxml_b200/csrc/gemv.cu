@@ -225,18 +225,15 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
       do_epi = sh[1] != 0;
       if (do_epi) {
         __threadfence();
-        for (int idx = tid; idx < Mp * kGemvBN; idx += kGemvConsumers) {
-          float sum = 0.f;
-          for (int cc = c_first; cc <= c_last; ++cc) {
-            float v;
-            if (cc == c) {
-              v = tile[(idx >> 6) * kTileLd + (idx & 63)];
-            } else {
-              v = __ldcg(ws + (long long)slot_of(cc) * Mp * kGemvBN + idx);
-            }
-            sum = (cc == c_first) ? v : sum + v;
+        // Sum every contribution (this CTA's too, already in the workspace) in CTA order; the slot
+        // address is computed once per contributor, the running sums stay in the tile.
+        for (int cc = c_first; cc <= c_last; ++cc) {
+          const float* src = ws + (long long)slot_of(cc) * Mp * kGemvBN;
+          for (int idx = tid; idx < Mp * kGemvBN; idx += kGemvConsumers) {
+            float* t = tile + (idx >> 6) * kTileLd + (idx & 63);
+            const float v = __ldcg(src + idx);
+            *t = (cc == c_first) ? v : *t + v;
           }
-          tile[(idx >> 6) * kTileLd + (idx & 63)] = sum;
         }
         if (tid == 0) counters[nb] = 0;
         named_bar_sync(1, kGemvConsumers);
@@ -282,14 +279,18 @@ int gemv_workspace_floats(int grid, int mt) { return grid * 2 * mt * 16 * 128; }
 int run_gemv_tc(const bf16* W, const bf16* X, long long Np, long long Kp, int M, const EpiParams& e, float* ws,
                 long long ws_floats, int* counters, int* status, int grid, bool pdl, cudaStream_t stream);
 
-// 0: tcgen05 kernel (default), 1: mma.sync kernel
+// 0: by shape (default), 1: mma.sync kernel, 2: tcgen05 kernel.
+// By shape: the tcgen05 kernel streams the large projections fastest (one thread issues every MMA),
+// but its 128-row blocks leave too few blocks per SM on the small ones, where the split-block
+// fix-up dominates; it is used once there are at least as many 128-row blocks as SMs.
 static int g_gemv_impl = 0;
 void set_gemv_impl(int impl) { g_gemv_impl = impl; }
 
 int run_gemv(const bf16* W, const bf16* X, long long Np, long long Kp, int M, const EpiParams& e, float* ws,
              long long ws_floats, int* counters, int* status, int grid, bool pdl, cudaStream_t stream) {
-  if (g_gemv_impl == 0 && Np % 128 == 0)
-    return run_gemv_tc(W, X, Np, Kp, M, e, ws, ws_floats, counters, status, grid, pdl, stream);
+  const bool tc_ok = Np % 128 == 0;
+  const bool use_tc = tc_ok && (g_gemv_impl == 2 || (g_gemv_impl == 0 && Np / 128 >= (grid > 0 ? grid : 148)));
+  if (use_tc) return run_gemv_tc(W, X, Np, Kp, M, e, ws, ws_floats, counters, status, grid, pdl, stream);
   if (M <= 0 || M > 64) return JX_ERR_SHAPE;
   if (Np % kGemvBN || Kp % kGemvBK || Np <= 0 || Kp <= 0) return JX_ERR_SHAPE;
   const int mt = M <= 16 ? 1 : (M <= 32 ? 2 : 4);

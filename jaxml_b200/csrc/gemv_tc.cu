@@ -27,7 +27,7 @@ struct TcCfg {
   static constexpr int kStages = MT == 1 ? 6 : (MT == 2 ? 5 : 4);
   static constexpr int kLd = kTcBN + 4;                    // staging tile [N][128 rows] float32
   static constexpr int kTileBytes = N * kLd * 4;
-  static constexpr int kBars = 2 * kStages + 4;
+  static constexpr int kBars = 2 * kStages + 5;
   static constexpr int kSmem = kStages * kStageBytes + kTileBytes + kBars * 8 + 32;
   static constexpr uint32_t kTmemCols = N <= 16 ? 32 : (N <= 32 ? 64 : 128);
 };
@@ -48,7 +48,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint64_t* empty = full + C::kStages;
   uint64_t* accf = empty + C::kStages;      // [2] accumulator ready
   uint64_t* acce = accf + 2;                // [2] accumulator drained
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acce + 2);
+  uint64_t* done = acce + 2;                // epilogue finished with TMEM
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
   volatile int* sh = reinterpret_cast<volatile int*>(tmem_slot + 1);   // [0] dead, [1] last-arriver
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -69,6 +70,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_init(&accf[b], 1);
       mbar_init(&acce[b], 4);
     }
+    mbar_init(done, 4);
     sh[0] = 0;
     sh[1] = 0;
     fence_barrier_init();
@@ -221,14 +223,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         do_epi = sh[1] != 0;
         if (do_epi) {
           __threadfence();
-          for (int idx = tid; idx < Mp * kTcBN; idx += 128) {
-            float sum = 0.f;
-            for (int cc = c_first; cc <= c_last; ++cc) {
-              const float v = (cc == c) ? tile[(idx >> 7) * C::kLd + (idx & 127)]
-                                        : __ldcg(ws + (long long)slot_of(cc) * Mp * kTcBN + idx);
-              sum = (cc == c_first) ? v : sum + v;
+          // Sum every contribution (this CTA's too, already in the workspace) in CTA order.  Each
+          // thread owns the same elements for every contributor, so the running sums live in the
+          // tile without further synchronisation; the slot address is computed once per contributor.
+          for (int cc = c_first; cc <= c_last; ++cc) {
+            const float* src = ws + (long long)slot_of(cc) * Mp * kTcBN;
+            for (int idx = tid; idx < Mp * kTcBN; idx += 128) {
+              float* t = tile + (idx >> 7) * C::kLd + (idx & 127);
+              const float v = __ldcg(src + idx);
+              *t = (cc == c_first) ? v : *t + v;
             }
-            tile[(idx >> 7) * C::kLd + (idx & 127)] = sum;
           }
           if (tid == 0) counters[nb] = 0;
           named_bar_sync(1, 128);
@@ -240,9 +244,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       named_bar_sync(1, 128);
     }
   }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
+  // Teardown without a CTA-wide barrier (the roles above leave their warps at different points): the
+  // epilogue warps arrive on `done` when their last TMEM read is complete; warp 1 waits for that and
+  // frees TMEM.  The producer warp just exits.
+  __syncwarp();
+  if (warp >= 2) {
+    tc_fence_before();
+    if (lane == 0) mbar_arrive(done);
+  } else if (warp == 1) {
+    if (!mbar_wait_bounded(done, 0)) set_status(status, JX_ERR_TIMEOUT);
     tc_fence_after();
     tmem_dealloc(tmem, C::kTmemCols);
   }

@@ -8,7 +8,7 @@ from tests.test_gpu_kernels import _assert_rounded_dot, _epi, _n, _pack, _rup, _
 pytestmark = pytest.mark.gpu
 
 
-@pytest.fixture(params=[0, 1], ids=["tcgen05", "mma_sync"])
+@pytest.fixture(params=[2, 1], ids=["tcgen05", "mma_sync"])
 def impl(request):
     N = _n()
     N.call("jx_set_decode_linear_impl", request.param)
