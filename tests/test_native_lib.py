@@ -29,4 +29,5 @@ def test_argument_errors_are_reported_without_a_gpu():
     assert b"null" in lib.jx_last_error()
     out = N.LL()
     assert lib.jx_linear_decode_workspace(148, 65, out) == N.JX_ERR_SHAPE
-    assert lib.jx_linear_decode_workspace(148, 16, out) == N.JX_OK and out.value == 148 * 2 * 16 * 64
+    # two partial-tile slots per CTA of 16 rows x 128 columns
+    assert lib.jx_linear_decode_workspace(148, 16, out) == N.JX_OK and out.value == 148 * 2 * 16 * 128
