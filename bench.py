@@ -258,7 +258,15 @@ def gpu_arm(args):
     key, sub = prng.split(prng.prng_key(0))
     ids_d = prompt.to(dev)
     rt.reset(torch.ones(B, P, dtype=torch.bool, device=dev), key, sub, n_new)
+    rt.prefill(ids_d, True, 1.0)                     # warm (first use allocates prefill buffers)
+    rt.reset(torch.ones(B, P, dtype=torch.bool, device=dev), key, sub, n_new)
+    torch.cuda.synchronize()
+    pf0, pf1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    pf0.record()
     rt.prefill(ids_d, True, 1.0)
+    pf1.record()
+    torch.cuda.synchronize()
+    prefill_ms = pf0.elapsed_time(pf1)
     rt.decode_step(True, 1.0)          # eager step: warms every kernel
     graph = rt.capture_decode(True, 1.0)
     for _ in range(args.warmup - 1):
@@ -329,7 +337,8 @@ def gpu_arm(args):
         line = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
-            "p50_step_ms": statistics.median(step_ms), "higher_is_better": True, "scaling": "strong",
+            "p50_step_ms": statistics.median(step_ms), "prefill_ms": prefill_ms,
+            "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (uniform-random prompt ids, N(0,0.02) random-init weights, seed 0)",
             "config": {"workload": "llama3-8b-shape bf16 greedy decode, batch 16, prompt 512, 256 new tokens",

@@ -145,6 +145,25 @@ typedef struct jx_dattn_args {
   int* status;
 } jx_dattn_args;
 
+/* Prefill attention on tensor cores: S query tokens per row (rows b*S + s), head_dim 64/128/256. */
+typedef struct jx_pattn_args {
+  int B, S, Hq, Hkv, hd;
+  int T;                 /* cache slots per row (S <= T) */
+  int window;            /* sliding window, 0 = none */
+  int _pad0;
+  long long cache_rows;  /* rows of the whole cache allocation viewed as [cache_rows, Hkv*hd] */
+  long long layer_row0;  /* first row of this layer (layer * B * T) */
+  const void* q;         /* [B*S, Hq, hd] */
+  const void* k_base;
+  const void* v_base;
+  const int* len_ptr;    /* [B]: valid keys = len_ptr[b] + len_add (right-padded prompt mask) */
+  int len_add;
+  float scale;
+  void* out;             /* K128 output [out_rp rows, Hq*hd] */
+  long long out_rp;
+  int* status;
+} jx_pattn_args;
+
 typedef struct jx_sample_args {
   int B, V;              /* rows, local vocabulary columns */
   const void* logits;
@@ -220,6 +239,10 @@ int jx_attention(const jx_attn_args* args, int dtype, int pdl, void* stream);
  * the valid keys, TMA-staged K/V tiles, exact reference rounding (see csrc/attention_decode.cu). */
 int jx_decode_attention_workspace(int B, int Hq, int hd, int T, int window, long long* bytes_out);
 int jx_decode_attention(const jx_dattn_args* args, int pdl, void* stream);
+
+/* Attention.mha prefill branch (causal + window + padding masks, nn/attention.py:321-400) for bf16
+ * caches on tensor cores, exact reference rounding (see csrc/attention_prefill.cu). */
+int jx_prefill_attention(const jx_pattn_args* args, int pdl, void* stream);
 
 /* greedy_fn / categorical sampling (inference_engine/sampling.py:75-188) + end-of-step bookkeeping. */
 int jx_sample(const jx_sample_args* args, int pdl, void* stream);

@@ -60,6 +60,12 @@ class JxDAttnArgs(ctypes.Structure):
                 ("status", P)]
 
 
+class JxPAttnArgs(ctypes.Structure):
+    _fields_ = [("B", I), ("S", I), ("Hq", I), ("Hkv", I), ("hd", I), ("T", I), ("window", I), ("_pad0", I),
+                ("cache_rows", LL), ("layer_row0", LL), ("q", P), ("k_base", P), ("v_base", P), ("len_ptr", P),
+                ("len_add", I), ("scale", F), ("out", P), ("out_rp", LL), ("status", P)]
+
+
 class JxSampleArgs(ctypes.Structure):
     _fields_ = [("B", I), ("V", I), ("logits", P), ("ld", LL), ("dtype", I), ("greedy", I), ("temp", F),
                 ("chunk", I), ("vocab_offset", LL), ("vocab_total", LL), ("rng", P), ("gumbel_tab", P), ("ws", P),
@@ -85,6 +91,7 @@ _PROTOS = {
     "jx_attention": (I, [ctypes.POINTER(JxAttnArgs), I, I, P]),
     "jx_decode_attention_workspace": (I, [I, I, I, I, I, ctypes.POINTER(LL)]),
     "jx_decode_attention": (I, [ctypes.POINTER(JxDAttnArgs), I, P]),
+    "jx_prefill_attention": (I, [ctypes.POINTER(JxPAttnArgs), I, P]),
     "jx_sample": (I, [ctypes.POINTER(JxSampleArgs), I, P]),
     "jx_sample_finalize": (I, [ctypes.POINTER(JxSampleArgs), P, I, P]),
 }

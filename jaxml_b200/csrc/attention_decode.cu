@@ -334,19 +334,25 @@ static PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
   return fn;
 }
 
-// 2-D bf16 tensor map over a row-major [rows, cols] matrix with a 64x64 box and 128-byte swizzle.
-int make_tmap_2d_bf16(CUtensorMap* map, const void* base, long long rows, long long cols, long long row_stride_elems) {
+// 2-D bf16 tensor map over a row-major [rows, cols] matrix with a [box_rows x 64] box and 128-byte swizzle.
+int make_tmap_2d_bf16_box(CUtensorMap* map, const void* base, long long rows, long long cols,
+                          long long row_stride_elems, int box_rows) {
   auto enc = tmap_encoder();
   if (!enc) return JX_ERR_CUDA;
   if ((reinterpret_cast<uintptr_t>(base) & 15) || ((row_stride_elems * 2) & 15) || cols % 64) return JX_ERR_ARG;
+  if (box_rows <= 0 || box_rows > 256) return JX_ERR_ARG;
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)(row_stride_elems * 2)};
-  cuuint32_t box[2] = {64, 64};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? JX_OK : JX_ERR_ARG;
+}
+
+int make_tmap_2d_bf16(CUtensorMap* map, const void* base, long long rows, long long cols, long long row_stride_elems) {
+  return make_tmap_2d_bf16_box(map, base, rows, cols, row_stride_elems, 64);
 }
 
 long long dattn_workspace_bytes(int B, int Hq, int T, int hd, int n_splits) {

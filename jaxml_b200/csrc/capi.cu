@@ -18,6 +18,7 @@ int run_attention_generic(int dtype, const jx_attn_args& p, bool pdl, cudaStream
 int run_sample(const jx_sample_args& p, bool pdl, cudaStream_t stream);
 int run_decode_attention(const jx_dattn_args& a, bool pdl, cudaStream_t stream);
 void set_gemv_impl(int impl);
+int run_prefill_attention(const jx_pattn_args& a, bool pdl, cudaStream_t stream);
 long long dattn_workspace_bytes(int B, int Hq, int T, int hd, int n_splits);
 int dattn_n_splits(int T, int window);
 int run_sample_finalize(const jx_sample_args& p, const unsigned long long* gathered, int n_shards,
@@ -211,6 +212,15 @@ int jx_decode_attention(const jx_dattn_args* args, int pdl, void* stream) {
   if (rc != JX_OK)
     return fail(rc, "jx_decode_attention: head_dim must be 64/128/256, Hq/Hkv <= 16, workspace large enough, "
                     "16-byte aligned q/cache");
+  return JX_OK;
+}
+
+int jx_prefill_attention(const jx_pattn_args* args, int pdl, void* stream) {
+  if (!args || !args->q || !args->k_base || !args->v_base || !args->out || !args->len_ptr)
+    return fail(JX_ERR_ARG, "jx_prefill_attention: null pointer");
+  const int rc = run_prefill_attention(*args, pdl != 0, (cudaStream_t)stream);
+  if (rc == JX_ERR_CUDA) return note_cuda("jx_prefill_attention");
+  if (rc != JX_OK) return fail(rc, "jx_prefill_attention: head_dim must be 64/128/256, Hq % Hkv == 0, S <= T");
   return JX_OK;
 }
 

@@ -415,6 +415,8 @@ class DecoderRuntime:
             self._qkv_rope_append(acts, li, lw, S, decode)
             if decode and self.fast_attn:
                 self._decode_attention(acts, li, lw)
+            elif not decode and self.fast_attn and S > 1:
+                self._prefill_attention(acts, li, lw, S)
             else:
                 self._generic_attention(acts, li, lw, S, decode)
             self._o_and_mlp(acts, lw, nx)
@@ -464,6 +466,21 @@ class DecoderRuntime:
         a.counters, a.status = ptr(self.attn_counters), ptr(self.status)
         self._launches += 2
         N.check(N.load().jx_decode_attention(a, 1, self.stream_ptr()), "jx_decode_attention")
+
+    def _prefill_attention(self, acts, li, lw, S):
+        W, cfg = self.w, self.w.cfg
+        a = N.JxPAttnArgs()
+        a.B, a.S, a.Hq, a.Hkv, a.hd, a.T = self.B, S, W.Hq, W.Hkv, W.hd, self.T
+        a.window = cfg.sliding_window if lw.sliding else 0
+        a.cache_rows = self.k_cache.shape[0] * self.B * self.T
+        a.layer_row0 = li * self.B * self.T
+        a.q, a.k_base, a.v_base = ptr(acts["q"]), ptr(self.k_cache), ptr(self.v_cache)
+        a.len_ptr, a.len_add = ptr(self.pos_id), 1
+        a.scale = cfg.attn_scale
+        a.out, a.out_rp = ptr(acts["attn"]), acts["Mp"]
+        a.status = ptr(self.status)
+        self._launches += 1
+        N.check(N.load().jx_prefill_attention(a, 1, self.stream_ptr()), "jx_prefill_attention")
 
     def _o_and_mlp(self, acts, lw, nx):
         """o_proj, residual / post-attention norm, MLP, residual and the next layer's input norm."""
