@@ -163,17 +163,21 @@ __global__ void __launch_bounds__(128) pattn_kernel(const __grid_constant__ CUte
           tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, 1));
           tm = fmaxf(tm, __shfl_xor_sync(0xffffffffu, tm, 2));
           const float mn = fmaxf(m[hh], tm);
-          if (mn == -INFINITY) continue;
+          // Rows differ in whether they see any key of this tile (sliding window), so every lane
+          // must still reach the full-warp shuffles below: guard the arithmetic, not the shuffles.
+          const bool live = mn != -INFINITY;
           float ts = 0.f;
 #pragma unroll
           for (int n = 0; n < NS; ++n) {
-            if (sacc[n][hh * 2] != -INFINITY) ts += expf(sacc[n][hh * 2] - mn);
-            if (sacc[n][hh * 2 + 1] != -INFINITY) ts += expf(sacc[n][hh * 2 + 1] - mn);
+            if (live && sacc[n][hh * 2] != -INFINITY) ts += expf(sacc[n][hh * 2] - mn);
+            if (live && sacc[n][hh * 2 + 1] != -INFINITY) ts += expf(sacc[n][hh * 2 + 1] - mn);
           }
           ts += __shfl_xor_sync(0xffffffffu, ts, 1);
           ts += __shfl_xor_sync(0xffffffffu, ts, 2);
-          l[hh] = (m[hh] == -INFINITY ? 0.f : l[hh] * expf(m[hh] - mn)) + ts;
-          m[hh] = mn;
+          if (live) {
+            l[hh] = (m[hh] == -INFINITY ? 0.f : l[hh] * expf(m[hh] - mn)) + ts;
+            m[hh] = mn;
+          }
         }
       } else {
         // probabilities rounded as the reference does, then O += P V
