@@ -221,6 +221,16 @@ int jx_set_decode_linear_impl(int impl);
 int jx_linear_decode(const void* W, const void* X, long long Np, long long Kp, int M, const jx_epilogue* epi,
                      float* ws, long long ws_floats, int* counters, int* status, int grid, int pdl, void* stream);
 
+/* jx_linear_decode for callers that cannot allocate device memory (no counterpart in the reference):
+ * for example a handler running inside a host framework's custom-call / FFI hook, which may only use
+ * the buffers it is handed, or a plugin that must not call cudaMalloc.  The split-K scratch is a
+ * fixed array compiled into this library (2.3 MiB of every GPU that loads it, until exit), so the
+ * sizes are capped: M <= 16 token rows, Np <= 262080 weight rows, at most 148 CTAs; larger requests fail
+ * with JX_ERR_SHAPE.  The first call on a device looks the array's address up (make it before any
+ * stream capture).  All calls share the array: calls that overlap on the GPU race and must not. */
+int jx_linear_decode_noalloc(const void* W, const void* X, long long Np, long long Kp, int M, const jx_epilogue* epi,
+                             int* status, int grid, int pdl, void* stream);
+
 /* Prefill projection (any M): bfloat16 K128 operands X [Mp, Kp], W [Np, Kp] (Mp, Np multiples of 128). */
 int jx_linear_prefill(const void* X, const void* W, long long Mp, long long Np, long long Kp, const jx_epilogue* epi,
                       int* status, int pdl, void* stream);
