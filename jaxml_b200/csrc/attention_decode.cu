@@ -22,6 +22,7 @@ namespace jxb {
 
 constexpr int kDaKeys = 128;        // keys per CTA
 constexpr int kDaTile = 64;         // keys per TMA tile
+constexpr int kPLd = kDaKeys + 8;   // padded row stride (bf16) of the probability tile: conflict-free ldmatrix
 
 struct DAttnParams {
   int B, Hq, Hkv, n_rep, T, n_splits;
@@ -213,6 +214,7 @@ __global__ void __launch_bounds__(128) dattn_pv_kernel(const __grid_constant__ C
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + 2 * TILE_BYTES);
   float* Ms = reinterpret_cast<float*>(bar + 2);   // [16]
   float* Ls = Ms + 16;                             // [16]
+  bf16* ptile = reinterpret_cast<bf16*>(Ls + 16);  // [16][kPLd]
   __shared__ int last_flag;
 
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
@@ -254,13 +256,18 @@ __global__ void __launch_bounds__(128) dattn_pv_kernel(const __grid_constant__ C
 
   const int mi = lane >> 3, r8 = lane & 7;
   const int r_lo = lane >> 2, r_hi = r_lo + 8;
-  const float M0 = Ms[r_lo], L0 = Ls[r_lo], M1 = Ms[r_hi], L1 = Ls[r_hi];
-  const float* sc0 = p.sc + ((long long)b * p.Hq + kvh * p.n_rep + r_lo) * p.T;
-  const float* sc1 = p.sc + ((long long)b * p.Hq + kvh * p.n_rep + r_hi) * p.T;
-  auto prob = [&](const float* sc, int row, float M, float L, int t) -> float {
-    if (row >= p.n_rep || t >= t1) return 0.f;
-    return rnd<bf16>(expf(__ldcg(sc + t) - M) / L);
-  };
+  // Probabilities of this CTA's keys, computed once (coalesced score reads) into a padded bf16 tile
+  // [16 rows][kDaKeys + 8] that every warp reads with ldmatrix.
+  for (int idx = threadIdx.x; idx < 16 * kDaKeys; idx += 128) {
+    const int row = idx / kDaKeys, k = idx % kDaKeys, t = t0 + k;
+    float pv = 0.f;
+    if (row < p.n_rep && t < t1) {
+      const float s = __ldcg(p.sc + ((long long)b * p.Hq + kvh * p.n_rep + row) * p.T + t);
+      pv = rnd<bf16>(expf(s - Ms[row]) / Ls[row]);
+    }
+    ptile[row * kPLd + k] = __float2bfloat16_rn(pv);
+  }
+  __syncthreads();
   float acc[NT][4] = {};
   bool ok = true;
   for (int i = 0; i < n_tiles && ok; ++i) {
@@ -272,11 +279,11 @@ __global__ void __launch_bounds__(128) dattn_pv_kernel(const __grid_constant__ C
     const uint32_t vb = smem_u32(vtile + i * TILE_BYTES);
 #pragma unroll
     for (int kk = 0; kk < kDaTile / 16; ++kk) {
-      const int tb = t0 + i * kDaTile + kk * 16 + (lane & 3) * 2;
-      const uint32_t a0 = pack_bf16x2(prob(sc0, r_lo, M0, L0, tb), prob(sc0, r_lo, M0, L0, tb + 1));
-      const uint32_t a1 = pack_bf16x2(prob(sc1, r_hi, M1, L1, tb), prob(sc1, r_hi, M1, L1, tb + 1));
-      const uint32_t a2 = pack_bf16x2(prob(sc0, r_lo, M0, L0, tb + 8), prob(sc0, r_lo, M0, L0, tb + 9));
-      const uint32_t a3 = pack_bf16x2(prob(sc1, r_hi, M1, L1, tb + 8), prob(sc1, r_hi, M1, L1, tb + 9));
+      uint32_t a0, a1, a2, a3;
+      {
+        const int row = (mi & 1) * 8 + r8, col = i * kDaTile + kk * 16 + (mi >> 1) * 8;
+        ldsm_x4(smem_u32(ptile + row * kPLd + col), a0, a1, a2, a3);
+      }
 #pragma unroll
       for (int n16 = 0; n16 < NT / 2; ++n16) {
         uint32_t b0, b1, b2, b3;
@@ -370,7 +377,7 @@ int dattn_n_splits(int T, int window) {
 template <int HD>
 static int launch_dattn(const CUtensorMap& km, const CUtensorMap& vm, const DAttnParams& p, bool pdl, cudaStream_t s) {
   const int smem_a = 1024 + 2 * kDaTile * HD * 2 + (HD / 64) * 2048 + 16 + 4 * 16 * 4;
-  const int smem_b = 1024 + 2 * kDaTile * HD * 2 + 16 + 32 * 4;
+  const int smem_b = 1024 + 2 * kDaTile * HD * 2 + 16 + 32 * 4 + 16 * kPLd * 2;
   static bool configured = false;
   if (!configured) {
     if (cudaFuncSetAttribute(dattn_scores_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_a) != cudaSuccess ||

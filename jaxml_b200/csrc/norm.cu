@@ -145,8 +145,144 @@ __global__ void __launch_bounds__(NT) norm_kernel(NormArgs p) {
   }
 }
 
+// ------------------------------------------------------------------------------------------------
+// bfloat16 rows with d % 8 == 0 and d <= 8192: one thread per 8 consecutive elements (a 16-byte vector),
+// the whole row in registers, one pass, 16-byte loads and stores (a K128 output keeps 8 consecutive K
+// elements of a row contiguous).  Same semantics as norm_kernel.
+// ------------------------------------------------------------------------------------------------
+__device__ __forceinline__ float vblock_sum(float v, float* red) {
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = (blockDim.x + 31) >> 5;
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = lane < nw ? red[lane] : 0.f;
+  for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+  return t;
+}
+
+__device__ __forceinline__ void vload8(const bf16* p, float* v) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+__device__ __forceinline__ void vstore8(bf16* p, const float* v) {
+  uint4 u;
+  u.x = pack_bf16x2(v[0], v[1]);
+  u.y = pack_bf16x2(v[2], v[3]);
+  u.z = pack_bf16x2(v[4], v[5]);
+  u.w = pack_bf16x2(v[6], v[7]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+
+// Normalise the 8 values of this thread (the row is spread over the block).
+__device__ __forceinline__ void vnormalize(const float* x, float* y, int d, int kind, float eps, const bf16* w,
+                                           const bf16* b, int j0, float* red) {
+  float wv[8], bv[8];
+  vload8(w + j0, wv);
+  if (b) vload8(b + j0, bv);
+  if (kind == JX_NORM_LAYER) {
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s += x[i];
+    const float mean = vblock_sum(s, red) / (float)d;
+    float v = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v += (x[i] - mean) * (x[i] - mean);
+    const float den = sqrtf(vblock_sum(v, red) / (float)d + eps);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) y[i] = rnd<bf16>((x[i] - mean) / den * wv[i] + (b ? bv[i] : 0.f));
+    return;
+  }
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) s += x[i] * x[i];
+  const float den = sqrtf(vblock_sum(s, red) / (float)d + eps);
+  if (kind == JX_NORM_RMS) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) y[i] = rnd<bf16>(wv[i] * rnd<bf16>(x[i] / den));
+  } else {
+    const float inv = 1.0f / den;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) y[i] = rnd<bf16>((wv[i] + 1.0f) * (x[i] * inv));
+  }
+}
+
+__global__ void __launch_bounds__(1024) norm_vec_kernel(NormArgs p) {
+  __shared__ float red[32];
+  const long long m = blockIdx.x;
+  const int j0 = threadIdx.x * 8;
+  pdl_wait();
+  pdl_trigger();
+  bf16* h = reinterpret_cast<bf16*>(p.h);
+  float x[8], y[8];
+  if (p.ids) {
+    int id = p.ids[m];
+    if (id < 0) id = 0;
+    if (id >= p.vocab) {
+      set_status(p.status, JX_ERR_RANGE);
+      id = 0;
+    }
+    vload8(reinterpret_cast<const bf16*>(p.table) + (long long)id * p.d + j0, x);
+    if (p.embed_scale != 0.f) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) x[i] = rnd<bf16>(x[i] * p.embed_scale);
+    }
+    vstore8(h + m * p.ldh + j0, x);
+  } else {
+    const long long src = p.row_map ? (long long)p.row_map[m] : m;
+    vload8(h + src * p.ldh + j0, x);
+  }
+  if (p.a) {
+    float a[8];
+    vload8(reinterpret_cast<const bf16*>(p.a) + m * p.lda + j0, a);
+    if (p.kind_pre != JX_NORM_NONE) {
+      float t[8];
+      vnormalize(a, t, p.d, p.kind_pre, p.eps, reinterpret_cast<const bf16*>(p.w_pre),
+                 reinterpret_cast<const bf16*>(p.b_pre), j0, red);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) x[i] = rnd<bf16>(x[i] + t[i]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) x[i] = rnd<bf16>(x[i] + a[i]);
+    }
+    vstore8(h + m * p.ldh + j0, x);
+  }
+  if (p.out) {
+    vnormalize(x, y, p.d, p.kind, p.eps, reinterpret_cast<const bf16*>(p.w), reinterpret_cast<const bf16*>(p.b), j0,
+               red);
+    bf16* o = reinterpret_cast<bf16*>(p.out);
+    vstore8(o + (p.out_rp > 0 ? k128_offset(m, j0, p.out_rp) : m * p.ldo + j0), y);
+  }
+  if (p.out2) {
+    vnormalize(x, y, p.d, p.kind, p.eps, reinterpret_cast<const bf16*>(p.w2), reinterpret_cast<const bf16*>(p.b2),
+               j0, red);
+    bf16* o = reinterpret_cast<bf16*>(p.out2);
+    vstore8(o + (p.out2_rp > 0 ? k128_offset(m, j0, p.out2_rp) : m * p.ldo2 + j0), y);
+  }
+}
+
 int run_norm(int dtype, const NormArgs& p, bool pdl, cudaStream_t stream) {
   if (p.M <= 0 || p.d <= 0) return JX_ERR_SHAPE;
+  const bool aligned = ((p.ldh | p.lda | p.ldo | p.ldo2) & 7) == 0;
+  if (dtype == JX_BF16 && p.d % 8 == 0 && p.d / 8 <= 1024 && (p.d / 8) % 32 == 0 && aligned) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.M);
+    cfg.blockDim = dim3(p.d / 8);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, norm_vec_kernel, p) == cudaSuccess ? JX_OK : JX_ERR_CUDA;
+  }
   constexpr int NT = 256;
   const size_t smem = (size_t)(2 * p.d + NT / 32 + 1) * sizeof(float);
   if (smem > 200 * 1024) return JX_ERR_SHAPE;
