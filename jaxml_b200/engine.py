@@ -58,10 +58,12 @@ class TPComm:
         self.dist.all_reduce(t, group=self.group)
 
     def all_gather_keys(self, keys: torch.Tensor) -> torch.Tensor:
-        if self._gather is None or self._gather.shape[1] != keys.numel():
-            self._gather = torch.empty(self.size, keys.numel(), dtype=keys.dtype, device=keys.device)
-        self.dist.all_gather_into_tensor(self._gather, keys, group=self.group)
-        return self._gather
+        """[n] per rank -> [size, n] (rank-major), gathered into one flat buffer."""
+        n = keys.numel()
+        if self._gather is None or self._gather.numel() != self.size * n:
+            self._gather = torch.empty(self.size * n, dtype=keys.dtype, device=keys.device)
+        self.dist.all_gather_into_tensor(self._gather, keys.reshape(-1), group=self.group)
+        return self._gather.view(self.size, n)
 
 
 def _device_count() -> int:

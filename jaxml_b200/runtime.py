@@ -158,7 +158,8 @@ class ModelWeights:
         if family == "gemma3":
             self.embed_scale = float(torch.tensor(d ** 0.5, dtype=torch.float32).to(dtype).float())
         self.gumbel = gumbel_table_bf16().to(dev)
-        torch.cuda.synchronize(dev)
+        if dev.type == "cuda":
+            torch.cuda.synchronize(dev)
 
     # -- packing helpers -------------------------------------------------------------------------
     def _pack_kn(self, w_kn: torch.Tensor, Np: int, Kp: int) -> torch.Tensor:
