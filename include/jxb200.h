@@ -41,6 +41,8 @@ extern "C" {
 #define JX_EPI_GLU_GELU_TANH 3    /* out = dtype(gelu_tanh(gate) * up), K128 output         models/gemma3.py:80-86 */
 #define JX_EPI_ACT_GELU_ERF 4     /* out = dtype(gelu_erf(acc + b))                         models/gpt_neox.py:75-80 */
 #define JX_EPI_RESID2 5           /* out = dtype(dtype(acc + res2) + res)  (parallel resid.) models/gpt_neox.py:126-129 */
+#define JX_EPI_STORE_F32 6        /* float out = acc + bias: a tensor-parallel partial sum, all-reduced in float32 */
+#define JX_EPI_ACC_F32 7          /* float out += acc + bias (GPT-NeoX parallel residual partials)            */
 
 /* Fused epilogue of a projection.  Output column n of a plain output lives at out[m*ldo + n]; a K128
  * output (out_rp > 0) is the tiled layout described in jx_pack_k128. */
@@ -69,7 +71,7 @@ typedef struct jx_norm_args {
   const int* ids;        /* embedding ids [M] or NULL */
   const void* table;     /* embedding table [vocab, d] */
   float embed_scale;     /* multiply gathered rows by this (0: none) */
-  int _pad0;
+  int a_f32;             /* `a` is float32 (an all-reduced partial sum): round it to the model dtype first */
   const int* row_map;    /* read h[row_map[m]] instead of h[m] (no write back) */
   const void* a;
   long long lda;

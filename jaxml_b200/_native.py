@@ -15,7 +15,8 @@ HEADER = os.path.join(os.path.dirname(PKG), "include", "jxb200.h")
 JX_OK, JX_ERR_ARG, JX_ERR_SHAPE, JX_ERR_DTYPE, JX_ERR_RANGE, JX_ERR_TIMEOUT, JX_ERR_CUDA, JX_ERR_UNSUPPORTED = range(8)
 JX_F32, JX_BF16 = 0, 1
 JX_NORM_NONE, JX_NORM_RMS, JX_NORM_GEMMA, JX_NORM_LAYER = 0, 1, 2, 3
-(JX_EPI_STORE, JX_EPI_RESID, JX_EPI_GLU_SILU, JX_EPI_GLU_GELU_TANH, JX_EPI_ACT_GELU_ERF, JX_EPI_RESID2) = range(6)
+(JX_EPI_STORE, JX_EPI_RESID, JX_EPI_GLU_SILU, JX_EPI_GLU_GELU_TANH, JX_EPI_ACT_GELU_ERF, JX_EPI_RESID2,
+ JX_EPI_STORE_F32, JX_EPI_ACC_F32) = range(8)
 
 STATUS_NAMES = {
     JX_OK: "ok", JX_ERR_ARG: "bad argument", JX_ERR_SHAPE: "bad shape", JX_ERR_DTYPE: "bad dtype",
@@ -36,7 +37,7 @@ class JxEpilogue(ctypes.Structure):
 
 class JxNormArgs(ctypes.Structure):
     _fields_ = [("M", I), ("d", I), ("eps", F), ("kind", I), ("kind_pre", I), ("vocab", I), ("ids", P),
-                ("table", P), ("embed_scale", F), ("_pad0", I), ("row_map", P), ("a", P), ("lda", LL), ("h", P),
+                ("table", P), ("embed_scale", F), ("a_f32", I), ("row_map", P), ("a", P), ("lda", LL), ("h", P),
                 ("ldh", LL), ("w_pre", P), ("b_pre", P), ("w", P), ("b", P), ("out", P), ("ldo", LL),
                 ("out_rp", LL), ("w2", P), ("b2", P), ("out2", P), ("ldo2", LL), ("out2_rp", LL), ("status", P)]
 

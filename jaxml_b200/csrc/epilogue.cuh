@@ -39,6 +39,21 @@ __device__ __forceinline__ void run_epilogue(const EpiParams& e, long long m0, i
     }
     return;
   }
+  if (e.kind == JX_EPI_STORE_F32 || e.kind == JX_EPI_ACC_F32) {
+    // float32 partial sums of a row-parallel projection: no rounding until they are all-reduced
+    float* out = reinterpret_cast<float*>(e.out);
+    for (int idx = tid; idx < rows * cols; idx += nthreads) {
+      const int m = idx / cols, j = idx - m * cols;
+      const long long row = m0 + m, n = n0 + j;
+      if (row >= e.M || n >= e.N) continue;
+      const float v = tile(m, j) + bias_at<T>(e, n);
+      if (e.kind == JX_EPI_STORE_F32)
+        out[row * e.ldo + n] = v;
+      else
+        out[row * e.ldo + n] += v;
+    }
+    return;
+  }
   for (int idx = tid; idx < rows * cols; idx += nthreads) {
     const int m = idx / cols, j = idx - m * cols;
     const long long row = m0 + m, n = n0 + j;

@@ -113,8 +113,11 @@ __global__ void __launch_bounds__(NT) norm_kernel(NormArgs p) {
 
   if (p.a) {
     const T* a = reinterpret_cast<const T*>(p.a);
+    const float* af = reinterpret_cast<const float*>(p.a);
+    // a float32 input (an all-reduced partial sum) is rounded to the model dtype first
+    auto a_at = [&](int j) { return p.a_f32 ? rnd<T>(af[m * p.lda + j]) : to_f(a[m * p.lda + j]); };
     if (p.kind_pre != JX_NORM_NONE) {
-      for (int j = threadIdx.x; j < d; j += NT) y[j] = to_f(a[m * p.lda + j]);
+      for (int j = threadIdx.x; j < d; j += NT) y[j] = a_at(j);
       __syncthreads();
       // normalise y in place: copy to a temp in the output half first
       float* t = y;
@@ -123,7 +126,7 @@ __global__ void __launch_bounds__(NT) norm_kernel(NormArgs p) {
       __syncthreads();
       for (int j = threadIdx.x; j < d; j += NT) x[j] = rnd<T>(x[j] + t[j]);
     } else {
-      for (int j = threadIdx.x; j < d; j += NT) x[j] = rnd<T>(x[j] + to_f(a[m * p.lda + j]));
+      for (int j = threadIdx.x; j < d; j += NT) x[j] = rnd<T>(x[j] + a_at(j));
     }
     __syncthreads();
     for (int j = threadIdx.x; j < d; j += NT) h[m * p.ldh + j] = from_f<T>(x[j]);
@@ -241,7 +244,15 @@ __global__ void __launch_bounds__(1024) norm_vec_kernel(NormArgs p) {
   }
   if (p.a) {
     float a[8];
-    vload8(reinterpret_cast<const bf16*>(p.a) + m * p.lda + j0, a);
+    if (p.a_f32) {
+      // a float32 input (an all-reduced partial sum) is rounded to bf16 first
+      const float4* af = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.a) + m * p.lda + j0);
+      const float4 u0 = af[0], u1 = af[1];
+      a[0] = rnd<bf16>(u0.x), a[1] = rnd<bf16>(u0.y), a[2] = rnd<bf16>(u0.z), a[3] = rnd<bf16>(u0.w);
+      a[4] = rnd<bf16>(u1.x), a[5] = rnd<bf16>(u1.y), a[6] = rnd<bf16>(u1.z), a[7] = rnd<bf16>(u1.w);
+    } else {
+      vload8(reinterpret_cast<const bf16*>(p.a) + m * p.lda + j0, a);
+    }
     if (p.kind_pre != JX_NORM_NONE) {
       float t[8];
       vnormalize(a, t, p.d, p.kind_pre, p.eps, reinterpret_cast<const bf16*>(p.w_pre),

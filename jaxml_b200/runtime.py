@@ -321,7 +321,9 @@ class DecoderRuntime:
         w, dev, dt = self.w, self.w.device, self.w.dtype
         a = {"M": M, "Mp": Mp}
         a["h"] = torch.zeros(Mp, w.d, dtype=dt, device=dev)
-        a["tmp"] = torch.zeros(Mp, w.d, dtype=dt, device=dev)
+        # Under tensor parallelism `tmp` holds float32 partial sums of the row-parallel projections, so
+        # the all-reduce adds unrounded values and the result is rounded once, as on one GPU.
+        a["tmp"] = torch.zeros(Mp, w.d, dtype=torch.float32 if self.comm is not None else dt, device=dev)
         a["qkv"] = torch.zeros(Mp, w.nqkv, dtype=dt, device=dev)
         a["q"] = torch.zeros(Mp, w.Hq * w.hd, dtype=dt, device=dev)
         if w.bf16:
@@ -361,6 +363,7 @@ class DecoderRuntime:
         args.embed_scale = W.embed_scale if ids is not None else 0.0
         args.row_map = ptr(row_map)
         args.a = ptr(a)
+        args.a_f32 = 1 if (a is not None and a.dtype == torch.float32 and W.dtype != torch.float32) else 0
         args.lda = W.d
         args.h = ptr(acts["h"])
         args.ldh = W.d
@@ -489,10 +492,11 @@ class DecoderRuntime:
         M, Mp, d, hd = acts["M"], acts["Mp"], W.d, W.hd
         tp = self.comm is not None
         parallel = fam == "neox" and cfg.use_parallel_residual
+        store = N.JX_EPI_STORE_F32 if tp else N.JX_EPI_STORE
         if fam == "gemma3" or parallel or tp:
             # o_proj result kept apart: Gemma normalises it, NeoX's parallel residual adds it with the
             # MLP output, and under tensor parallelism it is a partial sum to all-reduce first.
-            self._linear(acts, lw.wo, W.Np_d, W.Kp_o, "attn", N.JX_EPI_STORE, N_valid=d, bias=lw.bo,
+            self._linear(acts, lw.wo, W.Np_d, W.Kp_o, "attn", store, N_valid=d, bias=lw.bo,
                          out=acts["tmp"], ldo=d, K_logical=W.Hq * hd, N_cols=d)
             if not parallel:
                 self._allreduce(acts["tmp"], M)
@@ -526,11 +530,10 @@ class DecoderRuntime:
         down_kw = dict(N_valid=d, bias=lw.bd, K_logical=Fk, N_cols=d)
         if parallel and tp:
             # tmp = attn_partial + mlp_partial, all-reduced once; h += tmp in the next norm.
-            self._linear(acts, lw.wd, W.Np_d, W.Kp_f, "act", N.JX_EPI_RESID, out=acts["tmp"], ldo=d,
-                         res=acts["tmp"], ldr=d, **down_kw)
+            self._linear(acts, lw.wd, W.Np_d, W.Kp_f, "act", N.JX_EPI_ACC_F32, out=acts["tmp"], ldo=d, **down_kw)
             self._allreduce(acts["tmp"], M)
         elif fam == "gemma3" or tp:
-            self._linear(acts, lw.wd, W.Np_d, W.Kp_f, "act", N.JX_EPI_STORE, out=acts["tmp"], ldo=d, **down_kw)
+            self._linear(acts, lw.wd, W.Np_d, W.Kp_f, "act", store, out=acts["tmp"], ldo=d, **down_kw)
             self._allreduce(acts["tmp"], M)
         elif parallel:
             self._linear(acts, lw.wd, W.Np_d, W.Kp_f, "act", N.JX_EPI_RESID2, out=acts["h"], ldo=d,
