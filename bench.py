@@ -357,7 +357,12 @@ def gpu_arm(args):
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
-    rt.graph = None
+    # every graph that captured an NCCL all-reduce goes before the process group does
+    del graph, rt
+    engine.close()
+    import gc
+
+    gc.collect()
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()

@@ -211,6 +211,18 @@ class Engine:
             self._runtime = rt
         return rt
 
+    def close(self):
+        """Releases the decode runtime: its captured CUDA graph, activation buffers and KV cache.
+
+        Under tensor parallelism call it before ``destroy_process_group``: a captured graph that holds NCCL
+        calls keeps the communicator alive, and the process-group teardown then waits on it for good."""
+        if self._runtime is not None:
+            self._runtime.graph = None
+        self._runtime = None
+        if torch.cuda.is_available():
+            torch.cuda.synchronize()
+            torch.cuda.empty_cache()
+
     # -- generation ------------------------------------------------------------------------------------
     def generate(self, prompt_tokens, attention_mask=None, seed: int = 0, max_new_tokens: int = 10, top_k: int = 0,
                  top_p: float = 1.0, min_p: float = 0.0, temperature: float = 1.0, fuse_decoding: bool = False,
