@@ -56,6 +56,7 @@ def parse():
     ap.add_argument("--ctx", type=int, default=4096, help="context length of --micro attn")
     ap.add_argument("--shape", default="28672,4096", help="N,K of --micro gemv (default: fused gate/up)")
     ap.add_argument("--gemv-impl", type=int, default=0, help="--micro gemv kernel: 0 by shape, 1 mma.sync, 2 tcgen05")
+    ap.add_argument("--attn-impl", type=int, default=0, help="--micro attn form: 0 by shape, 1 split, 2 cluster")
     return ap.parse_args()
 
 
@@ -130,7 +131,8 @@ def step_bytes(cfg, B, ctx_mean, tp=1):
 
 def measure_gemv(rt, reps_layers=8):
     """Average duration of the decode projection kernel on the gate/up weights of distinct layers
-    (235 MB each, larger than L2), CUDA events on the launching stream."""
+    (235 MB each, larger than L2): back-to-back launches replayed from a CUDA graph, CUDA events on the
+    replay stream."""
     import torch
 
     from jaxml_b200 import _native as N
@@ -138,18 +140,12 @@ def measure_gemv(rt, reps_layers=8):
     w = rt.w
     acts = rt.dec
     layers = w.layers[:reps_layers]
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    for lw in layers[:2]:   # warm
-        rt._linear(acts, lw.wgu, w.Np_gu, w.Kp_d, "xn", N.JX_EPI_GLU_SILU, N_valid=w.F, out=acts["act"],
-                   ldo=w.F32, out_rp=acts["Mp"])
-    torch.cuda.synchronize()
-    start.record()
-    for lw in layers:
-        rt._linear(acts, lw.wgu, w.Np_gu, w.Kp_d, "xn", N.JX_EPI_GLU_SILU, N_valid=w.F, out=acts["act"],
-                   ldo=w.F32, out_rp=acts["Mp"])
-    end.record()
-    torch.cuda.synchronize()
-    ms = start.elapsed_time(end) / len(layers)
+
+    def launch_all(_stream):   # the runtime launches on torch's current stream (the capture stream)
+        for lw in layers:
+            rt._linear(acts, lw.wgu, w.Np_gu, w.Kp_d, "xn", N.JX_EPI_GLU_SILU, N_valid=w.F, out=acts["act"],
+                       ldo=w.F32, out_rp=acts["Mp"])
+    ms = _graph_ms(launch_all, len(layers))
     nbytes = 2 * w.Np_gu * w.Kp_d + 2 * acts["Mp"] * w.Kp_d + 2 * rt.B * w.F
     return ms, nbytes
 
@@ -368,6 +364,32 @@ def gpu_arm(args):
         dist.destroy_process_group()
 
 
+def _graph_ms(launch_all, n, reps=5):
+    """Device milliseconds per launch of `n` back-to-back launches issued by `launch_all(stream)`, captured
+    once in a CUDA graph and replayed `reps` times (CUDA events on the replay stream), so host-side
+    launch cost is not measured."""
+    import torch
+
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        launch_all(side.cuda_stream)          # warm: lazy module loading, one-time attribute setup
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=side):
+        launch_all(side.cuda_stream)
+    g.replay()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    cur = torch.cuda.current_stream()
+    start.record(cur)
+    for _ in range(reps):
+        g.replay()
+    end.record(cur)
+    torch.cuda.synchronize()
+    return start.elapsed_time(end) / (reps * n)
+
+
 def micro(args):
     """Single-kernel microbenchmarks on Llama-3-8B layer shapes (bf16, N(0,1) activations, N(0,0.02)
     weights): `gemv` = the decode projection on the gate/up weights of 8 distinct layers (1.9 GB, larger
@@ -379,10 +401,8 @@ def micro(args):
     N.load()
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    s = torch.cuda.current_stream().cuda_stream
     B = args.batch
     rup = lambda x, m: (x + m - 1) // m * m
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if args.micro == "gemv":
         Nn, K = (int(v) for v in args.shape.split(","))
         glu = Nn == 2 * 14336 and K == 4096
@@ -403,20 +423,10 @@ def micro(args):
         else:
             e.kind, e.M, e.N, e.out, e.ldo = N.JX_EPI_STORE, B, Nn, out.data_ptr(), Nn
 
-        def run(w):
+        def run(w, st):
             N.call("jx_linear_decode", w.data_ptr(), x.data_ptr(), Np, Kp, B, e, wsp.data_ptr(), wsp.numel(),
-                   cnt.data_ptr(), None, 148, 1, s)
-        for w in ws:
-            run(w)
-        reps = 5
-        torch.cuda.synchronize()
-        start.record()
-        for _ in range(reps):
-            for w in ws:
-                run(w)
-        end.record()
-        torch.cuda.synchronize()
-        ms = start.elapsed_time(end) / (reps * copies)
+                   cnt.data_ptr(), None, 148, 1, st)
+        ms = _graph_ms(lambda st: [run(w, st) for w in ws], copies)
         nbytes = 2 * Nn * K + 2 * B * K + 2 * B * (Nn // 2 if glu else Nn)
         line = {"micro": "gemv", "impl": ["by-shape", "mma.sync", "tcgen05"][args.gemv_impl], "shape": f"M={B} N={Nn} K={K}",
                 "us": ms * 1e3, "gbs": nbytes / ms / 1e6}
@@ -440,22 +450,14 @@ def micro(args):
                                                                   pos.data_ptr(), 2, hd ** -0.5)
         a.out, a.out_rp, a.ws, a.ws_bytes, a.counters = out.data_ptr(), max(Mp, rup(B, 16)), wsp.data_ptr(), wsp.numel() * 4, cnt.data_ptr()
 
-        def run(layer):
+        N.call("jx_set_decode_attention_impl", args.attn_impl)
+
+        def run(layer, st):
             a.layer_row0 = layer * B * T
-            N.call("jx_decode_attention", a, 1, s)
-        for l in range(L):
-            run(l)
-        reps = 5
-        torch.cuda.synchronize()
-        start.record()
-        for _ in range(reps):
-            for l in range(L):
-                run(l)
-        end.record()
-        torch.cuda.synchronize()
-        ms = start.elapsed_time(end) / (reps * L)
+            N.call("jx_decode_attention", a, 1, st)
+        ms = _graph_ms(lambda st: [run(l, st) for l in range(L)], L)
         nbytes = B * ctx * 2 * Hkv * hd * 2
-        line = {"micro": "attn", "shape": f"B={B} ctx={ctx} Hq={Hq} Hkv={Hkv} hd={hd}", "us": ms * 1e3,
+        line = {"micro": "attn", "impl": ["by-shape", "split", "cluster"][args.attn_impl], "shape": f"B={B} ctx={ctx} Hq={Hq} Hkv={Hkv} hd={hd}", "us": ms * 1e3,
                 "gbs": nbytes / ms / 1e6}
     print(json.dumps(line), flush=True)
 

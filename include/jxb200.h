@@ -251,6 +251,10 @@ int jx_attention(const jx_attn_args* args, int dtype, int pdl, void* stream);
  * the valid keys, TMA-staged K/V tiles, exact reference rounding (see csrc/attention_decode.cu). */
 int jx_decode_attention_workspace(int B, int Hq, int hd, int T, int window, long long* bytes_out);
 int jx_decode_attention(const jx_dattn_args* args, int pdl, void* stream);
+/* Form behind jx_decode_attention: 0 = by shape (default: the two-kernel split form), 1 = the split
+ * form, 2 = the single-pass thread-block-cluster form (key range (T, or the window) up to 8 CTAs x
+ * 1024 keys; JX_ERR_SHAPE otherwise). */
+int jx_set_decode_attention_impl(int impl);
 
 /* Attention.mha prefill branch (causal + window + padding masks, nn/attention.py:321-400) for bf16
  * caches on tensor cores, exact reference rounding (see csrc/attention_prefill.cu). */

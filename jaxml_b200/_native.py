@@ -93,6 +93,7 @@ _PROTOS = {
     "jx_attention": (I, [ctypes.POINTER(JxAttnArgs), I, I, P]),
     "jx_decode_attention_workspace": (I, [I, I, I, I, I, ctypes.POINTER(LL)]),
     "jx_decode_attention": (I, [ctypes.POINTER(JxDAttnArgs), I, P]),
+    "jx_set_decode_attention_impl": (I, [I]),
     "jx_prefill_attention": (I, [ctypes.POINTER(JxPAttnArgs), I, P]),
     "jx_sample": (I, [ctypes.POINTER(JxSampleArgs), I, P]),
     "jx_sample_finalize": (I, [ctypes.POINTER(JxSampleArgs), P, I, P]),

@@ -31,7 +31,8 @@ __global__ void __launch_bounds__(256) qkv_rope_append_kernel(QkvArgs p) {
   const T* sin = reinterpret_cast<const T*>(p.sin) + (long long)pos * p.rd;
   const int n_heads = p.Hq + 2 * p.Hkv;
   const int half = p.rd >> 1;
-  for (int head = warp; head < n_heads; head += 8) {
+  // grid.y spreads the heads of a row over CTAs of 8 warps, one head per warp
+  for (int head = blockIdx.y * 8 + warp; head < n_heads; head += 8 * gridDim.y) {
     const bool is_q = head < p.Hq, is_k = !is_q && head < p.Hq + p.Hkv;
     const T* src = row + (long long)head * p.hd;
     for (int j = lane; j < p.hd; j += 32) v[j] = to_f(src[j]);
@@ -77,7 +78,7 @@ int run_qkv_rope_append(int dtype, const QkvArgs& p, bool pdl, cudaStream_t stre
   if (p.M <= 0 || p.S <= 0 || p.hd <= 0 || p.hd > 256 || p.rd < 0 || p.rd > p.hd || (p.rd & 1)) return JX_ERR_SHAPE;
   if (p.decode && p.S != 1) return JX_ERR_SHAPE;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(p.M);
+  cfg.gridDim = dim3(p.M, (p.Hq + 2 * p.Hkv + 7) / 8);
   cfg.blockDim = dim3(256);
   cfg.dynamicSmemBytes = 8 * p.hd * sizeof(float);
   cfg.stream = stream;

@@ -94,10 +94,19 @@ def test_linear_decode_glu_resid_bias(impl, M):
     assert (h.double() - ref2).abs().max().item() <= 0.05 * ref2.abs().max().item()
 
 
+@pytest.fixture(params=[2, 1], ids=["cluster", "split"])
+def attn_form(request):
+    N = _n()
+    N.call("jx_set_decode_attention_impl", request.param)
+    yield request.param
+    N.call("jx_set_decode_attention_impl", 0)
+
+
 @pytest.mark.parametrize("hd,Hq,Hkv,window", [(128, 32, 8, 0), (256, 16, 8, 0), (256, 16, 8, 100), (64, 8, 8, 0),
                                                (128, 16, 1, 0), (128, 64, 8, 0)])
-def test_decode_attention_matches_oracle(hd, Hq, Hkv, window):
-    """Tensor-core decode attention vs the oracle's Attention.mha on a padded cache.
+def test_decode_attention_matches_oracle(attn_form, hd, Hq, Hkv, window):
+    """Tensor-core decode attention (single-pass cluster form and two-kernel split form) vs the oracle's
+    Attention.mha on a padded cache.
 
     The kernel rounds at the reference's points (scores, scale, probabilities, output), so results agree
     to about one bf16 ulp.  A q.k accumulated in a different order can round to the neighbouring bf16
