@@ -70,8 +70,8 @@ __global__ void __launch_bounds__(128) dattn_scores_kernel(const __grid_constant
 
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   int lo, valid;
   key_range(p, b, lo, valid);
   const int t0 = lo + split * kDaKeys;
@@ -221,8 +221,8 @@ __global__ void __launch_bounds__(128) dattn_pv_kernel(const __grid_constant__ C
 
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   int lo, valid;
   key_range(p, b, lo, valid);
   const int t0 = lo + split * kDaKeys;

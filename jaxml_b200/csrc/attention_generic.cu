@@ -17,8 +17,8 @@ __global__ void __launch_bounds__(128) attention_generic_kernel(AttnArgs p) {
   const int tid = threadIdx.x;
   const int kvh = h / (p.Hq / p.Hkv);
   const long long row = (long long)b * p.S + s;
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   int valid = p.len_ptr ? p.len_ptr[b] + p.len_add : p.T;
   if (valid > p.T) {
     set_status(p.status, JX_ERR_RANGE);

@@ -56,8 +56,8 @@ __global__ void __launch_bounds__(128) pattn_kernel(const __grid_constant__ CUte
   const int kvh = h / p.n_rep;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int s0 = qt * 64;
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   int valid = p.len_ptr[b] + p.len_add;
   if (valid > p.T) {
     set_status(p.status, JX_ERR_RANGE);

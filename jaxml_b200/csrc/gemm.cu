@@ -184,8 +184,8 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(const float* __restrict__
   const int tid = threadIdx.x;
   const int tr = tid / 32, tc = tid % 32;  // 8 x 32 threads: 4 rows x 4 cols each
   const long long m0 = (long long)blockIdx.y * kF32BM, n0 = (long long)blockIdx.x * kF32BN;
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   float acc[4][4] = {};
   for (int k0 = 0; k0 < K; k0 += kF32BK) {
     for (int i = tid; i < kF32BM * kF32BK; i += 256) {

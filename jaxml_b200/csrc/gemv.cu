@@ -25,7 +25,10 @@ constexpr int kTileLd = 68;         // padded float32 row stride of the staging 
 
 template <int MT>
 struct GemvCfg {
-  static constexpr int kStages = MT == 1 ? 8 : (MT == 2 ? 6 : 4);
+  // At M <= 16 the CTA stays under half the SM's shared memory (104 KB), so the next projection's CTA
+  // (this kernel's, or the tcgen05 kernel's at 116 KB) is resident beside it and streams its weights
+  // while this one finishes.
+  static constexpr int kStages = MT == 1 ? 5 : (MT == 2 ? 4 : 3);
   static constexpr int kWBytes = kGemvBN * kGemvBK * 2;   // 16 KB
   static constexpr int kXBytes = MT * 16 * kGemvBK * 2;   // 4 KB per m16 tile
   static constexpr int kStageBytes = kWBytes + kXBytes;
@@ -225,15 +228,43 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
       do_epi = sh[1] != 0;
       if (do_epi) {
         __threadfence();
-        // Sum every contribution (this CTA's too, already in the workspace) in CTA order; the slot
-        // address is computed once per contributor, the running sums stay in the tile.
-        for (int cc = c_first; cc <= c_last; ++cc) {
-          const float* src = ws + (long long)slot_of(cc) * Mp * kGemvBN;
-          for (int idx = tid; idx < Mp * kGemvBN; idx += kGemvConsumers) {
-            float* t = tile + (idx >> 6) * kTileLd + (idx & 63);
-            const float v = __ldcg(src + idx);
-            *t = (cc == c_first) ? v : *t + v;
+        // Sum every contribution (this CTA's too, already in the workspace) in CTA order.  Each thread
+        // owns MT float4 groups of the tile; the loads of up to 4 contributors are all issued before
+        // any is added, so the L2 round trips overlap instead of following one another.
+        float4 acc4[MT];
+        for (int cc0 = c_first; cc0 <= c_last; cc0 += 4) {
+          float4 v[4][MT];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            if (cc0 + u > c_last) break;
+            const float4* src = reinterpret_cast<const float4*>(ws + (long long)slot_of(cc0 + u) * Mp * kGemvBN);
+#pragma unroll
+            for (int q = 0; q < MT; ++q) v[u][q] = __ldcg(src + tid + q * kGemvConsumers);
           }
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            if (cc0 + u > c_last) break;
+#pragma unroll
+            for (int q = 0; q < MT; ++q) {
+              if (cc0 + u == c_first) {
+                acc4[q] = v[u][q];
+              } else {
+                acc4[q].x += v[u][q].x;
+                acc4[q].y += v[u][q].y;
+                acc4[q].z += v[u][q].z;
+                acc4[q].w += v[u][q].w;
+              }
+            }
+          }
+        }
+#pragma unroll
+        for (int q = 0; q < MT; ++q) {
+          const int e0 = (tid + q * kGemvConsumers) * 4;           // 4 consecutive columns of one row
+          float* t = tile + (e0 >> 6) * kTileLd + (e0 & 63);
+          t[0] = acc4[q].x;
+          t[1] = acc4[q].y;
+          t[2] = acc4[q].z;
+          t[3] = acc4[q].w;
         }
         if (tid == 0) counters[nb] = 0;
         named_bar_sync(1, kGemvConsumers);

@@ -24,7 +24,8 @@ struct TcCfg {
   static constexpr int kWBytes = kTcBN * kTcBK * 2;        // 32 KB
   static constexpr int kXBytes = N * kTcBK * 2;            // 4 / 8 / 16 KB
   static constexpr int kStageBytes = kWBytes + kXBytes;
-  static constexpr int kStages = MT == 1 ? 6 : (MT == 2 ? 5 : 4);
+  // 3 stages at M <= 16 (116 KB): the next projection's CTA fits beside this one (see gemv.cu).
+  static constexpr int kStages = MT == 1 ? 3 : (MT == 2 ? 5 : 4);
   static constexpr int kLd = kTcBN + 4;                    // staging tile [N][128 rows] float32
   static constexpr int kTileBytes = N * kLd * 4;
   static constexpr int kBars = 2 * kStages + 5;
@@ -224,14 +225,44 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (do_epi) {
           __threadfence();
           // Sum every contribution (this CTA's too, already in the workspace) in CTA order.  Each
-          // thread owns the same elements for every contributor, so the running sums live in the
-          // tile without further synchronisation; the slot address is computed once per contributor.
-          for (int cc = c_first; cc <= c_last; ++cc) {
-            const float* src = ws + (long long)slot_of(cc) * Mp * kTcBN;
-            for (int idx = tid; idx < Mp * kTcBN; idx += 128) {
-              float* t = tile + (idx >> 7) * C::kLd + (idx & 127);
-              const float v = __ldcg(src + idx);
-              *t = (cc == c_first) ? v : *t + v;
+          // thread owns 4*MT float4 groups of the tile, taken 4 at a time; the loads of up to 4
+          // contributors are all issued before any is added, so the L2 round trips overlap.
+#pragma unroll
+          for (int q0 = 0; q0 < 4 * MT; q0 += 4) {
+            float4 acc4[4];
+            for (int cc0 = c_first; cc0 <= c_last; cc0 += 4) {
+              float4 v[4][4];
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                if (cc0 + u > c_last) break;
+                const float4* src = reinterpret_cast<const float4*>(ws + (long long)slot_of(cc0 + u) * Mp * kTcBN);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) v[u][q] = __ldcg(src + tid + (q0 + q) * 128);
+              }
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                if (cc0 + u > c_last) break;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                  if (cc0 + u == c_first) {
+                    acc4[q] = v[u][q];
+                  } else {
+                    acc4[q].x += v[u][q].x;
+                    acc4[q].y += v[u][q].y;
+                    acc4[q].z += v[u][q].z;
+                    acc4[q].w += v[u][q].w;
+                  }
+                }
+              }
+            }
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const int e0 = (tid + (q0 + q) * 128) * 4;   // 4 consecutive weight rows of one token
+              float* t = tile + (e0 >> 7) * C::kLd + (e0 & 127);
+              t[0] = acc4[q].x;
+              t[1] = acc4[q].y;
+              t[2] = acc4[q].z;
+              t[3] = acc4[q].w;
             }
           }
           if (tid == 0) counters[nb] = 0;

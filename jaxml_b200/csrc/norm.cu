@@ -85,8 +85,8 @@ __global__ void __launch_bounds__(NT) norm_kernel(NormArgs p) {
   float* red = sm + 2 * p.d;  // [NT/32 + 1]
   const long long m = blockIdx.x;
   const int d = p.d;
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   T* h = reinterpret_cast<T*>(p.h);
 
   if (p.ids) {
@@ -221,8 +221,8 @@ __global__ void __launch_bounds__(1024) norm_vec_kernel(NormArgs p) {
   __shared__ float red[32];
   const long long m = blockIdx.x;
   const int j0 = threadIdx.x * 8;
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   bf16* h = reinterpret_cast<bf16*>(p.h);
   float x[8], y[8];
   if (p.ids) {

@@ -17,8 +17,8 @@ __global__ void __launch_bounds__(256) qkv_rope_append_kernel(QkvArgs p) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float* v = buf + warp * p.hd;
   const long long m = blockIdx.x;
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   const int b = (int)(m / p.S), s = (int)(m % p.S);
   int pos = s;
   if (p.decode) pos = p.pos_id[b] + 1;

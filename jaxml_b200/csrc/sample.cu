@@ -79,8 +79,8 @@ __global__ void __launch_bounds__(256) sample_kernel(SampleArgs p) {
   __shared__ int last_flag;
   const int b = blockIdx.y, cidx = blockIdx.x;
   const int nchunks = gridDim.x;
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   const T* row = reinterpret_cast<const T*>(p.logits) + (long long)b * p.ld;
   const int v0 = cidx * p.chunk, v1 = min(p.V, v0 + p.chunk);
   const uint32_t s0 = p.rng ? p.rng[2] : 0u, s1 = p.rng ? p.rng[3] : 0u;
