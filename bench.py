@@ -342,7 +342,7 @@ def gpu_arm(args):
                        "l2": "inputs larger than L2 (15 GB of weights per step)"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                          "frac": achieved / hbm_peak, "traffic": None,
-                         "kernel": "gemv_k128_kernel (gate/up projection, 235 MB weights per launch)",
+                         "kernel": "gemv_tc_kernel (tcgen05 decode projection, gate/up: 235 MB weights per launch)",
                          "peak_source": "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in peaks else "fallback"},
             "step_roofline": {"bytes_per_step": sbytes, "weight_bytes": wbytes, "kv_bytes": kvbytes,
                               "achieved_gbs": sbytes / (total_ms / args.steps * 1e-3) / 1e9,

@@ -236,6 +236,9 @@ int jx_linear_decode_noalloc(const void* W, const void* X, long long Np, long lo
 /* Prefill projection (any M): bfloat16 K128 operands X [Mp, Kp], W [Np, Kp] (Mp, Np multiples of 128). */
 int jx_linear_prefill(const void* X, const void* W, long long Mp, long long Np, long long Kp, const jx_epilogue* epi,
                       int* status, int pdl, void* stream);
+/* Kernel behind jx_linear_prefill: 0 = by shape (default: tcgen05/TMEM whenever the shape allows),
+ * 1 = mma.sync, 2 = tcgen05/TMEM (JX_ERR_SHAPE when the shape does not allow it). */
+int jx_set_prefill_linear_impl(int impl);
 
 /* float32 projection: X [M, K] (row stride ldx) times the reference's kernel layout W [K, N]. */
 int jx_linear_f32(const float* X, long long ldx, const float* W, int M, int N, int K, const jx_epilogue* epi, int pdl,

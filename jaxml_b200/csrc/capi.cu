@@ -19,6 +19,7 @@ int run_sample(const jx_sample_args& p, bool pdl, cudaStream_t stream);
 int run_decode_attention(const jx_dattn_args& a, bool pdl, cudaStream_t stream);
 void set_gemv_impl(int impl);
 void set_dattn_impl(int impl);
+void set_gemm_impl(int impl);
 int run_prefill_attention(const jx_pattn_args& a, bool pdl, cudaStream_t stream);
 long long dattn_workspace_bytes(int B, int Hq, int T, int hd, int n_splits);
 int dattn_n_splits(int T, int window);
@@ -213,6 +214,13 @@ int jx_decode_attention(const jx_dattn_args* args, int pdl, void* stream) {
   if (rc != JX_OK)
     return fail(rc, "jx_decode_attention: head_dim must be 64/128/256, Hq/Hkv <= 16, workspace large enough, "
                     "16-byte aligned q/cache");
+  return JX_OK;
+}
+
+int jx_set_prefill_linear_impl(int impl) {
+  if (impl < 0 || impl > 2)
+    return fail(JX_ERR_ARG, "jx_set_prefill_linear_impl: 0 (by shape), 1 (mma.sync), 2 (tcgen05)");
+  set_gemm_impl(impl);
   return JX_OK;
 }
 

@@ -1,6 +1,7 @@
 // Prefill projections (M > 64 token rows): Y[M, N] = X[M, K] . W[N, K]^T with the fused epilogues.
 //
-// bfloat16: both operands in the K128 tiled layout, so a 128 x 128 operand tile of one K chunk is a
+// bfloat16: the tcgen05 kernel (gemm_tc.cu) runs every shape it supports; this mma.sync kernel is the
+// fallback and the comparison path.  Both operands in the K128 tiled layout, so a 128 x 128 operand tile of one K chunk is a
 // single contiguous 32 KB run that one TMA bulk copy moves into shared memory.  A producer warp keeps
 // three stages in flight; eight consumer warps (2 x 4, 64 x 32 each) run mma.sync m16n8k16 with
 // conflict-free ldmatrix reads of the 8x8 core matrices.
@@ -146,8 +147,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                        threadIdx.x - 32, 256);
 }
 
+bool gemm_tc_supported(long long Mp, long long Np, long long Kp);
+int run_gemm_tc(const bf16* X, const bf16* W, long long Mp, long long Np, long long Kp, const EpiParams& e,
+                int* status, bool pdl, cudaStream_t stream);
+
+// 0: by shape (the tcgen05 kernel whenever it supports the shape), 1: mma.sync kernel, 2: tcgen05 kernel.
+static int g_gemm_impl = 0;
+void set_gemm_impl(int impl) { g_gemm_impl = impl; }
+
 int run_gemm_k128(const bf16* X, const bf16* W, long long Mp, long long Np, long long Kp, const EpiParams& e,
                   int* status, bool pdl, cudaStream_t stream) {
+  if (g_gemm_impl != 1 && gemm_tc_supported(Mp, Np, Kp)) return run_gemm_tc(X, W, Mp, Np, Kp, e, status, pdl, stream);
+  if (g_gemm_impl == 2) return JX_ERR_SHAPE;
   if (Mp % kGemmBM || Np % kGemmBN || Kp % kGemmBK || Mp <= 0 || Np <= 0 || Kp <= 0) return JX_ERR_SHAPE;
   if ((Np / kGemmBN) > 65535 * 1024LL || (Mp / kGemmBM) > 65535) return JX_ERR_SHAPE;
   static bool configured = false;

@@ -189,6 +189,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         set_status(status, JX_ERR_TIMEOUT);
         sh[0] = 1;
       }
+      ok = __all_sync(0xffffffffu, ok);   // tcgen05.ld is a warp-wide instruction
       tc_fence_after();
       if (ok) {
 #pragma unroll

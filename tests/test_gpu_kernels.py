@@ -121,8 +121,17 @@ def test_linear_decode_glu_and_resid():
     assert (got.float() - ref).abs().max().item() <= 0.02 * ref.abs().max().item()
 
 
-@pytest.mark.parametrize("M,Nn,K", [(300, 384, 512), (1024, 6144, 4096), (128, 128, 128)])
-def test_linear_prefill_matches_torch(M, Nn, K):
+@pytest.fixture(params=[2, 1], ids=["tcgen05", "mma_sync"])
+def prefill_impl(request):
+    N = _n()
+    N.call("jx_set_prefill_linear_impl", request.param)
+    yield request.param
+    N.call("jx_set_prefill_linear_impl", 0)
+
+
+@pytest.mark.parametrize("M,Nn,K", [(300, 384, 512), (1024, 6144, 4096), (128, 128, 128), (520, 1280, 2048)])
+def test_linear_prefill_matches_torch(prefill_impl, M, Nn, K):
+    """Prefill projection (tcgen05 and mma.sync kernels), including a 128-token last block (M=300, 520)."""
     N = _n()
     torch.manual_seed(2)
     x = torch.randn(M, K, device="cuda").to(torch.bfloat16)
@@ -183,3 +192,48 @@ def test_sample_kernel_bit_exact(dtype, greedy):
     assert rng.cpu().numpy().view(np.uint32).tolist() == [k2[0], k2[1], s2[0], s2[1]]
     assert int(cnt.abs().sum().item()) == 0
 
+
+
+def test_linear_prefill_glu_bias_resid(prefill_impl):
+    """Prefill projection epilogues: SwiGLU into the K128 layout, then a residual add with bias."""
+    N = _n()
+    torch.manual_seed(3)
+    M, F, K = 300, 192, 256
+    x = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+    g = (torch.randn(F, K, device="cuda") * 0.05).to(torch.bfloat16)
+    u = (torch.randn(F, K, device="cuda") * 0.05).to(torch.bfloat16)
+    wgu = torch.stack([g.reshape(-1, 32, K), u.reshape(-1, 32, K)], 1).reshape(2 * F, K)
+    Mp, Kp = _rup(M, 128), _rup(K, 128)
+    xp, wp = _pack(N, x, Mp, Kp), _pack(N, wgu, _rup(2 * F, 128), Kp)
+    Fp = _rup(F, 128)
+    act = torch.zeros(Mp * Fp, dtype=torch.bfloat16, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    e = _epi(N, N.JX_EPI_GLU_SILU, M, F, act, 0, out_rp=Mp)
+    N.call("jx_linear_prefill", xp.data_ptr(), wp.data_ptr(), Mp, _rup(2 * F, 128), Kp, e, status.data_ptr(), 0,
+           _stream())
+    got = torch.empty(M, F, dtype=torch.bfloat16, device="cuda")
+    N.call("jx_unpack_k128", act.data_ptr(), M, F, Mp, got.data_ptr(), N.JX_BF16, F, _stream())
+    gg = (x.float() @ g.float().T).to(torch.bfloat16).float()
+    uu = (x.float() @ u.float().T).to(torch.bfloat16).float()
+    a = (gg * torch.sigmoid(gg)).to(torch.bfloat16).float()
+    ref = (a * uu).to(torch.bfloat16).float()
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    assert (got.float() - ref).abs().max().item() <= 0.02 * ref.abs().max().item()
+    # down-style projection of the activations with bias and residual: out = bf16(bf16(a.Wd + b) + res)
+    D = 160
+    wd = (torch.randn(D, F, device="cuda") * 0.05).to(torch.bfloat16)
+    bias = (torch.randn(D, device="cuda") * 0.1).to(torch.bfloat16)
+    res = torch.randn(M, D, device="cuda").to(torch.bfloat16)
+    wdp = _pack(N, wd, _rup(D, 128), Fp)
+    out = torch.zeros(M, D, dtype=torch.bfloat16, device="cuda")
+    e2 = _epi(N, N.JX_EPI_RESID, M, D, out, D)
+    e2.bias, e2.res, e2.ldr = bias.data_ptr(), res.data_ptr(), D
+    N.call("jx_linear_prefill", act.data_ptr(), wdp.data_ptr(), Mp, _rup(D, 128), Fp, e2, status.data_ptr(), 0,
+           _stream())
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    y = (got.float() @ wd.float().T).to(torch.bfloat16).float()
+    want = ((y + bias.float()).to(torch.bfloat16).float() + res.float()).to(torch.bfloat16).float()
+    err = (out.float() - want).abs()
+    assert err.max().item() <= 0.02 * want.abs().max().item(), err.max().item()
