@@ -50,7 +50,7 @@ typedef struct jx_epilogue {
   int kind;
   int M;                 /* valid output rows */
   int N;                 /* valid output columns (GLU: F) */
-  int _pad0;
+  int pf_iters;          /* decode projections: see pf_w (0: no prefetch) */
   const void* bias;      /* per packed weight row, model dtype, or NULL */
   void* out;
   long long ldo;
@@ -59,6 +59,14 @@ typedef struct jx_epilogue {
   long long ldr;
   const void* res2;      /* RESID2 second addend */
   long long ldr2;
+  /* Decode projections only (jx_linear_decode): once this call has issued its own weight loads, each
+   * CTA prefetches into L2 the first pf_iters 128-wide K chunks that the same CTA of the NEXT decode
+   * projection will read (its K128 weights pf_w [pf_np, pf_kp], same grid), so that call starts from L2
+   * while this one finishes.  A cache hint only: results are unchanged.  No counterpart in the reference. */
+  const void* pf_w;
+  long long pf_np, pf_kp;
+  int pf_rows;           /* set by the library: weight rows per block of the next call's kernel */
+  int pf_grid;           /* set by the library: CTAs of the next call */
 } jx_epilogue;
 
 /* Row-wise embedding gather / residual add / normalisation (one launch per call). */
@@ -256,7 +264,7 @@ int jx_decode_attention_workspace(int B, int Hq, int hd, int T, int window, long
 int jx_decode_attention(const jx_dattn_args* args, int pdl, void* stream);
 /* Form behind jx_decode_attention: 0 = by shape (default: the two-kernel split form), 1 = the split
  * form, 2 = the single-pass thread-block-cluster form (key range (T, or the window) up to 8 CTAs x
- * 1024 keys; JX_ERR_SHAPE otherwise). */
+ * 2048 keys; JX_ERR_SHAPE otherwise). */
 int jx_set_decode_attention_impl(int impl);
 
 /* Attention.mha prefill branch (causal + window + padding masks, nn/attention.py:321-400) for bf16

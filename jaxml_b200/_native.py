@@ -31,8 +31,9 @@ F = ctypes.c_float
 
 
 class JxEpilogue(ctypes.Structure):
-    _fields_ = [("kind", I), ("M", I), ("N", I), ("_pad0", I), ("bias", P), ("out", P), ("ldo", LL),
-                ("out_rp", LL), ("res", P), ("ldr", LL), ("res2", P), ("ldr2", LL)]
+    _fields_ = [("kind", I), ("M", I), ("N", I), ("pf_iters", I), ("bias", P), ("out", P), ("ldo", LL),
+                ("out_rp", LL), ("res", P), ("ldr", LL), ("res2", P), ("ldr2", LL), ("pf_w", P), ("pf_np", LL),
+                ("pf_kp", LL), ("pf_rows", I), ("pf_grid", I)]
 
 
 class JxNormArgs(ctypes.Structure):

@@ -8,9 +8,9 @@
 //   o   = bf16(sum_t p_t v_t)                                          (float32 accumulation)
 // Only the valid (or in-window) keys are read, not the whole padded buffer.
 //
-// Two forms.  The single-pass cluster form (dattn_fused_kernel, below) covers key ranges up to 8 CTAs x
-// 1024 keys per (row, KV head) and is selected explicitly.  The default split form runs two kernels per
-// layer, each a grid of (key split, KV head, batch row) CTAs of 128 keys:
+// Two forms.  The single-pass form (dattn_warp_kernel, below; key ranges up to 8 CTAs x 2048 keys per
+// (row, KV head)) is selected explicitly.  The default split form runs two kernels per layer, each a grid
+// of (key split, KV head, batch row) CTAs of 128 keys:
 //   scores: K tiles arrive by TMA (2-D tensor map over the [L*B*T, Hkv*hd] cache, 128-byte swizzle);
 //           Q.K^T on mma.sync; the rounded scores go to a float32 workspace with per-split (max, sum).
 //   pv:     combines the split statistics into the exact softmax normaliser, forms the bf16
@@ -329,21 +329,24 @@ __global__ void __launch_bounds__(128) dattn_pv_kernel(const __grid_constant__ C
 }
 
 // ------------------------------------------------------------------------------------------------
-// Single-pass form: one thread-block cluster per (batch row, KV head), its CS CTAs splitting the key
-// range into contiguous runs of 64-key tiles.  Every CTA issues its K and V tiles at once (one
-// memory round trip when they fit the ring), keeps its rounded scores in shared memory, and the
-// cluster exchanges the per-row maxima and exp-sums through distributed shared memory, so each CTA
-// forms the exact probabilities bf16(exp(s - max) / sum) itself.  The partial outputs sum_t p_t v_t
-// are added across the cluster in rank order (deterministic) by the CTA that owns each column slice.
+// Single-pass form: a thread-block cluster of CS CTAs per (batch row, KV head) (CS = 1 when there are
+// at least as many head groups as SMs), the CTAs splitting the valid keys into contiguous runs of tiles.
+// Inside a CTA the 4 warps are independent pipelines: warp w owns tiles w, w+4, ... of the CTA's run,
+// streams their K and then their V tiles through its own two shared-memory slots (TMA, one mbarrier per
+// slot, refilled by the same warp), so no CTA-wide barrier is taken per tile.  Q stays in registers.
+//   scores : rounded like the reference, kept as bf16 in shared memory (exact: they are bf16 values)
+//   softmax: row maxima and exp-sums over the warps in warp order, then over the cluster in rank
+//            order through distributed shared memory; every CTA then forms the exact probabilities
+//            bf16(exp(s - max) / sum) of its keys directly as mma.sync A fragments
+//   output : each warp's partial sum_t p_t v_t, added over the warps in warp order and over the
+//            cluster in rank order (deterministic), rounded once to bf16 (K128 layout)
 // ------------------------------------------------------------------------------------------------
-constexpr int kFaKT = 64;                 // keys per tile
-constexpr int kFaMaxTiles = 16;           // tiles per CTA this form holds scores for (1024 keys)
-constexpr int kFaPLd = kFaKT + 8;         // padded bf16 row stride of the probability tile
+constexpr int kWaMaxKeys = 2048;          // keys per CTA this form keeps scores for
 
 struct FAttnParams {
   int B, Hq, Hkv, n_rep, T, window;
   int kt_cap;            // tiles per CTA the shared memory was sized for
-  int n_stages;          // ring stages
+  int _pad0;
   long long layer_row0;
   const bf16* q;         // [B, Hq, HD]
   const int* len_ptr;
@@ -355,46 +358,51 @@ struct FAttnParams {
 };
 
 template <int HD>
-struct FaSmem {
-  static constexpr int NB = HD / 64;
-  static constexpr int kTileBytes = kFaKT * HD * 2;
-  // byte offsets from the 1024-aligned base; `kt` = tiles per CTA, `ns` = ring stages
-  static __host__ __device__ int q_off(int ns) { return ns * kTileBytes; }
-  static __host__ __device__ int sc_off(int ns) { return q_off(ns) + NB * 2048; }
-  static __host__ __device__ int sc_ld(int kt) { return kt * kFaKT + 8; }
-  static __host__ __device__ int p_off(int ns, int kt) { return sc_off(ns) + 16 * sc_ld(kt) * 2; }
-  static __host__ __device__ int red_off(int ns, int kt) { return p_off(ns, kt) + 16 * kFaPLd * 2; }
-  static __host__ __device__ int bar_off(int ns, int kt) { return red_off(ns, kt) + (64 + 16 + 16 + 16 + 16) * 4; }
-  static __host__ __device__ int bytes(int ns, int kt) { return 1024 + bar_off(ns, kt) + ns * 8 + 16; }
+struct WaCfg {
+  static constexpr int KT = HD == 256 ? 32 : 64;     // keys per tile
+  static constexpr int NB = HD / 64;                 // 64-column blocks of a row
+  static constexpr int kBlockBytes = KT * 128;       // one [KT x 64] block, 128-byte swizzle
+  static constexpr int kTileBytes = NB * kBlockBytes;
+  static constexpr int NSW = HD == 64 ? 4 : 2;       // ring slots per warp
+  static constexpr int kRing = 4 * NSW * kTileBytes; // 128 KB
+  static constexpr int NKS = HD / 16;                // k-steps of q . k
+  static constexpr int NT = KT / 8;                  // n8 key tiles per tile
+  static constexpr int kMaxTiles = kWaMaxKeys / KT;
+  // byte offsets from the 1024-aligned base for `kt` tiles per CTA
+  static __host__ __device__ int q_off() { return kRing; }
+  static __host__ __device__ int sc_off() { return kRing + NB * 2048; }
+  static __host__ __device__ int sc_ld(int kt) { return kt * KT + 8; }
+  static __host__ __device__ int red_off(int kt) { return sc_off() + 16 * sc_ld(kt) * 2; }
+  static __host__ __device__ int bar_off(int kt) { return red_off(kt) + 192 * 4; }
+  static __host__ __device__ int bytes(int kt) { return 1024 + bar_off(kt) + 4 * NSW * 8 + 16; }
 };
 
 template <int HD>
-__global__ void __launch_bounds__(128) dattn_fused_kernel(const __grid_constant__ CUtensorMap kmap,
-                                                          const __grid_constant__ CUtensorMap vmap, FAttnParams p) {
-  using S = FaSmem<HD>;
-  constexpr int NB = S::NB;
-  constexpr int WCOLS = HD / 4;
-  constexpr int NT = WCOLS / 8;
+__global__ void __launch_bounds__(128) dattn_warp_kernel(const __grid_constant__ CUtensorMap kmap,
+                                                         const __grid_constant__ CUtensorMap vmap, FAttnParams p) {
+  using C = WaCfg<HD>;
+  constexpr int KT = C::KT, NSW = C::NSW;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const int ns = p.n_stages, kt_cap = p.kt_cap;
+  const int kt_cap = p.kt_cap;
   uint8_t* ring = smem;
-  uint8_t* qs = smem + S::q_off(ns);
-  bf16* sc = reinterpret_cast<bf16*>(smem + S::sc_off(ns));
-  const int sc_ld = S::sc_ld(kt_cap);
-  bf16* ptile = reinterpret_cast<bf16*>(smem + S::p_off(ns, kt_cap));
-  float* red = reinterpret_cast<float*>(smem + S::red_off(ns, kt_cap));   // [4 warps][16]
-  float* cmax = red + 64;        // [16] this CTA's row maxima (read by the cluster)
+  uint8_t* qs = smem + C::q_off();
+  bf16* sc = reinterpret_cast<bf16*>(smem + C::sc_off());
+  const int sc_ld = C::sc_ld(kt_cap);
+  float* redm = reinterpret_cast<float*>(smem + C::red_off(kt_cap));   // [4 warps][16] row maxima
+  float* reds = redm + 64;                                               // [4 warps][16] row exp-sums
+  float* cmax = reds + 64;       // [16] this CTA's row maxima (read by the cluster)
   float* csum = cmax + 16;       // [16] this CTA's row exp-sums (read by the cluster)
   float* Mrow = csum + 16;       // [16] cluster row maxima
   float* Lrow = Mrow + 16;       // [16] cluster row sums
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::bar_off(ns, kt_cap));
-  float* opart = reinterpret_cast<float*>(ring);   // [16][HD], reuses the ring once every tile is consumed
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::bar_off(kt_cap));
+  float* opart = reinterpret_cast<float*>(ring);   // [4 warps][16][HD], once every tile is consumed
 
   const int CS = gridDim.x;
   const uint32_t rank = cluster_ctarank();
   const int kvh = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_trigger();
   pdl_wait();
 
   int valid = p.len_ptr[b] + p.len_add;
@@ -403,37 +411,42 @@ __global__ void __launch_bounds__(128) dattn_fused_kernel(const __grid_constant_
     valid = p.T;
   }
   const int lo = (p.window > 0 && valid > p.window) ? valid - p.window : 0;
-  const int n_tiles = valid > lo ? (valid - lo + kFaKT - 1) / kFaKT : 0;
+  const int n_tiles = valid > lo ? (valid - lo + KT - 1) / KT : 0;
   int tpc = (n_tiles + CS - 1) / CS;
   if (tpc > kt_cap) {
     set_status(p.status, JX_ERR_RANGE);
     tpc = kt_cap;
   }
   const int my0 = (int)rank * tpc;
-  const int my_n = max(0, min(tpc, n_tiles - my0));       // tiles of this CTA
-  const int key0 = lo + my0 * kFaKT;                       // first key of this CTA
-  const int n_loads = 2 * my_n;                            // K tiles, then V tiles
+  const int my_n = max(0, min(tpc, n_tiles - my0));         // tiles of this CTA
+  const int key0 = lo + my0 * KT;                           // first key of this CTA
+  const int nw = my_n > warp ? (my_n - warp + 3) / 4 : 0;   // tiles of this warp: warp, warp+4, ...
   const long long row0 = p.layer_row0 + (long long)b * p.T;
+  uint64_t* wbar = bars + warp * NSW;
+  uint8_t* wring = ring + warp * NSW * C::kTileBytes;
 
-  auto issue = [&](int ld) {
-    const int s = ld % ns;
-    const bool is_v = ld >= my_n;
-    const int i = is_v ? ld - my_n : ld;
-    mbar_arrive_expect_tx(&full[s], S::kTileBytes);
-    const int y = (int)(row0 + key0 + i * kFaKT);
+  // load q of this warp: K tiles j = 0..nw-1, then V tiles (tile index warp + 4j)
+  auto issue = [&](int q) {
+    const int slot = q % NSW;
+    const bool is_v = q >= nw;
+    const int i = warp + 4 * (is_v ? q - nw : q);
+    mbar_arrive_expect_tx(&wbar[slot], C::kTileBytes);
+    const int y = (int)(row0 + key0 + i * KT);
 #pragma unroll
-    for (int c = 0; c < NB; ++c)
-      tma_load_2d(ring + s * S::kTileBytes + c * 8192, is_v ? &vmap : &kmap, kvh * HD + c * 64, y, &full[s]);
+    for (int c = 0; c < C::NB; ++c)
+      tma_load_2d(wring + slot * C::kTileBytes + c * C::kBlockBytes, is_v ? &vmap : &kmap, kvh * HD + c * 64, y,
+                  &wbar[slot]);
   };
-  if (threadIdx.x == 0) {
-    prefetch_tmap(&kmap);
-    prefetch_tmap(&vmap);
-    for (int s = 0; s < ns; ++s) mbar_init(&full[s], 1);
+  if (lane == 0) {
+    if (warp == 0) {
+      prefetch_tmap(&kmap);
+      prefetch_tmap(&vmap);
+    }
+    for (int s = 0; s < NSW; ++s) mbar_init(&wbar[s], 1);
     fence_barrier_init();
-    for (int ld = 0; ld < min(ns, n_loads); ++ld) issue(ld);
+    for (int q = 0; q < min(NSW, 2 * nw); ++q) issue(q);
   }
-  pdl_trigger();
-  // Q rows of this head group (rows >= n_rep are zero) into the swizzled layout.
+  // Q rows of this head group (rows >= n_rep are zero) into the swizzled layout, then into registers.
   for (int idx = threadIdx.x; idx < 16 * (HD / 8); idx += 128) {
     const int r = idx / (HD / 8), cg = idx % (HD / 8);
     uint4 v = make_uint4(0, 0, 0, 0);
@@ -442,154 +455,190 @@ __global__ void __launch_bounds__(128) dattn_fused_kernel(const __grid_constant_
     asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w));
   }
   __syncthreads();
-
   const int mi = lane >> 3, r8 = lane & 7;
+  uint32_t qf[C::NKS][4];
+#pragma unroll
+  for (int ks = 0; ks < C::NKS; ++ks) {
+    const int row = (mi & 1) * 8 + r8, ch = ks * 2 + (mi >> 1);
+    ldsm_x4(swz(smem_u32(qs + (ch >> 3) * 2048), row, ch & 7), qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3]);
+  }
+
   bool ok = true;
+  // ---- scores of this warp's tiles ----
   float mrow[2] = {-INFINITY, -INFINITY};   // rows lane/4 and lane/4 + 8
-  // ---- scores of this CTA's keys ----
-  for (int i = 0; i < my_n; ++i) {
-    const int s = i % ns;
-    if (ok && !mbar_wait_bounded(&full[s], (i / ns) & 1)) {
+  for (int j = 0; j < nw; ++j) {
+    const int slot = j % NSW, i = warp + 4 * j;
+    if (ok && !mbar_wait_bounded(&wbar[slot], (j / NSW) & 1)) {
       set_status(p.status, JX_ERR_TIMEOUT);
       ok = false;
     }
-    float acc[2][4] = {};
-    if (ok) {
-      const uint32_t kb = smem_u32(ring + s * S::kTileBytes);
+    ok = __all_sync(0xffffffffu, ok);
+    float acc[C::NT][4];
 #pragma unroll
-      for (int ks = 0; ks < HD / 16; ++ks) {
-        uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
-        {
-          const int row = (mi & 1) * 8 + r8, ch = ks * 2 + (mi >> 1);
-          ldsm_x4(swz(smem_u32(qs + (ch >> 3) * 2048), row, ch & 7), a0, a1, a2, a3);
+    for (int t = 0; t < C::NT; ++t) acc[t][0] = acc[t][1] = acc[t][2] = acc[t][3] = 0.f;
+    if (ok) {
+      const uint32_t kb = smem_u32(wring + slot * C::kTileBytes);
+#pragma unroll
+      for (int ks = 0; ks < C::NKS; ++ks)
+#pragma unroll
+        for (int n16 = 0; n16 < C::NT / 2; ++n16) {
+          uint32_t b0, b1, b2, b3;
+          const int row = n16 * 16 + (mi >> 1) * 8 + r8, ch = ks * 2 + (mi & 1);
+          ldsm_x4(swz(kb + (ch >> 3) * C::kBlockBytes, row, ch & 7), b0, b1, b2, b3);
+          mma_bf16(acc[2 * n16], qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3], b0, b1);
+          mma_bf16(acc[2 * n16 + 1], qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3], b2, b3);
         }
-        {
-          const int row = warp * 16 + (mi >> 1) * 8 + r8, ch = ks * 2 + (mi & 1);
-          ldsm_x4(swz(kb + (ch >> 3) * 8192, row, ch & 7), b0, b1, b2, b3);
-        }
-        mma_bf16(acc[0], a0, a1, a2, a3, b0, b1);
-        mma_bf16(acc[1], a0, a1, a2, a3, b2, b3);
-      }
     }
 #pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
+    for (int t = 0; t < C::NT; ++t)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        const int kl = warp * 16 + nt * 8 + (lane & 3) * 2 + (e & 1);   // key within the tile
+        const int kl = t * 8 + (lane & 3) * 2 + (e & 1);
         const int row = (lane >> 2) + (e >> 1) * 8;
         float v = -INFINITY;
-        if (key0 + i * kFaKT + kl < valid) {
-          v = rnd<bf16>(rnd<bf16>(acc[nt][e]) * p.scale_bf16);
+        if (key0 + i * KT + kl < valid) {
+          v = rnd<bf16>(rnd<bf16>(acc[t][e]) * p.scale_bf16);
           mrow[e >> 1] = fmaxf(mrow[e >> 1], v);
         }
-        sc[row * sc_ld + i * kFaKT + kl] = __float2bfloat16_rn(v);
+        sc[row * sc_ld + i * KT + kl] = __float2bfloat16_rn(v);
       }
-    __syncthreads();   // every warp is done with stage s
-    if (threadIdx.x == 0 && i + ns < n_loads) issue(i + ns);
+    __syncwarp();   // every lane is done reading the slot
+    if (lane == 0 && ok && j + NSW < 2 * nw) {
+      fence_proxy_async();
+      issue(j + NSW);
+    }
   }
-  // ---- cluster row maxima ----
+  // ---- row maxima: warps, then the cluster ----
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
     mrow[h] = fmaxf(mrow[h], __shfl_xor_sync(0xffffffffu, mrow[h], 1));
     mrow[h] = fmaxf(mrow[h], __shfl_xor_sync(0xffffffffu, mrow[h], 2));
   }
   if ((lane & 3) == 0) {
-    red[warp * 16 + (lane >> 2)] = mrow[0];
-    red[warp * 16 + (lane >> 2) + 8] = mrow[1];
+    redm[warp * 16 + (lane >> 2)] = mrow[0];
+    redm[warp * 16 + (lane >> 2) + 8] = mrow[1];
   }
   __syncthreads();
   if (threadIdx.x < 16) {
     const int r = threadIdx.x;
-    cmax[r] = fmaxf(fmaxf(red[r], red[16 + r]), fmaxf(red[32 + r], red[48 + r]));
+    cmax[r] = fmaxf(fmaxf(redm[r], redm[16 + r]), fmaxf(redm[32 + r], redm[48 + r]));
   }
   cluster_sync_all();
   if (threadIdx.x < 16) {
     const int r = threadIdx.x;
-    float M = -INFINITY;
-    for (int cr = 0; cr < CS; ++cr) M = fmaxf(M, dsmem_ld_f32(dsmem_map(smem_u32(cmax + r), cr)));
+    float v[8];   // every remote read is issued before any is used
+#pragma unroll
+    for (int cr = 0; cr < 8; ++cr) v[cr] = cr < CS ? dsmem_ld_f32(dsmem_map(smem_u32(cmax + r), cr)) : -INFINITY;
+    float M = v[0];
+#pragma unroll
+    for (int cr = 1; cr < 8; ++cr) M = fmaxf(M, v[cr]);
     Mrow[r] = M;
   }
   __syncthreads();
-  // ---- cluster row sums of exp(s - max): warp w sums rows 4w .. 4w+3 over this CTA's keys ----
-  const int my_keys = max(0, min(my_n * kFaKT, valid - key0));
-#pragma unroll
-  for (int rr = 0; rr < 4; ++rr) {
-    const int r = warp * 4 + rr;
+  // ---- row sums of exp(s - max) over this warp's keys, then the warps, then the cluster ----
+  for (int r = 0; r < p.n_rep; ++r) {
     const float M = Mrow[r];
     float l = 0.f;
-    if (r < p.n_rep && M != -INFINITY)
-      for (int k = lane; k < my_keys; k += 32) l += expf(__bfloat162float(sc[r * sc_ld + k]) - M);
+    if (M != -INFINITY)
+      for (int j = 0; j < nw; ++j) {
+        const int i = warp + 4 * j;
+        for (int kl = lane; kl < KT; kl += 32)
+          if (key0 + i * KT + kl < valid) l += expf(__bfloat162float(sc[r * sc_ld + i * KT + kl]) - M);
+      }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-    if (lane == 0) csum[r] = l;
+    if (lane == 0) reds[warp * 16 + r] = l;
+  }
+  __syncthreads();
+  if (threadIdx.x < 16) {
+    const int r = threadIdx.x;
+    csum[r] = r < p.n_rep ? ((reds[r] + reds[16 + r]) + reds[32 + r]) + reds[48 + r] : 0.f;   // warp order
   }
   cluster_sync_all();
   if (threadIdx.x < 16) {
     const int r = threadIdx.x;
-    float L = 0.f;
-    for (int cr = 0; cr < CS; ++cr) L += dsmem_ld_f32(dsmem_map(smem_u32(csum + r), cr));
+    float v[8];
+#pragma unroll
+    for (int cr = 0; cr < 8; ++cr) v[cr] = cr < CS ? dsmem_ld_f32(dsmem_map(smem_u32(csum + r), cr)) : 0.f;
+    float L = v[0];   // rank order
+#pragma unroll
+    for (int cr = 1; cr < 8; ++cr) L += v[cr];
     Lrow[r] = L;
   }
   __syncthreads();
 
-  // ---- P . V over this CTA's keys ----
-  float acc[NT][4] = {};
-  for (int i = 0; i < my_n; ++i) {
-    for (int idx = threadIdx.x; idx < 16 * kFaKT; idx += 128) {
-      const int r = idx / kFaKT, k = idx % kFaKT;
-      float pv = 0.f;
-      const float M = Mrow[r], L = Lrow[r];
-      if (r < p.n_rep && key0 + i * kFaKT + k < valid && M != -INFINITY && L > 0.f)
-        pv = rnd<bf16>(expf(__bfloat162float(sc[r * sc_ld + i * kFaKT + k]) - M) / L);
-      ptile[r * kFaPLd + k] = __float2bfloat16_rn(pv);
-    }
-    __syncthreads();
-    const int ld = my_n + i, s = ld % ns;
-    if (ok && !mbar_wait_bounded(&full[s], (ld / ns) & 1)) {
+  // ---- P . V over this warp's tiles ----
+  const int g = lane >> 2, t4 = lane & 3;
+  const bool lo_row = g < p.n_rep, hi_row = g + 8 < p.n_rep;
+  const float Mlo = lo_row ? Mrow[g] : 0.f, Llo = lo_row ? Lrow[g] : 0.f;
+  const float Mhi = hi_row ? Mrow[g + 8] : 0.f, Lhi = hi_row ? Lrow[g + 8] : 0.f;
+  auto prob = [&](bool row_ok, int r, float M, float L, int i, int kl) -> float {
+    if (!row_ok || key0 + i * KT + kl >= valid || M == -INFINITY || !(L > 0.f)) return 0.f;
+    return rnd<bf16>(expf(__bfloat162float(sc[r * sc_ld + i * KT + kl]) - M) / L);
+  };
+  float oacc[HD / 8][4];
+#pragma unroll
+  for (int t = 0; t < HD / 8; ++t) oacc[t][0] = oacc[t][1] = oacc[t][2] = oacc[t][3] = 0.f;
+  for (int j = 0; j < nw; ++j) {
+    const int q = nw + j, slot = q % NSW, i = warp + 4 * j;
+    if (ok && !mbar_wait_bounded(&wbar[slot], (q / NSW) & 1)) {
       set_status(p.status, JX_ERR_TIMEOUT);
       ok = false;
     }
+    ok = __all_sync(0xffffffffu, ok);
     if (ok) {
-      const uint32_t vb = smem_u32(ring + s * S::kTileBytes);
+      const uint32_t vb = smem_u32(wring + slot * C::kTileBytes);
 #pragma unroll
-      for (int kk = 0; kk < kFaKT / 16; ++kk) {
-        uint32_t a0, a1, a2, a3;
-        {
-          const int row = (mi & 1) * 8 + r8, col = kk * 16 + (mi >> 1) * 8;
-          ldsm_x4(smem_u32(ptile + row * kFaPLd + col), a0, a1, a2, a3);
-        }
+      for (int kk = 0; kk < KT / 16; ++kk) {
+        // A fragment of the probabilities: rows g, g+8; keys c, c+1 and c+8, c+9 of this 16-key step
+        const int c = kk * 16 + t4 * 2;
+        const uint32_t a0 = pack_bf16x2(prob(lo_row, g, Mlo, Llo, i, c), prob(lo_row, g, Mlo, Llo, i, c + 1));
+        const uint32_t a1 = pack_bf16x2(prob(hi_row, g + 8, Mhi, Lhi, i, c), prob(hi_row, g + 8, Mhi, Lhi, i, c + 1));
+        const uint32_t a2 = pack_bf16x2(prob(lo_row, g, Mlo, Llo, i, c + 8), prob(lo_row, g, Mlo, Llo, i, c + 9));
+        const uint32_t a3 =
+            pack_bf16x2(prob(hi_row, g + 8, Mhi, Lhi, i, c + 8), prob(hi_row, g + 8, Mhi, Lhi, i, c + 9));
 #pragma unroll
-        for (int n16 = 0; n16 < NT / 2; ++n16) {
+        for (int n16 = 0; n16 < HD / 16; ++n16) {
           uint32_t b0, b1, b2, b3;
           const int row = kk * 16 + (mi & 1) * 8 + r8;
-          const int ch = (warp * WCOLS) / 8 + n16 * 2 + (mi >> 1);
-          ldsm_x4_t(swz(vb + (ch >> 3) * 8192, row, ch & 7), b0, b1, b2, b3);
-          mma_bf16(acc[n16 * 2], a0, a1, a2, a3, b0, b1);
-          mma_bf16(acc[n16 * 2 + 1], a0, a1, a2, a3, b2, b3);
+          const int ch = n16 * 2 + (mi >> 1);
+          ldsm_x4_t(swz(vb + (ch >> 3) * C::kBlockBytes, row, ch & 7), b0, b1, b2, b3);
+          mma_bf16(oacc[n16 * 2], a0, a1, a2, a3, b0, b1);
+          mma_bf16(oacc[n16 * 2 + 1], a0, a1, a2, a3, b2, b3);
         }
       }
     }
-    __syncthreads();   // stage s and the probability tile are free again
-    if (threadIdx.x == 0 && ld + ns < n_loads) issue(ld + ns);
+    __syncwarp();
+    if (lane == 0 && ok && q + NSW < 2 * nw) {
+      fence_proxy_async();
+      issue(q + NSW);
+    }
   }
-  // ---- partial outputs -> shared memory (the ring is idle: every issued tile has been consumed) ----
+  // ---- partial outputs: warps in warp order, then the cluster in rank order ----
+  __syncthreads();   // every warp is done with its slots: the ring becomes the partial-output buffer
 #pragma unroll
-  for (int nt = 0; nt < NT; ++nt)
+  for (int t = 0; t < HD / 8; ++t)
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      const int row = (lane >> 2) + (e >> 1) * 8;
-      const int col = warp * WCOLS + nt * 8 + (lane & 3) * 2 + (e & 1);
-      opart[row * HD + col] = acc[nt][e];
+      const int row = g + (e >> 1) * 8;
+      const int col = t * 8 + t4 * 2 + (e & 1);
+      opart[(warp * 16 + row) * HD + col] = oacc[t][e];
     }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < 16 * HD; idx += 128)
+    opart[idx] = ((opart[idx] + opart[16 * HD + idx]) + opart[32 * HD + idx]) + opart[48 * HD + idx];
   cluster_sync_all();
-  // ---- each CTA sums one slice of the [n_rep, HD] output over the cluster, in rank order ----
   const int total = p.n_rep * HD;
   const int chunk = (total + CS - 1) / CS;
   const int e0 = (int)rank * chunk, e1 = min(total, e0 + chunk);
   for (int idx = e0 + threadIdx.x; idx < e1; idx += 128) {
     const uint32_t la = smem_u32(opart + idx);
-    float sum = 0.f;
-    for (int cr = 0; cr < CS; ++cr) sum += dsmem_ld_f32(dsmem_map(la, cr));
+    float v[8];
+#pragma unroll
+    for (int cr = 0; cr < 8; ++cr) v[cr] = cr < CS ? dsmem_ld_f32(dsmem_map(la, cr)) : 0.f;
+    float sum = v[0];   // rank order
+#pragma unroll
+    for (int cr = 1; cr < 8; ++cr) sum += v[cr];
     const int row = idx / HD, col = idx % HD;
     const long long ocol = (long long)(kvh * p.n_rep + row) * HD + col;
     p.out[k128_offset(b, ocol, p.out_rp)] = __float2bfloat16_rn(sum);
@@ -666,40 +715,51 @@ static int launch_dattn(const CUtensorMap& km, const CUtensorMap& vm, const DAtt
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
   cfg.dynamicSmemBytes = smem_a;
-  if (cudaLaunchKernelEx(&cfg, dattn_scores_kernel<HD>, km, p) != cudaSuccess) return JX_ERR_CUDA;
+  if (launch_ex(&cfg, dattn_scores_kernel<HD>, km, p) != cudaSuccess) return JX_ERR_CUDA;
   cfg.dynamicSmemBytes = smem_b;
-  if (cudaLaunchKernelEx(&cfg, dattn_pv_kernel<HD>, vm, p) != cudaSuccess) return JX_ERR_CUDA;
+  if (launch_ex(&cfg, dattn_pv_kernel<HD>, vm, p) != cudaSuccess) return JX_ERR_CUDA;
   return JX_OK;
 }
 
-// Cluster shape of the single-pass form for a key range of `range` keys: up to 8 CTAs of up to
-// kFaMaxTiles 64-key tiles each.  Returns false when the range needs more (the split form runs then).
-static bool fused_shape(int range, int hd, int& cs, int& kt, int& ns) {
-  const int n128 = (range + 127) / 128;
-  cs = n128 < 1 ? 1 : (n128 > 8 ? 8 : n128);
-  const int tiles = (range + kFaKT - 1) / kFaKT;
+// Cluster shape of the single-pass form for B x Hkv head groups over a key range of `range` keys: as
+// many CTAs per head group as fill the SMs once (one CTA per group when there are at least as many
+// groups as SMs), more when a CTA would hold more than kWaMaxKeys keys, at most 8.  Returns false when
+// the range needs more (the split form runs then).
+static bool fused_shape(int range, int kt_keys, int max_tiles, int groups, int sms, int& cs, int& kt) {
+  const int tiles = (range + kt_keys - 1) / kt_keys;
+  cs = groups >= sms ? 1 : sms / groups;
+  const int need = (tiles + max_tiles - 1) / max_tiles;
+  if (cs < need) cs = need;
+  if (cs > tiles) cs = tiles;
+  if (cs > 8) cs = 8;
+  if (cs < 1) cs = 1;
   kt = (tiles + cs - 1) / cs;
-  const int ns_max = hd == 256 ? 3 : 4;
-  ns = 2 * kt < ns_max ? 2 * kt : ns_max;
-  return kt <= kFaMaxTiles;
+  return kt <= max_tiles;
 }
 
 template <int HD>
-static int launch_dattn_fused(const CUtensorMap& km, const CUtensorMap& vm, const FAttnParams& p, int cs, bool pdl,
-                              cudaStream_t s) {
-  using S = FaSmem<HD>;
+static int launch_dattn_fused(const jx_dattn_args& a, FAttnParams& p, int sms, bool pdl, cudaStream_t s) {
+  using C = WaCfg<HD>;
+  const int range = (a.window > 0 && a.window < a.T) ? a.window : a.T;
+  int cs, kt;
+  if (!fused_shape(range, C::KT, C::kMaxTiles, a.B * a.Hkv, sms, cs, kt)) return JX_ERR_SHAPE;
+  CUtensorMap km, vm;
+  const long long cols = (long long)a.Hkv * a.hd;
+  int rc = make_tmap_2d_bf16_box(&km, a.k_base, a.cache_rows, cols, cols, C::KT);
+  if (rc == JX_OK) rc = make_tmap_2d_bf16_box(&vm, a.v_base, a.cache_rows, cols, cols, C::KT);
+  if (rc != JX_OK) return rc;
   static bool configured = false;
   if (!configured) {
-    const int max_bytes = S::bytes(HD == 256 ? 3 : 4, kFaMaxTiles);
-    if (cudaFuncSetAttribute(dattn_fused_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, max_bytes) !=
-        cudaSuccess)
+    if (cudaFuncSetAttribute(dattn_warp_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             C::bytes(C::kMaxTiles)) != cudaSuccess)
       return JX_ERR_CUDA;
     configured = true;
   }
+  p.kt_cap = kt;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(cs, p.Hkv, p.B);
   cfg.blockDim = dim3(128);
-  cfg.dynamicSmemBytes = S::bytes(p.n_stages, p.kt_cap);
+  cfg.dynamicSmemBytes = C::bytes(kt);
   cfg.stream = s;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -710,11 +770,12 @@ static int launch_dattn_fused(const CUtensorMap& km, const CUtensorMap& vm, cons
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 2 : 1;
-  return cudaLaunchKernelEx(&cfg, dattn_fused_kernel<HD>, km, vm, p) == cudaSuccess ? JX_OK : JX_ERR_CUDA;
+  return launch_ex(&cfg, dattn_warp_kernel<HD>, km, vm, p) == cudaSuccess ? JX_OK : JX_ERR_CUDA;
 }
 
-// 0: by shape (the split form; the cluster form measured slower on the Llama-8B decode shapes), 1: split
-// form, 2: cluster form.
+// 0: by shape (the split form: on the Llama-8B decode shapes the single-pass form measured 22.7 us against
+// 20.4 us at context 640, its fewer warps leaving the mma.sync latency exposed), 1: split form,
+// 2: single-pass form.
 static int g_dattn_impl = 0;
 void set_dattn_impl(int impl) { g_dattn_impl = impl; }
 
@@ -724,17 +785,11 @@ int run_decode_attention(const jx_dattn_args& a, bool pdl, cudaStream_t stream) 
   if (n_rep > 16) return JX_ERR_SHAPE;
   if (a.hd != 64 && a.hd != 128 && a.hd != 256) return JX_ERR_SHAPE;
   if (reinterpret_cast<uintptr_t>(a.q) & 15) return JX_ERR_ARG;
-  CUtensorMap km, vm;
-  const long long cols = (long long)a.Hkv * a.hd;
-  int rc = make_tmap_2d_bf16(&km, a.k_base, a.cache_rows, cols, cols);
-  if (rc == JX_OK) rc = make_tmap_2d_bf16(&vm, a.v_base, a.cache_rows, cols, cols);
-  if (rc != JX_OK) return rc;
+  if (a.out_rp < a.B || a.out_rp % 8) return JX_ERR_ARG;   // the K128 output must hold every batch row
 
-  const int range = (a.window > 0 && a.window < a.T) ? a.window : a.T;
-  int cs, kt, ns;
-  const bool fits = fused_shape(range, a.hd, cs, kt, ns);
-  if (g_dattn_impl == 2 && !fits) return JX_ERR_SHAPE;
-  if (fits && g_dattn_impl == 2) {
+  if (g_dattn_impl == 2) {
+    int sms = 148, dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     FAttnParams f;
     f.B = a.B;
     f.Hq = a.Hq;
@@ -742,8 +797,8 @@ int run_decode_attention(const jx_dattn_args& a, bool pdl, cudaStream_t stream) 
     f.n_rep = n_rep;
     f.T = a.T;
     f.window = a.window;
-    f.kt_cap = kt;
-    f.n_stages = ns;
+    f.kt_cap = 0;
+    f._pad0 = 0;
     f.layer_row0 = a.layer_row0;
     f.q = reinterpret_cast<const bf16*>(a.q);
     f.len_ptr = a.len_ptr;
@@ -752,12 +807,20 @@ int run_decode_attention(const jx_dattn_args& a, bool pdl, cudaStream_t stream) 
     f.out = reinterpret_cast<bf16*>(a.out);
     f.out_rp = a.out_rp;
     f.status = a.status;
+    int frc;
     switch (a.hd) {
-      case 64: return launch_dattn_fused<64>(km, vm, f, cs, pdl, stream);
-      case 128: return launch_dattn_fused<128>(km, vm, f, cs, pdl, stream);
-      default: return launch_dattn_fused<256>(km, vm, f, cs, pdl, stream);
+      case 64: frc = launch_dattn_fused<64>(a, f, sms, pdl, stream); break;
+      case 128: frc = launch_dattn_fused<128>(a, f, sms, pdl, stream); break;
+      default: frc = launch_dattn_fused<256>(a, f, sms, pdl, stream); break;
     }
+    if (frc != JX_ERR_SHAPE || g_dattn_impl == 2) return frc;   // key range too long: the split form
   }
+
+  CUtensorMap km, vm;
+  const long long cols = (long long)a.Hkv * a.hd;
+  int rc = make_tmap_2d_bf16(&km, a.k_base, a.cache_rows, cols, cols);
+  if (rc == JX_OK) rc = make_tmap_2d_bf16(&vm, a.v_base, a.cache_rows, cols, cols);
+  if (rc != JX_OK) return rc;
 
   const int n_splits = dattn_n_splits(a.T, a.window);
   if (dattn_workspace_bytes(a.B, a.Hq, a.T, a.hd, n_splits) > a.ws_bytes) return JX_ERR_ARG;

@@ -96,11 +96,11 @@ int run_attention_generic(int dtype, const AttnArgs& p, bool pdl, cudaStream_t s
   if (dtype == JX_BF16) {
     if (smem > 48 * 1024)
       cudaFuncSetAttribute(attention_generic_kernel<bf16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    err = cudaLaunchKernelEx(&cfg, attention_generic_kernel<bf16>, p);
+    err = launch_ex(&cfg, attention_generic_kernel<bf16>, p);
   } else if (dtype == JX_F32) {
     if (smem > 48 * 1024)
       cudaFuncSetAttribute(attention_generic_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    err = cudaLaunchKernelEx(&cfg, attention_generic_kernel<float>, p);
+    err = launch_ex(&cfg, attention_generic_kernel<float>, p);
   } else {
     return JX_ERR_DTYPE;
   }

@@ -274,7 +274,7 @@ static int launch_pattn(const jx_pattn_args& a, const PAttnParams& p, bool pdl, 
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, pattn_kernel<HD, KT>, km, vm, p) == cudaSuccess ? JX_OK : JX_ERR_CUDA;
+  return launch_ex(&cfg, pattn_kernel<HD, KT>, km, vm, p) == cudaSuccess ? JX_OK : JX_ERR_CUDA;
 }
 
 int run_prefill_attention(const jx_pattn_args& a, bool pdl, cudaStream_t stream) {

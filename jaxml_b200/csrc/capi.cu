@@ -212,7 +212,8 @@ int jx_decode_attention(const jx_dattn_args* args, int pdl, void* stream) {
   const int rc = run_decode_attention(*args, pdl != 0, (cudaStream_t)stream);
   if (rc == JX_ERR_CUDA) return note_cuda("jx_decode_attention");
   if (rc != JX_OK)
-    return fail(rc, "jx_decode_attention: head_dim must be 64/128/256, Hq/Hkv <= 16, workspace large enough, "
+    return fail(rc, "jx_decode_attention: head_dim must be 64/128/256, Hq/Hkv <= 16, out_rp >= B and a multiple "
+                    "of 8, workspace large enough, "
                     "16-byte aligned q/cache");
   return JX_OK;
 }

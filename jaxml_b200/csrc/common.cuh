@@ -7,11 +7,33 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <mutex>
+#include <unordered_set>
+#include <utility>
+
 #include "../../include/jxb200.h"
 
 namespace jxb {
 
 typedef __nv_bfloat16 bf16;
+
+// Every kernel of this library runs with the largest shared-memory carveout (set once per kernel).
+// With one carveout for all, an SM never has to change its L1 / shared-memory split between two of
+// our kernels, so a CTA of the next kernel (launched early by programmatic dependent launch) can be
+// resident beside a CTA of the current one whenever their shared memory fits together.
+inline void prefer_max_shared(const void* kernel) {
+  static std::mutex mu;
+  static std::unordered_set<const void*> done;
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.insert(kernel).second)
+    cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
+}
+
+template <typename... ExpTypes, typename... ActTypes>
+inline cudaError_t launch_ex(const cudaLaunchConfig_t* cfg, void (*kernel)(ExpTypes...), ActTypes&&... args) {
+  prefer_max_shared(reinterpret_cast<const void*>(kernel));
+  return cudaLaunchKernelEx(cfg, kernel, std::forward<ActTypes>(args)...);
+}
 
 // ------------------------------------------------------------------------------------------------
 // Numerics helpers
@@ -99,6 +121,36 @@ __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gsrc, uint3
           smem_u32(smem_dst)),
       "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
+}
+
+// L2 residency policies (cache hints only: they never change results).  Weights and KV-cache rows are
+// read once per decode step, so they are loaded evict-first; the next projection's weights, prefetched
+// ahead of use, are kept evict-last until read.
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// bulk_g2s with an L2 cache policy.
+__device__ __forceinline__ void bulk_g2s_hint(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar,
+                                              uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(gsrc), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
+// Bulk prefetch of global memory into L2 (no shared memory, no completion to wait for).
+__device__ __forceinline__ void bulk_prefetch_l2(const void* gsrc, uint32_t bytes, uint64_t policy) {
+  asm volatile("cp.async.bulk.prefetch.L2.global.L2::cache_hint [%0], %1, %2;" ::"l"(gsrc), "r"(bytes), "l"(policy)
+               : "memory");
 }
 
 // 2-D tiled tensor copy global -> shared (TMA), completing on an mbarrier.
@@ -245,6 +297,13 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Acquire load of a global counter (pairs with a contributor's fence + atomicAdd).
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
 }
 
 // Status word shared by all kernels of a call: the first error code sticks.

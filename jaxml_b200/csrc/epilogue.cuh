@@ -12,6 +12,22 @@ namespace jxb {
 
 typedef jx_epilogue EpiParams;
 
+// L2 prefetch of the next decode projection's first weight chunks for CTA c (jx_epilogue.pf_w): the
+// same stream-K split as the next call (pf_grid CTAs over pf_np / pf_rows blocks x pf_kp / 128 chunks).
+__device__ __forceinline__ void prefetch_next_weights(const EpiParams& e, int c) {
+  if (!e.pf_w || e.pf_iters <= 0 || c >= e.pf_grid) return;
+  const long long R = e.pf_rows, kc = e.pf_kp >> 7;
+  const long long total = (e.pf_np / R) * kc;
+  const long long it0 = total * c / e.pf_grid, it1 = total * (c + 1) / e.pf_grid;
+  const long long n = it1 - it0 < e.pf_iters ? it1 - it0 : e.pf_iters;
+  const uint64_t pol = l2_policy_evict_last();
+  const bf16* w = reinterpret_cast<const bf16*>(e.pf_w);
+  for (long long i = 0; i < n; ++i) {
+    const long long it = it0 + i, nb = it / kc, kk = it - nb * kc;
+    bulk_prefetch_l2(w + ((kk * (e.pf_np >> 3) + nb * (R >> 3)) << 10), (uint32_t)(R * 256), pol);
+  }
+}
+
 template <typename T>
 __device__ __forceinline__ float bias_at(const EpiParams& e, long long n) {
   return e.bias ? to_f(reinterpret_cast<const T*>(e.bias)[n]) : 0.0f;

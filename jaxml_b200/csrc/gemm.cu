@@ -177,7 +177,7 @@ int run_gemm_k128(const bf16* X, const bf16* W, long long Mp, long long Np, long
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, gemm_k128_kernel, X, W, Mp, Np, Kp, e, status) == cudaSuccess ? JX_OK
+  return launch_ex(&cfg, gemm_k128_kernel, X, W, Mp, Np, Kp, e, status) == cudaSuccess ? JX_OK
                                                                                               : JX_ERR_CUDA;
 }
 
@@ -244,7 +244,7 @@ int run_gemm_f32(const float* X, long long ldx, const float* W, int M, int N, in
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, gemm_f32_kernel, X, ldx, W, M, N, K, e) == cudaSuccess ? JX_OK : JX_ERR_CUDA;
+  return launch_ex(&cfg, gemm_f32_kernel, X, ldx, W, M, N, K, e) == cudaSuccess ? JX_OK : JX_ERR_CUDA;
 }
 
 }  // namespace jxb

@@ -275,7 +275,7 @@ int run_gemm_tc(const bf16* X, const bf16* W, long long Mp, long long Np, long l
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, gemm_tc_kernel, wm, xm, p) == cudaSuccess ? JX_OK : JX_ERR_CUDA;
+  return launch_ex(&cfg, gemm_tc_kernel, wm, xm, p) == cudaSuccess ? JX_OK : JX_ERR_CUDA;
 }
 
 }  // namespace jxb

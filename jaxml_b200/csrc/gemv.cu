@@ -84,10 +84,11 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
         const long long kk = it % kc;
         return X + ((kk * (Mp >> 3)) << 10);
       };
+      const uint64_t pol_w = l2_policy_evict_first();   // weights are read once per step
       // Weights do not depend on the previous kernel: start streaming them before waiting on it.
       for (int i = 0; i < pre; ++i) {
         mbar_arrive_expect_tx(&full[i], C::kStageBytes);
-        bulk_g2s(smem + i * C::kStageBytes, wsrc(it0 + i), C::kWBytes, &full[i]);
+        bulk_g2s_hint(smem + i * C::kStageBytes, wsrc(it0 + i), C::kWBytes, &full[i], pol_w);
       }
       pdl_wait();
       for (int i = 0; i < pre; ++i)
@@ -102,7 +103,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
           break;
         }
         mbar_arrive_expect_tx(&full[s], C::kStageBytes);
-        bulk_g2s(smem + s * C::kStageBytes, wsrc(it0 + i), C::kWBytes, &full[s]);
+        bulk_g2s_hint(smem + s * C::kStageBytes, wsrc(it0 + i), C::kWBytes, &full[s], pol_w);
         bulk_g2s(smem + s * C::kStageBytes + C::kWBytes, xsrc(it0 + i), C::kXBytes, &full[s]);
         issued = i + 1;
       }
@@ -114,6 +115,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
           break;
         }
       }
+      // Every own load has landed: warm L2 with what this CTA of the next projection reads first, while
+      // this CTA's split-K finish and epilogue run.
+      if (!sh[0]) prefetch_next_weights(e, c);
     }
     return;
   }
@@ -216,19 +220,33 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
         const int nbf = (int)(it_begin(total, G, cc) / kc);
         return cc * 2 + (nb == nbf ? 0 : 1);
       };
-      float* my = ws + (long long)slot_of(c) * Mp * kGemvBN;
-      for (int idx = tid; idx < Mp * kGemvBN; idx += kGemvConsumers) my[idx] = tile[(idx >> 6) * kTileLd + (idx & 63)];
-      __threadfence();
-      named_bar_sync(1, kGemvConsumers);
-      if (tid == 0) {
-        const int prev = atomicAdd(&counters[nb], 1);
-        sh[1] = (prev == c_last - c_first) ? 1 : 0;
+      // The CTA holding the block's first K chunks reaches the block last (they end its range, while the
+      // other contributors' parts start theirs).  When every other contributor has already published, it
+      // sums without publishing its own partial: its own values come from the tile.
+      bool fast = false;
+      if (c == c_first) {
+        if (tid == 0) sh[1] = (ld_acquire_gpu(&counters[nb]) == c_last - c_first) ? 1 : 0;
+        named_bar_sync(1, kGemvConsumers);
+        fast = sh[1] != 0;
+        named_bar_sync(1, kGemvConsumers);
       }
-      named_bar_sync(1, kGemvConsumers);
-      do_epi = sh[1] != 0;
+      if (fast) {
+        do_epi = true;
+      } else {
+        float* my = ws + (long long)slot_of(c) * Mp * kGemvBN;
+        for (int idx = tid; idx < Mp * kGemvBN; idx += kGemvConsumers) my[idx] = tile[(idx >> 6) * kTileLd + (idx & 63)];
+        __threadfence();
+        named_bar_sync(1, kGemvConsumers);
+        if (tid == 0) {
+          const int prev = atomicAdd(&counters[nb], 1);
+          sh[1] = (prev == c_last - c_first) ? 1 : 0;
+        }
+        named_bar_sync(1, kGemvConsumers);
+        do_epi = sh[1] != 0;
+      }
       if (do_epi) {
         __threadfence();
-        // Sum every contribution (this CTA's too, already in the workspace) in CTA order.  Each thread
+        // Sum every contribution (this CTA's too) in CTA order.  Each thread
         // owns MT float4 groups of the tile; the loads of up to 4 contributors are all issued before
         // any is added, so the L2 round trips overlap instead of following one another.
         float4 acc4[MT];
@@ -237,9 +255,17 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
             if (cc0 + u > c_last) break;
-            const float4* src = reinterpret_cast<const float4*>(ws + (long long)slot_of(cc0 + u) * Mp * kGemvBN);
+            if (fast && cc0 + u == c) {   // this CTA's own partial, still in the tile
 #pragma unroll
-            for (int q = 0; q < MT; ++q) v[u][q] = __ldcg(src + tid + q * kGemvConsumers);
+              for (int q = 0; q < MT; ++q) {
+                const int e0 = (tid + q * kGemvConsumers) * 4;
+                v[u][q] = *reinterpret_cast<const float4*>(tile + (e0 >> 6) * kTileLd + (e0 & 63));
+              }
+            } else {
+              const float4* src = reinterpret_cast<const float4*>(ws + (long long)slot_of(cc0 + u) * Mp * kGemvBN);
+#pragma unroll
+              for (int q = 0; q < MT; ++q) v[u][q] = __ldcg(src + tid + q * kGemvConsumers);
+            }
           }
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
@@ -299,7 +325,7 @@ static int launch_gemv(const bf16* W, const bf16* X, long long Np, long long Kp,
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  cudaError_t err = cudaLaunchKernelEx(&cfg, gemv_k128_kernel<MT>, W, X, Np, Kp, e, ws, counters, status);
+  cudaError_t err = launch_ex(&cfg, gemv_k128_kernel<MT>, W, X, Np, Kp, e, ws, counters, status);
   return err == cudaSuccess ? JX_OK : JX_ERR_CUDA;
 }
 
@@ -317,11 +343,31 @@ int run_gemv_tc(const bf16* W, const bf16* X, long long Np, long long Kp, int M,
 static int g_gemv_impl = 0;
 void set_gemv_impl(int impl) { g_gemv_impl = impl; }
 
-int run_gemv(const bf16* W, const bf16* X, long long Np, long long Kp, int M, const EpiParams& e, float* ws,
+static bool gemv_uses_tc(long long Np, int grid) {
+  return Np % 128 == 0 && (g_gemv_impl == 2 || (g_gemv_impl == 0 && Np / 128 >= (grid > 0 ? grid : 148)));
+}
+
+int run_gemv(const bf16* W, const bf16* X, long long Np, long long Kp, int M, const EpiParams& e_in, float* ws,
              long long ws_floats, int* counters, int* status, int grid, bool pdl, cudaStream_t stream) {
-  const bool tc_ok = Np % 128 == 0;
-  const bool use_tc = tc_ok && (g_gemv_impl == 2 || (g_gemv_impl == 0 && Np / 128 >= (grid > 0 ? grid : 148)));
-  if (use_tc) return run_gemv_tc(W, X, Np, Kp, M, e, ws, ws_floats, counters, status, grid, pdl, stream);
+  // L2 prefetch plan of the next decode projection (jx_epilogue.pf_w): the kernel and grid that call
+  // will get by the same rules, or no prefetch when its sizes or alignment are not a decode projection's.
+  EpiParams e = e_in;
+  e.pf_rows = 0;
+  e.pf_grid = 0;
+  if (e.pf_w && e.pf_iters > 0 && e.pf_np > 0 && e.pf_kp > 0) {
+    const int rows = gemv_uses_tc(e.pf_np, grid) ? 128 : 64;
+    const long long tot = (e.pf_np / rows) * (e.pf_kp / 128);
+    const int g = grid > 0 ? grid : 148;
+    if (e.pf_np % rows == 0 && e.pf_kp % 128 == 0 && !(reinterpret_cast<uintptr_t>(e.pf_w) & 15)) {
+      e.pf_rows = rows;
+      e.pf_grid = (int)(tot < g ? tot : g);
+    } else {
+      e.pf_w = nullptr;
+    }
+  } else {
+    e.pf_w = nullptr;
+  }
+  if (gemv_uses_tc(Np, grid)) return run_gemv_tc(W, X, Np, Kp, M, e, ws, ws_floats, counters, status, grid, pdl, stream);
   if (M <= 0 || M > 64) return JX_ERR_SHAPE;
   if (Np % kGemvBN || Kp % kGemvBK || Np <= 0 || Kp <= 0) return JX_ERR_SHAPE;
   const int mt = M <= 16 ? 1 : (M <= 32 ? 2 : 4);

@@ -95,9 +95,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       };
       auto xsrc = [&](long long it) { return X + (((it % kc) * (C::N >> 3)) << 10); };
       const int pre = n_it < C::kStages ? n_it : C::kStages;
+      const uint64_t pol_w = l2_policy_evict_first();   // weights are read once per step
       for (int i = 0; i < pre; ++i) {
         mbar_arrive_expect_tx(&full[i], C::kStageBytes);
-        bulk_g2s(smem + i * C::kStageBytes, wsrc(it0 + i), C::kWBytes, &full[i]);
+        bulk_g2s_hint(smem + i * C::kStageBytes, wsrc(it0 + i), C::kWBytes, &full[i], pol_w);
       }
       pdl_wait();
       for (int i = 0; i < pre; ++i)
@@ -111,12 +112,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           break;
         }
         mbar_arrive_expect_tx(&full[s], C::kStageBytes);
-        bulk_g2s(smem + s * C::kStageBytes, wsrc(it0 + i), C::kWBytes, &full[s]);
+        bulk_g2s_hint(smem + s * C::kStageBytes, wsrc(it0 + i), C::kWBytes, &full[s], pol_w);
         bulk_g2s(smem + s * C::kStageBytes + C::kWBytes, xsrc(it0 + i), C::kXBytes, &full[s]);
         issued = i + 1;
       }
       for (int i = (issued > C::kStages ? issued - C::kStages : 0); i < issued; ++i)
         if (!mbar_wait_bounded(&full[i % C::kStages], (i / C::kStages) & 1)) break;
+      // Every own load has landed: warm L2 with what this CTA of the next projection reads first, while
+      // this CTA's split-K finish and epilogue run.
+      if (!sh[0]) prefetch_next_weights(e, c);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
@@ -213,19 +217,33 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           const int nbf = (int)(tc_it_begin(total, G, cc) / kc);
           return cc * 2 + (nb == nbf ? 0 : 1);
         };
-        float* my = ws + (long long)slot_of(c) * Mp * kTcBN;
-        for (int idx = tid; idx < Mp * kTcBN; idx += 128) my[idx] = tile[(idx >> 7) * C::kLd + (idx & 127)];
-        __threadfence();
-        named_bar_sync(1, 128);
-        if (tid == 0) {
-          const int prev = atomicAdd(&counters[nb], 1);
-          sh[1] = (prev == c_last - c_first) ? 1 : 0;
+        // The CTA holding the block's first K chunks reaches the block last (they end its range, while
+        // the other contributors' parts start theirs).  When every other contributor has already
+        // published, it sums without publishing its own partial: its own values come from the tile.
+        bool fast = false;
+        if (c == c_first) {
+          if (tid == 0) sh[1] = (ld_acquire_gpu(&counters[nb]) == c_last - c_first) ? 1 : 0;
+          named_bar_sync(1, 128);
+          fast = sh[1] != 0;
+          named_bar_sync(1, 128);
         }
-        named_bar_sync(1, 128);
-        do_epi = sh[1] != 0;
+        if (fast) {
+          do_epi = true;
+        } else {
+          float* my = ws + (long long)slot_of(c) * Mp * kTcBN;
+          for (int idx = tid; idx < Mp * kTcBN; idx += 128) my[idx] = tile[(idx >> 7) * C::kLd + (idx & 127)];
+          __threadfence();
+          named_bar_sync(1, 128);
+          if (tid == 0) {
+            const int prev = atomicAdd(&counters[nb], 1);
+            sh[1] = (prev == c_last - c_first) ? 1 : 0;
+          }
+          named_bar_sync(1, 128);
+          do_epi = sh[1] != 0;
+        }
         if (do_epi) {
           __threadfence();
-          // Sum every contribution (this CTA's too, already in the workspace) in CTA order.  Each
+          // Sum every contribution (this CTA's too) in CTA order.  Each
           // thread owns 4*MT float4 groups of the tile, taken 4 at a time; the loads of up to 4
           // contributors are all issued before any is added, so the L2 round trips overlap.
 #pragma unroll
@@ -236,9 +254,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
               for (int u = 0; u < 4; ++u) {
                 if (cc0 + u > c_last) break;
-                const float4* src = reinterpret_cast<const float4*>(ws + (long long)slot_of(cc0 + u) * Mp * kTcBN);
+                if (fast && cc0 + u == c) {   // this CTA's own partial, still in the tile
 #pragma unroll
-                for (int q = 0; q < 4; ++q) v[u][q] = __ldcg(src + tid + (q0 + q) * 128);
+                  for (int q = 0; q < 4; ++q) {
+                    const int e0 = (tid + (q0 + q) * 128) * 4;
+                    v[u][q] = *reinterpret_cast<const float4*>(tile + (e0 >> 7) * C::kLd + (e0 & 127));
+                  }
+                } else {
+                  const float4* src = reinterpret_cast<const float4*>(ws + (long long)slot_of(cc0 + u) * Mp * kTcBN);
+#pragma unroll
+                  for (int q = 0; q < 4; ++q) v[u][q] = __ldcg(src + tid + (q0 + q) * 128);
+                }
               }
 #pragma unroll
               for (int u = 0; u < 4; ++u) {
@@ -310,7 +336,7 @@ static int launch_gemv_tc(const bf16* W, const bf16* X, long long Np, long long 
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, gemv_tc_kernel<MT>, W, X, Np, Kp, e, ws, counters, status) == cudaSuccess
+  return launch_ex(&cfg, gemv_tc_kernel<MT>, W, X, Np, Kp, e, ws, counters, status) == cudaSuccess
              ? JX_OK
              : JX_ERR_CUDA;
 }

@@ -292,7 +292,7 @@ int run_norm(int dtype, const NormArgs& p, bool pdl, cudaStream_t stream) {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, norm_vec_kernel, p) == cudaSuccess ? JX_OK : JX_ERR_CUDA;
+    return launch_ex(&cfg, norm_vec_kernel, p) == cudaSuccess ? JX_OK : JX_ERR_CUDA;
   }
   constexpr int NT = 256;
   const size_t smem = (size_t)(2 * p.d + NT / 32 + 1) * sizeof(float);
@@ -311,11 +311,11 @@ int run_norm(int dtype, const NormArgs& p, bool pdl, cudaStream_t stream) {
   if (dtype == JX_BF16) {
     if (smem > 48 * 1024)
       cudaFuncSetAttribute(norm_kernel<bf16, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    err = cudaLaunchKernelEx(&cfg, norm_kernel<bf16, NT>, p);
+    err = launch_ex(&cfg, norm_kernel<bf16, NT>, p);
   } else if (dtype == JX_F32) {
     if (smem > 48 * 1024)
       cudaFuncSetAttribute(norm_kernel<float, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    err = cudaLaunchKernelEx(&cfg, norm_kernel<float, NT>, p);
+    err = launch_ex(&cfg, norm_kernel<float, NT>, p);
   } else {
     return JX_ERR_DTYPE;
   }

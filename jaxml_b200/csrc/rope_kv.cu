@@ -89,9 +89,9 @@ int run_qkv_rope_append(int dtype, const QkvArgs& p, bool pdl, cudaStream_t stre
   cfg.numAttrs = pdl ? 1 : 0;
   cudaError_t err;
   if (dtype == JX_BF16)
-    err = cudaLaunchKernelEx(&cfg, qkv_rope_append_kernel<bf16>, p);
+    err = launch_ex(&cfg, qkv_rope_append_kernel<bf16>, p);
   else if (dtype == JX_F32)
-    err = cudaLaunchKernelEx(&cfg, qkv_rope_append_kernel<float>, p);
+    err = launch_ex(&cfg, qkv_rope_append_kernel<float>, p);
   else
     return JX_ERR_DTYPE;
   return err == cudaSuccess ? JX_OK : JX_ERR_CUDA;

@@ -178,9 +178,9 @@ int run_sample(const SampleArgs& p, bool pdl, cudaStream_t stream) {
   cfg.numAttrs = pdl ? 1 : 0;
   cudaError_t err;
   if (p.dtype == JX_BF16)
-    err = cudaLaunchKernelEx(&cfg, sample_kernel<bf16>, p);
+    err = launch_ex(&cfg, sample_kernel<bf16>, p);
   else if (p.dtype == JX_F32)
-    err = cudaLaunchKernelEx(&cfg, sample_kernel<float>, p);
+    err = launch_ex(&cfg, sample_kernel<float>, p);
   else
     return JX_ERR_DTYPE;
   return err == cudaSuccess ? JX_OK : JX_ERR_CUDA;

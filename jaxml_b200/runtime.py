@@ -382,13 +382,28 @@ class DecoderRuntime:
         self._launches += 1
         N.check(N.load().jx_norm(args, W.jdt, 1, self.stream_ptr()), "jx_norm")
 
+    # L2 prefetch of the next decode projection's weights (jx_epilogue.pf_*) is off: on the Llama-8B
+    # decode step every budget tried made the step slower (4.39 ms off, 4.46-4.99 ms on).
+    l2_prefetch = False
+
+    def _pf(self, w_t, Np, Kp, budget=40e6):
+        """L2 prefetch request for the next decode projection (jx_epilogue.pf_*): its weights, and how many
+        128-wide K chunks per CTA fit `budget` bytes over the grid (the library clamps it to what each
+        CTA of that call reads).  None while `l2_prefetch` is off."""
+        if not self.l2_prefetch:
+            return None
+        rows = 128 if (Np % 128 == 0 and Np // 128 >= self.grid) else 64
+        return (w_t, Np, Kp, max(1, int(budget // (self.grid * rows * 256))))
+
     def _linear(self, acts, w_t, Np, Kp, x_key, kind, *, N_valid, bias=None, out=None, ldo=0, out_rp=0, res=None,
-                ldr=0, res2=None, ldr2=0, K_logical=None, N_cols=None):
+                ldr=0, res2=None, ldr2=0, K_logical=None, N_cols=None, pf=None):
         W = self.w
         e = N.JxEpilogue()
         e.kind, e.M, e.N = kind, acts["M"], N_valid
         e.bias, e.out, e.ldo, e.out_rp = ptr(bias), ptr(out), ldo, out_rp
         e.res, e.ldr, e.res2, e.ldr2 = ptr(res), ldr, ptr(res2), ldr2
+        if pf is not None and W.bf16 and acts["Mp"] <= 64:
+            e.pf_w, e.pf_np, e.pf_kp, e.pf_iters = ptr(pf[0]), pf[1], pf[2], pf[3]
         lib = N.load()
         self._launches += 1
         if not W.bf16:
@@ -414,8 +429,10 @@ class DecoderRuntime:
         W = self.w
         for li, lw in enumerate(W.layers):
             nx = W.layers[li + 1] if li + 1 < len(W.layers) else None
+            # o_proj's weights are prefetched into L2 whole, during RoPE and attention
             self._linear(acts, lw.wqkv, W.Np_qkv, W.Kp_d, "xn", N.JX_EPI_STORE, N_valid=W.nqkv, bias=lw.bqkv,
-                         out=acts["qkv"], ldo=W.nqkv, K_logical=W.d, N_cols=W.nqkv)
+                         out=acts["qkv"], ldo=W.nqkv, K_logical=W.d, N_cols=W.nqkv,
+                         pf=self._pf(lw.wo, W.Np_d, W.Kp_o, budget=64e6))
             self._qkv_rope_append(acts, li, lw, S, decode)
             if decode and self.fast_attn:
                 self._decode_attention(acts, li, lw)
@@ -493,16 +510,20 @@ class DecoderRuntime:
         tp = self.comm is not None
         parallel = fam == "neox" and cfg.use_parallel_residual
         store = N.JX_EPI_STORE_F32 if tp else N.JX_EPI_STORE
+        # each decode projection warms L2 with the first weights of the one after it
+        pf_gu = self._pf(lw.wgu, W.Np_gu, W.Kp_d)
+        pf_d = self._pf(lw.wd, W.Np_d, W.Kp_f)
+        pf_next = self._pf(nx.wqkv, W.Np_qkv, W.Kp_d) if nx is not None else self._pf(W.lm_head, W.Np_v, W.Kp_d)
         if fam == "gemma3" or parallel or tp:
             # o_proj result kept apart: Gemma normalises it, NeoX's parallel residual adds it with the
             # MLP output, and under tensor parallelism it is a partial sum to all-reduce first.
             self._linear(acts, lw.wo, W.Np_d, W.Kp_o, "attn", store, N_valid=d, bias=lw.bo,
-                         out=acts["tmp"], ldo=d, K_logical=W.Hq * hd, N_cols=d)
+                         out=acts["tmp"], ldo=d, K_logical=W.Hq * hd, N_cols=d, pf=pf_gu)
             if not parallel:
                 self._allreduce(acts["tmp"], M)
         else:
             self._linear(acts, lw.wo, W.Np_d, W.Kp_o, "attn", N.JX_EPI_RESID, N_valid=d, bias=lw.bo,
-                         out=acts["h"], ldo=d, res=acts["h"], ldr=d, K_logical=W.Hq * hd, N_cols=d)
+                         out=acts["h"], ldo=d, res=acts["h"], ldr=d, K_logical=W.Hq * hd, N_cols=d, pf=pf_gu)
         # ---- MLP input ----
         if fam == "gemma3":
             pa = lw.norms["post_attention_layernorm"]
@@ -522,12 +543,13 @@ class DecoderRuntime:
         if W.glu:
             kind = N.JX_EPI_GLU_SILU if fam == "llama" else N.JX_EPI_GLU_GELU_TANH
             self._linear(acts, lw.wgu, W.Np_gu, W.Kp_d, mlp_in, kind, N_valid=W.F, bias=lw.bgu,
-                         out=acts["act"], ldo=W.F32, out_rp=Mp if W.bf16 else 0, K_logical=d, N_cols=2 * W.F32)
+                         out=acts["act"], ldo=W.F32, out_rp=Mp if W.bf16 else 0, K_logical=d, N_cols=2 * W.F32,
+                         pf=pf_d)
         else:
             self._linear(acts, lw.wgu, W.Np_gu, W.Kp_d, mlp_in, N.JX_EPI_ACT_GELU_ERF, N_valid=W.F, bias=lw.bgu,
-                         out=acts["act"], ldo=W.F, out_rp=Mp if W.bf16 else 0, K_logical=d, N_cols=W.F)
+                         out=acts["act"], ldo=W.F, out_rp=Mp if W.bf16 else 0, K_logical=d, N_cols=W.F, pf=pf_d)
         Fk = W.F32 if (W.glu and not W.bf16) else W.F
-        down_kw = dict(N_valid=d, bias=lw.bd, K_logical=Fk, N_cols=d)
+        down_kw = dict(N_valid=d, bias=lw.bd, K_logical=Fk, N_cols=d, pf=pf_next)
         if parallel and tp:
             # tmp = attn_partial + mlp_partial, all-reduced once; h += tmp in the next norm.
             self._linear(acts, lw.wd, W.Np_d, W.Kp_f, "act", N.JX_EPI_ACC_F32, out=acts["tmp"], ldo=d, **down_kw)
@@ -574,8 +596,9 @@ class DecoderRuntime:
         dec = self.dec
         fw, fb = W.final_norm
         self._norm(acts_src, w=fw, b=fb, row_map=row_map, M=self.B, out_acts=dec)
+        l0 = W.layers[0]   # the next decode step starts with layer 0's qkv projection
         self._linear(dec, W.lm_head, W.Np_v, W.Kp_d, "xn", N.JX_EPI_STORE, N_valid=W.V, out=self.logits_buf(),
-                     ldo=W.V, K_logical=W.d, N_cols=W.V)
+                     ldo=W.V, K_logical=W.d, N_cols=W.V, pf=self._pf(l0.wqkv, W.Np_qkv, W.Kp_d))
 
     def logits_buf(self):
         if getattr(self, "_logits", None) is None:

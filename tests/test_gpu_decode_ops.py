@@ -102,9 +102,10 @@ def attn_form(request):
     N.call("jx_set_decode_attention_impl", 0)
 
 
-@pytest.mark.parametrize("hd,Hq,Hkv,window", [(128, 32, 8, 0), (256, 16, 8, 0), (256, 16, 8, 100), (64, 8, 8, 0),
-                                               (128, 16, 1, 0), (128, 64, 8, 0)])
-def test_decode_attention_matches_oracle(attn_form, hd, Hq, Hkv, window):
+@pytest.mark.parametrize("hd,Hq,Hkv,window,B", [(128, 32, 8, 0, 3), (256, 16, 8, 0, 3), (256, 16, 8, 100, 3),
+                                                 (64, 8, 8, 0, 3), (128, 16, 1, 0, 3), (128, 64, 8, 0, 3),
+                                                 (128, 32, 8, 0, 20)])
+def test_decode_attention_matches_oracle(attn_form, hd, Hq, Hkv, window, B):
     """Tensor-core decode attention (single-pass cluster form and two-kernel split form) vs the oracle's
     Attention.mha on a padded cache.
 
@@ -116,8 +117,9 @@ def test_decode_attention_matches_oracle(attn_form, hd, Hq, Hkv, window):
 
     N = _n()
     torch.manual_seed(5)
-    B, T, L = 3, 768, 2
-    lens = torch.tensor([513, 200, 767], dtype=torch.int32)      # valid keys after the append
+    T, L = 768, 2
+    # valid keys after the append (B=20: 160 head groups, one CTA per group in the cluster form)
+    lens = torch.tensor(([513, 200, 767] * 7)[:B], dtype=torch.int32)
     kc = torch.randn(L, B, T, Hkv, hd).to(torch.bfloat16)
     vc = torch.randn(L, B, T, Hkv, hd).to(torch.bfloat16)
     q = torch.randn(B, Hq, hd).to(torch.bfloat16)
@@ -125,7 +127,7 @@ def test_decode_attention_matches_oracle(attn_form, hd, Hq, Hkv, window):
     layer = 1
     kd, vd, qd = kc.cuda(), vc.cuda(), q.cuda()
     pos = (lens - 2).cuda()
-    Mp = 16
+    Mp = _rup(B, 16)          # output rows of the K128 layout: every batch row must fit
     Kp = _rup(Hq * hd, 128)
     out = torch.zeros(Mp * Kp, dtype=torch.bfloat16, device="cuda")
     nb = N.LL()

@@ -15,7 +15,7 @@ def test_library_exports_every_header_symbol():
 
 def test_struct_layouts_match_the_header():
     # sizes compiled from include/jxb200.h with the host compiler (x86-64 LP64)
-    assert ctypes.sizeof(N.JxEpilogue) == 80
+    assert ctypes.sizeof(N.JxEpilogue) == 112
     assert ctypes.sizeof(N.JxNormArgs) == 192
     assert ctypes.sizeof(N.JxQkvArgs) == 128
     assert ctypes.sizeof(N.JxAttnArgs) == 104
@@ -31,3 +31,23 @@ def test_argument_errors_are_reported_without_a_gpu():
     assert lib.jx_linear_decode_workspace(148, 65, out) == N.JX_ERR_SHAPE
     # two partial-tile slots per CTA of 16 rows x 128 columns
     assert lib.jx_linear_decode_workspace(148, 16, out) == N.JX_OK and out.value == 148 * 2 * 16 * 128
+
+
+def test_decode_attention_rejects_an_output_too_small_for_the_batch():
+    """The K128 attention output must hold every batch row (out_rp >= B, a multiple of 8); the check runs
+    on the host before any device work, so it needs no GPU."""
+    lib = N.load()
+    a = N.JxDAttnArgs()
+    a.B, a.Hq, a.Hkv, a.hd, a.T, a.window, a.cache_rows, a.layer_row0 = 20, 32, 8, 128, 768, 0, 20 * 768, 0
+    fake = 1 << 20   # never dereferenced: the call fails before touching memory
+    a.q = a.k_base = a.v_base = a.out = a.ws = a.counters = a.len_ptr = fake
+    a.len_add, a.scale, a.ws_bytes = 2, 128 ** -0.5, 1 << 30
+    for rp in (16, 20):
+        a.out_rp = rp
+        assert lib.jx_decode_attention(a, 0, None) == N.JX_ERR_ARG
+        assert b"out_rp" in lib.jx_last_error()
+    for impl in (0, 1, 2, 3):
+        assert lib.jx_set_decode_attention_impl(impl) == (N.JX_OK if impl <= 2 else N.JX_ERR_ARG)
+        assert lib.jx_set_prefill_linear_impl(impl) == (N.JX_OK if impl <= 2 else N.JX_ERR_ARG)
+    lib.jx_set_decode_attention_impl(0)
+    lib.jx_set_prefill_linear_impl(0)
