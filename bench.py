@@ -51,7 +51,7 @@ def parse():
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--micro", choices=["gemv", "attn"], default=None,
+    ap.add_argument("--micro", choices=["gemv", "attn", "allreduce"], default=None,
                     help="single-kernel microbenchmark on Llama-3-8B layer shapes instead of the decode step")
     ap.add_argument("--ctx", type=int, default=4096, help="context length of --micro attn")
     ap.add_argument("--shape", default="28672,4096", help="N,K of --micro gemv (default: fused gate/up)")
@@ -390,6 +390,71 @@ def _graph_ms(launch_all, n, reps=5):
     return start.elapsed_time(end) / (reps * n)
 
 
+def micro_allreduce(args):
+    """Latency of one decode-step all-reduce of the row-parallel partial sums (batch x 4096 float32) at
+    TP = WORLD_SIZE (launch under torchrun): NCCL vs the NVLink peer kernel, each captured 64 times in a
+    CUDA graph and replayed; max over ranks.  Prints one JSON line from rank 0."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from jaxml_b200.engine import TPComm
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world < 2:
+        print(json.dumps({"micro": "allreduce", "skipped": "needs WORLD_SIZE >= 2 (torchrun)"}))
+        return
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    comm = TPComm()
+    n = args.batch * 4096
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    comm.prepare_peer(dev)
+    plain = torch.randn(n, device=dev)
+    res = torch.empty(n, device=dev)
+    for b in comm.peer.data:
+        b[:n].copy_(torch.randn(n, device=dev))
+
+    def peer_call():
+        comm.all_reduce_partial(comm.partial_buffer(n), res, status)
+    out = {}
+    for name, fn in (("nccl", lambda: dist.all_reduce(plain)), ("peer", peer_call)):
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(3):
+                fn()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            for _ in range(64):
+                fn()
+        g.replay()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(5):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / (5 * 64) * 1e3], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        out[name] = float(t.item())
+        del g
+    st = int(status.item())
+    comm.close()
+    if rank == 0:
+        print(json.dumps({"micro": "allreduce", "world": world, "floats": n, "bytes": 4 * n,
+                          "nccl_us": out["nccl"], "peer_us": out["peer"], "status": st}), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def micro(args):
     """Single-kernel microbenchmarks on Llama-3-8B layer shapes (bf16, N(0,1) activations, N(0,0.02)
     weights): `gemv` = the decode projection on the gate/up weights of 8 distinct layers (1.9 GB, larger
@@ -464,6 +529,9 @@ def micro(args):
 
 def main():
     args = parse()
+    if args.micro == "allreduce":
+        micro_allreduce(args)
+        return
     if args.micro:
         micro(args)
         return

@@ -278,6 +278,27 @@ int jx_sample_finalize(const jx_sample_args* args, const unsigned long long* gat
 /* Clear the split-K counters after an error (they are self-resetting otherwise). */
 int jx_memset_async(void* ptr, int value, long long bytes, void* stream);
 
+/* ---- tensor parallelism over NVLink peer memory ----
+ * The reference all-reduces the row-parallel o_proj / down_proj outputs through XLA's GSPMD collectives
+ * (inference_engine/engine.py:258-267 sharding rules, models/llama.py:133-137 residual adds); these
+ * calls replace that collective for decode-sized messages.  Each rank allocates one region with
+ * jx_comm_alloc (layout from jx_allreduce_layout for max_floats: flags and counters, then two float32
+ * partials buffers at data_offset0 / data_offset1), shares it with jx_ipc_get_handle (64-byte handle,
+ * exchanged by the caller) and maps the other ranks' regions with jx_ipc_open_handle.
+ * jx_allreduce_f32 sums the first n floats of partials buffer `which` of every region in rank order and
+ * writes them to `out` (every rank gets bit-identical values).  Consecutive calls must alternate
+ * `which`; all ranks make the same sequence of calls; each device wait is bounded (JX_ERR_TIMEOUT in
+ * *status). */
+int jx_comm_alloc(long long bytes, void** ptr_out);
+int jx_comm_free(void* ptr);
+int jx_ipc_get_handle(const void* ptr, unsigned char* handle_out);
+int jx_ipc_open_handle(const unsigned char* handle, void** ptr_out);
+int jx_ipc_close_handle(void* ptr);
+int jx_allreduce_layout(long long max_floats, long long* region_bytes_out, long long* data_offset0_out,
+                        long long* data_offset1_out);
+int jx_allreduce_f32(void* const* bases, int rank, int world, long long max_floats, int which, long long n,
+                     float* out, int* status, int pdl, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

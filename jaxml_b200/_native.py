@@ -99,6 +99,13 @@ _PROTOS = {
     "jx_prefill_attention": (I, [ctypes.POINTER(JxPAttnArgs), I, P]),
     "jx_sample": (I, [ctypes.POINTER(JxSampleArgs), I, P]),
     "jx_sample_finalize": (I, [ctypes.POINTER(JxSampleArgs), P, I, P]),
+    "jx_comm_alloc": (I, [LL, ctypes.POINTER(P)]),
+    "jx_comm_free": (I, [P]),
+    "jx_ipc_get_handle": (I, [P, ctypes.c_char_p]),
+    "jx_ipc_open_handle": (I, [ctypes.c_char_p, ctypes.POINTER(P)]),
+    "jx_ipc_close_handle": (I, [P]),
+    "jx_allreduce_layout": (I, [LL, ctypes.POINTER(LL), ctypes.POINTER(LL), ctypes.POINTER(LL)]),
+    "jx_allreduce_f32": (I, [ctypes.POINTER(P), I, I, LL, I, LL, P, P, I, P]),
 }
 
 _lib = None

@@ -262,3 +262,79 @@ int jx_sample_finalize(const jx_sample_args* args, const unsigned long long* gat
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------------------------------------
+// tensor-parallel peer memory and all-reduce
+// ------------------------------------------------------------------------------------------------
+namespace jxb {
+long long ar_region_bytes(long long max_floats);
+long long ar_data_offset(long long max_floats, int which);
+int run_allreduce_f32(void* const* bases, int rank, int world, long long max_floats, int which, long long n,
+                      float* out, int* status, bool pdl, cudaStream_t s);
+}  // namespace jxb
+
+extern "C" {
+
+int jx_comm_alloc(long long bytes, void** ptr_out) {
+  if (!ptr_out || bytes <= 0) return fail(JX_ERR_ARG, "jx_comm_alloc: null output or non-positive size");
+  void* p = nullptr;
+  if (cudaMalloc(&p, (size_t)bytes) != cudaSuccess) return note_cuda("jx_comm_alloc");
+  if (cudaMemset(p, 0, (size_t)bytes) != cudaSuccess) {
+    cudaFree(p);
+    return note_cuda("jx_comm_alloc");
+  }
+  *ptr_out = p;
+  return JX_OK;
+}
+
+int jx_comm_free(void* ptr) {
+  if (!ptr) return JX_OK;
+  return cudaFree(ptr) == cudaSuccess ? JX_OK : note_cuda("jx_comm_free");
+}
+
+int jx_ipc_get_handle(const void* ptr, unsigned char* handle_out) {
+  if (!ptr || !handle_out) return fail(JX_ERR_ARG, "jx_ipc_get_handle: null pointer");
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, const_cast<void*>(ptr)) != cudaSuccess) return note_cuda("jx_ipc_get_handle");
+  memcpy(handle_out, &h, sizeof(h));
+  return JX_OK;
+}
+
+int jx_ipc_open_handle(const unsigned char* handle, void** ptr_out) {
+  if (!handle || !ptr_out) return fail(JX_ERR_ARG, "jx_ipc_open_handle: null pointer");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* p = nullptr;
+  if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return note_cuda("jx_ipc_open_handle");
+  *ptr_out = p;
+  return JX_OK;
+}
+
+int jx_ipc_close_handle(void* ptr) {
+  if (!ptr) return JX_OK;
+  return cudaIpcCloseMemHandle(ptr) == cudaSuccess ? JX_OK : note_cuda("jx_ipc_close_handle");
+}
+
+int jx_allreduce_layout(long long max_floats, long long* region_bytes_out, long long* data_offset0_out,
+                        long long* data_offset1_out) {
+  if (max_floats <= 0 || !region_bytes_out || !data_offset0_out || !data_offset1_out)
+    return fail(JX_ERR_ARG, "jx_allreduce_layout: non-positive size or null output");
+  *region_bytes_out = jxb::ar_region_bytes(max_floats);
+  *data_offset0_out = jxb::ar_data_offset(max_floats, 0);
+  *data_offset1_out = jxb::ar_data_offset(max_floats, 1);
+  return JX_OK;
+}
+
+int jx_allreduce_f32(void* const* bases, int rank, int world, long long max_floats, int which, long long n,
+                     float* out, int* status, int pdl, void* stream) {
+  if (!bases) return fail(JX_ERR_ARG, "jx_allreduce_f32: null region table");
+  const int rc =
+      jxb::run_allreduce_f32(bases, rank, world, max_floats, which, n, out, status, pdl != 0, (cudaStream_t)stream);
+  if (rc == JX_ERR_CUDA) return note_cuda("jx_allreduce_f32");
+  if (rc != JX_OK)
+    return fail(rc, "jx_allreduce_f32: 1 <= world <= 8, 0 <= rank < world, which 0 or 1, n a positive multiple "
+                    "of 4 and at most max_floats, every region 256-byte aligned, out 16-byte aligned");
+  return JX_OK;
+}
+
+}  // extern "C"

@@ -42,8 +42,74 @@ class InferenceConfig:
             raise ValueError(f"dp_size must be positive, got {dp}.")
 
 
+class _RawF32:
+    """Zero-copy float32 view of device memory the library allocated (CUDA array interface)."""
+
+    def __init__(self, ptr: int, n: int):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (ptr, False), "version": 3}
+
+
+class PeerRegion:
+    """This rank's peer-mapped region for the NVLink all-reduce (include/jxb200.h, jx_allreduce_f32): a
+    library-allocated device buffer shared with the other ranks through CUDA IPC handles exchanged over
+    torch.distributed, and the other ranks' buffers mapped here.  `data[0]` and `data[1]` are the two
+    float32 partials buffers the row-parallel projections write into (consecutive all-reduces alternate)."""
+
+    def __init__(self, comm: "TPComm", max_floats: int, device: torch.device):
+        import ctypes
+
+        from . import _native as N
+
+        lib = N.load()
+        rb, off0, off1 = N.LL(), N.LL(), N.LL()
+        N.check(lib.jx_allreduce_layout(max_floats, rb, off0, off1), "jx_allreduce_layout")
+        self.max_floats = max_floats
+        self._lib, self._N = lib, N
+        with torch.cuda.device(device):
+            p = N.P()
+            N.check(lib.jx_comm_alloc(rb.value, ctypes.byref(p)), "jx_comm_alloc")
+            self.local = p.value
+            h = ctypes.create_string_buffer(64)
+            N.check(lib.jx_ipc_get_handle(self.local, h), "jx_ipc_get_handle")
+            handles = [None] * comm.size
+            comm.dist.all_gather_object(handles, h.raw, group=comm.group)
+            bases, self._opened = [], []
+            for r, hr in enumerate(handles):
+                if r == comm.rank:
+                    bases.append(self.local)
+                    continue
+                q = N.P()
+                N.check(lib.jx_ipc_open_handle(hr, ctypes.byref(q)), "jx_ipc_open_handle")
+                bases.append(q.value)
+                self._opened.append(q.value)
+        self.bases = (N.P * comm.size)(*bases)
+        self._raw = [_RawF32(self.local + o, max_floats) for o in (off0.value, off1.value)]
+        self.data = [torch.as_tensor(r, device=device) for r in self._raw]
+        self.rank, self.world = comm.rank, comm.size
+
+    def all_reduce(self, which: int, n: int, out: torch.Tensor, status: Optional[torch.Tensor] = None):
+        st = None if status is None else status.data_ptr()
+        stream = torch.cuda.current_stream(out.device).cuda_stream
+        rc = self._lib.jx_allreduce_f32(self.bases, self.rank, self.world, self.max_floats, which, n,
+                                        out.data_ptr(), st, 1, stream)
+        self._N.check(rc, "jx_allreduce_f32")
+
+    def close(self):
+        for q in self._opened:
+            self._lib.jx_ipc_close_handle(q)
+        self._opened = []
+        self.data = None
+        if self.local:
+            self._lib.jx_comm_free(self.local)
+            self.local = 0
+
+
 class TPComm:
-    """Collectives of one tensor-parallel group over NCCL (torch.distributed)."""
+    """Collectives of one tensor-parallel group: decode-sized all-reduces of the row-parallel partial sums
+    through the library's NVLink peer kernel (PeerRegion), everything else over NCCL (torch.distributed)."""
+
+    # peer all-reduce capacity in float32 elements: 64 token rows x 8192 hidden
+    PEER_MAX_FLOATS = 64 * 8192
 
     def __init__(self, group=None):
         import torch.distributed as dist
@@ -53,9 +119,56 @@ class TPComm:
         self.size = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self._gather = None
+        self.peer: Optional[PeerRegion] = None
+        self._peer_tried = False
+        self._which = 0
+
+    def prepare_peer(self, device: torch.device) -> Optional[PeerRegion]:
+        """Creates the peer region on first call (a collective: every rank makes it, outside any CUDA
+        graph capture); None when the peer path does not apply (CPU or non-NCCL group, one rank or more
+        than 8)."""
+        if not self._peer_tried:
+            self._peer_tried = True
+            if (device.type == "cuda" and 2 <= self.size <= 8 and self.dist.get_backend(self.group) == "nccl"):
+                self.peer = PeerRegion(self, self.PEER_MAX_FLOATS, device)
+        return self.peer
+
+    def partial_buffer(self, n_floats: int) -> Optional[torch.Tensor]:
+        """The float32 buffer the next peer all-reduce reads (the two buffers alternate call by call), or
+        None when the peer path is off or n_floats exceeds PEER_MAX_FLOATS."""
+        if self.peer is None or n_floats > self.PEER_MAX_FLOATS:
+            return None
+        return self.peer.data[self._which][:n_floats]
+
+    def all_reduce_partial(self, src: torch.Tensor, out: torch.Tensor, status: Optional[torch.Tensor] = None):
+        """Sum of every rank's `src` (a prefix of partial_buffer()) into this rank's `out`, in rank order."""
+        if src.data_ptr() != self.peer.data[self._which].data_ptr() or src.dtype != torch.float32:
+            raise ValueError("all_reduce_partial: src must be the buffer partial_buffer() returned")
+        if out.dtype != torch.float32 or not out.is_contiguous() or out.numel() < src.numel():
+            raise ValueError("all_reduce_partial: out must be a contiguous float32 tensor of src's size")
+        self.peer.all_reduce(self._which, src.numel(), out, status)
+        self._which ^= 1
 
     def all_reduce(self, t: torch.Tensor):
         self.dist.all_reduce(t, group=self.group)
+
+    def align(self, status: Optional[torch.Tensor] = None):
+        """Ends a pass (one decode step, one prefill) on partials buffer 0 by adding a 4-float all-reduce
+        when the pass made an odd number of peer all-reduces.  A captured pass then always starts on
+        buffer 0, so back-to-back replays keep alternating and no rank rewrites a buffer a peer may still
+        be reading.  Every rank makes the same calls."""
+        if self.peer is not None and self._which == 1:
+            if getattr(self, "_align_out", None) is None:
+                self._align_out = torch.empty(4, dtype=torch.float32, device=self.peer.data[0].device)
+            self.all_reduce_partial(self.partial_buffer(4), self._align_out, status)
+
+    def close(self):
+        """Releases the peer region (every rank, no kernels in flight)."""
+        if self.peer is not None:
+            torch.cuda.synchronize()
+            self.dist.barrier(group=self.group)
+            self.peer.close()
+            self.peer = None
 
     def all_gather_keys(self, keys: torch.Tensor) -> torch.Tensor:
         """[n] per rank -> [size, n] (rank-major), gathered into one flat buffer."""
@@ -222,6 +335,8 @@ class Engine:
         if torch.cuda.is_available():
             torch.cuda.synchronize()
             torch.cuda.empty_cache()
+        if self._comm is not None:
+            self._comm.close()
 
     # -- generation ------------------------------------------------------------------------------------
     def generate(self, prompt_tokens, attention_mask=None, seed: int = 0, max_new_tokens: int = 10, top_k: int = 0,

@@ -272,6 +272,8 @@ class DecoderRuntime:
         self.w = weights
         self.B, self.T = B, T
         self.comm = comm
+        if comm is not None:
+            comm.prepare_peer(weights.device)   # collective: outside any graph capture
         w = weights
         dev, dt = w.device, w.dtype
         cfg = w.cfg
@@ -420,9 +422,20 @@ class DecoderRuntime:
                                        self.stream_ptr())
             N.check(rc, "jx_linear_prefill")
 
-    def _allreduce(self, t: torch.Tensor, rows: int):
-        if self.comm is not None:
-            self.comm.all_reduce(t[:rows])
+    def _tp_dst(self, acts) -> torch.Tensor:
+        """Where a row-parallel projection writes its float32 partial sum: the peer partials buffer of the
+        next all-reduce for decode-sized activations, else acts["tmp"] (all-reduced in place by NCCL)."""
+        buf = self.comm.partial_buffer(acts["Mp"] * self.w.d) if acts["Mp"] <= 128 else None
+        return acts["tmp"] if buf is None else buf.view(acts["Mp"], self.w.d)
+
+    def _allreduce(self, src: torch.Tensor, rows: int, acts):
+        """All-reduce of the partial sums in `src` (from _tp_dst) into acts["tmp"]."""
+        if self.comm is None:
+            return
+        if src.data_ptr() == acts["tmp"].data_ptr():
+            self.comm.all_reduce(src[:rows])
+        else:
+            self.comm.all_reduce_partial(src[:rows].reshape(-1), acts["tmp"][:rows].reshape(-1), self.status)
 
     # -- one pass over the stack -----------------------------------------------------------------------
     def _layers(self, acts, S: int, decode: bool):
@@ -441,6 +454,8 @@ class DecoderRuntime:
             else:
                 self._generic_attention(acts, li, lw, S, decode)
             self._o_and_mlp(acts, lw, nx)
+        if self.comm is not None:
+            self.comm.align(self.status)
 
     def _qkv_rope_append(self, acts, li, lw, S, decode):
         W, cfg = self.w, self.w.cfg
@@ -517,10 +532,11 @@ class DecoderRuntime:
         if fam == "gemma3" or parallel or tp:
             # o_proj result kept apart: Gemma normalises it, NeoX's parallel residual adds it with the
             # MLP output, and under tensor parallelism it is a partial sum to all-reduce first.
+            dst = self._tp_dst(acts) if tp else acts["tmp"]
             self._linear(acts, lw.wo, W.Np_d, W.Kp_o, "attn", store, N_valid=d, bias=lw.bo,
-                         out=acts["tmp"], ldo=d, K_logical=W.Hq * hd, N_cols=d, pf=pf_gu)
+                         out=dst, ldo=d, K_logical=W.Hq * hd, N_cols=d, pf=pf_gu)
             if not parallel:
-                self._allreduce(acts["tmp"], M)
+                self._allreduce(dst, M, acts)
         else:
             self._linear(acts, lw.wo, W.Np_d, W.Kp_o, "attn", N.JX_EPI_RESID, N_valid=d, bias=lw.bo,
                          out=acts["h"], ldo=d, res=acts["h"], ldr=d, K_logical=W.Hq * hd, N_cols=d, pf=pf_gu)
@@ -551,12 +567,13 @@ class DecoderRuntime:
         Fk = W.F32 if (W.glu and not W.bf16) else W.F
         down_kw = dict(N_valid=d, bias=lw.bd, K_logical=Fk, N_cols=d, pf=pf_next)
         if parallel and tp:
-            # tmp = attn_partial + mlp_partial, all-reduced once; h += tmp in the next norm.
-            self._linear(acts, lw.wd, W.Np_d, W.Kp_f, "act", N.JX_EPI_ACC_F32, out=acts["tmp"], ldo=d, **down_kw)
-            self._allreduce(acts["tmp"], M)
+            # attn_partial + mlp_partial accumulate in dst, all-reduced once into tmp; h += tmp in the next norm.
+            self._linear(acts, lw.wd, W.Np_d, W.Kp_f, "act", N.JX_EPI_ACC_F32, out=dst, ldo=d, **down_kw)
+            self._allreduce(dst, M, acts)
         elif fam == "gemma3" or tp:
-            self._linear(acts, lw.wd, W.Np_d, W.Kp_f, "act", store, out=acts["tmp"], ldo=d, **down_kw)
-            self._allreduce(acts["tmp"], M)
+            dst = self._tp_dst(acts) if tp else acts["tmp"]
+            self._linear(acts, lw.wd, W.Np_d, W.Kp_f, "act", store, out=dst, ldo=d, **down_kw)
+            self._allreduce(dst, M, acts)
         elif parallel:
             self._linear(acts, lw.wd, W.Np_d, W.Kp_f, "act", N.JX_EPI_RESID2, out=acts["h"], ldo=d,
                          res=acts["h"], ldr=d, res2=acts["tmp"], ldr2=d, **down_kw)

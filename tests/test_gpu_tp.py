@@ -103,3 +103,93 @@ def test_tp2_logit_shards_and_tokens_match_oracle():
             out = O.forward("llama", cfg, params, tok[:, None], torch.bfloat16, kv_caches=out.kv_caches,
                             keep_last_n_logits=1)
     assert half == res[0][0][0].shape[1]
+
+
+def _allreduce_worker(rank, world, port, q):
+    import datetime
+
+    import torch.distributed as dist
+
+    from jaxml_b200.engine import TPComm
+
+    try:
+        torch.cuda.set_device(rank)
+        dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
+        comm = TPComm()
+        dev = torch.device("cuda", rank)
+        status = torch.zeros(1, dtype=torch.int32, device=dev)
+        assert comm.prepare_peer(dev) is not None
+        g = torch.Generator(device=dev).manual_seed(100 + rank)
+        out = torch.empty(TPComm.PEER_MAX_FLOATS, device=dev)
+
+        def reference(x):   # the rank-order sum of every rank's input
+            parts = [torch.empty_like(x) for _ in range(world)]
+            dist.all_gather(parts, x)
+            want = parts[0].clone()
+            for r in range(1, world):
+                want += parts[r]
+            return want
+
+        results = []
+        for n in (4, 16 * 4096, 1 * 4096, TPComm.PEER_MAX_FLOATS, 64 * 128, 8):
+            x = torch.randn(n, device=dev, generator=g)
+            src = comm.partial_buffer(n)
+            src.copy_(x)
+            want = reference(x)
+            comm.all_reduce_partial(src, out[:n], status)
+            torch.cuda.synchronize()
+            results.append((n, bool(torch.equal(out[:n], want)), out[:n].sum().item()))
+        # two calls (both buffers) captured in one CUDA graph and replayed: the call counter lives on
+        # the device and the buffers alternate
+        n = 16 * 4096
+        x = torch.randn(n, device=dev, generator=g)
+        srcs = [comm.partial_buffer(n)]
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        graph = torch.cuda.CUDAGraph()
+        out2 = torch.empty(n, device=dev)
+        with torch.cuda.graph(graph, stream=s):
+            comm.all_reduce_partial(srcs[0], out[:n], status)
+            srcs.append(comm.partial_buffer(n))
+            comm.all_reduce_partial(srcs[1], out2, status)
+        for rep in range(5):
+            srcs[0].copy_(x * (rep + 1))
+            srcs[1].copy_(x * (rep + 2))
+            torch.cuda.synchronize()
+            dist.barrier()
+            graph.replay()
+            torch.cuda.synchronize()
+            ok = torch.equal(out[:n], reference(x * (rep + 1))) and torch.equal(out2, reference(x * (rep + 2)))
+            results.append((f"graph{rep}", bool(ok), out2.sum().item()))
+        del graph
+        st = int(status.item())
+        comm.close()
+        q.put((rank, results, st, None))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:  # report to the parent instead of hanging it
+        q.put((rank, None, None, repr(e)))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_tp2_peer_allreduce_matches_rank_order_sum():
+    """NVLink peer all-reduce (jx_allreduce_f32): bit-identical to the rank-order sum on every rank, for
+    several sizes and across CUDA-graph replays."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_allreduce_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(2):
+        rank, results, st, err = q.get(timeout=240)
+        assert err is None, f"rank {rank}: {err}"
+        assert st == 0, f"rank {rank}: status {st}"
+        res[rank] = results
+    for p in procs:
+        p.join(timeout=60)
+    for (n0, ok0, s0), (n1, ok1, s1) in zip(res[0], res[1]):
+        assert ok0 and ok1, n0
+        assert s0 == s1, n0            # every rank holds the same values
