@@ -31,6 +31,11 @@ sys.path.insert(0, ROOT)
 
 METRIC = "decode tok/s (box) & p50 step latency, Llama-3-8B-shape bf16, TP=1/2/4/8"
 
+# DRAM bytes (read 235073024 + write 4625152) of one launch of the tcgen05 decode projection on the
+# gate/up shape (M=16, N=28672, K=4096), from an ncu --set full capture of
+# `python bench.py --micro gemv --shape 28672,4096`.
+GEMV_TC_GATEUP_TRAFFIC = 239698176
+
 
 def l8_config(num_layers=32):
     from jaxml_b200.config import ModelConfig
@@ -51,12 +56,14 @@ def parse():
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--micro", choices=["gemv", "attn", "allreduce"], default=None,
+    ap.add_argument("--micro", choices=["gemv", "attn", "gemm", "allreduce"], default=None,
                     help="single-kernel microbenchmark on Llama-3-8B layer shapes instead of the decode step")
     ap.add_argument("--ctx", type=int, default=4096, help="context length of --micro attn")
     ap.add_argument("--shape", default="28672,4096", help="N,K of --micro gemv (default: fused gate/up)")
     ap.add_argument("--gemv-impl", type=int, default=0, help="--micro gemv kernel: 0 by shape, 1 mma.sync, 2 tcgen05")
     ap.add_argument("--attn-impl", type=int, default=0, help="--micro attn form: 0 by shape, 1 split, 2 cluster")
+    ap.add_argument("--tokens", type=int, default=8192, help="token rows of --micro gemm (prefill B x P)")
+    ap.add_argument("--gemm-impl", type=int, default=0, help="--micro gemm kernel: 0 by shape, 1 mma.sync, 2 tcgen05")
     return ap.parse_args()
 
 
@@ -341,7 +348,10 @@ def gpu_arm(args):
                        "global_batch": B, "seq_len": P, "parallelism": f"tp{tp}",
                        "l2": "inputs larger than L2 (15 GB of weights per step)"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-                         "frac": achieved / hbm_peak, "traffic": None,
+                         "frac": achieved / hbm_peak, "traffic": GEMV_TC_GATEUP_TRAFFIC,
+                         "traffic_note": "dram__bytes_read.sum + dram__bytes_write.sum of one launch of this "
+                                         "kernel on the gate/up shape (ncu --set full, cold cache); "
+                                         "algorithmic bytes per launch: %d" % gemv_bytes,
                          "kernel": "gemv_tc_kernel (tcgen05 decode projection, gate/up: 235 MB weights per launch)",
                          "peak_source": "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in peaks else "fallback"},
             "step_roofline": {"bytes_per_step": sbytes, "weight_bytes": wbytes, "kv_bytes": kvbytes,
@@ -468,7 +478,34 @@ def micro(args):
     torch.cuda.set_device(dev)
     B = args.batch
     rup = lambda x, m: (x + m - 1) // m * m
-    if args.micro == "gemv":
+    if args.micro == "gemm":
+        # prefill projection: [tokens, K] x [N, K]^T, bf16 K128 operands, plain store epilogue
+        Nn, K = (int(v) for v in args.shape.split(","))
+        M = args.tokens
+        N.call("jx_set_prefill_linear_impl", args.gemm_impl)
+        Mp, Np, Kp = rup(M, 128), rup(Nn, 128), rup(K, 128)
+        copies = max(2, min(8, int(1.2e9 // (Nn * K * 2))))       # distinct weight copies
+        ws = [torch.empty(Np * Kp, dtype=torch.bfloat16, device=dev).normal_(0, 0.02) for _ in range(copies)]
+        x = torch.randn(Mp * Kp, device=dev).to(torch.bfloat16)
+        out = torch.empty(M, Nn, dtype=torch.bfloat16, device=dev)
+        st = torch.zeros(1, dtype=torch.int32, device=dev)
+        e = N.JxEpilogue()
+        e.kind, e.M, e.N, e.out, e.ldo = N.JX_EPI_STORE, M, Nn, out.data_ptr(), Nn
+
+        def run(w, stream):
+            N.call("jx_linear_prefill", x.data_ptr(), w.data_ptr(), Mp, Np, Kp, e, st.data_ptr(), 1, stream)
+        ms = _graph_ms(lambda stream: [run(w, stream) for w in ws], copies)
+        flops = 2.0 * M * Nn * K
+        peaks = {}
+        try:
+            peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+        except OSError:
+            pass
+        peak = peaks.get("bf16_tflops", 1590.0)
+        line = {"micro": "gemm", "impl": ["by-shape", "mma.sync", "tcgen05"][args.gemm_impl],
+                "shape": f"M={M} N={Nn} K={K}", "us": ms * 1e3, "tflops": flops / ms / 1e9,
+                "frac_of_measured_bf16": flops / ms / 1e9 / peak, "status": int(st.item())}
+    elif args.micro == "gemv":
         Nn, K = (int(v) for v in args.shape.split(","))
         glu = Nn == 2 * 14336 and K == 4096
         copies = max(2, min(64, int(2e9 // (Nn * K * 2))))       # distinct weight copies: > L2 in total
