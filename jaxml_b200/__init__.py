@@ -1,19 +1,23 @@
 """B200-native (sm_100a) implementation of jaxml's decode/prefill path.
 
 Public names mirror ``jaxml/__init__.py`` of the reference: ``Engine``, ``InferenceConfig``,
-``ModelConfig``, ``SamplingMethod`` (plus the model classes).  The kernels live in ``libjxb200.so``
+``ModelConfig``, ``SamplingMethod``, ``GenerationConfig``, ``TextGenerationPipeline`` (plus the model
+classes).  The kernels live in ``libjxb200.so``
 (``jaxml_b200/csrc``, C ABI in ``include/jxb200.h``).
 """
 from .config import ModelConfig
 from .engine import Engine, InferenceConfig
 from .models import GemmaModelWithHead, GPTNeoXModelWithHead, LlamaModelWithHead
 from .sampling import SamplingMethod
+from .text_generation import GenerationConfig, TextGenerationPipeline
 
 __all__ = [
     "Engine",
     "InferenceConfig",
     "ModelConfig",
     "SamplingMethod",
+    "GenerationConfig",
+    "TextGenerationPipeline",
     "LlamaModelWithHead",
     "GPTNeoXModelWithHead",
     "GemmaModelWithHead",

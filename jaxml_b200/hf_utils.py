@@ -105,3 +105,79 @@ def to_neox_jax_params(model, dtype=torch.float32) -> dict:
             name = re.sub(pat, rep, name)
         renamed[name] = value
     return torch_to_jax_states(renamed, dtype=dtype, head_dim=_head_dim(model.config))
+
+
+# ------------------------------------------------------------------------------------------------
+# Loading a Hugging Face causal LM (local path or hub id) into a model class + parameter tree
+# (hf_utils.py:96-250 of the reference: architecture names, dtype strings, model_type checks).
+# ------------------------------------------------------------------------------------------------
+_HF_DTYPES = {"float32": torch.float32, "fp32": torch.float32, "float16": torch.float16, "fp16": torch.float16,
+              "bfloat16": torch.bfloat16, "bf16": torch.bfloat16}
+
+
+def _normalize_hf_architecture(architecture) -> str:
+    if not isinstance(architecture, str):
+        raise TypeError(f"architecture must be a string, got {type(architecture)}.")
+    a = architecture.lower().replace("-", "_")
+    aliases = {"auto": "auto", "llama": "llama", "neox": "neox", "gpt_neox": "neox", "gemma": "gemma",
+               "gemma3": "gemma", "gemma_3": "gemma"}
+    if a not in aliases:
+        raise ValueError(f"Unsupported Hugging Face architecture {architecture!r}.")
+    return aliases[a]
+
+
+def _normalize_hf_model_name(name) -> str:
+    import os
+
+    try:
+        path = os.fspath(name)
+    except TypeError as e:
+        raise TypeError(f"name must be a string or path-like object, got {type(name)}.") from e
+    if not isinstance(path, str):
+        raise TypeError(f"name must resolve to a string path, got {type(path)}.")
+    if not path.strip():
+        raise ValueError("name must be non-empty.")
+    return path
+
+
+def _validate_hf_dtype(dtype):
+    if not isinstance(dtype, str) or dtype.lower() not in _HF_DTYPES:
+        raise ValueError(f"Unsupported dtype {dtype!r}; expected one of {sorted(_HF_DTYPES)}.")
+    return dtype
+
+
+def _check_model_type(config, expected: tuple, what: str):
+    mt = getattr(config, "model_type", None)
+    if mt not in expected:
+        raise ValueError(f"Expected Hugging Face {what} model_type to be one of {expected}, got {mt!r}.")
+
+
+def load_model_from_hf(name, architecture: str = "auto", dtype: str = "float32", **from_pretrained_kwargs):
+    """(model class instance, reference parameter tree) from a supported HF causal LM.  The model class
+    computes in `dtype`; leaves are CPU torch tensors in that dtype."""
+    from .config import ModelConfig
+    from .models import GemmaModelWithHead, GPTNeoXModelWithHead, LlamaModelWithHead
+
+    name = _normalize_hf_model_name(name)
+    dtype = _validate_hf_dtype(dtype)
+    arch = _normalize_hf_architecture(architecture)
+    try:
+        from transformers import AutoConfig, AutoModelForCausalLM
+    except ImportError as e:
+        raise ImportError("Please install transformers library.") from e
+    if arch == "auto":
+        mt = getattr(AutoConfig.from_pretrained(name, **from_pretrained_kwargs), "model_type", None)
+        arch = {"llama": "llama", "gpt_neox": "neox", "gemma3": "gemma", "gemma3_text": "gemma"}.get(mt)
+        if arch is None:
+            raise ValueError(f"Unsupported Hugging Face model type {mt!r}.")
+    tdt = _HF_DTYPES[dtype.lower()]
+    hf = AutoModelForCausalLM.from_pretrained(name, **from_pretrained_kwargs)
+    if arch == "llama":
+        _check_model_type(hf.config, ("llama",), "Llama")
+        return LlamaModelWithHead(ModelConfig.from_hf(hf.config), dtype=tdt), to_llama_jax_params(hf, dtype=tdt)
+    if arch == "neox":
+        _check_model_type(hf.config, ("gpt_neox",), "GPT-NeoX")
+        return GPTNeoXModelWithHead(ModelConfig.from_hf(hf.config), dtype=tdt), to_neox_jax_params(hf, dtype=tdt)
+    lm = getattr(hf, "language_model", hf)
+    _check_model_type(lm.config, ("gemma3_text", "gemma3"), "Gemma")
+    return GemmaModelWithHead(ModelConfig.from_hf(lm.config), dtype=tdt), to_gemma_jax_params(lm, dtype=tdt)

@@ -1,0 +1,85 @@
+"""GenerationConfig / TextGenerationPipeline (text_generation.py of the reference): validation and the
+tokenize -> generate -> decode plumbing, with a fake engine and tokenizer (no GPU)."""
+import numpy as np
+import pytest
+
+from jaxml_b200 import GenerationConfig, TextGenerationPipeline
+
+
+class _Tok:
+    """Character-level tokenizer: ids = ord(c) % 97 + 3, right padding with 0."""
+
+    def __call__(self, texts, return_tensors="np", padding=True, **kw):
+        ids = [[ord(c) % 97 + 3 for c in t] for t in texts]
+        n = max(len(x) for x in ids)
+        arr = np.zeros((len(ids), n), dtype=np.int64)
+        mask = np.zeros((len(ids), n), dtype=np.int64)
+        for i, x in enumerate(ids):
+            arr[i, :len(x)] = x
+            mask[i, :len(x)] = 1
+        return {"input_ids": arr, "attention_mask": mask}
+
+    def batch_decode(self, tokens, skip_special_tokens=True):
+        return ["".join(chr(int(t) + 60) for t in row) for row in tokens]
+
+
+class _Engine:
+    def __init__(self):
+        self.calls = []
+
+    def generate(self, prompt_tokens, attention_mask=None, **kw):
+        self.calls.append((np.asarray(prompt_tokens), attention_mask, kw))
+        B, P = np.asarray(prompt_tokens).shape
+        new = np.full((B, kw["max_new_tokens"]), 7, dtype=np.int32)
+        return np.concatenate([prompt_tokens, new], 1) if kw["include_prompt"] else new
+
+
+def test_generation_config_validates_like_the_reference():
+    c = GenerationConfig(seed=np.int64(3), max_new_tokens=5, top_p=1)
+    assert c.seed == 3 and isinstance(c.seed, int) and c.top_p == 1.0
+    with pytest.raises(TypeError, match="seed must be an integer"):
+        GenerationConfig(seed=True)
+    with pytest.raises(ValueError, match="max_new_tokens must be non-negative"):
+        GenerationConfig(max_new_tokens=-1)
+    with pytest.raises(ValueError, match="top_k must be non-negative"):
+        GenerationConfig(top_k=-2)
+    with pytest.raises(ValueError, match="temperature must be finite"):
+        GenerationConfig(temperature=float("inf"))
+    with pytest.raises(TypeError, match="top_p must be a real number"):
+        GenerationConfig(top_p="0.5")
+    with pytest.raises(TypeError, match="include_prompt must be a boolean"):
+        GenerationConfig(include_prompt=1)
+
+
+def test_pipeline_tokenize_generate_decode():
+    eng = _Engine()
+    pipe = TextGenerationPipeline(eng, _Tok())
+    out = pipe.generate_text(["ab", "xyz"], max_new_tokens=2, temperature=0.0)
+    assert isinstance(out, list) and len(out) == 2
+    ids, mask, kw = eng.calls[-1]
+    assert ids.shape == (2, 3) and mask.dtype == bool and not mask[0, 2]
+    assert kw["max_new_tokens"] == 2 and kw["temperature"] == 0.0 and kw["include_prompt"] is True
+    single = pipe.generate_text("hi", GenerationConfig(max_new_tokens=1), include_prompt=False)
+    assert isinstance(single, str) and len(single) == 1
+    toks = pipe.generate_tokens("hi", max_new_tokens=3)
+    assert toks.shape == (1, 5)
+
+
+def test_pipeline_rejects_bad_inputs():
+    with pytest.raises(TypeError, match="engine must provide a callable generate"):
+        TextGenerationPipeline(object(), _Tok())
+    with pytest.raises(TypeError, match="batch_decode"):
+        TextGenerationPipeline(_Engine(), lambda x: x)
+    pipe = TextGenerationPipeline(_Engine(), _Tok())
+    with pytest.raises(ValueError, match="at least one prompt"):
+        pipe.generate_text([])
+    with pytest.raises(TypeError, match="prompts must be a string"):
+        pipe.generate_text([1, 2])
+    with pytest.raises(TypeError, match="generation_config must be a GenerationConfig"):
+        pipe.generate_tokens("a", generation_config={"seed": 1})
+
+    class _BadEngine(_Engine):
+        def generate(self, prompt_tokens, attention_mask=None, **kw):
+            return np.zeros((1, 1), dtype=np.int32)
+    with pytest.raises(ValueError, match="token length must match"):
+        TextGenerationPipeline(_BadEngine(), _Tok()).generate_tokens("abc", max_new_tokens=4)
