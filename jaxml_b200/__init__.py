@@ -1,10 +1,11 @@
 """B200-native (sm_100a) implementation of jaxml's decode/prefill path.
 
 Public names mirror ``jaxml/__init__.py`` of the reference: ``Engine``, ``InferenceConfig``,
-``ModelConfig``, ``SamplingMethod``, ``GenerationConfig``, ``TextGenerationPipeline`` (plus the model
-classes).  The kernels live in ``libjxb200.so``
+``ModelConfig``, ``SamplingMethod``, ``GenerationConfig``, ``TextGenerationPipeline``, ``KVCache`` (plus
+the model classes).  The kernels live in ``libjxb200.so``
 (``jaxml_b200/csrc``, C ABI in ``include/jxb200.h``).
 """
+from .cache import KVCache
 from .config import ModelConfig
 from .engine import Engine, InferenceConfig
 from .models import GemmaModelWithHead, GPTNeoXModelWithHead, LlamaModelWithHead
@@ -18,6 +19,7 @@ __all__ = [
     "SamplingMethod",
     "GenerationConfig",
     "TextGenerationPipeline",
+    "KVCache",
     "LlamaModelWithHead",
     "GPTNeoXModelWithHead",
     "GemmaModelWithHead",
