@@ -170,6 +170,14 @@ class TPComm:
             self.peer.close()
             self.peer = None
 
+    def all_gather_vocab(self, logits: torch.Tensor) -> torch.Tensor:
+        """[B, V/size] vocabulary shard per rank -> [B, V] (rank r's shard at columns r*V/size ...)."""
+        B, n = logits.shape
+        if getattr(self, "_vgather", None) is None or self._vgather.numel() != self.size * B * n:
+            self._vgather = torch.empty(self.size * B * n, dtype=logits.dtype, device=logits.device)
+        self.dist.all_gather_into_tensor(self._vgather, logits.contiguous().reshape(-1), group=self.group)
+        return self._vgather.view(self.size, B, n).permute(1, 0, 2).reshape(B, self.size * n)
+
     def all_gather_keys(self, keys: torch.Tensor) -> torch.Tensor:
         """[n] per rank -> [size, n] (rank-major), gathered into one flat buffer."""
         n = keys.numel()
@@ -362,8 +370,9 @@ class Engine:
         B, P = prompt.shape
         if max_new_tokens == 0:
             return prompt.clone() if include_prompt else prompt[:, :0].clone()
-        method.require_device_support()
         rt = self._runtime_for(B, self.buffer_length(P, max_new_tokens))
+        rt.filters = ((sp.top_k if method.use_top_k else 0, sp.top_p if method.use_top_p else 1.0,
+                       sp.min_p if method.use_min_p else 0.0) if method.uses_filters else None)
         dev = self._weights.device
         pin = prompt.pin_memory() if not prompt.is_cuda else prompt
         ids_d = pin.to(dev, non_blocking=True)

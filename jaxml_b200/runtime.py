@@ -304,6 +304,9 @@ class DecoderRuntime:
         self.sample_chunk = 4096
         nchunks = (w.V + self.sample_chunk - 1) // self.sample_chunk
         self.sample_ws = torch.zeros(B * nchunks, dtype=torch.int64, device=dev)
+        # min-p / top-k / top-p: (top_k, top_p, min_p) of the current generation, or None
+        self.filters = None
+        self._flog = None
         self.sample_counters = torch.zeros(B + 1, dtype=torch.int32, device=dev)
         self.row_best = torch.zeros(B, dtype=torch.int64, device=dev)
         self.row_map = (torch.arange(B, dtype=torch.int32, device=dev))
@@ -622,6 +625,22 @@ class DecoderRuntime:
             self._logits = torch.zeros(self.dec["Mp"], self.w.V, dtype=self.w.dtype, device=self.w.device)
         return self._logits
 
+    def _filtered_logits(self):
+        """Full-vocabulary logits [B, V] after the min-p / top-k / top-p filters (tensor parallelism: the
+        vocabulary shards are all-gathered first, so every rank filters and samples the same values)."""
+        W = self.w
+        lg = self.logits_buf()[:self.B]
+        if self.comm is not None:
+            lg = self.comm.all_gather_vocab(lg)
+        if self._flog is None or tuple(self._flog.shape) != (self.B, W.V_total):
+            self._flog = torch.empty(self.B, W.V_total, dtype=W.dtype, device=W.device)
+            nchunks = (W.V_total + self.sample_chunk - 1) // self.sample_chunk
+            self._flog_ws = torch.zeros(self.B * nchunks, dtype=torch.int64, device=W.device)
+        from .sampling import filter_logits_
+
+        top_k, top_p, min_p = self.filters
+        return filter_logits_(lg, self._flog, top_k, top_p, min_p)
+
     def _sample(self, greedy: bool, temp: float, update_pos: bool):
         W = self.w
         s = N.JxSampleArgs()
@@ -635,6 +654,13 @@ class DecoderRuntime:
         s.rng, s.gumbel_tab = ptr(self.rng), ptr(W.gumbel)
         s.ws, s.row_best, s.counters = ptr(self.sample_ws), ptr(self.row_best), ptr(self.sample_counters)
         tp = self.comm is not None
+        if self.filters is not None and not greedy:
+            # filtered full-vocabulary logits, sampled as one shard on every rank
+            flog = self._filtered_logits()
+            s.V, s.logits, s.ld = W.V_total, ptr(flog), W.V_total
+            s.vocab_offset, s.vocab_total = 0, W.V_total
+            s.ws = ptr(self._flog_ws)
+            tp = False
         s.finalize = 0 if tp else 1
         s.ld_tok = self.tokens_out.shape[1]
         s.tokens_out, s.step, s.next_ids = ptr(self.tokens_out), ptr(self.step), ptr(self.next_ids)
@@ -695,7 +721,7 @@ class DecoderRuntime:
 
     def capture_decode(self, greedy: bool, temp: float):
         """Captures one decode step in a CUDA graph (run one eager step first to warm up)."""
-        key = (greedy, float(temp))
+        key = (greedy, float(temp), self.filters)
         if self.graph is not None and self.graph[0] == key:
             return self.graph[1]
         g = torch.cuda.CUDAGraph()

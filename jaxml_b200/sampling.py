@@ -1,9 +1,9 @@
 """Sampling-method selection, as ``inference_engine/sampling.py:90-188`` of the reference.
 
 The selection logic (``normalize_sampling_params`` clipping and warnings, ``SamplingMethod.from_values``)
-runs on the host; the selected method runs on the GPU (``csrc/sample.cu``): greedy argmax and plain
-temperature sampling.  The min-p / top-k / top-p filters are not implemented on the device yet and
-raise ``NotImplementedError`` when selected.
+runs on the host; the selected method runs on the GPU: greedy argmax and temperature sampling in
+``csrc/sample.cu``, preceded for min-p / top-k / top-p by ``filter_logits_`` (``sampling.py:34-72``,
+applied in the reference's order min-p, top-k, top-p) on the device logits.
 """
 from __future__ import annotations
 
@@ -14,6 +14,8 @@ import operator
 from dataclasses import dataclass
 
 import numpy as np
+
+import torch
 
 from ._checks import normalize_bool
 
@@ -85,12 +87,39 @@ class SamplingMethod:
                    use_min_p=p.min_p > 0.0 and not greedy, use_greedy=greedy)
 
     @property
-    def device_supported(self) -> bool:
-        return self.use_greedy or not (self.use_top_k or self.use_top_p or self.use_min_p)
+    def uses_filters(self) -> bool:
+        return not self.use_greedy and (self.use_top_k or self.use_top_p or self.use_min_p)
 
-    def require_device_support(self):
-        if not self.device_supported:
-            raise NotImplementedError(
-                "min-p / top-k / top-p filtering is not implemented on the GPU path; use greedy decoding "
-                "(temperature <= 0) or plain temperature sampling."
-            )
+
+def _probs(logits: torch.Tensor) -> torch.Tensor:
+    """Vocabulary softmax in float32, rounded to the logits' dtype (the reference applies jax.nn.softmax
+    to model-dtype logits), returned as float32."""
+    x = logits.float()
+    e = torch.exp(x - x.amax(dim=-1, keepdim=True))
+    return (e / e.sum(dim=-1, keepdim=True)).to(logits.dtype).float()
+
+
+def filter_logits_(logits: torch.Tensor, out: torch.Tensor, top_k: int, top_p: float, min_p: float) -> torch.Tensor:
+    """min-p, then top-k, then top-p filtering of device logits ``[B, V]`` into ``out`` (filtered entries
+    -inf), inference_engine/sampling.py:34-72.  The reference's own comparisons are kept: min-p keeps
+    probabilities >= min_p (unless that keeps nothing in a row), top-k keeps logits >= the k-th largest
+    (ties included), top-p keeps logits >= the sorted logit at the count of cumulative probabilities
+    below top_p.  Where the reference's JAX arithmetic is not visible from its source: probabilities in
+    float32 rounded to the logits' dtype, the cumulative sum in float32, a cutoff index past the end
+    clamped to the last entry.  Device tensor ops only (capturable in a CUDA graph)."""
+    neg = torch.tensor(float("-inf"), dtype=logits.dtype, device=logits.device)
+    x = logits
+    if min_p > 0.0:
+        keep = _probs(x) >= min_p
+        x = torch.where(keep.any(dim=-1, keepdim=True), torch.where(keep, x, neg), x)
+    if top_k > 0:
+        k = min(int(top_k), x.shape[-1])
+        cutoff = torch.topk(x.float(), k, dim=-1).values[..., -1:]
+        x = torch.where(x.float() >= cutoff, x, neg)
+    if top_p < 1.0:
+        srt = torch.sort(x.float(), dim=-1, descending=True).values
+        cum = torch.cumsum(_probs(srt.to(x.dtype)), dim=-1)
+        idx = (cum < top_p).sum(dim=-1, keepdim=True).clamp(max=x.shape[-1] - 1)
+        x = torch.where(x.float() < torch.gather(srt, -1, idx), neg, x)
+    out.copy_(x)
+    return out

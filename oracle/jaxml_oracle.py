@@ -397,10 +397,46 @@ def forward(family: str, cfg, params, input_ids, dtype, attention_mask=None, kv_
 # ----------------------------------------------------------------------------------------------
 # Generation (Engine.generate with greedy / temperature sampling)
 # ----------------------------------------------------------------------------------------------
-def sample(logits: torch.Tensor, key, temperature: float, greedy: bool) -> torch.Tensor:
-    """``greedy_fn`` / ``categorical(subkey, logits/temp)`` on ``[B,1,V]`` logits; returns ``[B,1]`` int32."""
+def _probs(logits: torch.Tensor) -> torch.Tensor:
+    """softmax over the vocabulary: float32 arithmetic, result rounded to the logits' dtype (the
+    reference applies jax.nn.softmax to model-dtype logits)."""
+    x = logits.to(torch.float32)
+    e = torch.exp(x - x.max(dim=-1, keepdim=True).values)
+    return (e / e.sum(dim=-1, keepdim=True)).to(logits.dtype).to(torch.float32)
+
+
+def filter_logits(logits: torch.Tensor, top_k: int = 0, top_p: float = 1.0, min_p: float = 0.0) -> torch.Tensor:
+    """min-p, then top-k, then top-p filtering of ``[..., V]`` logits, filtered entries set to -inf
+    (inference_engine/sampling.py:34-72 and :169-188 for the order).  Restated choices where the
+    reference's JAX arithmetic is not visible from its source: probabilities are computed in float32 and
+    rounded to the logits' dtype; the top-p cumulative sum runs in float32 over those rounded
+    probabilities; a cutoff index past the end is clamped to the last sorted entry."""
+    neg = torch.tensor(float("-inf"), dtype=logits.dtype)
+    if min_p > 0.0:
+        keep = _probs(logits) >= min_p
+        any_kept = keep.any(dim=-1, keepdim=True)
+        logits = torch.where(any_kept, torch.where(keep, logits, neg), logits)
+    if top_k > 0:
+        k = min(top_k, logits.shape[-1])
+        cutoff = torch.topk(logits.to(torch.float32), k, dim=-1).values[..., -1:]
+        logits = torch.where(logits.to(torch.float32) >= cutoff, logits, neg)
+    if top_p < 1.0:
+        srt = torch.sort(logits.to(torch.float32), dim=-1, descending=True).values
+        cum = torch.cumsum(_probs(srt.to(logits.dtype)), dim=-1)
+        idx = (cum < top_p).sum(dim=-1, keepdim=True).clamp(max=logits.shape[-1] - 1)
+        cutoff = torch.gather(srt, -1, idx)
+        logits = torch.where(logits.to(torch.float32) < cutoff, neg, logits)
+    return logits
+
+
+def sample(logits: torch.Tensor, key, temperature: float, greedy: bool, top_k: int = 0, top_p: float = 1.0,
+           min_p: float = 0.0) -> torch.Tensor:
+    """``greedy_fn`` / ``categorical(subkey, filtered logits / temp)`` on ``[B,1,V]`` logits; returns
+    ``[B,1]`` int32."""
     if greedy:
         return torch.argmax(_f32(logits), dim=-1).to(torch.int32)
+    if top_k > 0 or top_p < 1.0 or min_p > 0.0:
+        logits = filter_logits(logits, top_k, top_p, min_p)
     arr = _f32(logits).numpy()
     if logits.dtype == torch.bfloat16:
         out = threefry.categorical_bf16(key, arr, temperature)
@@ -411,8 +447,8 @@ def sample(logits: torch.Tensor, key, temperature: float, greedy: bool) -> torch
 
 def generate(family: str, cfg, params, prompt_tokens, dtype, max_new_tokens: int = 10, temperature: float = 1.0,
              seed: int = 0, cache_stride: int = 256, attention_mask=None, include_prompt: bool = True,
-             top_k: int = 0, top_p: float = 1.0):
-    """``Engine.generate`` for the greedy and plain-temperature methods, including the chunk/resize loop."""
+             top_k: int = 0, top_p: float = 1.0, min_p: float = 0.0):
+    """``Engine.generate`` (greedy, temperature, min-p / top-k / top-p), including the chunk/resize loop."""
     prompt = _t(prompt_tokens).to(torch.int32)
     if prompt.ndim == 1:
         prompt = prompt[None]
@@ -440,7 +476,7 @@ def generate(family: str, cfg, params, prompt_tokens, dtype, max_new_tokens: int
             caches = out.kv_caches
             ks = threefry.split(key)
             key, sub = ks[0], ks[1]
-            tok = sample(out.logits[:, -1:], sub, temperature, greedy)
+            tok = sample(out.logits[:, -1:], sub, temperature, greedy, top_k, top_p, min_p)
             chunk.append(tok)
             steps = count - 1
         else:
@@ -451,7 +487,7 @@ def generate(family: str, cfg, params, prompt_tokens, dtype, max_new_tokens: int
             key, sub = ks[0], ks[1]
             out = forward(family, cfg, params, tok, dtype, kv_caches=caches, keep_last_n_logits=1)
             caches = out.kv_caches
-            tok = sample(out.logits, sub, temperature, greedy)
+            tok = sample(out.logits, sub, temperature, greedy, top_k, top_p, min_p)
             chunk.append(tok)
         chunk = torch.cat(chunk, dim=1)
         out_tokens.append(chunk)

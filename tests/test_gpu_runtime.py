@@ -96,6 +96,22 @@ def test_temperature_generation_matches_oracle(dtype, hf_models):
         assert torch.equal(toks[:, 0], want[:, 0].to(torch.int32))
 
 
+@pytest.mark.parametrize("top_k,top_p,min_p", [(20, 1.0, 0.0), (0, 0.9, 0.0), (0, 1.0, 0.05), (30, 0.85, 0.02)])
+def test_filtered_sampling_matches_oracle_f32(top_k, top_p, min_p, hf_models):
+    """min-p / top-k / top-p (device filter, then the threefry/Gumbel sample) vs the oracle, float32."""
+    _, cfg, params = hf_models["llama"]
+    B, P, n = 3, 7, 8
+    g = torch.Generator().manual_seed(4)
+    ids = torch.randint(0, cfg.vocab_size, (B, P), generator=g, dtype=torch.int32)
+    rt = _runtime("llama", cfg, params, torch.float32, B, 256)
+    rt.filters = (top_k, top_p, min_p)
+    toks = rt.generate(ids.cuda(), torch.ones(B, P, dtype=torch.bool, device="cuda"), n, False, 0.8, 7).cpu()
+    rt.check_status()
+    want = O.generate("llama", cfg, params, ids, torch.float32, max_new_tokens=n, temperature=0.8, seed=7,
+                      include_prompt=False, top_k=top_k, top_p=top_p, min_p=min_p)
+    assert torch.equal(toks, want.to(torch.int32))
+
+
 def test_padded_prompt_matches_oracle(hf_models):
     _, cfg, params = hf_models["llama"]
     B, P, T = 3, 9, 256
