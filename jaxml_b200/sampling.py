@@ -107,19 +107,19 @@ def filter_logits_(logits: torch.Tensor, out: torch.Tensor, top_k: int, top_p: f
     below top_p.  Where the reference's JAX arithmetic is not visible from its source: probabilities in
     float32 rounded to the logits' dtype, the cumulative sum in float32, a cutoff index past the end
     clamped to the last entry.  Device tensor ops only (capturable in a CUDA graph)."""
-    neg = torch.tensor(float("-inf"), dtype=logits.dtype, device=logits.device)
+    neg = float("-inf")   # a scalar: no host-to-device copy while a CUDA graph is being captured
     x = logits
     if min_p > 0.0:
         keep = _probs(x) >= min_p
-        x = torch.where(keep.any(dim=-1, keepdim=True), torch.where(keep, x, neg), x)
+        x = x.masked_fill(keep.any(dim=-1, keepdim=True) & ~keep, neg)
     if top_k > 0:
         k = min(int(top_k), x.shape[-1])
         cutoff = torch.topk(x.float(), k, dim=-1).values[..., -1:]
-        x = torch.where(x.float() >= cutoff, x, neg)
+        x = x.masked_fill(x.float() < cutoff, neg)
     if top_p < 1.0:
         srt = torch.sort(x.float(), dim=-1, descending=True).values
         cum = torch.cumsum(_probs(srt.to(x.dtype)), dim=-1)
         idx = (cum < top_p).sum(dim=-1, keepdim=True).clamp(max=x.shape[-1] - 1)
-        x = torch.where(x.float() < torch.gather(srt, -1, idx), neg, x)
+        x = x.masked_fill(x.float() < torch.gather(srt, -1, idx), neg)
     out.copy_(x)
     return out

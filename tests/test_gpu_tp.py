@@ -60,6 +60,12 @@ def _worker(rank, world, port, ids, q):
             logits.append(rt.logits_buf()[:B].float().cpu())
             toks.append(rt.next_ids.cpu())
         rt.check_status()
+        # filtered temperature sampling over the gathered vocabulary: every rank must draw the same tokens
+        rt.filters = (20, 0.9, 0.01)
+        ftoks = rt.generate(ids.cuda(), torch.ones(B, P, dtype=torch.bool, device="cuda"), 6, False, 0.8, 3).cpu()
+        rt.check_status()
+        rt.graph = None
+        toks.append(ftoks)
         q.put((rank, logits, toks, None))
         dist.barrier()
         dist.destroy_process_group()
