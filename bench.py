@@ -56,7 +56,9 @@ def parse():
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--micro", choices=["gemv", "attn", "gemm", "allreduce"], default=None,
+    ap.add_argument("--tp-pull", action="store_true",
+                    help="tensor-parallel decode: separate pull all-reduce kernels instead of the push-fused projections")
+    ap.add_argument("--micro", choices=["gemv", "attn", "gemm", "allreduce", "tpx"], default=None,
                     help="single-kernel microbenchmark on Llama-3-8B layer shapes instead of the decode step")
     ap.add_argument("--ctx", type=int, default=4096, help="context length of --micro attn")
     ap.add_argument("--shape", default="28672,4096", help="N,K of --micro gemv (default: fused gate/up)")
@@ -241,6 +243,10 @@ def gpu_arm(args):
     from jaxml_b200.models import random_params
 
     tp = world
+    if args.tp_pull:
+        from jaxml_b200.runtime import DecoderRuntime
+
+        DecoderRuntime.peer_push = False
     cfg = l8_config(args.layers)
     B, P = args.batch, args.prompt
     n_new = 1 + args.warmup + args.steps
@@ -346,6 +352,7 @@ def gpu_arm(args):
             "data": "synthetic (uniform-random prompt ids, N(0,0.02) random-init weights, seed 0)",
             "config": {"workload": "llama3-8b-shape bf16 greedy decode, batch 16, prompt 512, 256 new tokens",
                        "global_batch": B, "seq_len": P, "parallelism": f"tp{tp}",
+                       "tp_exchange": None if tp == 1 else ("pull all-reduce" if args.tp_pull else "push-fused"),
                        "l2": "inputs larger than L2 (15 GB of weights per step)"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                          "frac": achieved / hbm_peak, "traffic": GEMV_TC_GATEUP_TRAFFIC,
@@ -465,6 +472,92 @@ def micro_allreduce(args):
     dist.destroy_process_group()
 
 
+def micro_tp_exchange(args):
+    """One row-parallel decode projection of the Llama-3-8B shape and its exchange, at TP = WORLD_SIZE
+    (launch under torchrun): the projection (o_proj: K = 4096 / TP, down: K = 14336 / TP; N = 4096, batch
+    rows) followed by the norm that consumes the sum, three ways, each captured 32 times in a CUDA graph
+    and replayed (max over ranks): `local` = no exchange (the projection's float32 partial fed to the
+    norm as is: the compute-only floor), `pull` = projection, jx_allreduce_f32, norm, `push` = projection
+    with JX_EPI_PUSH_F32 and the push-mode norm.  Prints one JSON line per shape from rank 0."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from jaxml_b200 import _native as N
+    from jaxml_b200.engine import TPComm
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world < 2:
+        print(json.dumps({"micro": "tpx", "skipped": "needs WORLD_SIZE >= 2 (torchrun)"}))
+        return
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    lib = N.load()
+    comm = TPComm()
+    peer = comm.prepare_peer(dev)
+    M, d, Mp = args.batch, 4096, 16 if args.batch <= 16 else 64
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    ws_n = N.LL()
+    N.check(lib.jx_linear_decode_workspace(148, 64, ws_n), "ws")
+    ws = torch.zeros(ws_n.value, dtype=torch.float32, device=dev)
+    cnt = torch.zeros(d // 64 + 1, dtype=torch.int32, device=dev)
+    nw = torch.ones(d, dtype=torch.bfloat16, device=dev)
+    h = torch.zeros(M, d, dtype=torch.bfloat16, device=dev)
+    xn = torch.zeros(M, d, dtype=torch.bfloat16, device=dev)
+    part = torch.zeros(M, d, dtype=torch.float32, device=dev)
+    tmp = torch.zeros(M, d, dtype=torch.float32, device=dev)
+    for name, K in (("o_proj", 4096 // world), ("down", 14336 // world)):
+        copies = 4   # distinct weight copies (4 x 2 x 4096 x K bytes, above L2 for the down shape)
+        ws_list = [(0.02 * torch.randn(d * K, device=dev)).to(torch.bfloat16) for _ in range(copies)]
+        xp = torch.randn(Mp * K, device=dev).to(torch.bfloat16)
+
+        def one(stream, mode, i):
+            e = N.JxEpilogue()
+            e.M, e.N, e.ldo = M, d, d
+            if mode == "push":
+                peer.push_epilogue(e, d)
+            else:
+                e.kind = N.JX_EPI_STORE_F32
+                e.out = (part if mode == "local" else comm.partial_buffer(M * d)).data_ptr()
+            src = comm.partial_buffer(M * d) if mode == "pull" else None
+            N.check(lib.jx_linear_decode(ws_list[i % copies].data_ptr(), xp.data_ptr(), d, K, M, e, ws.data_ptr(),
+                                         ws.numel(), cnt.data_ptr(), status.data_ptr(), 148, 1, stream), "linear")
+            if mode == "pull":
+                comm.all_reduce_partial(src, tmp.view(-1), status)
+            a = N.JxNormArgs()
+            a.M, a.d, a.eps, a.kind = M, d, 1e-5, N.JX_NORM_RMS
+            a.h, a.ldh, a.w, a.out, a.ldo, a.status = h.data_ptr(), d, nw.data_ptr(), xn.data_ptr(), d, status.data_ptr()
+            if mode == "push":
+                peer.push_norm(a, d, d)
+            else:
+                a.a, a.a_f32, a.lda = (part if mode == "local" else tmp).data_ptr(), 1, d
+            N.check(lib.jx_norm(a, N.JX_BF16, 1, stream), "norm")
+
+        out = {}
+        for mode in ("local", "pull", "push"):
+            def launch_all(stream, mode=mode):
+                for i in range(32):   # the current stream is `stream` here (warm-up and capture)
+                    one(stream, mode, i)
+            dist.barrier()
+            ms = _graph_ms(launch_all, 32, reps=5)
+            t = torch.tensor([ms * 1e3], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            out[mode] = float(t.item())
+        del ws_list
+        if rank == 0:
+            print(json.dumps({"micro": "tpx", "world": world, "shape": name, "M": M, "N": d, "K": K,
+                              "local_us": out["local"], "pull_us": out["pull"], "push_us": out["push"],
+                              "status": int(status.item())}), flush=True)
+    torch.cuda.synchronize()
+    comm.close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def micro(args):
     """Single-kernel microbenchmarks on Llama-3-8B layer shapes (bf16, N(0,1) activations, N(0,0.02)
     weights): `gemv` = the decode projection on the gate/up weights of 8 distinct layers (1.9 GB, larger
@@ -568,6 +661,9 @@ def main():
     args = parse()
     if args.micro == "allreduce":
         micro_allreduce(args)
+        return
+    if args.micro == "tpx":
+        micro_tp_exchange(args)
         return
     if args.micro:
         micro(args)

@@ -43,6 +43,7 @@ extern "C" {
 #define JX_EPI_RESID2 5           /* out = dtype(dtype(acc + res2) + res)  (parallel resid.) models/gpt_neox.py:126-129 */
 #define JX_EPI_STORE_F32 6        /* float out = acc + bias: a tensor-parallel partial sum, all-reduced in float32 */
 #define JX_EPI_ACC_F32 7          /* float out += acc + bias (GPT-NeoX parallel residual partials)            */
+#define JX_EPI_PUSH_F32 8         /* float acc + bias stored into every rank's receive slot (peer_* fields)   */
 
 /* Fused epilogue of a projection.  Output column n of a plain output lives at out[m*ldo + n]; a K128
  * output (out_rp > 0) is the tiled layout described in jx_pack_k128. */
@@ -67,6 +68,20 @@ typedef struct jx_epilogue {
   long long pf_np, pf_kp;
   int pf_rows;           /* set by the library: weight rows per block of the next call's kernel */
   int pf_grid;           /* set by the library: CTAs of the next call */
+  /* JX_EPI_PUSH_F32 (tensor parallelism, decode projections): a row-parallel projection and its
+   * all-reduce in one kernel.  Each finished block's float32 partial (M rows x 64 columns) is stored
+   * over NVLink into this rank's receive slot of every rank's peer region, then the block's 64-column
+   * units are flagged at every rank; a jx_norm with peer_recv set consumes the sum (no counterpart in the
+   * reference, which all-reduces through XLA).  Offsets are bytes within every rank's region (layout
+   * from jx_comm_layout); `ldo` gives the element index (row * ldo + column) inside the slot.  Calls
+   * alternate between two sets of slots and flags by the parity of the push epoch, which the device
+   * keeps, so captured CUDA graphs replay correctly whatever number of pushes a pass makes. */
+  const void* peer_bases;      /* device array [peer_world] of the ranks' region bases, mapped here */
+  long long peer_recv_off;     /* receive slots: slot (set s, source r) at + (s * peer_world + r) * peer_slot_bytes */
+  long long peer_slot_bytes;
+  long long peer_flag_off;     /* flags: [2 sets][256 units][8 sources] uint32 */
+  long long peer_seq_off;      /* push epoch counter */
+  int peer_rank, peer_world;
 } jx_epilogue;
 
 /* Row-wise embedding gather / residual add / normalisation (one launch per call). */
@@ -96,6 +111,15 @@ typedef struct jx_norm_args {
   void* out2;
   long long ldo2, out2_rp;
   int* status;
+  /* Tensor parallelism, push mode (peer_recv set): `a` is the rank-order sum of the float32 partials that
+   * the row-parallel projection (JX_EPI_PUSH_F32) stored into this rank's receive slots; the kernel
+   * first waits, bounded, for the flags of every 64-column unit from every rank, and its last CTA
+   * advances the push epoch.  bfloat16 models with d / 8 a multiple of 32 (the vectorised kernel). */
+  const void* peer_recv;       /* this rank's receive slots: [2 sets][peer_world sources][peer_stride floats] */
+  long long peer_stride;
+  const unsigned* peer_flags;  /* this rank's push flags: [2 sets][256 units][8 sources] */
+  unsigned* peer_seq;          /* this rank's push epoch counter ([0] epoch, [1] finished CTAs) */
+  int peer_world, peer_units;
 } jx_norm_args;
 
 typedef struct jx_qkv_args {
@@ -282,20 +306,23 @@ int jx_memset_async(void* ptr, int value, long long bytes, void* stream);
  * The reference all-reduces the row-parallel o_proj / down_proj outputs through XLA's GSPMD collectives
  * (inference_engine/engine.py:258-267 sharding rules, models/llama.py:133-137 residual adds); these
  * calls replace that collective for decode-sized messages.  Each rank allocates one region with
- * jx_comm_alloc (layout from jx_allreduce_layout for max_floats: flags and counters, then two float32
- * partials buffers at data_offset0 / data_offset1), shares it with jx_ipc_get_handle (64-byte handle,
- * exchanged by the caller) and maps the other ranks' regions with jx_ipc_open_handle.
- * jx_allreduce_f32 sums the first n floats of partials buffer `which` of every region in rank order and
- * writes them to `out` (every rank gets bit-identical values).  Consecutive calls must alternate
- * `which`; all ranks make the same sequence of calls; each device wait is bounded (JX_ERR_TIMEOUT in
- * *status). */
+ * jx_comm_alloc (layout from jx_comm_layout), shares it with jx_ipc_get_handle (64-byte handle,
+ * exchanged by the caller), maps the other ranks' regions with jx_ipc_open_handle and writes the table
+ * of mapped bases into its own region (base_table offset).  Two forms:
+ *   - jx_allreduce_f32: sums the first n floats of partials buffer `which` of every region in rank order
+ *     into `out` (every rank gets bit-identical values);
+ *   - the push form: a decode projection with JX_EPI_PUSH_F32 followed by a jx_norm with peer_recv set.
+ * Consecutive calls (of either form) alternate `which`; all ranks make the same sequence of calls; every
+ * device wait is bounded (JX_ERR_TIMEOUT in *status).
+ * jx_comm_layout fills out10: [0] region bytes, [1] / [2] all-reduce buffers 0 / 1, [3] push receive
+ * slots (+ (which * world + source) * [4]), [4] receive slot stride, [5] push flags (+ which * [6]),
+ * [6] flags bytes per call, [7] push epoch counter, [8] base table, [9] units per call at most. */
 int jx_comm_alloc(long long bytes, void** ptr_out);
 int jx_comm_free(void* ptr);
 int jx_ipc_get_handle(const void* ptr, unsigned char* handle_out);
 int jx_ipc_open_handle(const unsigned char* handle, void** ptr_out);
 int jx_ipc_close_handle(void* ptr);
-int jx_allreduce_layout(long long max_floats, long long* region_bytes_out, long long* data_offset0_out,
-                        long long* data_offset1_out);
+int jx_comm_layout(long long max_floats, int world, long long* out10);
 int jx_allreduce_f32(void* const* bases, int rank, int world, long long max_floats, int which, long long n,
                      float* out, int* status, int pdl, void* stream);
 

@@ -16,7 +16,7 @@ JX_OK, JX_ERR_ARG, JX_ERR_SHAPE, JX_ERR_DTYPE, JX_ERR_RANGE, JX_ERR_TIMEOUT, JX_
 JX_F32, JX_BF16 = 0, 1
 JX_NORM_NONE, JX_NORM_RMS, JX_NORM_GEMMA, JX_NORM_LAYER = 0, 1, 2, 3
 (JX_EPI_STORE, JX_EPI_RESID, JX_EPI_GLU_SILU, JX_EPI_GLU_GELU_TANH, JX_EPI_ACT_GELU_ERF, JX_EPI_RESID2,
- JX_EPI_STORE_F32, JX_EPI_ACC_F32) = range(8)
+ JX_EPI_STORE_F32, JX_EPI_ACC_F32, JX_EPI_PUSH_F32) = range(9)
 
 STATUS_NAMES = {
     JX_OK: "ok", JX_ERR_ARG: "bad argument", JX_ERR_SHAPE: "bad shape", JX_ERR_DTYPE: "bad dtype",
@@ -33,14 +33,17 @@ F = ctypes.c_float
 class JxEpilogue(ctypes.Structure):
     _fields_ = [("kind", I), ("M", I), ("N", I), ("pf_iters", I), ("bias", P), ("out", P), ("ldo", LL),
                 ("out_rp", LL), ("res", P), ("ldr", LL), ("res2", P), ("ldr2", LL), ("pf_w", P), ("pf_np", LL),
-                ("pf_kp", LL), ("pf_rows", I), ("pf_grid", I)]
+                ("pf_kp", LL), ("pf_rows", I), ("pf_grid", I), ("peer_bases", P), ("peer_recv_off", LL),
+                ("peer_slot_bytes", LL), ("peer_flag_off", LL), ("peer_seq_off", LL), ("peer_rank", I), ("peer_world", I)]
 
 
 class JxNormArgs(ctypes.Structure):
     _fields_ = [("M", I), ("d", I), ("eps", F), ("kind", I), ("kind_pre", I), ("vocab", I), ("ids", P),
                 ("table", P), ("embed_scale", F), ("a_f32", I), ("row_map", P), ("a", P), ("lda", LL), ("h", P),
                 ("ldh", LL), ("w_pre", P), ("b_pre", P), ("w", P), ("b", P), ("out", P), ("ldo", LL),
-                ("out_rp", LL), ("w2", P), ("b2", P), ("out2", P), ("ldo2", LL), ("out2_rp", LL), ("status", P)]
+                ("out_rp", LL), ("w2", P), ("b2", P), ("out2", P), ("ldo2", LL), ("out2_rp", LL), ("status", P),
+                ("peer_recv", P), ("peer_stride", LL), ("peer_flags", P), ("peer_seq", P), ("peer_world", I),
+                ("peer_units", I)]
 
 
 class JxQkvArgs(ctypes.Structure):
@@ -104,7 +107,7 @@ _PROTOS = {
     "jx_ipc_get_handle": (I, [P, ctypes.c_char_p]),
     "jx_ipc_open_handle": (I, [ctypes.c_char_p, ctypes.POINTER(P)]),
     "jx_ipc_close_handle": (I, [P]),
-    "jx_allreduce_layout": (I, [LL, ctypes.POINTER(LL), ctypes.POINTER(LL), ctypes.POINTER(LL)]),
+    "jx_comm_layout": (I, [LL, I, ctypes.POINTER(LL)]),
     "jx_allreduce_f32": (I, [ctypes.POINTER(P), I, I, LL, I, LL, P, P, I, P]),
 }
 

@@ -159,13 +159,15 @@ int jx_linear_decode(const void* W, const void* X, long long Np, long long Kp, i
   const int rc = run_gemv((const bf16*)W, (const bf16*)X, Np, Kp, M, *epi, ws, ws_floats, counters, status, grid,
                           pdl != 0, (cudaStream_t)stream);
   if (rc == JX_ERR_CUDA) return note_cuda("jx_linear_decode");
-  if (rc != JX_OK) return fail(rc, "jx_linear_decode: bad shape (M<=64, Np%64, Kp%128), alignment or workspace");
+  if (rc != JX_OK)
+    return fail(rc, "jx_linear_decode: bad shape (M<=64, Np%64, Kp%128), alignment, workspace or push fields");
   return JX_OK;
 }
 
 int jx_linear_prefill(const void* X, const void* W, long long Mp, long long Np, long long Kp, const jx_epilogue* epi,
                       int* status, int pdl, void* stream) {
   if (!W || !X || !epi) return fail(JX_ERR_ARG, "jx_linear_prefill: null pointer");
+  if (epi->kind == JX_EPI_PUSH_F32) return fail(JX_ERR_UNSUPPORTED, "jx_linear_prefill: the push epilogue is decode-only");
   const int rc = run_gemm_k128((const bf16*)X, (const bf16*)W, Mp, Np, Kp, *epi, status, pdl != 0, (cudaStream_t)stream);
   if (rc == JX_ERR_CUDA) return note_cuda("jx_linear_prefill");
   if (rc != JX_OK) return fail(rc, "jx_linear_prefill: Mp, Np and Kp must be multiples of 128");
@@ -175,6 +177,7 @@ int jx_linear_prefill(const void* X, const void* W, long long Mp, long long Np, 
 int jx_linear_f32(const float* X, long long ldx, const float* W, int M, int N, int K, const jx_epilogue* epi, int pdl,
                   void* stream) {
   if (!X || !W || !epi) return fail(JX_ERR_ARG, "jx_linear_f32: null pointer");
+  if (epi->kind == JX_EPI_PUSH_F32) return fail(JX_ERR_UNSUPPORTED, "jx_linear_f32: the push epilogue is decode-only");
   const int rc = run_gemm_f32(X, ldx, W, M, N, K, *epi, pdl != 0, (cudaStream_t)stream);
   if (rc == JX_ERR_CUDA) return note_cuda("jx_linear_f32");
   if (rc != JX_OK) return fail(rc, "jx_linear_f32: bad shape");
@@ -267,8 +270,9 @@ int jx_sample_finalize(const jx_sample_args* args, const unsigned long long* gat
 // tensor-parallel peer memory and all-reduce
 // ------------------------------------------------------------------------------------------------
 namespace jxb {
-long long ar_region_bytes(long long max_floats);
+long long ar_region_bytes(long long max_floats, int world);
 long long ar_data_offset(long long max_floats, int which);
+void comm_layout(long long max_floats, int world, long long* out);
 int run_allreduce_f32(void* const* bases, int rank, int world, long long max_floats, int which, long long n,
                       float* out, int* status, bool pdl, cudaStream_t s);
 }  // namespace jxb
@@ -315,13 +319,10 @@ int jx_ipc_close_handle(void* ptr) {
   return cudaIpcCloseMemHandle(ptr) == cudaSuccess ? JX_OK : note_cuda("jx_ipc_close_handle");
 }
 
-int jx_allreduce_layout(long long max_floats, long long* region_bytes_out, long long* data_offset0_out,
-                        long long* data_offset1_out) {
-  if (max_floats <= 0 || !region_bytes_out || !data_offset0_out || !data_offset1_out)
-    return fail(JX_ERR_ARG, "jx_allreduce_layout: non-positive size or null output");
-  *region_bytes_out = jxb::ar_region_bytes(max_floats);
-  *data_offset0_out = jxb::ar_data_offset(max_floats, 0);
-  *data_offset1_out = jxb::ar_data_offset(max_floats, 1);
+int jx_comm_layout(long long max_floats, int world, long long* out10) {
+  if (max_floats <= 0 || world < 1 || world > 8 || !out10)
+    return fail(JX_ERR_ARG, "jx_comm_layout: max_floats > 0, 1 <= world <= 8, non-null output");
+  jxb::comm_layout(max_floats, world, out10);
   return JX_OK;
 }
 

@@ -3,7 +3,7 @@
 // sharding through XLA's GSPMD collectives, inference_engine/engine.py:258-267 and models/llama.py:133-137).
 //
 // Every rank owns one device region (cudaMalloc'd here, shared with the other ranks through CUDA IPC):
-//   [flags: kArMaxCtas x kArMaxRanks uint32][seq + finish counter][partials buffer 0][partials buffer 1]
+//   [header: flags, counters, the ranks' base table][partials buffer 0][partials buffer 1][push slots]
 // One-shot algorithm with one handshake, CTA b of every rank working on the same slice:
 //   1. pdl wait (the partial in buffer `which` was written by the previous kernel), read seq; v = seq + 1
 //   2. write v into flags[b][my rank] of every rank (release, system scope); wait until this rank's
@@ -24,7 +24,15 @@ constexpr int kArMaxRanks = 8;
 constexpr int kArMaxCtas = 64;
 constexpr int kArThreads = 512;
 constexpr long long kArFlagBytes = (long long)kArMaxCtas * kArMaxRanks * 4;
-constexpr long long kArHeaderBytes = kArFlagBytes + 256;    // flags, then seq (+0) and finish count (+4)
+// Region header: all-reduce flags, all-reduce counters (+0 seq, +4 finished CTAs), push counters (+0 epoch,
+// +4 finished CTAs), the table of every rank's region base as mapped in this process, push flags
+// [2 calls][kPushMaxUnits 64-column units][kArMaxRanks sources].
+constexpr long long kArCtrOff = kArFlagBytes;
+constexpr long long kPushSeqOff = kArCtrOff + 256;
+constexpr long long kBasesOff = kPushSeqOff + 256;
+constexpr long long kPushFlagOff = kBasesOff + 256;
+constexpr long long kPushFlagBytes = 2LL * kPushMaxUnits * kArMaxRanks * 4;
+constexpr long long kArHeaderBytes = kPushFlagOff + kPushFlagBytes;
 
 struct ArParams {
   unsigned char* base[kArMaxRanks];   // every rank's region (this rank's own included)
@@ -34,15 +42,6 @@ struct ArParams {
   float* out;                         // this rank's result
   int* status;
 };
-
-__device__ __forceinline__ void st_release_sys(unsigned int* p, unsigned int v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int* p) {
-  unsigned int v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
 
 // Signal CTA b's readiness to every rank and wait for every rank's.  Thread r < world does rank r.
 // Returns false on timeout.
@@ -70,7 +69,7 @@ __global__ void __launch_bounds__(kArThreads) allreduce_f32_kernel(ArParams p) {
   __shared__ unsigned int s_seq;
   pdl_trigger();
   pdl_wait();
-  unsigned int* ctr = reinterpret_cast<unsigned int*>(p.base[p.rank] + kArFlagBytes);   // [0] seq, [1] finished
+  unsigned int* ctr = reinterpret_cast<unsigned int*>(p.base[p.rank] + kArCtrOff);   // [0] seq, [1] finished
   if (threadIdx.x == 0) s_seq = *reinterpret_cast<volatile unsigned int*>(ctr);
   __syncthreads();
   const unsigned int v = s_seq + 1;
@@ -110,8 +109,24 @@ __global__ void __launch_bounds__(kArThreads) allreduce_f32_kernel(ArParams p) {
 }
 
 static long long ar_buffer_bytes(long long max_floats) { return ((max_floats * 4 + 255) / 256) * 256; }
-long long ar_region_bytes(long long max_floats) { return kArHeaderBytes + 2 * ar_buffer_bytes(max_floats); }
+// Layout: header, all-reduce partials buffers 0 and 1, push receive slots [2 calls][world sources].
+long long ar_region_bytes(long long max_floats, int world) {
+  return kArHeaderBytes + (2 + 2LL * world) * ar_buffer_bytes(max_floats);
+}
 long long ar_data_offset(long long max_floats, int which) { return kArHeaderBytes + which * ar_buffer_bytes(max_floats); }
+void comm_layout(long long max_floats, int world, long long* out) {
+  const long long buf = ar_buffer_bytes(max_floats);
+  out[0] = ar_region_bytes(max_floats, world);
+  out[1] = ar_data_offset(max_floats, 0);
+  out[2] = ar_data_offset(max_floats, 1);
+  out[3] = kArHeaderBytes + 2 * buf;   // push receive slots: + ((which * world + source) * recv_stride)
+  out[4] = buf;                        // recv_stride (bytes between source slots)
+  out[5] = kPushFlagOff;               // push flags: + which * kPushMaxUnits * kArMaxRanks * 4
+  out[6] = (long long)kPushMaxUnits * kArMaxRanks * 4;
+  out[7] = kPushSeqOff;
+  out[8] = kBasesOff;
+  out[9] = kPushMaxUnits;
+}
 
 int run_allreduce_f32(void* const* bases, int rank, int world, long long max_floats, int which, long long n,
                       float* out, int* status, bool pdl, cudaStream_t s) {

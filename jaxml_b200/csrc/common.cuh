@@ -306,6 +306,23 @@ __device__ __forceinline__ int ld_acquire_gpu(const int* p) {
   return v;
 }
 
+// Push-mode row-parallel outputs are flagged in units of 64 columns, at most this many per call.
+constexpr int kPushMaxUnits = 256;
+
+// System-scope release / acquire on a uint32 flag (flags that other GPUs write over NVLink).
+__device__ __forceinline__ void st_release_sys(unsigned int* p, unsigned int v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_relaxed_sys(unsigned int* p, unsigned int v) {
+  asm volatile("st.relaxed.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+__device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 // Status word shared by all kernels of a call: the first error code sticks.
 __device__ __forceinline__ void set_status(int* status, int code) {
   if (status) atomicCAS(status, 0, code);

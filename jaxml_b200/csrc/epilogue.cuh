@@ -28,6 +28,30 @@ __device__ __forceinline__ void prefetch_next_weights(const EpiParams& e, int c)
   }
 }
 
+// After a JX_EPI_PUSH_F32 epilogue of output columns [n0, n0 + cols) (called by one thread once every
+// thread of the block has stored): flag its 64-column units at every rank with this call's epoch
+// (the receiving rank's push counter + 1, which is ours too: all ranks make the same calls).
+__device__ __forceinline__ unsigned push_epoch(const EpiParams& e) {
+  const unsigned char* const* bases = reinterpret_cast<const unsigned char* const*>(e.peer_bases);
+  return *reinterpret_cast<const volatile unsigned*>(bases[e.peer_rank] + e.peer_seq_off);
+}
+
+__device__ __forceinline__ void push_signal(const EpiParams& e, long long n0, int cols) {
+  const unsigned char* const* bases = reinterpret_cast<const unsigned char* const*>(e.peer_bases);
+  const unsigned ep = push_epoch(e), v = ep + 1;
+  // Release pattern: the CTA barrier before this call orders every thread's slot stores before this
+  // thread's fence (cumulativity), and the fence orders them before the flag stores below.
+  fence_acq_rel_sys();
+  const long long set_off = e.peer_flag_off + (long long)(ep & 1) * kPushMaxUnits * 8 * 4;
+  const int u0 = (int)(n0 >> 6), nu = cols >> 6;
+  for (int r = 0; r < e.peer_world; ++r)
+    for (int u = 0; u < nu; ++u) {
+      unsigned* f = reinterpret_cast<unsigned*>(const_cast<unsigned char*>(bases[r]) + set_off) + (u0 + u) * 8 +
+                    e.peer_rank;
+      st_relaxed_sys(f, v);
+    }
+}
+
 template <typename T>
 __device__ __forceinline__ float bias_at(const EpiParams& e, long long n) {
   return e.bias ? to_f(reinterpret_cast<const T*>(e.bias)[n]) : 0.0f;
@@ -52,6 +76,28 @@ __device__ __forceinline__ void run_epilogue(const EpiParams& e, long long m0, i
       const float a = rnd<T>(e.kind == JX_EPI_GLU_SILU ? silu_f(g) : gelu_tanh_f(g));
       const long long o = e.out_rp > 0 ? k128_offset(row, col, e.out_rp) : row * e.ldo + col;
       reinterpret_cast<T*>(e.out)[o] = from_f<T>(a * u);
+    }
+    return;
+  }
+  if (e.kind == JX_EPI_PUSH_F32) {
+    // row-parallel partial sums stored over NVLink into this rank's receive slot of every rank's region
+    // (the flags follow in push_signal, once every thread of the CTA has stored its part)
+    const unsigned char* const* bases = reinterpret_cast<const unsigned char* const*>(e.peer_bases);
+    const long long slot =
+        e.peer_recv_off + ((long long)(push_epoch(e) & 1) * e.peer_world + e.peer_rank) * e.peer_slot_bytes;
+    const int q4 = cols >> 2;
+    for (int idx = tid; idx < rows * q4; idx += nthreads) {
+      const int m = idx / q4, j = (idx - m * q4) * 4;
+      const long long row = m0 + m, n = n0 + j;
+      if (row >= e.M || n >= e.N) continue;
+      float4 v;
+      v.x = tile(m, j) + bias_at<T>(e, n);
+      v.y = tile(m, j + 1) + bias_at<T>(e, n + 1);
+      v.z = tile(m, j + 2) + bias_at<T>(e, n + 2);
+      v.w = tile(m, j + 3) + bias_at<T>(e, n + 3);
+      const long long off = slot + (row * e.ldo + n) * 4;
+      for (int r = 0; r < e.peer_world; ++r)
+        *reinterpret_cast<float4*>(const_cast<unsigned char*>(bases[r]) + off) = v;
     }
     return;
   }

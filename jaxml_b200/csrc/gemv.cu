@@ -301,6 +301,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
                          [&](int m, int j) { return tile[m * kTileLd + j]; }, tid, kGemvConsumers);
     }
     named_bar_sync(1, kGemvConsumers);
+    if (do_epi && !dead && e.kind == JX_EPI_PUSH_F32 && tid == 0) push_signal(e, nb * kGemvBN, kGemvBN);
   }
 }
 
@@ -352,6 +353,15 @@ int run_gemv(const bf16* W, const bf16* X, long long Np, long long Kp, int M, co
   // L2 prefetch plan of the next decode projection (jx_epilogue.pf_w): the kernel and grid that call
   // will get by the same rules, or no prefetch when its sizes or alignment are not a decode projection's.
   EpiParams e = e_in;
+  if (e.kind == JX_EPI_PUSH_F32) {
+    // every rank's receive slot and flags sit at the same offsets of its region; units of 64 columns
+    if (!e.peer_bases || e.peer_world < 1 || e.peer_world > 8 || e.peer_rank < 0 || e.peer_rank >= e.peer_world ||
+        e.N <= 0 || e.N % 64 || e.N > Np || Np / 64 > kPushMaxUnits || (e.ldo & 3) || e.ldo < e.N ||
+        (e.peer_recv_off & 15) || (e.peer_slot_bytes & 15) || (long long)e.M * e.ldo * 4 > e.peer_slot_bytes ||
+        (e.peer_flag_off & 3) || (e.peer_seq_off & 7) ||
+        (reinterpret_cast<uintptr_t>(e.peer_bases) & 7))
+      return JX_ERR_ARG;
+  }
   e.pf_rows = 0;
   e.pf_grid = 0;
   if (e.pf_w && e.pf_iters > 0 && e.pf_np > 0 && e.pf_kp > 0) {

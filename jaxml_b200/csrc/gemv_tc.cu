@@ -300,6 +300,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         run_epilogue<bf16>(e, 0, (int)Mp, nb * kTcBN, kTcBN, [&](int m, int j) { return tile[m * C::kLd + j]; },
                            tid, 128);
       named_bar_sync(1, 128);
+      if (do_epi && !sh[0] && e.kind == JX_EPI_PUSH_F32 && tid == 0) push_signal(e, nb * kTcBN, kTcBN);
     }
   }
   // Teardown without a CTA-wide barrier (the roles above leave their warps at different points): the

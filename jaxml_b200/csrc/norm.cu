@@ -217,12 +217,54 @@ __device__ __forceinline__ void vnormalize(const float* x, float* y, int d, int 
   }
 }
 
+// Push mode: wait, bounded, until every 64-column unit carries epoch v from every rank (thread t polls
+// unit t / world, source t % world).  False on timeout.
+__device__ __forceinline__ bool peer_wait(const NormArgs& p, unsigned v) {
+  bool ok = true;
+  const int t = threadIdx.x;
+  if (t < p.peer_units * p.peer_world) {
+    const unsigned* f = p.peer_flags + ((v - 1) & 1) * kPushMaxUnits * 8 + (t / p.peer_world) * 8 + (t % p.peer_world);
+    if (ld_acquire_sys(f) != v) {
+      const uint64_t t0 = globaltimer_ns();
+      while (ld_acquire_sys(f) != v) {
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+          ok = false;
+          break;
+        }
+      }
+    }
+  }
+  return __syncthreads_and(ok) != 0;
+}
+
+// Rank-order float32 sum of the 8 partials at (m, j0) in this rank's receive slots of set `set`.
+__device__ __forceinline__ void peer_sum8(const NormArgs& p, unsigned set, long long m, int j0, float4& s0,
+                                          float4& s1) {
+  const float* base =
+      reinterpret_cast<const float*>(p.peer_recv) + (long long)set * p.peer_world * p.peer_stride + m * p.lda + j0;
+  s0 = __ldcv(reinterpret_cast<const float4*>(base));
+  s1 = __ldcv(reinterpret_cast<const float4*>(base) + 1);
+  for (int r = 1; r < p.peer_world; ++r) {
+    const float4* q = reinterpret_cast<const float4*>(base + r * p.peer_stride);
+    const float4 u0 = __ldcv(q), u1 = __ldcv(q + 1);
+    s0.x += u0.x, s0.y += u0.y, s0.z += u0.z, s0.w += u0.w;
+    s1.x += u1.x, s1.y += u1.y, s1.z += u1.z, s1.w += u1.w;
+  }
+}
+
 __global__ void __launch_bounds__(1024) norm_vec_kernel(NormArgs p) {
   __shared__ float red[32];
+  __shared__ unsigned s_epoch;
   const long long m = blockIdx.x;
   const int j0 = threadIdx.x * 8;
   pdl_trigger();
   pdl_wait();
+  const bool push = p.peer_world > 0;
+  if (push) {
+    if (threadIdx.x == 0) s_epoch = *reinterpret_cast<volatile unsigned*>(p.peer_seq);
+    __syncthreads();
+    if (!peer_wait(p, s_epoch + 1) && threadIdx.x == 0) set_status(p.status, JX_ERR_TIMEOUT);
+  }
   bf16* h = reinterpret_cast<bf16*>(p.h);
   float x[8], y[8];
   if (p.ids) {
@@ -242,9 +284,14 @@ __global__ void __launch_bounds__(1024) norm_vec_kernel(NormArgs p) {
     const long long src = p.row_map ? (long long)p.row_map[m] : m;
     vload8(h + src * p.ldh + j0, x);
   }
-  if (p.a) {
+  if (p.a || push) {
     float a[8];
-    if (p.a_f32) {
+    if (push) {
+      float4 u0, u1;
+      peer_sum8(p, s_epoch & 1, m, j0, u0, u1);
+      a[0] = rnd<bf16>(u0.x), a[1] = rnd<bf16>(u0.y), a[2] = rnd<bf16>(u0.z), a[3] = rnd<bf16>(u0.w);
+      a[4] = rnd<bf16>(u1.x), a[5] = rnd<bf16>(u1.y), a[6] = rnd<bf16>(u1.z), a[7] = rnd<bf16>(u1.w);
+    } else if (p.a_f32) {
       // a float32 input (an all-reduced partial sum) is rounded to bf16 first
       const float4* af = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.a) + m * p.lda + j0);
       const float4 u0 = af[0], u1 = af[1];
@@ -277,12 +324,33 @@ __global__ void __launch_bounds__(1024) norm_vec_kernel(NormArgs p) {
     bf16* o = reinterpret_cast<bf16*>(p.out2);
     vstore8(o + (p.out2_rp > 0 ? k128_offset(m, j0, p.out2_rp) : m * p.ldo2 + j0), y);
   }
+  if (push) {
+    // every CTA read the epoch before arriving, so the last to arrive may advance it
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      if (atomicAdd(p.peer_seq + 1, 1u) == gridDim.x - 1) {
+        p.peer_seq[1] = 0;
+        p.peer_seq[0] = s_epoch + 1;
+        __threadfence();
+      }
+    }
+  }
 }
 
 int run_norm(int dtype, const NormArgs& p, bool pdl, cudaStream_t stream) {
   if (p.M <= 0 || p.d <= 0) return JX_ERR_SHAPE;
   const bool aligned = ((p.ldh | p.lda | p.ldo | p.ldo2) & 7) == 0;
-  if (dtype == JX_BF16 && p.d % 8 == 0 && p.d / 8 <= 1024 && (p.d / 8) % 32 == 0 && aligned) {
+  const bool vec = dtype == JX_BF16 && p.d % 8 == 0 && p.d / 8 <= 1024 && (p.d / 8) % 32 == 0 && aligned;
+  if (p.peer_world != 0) {
+    // push mode: the vectorised kernel only; the partials are float32 rows of lda floats
+    if (!vec || p.peer_world < 1 || p.peer_world > 8 || p.d % 64 || p.peer_units != p.d / 64) return JX_ERR_SHAPE;
+    if (!p.peer_recv || !p.peer_flags || !p.peer_seq || p.a) return JX_ERR_ARG;
+    if ((p.lda & 3) || (p.peer_stride & 3) || ((uintptr_t)p.peer_recv & 15) || ((uintptr_t)p.peer_seq & 7) ||
+        (long long)p.M * p.lda > p.peer_stride)
+      return JX_ERR_ARG;
+  }
+  if (vec) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(p.M);
     cfg.blockDim = dim3(p.d / 8);

@@ -43,17 +43,24 @@ class InferenceConfig:
 
 
 class _RawF32:
-    """Zero-copy float32 view of device memory the library allocated (CUDA array interface)."""
+    """Zero-copy view of device memory the library allocated (CUDA array interface); float32 unless
+    another typestr is given."""
 
-    def __init__(self, ptr: int, n: int):
-        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (ptr, False), "version": 3}
+    def __init__(self, ptr: int, n: int, typestr: str = "<f4"):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": typestr, "data": (ptr, False), "version": 3}
 
 
 class PeerRegion:
-    """This rank's peer-mapped region for the NVLink all-reduce (include/jxb200.h, jx_allreduce_f32): a
-    library-allocated device buffer shared with the other ranks through CUDA IPC handles exchanged over
-    torch.distributed, and the other ranks' buffers mapped here.  `data[0]` and `data[1]` are the two
-    float32 partials buffers the row-parallel projections write into (consecutive all-reduces alternate)."""
+    """This rank's peer-mapped region for tensor parallelism over NVLink (include/jxb200.h,
+    jx_comm_layout): a library-allocated device buffer shared with the other ranks through CUDA IPC handles
+    exchanged over torch.distributed, and the other ranks' buffers mapped here.
+
+    - `data[0]` and `data[1]`: the two float32 partials buffers of the pull all-reduce (jx_allreduce_f32);
+      consecutive all-reduces alternate.
+    - push mode (a decode projection with JX_EPI_PUSH_F32 feeding a jx_norm with peer_recv): every rank
+      stores its partial into its own receive slot of every region; `bases_dev` is the device table of the
+      ranks' region bases the kernels index, `recv_off` / `slot_bytes` / `flag_off` / `seq_off` the byte
+      offsets shared by every region."""
 
     def __init__(self, comm: "TPComm", max_floats: int, device: torch.device):
         import ctypes
@@ -61,14 +68,15 @@ class PeerRegion:
         from . import _native as N
 
         lib = N.load()
-        rb, off0, off1 = N.LL(), N.LL(), N.LL()
-        N.check(lib.jx_allreduce_layout(max_floats, rb, off0, off1), "jx_allreduce_layout")
+        off = (N.LL * 10)()
+        N.check(lib.jx_comm_layout(max_floats, comm.size, off), "jx_comm_layout")
         self.max_floats = max_floats
         self._lib, self._N = lib, N
         with torch.cuda.device(device):
             p = N.P()
-            N.check(lib.jx_comm_alloc(rb.value, ctypes.byref(p)), "jx_comm_alloc")
+            N.check(lib.jx_comm_alloc(off[0], ctypes.byref(p)), "jx_comm_alloc")
             self.local = p.value
+            torch.cuda.synchronize(device)   # the zeroed flags before any peer can write them
             h = ctypes.create_string_buffer(64)
             N.check(lib.jx_ipc_get_handle(self.local, h), "jx_ipc_get_handle")
             handles = [None] * comm.size
@@ -82,10 +90,41 @@ class PeerRegion:
                 N.check(lib.jx_ipc_open_handle(hr, ctypes.byref(q)), "jx_ipc_open_handle")
                 bases.append(q.value)
                 self._opened.append(q.value)
+            # the bases table the push kernels read, inside this rank's own region
+            self.bases_dev = self.local + off[8]
+            table = torch.as_tensor(_RawF32(self.bases_dev, comm.size, "<i8"), device=device)
+            table.copy_(torch.tensor(bases, dtype=torch.int64))
+            torch.cuda.synchronize(device)
         self.bases = (N.P * comm.size)(*bases)
-        self._raw = [_RawF32(self.local + o, max_floats) for o in (off0.value, off1.value)]
+        self._raw = [_RawF32(self.local + o, max_floats) for o in (off[1], off[2])]
         self.data = [torch.as_tensor(r, device=device) for r in self._raw]
         self.rank, self.world = comm.rank, comm.size
+        self.recv_off, self.slot_bytes = off[3], off[4]
+        self.flag_off, self.seq_off, self.max_units = off[5], off[7], off[9]
+
+    def push_epilogue(self, epi, ldo: int):
+        """Fills the JX_EPI_PUSH_F32 fields of a jx_epilogue (rows of `ldo` floats in the slot)."""
+        N = self._N
+        epi.kind = N.JX_EPI_PUSH_F32
+        epi.ldo = ldo
+        epi.peer_bases = self.bases_dev
+        epi.peer_recv_off = self.recv_off
+        epi.peer_slot_bytes = self.slot_bytes
+        epi.peer_flag_off = self.flag_off
+        epi.peer_seq_off = self.seq_off
+        epi.peer_rank, epi.peer_world = self.rank, self.world
+
+    def push_norm(self, args, d: int, lda: int):
+        """Fills the push-mode fields of a jx_norm_args (the sum of the last push replaces `a`)."""
+        args.a = None
+        args.a_f32 = 0
+        args.lda = lda
+        args.peer_recv = self.local + self.recv_off
+        args.peer_stride = self.slot_bytes // 4
+        args.peer_flags = self.local + self.flag_off
+        args.peer_seq = self.local + self.seq_off
+        args.peer_world = self.world
+        args.peer_units = d // 64
 
     def all_reduce(self, which: int, n: int, out: torch.Tensor, status: Optional[torch.Tensor] = None):
         st = None if status is None else status.data_ptr()
@@ -152,15 +191,18 @@ class TPComm:
     def all_reduce(self, t: torch.Tensor):
         self.dist.all_reduce(t, group=self.group)
 
-    def align(self, status: Optional[torch.Tensor] = None):
+    def align(self, status: Optional[torch.Tensor] = None) -> bool:
         """Ends a pass (one decode step, one prefill) on partials buffer 0 by adding a 4-float all-reduce
         when the pass made an odd number of peer all-reduces.  A captured pass then always starts on
         buffer 0, so back-to-back replays keep alternating and no rank rewrites a buffer a peer may still
-        be reading.  Every rank makes the same calls."""
+        be reading.  Every rank makes the same calls.  True when it launched that all-reduce.  (Push-mode
+        projections need no alignment: their set follows the device-side epoch.)"""
         if self.peer is not None and self._which == 1:
             if getattr(self, "_align_out", None) is None:
                 self._align_out = torch.empty(4, dtype=torch.float32, device=self.peer.data[0].device)
             self.all_reduce_partial(self.partial_buffer(4), self._align_out, status)
+            return True
+        return False
 
     def close(self):
         """Releases the peer region (every rank, no kernels in flight)."""

@@ -320,6 +320,7 @@ class DecoderRuntime:
         self.graph = None
         self._launches = 0
         self.launches_last_step = 0
+        self._push_pending = False
 
     # -- buffers ------------------------------------------------------------------------------------
     def _alloc_acts(self, M: int, Mp: int) -> dict:
@@ -383,6 +384,10 @@ class DecoderRuntime:
             args.out2 = ptr(oa[out2_key])
             args.ldo2 = W.d
             args.out2_rp = oa["Mp"] if W.bf16 else 0
+        if self._push_pending and a is not None and a.data_ptr() == acts["tmp"].data_ptr():
+            # `a` is the sum of the partials the last projection pushed into the receive slots
+            self.comm.peer.push_norm(args, W.d, W.d)
+            self._push_pending = False
         args.status = ptr(self.status)
         self._launches += 1
         N.check(N.load().jx_norm(args, W.jdt, 1, self.stream_ptr()), "jx_norm")
@@ -409,6 +414,9 @@ class DecoderRuntime:
         e.res, e.ldr, e.res2, e.ldr2 = ptr(res), ldr, ptr(res2), ldr2
         if pf is not None and W.bf16 and acts["Mp"] <= 64:
             e.pf_w, e.pf_np, e.pf_kp, e.pf_iters = ptr(pf[0]), pf[1], pf[2], pf[3]
+        if kind == N.JX_EPI_PUSH_F32:
+            self.comm.peer.push_epilogue(e, ldo)
+            self._push_pending = True
         lib = N.load()
         self._launches += 1
         if not W.bf16:
@@ -425,6 +433,17 @@ class DecoderRuntime:
                                        self.stream_ptr())
             N.check(rc, "jx_linear_prefill")
 
+    # Tensor-parallel decode of the sequential-residual families: each row-parallel projection pushes its
+    # float32 partial into every rank's receive slot (JX_EPI_PUSH_F32) and the norm that follows sums
+    # them, with no all-reduce kernel in between.  Off: the pull all-reduce (jx_allreduce_f32).
+    peer_push = True
+
+    def _push_ok(self, acts) -> bool:
+        W = self.w
+        return (self.peer_push and self.comm is not None and self.comm.peer is not None and W.bf16
+                and acts["Mp"] <= 64 and W.d % 256 == 0 and W.d <= 8192
+                and acts["Mp"] * W.d <= self.comm.PEER_MAX_FLOATS)
+
     def _tp_dst(self, acts) -> torch.Tensor:
         """Where a row-parallel projection writes its float32 partial sum: the peer partials buffer of the
         next all-reduce for decode-sized activations, else acts["tmp"] (all-reduced in place by NCCL)."""
@@ -438,6 +457,7 @@ class DecoderRuntime:
         if src.data_ptr() == acts["tmp"].data_ptr():
             self.comm.all_reduce(src[:rows])
         else:
+            self._launches += 1
             self.comm.all_reduce_partial(src[:rows].reshape(-1), acts["tmp"][:rows].reshape(-1), self.status)
 
     # -- one pass over the stack -----------------------------------------------------------------------
@@ -457,8 +477,8 @@ class DecoderRuntime:
             else:
                 self._generic_attention(acts, li, lw, S, decode)
             self._o_and_mlp(acts, lw, nx)
-        if self.comm is not None:
-            self.comm.align(self.status)
+        if self.comm is not None and self.comm.align(self.status):
+            self._launches += 1
 
     def _qkv_rope_append(self, acts, li, lw, S, decode):
         W, cfg = self.w, self.w.cfg
@@ -532,7 +552,11 @@ class DecoderRuntime:
         pf_gu = self._pf(lw.wgu, W.Np_gu, W.Kp_d)
         pf_d = self._pf(lw.wd, W.Np_d, W.Kp_f)
         pf_next = self._pf(nx.wqkv, W.Np_qkv, W.Kp_d) if nx is not None else self._pf(W.lm_head, W.Np_v, W.Kp_d)
-        if fam == "gemma3" or parallel or tp:
+        push = tp and not parallel and self._push_ok(acts)
+        if push:
+            self._linear(acts, lw.wo, W.Np_d, W.Kp_o, "attn", N.JX_EPI_PUSH_F32, N_valid=d, bias=lw.bo,
+                         ldo=d, K_logical=W.Hq * hd, N_cols=d)
+        elif fam == "gemma3" or parallel or tp:
             # o_proj result kept apart: Gemma normalises it, NeoX's parallel residual adds it with the
             # MLP output, and under tensor parallelism it is a partial sum to all-reduce first.
             dst = self._tp_dst(acts) if tp else acts["tmp"]
@@ -573,6 +597,9 @@ class DecoderRuntime:
             # attn_partial + mlp_partial accumulate in dst, all-reduced once into tmp; h += tmp in the next norm.
             self._linear(acts, lw.wd, W.Np_d, W.Kp_f, "act", N.JX_EPI_ACC_F32, out=dst, ldo=d, **down_kw)
             self._allreduce(dst, M, acts)
+        elif push:
+            self._linear(acts, lw.wd, W.Np_d, W.Kp_f, "act", N.JX_EPI_PUSH_F32, ldo=d,
+                         **dict(down_kw, pf=None))
         elif fam == "gemma3" or tp:
             dst = self._tp_dst(acts) if tp else acts["tmp"]
             self._linear(acts, lw.wd, W.Np_d, W.Kp_f, "act", store, out=dst, ldo=d, **down_kw)

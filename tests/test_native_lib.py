@@ -15,11 +15,45 @@ def test_library_exports_every_header_symbol():
 
 def test_struct_layouts_match_the_header():
     # sizes compiled from include/jxb200.h with the host compiler (x86-64 LP64)
-    assert ctypes.sizeof(N.JxEpilogue) == 112
-    assert ctypes.sizeof(N.JxNormArgs) == 192
+    assert ctypes.sizeof(N.JxEpilogue) == 160
+    assert ctypes.sizeof(N.JxNormArgs) == 232
     assert ctypes.sizeof(N.JxQkvArgs) == 128
     assert ctypes.sizeof(N.JxAttnArgs) == 104
     assert ctypes.sizeof(N.JxSampleArgs) == 168
+
+
+def test_struct_field_offsets_match_the_c_compiler(tmp_path):
+    """Every ctypes field sits at the offset the C compiler gives the header's field of the same name."""
+    import os
+    import shutil
+    import subprocess
+
+    import pytest
+
+    if shutil.which("gcc") is None:
+        pytest.skip("no C compiler")
+    pairs = [(N.JxEpilogue, "jx_epilogue"), (N.JxNormArgs, "jx_norm_args"), (N.JxQkvArgs, "jx_qkv_args"),
+             (N.JxAttnArgs, "jx_attn_args"), (N.JxDAttnArgs, "jx_dattn_args"), (N.JxPAttnArgs, "jx_pattn_args"),
+             (N.JxSampleArgs, "jx_sample_args")]
+    inc = os.path.join(os.path.dirname(N.__file__), os.pardir, "include")
+    lines = ["#include <stdio.h>", "#include <stddef.h>", '#include "jxb200.h"', "int main(void) {"]
+    for cls, cname in pairs:
+        lines.append(f'  printf("{cname} sizeof %zu\\n", sizeof({cname}));')
+        for f, _ in cls._fields_:
+            lines.append(f'  printf("{cname} {f} %zu\\n", offsetof({cname}, {f}));')
+    lines += ["  return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines) + "\n")
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-I", inc, str(src), "-o", str(exe)], check=True)
+    got = {}
+    for ln in subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.splitlines():
+        c, f, v = ln.split()
+        got[(c, f)] = int(v)
+    for cls, cname in pairs:
+        assert got[(cname, "sizeof")] == ctypes.sizeof(cls), cname
+        for f, _ in cls._fields_:
+            assert got[(cname, f)] == getattr(cls, f).offset, (cname, f)
 
 
 def test_argument_errors_are_reported_without_a_gpu():
