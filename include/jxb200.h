@@ -283,7 +283,10 @@ int jx_qkv_rope_append(const jx_qkv_args* args, int dtype, int pdl, void* stream
 int jx_attention(const jx_attn_args* args, int dtype, int pdl, void* stream);
 
 /* Attention.mha decode branch (nn/attention.py:321-400) for bf16 caches on tensor cores: split over
- * the valid keys, TMA-staged K/V tiles, exact reference rounding (see csrc/attention_decode.cu). */
+ * the valid keys, TMA-staged K/V tiles, exact reference rounding (see csrc/attention_decode.cu).
+ * With pdl = 1 the kernel loads the keys of earlier positions before waiting on the kernel launched
+ * just before it on the stream, so that kernel must release its dependents only after its own wait
+ * (jx_qkv_rope_append does); otherwise pass pdl = 0. */
 int jx_decode_attention_workspace(int B, int Hq, int hd, int T, int window, long long* bytes_out);
 int jx_decode_attention(const jx_dattn_args* args, int pdl, void* stream);
 /* Form behind jx_decode_attention: 0 = by shape (default: the two-kernel split form), 1 = the split

@@ -70,26 +70,34 @@ __global__ void __launch_bounds__(128) dattn_scores_kernel(const __grid_constant
 
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  pdl_trigger();
-  pdl_wait();
+  // The kernel before this one (RoPE + cache append) releases it only after its own wait, so the
+  // positions and the keys of earlier steps are complete here: tiles that end before this step's key
+  // (position valid - 1) are loaded before waiting; the rest, and q, after.
   int lo, valid;
   key_range(p, b, lo, valid);
   const int t0 = lo + split * kDaKeys;
   if (t0 >= valid) return;
   const int t1 = min(t0 + kDaKeys, valid);
   const int n_tiles = (t1 - t0 + kDaTile - 1) / kDaTile;
+  auto issue = [&](int i) {
+    mbar_arrive_expect_tx(&bar[i], TILE_BYTES);
+    const int y = (int)(p.layer_row0 + (long long)b * p.T + t0 + i * kDaTile);
+#pragma unroll
+    for (int c = 0; c < NB; ++c) tma_load_2d(ktile + i * TILE_BYTES + c * 8192, &kmap, kvh * HD + c * 64, y, &bar[i]);
+  };
+  int n_early = 0;
   if (threadIdx.x == 0) {
     prefetch_tmap(&kmap);
     mbar_init(&bar[0], 1);
     mbar_init(&bar[1], 1);
     fence_barrier_init();
-    for (int i = 0; i < n_tiles; ++i) {
-      mbar_arrive_expect_tx(&bar[i], TILE_BYTES);
-      const int y = (int)(p.layer_row0 + (long long)b * p.T + t0 + i * kDaTile);
-#pragma unroll
-      for (int c = 0; c < NB; ++c) tma_load_2d(ktile + i * TILE_BYTES + c * 8192, &kmap, kvh * HD + c * 64, y, &bar[i]);
-    }
+    while (n_early < n_tiles && t0 + (n_early + 1) * kDaTile <= valid - 1) issue(n_early++);
   }
+  pdl_wait();
+  // the pv kernel after this one loads values before its own wait: release it only now
+  pdl_trigger();
+  if (threadIdx.x == 0)
+    for (int i = n_early; i < n_tiles; ++i) issue(i);
   // Q rows of this head group (rows >= n_rep are zero) into the swizzled layout.
   for (int idx = threadIdx.x; idx < 16 * (HD / 8); idx += 128) {
     const int r = idx / (HD / 8), cg = idx % (HD / 8);
@@ -222,7 +230,8 @@ __global__ void __launch_bounds__(128) dattn_pv_kernel(const __grid_constant__ C
   const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   pdl_trigger();
-  pdl_wait();
+  // The scores kernel before this one releases it only after its own wait, so every value of the cache
+  // (this step's included) and the positions are complete: the value tiles load while it finishes.
   int lo, valid;
   key_range(p, b, lo, valid);
   const int t0 = lo + split * kDaKeys;
@@ -242,6 +251,7 @@ __global__ void __launch_bounds__(128) dattn_pv_kernel(const __grid_constant__ C
       for (int c = 0; c < NB; ++c) tma_load_2d(vtile + i * TILE_BYTES + c * 8192, &vmap, kvh * HD + c * 64, y, &bar[i]);
     }
   }
+  pdl_wait();
   // exact softmax normaliser of each row from the split statistics
   if (threadIdx.x < 16) {
     const int row = threadIdx.x;

@@ -17,8 +17,11 @@ __global__ void __launch_bounds__(256) qkv_rope_append_kernel(QkvArgs p) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float* v = buf + warp * p.hd;
   const long long m = blockIdx.x;
-  pdl_trigger();
+  // Dependents are released only after this grid's own wait: when the decode attention that follows
+  // starts, every kernel before this one has completed, so it may load the keys and values of earlier
+  // steps before its own wait.
   pdl_wait();
+  pdl_trigger();
   const int b = (int)(m / p.S), s = (int)(m % p.S);
   int pos = s;
   if (p.decode) pos = p.pos_id[b] + 1;
