@@ -158,6 +158,22 @@ typedef struct jx_attn_args {
   int* status;
 } jx_attn_args;
 
+/* Standalone rotary embedding: q [M, Hq, hd] and k [M, Hk, hd] rows at positions pos[M] (outputs may
+ * alias the inputs). */
+typedef struct jx_rope_args {
+  int M;                 /* token rows */
+  int Hq, Hk, hd, rd;    /* heads of q and of k, head dim (<= 256), rotary dim (even, <= hd) */
+  int n_pos;             /* rows of the cos / sin tables; a position outside [0, n_pos) -> JX_ERR_RANGE */
+  const void* q;
+  const void* k;
+  void* q_out;
+  void* k_out;
+  const void* cos;       /* [n_pos, rd] in the dtype of q and k */
+  const void* sin;
+  const int* pos;        /* [M] */
+  int* status;
+} jx_rope_args;
+
 /* Decode attention on tensor cores: one query token per batch row, head_dim 64/128/256, n_rep <= 16. */
 typedef struct jx_dattn_args {
   int B, Hq, Hkv, hd;
@@ -278,6 +294,9 @@ int jx_linear_f32(const float* X, long long ldx, const float* W, int M, int N, i
 
 /* QK-norm + RoPE (nn/position.py:78-141) + KV-cache append (cache.py:183-243). */
 int jx_qkv_rope_append(const jx_qkv_args* args, int dtype, int pdl, void* stream);
+
+/* RotaryEmbedding.apply_rotary_pos_emb (nn/position.py:78-141) for any positions. */
+int jx_rope_apply(const jx_rope_args* args, int dtype, int pdl, void* stream);
 
 /* Attention.mha (nn/attention.py:321-400) on the cache, any head size (CUDA cores). */
 int jx_attention(const jx_attn_args* args, int dtype, int pdl, void* stream);

@@ -2,9 +2,10 @@
 
 Public names mirror ``jaxml/__init__.py`` of the reference: ``Engine``, ``InferenceConfig``,
 ``ModelConfig``, ``SamplingMethod``, ``GenerationConfig``, ``TextGenerationPipeline``, ``KVCache`` (plus
-the model classes).  The kernels live in ``libjxb200.so``
+the model classes), and ``jaxml_b200.nn`` mirrors ``jaxml.nn``.  The kernels live in ``libjxb200.so``
 (``jaxml_b200/csrc``, C ABI in ``include/jxb200.h``).
 """
+from . import nn
 from .cache import KVCache
 from .config import ModelConfig
 from .engine import Engine, InferenceConfig

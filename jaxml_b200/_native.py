@@ -58,6 +58,11 @@ class JxAttnArgs(ctypes.Structure):
                 ("ldo", LL), ("out_rp", LL), ("status", P)]
 
 
+class JxRopeArgs(ctypes.Structure):
+    _fields_ = [("M", I), ("Hq", I), ("Hk", I), ("hd", I), ("rd", I), ("n_pos", I), ("q", P), ("k", P), ("q_out", P),
+                ("k_out", P), ("cos", P), ("sin", P), ("pos", P), ("status", P)]
+
+
 class JxDAttnArgs(ctypes.Structure):
     _fields_ = [("B", I), ("Hq", I), ("Hkv", I), ("hd", I), ("T", I), ("window", I), ("cache_rows", LL),
                 ("layer_row0", LL), ("q", P), ("k_base", P), ("v_base", P), ("len_ptr", P), ("len_add", I),
@@ -95,6 +100,7 @@ _PROTOS = {
     "jx_linear_prefill": (I, [P, P, LL, LL, LL, ctypes.POINTER(JxEpilogue), P, I, P]),
     "jx_linear_f32": (I, [P, LL, P, I, I, I, ctypes.POINTER(JxEpilogue), I, P]),
     "jx_qkv_rope_append": (I, [ctypes.POINTER(JxQkvArgs), I, I, P]),
+    "jx_rope_apply": (I, [ctypes.POINTER(JxRopeArgs), I, I, P]),
     "jx_attention": (I, [ctypes.POINTER(JxAttnArgs), I, I, P]),
     "jx_decode_attention_workspace": (I, [I, I, I, I, I, ctypes.POINTER(LL)]),
     "jx_decode_attention": (I, [ctypes.POINTER(JxDAttnArgs), I, P]),

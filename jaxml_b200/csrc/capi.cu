@@ -15,6 +15,7 @@ int run_gemm_f32(const float* X, long long ldx, const float* W, int M, int N, in
                  cudaStream_t stream);
 int run_qkv_rope_append(int dtype, const jx_qkv_args& p, bool pdl, cudaStream_t stream);
 int run_attention_generic(int dtype, const jx_attn_args& p, bool pdl, cudaStream_t stream);
+int run_rope_apply(int dtype, const jx_rope_args& p, bool pdl, cudaStream_t stream);
 int run_sample(const jx_sample_args& p, bool pdl, cudaStream_t stream);
 int run_decode_attention(const jx_dattn_args& a, bool pdl, cudaStream_t stream);
 void set_gemv_impl(int impl);
@@ -191,6 +192,16 @@ int jx_qkv_rope_append(const jx_qkv_args* args, int dtype, int pdl, void* stream
   const int rc = run_qkv_rope_append(dtype, *args, pdl != 0, (cudaStream_t)stream);
   if (rc == JX_ERR_CUDA) return note_cuda("jx_qkv_rope_append");
   if (rc != JX_OK) return fail(rc, "jx_qkv_rope_append: unsupported head size / rotary dim / dtype");
+  return JX_OK;
+}
+
+int jx_rope_apply(const jx_rope_args* args, int dtype, int pdl, void* stream) {
+  if (!args || !args->cos || !args->sin || !args->pos || (args->Hq > 0 && (!args->q || !args->q_out)) ||
+      (args->Hk > 0 && (!args->k || !args->k_out)))
+    return fail(JX_ERR_ARG, "jx_rope_apply: null pointer");
+  const int rc = run_rope_apply(dtype, *args, pdl != 0, (cudaStream_t)stream);
+  if (rc == JX_ERR_CUDA) return note_cuda("jx_rope_apply");
+  if (rc != JX_OK) return fail(rc, "jx_rope_apply: unsupported head size / rotary dim / dtype");
   return JX_OK;
 }
 

@@ -100,4 +100,73 @@ int run_qkv_rope_append(int dtype, const QkvArgs& p, bool pdl, cudaStream_t stre
   return err == cudaSuccess ? JX_OK : JX_ERR_CUDA;
 }
 
+// ------------------------------------------------------------------------------------------------
+// Standalone rotary embedding (RotaryEmbedding.apply_rotary_pos_emb, nn/position.py:78-141): q and k
+// rows at arbitrary positions, cos / sin tables in the same dtype, the first rd dims rotated with
+// rotate_half in the model dtype (q*cos and rotate_half(q)*sin each rounded, then their sum), the rest
+// passed through.  One warp per head, grid (rows, ceil((Hq + Hk) / 8)).
+// ------------------------------------------------------------------------------------------------
+template <typename T>
+__global__ void __launch_bounds__(256) rope_apply_kernel(jx_rope_args p) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long m = blockIdx.x;
+  pdl_trigger();
+  pdl_wait();
+  const int pos = p.pos[m];
+  const bool bad = pos < 0 || pos >= p.n_pos;
+  if (bad && threadIdx.x == 0) set_status(p.status, JX_ERR_RANGE);
+  const int half = p.rd >> 1;
+  for (int head = blockIdx.y * 8 + warp; head < p.Hq + p.Hk; head += 8 * gridDim.y) {
+    const bool is_q = head < p.Hq;
+    const T* src = reinterpret_cast<const T*>(is_q ? p.q : p.k) +
+                   (m * (is_q ? p.Hq : p.Hk) + (is_q ? head : head - p.Hq)) * (long long)p.hd;
+    T* dst = reinterpret_cast<T*>(is_q ? p.q_out : p.k_out) +
+             (m * (is_q ? p.Hq : p.Hk) + (is_q ? head : head - p.Hq)) * (long long)p.hd;
+    const T* cos = reinterpret_cast<const T*>(p.cos) + (long long)(bad ? 0 : pos) * p.rd;
+    const T* sin = reinterpret_cast<const T*>(p.sin) + (long long)(bad ? 0 : pos) * p.rd;
+    // every lane reads its inputs before any lane writes (dst may alias src)
+    float o[8];
+    int cnt = 0;
+    for (int j = lane; j < p.hd; j += 32, ++cnt) {
+      const float x = to_f(src[j]);
+      if (bad) {
+        o[cnt] = 0.f;
+      } else if (j < p.rd) {
+        const float rot = j < half ? -to_f(src[j + half]) : to_f(src[j - half]);
+        // separate roundings of both products (no fused multiply-add), as two dtype multiplies then an add
+        o[cnt] = rnd<T>(__fadd_rn(rnd<T>(__fmul_rn(x, to_f(cos[j]))), rnd<T>(__fmul_rn(rot, to_f(sin[j])))));
+      } else {
+        o[cnt] = x;
+      }
+    }
+    __syncwarp();
+    cnt = 0;
+    for (int j = lane; j < p.hd; j += 32, ++cnt) dst[j] = from_f<T>(o[cnt]);
+    __syncwarp();
+  }
+}
+
+int run_rope_apply(int dtype, const jx_rope_args& p, bool pdl, cudaStream_t stream) {
+  if (p.M <= 0 || p.Hq < 0 || p.Hk < 0 || p.Hq + p.Hk <= 0 || p.hd <= 0 || p.hd > 256 || p.rd <= 0 ||
+      p.rd > p.hd || (p.rd & 1) || p.n_pos <= 0 || p.M > 2147483647)
+    return JX_ERR_SHAPE;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.M, (p.Hq + p.Hk + 7) / 8);
+  cfg.blockDim = dim3(256);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  cudaError_t err;
+  if (dtype == JX_BF16)
+    err = launch_ex(&cfg, rope_apply_kernel<bf16>, p);
+  else if (dtype == JX_F32)
+    err = launch_ex(&cfg, rope_apply_kernel<float>, p);
+  else
+    return JX_ERR_DTYPE;
+  return err == cudaSuccess ? JX_OK : JX_ERR_CUDA;
+}
+
 }  // namespace jxb

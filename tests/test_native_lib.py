@@ -34,7 +34,7 @@ def test_struct_field_offsets_match_the_c_compiler(tmp_path):
         pytest.skip("no C compiler")
     pairs = [(N.JxEpilogue, "jx_epilogue"), (N.JxNormArgs, "jx_norm_args"), (N.JxQkvArgs, "jx_qkv_args"),
              (N.JxAttnArgs, "jx_attn_args"), (N.JxDAttnArgs, "jx_dattn_args"), (N.JxPAttnArgs, "jx_pattn_args"),
-             (N.JxSampleArgs, "jx_sample_args")]
+             (N.JxSampleArgs, "jx_sample_args"), (N.JxRopeArgs, "jx_rope_args")]
     inc = os.path.join(os.path.dirname(N.__file__), os.pardir, "include")
     lines = ["#include <stdio.h>", "#include <stddef.h>", '#include "jxb200.h"', "int main(void) {"]
     for cls, cname in pairs:
