@@ -63,7 +63,7 @@ def parse():
     ap.add_argument("--ctx", type=int, default=4096, help="context length of --micro attn")
     ap.add_argument("--shape", default="28672,4096", help="N,K of --micro gemv (default: fused gate/up)")
     ap.add_argument("--gemv-impl", type=int, default=0, help="--micro gemv kernel: 0 by shape, 1 mma.sync, 2 tcgen05")
-    ap.add_argument("--attn-impl", type=int, default=0, help="--micro attn form: 0 by shape, 1 split, 2 cluster")
+    ap.add_argument("--attn-impl", type=int, default=0, help="--micro attn form: 0 by shape, 1 split, 2 cluster, 3 column pv")
     ap.add_argument("--tokens", type=int, default=8192, help="token rows of --micro gemm (prefill B x P)")
     ap.add_argument("--gemm-impl", type=int, default=0, help="--micro gemm kernel: 0 by shape, 1 mma.sync, 2 tcgen05")
     return ap.parse_args()
@@ -652,7 +652,7 @@ def micro(args):
             N.call("jx_decode_attention", a, 1, st)
         ms = _graph_ms(lambda st: [run(l, st) for l in range(L)], L)
         nbytes = B * ctx * 2 * Hkv * hd * 2
-        line = {"micro": "attn", "impl": ["by-shape", "split", "cluster"][args.attn_impl], "shape": f"B={B} ctx={ctx} Hq={Hq} Hkv={Hkv} hd={hd}", "us": ms * 1e3,
+        line = {"micro": "attn", "impl": ["by-shape", "split", "cluster", "column"][args.attn_impl], "shape": f"B={B} ctx={ctx} Hq={Hq} Hkv={Hkv} hd={hd}", "us": ms * 1e3,
                 "gbs": nbytes / ms / 1e6}
     print(json.dumps(line), flush=True)
 

@@ -308,9 +308,10 @@ int jx_attention(const jx_attn_args* args, int dtype, int pdl, void* stream);
  * (jx_qkv_rope_append does); otherwise pass pdl = 0. */
 int jx_decode_attention_workspace(int B, int Hq, int hd, int T, int window, long long* bytes_out);
 int jx_decode_attention(const jx_dattn_args* args, int pdl, void* stream);
-/* Form behind jx_decode_attention: 0 = by shape (default: the two-kernel split form), 1 = the split
- * form, 2 = the single-pass thread-block-cluster form (key range (T, or the window) up to 8 CTAs x
- * 2048 keys; JX_ERR_SHAPE otherwise). */
+/* Form behind jx_decode_attention: 0 = by shape (default: the two-kernel split form), 1 = split scores
+ * + split pv,
+ * 2 = the single-pass thread-block-cluster form (key range (T, or the window) up to 8 CTAs x 2048 keys;
+ * JX_ERR_SHAPE otherwise), 3 = split scores + column pv. */
 int jx_set_decode_attention_impl(int impl);
 
 /* Attention.mha prefill branch (causal + window + padding masks, nn/attention.py:321-400) for bf16

@@ -339,6 +339,129 @@ __global__ void __launch_bounds__(128) dattn_pv_kernel(const __grid_constant__ C
 }
 
 // ------------------------------------------------------------------------------------------------
+// Column form of the pv step: one CTA per (64-column block of the head, KV head, batch row) runs over
+// all valid keys, so no split partials and no cross-CTA reduction are needed.  The value tiles
+// [64 keys x 64 columns] stream through a ring of kPcStages stages; warp w consumes tiles w, w+4, ...
+// and refills the stages it owns (kPcStages % 4 == 0) as it frees them.  The first kPcStages tiles are
+// issued before the wait on the scores kernel (which releases dependents after its own wait, so the
+// values are complete).  Each warp forms the exact bf16 probabilities of its tile from the scores and
+// the split statistics, accumulates P.V on mma.sync, and the four warp partials are added in warp order
+// (deterministic), rounded once to bf16 (K128 layout).
+// ------------------------------------------------------------------------------------------------
+constexpr int kPcStages = 8;
+constexpr int kPcLd = 64 + 8;   // padded row stride (bf16) of a warp's probability tile
+
+template <int HD>
+__global__ void __launch_bounds__(128) dattn_pvcol_kernel(const __grid_constant__ CUtensorMap vmap, DAttnParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* vring = smem;                                             // kPcStages x [64 x 64] bf16, 128B swizzle
+  bf16* ptiles = reinterpret_cast<bf16*>(smem + kPcStages * 8192);   // [4 warps][16][kPcLd]
+  uint64_t* full = reinterpret_cast<uint64_t*>(ptiles + 4 * 16 * kPcLd);
+  __shared__ float Ms[16], Ls[16];
+
+  const int cb = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_trigger();
+  int lo, valid;
+  key_range(p, b, lo, valid);
+  const int n_tiles = valid > lo ? (valid - lo + 63) / 64 : 0;
+  auto issue = [&](int i) {
+    const int st = i % kPcStages;
+    mbar_arrive_expect_tx(&full[st], 8192);
+    tma_load_2d(vring + st * 8192, &vmap, kvh * HD + cb * 64, (int)(p.layer_row0 + (long long)b * p.T + lo + i * 64),
+                &full[st]);
+  };
+  if (threadIdx.x == 0) {
+    prefetch_tmap(&vmap);
+    for (int st = 0; st < kPcStages; ++st) mbar_init(&full[st], 1);
+    fence_barrier_init();
+    for (int i = 0; i < n_tiles && i < kPcStages; ++i) issue(i);
+  }
+  __syncthreads();
+  pdl_wait();
+  // exact softmax normaliser of each row from the split statistics
+  if (threadIdx.x < 16) {
+    const int row = threadIdx.x;
+    float M = -INFINITY, L = 0.f;
+    if (row < p.n_rep) {
+      const int n_active = (valid - lo + kDaKeys - 1) / kDaKeys;
+      const float* st = p.stats + ((long long)b * p.Hq + kvh * p.n_rep + row) * p.n_splits * 2;
+      for (int s2 = 0; s2 < n_active; ++s2) M = fmaxf(M, st[s2 * 2]);
+      for (int s2 = 0; s2 < n_active; ++s2) L += st[s2 * 2 + 1] * expf(st[s2 * 2] - M);
+    }
+    Ms[row] = M;
+    Ls[row] = L;
+  }
+  __syncthreads();
+
+  const int mi = lane >> 3, r8 = lane & 7;
+  bf16* pt = ptiles + warp * 16 * kPcLd;
+  const float* sc = p.sc + ((long long)b * p.Hq + kvh * p.n_rep) * p.T;
+  float acc[8][4] = {};
+  bool ok = true;
+  for (int i = warp; i < n_tiles; i += 4) {
+    const int st = i % kPcStages;
+    const int t0 = lo + i * 64;
+    // probabilities of this tile's keys (rows >= n_rep and keys past the range are zero)
+    for (int idx = lane; idx < 16 * 64; idx += 32) {
+      const int row = idx >> 6, k = idx & 63, t = t0 + k;
+      float pv = 0.f;
+      if (row < p.n_rep && t < valid) pv = rnd<bf16>(expf(__ldcg(sc + (long long)row * p.T + t) - Ms[row]) / Ls[row]);
+      pt[row * kPcLd + k] = __float2bfloat16_rn(pv);
+    }
+    __syncwarp();
+    if (!mbar_wait_bounded(&full[st], (i / kPcStages) & 1)) {
+      // this warp's only other copy in flight is tile i + 4: let it land (bounded) before leaving
+      if (lane == 0) set_status(p.status, JX_ERR_TIMEOUT);
+      if (i + 4 < n_tiles) mbar_wait_bounded(&full[(i + 4) % kPcStages], ((i + 4) / kPcStages) & 1);
+      ok = false;
+      break;
+    }
+    {
+      const uint32_t vb = smem_u32(vring + st * 8192);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4(smem_u32(pt + ((mi & 1) * 8 + r8) * kPcLd + kk * 16 + (mi >> 1) * 8), a0, a1, a2, a3);
+#pragma unroll
+        for (int n16 = 0; n16 < 4; ++n16) {
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4_t(swz(vb, kk * 16 + (mi & 1) * 8 + r8, n16 * 2 + (mi >> 1)), b0, b1, b2, b3);
+          mma_bf16(acc[n16 * 2], a0, a1, a2, a3, b0, b1);
+          mma_bf16(acc[n16 * 2 + 1], a0, a1, a2, a3, b2, b3);
+        }
+      }
+    }
+    __syncwarp();
+    // refill the stage just freed with this warp's tile i + kPcStages
+    if (lane == 0 && i + kPcStages < n_tiles) {
+      fence_proxy_async();
+      issue(i + kPcStages);
+    }
+  }
+  if (!__syncthreads_and(ok)) return;
+  // warp partials into the (now idle) ring, then summed in warp order
+  float* red = reinterpret_cast<float*>(vring);   // [4 warps][16][64]
+  {
+    const int r_lo = lane >> 2;
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        red[(warp * 16 + r_lo + (e >> 1) * 8) * 64 + nt * 8 + (lane & 3) * 2 + (e & 1)] = acc[nt][e];
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < p.n_rep * 64; idx += 128) {
+    const int row = idx >> 6, col = idx & 63;
+    const float sum = ((red[row * 64 + col] + red[(16 + row) * 64 + col]) + red[(32 + row) * 64 + col]) +
+                      red[(48 + row) * 64 + col];
+    const long long ocol = (long long)(kvh * p.n_rep + row) * HD + cb * 64 + col;
+    p.out[k128_offset(b, ocol, p.out_rp)] = __float2bfloat16_rn(sum);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
 // Single-pass form: a thread-block cluster of CS CTAs per (batch row, KV head) (CS = 1 when there are
 // at least as many head groups as SMs), the CTAs splitting the valid keys into contiguous runs of tiles.
 // Inside a CTA the 4 warps are independent pipelines: warp w owns tiles w, w+4, ... of the CTA's run,
@@ -705,13 +828,16 @@ int dattn_n_splits(int T, int window) {
 }
 
 template <int HD>
-static int launch_dattn(const CUtensorMap& km, const CUtensorMap& vm, const DAttnParams& p, bool pdl, cudaStream_t s) {
+static int launch_dattn(const CUtensorMap& km, const CUtensorMap& vm, const DAttnParams& p, bool column_pv, bool pdl,
+                        cudaStream_t s) {
   const int smem_a = 1024 + 2 * kDaTile * HD * 2 + (HD / 64) * 2048 + 16 + 4 * 16 * 4;
   const int smem_b = 1024 + 2 * kDaTile * HD * 2 + 16 + 32 * 4 + 16 * kPLd * 2;
+  const int smem_c = 1024 + kPcStages * 8192 + 4 * 16 * kPcLd * 2 + kPcStages * 8;
   static bool configured = false;
   if (!configured) {
     if (cudaFuncSetAttribute(dattn_scores_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_a) != cudaSuccess ||
-        cudaFuncSetAttribute(dattn_pv_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_b) != cudaSuccess)
+        cudaFuncSetAttribute(dattn_pv_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_b) != cudaSuccess ||
+        cudaFuncSetAttribute(dattn_pvcol_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_c) != cudaSuccess)
       return JX_ERR_CUDA;
     configured = true;
   }
@@ -726,6 +852,11 @@ static int launch_dattn(const CUtensorMap& km, const CUtensorMap& vm, const DAtt
   cfg.numAttrs = pdl ? 1 : 0;
   cfg.dynamicSmemBytes = smem_a;
   if (launch_ex(&cfg, dattn_scores_kernel<HD>, km, p) != cudaSuccess) return JX_ERR_CUDA;
+  if (column_pv) {
+    cfg.gridDim = dim3(HD / 64, p.Hkv, p.B);
+    cfg.dynamicSmemBytes = smem_c;
+    return launch_ex(&cfg, dattn_pvcol_kernel<HD>, vm, p) == cudaSuccess ? JX_OK : JX_ERR_CUDA;
+  }
   cfg.dynamicSmemBytes = smem_b;
   if (launch_ex(&cfg, dattn_pv_kernel<HD>, vm, p) != cudaSuccess) return JX_ERR_CUDA;
   return JX_OK;
@@ -783,9 +914,11 @@ static int launch_dattn_fused(const jx_dattn_args& a, FAttnParams& p, int sms, b
   return launch_ex(&cfg, dattn_warp_kernel<HD>, km, vm, p) == cudaSuccess ? JX_OK : JX_ERR_CUDA;
 }
 
-// 0: by shape (the split form: on the Llama-8B decode shapes the single-pass form measured 22.7 us against
-// 20.4 us at context 640, its fewer warps leaving the mma.sync latency exposed), 1: split form,
-// 2: single-pass form.
+// 0: by shape (the split form), 1: split form (split pv), 2: single-pass form, 3: split scores + column
+// pv.  Neither alternative is chosen by shape: on the Llama-8B decode shape (B=16) the single-pass form
+// measured 22.7 us against 20.4 us for the split form at context 640 (its fewer warps leave the mma.sync
+// latency exposed), and the column pv 22.4 / 122.7 us against 17.6 / 87.4 us at context 640 / 4096 (each
+// warp forms the probabilities of its tiles serially, one L2 round trip per tile).
 static int g_dattn_impl = 0;
 void set_dattn_impl(int impl) { g_dattn_impl = impl; }
 
@@ -855,10 +988,11 @@ int run_decode_attention(const jx_dattn_args& a, bool pdl, cudaStream_t stream) 
   p.opart = p.stats + (long long)a.B * a.Hq * n_splits * 2;
   p.counters = a.counters;
   p.status = a.status;
+  const bool column_pv = g_dattn_impl == 3;
   switch (a.hd) {
-    case 64: return launch_dattn<64>(km, vm, p, pdl, stream);
-    case 128: return launch_dattn<128>(km, vm, p, pdl, stream);
-    default: return launch_dattn<256>(km, vm, p, pdl, stream);
+    case 64: return launch_dattn<64>(km, vm, p, column_pv, pdl, stream);
+    case 128: return launch_dattn<128>(km, vm, p, column_pv, pdl, stream);
+    default: return launch_dattn<256>(km, vm, p, column_pv, pdl, stream);
   }
 }
 

@@ -94,7 +94,7 @@ def test_linear_decode_glu_resid_bias(impl, M):
     assert (h.double() - ref2).abs().max().item() <= 0.05 * ref2.abs().max().item()
 
 
-@pytest.fixture(params=[2, 1], ids=["cluster", "split"])
+@pytest.fixture(params=[2, 1, 3], ids=["cluster", "split", "column"])
 def attn_form(request):
     N = _n()
     N.call("jx_set_decode_attention_impl", request.param)
@@ -106,8 +106,8 @@ def attn_form(request):
                                                  (64, 8, 8, 0, 3), (128, 16, 1, 0, 3), (128, 64, 8, 0, 3),
                                                  (128, 32, 8, 0, 20)])
 def test_decode_attention_matches_oracle(attn_form, hd, Hq, Hkv, window, B):
-    """Tensor-core decode attention (single-pass cluster form and two-kernel split form) vs the oracle's
-    Attention.mha on a padded cache.
+    """Tensor-core decode attention (single-pass cluster form; split scores with the split or the column
+    pv) vs the oracle's Attention.mha on a padded cache.
 
     The kernel rounds at the reference's points (scores, scale, probabilities, output), so results agree
     to about one bf16 ulp.  A q.k accumulated in a different order can round to the neighbouring bf16
