@@ -63,7 +63,7 @@ def parse():
     ap.add_argument("--ctx", type=int, default=4096, help="context length of --micro attn")
     ap.add_argument("--shape", default="28672,4096", help="N,K of --micro gemv (default: fused gate/up)")
     ap.add_argument("--gemv-impl", type=int, default=0, help="--micro gemv kernel: 0 by shape, 1 mma.sync, 2 tcgen05")
-    ap.add_argument("--attn-impl", type=int, default=0, help="--micro attn form: 0 by shape, 1 split, 2 cluster, 3 column pv")
+    ap.add_argument("--attn-impl", type=int, default=0, help="decode attention form: 0 by shape, 1 split, 2 cluster, 3 column pv, 4 cluster-split")
     ap.add_argument("--tokens", type=int, default=8192, help="token rows of --micro gemm (prefill B x P)")
     ap.add_argument("--gemm-impl", type=int, default=0, help="--micro gemm kernel: 0 by shape, 1 mma.sync, 2 tcgen05")
     return ap.parse_args()
@@ -243,6 +243,10 @@ def gpu_arm(args):
     from jaxml_b200.models import random_params
 
     tp = world
+    if args.attn_impl:
+        from jaxml_b200 import _native as N
+
+        N.call("jx_set_decode_attention_impl", args.attn_impl)
     if args.tp_pull:
         from jaxml_b200.runtime import DecoderRuntime
 
@@ -353,6 +357,7 @@ def gpu_arm(args):
             "config": {"workload": "llama3-8b-shape bf16 greedy decode, batch 16, prompt 512, 256 new tokens",
                        "global_batch": B, "seq_len": P, "parallelism": f"tp{tp}",
                        "tp_exchange": None if tp == 1 else ("pull all-reduce" if args.tp_pull else "push-fused"),
+                       "decode_attention": ["by shape", "split", "cluster", "column pv", "cluster-split"][args.attn_impl],
                        "l2": "inputs larger than L2 (15 GB of weights per step)"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                          "frac": achieved / hbm_peak, "traffic": GEMV_TC_GATEUP_TRAFFIC,
@@ -652,7 +657,7 @@ def micro(args):
             N.call("jx_decode_attention", a, 1, st)
         ms = _graph_ms(lambda st: [run(l, st) for l in range(L)], L)
         nbytes = B * ctx * 2 * Hkv * hd * 2
-        line = {"micro": "attn", "impl": ["by-shape", "split", "cluster", "column"][args.attn_impl], "shape": f"B={B} ctx={ctx} Hq={Hq} Hkv={Hkv} hd={hd}", "us": ms * 1e3,
+        line = {"micro": "attn", "impl": ["by-shape", "split", "cluster", "column", "cluster-split"][args.attn_impl], "shape": f"B={B} ctx={ctx} Hq={Hq} Hkv={Hkv} hd={hd}", "us": ms * 1e3,
                 "gbs": nbytes / ms / 1e6}
     print(json.dumps(line), flush=True)
 

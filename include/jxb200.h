@@ -311,7 +311,9 @@ int jx_decode_attention(const jx_dattn_args* args, int pdl, void* stream);
 /* Form behind jx_decode_attention: 0 = by shape (default: the two-kernel split form), 1 = split scores
  * + split pv,
  * 2 = the single-pass thread-block-cluster form (key range (T, or the window) up to 8 CTAs x 2048 keys;
- * JX_ERR_SHAPE otherwise), 3 = split scores + column pv. */
+ * JX_ERR_SHAPE otherwise), 3 = split scores + column pv, 4 = the cluster-split form (one kernel, the
+ * key splits of a head group in one thread-block cluster; up to 16 splits of 128 keys, JX_ERR_SHAPE
+ * otherwise). */
 int jx_set_decode_attention_impl(int impl);
 
 /* Attention.mha prefill branch (causal + window + padding masks, nn/attention.py:321-400) for bf16

@@ -339,6 +339,248 @@ __global__ void __launch_bounds__(128) dattn_pv_kernel(const __grid_constant__ C
 }
 
 // ------------------------------------------------------------------------------------------------
+// Cluster-split form: the split form's decomposition (one CTA per 128 keys of a (KV head, batch row))
+// in one kernel, the key splits of a head group forming one thread-block cluster (co-scheduled), so
+// the softmax statistics and the output partials are exchanged through distributed shared memory
+// instead of global memory and a second kernel.  Per CTA: K tiles (those of earlier steps before the
+// wait, as in the scores kernel), q.k on mma.sync with the scores kept in registers, this CTA's row
+// (max, sum) published in shared memory, the V tiles loaded into the freed K slots while the cluster
+// exchanges the statistics, exact bf16 probabilities from the cluster-wide (max, sum) in rank order,
+// P.V, and the partials summed over the cluster in rank order (the same sums as the split form).
+// ------------------------------------------------------------------------------------------------
+template <int HD>
+__global__ void __launch_bounds__(128) dattn_csplit_kernel(const __grid_constant__ CUtensorMap kmap,
+                                                           const __grid_constant__ CUtensorMap vmap, DAttnParams p) {
+  constexpr int NB = HD / 64;
+  constexpr int TILE_BYTES = kDaTile * HD * 2;
+  constexpr int WCOLS = HD / 4;             // output columns per warp in P.V
+  constexpr int NT = WCOLS / 8;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* ktile = smem;                                   // 2 tiles: K, then V, then the output partial
+  uint8_t* qs = smem + 2 * TILE_BYTES;                     // NB blocks of [16 x 64]
+  bf16* ptile = reinterpret_cast<bf16*>(qs + NB * 2048);   // [16][kPLd]
+  uint64_t* bar = reinterpret_cast<uint64_t*>(ptile + 16 * kPLd);   // [0,1] K tiles, [2,3] V tiles
+  float* red = reinterpret_cast<float*>(bar + 4);          // [4 warps][16 rows]
+  __shared__ float cmax[16], csum[16], Ms[16], Ls[16];
+
+  const int kvh = blockIdx.y, b = blockIdx.z;
+  const int rank = (int)cluster_ctarank(), CS = (int)gridDim.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  pdl_trigger();
+  int lo, valid;
+  key_range(p, b, lo, valid);
+  const int t0 = lo + rank * kDaKeys;
+  const int t1 = min(t0 + kDaKeys, valid);
+  const int n_tiles = t0 < valid ? (t1 - t0 + kDaTile - 1) / kDaTile : 0;
+  auto issue = [&](const CUtensorMap* map, int i, uint64_t* bb) {
+    mbar_arrive_expect_tx(bb, TILE_BYTES);
+    const int y = (int)(p.layer_row0 + (long long)b * p.T + t0 + i * kDaTile);
+#pragma unroll
+    for (int c = 0; c < NB; ++c) tma_load_2d(ktile + i * TILE_BYTES + c * 8192, map, kvh * HD + c * 64, y, bb);
+  };
+  int n_early = 0;
+  if (threadIdx.x == 0) {
+    prefetch_tmap(&kmap);
+    prefetch_tmap(&vmap);
+    for (int i = 0; i < 4; ++i) mbar_init(&bar[i], 1);
+    fence_barrier_init();
+    while (n_early < n_tiles && t0 + (n_early + 1) * kDaTile <= valid - 1) issue(&kmap, n_early, &bar[n_early]), ++n_early;
+  }
+  pdl_wait();
+  if (threadIdx.x == 0)
+    for (int i = n_early; i < n_tiles; ++i) issue(&kmap, i, &bar[i]);
+  for (int idx = threadIdx.x; idx < 16 * (HD / 8); idx += 128) {
+    const int r = idx / (HD / 8), cg = idx % (HD / 8);
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (r < p.n_rep)
+      v = *reinterpret_cast<const uint4*>(p.q + ((long long)b * p.Hq + kvh * p.n_rep + r) * HD + cg * 8);
+    const uint32_t a = swz(smem_u32(qs + (cg >> 3) * 2048), r, cg & 7);
+    asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w));
+  }
+  __syncthreads();
+
+  const int mi = lane >> 3, r8 = lane & 7;
+  const int r_lo = lane >> 2, r_hi = r_lo + 8;
+  float s[2][2][4];
+  float mrow[2] = {-INFINITY, -INFINITY};
+  bool ok = true;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) s[i][nt][e] = -INFINITY;
+    if (i >= n_tiles || !ok) continue;
+    if (!mbar_wait_bounded(&bar[i], 0)) {
+      set_status(p.status, JX_ERR_TIMEOUT);
+      ok = false;
+      continue;
+    }
+    float acc[2][4] = {};
+    const uint32_t kb = smem_u32(ktile + i * TILE_BYTES);
+#pragma unroll
+    for (int ks = 0; ks < HD / 16; ++ks) {
+      uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
+      {
+        const int row = (mi & 1) * 8 + r8, ch = ks * 2 + (mi >> 1);
+        ldsm_x4(swz(smem_u32(qs + (ch >> 3) * 2048), row, ch & 7), a0, a1, a2, a3);
+      }
+      {
+        const int row = warp * 16 + (mi >> 1) * 8 + r8, ch = ks * 2 + (mi & 1);
+        ldsm_x4(swz(kb + (ch >> 3) * 8192, row, ch & 7), b0, b1, b2, b3);
+      }
+      mma_bf16(acc[0], a0, a1, a2, a3, b0, b1);
+      mma_bf16(acc[1], a0, a1, a2, a3, b2, b3);
+    }
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int t = t0 + i * kDaTile + warp * 16 + nt * 8 + (lane & 3) * 2 + (e & 1);
+        if (t < t1) {
+          const float v = rnd<bf16>(rnd<bf16>(acc[nt][e]) * p.scale_bf16);
+          s[i][nt][e] = v;
+          mrow[e >> 1] = fmaxf(mrow[e >> 1], v);
+        }
+      }
+  }
+  ok = __syncthreads_and(ok) != 0;   // every warp is done with the K tiles
+  // the V tiles go into the freed K slots while the statistics are exchanged
+  if (threadIdx.x == 0 && ok) {
+    fence_proxy_async();
+    for (int i = 0; i < n_tiles; ++i) issue(&vmap, i, &bar[2 + i]);
+  }
+  // this CTA's row maxima and exp-sums (as the scores kernel computes them)
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    mrow[h] = fmaxf(mrow[h], __shfl_xor_sync(0xffffffffu, mrow[h], 1));
+    mrow[h] = fmaxf(mrow[h], __shfl_xor_sync(0xffffffffu, mrow[h], 2));
+  }
+  if ((lane & 3) == 0) {
+    red[warp * 16 + r_lo] = mrow[0];
+    red[warp * 16 + r_hi] = mrow[1];
+  }
+  __syncthreads();
+  float m[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int row = r_lo + h * 8;
+    m[h] = fmaxf(fmaxf(red[row], red[16 + row]), fmaxf(red[32 + row], red[48 + row]));
+  }
+  __syncthreads();
+  float l[2] = {0.f, 0.f};
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int row = r_lo + (e >> 1) * 8;
+        const int t = t0 + i * kDaTile + warp * 16 + nt * 8 + (lane & 3) * 2 + (e & 1);
+        if (t < t1 && row < p.n_rep) l[e >> 1] += expf(s[i][nt][e] - m[e >> 1]);
+      }
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    l[h] += __shfl_xor_sync(0xffffffffu, l[h], 1);
+    l[h] += __shfl_xor_sync(0xffffffffu, l[h], 2);
+  }
+  if ((lane & 3) == 0) {
+    red[warp * 16 + r_lo] = l[0];
+    red[warp * 16 + r_hi] = l[1];
+  }
+  __syncthreads();
+  if (warp == 0 && (lane & 3) == 0) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int row = r_lo + h * 8;
+      cmax[row] = m[h];
+      csum[row] = (red[row] + red[16 + row]) + (red[32 + row] + red[48 + row]);
+    }
+  }
+  cluster_sync_all();
+  // cluster-wide normaliser of each row, over the ranks in order (the split statistics of the split form)
+  if (threadIdx.x < 16) {
+    const int row = threadIdx.x;
+    float M = -INFINITY, L = 0.f;
+    if (row < p.n_rep) {
+      const uint32_t am = smem_u32(cmax + row), as = smem_u32(csum + row);
+      for (int cr = 0; cr < CS; ++cr) M = fmaxf(M, dsmem_ld_f32(dsmem_map(am, cr)));
+      for (int cr = 0; cr < CS; ++cr)
+        L += dsmem_ld_f32(dsmem_map(as, cr)) * expf(dsmem_ld_f32(dsmem_map(am, cr)) - M);
+    }
+    Ms[row] = M;
+    Ls[row] = L;
+  }
+  __syncthreads();
+  // exact bf16 probabilities of this CTA's keys into the probability tile
+  for (int idx = threadIdx.x; idx < 16 * kPLd; idx += 128) ptile[idx] = __float2bfloat16_rn(0.f);
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int row = r_lo + (e >> 1) * 8;
+        const int k = i * kDaTile + warp * 16 + nt * 8 + (lane & 3) * 2 + (e & 1);
+        if (t0 + k < t1 && row < p.n_rep)
+          ptile[row * kPLd + k] = __float2bfloat16_rn(rnd<bf16>(expf(s[i][nt][e] - Ms[row]) / Ls[row]));
+      }
+  __syncthreads();
+  float acc[NT][4] = {};
+  for (int i = 0; i < n_tiles && ok; ++i) {
+    if (!mbar_wait_bounded(&bar[2 + i], 0)) {
+      set_status(p.status, JX_ERR_TIMEOUT);
+      ok = false;
+      continue;
+    }
+    const uint32_t vb = smem_u32(ktile + i * TILE_BYTES);
+#pragma unroll
+    for (int kk = 0; kk < kDaTile / 16; ++kk) {
+      uint32_t a0, a1, a2, a3;
+      {
+        const int row = (mi & 1) * 8 + r8, col = i * kDaTile + kk * 16 + (mi >> 1) * 8;
+        ldsm_x4(smem_u32(ptile + row * kPLd + col), a0, a1, a2, a3);
+      }
+#pragma unroll
+      for (int n16 = 0; n16 < NT / 2; ++n16) {
+        uint32_t b0, b1, b2, b3;
+        const int row = kk * 16 + (mi & 1) * 8 + r8;
+        const int ch = (warp * WCOLS) / 8 + n16 * 2 + (mi >> 1);
+        ldsm_x4_t(swz(vb + (ch >> 3) * 8192, row, ch & 7), b0, b1, b2, b3);
+        mma_bf16(acc[n16 * 2], a0, a1, a2, a3, b0, b1);
+        mma_bf16(acc[n16 * 2 + 1], a0, a1, a2, a3, b2, b3);
+      }
+    }
+  }
+  __syncthreads();   // every warp is done with the V tiles: the slots take the partial
+  float* part = reinterpret_cast<float*>(ktile);   // [16][HD]
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int row = (e >> 1) ? r_hi : r_lo;
+      part[row * HD + warp * WCOLS + nt * 8 + (lane & 3) * 2 + (e & 1)] = acc[nt][e];
+    }
+  cluster_sync_all();
+  // rank r sums its slice of the outputs over the ranks in order and rounds it once
+  {
+    const int total = p.n_rep * HD, chunk = (total + CS - 1) / CS;
+    const int e0 = rank * chunk, e1 = min(e0 + chunk, total);
+    for (int idx = e0 + threadIdx.x; idx < e1; idx += 128) {
+      const int row = idx / HD, col = idx % HD;
+      const uint32_t la = smem_u32(part + row * HD + col);
+      float sum = 0.f;
+      for (int cr = 0; cr < CS; ++cr) sum += dsmem_ld_f32(dsmem_map(la, cr));
+      const long long ocol = (long long)(kvh * p.n_rep + row) * HD + col;
+      if (ok) p.out[k128_offset(b, ocol, p.out_rp)] = __float2bfloat16_rn(sum);
+    }
+  }
+  cluster_sync_all();   // no CTA leaves while another may still read its shared memory
+}
+
+// ------------------------------------------------------------------------------------------------
 // Column form of the pv step: one CTA per (64-column block of the head, KV head, batch row) runs over
 // all valid keys, so no split partials and no cross-CTA reduction are needed.  The value tiles
 // [64 keys x 64 columns] stream through a ring of kPcStages stages; warp w consumes tiles w, w+4, ...
@@ -914,10 +1156,40 @@ static int launch_dattn_fused(const jx_dattn_args& a, FAttnParams& p, int sms, b
   return launch_ex(&cfg, dattn_warp_kernel<HD>, km, vm, p) == cudaSuccess ? JX_OK : JX_ERR_CUDA;
 }
 
+template <int HD>
+static int launch_dattn_csplit(const CUtensorMap& km, const CUtensorMap& vm, const DAttnParams& p, bool pdl,
+                               cudaStream_t s) {
+  const int smem = 1024 + 2 * kDaTile * HD * 2 + (HD / 64) * 2048 + 16 * kPLd * 2 + 4 * 8 + 64 * 4;
+  static bool configured = false;
+  if (!configured) {
+    if (cudaFuncSetAttribute(dattn_csplit_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess ||
+        cudaFuncSetAttribute(dattn_csplit_kernel<HD>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
+      return JX_ERR_CUDA;
+    configured = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.n_splits, p.Hkv, p.B);
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = p.n_splits;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 2 : 1;
+  return launch_ex(&cfg, dattn_csplit_kernel<HD>, km, vm, p) == cudaSuccess ? JX_OK : JX_ERR_CUDA;
+}
+
 // 0: by shape (the split form), 1: split form (split pv), 2: single-pass form, 3: split scores + column
-// pv.  Neither alternative is chosen by shape: on the Llama-8B decode shape (B=16) the single-pass form
-// measured 22.7 us against 20.4 us for the split form at context 640 (its fewer warps leave the mma.sync
-// latency exposed), and the column pv 22.4 / 122.7 us against 17.6 / 87.4 us at context 640 / 4096 (each
+// pv, 4: cluster-split form (key ranges up to 16 splits of 128 keys).  No alternative is chosen by
+// shape: the cluster-split form measured 23.1 / 50.3 us against 17.6 / 43.5 us for the split form at
+// context 640 / 2000 (B=16; its T-sized grid of clusters does not fit one wave), the single-pass form
+// 22.7 us against 20.4 us at context 640 (its fewer warps leave the mma.sync latency exposed), and the
+// column pv 22.4 / 122.7 us against 17.6 / 87.4 us at context 640 / 4096 (each
 // warp forms the probabilities of its tiles serially, one L2 round trip per tile).
 static int g_dattn_impl = 0;
 void set_dattn_impl(int impl) { g_dattn_impl = impl; }
@@ -988,6 +1260,14 @@ int run_decode_attention(const jx_dattn_args& a, bool pdl, cudaStream_t stream) 
   p.opart = p.stats + (long long)a.B * a.Hq * n_splits * 2;
   p.counters = a.counters;
   p.status = a.status;
+  if (g_dattn_impl == 4) {
+    if (n_splits > 16) return JX_ERR_SHAPE;
+    switch (a.hd) {
+      case 64: return launch_dattn_csplit<64>(km, vm, p, pdl, stream);
+      case 128: return launch_dattn_csplit<128>(km, vm, p, pdl, stream);
+      default: return launch_dattn_csplit<256>(km, vm, p, pdl, stream);
+    }
+  }
   const bool column_pv = g_dattn_impl == 3;
   switch (a.hd) {
     case 64: return launch_dattn<64>(km, vm, p, column_pv, pdl, stream);

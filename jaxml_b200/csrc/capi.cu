@@ -240,8 +240,9 @@ int jx_set_prefill_linear_impl(int impl) {
 }
 
 int jx_set_decode_attention_impl(int impl) {
-  if (impl < 0 || impl > 3)
-    return fail(JX_ERR_ARG, "jx_set_decode_attention_impl: 0 (by shape), 1 (split), 2 (cluster), 3 (column pv)");
+  if (impl < 0 || impl > 4)
+    return fail(JX_ERR_ARG,
+                "jx_set_decode_attention_impl: 0 (by shape), 1 (split), 2 (cluster), 3 (column pv), 4 (cluster-split)");
   set_dattn_impl(impl);
   return JX_OK;
 }

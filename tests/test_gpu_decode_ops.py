@@ -94,7 +94,7 @@ def test_linear_decode_glu_resid_bias(impl, M):
     assert (h.double() - ref2).abs().max().item() <= 0.05 * ref2.abs().max().item()
 
 
-@pytest.fixture(params=[2, 1, 3], ids=["cluster", "split", "column"])
+@pytest.fixture(params=[2, 1, 3, 4], ids=["cluster", "split", "column", "cluster-split"])
 def attn_form(request):
     N = _n()
     N.call("jx_set_decode_attention_impl", request.param)
@@ -107,7 +107,7 @@ def attn_form(request):
                                                  (128, 32, 8, 0, 20)])
 def test_decode_attention_matches_oracle(attn_form, hd, Hq, Hkv, window, B):
     """Tensor-core decode attention (single-pass cluster form; split scores with the split or the column
-    pv) vs the oracle's Attention.mha on a padded cache.
+    pv; the cluster-split form) vs the oracle's Attention.mha on a padded cache.
 
     The kernel rounds at the reference's points (scores, scale, probabilities, output), so results agree
     to about one bf16 ulp.  A q.k accumulated in a different order can round to the neighbouring bf16
