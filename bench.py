@@ -63,6 +63,7 @@ def parse():
     ap.add_argument("--ctx", type=int, default=4096, help="context length of --micro attn")
     ap.add_argument("--shape", default="28672,4096", help="N,K of --micro gemv (default: fused gate/up)")
     ap.add_argument("--gemv-impl", type=int, default=0, help="--micro gemv kernel: 0 by shape, 1 mma.sync, 2 tcgen05")
+    ap.add_argument("--grids", default="148", help="--micro gemv: comma-separated CTA counts to time (one line each)")
     ap.add_argument("--attn-impl", type=int, default=0, help="decode attention form: 0 by shape, 1 split, 2 cluster, 3 column pv, 4 cluster-split")
     ap.add_argument("--tokens", type=int, default=8192, help="token rows of --micro gemm (prefill B x P)")
     ap.add_argument("--gemm-impl", type=int, default=0, help="--micro gemm kernel: 0 by shape, 1 mma.sync, 2 tcgen05")
@@ -623,13 +624,19 @@ def micro(args):
         else:
             e.kind, e.M, e.N, e.out, e.ldo = N.JX_EPI_STORE, B, Nn, out.data_ptr(), Nn
 
-        def run(w, st):
+        def run(w, st, grid):
             N.call("jx_linear_decode", w.data_ptr(), x.data_ptr(), Np, Kp, B, e, wsp.data_ptr(), wsp.numel(),
-                   cnt.data_ptr(), None, 148, 1, st)
-        ms = _graph_ms(lambda st: [run(w, st) for w in ws], copies)
+                   cnt.data_ptr(), None, grid, 1, st)
         nbytes = 2 * Nn * K + 2 * B * K + 2 * B * (Nn // 2 if glu else Nn)
+        grids = [int(g) for g in args.grids.split(",")]
+        for grid in grids[:-1]:
+            ms = _graph_ms(lambda st: [run(w, st, grid) for w in ws], copies)
+            print(json.dumps({"micro": "gemv", "impl": ["by-shape", "mma.sync", "tcgen05"][args.gemv_impl],
+                              "shape": f"M={B} N={Nn} K={K}", "grid": grid, "us": ms * 1e3,
+                              "gbs": nbytes / ms / 1e6}), flush=True)
+        ms = _graph_ms(lambda st: [run(w, st, grids[-1]) for w in ws], copies)
         line = {"micro": "gemv", "impl": ["by-shape", "mma.sync", "tcgen05"][args.gemv_impl], "shape": f"M={B} N={Nn} K={K}",
-                "us": ms * 1e3, "gbs": nbytes / ms / 1e6}
+                "grid": grids[-1], "us": ms * 1e3, "gbs": nbytes / ms / 1e6}
     else:
         ctx, L = args.ctx, 8
         Hq, Hkv, hd = 32, 8, 128

@@ -25,9 +25,9 @@ constexpr int kTileLd = 68;         // padded float32 row stride of the staging 
 
 template <int MT>
 struct GemvCfg {
-  // At M <= 16 the CTA stays under half the SM's shared memory (104 KB), so the next projection's CTA
-  // (this kernel's, or the tcgen05 kernel's at 116 KB) is resident beside it and streams its weights
-  // while this one finishes.
+  // 5 stages at M <= 16 (104 KB).  Doubling them (10 stages, 205 KB) made every mma.sync projection of
+  // the Llama-8B decode step slower (o_proj 12.3 -> 13.3 us, qkv 15.2 -> 16.4, down 27.2 -> 28.2) and
+  // the step 4.35 -> 4.41 ms: a smaller CTA starts beside the tail of the kernel before it.
   static constexpr int kStages = MT == 1 ? 5 : (MT == 2 ? 4 : 3);
   static constexpr int kWBytes = kGemvBN * kGemvBK * 2;   // 16 KB
   static constexpr int kXBytes = MT * 16 * kGemvBK * 2;   // 4 KB per m16 tile

@@ -24,8 +24,8 @@ struct TcCfg {
   static constexpr int kWBytes = kTcBN * kTcBK * 2;        // 32 KB
   static constexpr int kXBytes = N * kTcBK * 2;            // 4 / 8 / 16 KB
   static constexpr int kStageBytes = kWBytes + kXBytes;
-  // 3 stages at M <= 16 (116 KB): the next projection's CTA fits beside this one (see gemv.cu).
-  static constexpr int kStages = MT == 1 ? 3 : (MT == 2 ? 5 : 4);
+  // As many stages as shared memory holds (see gemv.cu).
+  static constexpr int kStages = MT == 1 ? 5 : (MT == 2 ? 5 : 4);
   static constexpr int kLd = kTcBN + 4;                    // staging tile [N][128 rows] float32
   static constexpr int kTileBytes = N * kLd * 4;
   static constexpr int kBars = 2 * kStages + 5;
