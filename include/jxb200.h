@@ -193,6 +193,15 @@ typedef struct jx_dattn_args {
   long long ws_bytes;
   int* counters;         /* [B * Hkv], zero-initialised once, self-resetting */
   int* status;
+  /* RoPE and the cache append fused in (qkv != NULL; the split form only, no QK norm): q and this
+   * step's k and v are read unrotated from the fused projection output, q and k are rotated on their
+   * first rd dims like jx_qkv_rope_append (rotate_half, in bf16), and k and v are written into the
+   * cache at position len_ptr[b] + len_add - 1 (JX_ERR_RANGE beyond max_pos); `q` is then unused. */
+  const void* qkv;       /* [B, ld_qkv] bf16: Hq q heads, Hkv k heads, Hkv v heads of hd each */
+  long long ld_qkv;
+  const void* cos;       /* [max_pos, rd] bf16 */
+  const void* sin;
+  int rd, max_pos;
 } jx_dattn_args;
 
 /* Prefill attention on tensor cores: S query tokens per row (rows b*S + s), head_dim 64/128/256. */

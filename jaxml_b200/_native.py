@@ -67,7 +67,7 @@ class JxDAttnArgs(ctypes.Structure):
     _fields_ = [("B", I), ("Hq", I), ("Hkv", I), ("hd", I), ("T", I), ("window", I), ("cache_rows", LL),
                 ("layer_row0", LL), ("q", P), ("k_base", P), ("v_base", P), ("len_ptr", P), ("len_add", I),
                 ("scale", F), ("out", P), ("out_rp", LL), ("ws", P), ("ws_bytes", LL), ("counters", P),
-                ("status", P)]
+                ("status", P), ("qkv", P), ("ld_qkv", LL), ("cos", P), ("sin", P), ("rd", I), ("max_pos", I)]
 
 
 class JxPAttnArgs(ctypes.Structure):

@@ -40,7 +40,40 @@ struct DAttnParams {
   float* opart;          // [B, Hq, n_splits, HD]
   int* counters;         // [B * Hkv]
   int* status;
+  // RoPE + cache append fused in (qkv != nullptr): see jx_dattn_args
+  const bf16* qkv;
+  long long ld_qkv;
+  const bf16* cos;
+  const bf16* sin;
+  int rd, max_pos;
+  bf16* k_cache;         // the cache allocations, written at this step's position
+  bf16* v_cache;
 };
+
+// 8 consecutive elements [j0, j0 + 8) of one head of the projection output, rotated on its first rd
+// dims at table row `pos` exactly as qkv_rope_append_kernel does (rotate_half, products and sum each
+// rounded to bf16), packed as bf16.
+__device__ __forceinline__ uint4 rope8(const bf16* head, int j0, int hd, int rd, const bf16* cos, const bf16* sin,
+                                       int pos) {
+  const int half = rd >> 1;
+  float o[8];
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    const int j = j0 + u;
+    const float x = __bfloat162float(head[j]);
+    if (j < rd) {
+      const float rot = j < half ? -__bfloat162float(head[j + half]) : __bfloat162float(head[j - half]);
+      const float a = rnd<bf16>(x * __bfloat162float(cos[(long long)pos * rd + j]));
+      const float c = rnd<bf16>(rot * __bfloat162float(sin[(long long)pos * rd + j]));
+      o[u] = rnd<bf16>(a + c);
+    } else {
+      o[u] = x;
+    }
+  }
+  (void)hd;
+  return make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]), pack_bf16x2(o[4], o[5]),
+                    pack_bf16x2(o[6], o[7]));
+}
 
 // Address of the 16-byte chunk `c` (8 bf16 columns) of row r in a [rows x 64] block stored with the
 // 128-byte swizzle (chunk index XOR row % 8), the layout TMA writes with CU_TENSOR_MAP_SWIZZLE_128B.
@@ -98,14 +131,47 @@ __global__ void __launch_bounds__(128) dattn_scores_kernel(const __grid_constant
   pdl_trigger();
   if (threadIdx.x == 0)
     for (int i = n_early; i < n_tiles; ++i) issue(i);
+  // Fused RoPE: this step's position, its table row (row 0 with a range error beyond the table)
+  const bool fused = p.qkv != nullptr;
+  int pos = valid - 1;
+  if (fused && pos >= p.max_pos) {
+    if (threadIdx.x == 0) set_status(p.status, JX_ERR_RANGE);
+    pos = 0;
+  }
+  const bf16* qkv_row = fused ? p.qkv + (long long)b * p.ld_qkv : nullptr;
   // Q rows of this head group (rows >= n_rep are zero) into the swizzled layout.
   for (int idx = threadIdx.x; idx < 16 * (HD / 8); idx += 128) {
     const int r = idx / (HD / 8), cg = idx % (HD / 8);
     uint4 v = make_uint4(0, 0, 0, 0);
-    if (r < p.n_rep)
-      v = *reinterpret_cast<const uint4*>(p.q + ((long long)b * p.Hq + kvh * p.n_rep + r) * HD + cg * 8);
+    if (r < p.n_rep) {
+      if (fused)
+        v = rope8(qkv_row + (long long)(kvh * p.n_rep + r) * HD, cg * 8, HD, p.rd, p.cos, p.sin, pos);
+      else
+        v = *reinterpret_cast<const uint4*>(p.q + ((long long)b * p.Hq + kvh * p.n_rep + r) * HD + cg * 8);
+    }
     const uint32_t a = swz(smem_u32(qs + (cg >> 3) * 2048), r, cg & 7);
     asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w));
+  }
+  // The CTA holding this step's key appends the rotated k and the v of this KV head to the cache and
+  // puts the k into its loaded tile (whose row was read from the cache before the append).
+  if (fused && valid - 1 >= t0 && valid - 1 < t1) {
+    const int kpos = valid - 1;
+    const int tile = (kpos - t0) / kDaTile, trow = (kpos - t0) % kDaTile;
+    const long long crow = (p.layer_row0 + (long long)b * p.T + kpos) * ((long long)p.Hkv * HD) + (long long)kvh * HD;
+    uint4 k8 = make_uint4(0, 0, 0, 0);
+    const int j0 = threadIdx.x * 8;
+    if (j0 < HD) {
+      k8 = rope8(qkv_row + (long long)(p.Hq + kvh) * HD, j0, HD, p.rd, p.cos, p.sin, pos);
+      const uint4 v8 = *reinterpret_cast<const uint4*>(qkv_row + (long long)(p.Hq + p.Hkv + kvh) * HD + j0);
+      *reinterpret_cast<uint4*>(p.k_cache + crow + j0) = k8;
+      *reinterpret_cast<uint4*>(p.v_cache + crow + j0) = v8;
+    }
+    const bool landed = mbar_wait_bounded(&bar[tile], 0);
+    if (!landed && threadIdx.x == 0) set_status(p.status, JX_ERR_TIMEOUT);
+    if (landed && j0 < HD) {
+      const uint32_t a = swz(smem_u32(ktile + tile * TILE_BYTES + (j0 >> 6) * 8192), trow, (j0 & 63) >> 3);
+      asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(k8.x), "r"(k8.y), "r"(k8.z), "r"(k8.w));
+    }
   }
   __syncthreads();
 
@@ -239,19 +305,26 @@ __global__ void __launch_bounds__(128) dattn_pv_kernel(const __grid_constant__ C
   if (t0 >= valid) return;
   const int t1 = min(t0 + kDaKeys, valid);
   const int n_tiles = (t1 - t0 + kDaTile - 1) / kDaTile;
+  // With the append fused into the scores kernel, the tile holding this step's value loads after the wait.
+  auto issue = [&](int i) {
+    mbar_arrive_expect_tx(&bar[i], TILE_BYTES);
+    const int y = (int)(p.layer_row0 + (long long)b * p.T + t0 + i * kDaTile);
+#pragma unroll
+    for (int c = 0; c < NB; ++c) tma_load_2d(vtile + i * TILE_BYTES + c * 8192, &vmap, kvh * HD + c * 64, y, &bar[i]);
+  };
+  int n_early = n_tiles;
+  if (p.qkv != nullptr)
+    for (n_early = 0; n_early < n_tiles && t0 + (n_early + 1) * kDaTile <= valid - 1;) ++n_early;
   if (threadIdx.x == 0) {
     prefetch_tmap(&vmap);
     mbar_init(&bar[0], 1);
     mbar_init(&bar[1], 1);
     fence_barrier_init();
-    for (int i = 0; i < n_tiles; ++i) {
-      mbar_arrive_expect_tx(&bar[i], TILE_BYTES);
-      const int y = (int)(p.layer_row0 + (long long)b * p.T + t0 + i * kDaTile);
-#pragma unroll
-      for (int c = 0; c < NB; ++c) tma_load_2d(vtile + i * TILE_BYTES + c * 8192, &vmap, kvh * HD + c * 64, y, &bar[i]);
-    }
+    for (int i = 0; i < n_early; ++i) issue(i);
   }
   pdl_wait();
+  if (threadIdx.x == 0)
+    for (int i = n_early; i < n_tiles; ++i) issue(i);
   // exact softmax normaliser of each row from the split statistics
   if (threadIdx.x < 16) {
     const int row = threadIdx.x;
@@ -1199,7 +1272,15 @@ int run_decode_attention(const jx_dattn_args& a, bool pdl, cudaStream_t stream) 
   const int n_rep = a.Hq / a.Hkv;
   if (n_rep > 16) return JX_ERR_SHAPE;
   if (a.hd != 64 && a.hd != 128 && a.hd != 256) return JX_ERR_SHAPE;
-  if (reinterpret_cast<uintptr_t>(a.q) & 15) return JX_ERR_ARG;
+  if (a.qkv) {
+    // fused RoPE + append: the split form only; 16-byte rows of the projection output and tables
+    if (g_dattn_impl >= 2) return JX_ERR_UNSUPPORTED;
+    if (!a.cos || !a.sin || a.rd <= 0 || a.rd > a.hd || (a.rd & 1) || a.max_pos <= 0 ||
+        a.ld_qkv < (long long)(a.Hq + 2 * a.Hkv) * a.hd || (a.ld_qkv & 7) || (reinterpret_cast<uintptr_t>(a.qkv) & 15))
+      return JX_ERR_ARG;
+  } else if (reinterpret_cast<uintptr_t>(a.q) & 15) {
+    return JX_ERR_ARG;
+  }
   if (a.out_rp < a.B || a.out_rp % 8) return JX_ERR_ARG;   // the K128 output must hold every batch row
 
   if (g_dattn_impl == 2) {
@@ -1260,6 +1341,14 @@ int run_decode_attention(const jx_dattn_args& a, bool pdl, cudaStream_t stream) 
   p.opart = p.stats + (long long)a.B * a.Hq * n_splits * 2;
   p.counters = a.counters;
   p.status = a.status;
+  p.qkv = reinterpret_cast<const bf16*>(a.qkv);
+  p.ld_qkv = a.ld_qkv;
+  p.cos = reinterpret_cast<const bf16*>(a.cos);
+  p.sin = reinterpret_cast<const bf16*>(a.sin);
+  p.rd = a.rd;
+  p.max_pos = a.max_pos;
+  p.k_cache = reinterpret_cast<bf16*>(const_cast<void*>(a.k_base));
+  p.v_cache = reinterpret_cast<bf16*>(const_cast<void*>(a.v_base));
   if (g_dattn_impl == 4) {
     if (n_splits > 16) return JX_ERR_SHAPE;
     switch (a.hd) {

@@ -221,14 +221,16 @@ int jx_decode_attention_workspace(int B, int Hq, int hd, int T, int window, long
 }
 
 int jx_decode_attention(const jx_dattn_args* args, int pdl, void* stream) {
-  if (!args || !args->q || !args->k_base || !args->v_base || !args->out || !args->ws || !args->counters || !args->len_ptr)
+  if (!args || !(args->q || args->qkv) || !args->k_base || !args->v_base || !args->out || !args->ws || !args->counters ||
+      !args->len_ptr)
     return fail(JX_ERR_ARG, "jx_decode_attention: null pointer");
   const int rc = run_decode_attention(*args, pdl != 0, (cudaStream_t)stream);
   if (rc == JX_ERR_CUDA) return note_cuda("jx_decode_attention");
+  if (rc == JX_ERR_UNSUPPORTED) return fail(rc, "jx_decode_attention: the fused RoPE inputs (qkv) need the split form");
   if (rc != JX_OK)
     return fail(rc, "jx_decode_attention: head_dim must be 64/128/256, Hq/Hkv <= 16, out_rp >= B and a multiple "
-                    "of 8, workspace large enough, "
-                    "16-byte aligned q/cache");
+                    "of 8, workspace large enough, 16-byte aligned q/cache, and with qkv: tables, 0 < rd <= hd "
+                    "even, ld_qkv >= (Hq + 2 Hkv) hd and a multiple of 8");
   return JX_OK;
 }
 

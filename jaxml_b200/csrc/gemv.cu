@@ -70,8 +70,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
     fence_barrier_init();
   }
   __syncthreads();
-  pdl_trigger();
 
+  // Dependents are released only by threads past their own wait on the previous kernel, so a kernel
+  // launched behind this one finds every kernel before this one complete.
   if (warp == 0) {
     // ---------------- producer ----------------
     if (lane == 0 && n_it > 0) {
@@ -91,6 +92,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
         bulk_g2s_hint(smem + i * C::kStageBytes, wsrc(it0 + i), C::kWBytes, &full[i], pol_w);
       }
       pdl_wait();
+      pdl_trigger();
       for (int i = 0; i < pre; ++i)
         bulk_g2s(smem + i * C::kStageBytes + C::kWBytes, xsrc(it0 + i), C::kXBytes, &full[i]);
       int issued = pre;
@@ -124,6 +126,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
 
   // ---------------- consumers ----------------
   pdl_wait();
+  pdl_trigger();
   const int cw = (warp - 1) & 3;       // owns weight rows [cw*16, cw*16+16) of each 64-row block
   const int khalf = (warp - 1) >> 2;   // and K steps [khalf*4, khalf*4+4) of each chunk
   const int tid = threadIdx.x - 32;    // 0..255

@@ -84,7 +84,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  pdl_trigger();
+  // Dependents are released only by threads past their own wait on the previous kernel (the producer
+  // and the epilogue warps; the MMA warp never waits), so a kernel launched behind this one finds
+  // every kernel before this one complete.
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -101,6 +103,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         bulk_g2s_hint(smem + i * C::kStageBytes, wsrc(it0 + i), C::kWBytes, &full[i], pol_w);
       }
       pdl_wait();
+      pdl_trigger();
       for (int i = 0; i < pre; ++i)
         bulk_g2s(smem + i * C::kStageBytes + C::kWBytes, xsrc(it0 + i), C::kXBytes, &full[i]);
       int issued = pre;
@@ -170,6 +173,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   } else {
     // ---------------- epilogue (warps 2..5, 128 threads) ----------------
     pdl_wait();
+    pdl_trigger();
     const int tid = threadIdx.x - 64;
     const int quad = warp & 3;                 // TMEM lane quadrant this warp may read
     const int row = quad * 32 + lane;          // weight row within the block

@@ -469,9 +469,11 @@ class DecoderRuntime:
             self._linear(acts, lw.wqkv, W.Np_qkv, W.Kp_d, "xn", N.JX_EPI_STORE, N_valid=W.nqkv, bias=lw.bqkv,
                          out=acts["qkv"], ldo=W.nqkv, K_logical=W.d, N_cols=W.nqkv,
                          pf=self._pf(lw.wo, W.Np_d, W.Kp_o, budget=64e6))
-            self._qkv_rope_append(acts, li, lw, S, decode)
+            fuse_rope = decode and self.fast_attn and self.fused_rope and lw.qn is None
+            if not fuse_rope:
+                self._qkv_rope_append(acts, li, lw, S, decode)
             if decode and self.fast_attn:
-                self._decode_attention(acts, li, lw)
+                self._decode_attention(acts, li, lw, fuse_rope)
             elif not decode and self.fast_attn and S > 1:
                 self._prefill_attention(acts, li, lw, S)
             else:
@@ -510,9 +512,17 @@ class DecoderRuntime:
         self._launches += 1
         N.check(N.load().jx_attention(at, W.jdt, 1, self.stream_ptr()), "jx_attention")
 
-    def _decode_attention(self, acts, li, lw):
+    # Decode attention reads q, k and v straight from the fused projection output and does the RoPE and
+    # the cache append itself (no separate RoPE kernel) for the families without QK norm.
+    fused_rope = True
+
+    def _decode_attention(self, acts, li, lw, fuse_rope=False):
         W, cfg = self.w, self.w.cfg
         a = N.JxDAttnArgs()
+        if fuse_rope:
+            cos, sin = (W.cos_l, W.sin_l) if lw.local_rope else (W.cos, W.sin)
+            a.qkv, a.ld_qkv, a.cos, a.sin = ptr(acts["qkv"]), W.nqkv, ptr(cos), ptr(sin)
+            a.rd, a.max_pos = W.rd, cfg.max_position_embeddings
         a.B, a.Hq, a.Hkv, a.hd, a.T = self.B, W.Hq, W.Hkv, W.hd, self.T
         a.window = cfg.sliding_window if lw.sliding else 0
         a.cache_rows = self.k_cache.shape[0] * self.B * self.T

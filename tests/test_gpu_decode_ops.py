@@ -156,3 +156,76 @@ def test_decode_attention_matches_oracle(attn_form, hd, Hq, Hkv, window, B):
         err = (got - want).abs()
         assert err.max().item() <= 2e-3, err.max().item()
         assert (err <= ulp + 1e-6).float().mean().item() >= 0.99
+
+
+def _dattn_call(N, B, Hq, Hkv, hd, T, L, layer, q, kd, vd, pos, fused=None):
+    """jx_decode_attention (split form) on cache `kd` / `vd`; `fused` = (qkv, cos, sin, rd, max_pos) reads q,
+    k and v from the projection output and appends instead of `q`.  Returns the [B, Hq*hd] output."""
+    Mp, Kp = _rup(B, 16), _rup(Hq * hd, 128)
+    out = torch.zeros(Mp * Kp, dtype=torch.bfloat16, device="cuda")
+    nb = N.LL()
+    N.check(N.load().jx_decode_attention_workspace(B, Hq, hd, T, 0, nb), "ws")
+    ws = torch.zeros(nb.value // 4 + 1, dtype=torch.float32, device="cuda")
+    cnt = torch.zeros(B * Hkv, dtype=torch.int32, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    a = N.JxDAttnArgs()
+    a.B, a.Hq, a.Hkv, a.hd, a.T, a.window = B, Hq, Hkv, hd, T, 0
+    a.cache_rows, a.layer_row0 = L * B * T, layer * B * T
+    a.q, a.k_base, a.v_base = (None if q is None else q.data_ptr()), kd.data_ptr(), vd.data_ptr()
+    a.len_ptr, a.len_add, a.scale = pos.data_ptr(), 2, hd ** -0.5
+    a.out, a.out_rp = out.data_ptr(), Mp
+    a.ws, a.ws_bytes, a.counters, a.status = ws.data_ptr(), ws.numel() * 4, cnt.data_ptr(), status.data_ptr()
+    if fused is not None:
+        qkv, cos, sin, rd, max_pos = fused
+        a.qkv, a.ld_qkv, a.cos, a.sin, a.rd, a.max_pos = qkv.data_ptr(), qkv.shape[1], cos.data_ptr(), sin.data_ptr(), rd, max_pos
+    N.call("jx_decode_attention", a, 1, _stream())
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    got = torch.empty(B, Hq * hd, dtype=torch.bfloat16, device="cuda")
+    N.call("jx_unpack_k128", out.data_ptr(), B, Hq * hd, Mp, got.data_ptr(), N.JX_BF16, Hq * hd, _stream())
+    torch.cuda.synchronize()
+    return got
+
+
+@pytest.mark.parametrize("hd,Hq,Hkv,rd,B", [(128, 32, 8, 128, 3), (64, 8, 8, 16, 5), (128, 16, 2, 128, 20),
+                                             (256, 16, 8, 256, 3)])
+def test_decode_attention_fused_rope_matches_separate_kernels(hd, Hq, Hkv, rd, B):
+    """RoPE + cache append fused into the decode attention: the same output bits and the same cache as
+    jx_qkv_rope_append followed by the attention on its q."""
+    from oracle import jaxml_oracle as O
+
+    N = _n()
+    torch.manual_seed(7)
+    T, L, layer, max_pos = 768, 2, 1, 1024
+    lens = torch.tensor(([513, 200, 767, 64, 1] * 4)[:B], dtype=torch.int32)   # valid keys after the append
+    kc = torch.randn(L, B, T, Hkv, hd).to(torch.bfloat16).cuda()
+    vc = torch.randn(L, B, T, Hkv, hd).to(torch.bfloat16).cuda()
+    qkv = torch.randn(B, (Hq + 2 * Hkv) * hd).to(torch.bfloat16).cuda()
+    cos, sin = (t.cuda() for t in O.rope_tables(hd, rd / hd, 10000.0, 1.0, max_pos, torch.bfloat16))
+    pos = (lens - 2).cuda()
+    # separate kernels
+    k1, v1 = kc.clone(), vc.clone()
+    q = torch.empty(B, Hq * hd, dtype=torch.bfloat16, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    qa = N.JxQkvArgs()
+    qa.M, qa.S, qa.Hq, qa.Hkv, qa.hd, qa.rd = B, 1, Hq, Hkv, hd, rd
+    qa.qkv, qa.ld_qkv, qa.qn_w, qa.kn_w, qa.eps = qkv.data_ptr(), qkv.shape[1], None, None, 1e-6
+    qa.max_pos, qa.cos, qa.sin, qa.pos_id, qa.decode, qa.T = max_pos, cos.data_ptr(), sin.data_ptr(), pos.data_ptr(), 1, T
+    qa.q_out, qa.k_cache, qa.v_cache, qa.status = q.data_ptr(), k1[layer].data_ptr(), v1[layer].data_ptr(), status.data_ptr()
+    N.call("jx_qkv_rope_append", qa, N.JX_BF16, 0, _stream())
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    out1 = _dattn_call(N, B, Hq, Hkv, hd, T, L, layer, q, k1, v1, pos)
+    # fused
+    k2, v2 = kc.clone(), vc.clone()
+    out2 = _dattn_call(N, B, Hq, Hkv, hd, T, L, layer, None, k2, v2, pos, fused=(qkv, cos, sin, rd, max_pos))
+    assert torch.equal(k1, k2) and torch.equal(v1, v2)
+    assert torch.equal(out1, out2)
+    # the other forms do not take the fused inputs
+    for form in (2, 3, 4):
+        N.call("jx_set_decode_attention_impl", form)
+        try:
+            with pytest.raises(RuntimeError):
+                _dattn_call(N, B, Hq, Hkv, hd, T, L, layer, None, k2, v2, pos, fused=(qkv, cos, sin, rd, max_pos))
+        finally:
+            N.call("jx_set_decode_attention_impl", 0)

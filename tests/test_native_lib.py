@@ -80,8 +80,8 @@ def test_decode_attention_rejects_an_output_too_small_for_the_batch():
         a.out_rp = rp
         assert lib.jx_decode_attention(a, 0, None) == N.JX_ERR_ARG
         assert b"out_rp" in lib.jx_last_error()
-    for impl in (0, 1, 2, 3):
-        assert lib.jx_set_decode_attention_impl(impl) == (N.JX_OK if impl <= 2 else N.JX_ERR_ARG)
+    for impl in (0, 1, 2, 3, 4, 5):
+        assert lib.jx_set_decode_attention_impl(impl) == (N.JX_OK if impl <= 4 else N.JX_ERR_ARG)
         assert lib.jx_set_prefill_linear_impl(impl) == (N.JX_OK if impl <= 2 else N.JX_ERR_ARG)
     lib.jx_set_decode_attention_impl(0)
     lib.jx_set_prefill_linear_impl(0)
