@@ -31,10 +31,10 @@ sys.path.insert(0, ROOT)
 
 METRIC = "decode tok/s (box) & p50 step latency, Llama-3-8B-shape bf16, TP=1/2/4/8"
 
-# DRAM bytes (read 235073024 + write 4625152) of one launch of the tcgen05 decode projection on the
+# DRAM bytes (read 235079424 + write 4493056) of one launch of the tcgen05 decode projection on the
 # gate/up shape (M=16, N=28672, K=4096), from an ncu --set full capture of
 # `python bench.py --micro gemv --shape 28672,4096`.
-GEMV_TC_GATEUP_TRAFFIC = 239698176
+GEMV_TC_GATEUP_TRAFFIC = 239572480
 
 
 def l8_config(num_layers=32):
