@@ -64,6 +64,7 @@ def parse():
     ap.add_argument("--shape", default="28672,4096", help="N,K of --micro gemv (default: fused gate/up)")
     ap.add_argument("--gemv-impl", type=int, default=0, help="--micro gemv kernel: 0 by shape, 1 mma.sync, 2 tcgen05")
     ap.add_argument("--grids", default="148", help="--micro gemv: comma-separated CTA counts to time (one line each)")
+    ap.add_argument("--tile-groups", default="", help="--micro gemm: comma-separated tile-group sizes to time")
     ap.add_argument("--attn-impl", type=int, default=0, help="decode attention form: 0 by shape, 1 split, 2 cluster, 3 column pv, 4 cluster-split")
     ap.add_argument("--tokens", type=int, default=8192, help="token rows of --micro gemm (prefill B x P)")
     ap.add_argument("--gemm-impl", type=int, default=0, help="--micro gemm kernel: 0 by shape, 1 mma.sync, 2 tcgen05")
@@ -593,7 +594,6 @@ def micro(args):
 
         def run(w, stream):
             N.call("jx_linear_prefill", x.data_ptr(), w.data_ptr(), Mp, Np, Kp, e, st.data_ptr(), 1, stream)
-        ms = _graph_ms(lambda stream: [run(w, stream) for w in ws], copies)
         flops = 2.0 * M * Nn * K
         peaks = {}
         try:
@@ -601,9 +601,16 @@ def micro(args):
         except OSError:
             pass
         peak = peaks.get("bf16_tflops", 1590.0)
-        line = {"micro": "gemm", "impl": ["by-shape", "mma.sync", "tcgen05"][args.gemm_impl],
-                "shape": f"M={M} N={Nn} K={K}", "us": ms * 1e3, "tflops": flops / ms / 1e9,
-                "frac_of_measured_bf16": flops / ms / 1e9 / peak, "status": int(st.item())}
+        groups = [int(g) for g in args.tile_groups.split(",")] if args.tile_groups else [None]
+        for gi, gm in enumerate(groups):
+            if gm is not None:
+                N.call("jx_set_prefill_tile_group", gm)
+            ms = _graph_ms(lambda stream: [run(w, stream) for w in ws], copies)
+            line = {"micro": "gemm", "impl": ["by-shape", "mma.sync", "tcgen05"][args.gemm_impl],
+                    "shape": f"M={M} N={Nn} K={K}", "tile_group": gm, "us": ms * 1e3, "tflops": flops / ms / 1e9,
+                    "frac_of_measured_bf16": flops / ms / 1e9 / peak, "status": int(st.item())}
+            if gi < len(groups) - 1:
+                print(json.dumps(line), flush=True)
     elif args.micro == "gemv":
         Nn, K = (int(v) for v in args.shape.split(","))
         glu = Nn == 2 * 14336 and K == 4096

@@ -297,6 +297,10 @@ int jx_linear_prefill(const void* X, const void* W, long long Mp, long long Np, 
  * 1 = mma.sync, 2 = tcgen05/TMEM (JX_ERR_SHAPE when the shape does not allow it). */
 int jx_set_prefill_linear_impl(int impl);
 
+/* Tile order of the tcgen05 prefill projection (process-wide): gm > 0 runs the tiles of gm 256-token
+ * blocks x all weight blocks before the next gm token blocks; 0 = token blocks fastest over the grid. */
+int jx_set_prefill_tile_group(int gm);
+
 /* float32 projection: X [M, K] (row stride ldx) times the reference's kernel layout W [K, N]. */
 int jx_linear_f32(const float* X, long long ldx, const float* W, int M, int N, int K, const jx_epilogue* epi, int pdl,
                   void* stream);

@@ -21,6 +21,7 @@ int run_decode_attention(const jx_dattn_args& a, bool pdl, cudaStream_t stream);
 void set_gemv_impl(int impl);
 void set_dattn_impl(int impl);
 void set_gemm_impl(int impl);
+void set_gemm_tile_group(int gm);
 int run_prefill_attention(const jx_pattn_args& a, bool pdl, cudaStream_t stream);
 long long dattn_workspace_bytes(int B, int Hq, int T, int hd, int n_splits);
 int dattn_n_splits(int T, int window);
@@ -231,6 +232,12 @@ int jx_decode_attention(const jx_dattn_args* args, int pdl, void* stream) {
     return fail(rc, "jx_decode_attention: head_dim must be 64/128/256, Hq/Hkv <= 16, out_rp >= B and a multiple "
                     "of 8, workspace large enough, 16-byte aligned q/cache, and with qkv: tables, 0 < rd <= hd "
                     "even, ld_qkv >= (Hq + 2 Hkv) hd and a multiple of 8");
+  return JX_OK;
+}
+
+int jx_set_prefill_tile_group(int gm) {
+  if (gm < 0) return fail(JX_ERR_ARG, "jx_set_prefill_tile_group: gm >= 0");
+  set_gemm_tile_group(gm);
   return JX_OK;
 }
 

@@ -38,9 +38,26 @@ constexpr uint32_t kGtTmemCols = 512;
 struct GtParams {
   long long Mp, Np, Kp;
   int nM, nN, tiles;
+  int gm;                // token blocks per tile group (0: token blocks fastest over the whole grid)
   EpiParams e;
   int* status;
 };
+
+// Tile t -> (token block mb, weight block nb).  With tile groups, the tiles of gm token blocks x all
+// weight blocks come first (token block fastest inside the group), so the activations of a group stay
+// in L2 while the weights stream past; otherwise token blocks are fastest over the whole grid.
+__device__ __forceinline__ void gt_tile(const GtParams& p, int t, int& mb, int& nb) {
+  if (p.gm <= 0 || p.gm >= p.nM) {
+    mb = t % p.nM;
+    nb = t / p.nM;
+    return;
+  }
+  const int per_group = p.gm * p.nN;
+  const int g = t / per_group, r = t - g * per_group;
+  const int width = min(p.gm, p.nM - g * p.gm);   // the last group may hold fewer token blocks
+  mb = g * p.gm + r % width;
+  nb = r / width;
+}
 
 __global__ void __launch_bounds__(kGtThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap, GtParams p) {
@@ -90,7 +107,8 @@ __global__ void __launch_bounds__(kGtThreads, 1)
       pdl_wait();
       int cnt = 0;
       for (int t = blockIdx.x; t < p.tiles && !*dead; t += G) {
-        const int mb = t % p.nM, nb = t / p.nM;
+        int mb, nb;
+        gt_tile(p, t, mb, nb);
         const int wz = nb * (kGtBM / 8), xz = mb * (kGtBN / 8);
         for (int j = 0; j < ksteps; ++j, ++cnt) {
           const int s = cnt % kGtStages;
@@ -114,7 +132,9 @@ __global__ void __launch_bounds__(kGtThreads, 1)
     if (lane == 0) {
       int cnt = 0, ti = 0;
       for (int t = blockIdx.x; t < p.tiles && !*dead; t += G, ++ti) {
-        const int mb = t % p.nM;
+        int mb, nb;
+        gt_tile(p, t, mb, nb);
+        (void)nb;
         const bool half = (p.Mp - (long long)mb * kGtBN) < kGtBN;   // 128-token last block
         const uint32_t idesc = half ? umma_idesc_bf16_f32(kGtBM, 128) : umma_idesc_bf16_f32(kGtBM, kGtBN);
         const int buf = ti & 1;
@@ -156,7 +176,8 @@ __global__ void __launch_bounds__(kGtThreads, 1)
     const int row = quad * 32 + lane;
     int ti = 0;
     for (int t = blockIdx.x; t < p.tiles; t += G, ++ti) {
-      const int mb = t % p.nM, nb = t / p.nM;
+      int mb, nb;
+        gt_tile(p, t, mb, nb);
       const int buf = ti & 1;
       const int ntok = (p.Mp - (long long)mb * kGtBN) < kGtBN ? 128 : kGtBN;
       bool ok = !*dead && mbar_wait_bounded(&accf[buf], (ti >> 1) & 1);
@@ -240,6 +261,9 @@ bool gemm_tc_supported(long long Mp, long long Np, long long Kp) {
          (Kp / 128) * (Np / 8) < (1LL << 31) && (Kp / 128) * (Mp / 8) < (1LL << 31);
 }
 
+static int g_tile_group = 0;
+void set_gemm_tile_group(int gm) { g_tile_group = gm; }
+
 int run_gemm_tc(const bf16* X, const bf16* W, long long Mp, long long Np, long long Kp, const EpiParams& e,
                 int* status, bool pdl, cudaStream_t stream) {
   if (!gemm_tc_supported(Mp, Np, Kp)) return JX_ERR_SHAPE;
@@ -260,6 +284,7 @@ int run_gemm_tc(const bf16* X, const bf16* W, long long Mp, long long Np, long l
   p.nM = (int)((Mp + kGtBN - 1) / kGtBN);
   p.nN = (int)(Np / kGtBM);
   p.tiles = p.nM * p.nN;
+  p.gm = g_tile_group;
   p.e = e;
   p.status = status;
   int sms = 148;
