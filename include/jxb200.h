@@ -82,6 +82,20 @@ typedef struct jx_epilogue {
   long long peer_flag_off;     /* flags: [2 sets][256 units][8 sources] uint32 */
   long long peer_seq_off;      /* push epoch counter */
   int peer_rank, peer_world;
+  /* Normalisation prologue (decode projections at M <= 16; pn_h != NULL): before the activations are
+   * loaded, CTA m < M writes row m of the activation operand X (K128 layout) as the norm of row m of h
+   * (jx_norm's kinds RMS / GEMMA / LAYER, no residual input), and every CTA waits for those rows: the
+   * RMSNorm / LayerNorm of models/llama.py:133-137 and gpt_neox.py run in the projection's prologue
+   * instead of a separate jx_norm launch.  pn_sync: [2 + 16] ints, zero-initialised once, shared by the
+   * prologue calls on one stream ([0] epoch, [1] arrivals, [2 + m] row flags). */
+  const void* pn_h;            /* [M, pn_ldh] model dtype (bf16) */
+  long long pn_ldh;
+  const void* pn_w;            /* [pn_d] */
+  const void* pn_b;            /* [pn_d] (LayerNorm) or NULL */
+  int* pn_sync;
+  int pn_kind, pn_d;
+  float pn_eps;
+  int _pad1;
 } jx_epilogue;
 
 /* Row-wise embedding gather / residual add / normalisation (one launch per call). */

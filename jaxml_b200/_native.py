@@ -34,7 +34,9 @@ class JxEpilogue(ctypes.Structure):
     _fields_ = [("kind", I), ("M", I), ("N", I), ("pf_iters", I), ("bias", P), ("out", P), ("ldo", LL),
                 ("out_rp", LL), ("res", P), ("ldr", LL), ("res2", P), ("ldr2", LL), ("pf_w", P), ("pf_np", LL),
                 ("pf_kp", LL), ("pf_rows", I), ("pf_grid", I), ("peer_bases", P), ("peer_recv_off", LL),
-                ("peer_slot_bytes", LL), ("peer_flag_off", LL), ("peer_seq_off", LL), ("peer_rank", I), ("peer_world", I)]
+                ("peer_slot_bytes", LL), ("peer_flag_off", LL), ("peer_seq_off", LL), ("peer_rank", I), ("peer_world", I),
+                ("pn_h", P), ("pn_ldh", LL), ("pn_w", P), ("pn_b", P), ("pn_sync", P), ("pn_kind", I), ("pn_d", I),
+                ("pn_eps", F), ("_pad1", I)]
 
 
 class JxNormArgs(ctypes.Structure):

@@ -52,6 +52,135 @@ __device__ __forceinline__ void push_signal(const EpiParams& e, long long n0, in
     }
 }
 
+// ---- normalisation prologue (jx_epilogue.pn_*) ----
+__device__ __forceinline__ void pn_load8(const bf16* p, float* v) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+// Sum over the nt threads of a named barrier group (tid in [0, nt), nt a multiple of 32, red >= nt / 32).
+__device__ __forceinline__ float pn_group_sum(float v, float* red, int tid, int nt, int bar) {
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  if ((tid & 31) == 0) red[tid >> 5] = v;
+  named_bar_sync(bar, nt);
+  float t = 0.f;
+  for (int w = 0; w < nt / 32; ++w) t += red[w];
+  named_bar_sync(bar, nt);
+  return t;
+}
+
+// Row m of h normalised (jx_norm's arithmetic: float32 statistics, the reference's bf16 roundings) into
+// row m of the K128 activation operand X with Mp row padding, by the nt threads of barrier group `bar`.
+__device__ __forceinline__ void prologue_norm_row(const EpiParams& e, bf16* X, long long Mp, int m, int tid, int nt,
+                                                  int bar, float* red) {
+  const bf16* h = reinterpret_cast<const bf16*>(e.pn_h) + (long long)m * e.pn_ldh;
+  const bf16* w = reinterpret_cast<const bf16*>(e.pn_w);
+  const bf16* b = reinterpret_cast<const bf16*>(e.pn_b);
+  const int d = e.pn_d;
+  float s = 0.f, s2 = 0.f;
+  for (int j = tid * 8; j < d; j += nt * 8) {
+    float x[8];
+    pn_load8(h + j, x);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      s += x[i];
+      s2 += x[i] * x[i];
+    }
+  }
+  float mean = 0.f, den;
+  if (e.pn_kind == JX_NORM_LAYER) {
+    mean = pn_group_sum(s, red, tid, nt, bar) / (float)d;
+    float v = 0.f;
+    for (int j = tid * 8; j < d; j += nt * 8) {
+      float x[8];
+      pn_load8(h + j, x);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v += (x[i] - mean) * (x[i] - mean);
+    }
+    den = sqrtf(pn_group_sum(v, red, tid, nt, bar) / (float)d + e.pn_eps);
+  } else {
+    den = sqrtf(pn_group_sum(s2, red, tid, nt, bar) / (float)d + e.pn_eps);
+  }
+  const float inv = 1.0f / den;
+  for (int j = tid * 8; j < d; j += nt * 8) {
+    float x[8], wv[8], bv[8], y[8];
+    pn_load8(h + j, x);
+    pn_load8(w + j, wv);
+    if (b) pn_load8(b + j, bv);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (e.pn_kind == JX_NORM_LAYER)
+        y[i] = rnd<bf16>((x[i] - mean) / den * wv[i] + (b ? bv[i] : 0.f));
+      else if (e.pn_kind == JX_NORM_RMS)
+        y[i] = rnd<bf16>(wv[i] * rnd<bf16>(x[i] / den));
+      else
+        y[i] = rnd<bf16>((wv[i] + 1.0f) * (x[i] * inv));
+    }
+    uint4 u;
+    u.x = pack_bf16x2(y[0], y[1]);
+    u.y = pack_bf16x2(y[2], y[3]);
+    u.z = pack_bf16x2(y[4], y[5]);
+    u.w = pack_bf16x2(y[6], y[7]);
+    *reinterpret_cast<uint4*>(X + k128_offset(m, j, Mp)) = u;
+  }
+}
+
+// The prologue's part of a CTA: CTA c < M normalises row c and flags it with epoch ep + 1 (after every
+// thread of the group has stored).  Called by the nt threads of barrier group `bar` after their wait on
+// the previous kernel.
+__device__ __forceinline__ void prologue_rows(const EpiParams& e, bf16* X, long long Mp, int c, int ep, int tid, int nt,
+                                              int bar, float* red) {
+  if (c >= e.M) return;
+  prologue_norm_row(e, X, Mp, c, tid, nt, bar, red);
+  named_bar_sync(bar, nt);
+  if (tid == 0) {
+    __threadfence();
+    st_release_gpu(e.pn_sync + 2 + c, ep + 1);
+  }
+}
+
+// Wait (bounded) until the M rows of this call's X are written; then async-proxy loads may read them.
+// The row flags are read together (independent relaxed loads, one round trip per poll), then one
+// acquire fence orders the rows' contents before the loads that follow.
+__device__ __forceinline__ bool prologue_wait(const EpiParams& e, int ep) {
+  const volatile int* f = e.pn_sync + 2;
+  uint64_t t0 = 0;
+  for (bool first = true;; first = false) {
+    int v[16];
+#pragma unroll
+    for (int m = 0; m < 16; ++m) v[m] = m < e.M ? f[m] : ep + 1;
+    bool all = true;
+#pragma unroll
+    for (int m = 0; m < 16; ++m) all &= v[m] == ep + 1;
+    if (all) break;
+    if (first) {
+      t0 = globaltimer_ns();
+    } else if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      return false;
+    }
+  }
+  asm volatile("fence.acq_rel.gpu;" ::: "memory");
+  fence_proxy_async_global();
+  return true;
+}
+
+// End of a CTA of a prologue call (one thread, after every thread of the CTA has read the epoch): the
+// last CTA to arrive advances the epoch for the next call.
+__device__ __forceinline__ void prologue_arrive(const EpiParams& e, int ep) {
+  __threadfence();
+  if (atomicAdd(e.pn_sync + 1, 1) == (int)(gridDim.x * gridDim.y * gridDim.z) - 1) {
+    e.pn_sync[1] = 0;
+    e.pn_sync[0] = ep + 1;
+    __threadfence();
+  }
+}
+
 template <typename T>
 __device__ __forceinline__ float bias_at(const EpiParams& e, long long n) {
   return e.bias ? to_f(reinterpret_cast<const T*>(e.bias)[n]) : 0.0f;

@@ -93,6 +93,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
       }
       pdl_wait();
       pdl_trigger();
+      // normalisation prologue: the activations exist once CTAs 0..M-1 have written them
+      if (e.pn_h && !prologue_wait(e, *reinterpret_cast<volatile int*>(e.pn_sync))) set_status(status, JX_ERR_TIMEOUT);
       for (int i = 0; i < pre; ++i)
         bulk_g2s(smem + i * C::kStageBytes + C::kWBytes, xsrc(it0 + i), C::kXBytes, &full[i]);
       int issued = pre;
@@ -130,6 +132,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
   const int cw = (warp - 1) & 3;       // owns weight rows [cw*16, cw*16+16) of each 64-row block
   const int khalf = (warp - 1) >> 2;   // and K steps [khalf*4, khalf*4+4) of each chunk
   const int tid = threadIdx.x - 32;    // 0..255
+  __shared__ float pn_red[kGemvConsumers / 32];
+  const int pn_ep = e.pn_h ? *reinterpret_cast<volatile int*>(e.pn_sync) : 0;
+  if (e.pn_h) prologue_rows(e, const_cast<bf16*>(X), Mp, c, pn_ep, tid, kGemvConsumers, 1, pn_red);
   float acc[MT][2][4];
   bool dead = false;
 
@@ -306,6 +311,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
     named_bar_sync(1, kGemvConsumers);
     if (do_epi && !dead && e.kind == JX_EPI_PUSH_F32 && tid == 0) push_signal(e, nb * kGemvBN, kGemvBN);
   }
+  if (e.pn_h) {
+    named_bar_sync(1, kGemvConsumers);
+    if (tid == 0) prologue_arrive(e, pn_ep);
+  }
 }
 
 template <int MT>
@@ -356,6 +365,18 @@ int run_gemv(const bf16* W, const bf16* X, long long Np, long long Kp, int M, co
   // L2 prefetch plan of the next decode projection (jx_epilogue.pf_w): the kernel and grid that call
   // will get by the same rules, or no prefetch when its sizes or alignment are not a decode projection's.
   EpiParams e = e_in;
+  if (e.pn_h) {
+    // normalisation prologue: one CTA per token row, rows of whole 16-byte vectors
+    // (CTAs 0..M-1 must exist: the grid the chosen kernel gets is at least M)
+    const long long tot = gemv_uses_tc(Np, grid) ? (Np / 128) * (Kp / 128) : (Np / kGemvBN) * (Kp / kGemvBK);
+    const long long g = grid > 0 ? grid : 148;
+    if (M > 16 || !e.pn_w || !e.pn_sync || e.pn_d <= 0 || e.pn_d % 8 || e.pn_d > Kp || (e.pn_ldh & 7) ||
+        e.pn_ldh < e.pn_d || (e.pn_kind != JX_NORM_RMS && e.pn_kind != JX_NORM_GEMMA && e.pn_kind != JX_NORM_LAYER) ||
+        ((reinterpret_cast<uintptr_t>(e.pn_h) | reinterpret_cast<uintptr_t>(e.pn_w) |
+          reinterpret_cast<uintptr_t>(e.pn_b) | reinterpret_cast<uintptr_t>(X)) & 15) ||
+        (reinterpret_cast<uintptr_t>(e.pn_sync) & 3) || (g < tot ? g : tot) < M)
+      return JX_ERR_ARG;
+  }
   if (e.kind == JX_EPI_PUSH_F32) {
     // every rank's receive slot and flags sit at the same offsets of its region; units of 64 columns
     if (!e.peer_bases || e.peer_world < 1 || e.peer_world > 8 || e.peer_rank < 0 || e.peer_rank >= e.peer_world ||

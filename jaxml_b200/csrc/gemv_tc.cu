@@ -104,6 +104,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       pdl_wait();
       pdl_trigger();
+      // normalisation prologue: the activations exist once CTAs 0..M-1 have written them
+      if (e.pn_h && !prologue_wait(e, *reinterpret_cast<volatile int*>(e.pn_sync))) set_status(status, JX_ERR_TIMEOUT);
       for (int i = 0; i < pre; ++i)
         bulk_g2s(smem + i * C::kStageBytes + C::kWBytes, xsrc(it0 + i), C::kXBytes, &full[i]);
       int issued = pre;
@@ -175,6 +177,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     pdl_wait();
     pdl_trigger();
     const int tid = threadIdx.x - 64;
+    __shared__ float pn_red[4];
+    const int pn_ep = e.pn_h ? *reinterpret_cast<volatile int*>(e.pn_sync) : 0;
+    if (e.pn_h) prologue_rows(e, const_cast<bf16*>(X), C::N, c, pn_ep, tid, 128, 1, pn_red);
     const int quad = warp & 3;                 // TMEM lane quadrant this warp may read
     const int row = quad * 32 + lane;          // weight row within the block
     const long long Mp = C::N;
@@ -305,6 +310,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                            tid, 128);
       named_bar_sync(1, 128);
       if (do_epi && !sh[0] && e.kind == JX_EPI_PUSH_F32 && tid == 0) push_signal(e, nb * kTcBN, kTcBN);
+    }
+    if (e.pn_h) {
+      named_bar_sync(1, 128);
+      if (tid == 0) prologue_arrive(e, pn_ep);
     }
   }
   // Teardown without a CTA-wide barrier (the roles above leave their warps at different points): the

@@ -229,3 +229,60 @@ def test_decode_attention_fused_rope_matches_separate_kernels(hd, Hq, Hkv, rd, B
                 _dattn_call(N, B, Hq, Hkv, hd, T, L, layer, None, k2, v2, pos, fused=(qkv, cos, sin, rd, max_pos))
         finally:
             N.call("jx_set_decode_attention_impl", 0)
+
+
+@pytest.mark.parametrize("kind", ["rms", "gemma", "layer"])
+@pytest.mark.parametrize("M", [1, 5, 16])
+def test_linear_decode_norm_prologue(impl, kind, M):
+    """Normalisation prologue of the decode projection (jx_epilogue.pn_*): the activation rows it writes
+    match jx_norm's (same arithmetic, another float32 summation order: at most one bf16 ulp on a few
+    elements), the projection of them matches the projection of jx_norm's output, and the epoch and
+    arrival counters advance and reset over back-to-back calls."""
+    N = _n()
+    torch.manual_seed(11)
+    d, Nn, Mp = 4096, 6144, 16
+    knd = {"rms": N.JX_NORM_RMS, "gemma": N.JX_NORM_GEMMA, "layer": N.JX_NORM_LAYER}[kind]
+    h = (2 * torch.randn(M, d, device="cuda")).to(torch.bfloat16)
+    w = (1 + 0.1 * torch.randn(d, device="cuda")).to(torch.bfloat16)
+    b = (0.1 * torch.randn(d, device="cuda")).to(torch.bfloat16) if kind == "layer" else None
+    wt = (torch.randn(Nn, d, device="cuda") * 0.02).to(torch.bfloat16)
+    wp = _pack(N, wt, Nn, d)
+    ws, cnt = _ws(N, Nn)
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    # reference: jx_norm into the K128 activations, then the projection
+    xn_ref = torch.zeros(Mp * d, dtype=torch.bfloat16, device="cuda")
+    a = N.JxNormArgs()
+    a.M, a.d, a.eps, a.kind = M, d, 1e-5, knd
+    a.h, a.ldh, a.w, a.b = h.data_ptr(), d, w.data_ptr(), None if b is None else b.data_ptr()
+    a.out, a.ldo, a.out_rp, a.status = xn_ref.data_ptr(), d, Mp, status.data_ptr()
+    N.call("jx_norm", a, N.JX_BF16, 0, _stream())
+    out_ref = torch.zeros(M, Nn, dtype=torch.bfloat16, device="cuda")
+    e = _epi(N, N.JX_EPI_STORE, M, Nn, out_ref, Nn)
+    N.call("jx_linear_decode", wp.data_ptr(), xn_ref.data_ptr(), Nn, d, M, e, ws.data_ptr(), ws.numel(),
+           cnt.data_ptr(), status.data_ptr(), 148, 1, _stream())
+    # prologue
+    sync = torch.zeros(18, dtype=torch.int32, device="cuda")
+    xn = torch.zeros(Mp * d, dtype=torch.bfloat16, device="cuda")
+    out = torch.zeros(M, Nn, dtype=torch.bfloat16, device="cuda")
+    e2 = _epi(N, N.JX_EPI_STORE, M, Nn, out, Nn)
+    e2.pn_h, e2.pn_ldh, e2.pn_w, e2.pn_b = h.data_ptr(), d, w.data_ptr(), None if b is None else b.data_ptr()
+    e2.pn_sync, e2.pn_kind, e2.pn_d, e2.pn_eps = sync.data_ptr(), knd, d, 1e-5
+    for rep in range(3):
+        xn.zero_()
+        N.call("jx_linear_decode", wp.data_ptr(), xn.data_ptr(), Nn, d, M, e2, ws.data_ptr(), ws.numel(),
+               cnt.data_ptr(), status.data_ptr(), 148, 1, _stream())
+        torch.cuda.synchronize()
+        assert int(status.item()) == 0
+        assert sync[0].item() == rep + 1 and sync[1].item() == 0 and int(cnt.abs().sum().item()) == 0
+        got = torch.empty(M, d, dtype=torch.bfloat16, device="cuda")
+        ref = torch.empty(M, d, dtype=torch.bfloat16, device="cuda")
+        N.call("jx_unpack_k128", xn.data_ptr(), M, d, Mp, got.data_ptr(), N.JX_BF16, d, _stream())
+        N.call("jx_unpack_k128", xn_ref.data_ptr(), M, d, Mp, ref.data_ptr(), N.JX_BF16, d, _stream())
+        torch.cuda.synchronize()
+        diff = (got.float() - ref.float()).abs()
+        ulp = torch.exp2(torch.floor(torch.log2(ref.float().abs().clamp_min(1e-30))) - 7)
+        assert bool((diff <= ulp + 1e-12).all()) and (diff > 0).float().mean().item() <= 0.01
+        err = (out.float() - out_ref.float()).abs().max().item()
+        assert err <= 2e-2 * max(1.0, out_ref.float().abs().max().item()), err
+        if bool((diff == 0).all()):
+            assert torch.equal(out, out_ref)
