@@ -85,3 +85,26 @@ def test_decode_attention_rejects_an_output_too_small_for_the_batch():
         assert lib.jx_set_prefill_linear_impl(impl) == (N.JX_OK if impl <= 2 else N.JX_ERR_ARG)
     lib.jx_set_decode_attention_impl(0)
     lib.jx_set_prefill_linear_impl(0)
+
+
+def test_comm_layout_regions_do_not_overlap():
+    """jx_comm_layout (host only): every part of a rank's peer region (header with the all-reduce flags,
+    counters, push epoch, bases table and push flags; two pull buffers; 2 x world push receive slots) is
+    16-byte aligned, large enough and disjoint, for each world size and message size."""
+    lib = N.load()
+    for world in (1, 2, 4, 8):
+        for max_floats in (4, 1000, 64 * 8192):
+            out = (N.LL * 10)()
+            assert lib.jx_comm_layout(max_floats, world, out) == N.JX_OK
+            size, b0, b1, recv, stride, flags, flag_set, seq, bases, units = list(out)
+            assert units == 256 and flag_set == 256 * 8 * 4 and stride >= 4 * max_floats
+            parts = [(seq, 8), (bases, 8 * world), (flags, 2 * flag_set), (b0, 4 * max_floats), (b1, 4 * max_floats)]
+            parts += [(recv + i * stride, 4 * max_floats) for i in range(2 * world)]
+            for off, n in parts:
+                assert off % 16 == 0 and off + n <= size
+            spans = sorted(parts)
+            for (o1, n1), (o2, _) in zip(spans, spans[1:]):
+                assert o1 + n1 <= o2, (world, max_floats, spans)
+    bad = (N.LL * 10)()
+    assert lib.jx_comm_layout(0, 2, bad) == N.JX_ERR_ARG
+    assert lib.jx_comm_layout(16, 9, bad) == N.JX_ERR_ARG
