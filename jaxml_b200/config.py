@@ -124,10 +124,22 @@ class ModelConfig:
             kind = "gemma3"
         else:
             raise ValueError(f"Unsupported config class {config.__class__}")
-        hidden = normalize_count("hidden_size", config.hidden_size)
-        inter = normalize_count("intermediate_size", config.intermediate_size)
+        # shared fields, validated under their HF names before anything is derived from them
+        hidden = _hf_count("hidden_size", config.hidden_size)
+        inter = _hf_count("intermediate_size", config.intermediate_size)
         factor = math.gcd(inter, hidden)
-        head_dim = getattr(config, "head_dim", None) or hidden // config.num_attention_heads
+        head_dim = getattr(config, "head_dim", None)
+        if head_dim is not None:
+            head_dim = _hf_count("head_dim", head_dim)
+        else:
+            heads = _hf_count("num_attention_heads", config.num_attention_heads)
+            if hidden % heads:
+                raise ValueError("hidden_size must be divisible by num_attention_heads when head_dim is not set.")
+            head_dim = hidden // heads
+        num_heads = _hf_count("num_attention_heads", config.num_attention_heads)
+        num_layers = _hf_count("num_hidden_layers", config.num_hidden_layers)
+        max_pos = _hf_count("max_position_embeddings", config.max_position_embeddings)
+        vocab = _hf_count("vocab_size", config.vocab_size)
         rope = _hf_rope_parameters(config, "full_attention" if kind == "gemma3" else None)
         rope_theta = float(rope.get("rope_theta", getattr(config, "rope_theta", None)
                                     or getattr(config, "rotary_emb_base", None) or 10000.0))
@@ -139,10 +151,10 @@ class ModelConfig:
                   sliding_window_pattern=None)
         if kind == "llama":
             norm_eps = config.rms_norm_eps
-            num_kv = config.num_key_value_heads
+            num_kv = _hf_count("num_key_value_heads", config.num_key_value_heads)
         elif kind == "gpt_neox":
             norm_eps = config.layer_norm_eps
-            num_kv = config.num_attention_heads
+            num_kv = num_heads
             rotary_pct = getattr(config, "rotary_pct", None)
             if rotary_pct is None:
                 rotary_pct = rope.get("partial_rotary_factor", 1.0)
@@ -150,15 +162,29 @@ class ModelConfig:
                       use_bias=True)
             rope_scale = 1.0
         else:
-            attn_scale = float(config.query_pre_attn_scalar) ** -0.5
+            qpas = normalize_float("query_pre_attn_scalar", config.query_pre_attn_scalar)
+            if qpas <= 0:
+                raise ValueError(f"query_pre_attn_scalar must be positive, got {qpas}.")
+            attn_scale = qpas ** -0.5
             norm_eps = config.rms_norm_eps
-            num_kv = config.num_key_value_heads
+            num_kv = _hf_count("num_key_value_heads", config.num_key_value_heads)
             kw.update(sliding_window=config.sliding_window, sliding_window_pattern=_gemma_pattern(config))
-        return cls(hidden_size=hidden, head_dim=head_dim, num_heads=config.num_attention_heads,
-                   num_layers=config.num_hidden_layers, max_position_embeddings=config.max_position_embeddings,
-                   vocab_size=config.vocab_size, intermediate_ratio=(inter // factor, hidden // factor),
+        pct = kw["rotary_pct"]
+        if (head_dim if pct >= 1.0 else int(head_dim * pct)) <= 0:
+            raise ValueError(f"rotary_pct must produce a positive rotary dimension, got rotary_pct={pct} and "
+                             f"head_dim={head_dim}.")
+        return cls(hidden_size=hidden, head_dim=head_dim, num_heads=num_heads,
+                   num_layers=num_layers, max_position_embeddings=max_pos,
+                   vocab_size=vocab, intermediate_ratio=(inter // factor, hidden // factor),
                    norm_eps=norm_eps, num_kv_heads=num_kv, use_rope=True, rope_theta=rope_theta,
                    rope_scale=rope_scale, attn_scale=attn_scale, **kw)
+
+
+def _hf_count(name: str, value) -> int:
+    value = normalize_count(name, value)
+    if value <= 0:
+        raise ValueError(f"{name} must be positive, got {value}.")
+    return value
 
 
 def _hf_rope_parameters(config, kind):

@@ -80,3 +80,78 @@ def test_non_boolean_flags(field):
 def test_invalid_invariants(overrides, match):
     with pytest.raises(ValueError, match=match):
         ModelConfig(**_kw(**overrides))
+
+
+# ---- ModelConfig.from_hf (the reference's from_hf cases; transformers configs only, no weights) ----
+def _llama_hf(**kw):
+    from transformers import LlamaConfig
+
+    return LlamaConfig(**({"hidden_size": 48, "intermediate_size": 144, "num_hidden_layers": 2,
+                           "max_position_embeddings": 256, "vocab_size": 1024, "num_attention_heads": 6,
+                           "num_key_value_heads": 3} | kw))
+
+
+def test_from_hf_llama_subclass_and_fields():
+    from transformers import LlamaConfig
+
+    class CustomLlamaConfig(LlamaConfig):
+        pass
+
+    hf = CustomLlamaConfig(hidden_size=48, intermediate_size=144, num_hidden_layers=2, max_position_embeddings=256,
+                           vocab_size=1024, num_attention_heads=6, num_key_value_heads=3, rope_theta=5000.0,
+                           rms_norm_eps=1e-5)
+    c = ModelConfig.from_hf(hf)
+    assert (c.hidden_size, c.head_dim, c.num_heads, c.num_key_value_heads, c.intermediate_size) == (48, 8, 6, 3, 144)
+    assert c.rope_theta == 5000.0 and c.norm_eps == 1e-5
+    hf = _llama_hf()
+    object.__setattr__(hf, "head_dim", np.int64(8))
+    assert ModelConfig.from_hf(hf).head_dim == 8
+
+
+@pytest.mark.parametrize("head_dim,exc,match", [(0, ValueError, "head_dim must be positive"),
+                                                (-1, ValueError, "head_dim must be positive"),
+                                                (True, TypeError, "head_dim must be an integer"),
+                                                (1.5, TypeError, "head_dim must be an integer")])
+def test_from_hf_invalid_head_dim(head_dim, exc, match):
+    hf = _llama_hf()
+    object.__setattr__(hf, "head_dim", head_dim)
+    with pytest.raises(exc, match=match):
+        ModelConfig.from_hf(hf)
+
+
+def test_from_hf_non_divisible_head_dim_fallback():
+    hf = _llama_hf()
+    object.__setattr__(hf, "hidden_size", 50)
+    object.__setattr__(hf, "intermediate_size", 150)
+    object.__setattr__(hf, "head_dim", None)
+    with pytest.raises(ValueError, match="hidden_size must be divisible"):
+        ModelConfig.from_hf(hf)
+
+
+@pytest.mark.parametrize("field,value,exc,match", [
+    ("hidden_size", True, TypeError, "hidden_size must be an integer"),
+    ("hidden_size", 0, ValueError, "hidden_size must be positive"),
+    ("intermediate_size", np.bool_(True), TypeError, "intermediate_size must be an integer"),
+    ("intermediate_size", 0, ValueError, "intermediate_size must be positive"),
+    ("num_attention_heads", True, TypeError, "num_attention_heads must be an integer"),
+    ("num_attention_heads", 0, ValueError, "num_attention_heads must be positive"),
+    ("num_hidden_layers", np.bool_(True), TypeError, "num_hidden_layers must be an integer"),
+    ("num_hidden_layers", 0, ValueError, "num_hidden_layers must be positive"),
+    ("max_position_embeddings", 1.5, TypeError, "max_position_embeddings must be an integer"),
+    ("max_position_embeddings", 0, ValueError, "max_position_embeddings must be positive"),
+    ("vocab_size", "1024", TypeError, "vocab_size must be an integer"),
+    ("vocab_size", 0, ValueError, "vocab_size must be positive"),
+    ("num_key_value_heads", True, TypeError, "num_key_value_heads must be an integer"),
+    ("num_key_value_heads", 0, ValueError, "num_key_value_heads must be positive"),
+])
+def test_from_hf_invalid_fields(field, value, exc, match):
+    hf = _llama_hf()
+    object.__setattr__(hf, "head_dim", 8)
+    object.__setattr__(hf, field, value)
+    with pytest.raises(exc, match=match):
+        ModelConfig.from_hf(hf)
+
+
+def test_from_hf_unsupported_config():
+    with pytest.raises(ValueError, match="Unsupported config class"):
+        ModelConfig.from_hf(object())
