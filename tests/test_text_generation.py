@@ -83,3 +83,71 @@ def test_pipeline_rejects_bad_inputs():
             return np.zeros((1, 1), dtype=np.int32)
     with pytest.raises(ValueError, match="token length must match"):
         TextGenerationPipeline(_BadEngine(), _Tok()).generate_tokens("abc", max_new_tokens=4)
+
+
+class _Static:
+    """Tokenizer returning a fixed encoding (records calls)."""
+
+    def __init__(self, encoded):
+        self.encoded, self.calls = encoded, 0
+
+    def __call__(self, texts, **kw):
+        self.calls += 1
+        return self.encoded
+
+    def batch_decode(self, tokens, **kw):
+        return ["x"] * len(tokens)
+
+
+@pytest.mark.parametrize("kwargs,exc,match", [
+    ({"max_new_tokens": True}, TypeError, "max_new_tokens must be an integer"),
+    ({"max_new_tokens": -1}, ValueError, "max_new_tokens must be non-negative"),
+    ({"top_k": -1}, ValueError, "top_k must be non-negative"),
+    ({"include_prompt": 1}, TypeError, "include_prompt must be a boolean"),
+    ({"seed": True}, TypeError, "seed must be an integer"),
+    ({"temperature": np.nan}, ValueError, "temperature must be finite"),
+    ({"fuse_decoding": 1}, TypeError, "fuse_decoding must be a boolean"),
+    ({"unknown_option": 1}, TypeError, "unexpected keyword argument"),
+])
+def test_generation_overrides_are_validated_before_tokenizing(kwargs, exc, match):
+    tok, eng = _Static({"input_ids": np.ones((1, 2), dtype=np.int32)}), _Engine()
+    pipe = TextGenerationPipeline(eng, tok)
+    for fn in (pipe.generate_tokens, pipe.generate_text):
+        with pytest.raises(exc, match=match):
+            fn("hello", **kwargs)
+    assert tok.calls == 0 and eng.calls == []
+
+
+def test_kwargs_mappings_are_validated_before_tokenizing():
+    tok, eng = _Static({"input_ids": np.ones((1, 2), dtype=np.int32)}), _Engine()
+    pipe = TextGenerationPipeline(eng, tok)
+    with pytest.raises(TypeError, match="tokenize_kwargs must be a mapping"):
+        pipe.generate_tokens("hello", tokenize_kwargs=["padding"])
+    with pytest.raises(TypeError, match="decode_kwargs must be a mapping"):
+        pipe.generate_text("hello", decode_kwargs=["skip_special_tokens"])
+    assert tok.calls == 0 and eng.calls == []
+
+
+@pytest.mark.parametrize("encoded,exc,match", [
+    ({"input_ids": np.ones((2,), dtype=np.int32)}, ValueError, "input_ids must be a 2D array"),
+    ({"input_ids": np.ones((1, 2), dtype=np.float32)}, TypeError, "integer token ids"),
+    ({"input_ids": np.ones((0, 2), dtype=np.int32)}, ValueError, "at least one batch row"),
+    ({"input_ids": np.ones((1, 0), dtype=np.int32)}, ValueError, "at least one token"),
+    ({"input_ids": np.array([[1, -1]], dtype=np.int32)}, ValueError, "token ids must be non-negative"),
+    ({"input_ids": np.ones((1, 2), dtype=np.int32), "attention_mask": np.ones((2,), dtype=np.int32)},
+     ValueError, "attention_mask must be a 2D array"),
+    ({"input_ids": np.ones((1, 2), dtype=np.int32), "attention_mask": np.ones((1, 2), dtype=np.float32)},
+     TypeError, "attention_mask must be boolean or integer"),
+    ({"input_ids": np.ones((1, 2), dtype=np.int32), "attention_mask": np.ones((1, 3), dtype=np.int32)},
+     ValueError, "attention_mask shape must match"),
+    ({"input_ids": np.ones((1, 2), dtype=np.int32), "attention_mask": np.zeros((1, 2), dtype=np.int32)},
+     ValueError, "at least one valid token"),
+    ({"input_ids": np.ones((1, 2), dtype=np.int32), "attention_mask": np.array([[1, 2]], dtype=np.int32)},
+     ValueError, "integer values must be 0 or 1"),
+    ({}, ValueError, "tokenizer output must contain 'input_ids'"),
+])
+def test_tokenizer_arrays_are_validated_before_generation(encoded, exc, match):
+    tok, eng = _Static(encoded), _Engine()
+    with pytest.raises(exc, match=match):
+        TextGenerationPipeline(eng, tok).generate_tokens("hello")
+    assert tok.calls == 1 and eng.calls == []
