@@ -7,6 +7,9 @@ random parameter tree in the reference's Flax layout.
 """
 from __future__ import annotations
 
+from dataclasses import dataclass
+from typing import Optional
+
 import torch
 
 from ._checks import normalize_dtype
@@ -54,8 +57,82 @@ class _DecoderWithHead:
         """Random N(0, std) kernels, unit norm weights, in the reference's parameter layout."""
         return random_params(self.family, self.config, seed=seed, std=std)
 
+    def apply(self, params, input_ids, attention_mask=None, position_ids=None, kv_caches=None, use_cache=False,
+              output_attentions=False, output_hidden_states=False, keep_last_n_logits: int = 0):
+        """``*ModelWithHead.__call__`` (models/llama.py:247-273, gpt_neox.py:245-272, gemma3.py:304-331)
+        on the GPU kernels for a cache-free forward: logits ``[B, S]`` (or the last ``keep_last_n_logits``
+        positions) in the model dtype, in a ``CausalLMOutputWithCache``.  Right-padded masks; token ids
+        below 0 read row 0 like the reference.  Cached decoding, position ids, per-layer hidden states
+        and attention weights are the Engine's business here and raise ``NotImplementedError``."""
+        import numpy as np
+
+        from ._checks import normalize_bool, normalize_count
+
+        use_cache = normalize_bool("use_cache", use_cache)
+        output_attentions = normalize_bool("output_attentions", output_attentions)
+        output_hidden_states = normalize_bool("output_hidden_states", output_hidden_states)
+        keep = normalize_count("keep_last_n_logits", keep_last_n_logits)
+        if keep < 0:
+            raise ValueError(f"keep_last_n_logits must be non-negative, got {keep}.")
+        if kv_caches is not None or use_cache or position_ids is not None:
+            raise NotImplementedError("apply with KV caches or position ids: use Engine.generate for cached decoding.")
+        if output_attentions or output_hidden_states:
+            raise NotImplementedError("apply does not return attention weights or per-layer hidden states.")
+        ids = input_ids if isinstance(input_ids, torch.Tensor) else torch.as_tensor(np.asarray(input_ids))
+        if ids.ndim == 1:
+            ids = ids[None]
+        if ids.ndim != 2 or ids.numel() == 0:
+            raise ValueError(f"input_ids must be a non-empty [batch, length] array, got shape {tuple(ids.shape)}.")
+        if ids.is_floating_point() or ids.dtype == torch.bool:
+            raise TypeError(f"input_ids must contain integer token ids, got dtype {ids.dtype}.")
+        if bool((ids >= self.config.vocab_size).any()):
+            raise ValueError(f"input_ids must be below vocab_size={self.config.vocab_size}.")
+        ids = torch.where(ids < 0, torch.zeros_like(ids), ids).to(torch.int32)
+        B, S = ids.shape
+        mask = torch.ones(B, S, dtype=torch.bool) if attention_mask is None else (
+            attention_mask if isinstance(attention_mask, torch.Tensor) else torch.as_tensor(np.asarray(attention_mask)))
+        if mask.ndim == 1:
+            mask = mask[None]
+        mask = mask.to(torch.bool)
+        if tuple(mask.shape) != (B, S):
+            raise ValueError(f"attention_mask shape must match input_ids, got {tuple(mask.shape)} and {(B, S)}.")
+        if S > 1 and bool((mask[:, :-1].to(torch.int8) < mask[:, 1:].to(torch.int8)).any()):
+            raise NotImplementedError("apply takes right-padded attention masks (the kernels attend to key prefixes).")
+        rt = self._runtime(params, B, S)
+        dev = rt.w.device
+        logits = rt.forward_logits(ids.to(dev), mask.to(dev), keep)
+        return CausalLMOutputWithCache(logits=logits)
+
+    def _runtime(self, params, B: int, S: int):
+        """Packed weights (cached per parameter tree) and a runtime sized for B rows of S tokens."""
+        from .runtime import DecoderRuntime, ModelWeights
+
+        dev = torch.device("cuda", torch.cuda.current_device())
+        cache = self.__dict__.setdefault("_apply_cache", {})
+        key = (id(params), dev.index)
+        if cache.get("key") != key:
+            cache.clear()
+            cache["key"] = key
+            cache["params"] = params   # keeps the tree alive while its id is the cache key
+            cache["weights"] = ModelWeights(self.family, self.config, params, self.dtype, dev)
+        T = ((S + 255) // 256) * 256
+        rt = cache.get("rt")
+        if rt is None or rt.B != B or rt.T < T:
+            cache["rt"] = rt = DecoderRuntime(cache["weights"], B, T)
+        return rt
+
     def __repr__(self) -> str:
         return f"{type(self).__name__}(config={self.config!r}, dtype={self.dtype})"
+
+
+@dataclass
+class CausalLMOutputWithCache:
+    """``outputs.py``: logits, and (not produced by ``apply`` here) caches, hidden states, weights."""
+
+    logits: torch.Tensor
+    kv_caches: Optional[tuple] = None
+    hidden_states: Optional[tuple] = None
+    attention_weights: Optional[tuple] = None
 
 
 class LlamaModelWithHead(_DecoderWithHead):

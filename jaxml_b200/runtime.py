@@ -783,6 +783,33 @@ class DecoderRuntime:
         self._head(acts, rm)
         self._sample(greedy, temp, update_pos=False)
 
+    def forward_logits(self, ids: torch.Tensor, prompt_mask: torch.Tensor, keep: int = 0) -> torch.Tensor:
+        """The reference's ``*ModelWithHead.__call__`` without a cache (models/llama.py:247-273): the rows
+        [B, P] (device int32, right-padded ``prompt_mask``) through the stack, then the final norm and the
+        LM head over the last ``keep`` positions of every row (all P when ``keep`` is 0).  Returns logits
+        [B, kept, V] in the model dtype.  Single GPU only."""
+        if self.comm is not None:
+            raise NotImplementedError("forward_logits under tensor parallelism (the Engine path covers it).")
+        W = self.w
+        B, P = ids.shape
+        self.reset(prompt_mask, np.zeros(2, np.uint32), np.zeros(2, np.uint32), 1)
+        acts = self._prefill_acts(B * P)
+        self.k_cache.zero_()
+        self.v_cache.zero_()
+        self._input_norm(acts, W.layers[0], ids=ids.reshape(-1).contiguous())
+        self._layers(acts, P, decode=False)
+        n = P if keep <= 0 else min(keep, P)
+        dev = ids.device
+        rows = (torch.arange(B, device=dev)[:, None] * P + torch.arange(P - n, P, device=dev)[None]).reshape(-1)
+        M2 = B * n
+        out_acts = self._alloc_acts(M2, _rup(M2, 128) if W.bf16 else M2)
+        fw, fb = W.final_norm
+        self._norm(acts, w=fw, b=fb, row_map=rows.to(torch.int32).contiguous(), M=M2, out_acts=out_acts)
+        logits = torch.empty(M2, W.V, dtype=W.dtype, device=dev)
+        self._linear(out_acts, W.lm_head, W.Np_v, W.Kp_d, "xn", N.JX_EPI_STORE, N_valid=W.V, out=logits, ldo=W.V,
+                     K_logical=W.d, N_cols=W.V)
+        return logits.view(B, n, W.V)
+
     def decode_step(self, greedy: bool, temp: float):
         self._launches = 0
         acts = self.dec
