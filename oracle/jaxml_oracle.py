@@ -1,7 +1,7 @@
 """Oracle (test infrastructure only): jaxml's decoder math restated on torch CPU tensors.
 
 Only ``tests/``, ``__graft_entry__.smoke()`` and the CPU-baseline leg of ``bench.py`` import this
-module, and only as the checker; the product path never calls it.
+module, and only to compare against; the product path never calls it.
 
 Every function follows the reference's JAX/Flax code op by op, including where it rounds to the
 model dtype (bfloat16 configs round after every op; float32 configs are plain float32):

@@ -1,7 +1,7 @@
 """Oracle (test infrastructure only): JAX's threefry PRNG and categorical sampling, restated in numpy.
 
 Only tests, ``__graft_entry__.smoke()`` and the CPU-baseline leg of ``bench.py`` use this module,
-and only as the checker. The product samples on the GPU (``jaxml_b200/csrc/sample.cu``).
+and only to compare against. The product samples on the GPU (``jaxml_b200/csrc/sample.cu``).
 
 What the reference calls (JAX 0.10.1, pinned in ``pyproject.toml:14`` / ``uv.lock:245-246`` of the
 reference; JAX itself is not in the reference tree and is not installed here):
