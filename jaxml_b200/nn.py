@@ -190,7 +190,9 @@ def _packed_weight(w_kn: torch.Tensor, Np: int, Kp: int) -> torch.Tensor:
     K, Nn = w_kn.shape
     packed = _pack(w_kn, Nn, K, Nn, 1, Np, Kp)
     _PACKED[key] = (w_kn, packed)        # holds the source so its address is not reused while cached
-    while len(_PACKED) > 64:
+    # least recently used first out, beyond 64 entries or 2 GiB of packed weights
+    while len(_PACKED) > 1 and (len(_PACKED) > 64 or
+                                sum(v[1].numel() * 2 for v in _PACKED.values()) > (2 << 30)):
         _PACKED.popitem(last=False)
     return packed
 
