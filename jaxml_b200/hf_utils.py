@@ -12,7 +12,7 @@ from collections.abc import Mapping
 
 import torch
 
-from ._checks import normalize_dtype
+from ._checks import normalize_count, normalize_dtype
 
 _NORM_KEYS = {"post_attention_layernorm", "pre_feedforward_layernorm", "post_feedforward_layernorm",
               "input_layernorm", "norm", "q_norm", "k_norm"}
@@ -72,17 +72,49 @@ def torch_to_jax_states(states, dtype=torch.float32, head_dim: int | None = None
     return tree
 
 
+def _positive(name: str, value) -> int:
+    value = normalize_count(name, value)
+    if value <= 0:
+        raise ValueError(f"{name} must be positive, got {value}.")
+    return value
+
+
 def _head_dim(config) -> int:
+    """The config's head_dim, else hidden_size / num_attention_heads (validated like the reference)."""
     hd = getattr(config, "head_dim", None)
-    return hd if hd else config.hidden_size // config.num_attention_heads
+    if hd is not None:
+        return _positive("head_dim", hd)
+    hidden = _positive("hidden_size", config.hidden_size)
+    heads = _positive("num_attention_heads", config.num_attention_heads)
+    if hidden % heads:
+        raise ValueError("hidden_size must be divisible by num_attention_heads when head_dim is not set.")
+    return hidden // heads
+
+
+def _model_states(model, what: str):
+    """(config, state dict) of an HF-like model, checked before any conversion."""
+    config = getattr(model, "config", None)
+    if config is None:
+        raise ValueError(f"Expected the {what} model to expose a config.")
+    sd = getattr(model, "state_dict", None)
+    if not callable(sd):
+        raise TypeError(f"Expected the {what} model to provide a callable state_dict.")
+    states = sd()
+    if not isinstance(states, Mapping):
+        raise TypeError(f"The {what} model's state_dict must be a mapping, got {type(states)}.")
+    if not states:
+        raise ValueError("PyTorch state dict must contain at least one tensor.")
+    return config, states
 
 
 def to_llama_jax_params(model, dtype=torch.float32) -> dict:
-    return torch_to_jax_states(model.state_dict(), dtype=dtype, head_dim=_head_dim(model.config))
+    config, states = _model_states(model, "Llama")
+    return torch_to_jax_states(states, dtype=dtype, head_dim=_head_dim(config))
 
 
 def to_gemma_jax_params(model, dtype=torch.float32) -> dict:
-    return torch_to_jax_states(model.state_dict(), dtype=dtype, head_dim=_head_dim(model.config))
+    config, states = _model_states(model, "Gemma")
+    return torch_to_jax_states(states, dtype=dtype, head_dim=_head_dim(config))
 
 
 _NEOX_SUB = (
@@ -98,13 +130,16 @@ _NEOX_SUB = (
 
 
 def to_neox_jax_params(model, dtype=torch.float32) -> dict:
-    renamed = {}
-    for key, value in model.state_dict().items():
+    config, states = _model_states(model, "GPT-NeoX")
+    renamed, origin = {}, {}
+    for key, value in states.items():
         name = key
         for pat, rep in _NEOX_SUB:
             name = re.sub(pat, rep, name)
-        renamed[name] = value
-    return torch_to_jax_states(renamed, dtype=dtype, head_dim=_head_dim(model.config))
+        if name in renamed:
+            raise ValueError(f"State keys {origin[name]!r} and {key!r} map to the same jaxml destination {name!r}.")
+        renamed[name], origin[name] = value, key
+    return torch_to_jax_states(renamed, dtype=dtype, head_dim=_head_dim(config))
 
 
 # ------------------------------------------------------------------------------------------------

@@ -1,0 +1,77 @@
+"""HF state dict -> reference parameter tree conversion checks (the reference's
+``tests/test_hf_utils.py`` conversion cases), CPU only."""
+from types import SimpleNamespace
+
+import numpy as np
+import pytest
+import torch
+
+from jaxml_b200.hf_utils import to_gemma_jax_params, to_llama_jax_params, to_neox_jax_params
+
+
+class _Fake:
+    def __init__(self, config, states=None):
+        self.config = config
+        self.states = states if states is not None else {
+            f"{n}.weight": torch.arange(32, dtype=torch.float32).reshape(4, 8) for n in ("q_proj", "k_proj", "v_proj")}
+
+    def state_dict(self):
+        return self.states
+
+
+def test_head_dim_fallbacks():
+    p = to_llama_jax_params(_Fake(SimpleNamespace(hidden_size=8, num_attention_heads=2)))
+    assert p["params"]["q_proj"]["kernel"].shape == (8, 1, 4)
+    p = to_gemma_jax_params(_Fake(SimpleNamespace(hidden_size=8, num_attention_heads=2, head_dim=None)))
+    assert p["params"]["k_proj"]["kernel"].shape == (8, 1, 4)
+    p = to_llama_jax_params(_Fake(SimpleNamespace(hidden_size=8, num_attention_heads=2, head_dim=np.int64(4))))
+    assert p["params"]["q_proj"]["kernel"].shape == (8, 1, 4)
+    p = to_neox_jax_params(_Fake(SimpleNamespace(hidden_size=8, num_attention_heads=2, head_dim=None)))
+    assert p["params"]["q_proj"]["kernel"].shape == (8, 1, 4)
+
+
+def test_model_surface_is_checked():
+    with pytest.raises(ValueError, match="Llama model to expose a config"):
+        to_llama_jax_params(SimpleNamespace(state_dict=lambda: {}))
+    cfg = SimpleNamespace(hidden_size=8, num_attention_heads=2)
+    with pytest.raises(TypeError, match="callable state_dict"):
+        to_llama_jax_params(SimpleNamespace(config=cfg))
+    with pytest.raises(TypeError, match="state_dict must be a mapping"):
+        to_llama_jax_params(SimpleNamespace(config=cfg, state_dict=lambda: []))
+    with pytest.raises(ValueError, match="state dict must contain at least one tensor"):
+        to_llama_jax_params(SimpleNamespace(config=cfg, state_dict=lambda: {}))
+
+
+@pytest.mark.parametrize("head_dim,exc,match", [(0, ValueError, "head_dim must be positive"),
+                                                (-1, ValueError, "head_dim must be positive"),
+                                                (True, TypeError, "head_dim must be an integer"),
+                                                (np.bool_(True), TypeError, "head_dim must be an integer"),
+                                                (1.5, TypeError, "head_dim must be an integer")])
+def test_invalid_head_dim(head_dim, exc, match):
+    with pytest.raises(exc, match=match):
+        to_llama_jax_params(_Fake(SimpleNamespace(hidden_size=8, num_attention_heads=2, head_dim=head_dim)))
+
+
+@pytest.mark.parametrize("cfg,match", [
+    (SimpleNamespace(hidden_size=10, num_attention_heads=3), "hidden_size must be divisible"),
+    (SimpleNamespace(hidden_size=8.0, num_attention_heads=2), "hidden_size must be an integer"),
+    (SimpleNamespace(hidden_size=8, num_attention_heads=True), "num_attention_heads must be an integer"),
+    (SimpleNamespace(hidden_size=0, num_attention_heads=2), "hidden_size must be positive"),
+    (SimpleNamespace(hidden_size=8, num_attention_heads=0), "num_attention_heads must be positive"),
+])
+def test_invalid_head_dim_fallback(cfg, match):
+    with pytest.raises((TypeError, ValueError), match=match):
+        to_llama_jax_params(_Fake(cfg))
+
+
+def test_neox_renames_without_mutating_and_rejects_collisions():
+    cfg = SimpleNamespace(hidden_size=8, num_attention_heads=2, head_dim=None)
+    model = _Fake(cfg, {"gpt_neox.embed_in.weight": torch.arange(32, dtype=torch.float32).reshape(4, 8),
+                        "gpt_neox.final_layer_norm.weight": torch.arange(8, dtype=torch.float32)})
+    p = to_neox_jax_params(model)
+    assert "embed_tokens" in p["params"]["gpt_neox"] and "norm" in p["params"]["gpt_neox"]
+    assert set(model.states) == {"gpt_neox.embed_in.weight", "gpt_neox.final_layer_norm.weight"}
+    clash = _Fake(cfg, {"gpt_neox.layers.0.attention.dense.weight": torch.zeros(8, 8),
+                        "gpt_neox.layers.0.self_attn.o_proj.weight": torch.zeros(8, 8)})
+    with pytest.raises(ValueError, match="map to the same jaxml destination"):
+        to_neox_jax_params(clash)
