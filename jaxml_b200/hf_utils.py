@@ -176,7 +176,14 @@ def _normalize_hf_model_name(name) -> str:
 
 
 def _validate_hf_dtype(dtype):
-    if not isinstance(dtype, str) or dtype.lower() not in _HF_DTYPES:
+    if isinstance(dtype, torch.dtype):
+        name = str(dtype).replace("torch.", "")
+        if name not in _HF_DTYPES:
+            raise ValueError(f"Unsupported dtype {dtype!r}; expected one of {sorted(_HF_DTYPES)}.")
+        return name
+    if not isinstance(dtype, str):
+        raise TypeError(f"Expected dtype to be a string such as 'float32' or 'bfloat16', got {dtype!r}.")
+    if dtype.lower() not in _HF_DTYPES:
         raise ValueError(f"Unsupported dtype {dtype!r}; expected one of {sorted(_HF_DTYPES)}.")
     return dtype
 

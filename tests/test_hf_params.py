@@ -75,3 +75,31 @@ def test_neox_renames_without_mutating_and_rejects_collisions():
                         "gpt_neox.layers.0.self_attn.o_proj.weight": torch.zeros(8, 8)})
     with pytest.raises(ValueError, match="map to the same jaxml destination"):
         to_neox_jax_params(clash)
+
+
+@pytest.mark.parametrize("name,exc,match", [("", ValueError, "non-empty"), ("   ", ValueError, "non-empty"),
+                                            (123, TypeError, "string or path-like")])
+def test_load_model_from_hf_rejects_invalid_names_before_loading(name, exc, match):
+    from jaxml_b200.hf_utils import load_model_from_hf
+
+    with pytest.raises(exc, match=match):
+        load_model_from_hf(name)
+
+
+@pytest.mark.parametrize("dtype,exc,match", [(np.float32, TypeError, "Expected dtype"),
+                                             ("bad", ValueError, "Unsupported dtype"),
+                                             (torch.int32, ValueError, "Unsupported dtype")])
+def test_load_model_from_hf_rejects_invalid_dtypes_before_loading(dtype, exc, match):
+    from jaxml_b200.hf_utils import load_model_from_hf
+
+    with pytest.raises(exc, match=match):
+        load_model_from_hf("some/model", dtype=dtype)
+
+
+def test_load_model_from_hf_architecture_argument():
+    from jaxml_b200.hf_utils import load_model_from_hf
+
+    with pytest.raises(ValueError, match="Unsupported"):
+        load_model_from_hf("some/model", architecture="mamba")
+    with pytest.raises(TypeError, match="architecture must be a string"):
+        load_model_from_hf("some/model", architecture=3)
