@@ -14,6 +14,7 @@ import torch
 
 from ._checks import normalize_dtype
 from .config import ModelConfig
+from .nn import GemmaRMSNorm  # noqa: F401  (models/gemma3.py:89-106 lives in jaxml.models)
 
 
 class _DecoderWithHead:
