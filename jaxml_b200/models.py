@@ -79,24 +79,42 @@ class _DecoderWithHead:
             raise NotImplementedError("apply with KV caches or position ids: use Engine.generate for cached decoding.")
         if output_attentions or output_hidden_states:
             raise NotImplementedError("apply does not return attention weights or per-layer hidden states.")
+        # input checks of models/_utils.py:78-177 (same messages), before any device work
         ids = input_ids if isinstance(input_ids, torch.Tensor) else torch.as_tensor(np.asarray(input_ids))
-        if ids.ndim == 1:
-            ids = ids[None]
-        if ids.ndim != 2 or ids.numel() == 0:
-            raise ValueError(f"input_ids must be a non-empty [batch, length] array, got shape {tuple(ids.shape)}.")
-        if ids.is_floating_point() or ids.dtype == torch.bool:
+        if ids.ndim != 2:
+            raise ValueError(f"input_ids must be a 2D array, got shape {tuple(ids.shape)}.")
+        if ids.is_floating_point() or ids.is_complex() or ids.dtype == torch.bool:
             raise TypeError(f"input_ids must contain integer token ids, got dtype {ids.dtype}.")
+        if ids.shape[0] == 0:
+            raise ValueError("input_ids must contain at least one batch row.")
+        if ids.shape[1] == 0:
+            raise ValueError("input_ids must contain at least one token.")
         if bool((ids >= self.config.vocab_size).any()):
-            raise ValueError(f"input_ids must be below vocab_size={self.config.vocab_size}.")
-        ids = torch.where(ids < 0, torch.zeros_like(ids), ids).to(torch.int32)
+            raise ValueError(f"input_ids token ids must be less than vocab_size={self.config.vocab_size}.")
         B, S = ids.shape
-        mask = torch.ones(B, S, dtype=torch.bool) if attention_mask is None else (
-            attention_mask if isinstance(attention_mask, torch.Tensor) else torch.as_tensor(np.asarray(attention_mask)))
-        if mask.ndim == 1:
-            mask = mask[None]
-        mask = mask.to(torch.bool)
-        if tuple(mask.shape) != (B, S):
-            raise ValueError(f"attention_mask shape must match input_ids, got {tuple(mask.shape)} and {(B, S)}.")
+        if attention_mask is None:
+            # negative ids are placeholders: masked out by default
+            mask = ids >= 0
+            if not bool(mask.any(dim=1).all()):
+                raise ValueError("input_ids must contain at least one non-negative token per batch row when "
+                                 "attention_mask is None.")
+        else:
+            mask = attention_mask if isinstance(attention_mask, torch.Tensor) else torch.as_tensor(
+                np.asarray(attention_mask))
+            if mask.ndim != 2:
+                raise ValueError(f"attention_mask must be a 2D array, got shape {tuple(mask.shape)}.")
+            if tuple(mask.shape) != (B, S):
+                raise ValueError(f"attention_mask shape must match input_ids, got {tuple(mask.shape)} and {(B, S)}.")
+            if mask.is_floating_point() or mask.is_complex():
+                raise TypeError(f"attention_mask must be boolean or integer, got dtype {mask.dtype}.")
+            if mask.dtype != torch.bool and bool(((mask != 0) & (mask != 1)).any()):
+                raise ValueError("attention_mask integer values must be 0 or 1.")
+            mask = mask.to(torch.bool)
+            if not bool(mask.any(dim=1).all()):
+                raise ValueError("attention_mask must contain at least one valid token per batch row.")
+            if bool((mask & (ids < 0)).any()):
+                raise ValueError("attention_mask must not mark negative placeholder token ids as valid.")
+        ids = torch.where(ids < 0, torch.zeros_like(ids), ids).to(torch.int32)
         if S > 1 and bool((mask[:, :-1].to(torch.int8) < mask[:, 1:].to(torch.int8)).any()):
             raise NotImplementedError("apply takes right-padded attention masks (the kernels attend to key prefixes).")
         rt = self._runtime(params, B, S)
