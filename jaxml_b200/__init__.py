@@ -9,7 +9,8 @@ from . import nn
 from .cache import KVCache
 from .config import ModelConfig
 from .engine import Engine, InferenceConfig
-from .models import GemmaModelWithHead, GPTNeoXModelWithHead, LlamaModelWithHead
+from .models import (GemmaModel, GemmaModelWithHead, GPTNeoXModel, GPTNeoXModelWithHead, LlamaModel,
+                     LlamaModelWithHead)
 from .sampling import SamplingMethod
 from .text_generation import GenerationConfig, TextGenerationPipeline
 
@@ -24,4 +25,7 @@ __all__ = [
     "LlamaModelWithHead",
     "GPTNeoXModelWithHead",
     "GemmaModelWithHead",
+    "LlamaModel",
+    "GPTNeoXModel",
+    "GemmaModel",
 ]

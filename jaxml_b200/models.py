@@ -79,48 +79,16 @@ class _DecoderWithHead:
             raise NotImplementedError("apply with KV caches or position ids: use Engine.generate for cached decoding.")
         if output_attentions or output_hidden_states:
             raise NotImplementedError("apply does not return attention weights or per-layer hidden states.")
-        # input checks of models/_utils.py:78-177 (same messages), before any device work
-        ids = input_ids if isinstance(input_ids, torch.Tensor) else torch.as_tensor(np.asarray(input_ids))
-        if ids.ndim != 2:
-            raise ValueError(f"input_ids must be a 2D array, got shape {tuple(ids.shape)}.")
-        if ids.is_floating_point() or ids.is_complex() or ids.dtype == torch.bool:
-            raise TypeError(f"input_ids must contain integer token ids, got dtype {ids.dtype}.")
-        if ids.shape[0] == 0:
-            raise ValueError("input_ids must contain at least one batch row.")
-        if ids.shape[1] == 0:
-            raise ValueError("input_ids must contain at least one token.")
-        if bool((ids >= self.config.vocab_size).any()):
-            raise ValueError(f"input_ids token ids must be less than vocab_size={self.config.vocab_size}.")
+        ids, mask = _check_model_inputs(self.config, input_ids, attention_mask)
         B, S = ids.shape
-        if attention_mask is None:
-            # negative ids are placeholders: masked out by default
-            mask = ids >= 0
-            if not bool(mask.any(dim=1).all()):
-                raise ValueError("input_ids must contain at least one non-negative token per batch row when "
-                                 "attention_mask is None.")
-        else:
-            mask = attention_mask if isinstance(attention_mask, torch.Tensor) else torch.as_tensor(
-                np.asarray(attention_mask))
-            if mask.ndim != 2:
-                raise ValueError(f"attention_mask must be a 2D array, got shape {tuple(mask.shape)}.")
-            if tuple(mask.shape) != (B, S):
-                raise ValueError(f"attention_mask shape must match input_ids, got {tuple(mask.shape)} and {(B, S)}.")
-            if mask.is_floating_point() or mask.is_complex():
-                raise TypeError(f"attention_mask must be boolean or integer, got dtype {mask.dtype}.")
-            if mask.dtype != torch.bool and bool(((mask != 0) & (mask != 1)).any()):
-                raise ValueError("attention_mask integer values must be 0 or 1.")
-            mask = mask.to(torch.bool)
-            if not bool(mask.any(dim=1).all()):
-                raise ValueError("attention_mask must contain at least one valid token per batch row.")
-            if bool((mask & (ids < 0)).any()):
-                raise ValueError("attention_mask must not mark negative placeholder token ids as valid.")
-        ids = torch.where(ids < 0, torch.zeros_like(ids), ids).to(torch.int32)
-        if S > 1 and bool((mask[:, :-1].to(torch.int8) < mask[:, 1:].to(torch.int8)).any()):
-            raise NotImplementedError("apply takes right-padded attention masks (the kernels attend to key prefixes).")
         rt = self._runtime(params, B, S)
         dev = rt.w.device
         logits = rt.forward_logits(ids.to(dev), mask.to(dev), keep)
         return CausalLMOutputWithCache(logits=logits)
+
+    def _full_tree(self, params):
+        """The parameter tree the runtime packs (the with-head layout)."""
+        return params
 
     def _runtime(self, params, B: int, S: int):
         """Packed weights (cached per parameter tree) and a runtime sized for B rows of S tokens."""
@@ -133,7 +101,7 @@ class _DecoderWithHead:
             cache.clear()
             cache["key"] = key
             cache["params"] = params   # keeps the tree alive while its id is the cache key
-            cache["weights"] = ModelWeights(self.family, self.config, params, self.dtype, dev)
+            cache["weights"] = ModelWeights(self.family, self.config, self._full_tree(params), self.dtype, dev)
         T = ((S + 255) // 256) * 256
         rt = cache.get("rt")
         if rt is None or rt.B != B or rt.T < T:
@@ -144,11 +112,66 @@ class _DecoderWithHead:
         return f"{type(self).__name__}(config={self.config!r}, dtype={self.dtype})"
 
 
+def _check_model_inputs(config, input_ids, attention_mask):
+    """input_ids / attention_mask checks of models/_utils.py:78-177 (same messages); returns int32 ids with
+    negative placeholders mapped to row 0 and the boolean mask.  Raised before any device work."""
+    import numpy as np
+
+    ids = input_ids if isinstance(input_ids, torch.Tensor) else torch.as_tensor(np.asarray(input_ids))
+    if ids.ndim != 2:
+        raise ValueError(f"input_ids must be a 2D array, got shape {tuple(ids.shape)}.")
+    if ids.is_floating_point() or ids.is_complex() or ids.dtype == torch.bool:
+        raise TypeError(f"input_ids must contain integer token ids, got dtype {ids.dtype}.")
+    if ids.shape[0] == 0:
+        raise ValueError("input_ids must contain at least one batch row.")
+    if ids.shape[1] == 0:
+        raise ValueError("input_ids must contain at least one token.")
+    if bool((ids >= config.vocab_size).any()):
+        raise ValueError(f"input_ids token ids must be less than vocab_size={config.vocab_size}.")
+    B, S = ids.shape
+    if attention_mask is None:
+        # negative ids are placeholders: masked out by default
+        mask = ids >= 0
+        if not bool(mask.any(dim=1).all()):
+            raise ValueError("input_ids must contain at least one non-negative token per batch row when "
+                             "attention_mask is None.")
+    else:
+        mask = attention_mask if isinstance(attention_mask, torch.Tensor) else torch.as_tensor(
+            np.asarray(attention_mask))
+        if mask.ndim != 2:
+            raise ValueError(f"attention_mask must be a 2D array, got shape {tuple(mask.shape)}.")
+        if tuple(mask.shape) != (B, S):
+            raise ValueError(f"attention_mask shape must match input_ids, got {tuple(mask.shape)} and {(B, S)}.")
+        if mask.is_floating_point() or mask.is_complex():
+            raise TypeError(f"attention_mask must be boolean or integer, got dtype {mask.dtype}.")
+        if mask.dtype != torch.bool and bool(((mask != 0) & (mask != 1)).any()):
+            raise ValueError("attention_mask integer values must be 0 or 1.")
+        mask = mask.to(torch.bool)
+        if not bool(mask.any(dim=1).all()):
+            raise ValueError("attention_mask must contain at least one valid token per batch row.")
+        if bool((mask & (ids < 0)).any()):
+            raise ValueError("attention_mask must not mark negative placeholder token ids as valid.")
+    ids = torch.where(ids < 0, torch.zeros_like(ids), ids).to(torch.int32)
+    if S > 1 and bool((mask[:, :-1].to(torch.int8) < mask[:, 1:].to(torch.int8)).any()):
+        raise NotImplementedError("apply takes right-padded attention masks (the kernels attend to key prefixes).")
+    return ids, mask
+
+
 @dataclass
 class CausalLMOutputWithCache:
     """``outputs.py``: logits, and (not produced by ``apply`` here) caches, hidden states, weights."""
 
     logits: torch.Tensor
+    kv_caches: Optional[tuple] = None
+    hidden_states: Optional[tuple] = None
+    attention_weights: Optional[tuple] = None
+
+
+@dataclass
+class BaseModelOutputWithCache:
+    """``outputs.py``: the decoder stack's final hidden states (and, not produced here, caches etc.)."""
+
+    last_hidden_state: torch.Tensor
     kv_caches: Optional[tuple] = None
     hidden_states: Optional[tuple] = None
     attention_weights: Optional[tuple] = None
@@ -163,6 +186,59 @@ class GPTNeoXModelWithHead(_DecoderWithHead):
 
 
 class GemmaModelWithHead(_DecoderWithHead):
+    family = "gemma3"
+
+
+class _DecoderStack(_DecoderWithHead):
+    """``*Model`` (the stack without the LM head): parameters are the body subtree
+    (``{"params": {"embed_tokens": ..., "layers_0": ..., "norm": ...}}``)."""
+
+    @property
+    def _body(self) -> str:
+        return "gpt_neox" if self.family == "neox" else "model"
+
+    def init(self, seed: int = 0, *_, std: float = 0.02) -> dict:
+        return {"params": random_params(self.family, self.config, seed=seed, std=std)["params"][self._body]}
+
+    def _full_tree(self, params):
+        if not isinstance(params, dict) or "params" not in params:
+            raise ValueError("params must be a mapping with a 'params' entry.")
+        body = params["params"]
+        emb = body["embed_tokens"]["embedding"]
+        emb = emb if isinstance(emb, torch.Tensor) else torch.as_tensor(emb)
+        # the stack's output does not depend on the head; the tied embedding stands in for it
+        return {"params": {self._body: body, "lm_head": {"kernel": emb.T}}}
+
+    def apply(self, params, input_ids, attention_mask=None, position_ids=None, kv_caches=None,
+              output_attentions=False, output_hidden_states=False, use_cache=False):
+        """``*Model.__call__`` (models/llama.py:161-225, gpt_neox.py:158-222, gemma3.py:215-283) on the GPU
+        kernels for a cache-free forward: ``last_hidden_state`` [B, S, d] after the final norm, in a
+        ``BaseModelOutputWithCache``.  Same inputs, checks and limits as ``*ModelWithHead.apply``."""
+        from ._checks import normalize_bool
+
+        use_cache = normalize_bool("use_cache", use_cache)
+        output_attentions = normalize_bool("output_attentions", output_attentions)
+        output_hidden_states = normalize_bool("output_hidden_states", output_hidden_states)
+        if kv_caches is not None or use_cache or position_ids is not None:
+            raise NotImplementedError("apply with KV caches or position ids: use Engine.generate for cached decoding.")
+        if output_attentions or output_hidden_states:
+            raise NotImplementedError("apply does not return attention weights or per-layer hidden states.")
+        ids, mask = _check_model_inputs(self.config, input_ids, attention_mask)
+        B, S = ids.shape
+        rt = self._runtime(params, B, S)
+        dev = rt.w.device
+        return BaseModelOutputWithCache(last_hidden_state=rt.forward_hidden(ids.to(dev), mask.to(dev)))
+
+
+class LlamaModel(_DecoderStack):
+    family = "llama"
+
+
+class GPTNeoXModel(_DecoderStack):
+    family = "neox"
+
+
+class GemmaModel(_DecoderStack):
     family = "gemma3"
 
 

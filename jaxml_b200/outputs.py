@@ -7,16 +7,8 @@ from typing import Optional
 import torch
 
 from .cache import KVCache
-from .models import CausalLMOutputWithCache
+from .models import BaseModelOutputWithCache, CausalLMOutputWithCache
 from .nn import AttentionOutput
-
-
-@dataclass
-class BaseModelOutputWithCache:
-    last_hidden_state: torch.Tensor
-    kv_caches: Optional[tuple] = None
-    hidden_states: Optional[tuple] = None
-    attention_weights: Optional[tuple] = None
 
 
 @dataclass

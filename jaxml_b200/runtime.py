@@ -783,13 +783,11 @@ class DecoderRuntime:
         self._head(acts, rm)
         self._sample(greedy, temp, update_pos=False)
 
-    def forward_logits(self, ids: torch.Tensor, prompt_mask: torch.Tensor, keep: int = 0) -> torch.Tensor:
-        """The reference's ``*ModelWithHead.__call__`` without a cache (models/llama.py:247-273): the rows
-        [B, P] (device int32, right-padded ``prompt_mask``) through the stack, then the final norm and the
-        LM head over the last ``keep`` positions of every row (all P when ``keep`` is 0).  Returns logits
-        [B, kept, V] in the model dtype.  Single GPU only."""
+    def _forward_normed(self, ids: torch.Tensor, prompt_mask: torch.Tensor, keep: int) -> tuple:
+        """Rows [B, P] (device int32, right-padded ``prompt_mask``) through the stack, then the final norm
+        of the last ``keep`` positions of every row (all P when 0) into fresh activation buffers."""
         if self.comm is not None:
-            raise NotImplementedError("forward_logits under tensor parallelism (the Engine path covers it).")
+            raise NotImplementedError("a cache-free forward under tensor parallelism (the Engine path covers it).")
         W = self.w
         B, P = ids.shape
         self.reset(prompt_mask, np.zeros(2, np.uint32), np.zeros(2, np.uint32), 1)
@@ -805,10 +803,32 @@ class DecoderRuntime:
         out_acts = self._alloc_acts(M2, _rup(M2, 128) if W.bf16 else M2)
         fw, fb = W.final_norm
         self._norm(acts, w=fw, b=fb, row_map=rows.to(torch.int32).contiguous(), M=M2, out_acts=out_acts)
-        logits = torch.empty(M2, W.V, dtype=W.dtype, device=dev)
+        return out_acts, n
+
+    def forward_logits(self, ids: torch.Tensor, prompt_mask: torch.Tensor, keep: int = 0) -> torch.Tensor:
+        """The reference's ``*ModelWithHead.__call__`` without a cache (models/llama.py:247-273): final norm
+        and LM head over the last ``keep`` positions of every row (all when 0).  Returns logits
+        [B, kept, V] in the model dtype.  Single GPU only."""
+        W = self.w
+        B = ids.shape[0]
+        out_acts, n = self._forward_normed(ids, prompt_mask, keep)
+        logits = torch.empty(B * n, W.V, dtype=W.dtype, device=ids.device)
         self._linear(out_acts, W.lm_head, W.Np_v, W.Kp_d, "xn", N.JX_EPI_STORE, N_valid=W.V, out=logits, ldo=W.V,
                      K_logical=W.d, N_cols=W.V)
         return logits.view(B, n, W.V)
+
+    def forward_hidden(self, ids: torch.Tensor, prompt_mask: torch.Tensor) -> torch.Tensor:
+        """The reference's ``*Model.__call__`` without a cache (models/llama.py:161-225): the final-normed
+        hidden states [B, P, d] in the model dtype.  Single GPU only."""
+        W = self.w
+        B, P = ids.shape
+        out_acts, _ = self._forward_normed(ids, prompt_mask, 0)
+        if not W.bf16:
+            return out_acts["xn"][:B * P].reshape(B, P, W.d).clone()
+        out = torch.empty(B * P, W.d, dtype=W.dtype, device=ids.device)
+        N.check(N.load().jx_unpack_k128(ptr(out_acts["xn"]), B * P, W.d, out_acts["Mp"], ptr(out), N.JX_BF16, W.d,
+                                        self.stream_ptr()), "jx_unpack_k128")
+        return out.view(B, P, W.d)
 
     def decode_step(self, greedy: bool, temp: float):
         self._launches = 0

@@ -40,3 +40,21 @@ def test_model_apply_matches_oracle(family, dtype, hf_models):
         ref = O.forward(family, cfg, params, ids, dtype, attention_mask=mask).logits
         _close(got[0], ref[0], dtype)
         _close(got[1, :6], ref[1, :6], dtype)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16], ids=["f32", "bf16"])
+@pytest.mark.parametrize("family", ["llama", "neox", "gemma3"])
+def test_stack_model_apply_matches_oracle(family, dtype, hf_models):
+    """``*Model.apply``: the final-norm hidden states of every position against the oracle's."""
+    from jaxml_b200.models import GemmaModel, GPTNeoXModel, LlamaModel
+
+    _, cfg, params = hf_models[family]
+    cls = {"llama": LlamaModel, "neox": GPTNeoXModel, "gemma3": GemmaModel}[family]
+    body = "gpt_neox" if family == "neox" else "model"
+    model = cls(cfg, dtype=dtype)
+    g = torch.Generator().manual_seed(6)
+    ids = torch.randint(0, cfg.vocab_size, (2, 11), generator=g, dtype=torch.int32)
+    want = O.forward(family, cfg, params, ids, dtype).last_hidden_state
+    out = model.apply({"params": params["params"][body]}, ids).last_hidden_state
+    assert tuple(out.shape) == (2, 11, cfg.hidden_size) and out.dtype == dtype
+    _close(out, want, dtype)

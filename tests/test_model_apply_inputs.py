@@ -74,3 +74,31 @@ def test_unsupported_options():
         model.apply(params, ids, use_cache=1)
     with pytest.raises(ValueError, match="keep_last_n_logits must be non-negative"):
         model.apply(params, ids, keep_last_n_logits=-1)
+
+
+@pytest.mark.parametrize("fam", ["llama", "neox", "gemma3"])
+def test_stack_model_init_and_input_checks(fam):
+    """``*Model`` (the stack without the head) takes the body subtree and applies the same input checks."""
+    from jaxml_b200.models import GemmaModel, GPTNeoXModel, LlamaModel
+
+    cls = {"llama": LlamaModel, "neox": GPTNeoXModel, "gemma3": GemmaModel}[fam]
+    cfg = ModelConfig(head_dim=8, hidden_size=32, num_heads=4, num_kv_heads=4, num_layers=1,
+                      max_position_embeddings=64, vocab_size=50)
+    model = cls(cfg)
+    params = model.init(0)
+    assert "embed_tokens" in params["params"] and "lm_head" not in params["params"]
+    body = "gpt_neox" if fam == "neox" else "model"
+    full = random_params(fam, cfg, seed=0)["params"][body]
+    for k in full["embed_tokens"]:
+        assert torch.equal(torch.as_tensor(params["params"]["embed_tokens"][k]), torch.as_tensor(full["embed_tokens"][k]))
+    tree = model._full_tree(params)
+    assert set(tree["params"]) == {body, "lm_head"}
+    assert tuple(tree["params"]["lm_head"]["kernel"].shape) == (32, 50)
+    with pytest.raises(ValueError, match="input_ids must be a 2D array"):
+        model.apply(params, torch.arange(4, dtype=torch.int32))
+    with pytest.raises(ValueError, match="less than vocab_size"):
+        model.apply(params, torch.tensor([[0, 50]], dtype=torch.int32))
+    with pytest.raises(NotImplementedError, match="KV caches"):
+        model.apply(params, torch.ones(1, 4, dtype=torch.int32), use_cache=True)
+    with pytest.raises(NotImplementedError, match="hidden states"):
+        model.apply(params, torch.ones(1, 4, dtype=torch.int32), output_hidden_states=True)
