@@ -325,6 +325,13 @@ int jx_qkv_rope_append(const jx_qkv_args* args, int dtype, int pdl, void* stream
 /* RotaryEmbedding.apply_rotary_pos_emb (nn/position.py:78-141) for any positions. */
 int jx_rope_apply(const jx_rope_args* args, int dtype, int pdl, void* stream);
 
+/* Element-wise MLP activation on separate projection outputs [M, F] (leading dims ldg / ldu / ldo):
+ * kind JX_EPI_GLU_SILU / JX_EPI_GLU_GELU_TANH: out = dtype(dtype(act(gate)) * up) (models/llama.py:90-95,
+ * models/gemma3.py:85-90); JX_EPI_ACT_GELU_ERF: out = dtype(gelu_erf(gate)), up unused
+ * (models/gpt_neox.py:84-88).  dtype JX_F32 or JX_BF16. */
+int jx_mlp_act(const void* gate, long long ldg, const void* up, long long ldu, void* out, long long ldo, long long M,
+               long long F, int kind, int dtype, int pdl, void* stream);
+
 /* Attention.mha (nn/attention.py:321-400) on the cache, any head size (CUDA cores). */
 int jx_attention(const jx_attn_args* args, int dtype, int pdl, void* stream);
 

@@ -104,6 +104,7 @@ _PROTOS = {
     "jx_linear_f32": (I, [P, LL, P, I, I, I, ctypes.POINTER(JxEpilogue), I, P]),
     "jx_qkv_rope_append": (I, [ctypes.POINTER(JxQkvArgs), I, I, P]),
     "jx_rope_apply": (I, [ctypes.POINTER(JxRopeArgs), I, I, P]),
+    "jx_mlp_act": (I, [P, LL, P, LL, P, LL, LL, LL, I, I, I, P]),
     "jx_attention": (I, [ctypes.POINTER(JxAttnArgs), I, I, P]),
     "jx_decode_attention_workspace": (I, [I, I, I, I, I, ctypes.POINTER(LL)]),
     "jx_decode_attention": (I, [ctypes.POINTER(JxDAttnArgs), I, P]),

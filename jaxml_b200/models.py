@@ -14,6 +14,8 @@ import torch
 
 from ._checks import normalize_dtype
 from .config import ModelConfig
+from .decoders import (GemmaDecoder, GemmaMLP, GPTNeoXDecoder, GPTNeoXMLP, LlamaDecoder,  # noqa: F401
+                       LlamaMLP)
 from .nn import GemmaRMSNorm  # noqa: F401  (models/gemma3.py:89-106 lives in jaxml.models)
 
 
@@ -60,31 +62,90 @@ class _DecoderWithHead:
 
     def apply(self, params, input_ids, attention_mask=None, position_ids=None, kv_caches=None, use_cache=False,
               output_attentions=False, output_hidden_states=False, keep_last_n_logits: int = 0):
-        """``*ModelWithHead.__call__`` (models/llama.py:247-273, gpt_neox.py:245-272, gemma3.py:304-331)
-        on the GPU kernels for a cache-free forward: logits ``[B, S]`` (or the last ``keep_last_n_logits``
-        positions) in the model dtype, in a ``CausalLMOutputWithCache``.  Right-padded masks; token ids
-        below 0 read row 0 like the reference.  Cached decoding, position ids, per-layer hidden states
-        and attention weights are the Engine's business here and raise ``NotImplementedError``."""
-        import numpy as np
+        """``*ModelWithHead.__call__`` (models/llama.py:247-273, gpt_neox.py:245-272, gemma3.py:304-331) on
+        the GPU kernels: logits ``[B, S]`` (or the last ``keep_last_n_logits`` positions) in the model dtype,
+        in a ``CausalLMOutputWithCache``.  A cache-free call without position ids or hidden states runs on
+        the fused prefill runtime; calls with KV caches (a prompt into empty caches, or one token per row
+        into populated ones), position ids or ``output_hidden_states`` run layer by layer through the
+        decoder blocks.  Masks must be right-padded; attention weights are not produced
+        (``output_attentions=True`` raises ``NotImplementedError``)."""
+        from ._checks import normalize_count
 
-        from ._checks import normalize_bool, normalize_count
+        keep = normalize_count("keep_last_n_logits", keep_last_n_logits)
+        if keep < 0:
+            raise ValueError(f"keep_last_n_logits must be non-negative, got {keep}.")
+        hidden, caches, states, is_logits = self._stack(params, input_ids, attention_mask, position_ids, kv_caches,
+                                                        use_cache, output_attentions, output_hidden_states, keep)
+        if is_logits:
+            return CausalLMOutputWithCache(logits=hidden, kv_caches=caches)
+        h = hidden if keep == 0 else hidden[:, -keep:]
+        head = self._head_kernel(params)
+        B, n, d = h.shape
+        from . import nn as _nn
+
+        logits = _nn._dense(h.reshape(B * n, d), head, None, self.dtype).reshape(B, n, -1)
+        _nn._check_status(h.device, "lm_head")
+        return CausalLMOutputWithCache(logits=logits, kv_caches=caches, hidden_states=states)
+
+    def _head_kernel(self, params) -> torch.Tensor:
+        """The LM head kernel [d, V] on the device in the model dtype (cached with the converted tree)."""
+        return self._device_params(params)["lm_head"]["kernel"]
+
+    def _body(self, params) -> dict:
+        return self._device_params(params)["gpt_neox" if self.family == "neox" else "model"]
+
+    def _device_params(self, params) -> dict:
+        """The whole parameter tree on the device in the model dtype, cached per tree."""
+        from .decoders import device_tree
+
+        dev = torch.device("cuda", torch.cuda.current_device())
+        cache = self.__dict__.setdefault("_layered_cache", {})
+        key = (id(params), dev.index, self.dtype)
+        if cache.get("key") != key:
+            cache.clear()
+            if not isinstance(params, dict) or "params" not in params:
+                raise ValueError("params must be a mapping with a 'params' entry.")
+            cache["key"] = key
+            cache["params"] = params   # keeps the tree alive while its id is the cache key
+            cache["tree"] = device_tree(self._full_tree(params)["params"], self.dtype, dev)
+            cache["rope"] = {}
+        return cache["tree"]
+
+    def _stack(self, params, input_ids, attention_mask, position_ids, kv_caches, use_cache, output_attentions,
+               output_hidden_states, keep):
+        """The stack below the head.  Returns ``(last_hidden_state, kv_caches, hidden_states, False)``; on the
+        fused runtime path of a model with a head, ``(logits, kv_caches, None, True)``."""
+        from ._checks import normalize_bool
 
         use_cache = normalize_bool("use_cache", use_cache)
         output_attentions = normalize_bool("output_attentions", output_attentions)
         output_hidden_states = normalize_bool("output_hidden_states", output_hidden_states)
-        keep = normalize_count("keep_last_n_logits", keep_last_n_logits)
-        if keep < 0:
-            raise ValueError(f"keep_last_n_logits must be non-negative, got {keep}.")
-        if kv_caches is not None or use_cache or position_ids is not None:
-            raise NotImplementedError("apply with KV caches or position ids: use Engine.generate for cached decoding.")
-        if output_attentions or output_hidden_states:
-            raise NotImplementedError("apply does not return attention weights or per-layer hidden states.")
-        ids, mask = _check_model_inputs(self.config, input_ids, attention_mask)
-        B, S = ids.shape
-        rt = self._runtime(params, B, S)
-        dev = rt.w.device
-        logits = rt.forward_logits(ids.to(dev), mask.to(dev), keep)
-        return CausalLMOutputWithCache(logits=logits)
+        ids, mask, kv_caches, pos = _prepare_model_inputs(self.config, input_ids, attention_mask, kv_caches,
+                                                          position_ids)
+        if output_attentions:
+            raise NotImplementedError("output_attentions: the CUDA attention kernels do not return the weights.")
+        L = self.config.num_layers
+        if mask is not None and not _right_padded(mask):
+            raise NotImplementedError("apply takes right-padded attention masks (the kernels attend to key prefixes).")
+        if kv_caches is None and pos is None and not output_hidden_states:
+            B, S = ids.shape
+            rt = self._runtime(params, B, S)
+            dev = rt.w.device
+            caches = (None,) * L if use_cache else None
+            if self._has_head:
+                return rt.forward_logits(ids.to(dev), mask.to(dev), keep), caches, None, True
+            return rt.forward_hidden(ids.to(dev), mask.to(dev)), caches, None, False
+        from .decoders import layered_forward, _cached_sequence_length
+
+        body = self._body(params)
+        dev = body["embed_tokens"]["embedding"].device
+        cached_len = _cached_sequence_length(kv_caches)
+        h, caches, states = layered_forward(
+            self.family, self.config, self.dtype, body, ids.to(dev), None if mask is None else mask.to(dev),
+            None if pos is None else pos.to(dev), kv_caches, cached_len, self.__dict__["_layered_cache"]["rope"])
+        return h, (caches if use_cache else None), (states if output_hidden_states else None), False
+
+    _has_head = True
 
     def _full_tree(self, params):
         """The parameter tree the runtime packs (the with-head layout)."""
@@ -112,12 +173,25 @@ class _DecoderWithHead:
         return f"{type(self).__name__}(config={self.config!r}, dtype={self.dtype})"
 
 
-def _check_model_inputs(config, input_ids, attention_mask):
-    """input_ids / attention_mask checks of models/_utils.py:78-177 (same messages); returns int32 ids with
-    negative placeholders mapped to row 0 and the boolean mask.  Raised before any device work."""
+def _right_padded(mask: torch.Tensor) -> bool:
+    return mask.shape[1] <= 1 or not bool((mask[:, :-1].to(torch.int8) < mask[:, 1:].to(torch.int8)).any())
+
+
+def _as_t(x) -> torch.Tensor:
     import numpy as np
 
-    ids = input_ids if isinstance(input_ids, torch.Tensor) else torch.as_tensor(np.asarray(input_ids))
+    return x if isinstance(x, torch.Tensor) else torch.as_tensor(np.asarray(x))
+
+
+def _prepare_model_inputs(config, input_ids, attention_mask, kv_caches=None, position_ids=None):
+    """models/_utils.py:78-217 (``prepare_model_inputs``, ``prepare_position_ids``,
+    ``prepare_default_attention_mask``) with the same messages, raised before any device work.  Returns
+    ``(ids, mask, kv_caches, position_ids)``: int32 ids with negative placeholders mapped to 0, the
+    boolean mask (the default ``ids >= 0`` unless populated caches carry the mask, then None or the
+    caller's), the caches as a tuple (or None) and the position ids (or None)."""
+    from .cache import KVCache
+
+    ids = _as_t(input_ids)
     if ids.ndim != 2:
         raise ValueError(f"input_ids must be a 2D array, got shape {tuple(ids.shape)}.")
     if ids.is_floating_point() or ids.is_complex() or ids.dtype == torch.bool:
@@ -128,38 +202,79 @@ def _check_model_inputs(config, input_ids, attention_mask):
         raise ValueError("input_ids must contain at least one token.")
     if bool((ids >= config.vocab_size).any()):
         raise ValueError(f"input_ids token ids must be less than vocab_size={config.vocab_size}.")
-    B, S = ids.shape
-    if attention_mask is None:
-        # negative ids are placeholders: masked out by default
-        mask = ids >= 0
-        if not bool(mask.any(dim=1).all()):
-            raise ValueError("input_ids must contain at least one non-negative token per batch row when "
-                             "attention_mask is None.")
-    else:
-        mask = attention_mask if isinstance(attention_mask, torch.Tensor) else torch.as_tensor(
-            np.asarray(attention_mask))
+    L = config.num_layers
+    if kv_caches is not None:
+        try:
+            kv_caches = tuple(kv_caches)
+        except TypeError as e:
+            raise TypeError("kv_caches must be a sequence containing one cache per layer.") from e
+        if len(kv_caches) != L:
+            raise ValueError(f"kv_caches must contain one cache per layer, got {len(kv_caches)} and expected {L}.")
+        for idx, c in enumerate(kv_caches):
+            if c is not None and not isinstance(c, KVCache):
+                raise TypeError(f"kv_caches entries must be KVCache instances or None, got {type(c)} at index {idx}.")
+            if c is not None:
+                c.validate_state()
+    expected = tuple(ids.shape)
+    populated = () if kv_caches is None else tuple(
+        tuple(c.mask.shape) for c in kv_caches if c is not None and c.mask is not None)
+    if populated:
+        expected = populated[0]
+        if any(s != expected for s in populated):
+            raise ValueError("kv_caches populated entries must share attention mask shape.")
+        if expected[0] != ids.shape[0]:
+            raise ValueError("kv_caches populated entries must share input_ids batch size; "
+                             f"got {expected[0]} and {ids.shape[0]}.")
+    mask = None
+    if attention_mask is not None:
+        mask = _as_t(attention_mask)
         if mask.ndim != 2:
             raise ValueError(f"attention_mask must be a 2D array, got shape {tuple(mask.shape)}.")
-        if tuple(mask.shape) != (B, S):
-            raise ValueError(f"attention_mask shape must match input_ids, got {tuple(mask.shape)} and {(B, S)}.")
         if mask.is_floating_point() or mask.is_complex():
             raise TypeError(f"attention_mask must be boolean or integer, got dtype {mask.dtype}.")
+        if tuple(mask.shape) != expected:
+            raise ValueError("attention_mask shape must match input_ids shape or populated KV cache mask shape; "
+                             f"got {tuple(mask.shape)} and expected {expected}.")
         if mask.dtype != torch.bool and bool(((mask != 0) & (mask != 1)).any()):
             raise ValueError("attention_mask integer values must be 0 or 1.")
         mask = mask.to(torch.bool)
         if not bool(mask.any(dim=1).all()):
             raise ValueError("attention_mask must contain at least one valid token per batch row.")
-        if bool((mask & (ids < 0)).any()):
-            raise ValueError("attention_mask must not mark negative placeholder token ids as valid.")
+        if tuple(mask.shape) == tuple(ids.shape) and bool((mask & (ids.to(mask.device) < 0)).any()):
+            raise ValueError("attention_mask must not mark negative placeholder input_ids as valid.")
+    negative = bool((ids < 0).any())
+    if negative and mask is not None and tuple(mask.shape) != tuple(ids.shape):
+        raise ValueError("input_ids must not contain negative placeholder ids when attention_mask is not token-shaped.")
+    if negative and mask is None and populated:
+        raise ValueError("input_ids must not contain negative placeholder ids when using populated KV caches.")
+    pos = None
+    if position_ids is not None:
+        pos = _as_t(position_ids)
+        if pos.ndim != 2:
+            raise ValueError(f"position_ids must be a 2D array, got shape {tuple(pos.shape)}.")
+        if pos.is_floating_point() or pos.is_complex() or pos.dtype == torch.bool:
+            raise TypeError(f"position_ids must contain integer positions, got dtype {pos.dtype}.")
+        if pos.shape[1] != ids.shape[1] or pos.shape[0] not in (1, ids.shape[0]):
+            raise ValueError("position_ids shape must be broadcastable to input_ids batch and sequence axes, "
+                             f"got {tuple(pos.shape)} and {tuple(ids.shape)}.")
+        if bool((pos < 0).any()):
+            raise ValueError("position_ids must contain non-negative positions.")
+        if bool((pos >= config.max_position_embeddings).any()):
+            raise ValueError(
+                f"position_ids must be less than max_position_embeddings={config.max_position_embeddings}.")
+    if mask is None and not populated:
+        mask = ids >= 0
+        if not bool(mask.any(dim=1).all()):
+            raise ValueError("input_ids must contain at least one non-negative token per batch row when "
+                             "attention_mask is omitted.")
     ids = torch.where(ids < 0, torch.zeros_like(ids), ids).to(torch.int32)
-    if S > 1 and bool((mask[:, :-1].to(torch.int8) < mask[:, 1:].to(torch.int8)).any()):
-        raise NotImplementedError("apply takes right-padded attention masks (the kernels attend to key prefixes).")
-    return ids, mask
+    return ids, mask, kv_caches, pos
 
 
 @dataclass
 class CausalLMOutputWithCache:
-    """``outputs.py``: logits, and (not produced by ``apply`` here) caches, hidden states, weights."""
+    """``outputs.py``: logits, the updated caches and per-layer hidden states when asked for (attention
+    weights are not produced)."""
 
     logits: torch.Tensor
     kv_caches: Optional[tuple] = None
@@ -169,7 +284,8 @@ class CausalLMOutputWithCache:
 
 @dataclass
 class BaseModelOutputWithCache:
-    """``outputs.py``: the decoder stack's final hidden states (and, not produced here, caches etc.)."""
+    """``outputs.py``: the decoder stack's final hidden states, the updated caches and per-layer hidden
+    states when asked for (attention weights are not produced)."""
 
     last_hidden_state: torch.Tensor
     kv_caches: Optional[tuple] = None
@@ -193,12 +309,14 @@ class _DecoderStack(_DecoderWithHead):
     """``*Model`` (the stack without the LM head): parameters are the body subtree
     (``{"params": {"embed_tokens": ..., "layers_0": ..., "norm": ...}}``)."""
 
+    _has_head = False
+
     @property
-    def _body(self) -> str:
+    def _body_key(self) -> str:
         return "gpt_neox" if self.family == "neox" else "model"
 
     def init(self, seed: int = 0, *_, std: float = 0.02) -> dict:
-        return {"params": random_params(self.family, self.config, seed=seed, std=std)["params"][self._body]}
+        return {"params": random_params(self.family, self.config, seed=seed, std=std)["params"][self._body_key]}
 
     def _full_tree(self, params):
         if not isinstance(params, dict) or "params" not in params:
@@ -207,27 +325,17 @@ class _DecoderStack(_DecoderWithHead):
         emb = body["embed_tokens"]["embedding"]
         emb = emb if isinstance(emb, torch.Tensor) else torch.as_tensor(emb)
         # the stack's output does not depend on the head; the tied embedding stands in for it
-        return {"params": {self._body: body, "lm_head": {"kernel": emb.T}}}
+        return {"params": {self._body_key: body, "lm_head": {"kernel": emb.T}}}
 
     def apply(self, params, input_ids, attention_mask=None, position_ids=None, kv_caches=None,
               output_attentions=False, output_hidden_states=False, use_cache=False):
-        """``*Model.__call__`` (models/llama.py:161-225, gpt_neox.py:158-222, gemma3.py:215-283) on the GPU
-        kernels for a cache-free forward: ``last_hidden_state`` [B, S, d] after the final norm, in a
-        ``BaseModelOutputWithCache``.  Same inputs, checks and limits as ``*ModelWithHead.apply``."""
-        from ._checks import normalize_bool
-
-        use_cache = normalize_bool("use_cache", use_cache)
-        output_attentions = normalize_bool("output_attentions", output_attentions)
-        output_hidden_states = normalize_bool("output_hidden_states", output_hidden_states)
-        if kv_caches is not None or use_cache or position_ids is not None:
-            raise NotImplementedError("apply with KV caches or position ids: use Engine.generate for cached decoding.")
-        if output_attentions or output_hidden_states:
-            raise NotImplementedError("apply does not return attention weights or per-layer hidden states.")
-        ids, mask = _check_model_inputs(self.config, input_ids, attention_mask)
-        B, S = ids.shape
-        rt = self._runtime(params, B, S)
-        dev = rt.w.device
-        return BaseModelOutputWithCache(last_hidden_state=rt.forward_hidden(ids.to(dev), mask.to(dev)))
+        """``*Model.__call__`` (models/llama.py:161-225, gpt_neox.py:158-222, gemma3.py:215-283):
+        ``last_hidden_state`` [B, S, d] after the final norm, the updated caches (``use_cache``) and the
+        per-layer hidden states (``output_hidden_states``) in a ``BaseModelOutputWithCache``.  Same inputs,
+        paths and limits as ``*ModelWithHead.apply``."""
+        h, caches, states, _ = self._stack(params, input_ids, attention_mask, position_ids, kv_caches, use_cache,
+                                           output_attentions, output_hidden_states, 0)
+        return BaseModelOutputWithCache(last_hidden_state=h, kv_caches=caches, hidden_states=states)
 
 
 class LlamaModel(_DecoderStack):

@@ -6,16 +6,9 @@ from typing import Optional
 
 import torch
 
-from .cache import KVCache
+from .decoders import DecoderOutput
 from .models import BaseModelOutputWithCache, CausalLMOutputWithCache
 from .nn import AttentionOutput
-
-
-@dataclass
-class DecoderOutput:
-    hidden_states: torch.Tensor
-    kv_cache: Optional[KVCache] = None
-    attention_weight: Optional[torch.Tensor] = None
 
 
 @dataclass

@@ -58,3 +58,88 @@ def test_stack_model_apply_matches_oracle(family, dtype, hf_models):
     out = model.apply({"params": params["params"][body]}, ids).last_hidden_state
     assert tuple(out.shape) == (2, 11, cfg.hidden_size) and out.dtype == dtype
     _close(out, want, dtype)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16], ids=["f32", "bf16"])
+@pytest.mark.parametrize("family", ["llama", "neox", "gemma3"])
+def test_apply_with_kv_caches_matches_oracle(family, dtype, hf_models):
+    """A right-padded prompt into empty ``KVCache`` objects, then one token per row into the populated
+    caches, through ``*ModelWithHead.apply`` (the decoder blocks), against the oracle's cached forward:
+    logits, cache contents, masks and positions."""
+    from jaxml_b200.cache import KVCache
+
+    _, cfg, params = hf_models[family]
+    model = CLASSES[family](cfg, dtype=dtype)
+    L, T = cfg.num_layers, 16
+    g = torch.Generator().manual_seed(7)
+    ids = torch.randint(0, cfg.vocab_size, (2, 6), generator=g, dtype=torch.int32)
+    mask = torch.ones(2, 6, dtype=torch.bool)
+    mask[1, 4:] = False
+    out = model.apply(params, ids, attention_mask=mask, kv_caches=tuple(KVCache.init(T, dtype=dtype) for _ in range(L)),
+                      use_cache=True)
+    ref = O.forward(family, cfg, params, ids, dtype, attention_mask=mask,
+                    kv_caches=[O.OracleKVCache(T, dtype) for _ in range(L)])
+    _close(out.logits[0], ref.logits[0], dtype)
+    _close(out.logits[1, :4], ref.logits[1, :4], dtype)
+    caches, ocaches = out.kv_caches, ref.kv_caches
+    for step in range(4):
+        for c, oc in zip(caches, ocaches):
+            assert torch.equal(c.mask.cpu(), oc.mask)
+            assert torch.equal(c.pos_id.cpu().long(), oc.pos_id.long())
+            _close(c.k, oc.k, dtype)
+            _close(c.v, oc.v, dtype)
+        if step == 3:
+            break
+        nxt = torch.randint(0, cfg.vocab_size, (2, 1), generator=g, dtype=torch.int32)
+        out = model.apply(params, nxt, kv_caches=caches, use_cache=True)
+        ref = O.forward(family, cfg, params, nxt, dtype, kv_caches=list(ocaches))
+        assert tuple(out.logits.shape) == (2, 1, cfg.vocab_size)
+        _close(out.logits, ref.logits, dtype)
+        caches, ocaches = out.kv_caches, ref.kv_caches
+
+
+@pytest.mark.parametrize("family", ["llama", "neox", "gemma3"])
+def test_apply_hidden_states_and_position_ids(family, hf_models):
+    """``output_hidden_states`` (every layer's input, then the final-norm output), ``use_cache`` without
+    caches, and explicit (broadcast) position ids, against the oracle."""
+    from jaxml_b200.models import GemmaModel, GPTNeoXModel, LlamaModel
+
+    _, cfg, params = hf_models[family]
+    dtype = torch.float32
+    model = CLASSES[family](cfg, dtype=dtype)
+    g = torch.Generator().manual_seed(8)
+    ids = torch.randint(0, cfg.vocab_size, (2, 5), generator=g, dtype=torch.int32)
+    ref = O.forward(family, cfg, params, ids, dtype)
+    out = model.apply(params, ids, output_hidden_states=True, use_cache=True)
+    assert out.kv_caches == (None,) * cfg.num_layers
+    assert len(out.hidden_states) == cfg.num_layers + 1
+    for got, want in zip(out.hidden_states, ref.hidden_states):
+        _close(got, want, dtype)
+    _close(out.logits, ref.logits, dtype)
+    stack = {"llama": LlamaModel, "neox": GPTNeoXModel, "gemma3": GemmaModel}[family](cfg, dtype=dtype)
+    body = params["params"]["gpt_neox" if family == "neox" else "model"]
+    sout = stack.apply({"params": body}, ids, output_hidden_states=True)
+    _close(sout.last_hidden_state, ref.last_hidden_state, dtype)
+    assert len(sout.hidden_states) == cfg.num_layers + 1 and sout.kv_caches is None
+    pos = torch.arange(5, dtype=torch.int32)[None] + 3
+    ref = O.forward(family, cfg, params, ids, dtype, position_ids=pos.expand(2, 5))
+    out = model.apply(params, ids, position_ids=pos)
+    _close(out.logits, ref.logits, dtype)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16], ids=["f32", "bf16"])
+@pytest.mark.parametrize("family", ["llama", "neox", "gemma3"])
+def test_mlp_blocks_match_oracle(family, dtype, hf_models):
+    """``LlamaMLP`` / ``GPTNeoXMLP`` / ``GemmaMLP`` (projections + ``jx_mlp_act``) against the oracle's MLP."""
+    from jaxml_b200.models import GemmaMLP, GPTNeoXMLP, LlamaMLP
+
+    _, cfg, params = hf_models[family]
+    lp = params["params"]["gpt_neox" if family == "neox" else "model"]["layers_0"]
+    cls = {"llama": LlamaMLP, "neox": GPTNeoXMLP, "gemma3": GemmaMLP}[family]
+    g = torch.Generator().manual_seed(9)
+    x = torch.randn(2, 3, cfg.hidden_size, generator=g).to(dtype)
+    mp = {k: {kk: torch.as_tensor(vv).cuda() for kk, vv in v.items()} for k, v in lp["mlp"].items()}
+    got = cls(cfg, dtype=dtype).apply({"params": mp}, x.cuda())
+    want = O._mlp(family, lp, x, dtype)
+    assert got.dtype == dtype and tuple(got.shape) == (2, 3, cfg.hidden_size)
+    _close(got, want, dtype)

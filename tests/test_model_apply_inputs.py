@@ -61,19 +61,94 @@ def test_mask_contents():
         model.apply(params, torch.tensor([[-100, 1]], dtype=torch.int32))
 
 
-def test_unsupported_options():
+def test_unsupported_options_and_flag_types():
     model, params = MODELS[0]
     ids = torch.ones(1, 3, dtype=torch.int32)
-    for kw in ({"use_cache": True}, {"kv_caches": ()}, {"position_ids": torch.zeros(1, 3, dtype=torch.int32)}):
-        with pytest.raises(NotImplementedError):
+    with pytest.raises(NotImplementedError, match="output_attentions"):
+        model.apply(params, ids, output_attentions=True)
+    for kw, match in (({"use_cache": 1}, "use_cache must be a boolean"),
+                      ({"use_cache": None}, "use_cache must be a boolean"),
+                      ({"output_attentions": 1}, "output_attentions must be a boolean"),
+                      ({"output_hidden_states": "true"}, "output_hidden_states must be a boolean")):
+        with pytest.raises(TypeError, match=match):
             model.apply(params, ids, **kw)
-    for kw in ({"output_attentions": True}, {"output_hidden_states": True}):
-        with pytest.raises(NotImplementedError):
-            model.apply(params, ids, **kw)
-    with pytest.raises(TypeError, match="use_cache must be a boolean"):
-        model.apply(params, ids, use_cache=1)
-    with pytest.raises(ValueError, match="keep_last_n_logits must be non-negative"):
-        model.apply(params, ids, keep_last_n_logits=-1)
+    for keep, exc, match in ((True, TypeError, "keep_last_n_logits must be an integer"),
+                             (np.bool_(True), TypeError, "keep_last_n_logits must be an integer"),
+                             (1.5, TypeError, "keep_last_n_logits must be an integer"),
+                             (-1, ValueError, "keep_last_n_logits must be non-negative")):
+        with pytest.raises(exc, match=match):
+            model.apply(params, ids, keep_last_n_logits=keep)
+
+
+@pytest.mark.parametrize("pos,exc,match", [
+    (torch.arange(4, dtype=torch.int32), ValueError, "position_ids must be a 2D array"),
+    (torch.ones(1, 4), TypeError, "integer positions"),
+    (torch.ones(1, 3, dtype=torch.int32), ValueError, "position_ids shape must be broadcastable"),
+    (torch.tensor([[-1, 0, 1, 2]], dtype=torch.int32), ValueError, "non-negative positions"),
+    (torch.tensor([[0, 1, 2, 64]], dtype=torch.int32), ValueError, "less than max_position_embeddings=64"),
+])
+def test_invalid_position_ids(pos, exc, match):
+    model, params = MODELS[0]
+    with pytest.raises(exc, match=match):
+        model.apply(params, torch.arange(4, dtype=torch.int32)[None], position_ids=pos)
+
+
+def _populated(B=1, T=8, n=2, mask_dtype=torch.bool):
+    from jaxml_b200.cache import KVCache
+
+    k = torch.randn(B, n, 4, 8)
+    return KVCache.init(T, k=k, v=torch.randn_like(k), mask=torch.ones(B, n, dtype=mask_dtype))
+
+
+def test_kv_cache_argument_checks():
+    """models/_utils.py:99-177 checks on the caches, raised before any device work (the reference's
+    ``tests/test_model_inputs.py`` cases)."""
+    from jaxml_b200.cache import KVCache
+
+    model, params = MODELS[0]
+    ids = torch.tensor([[2]], dtype=torch.int32)
+    with pytest.raises(ValueError, match="one cache per layer"):
+        model.apply(params, ids, kv_caches=())
+    with pytest.raises(TypeError, match="kv_caches must be a sequence"):
+        model.apply(params, ids, kv_caches=3)
+    with pytest.raises(TypeError, match="KVCache instances or None"):
+        model.apply(params, ids, kv_caches=(object(),))
+    bad = KVCache(k=None, v=torch.zeros(1), max_seq_len=8, mask=None)
+    with pytest.raises(ValueError, match="k is empty"):
+        model.apply(params, ids, kv_caches=(bad,))
+    c = _populated()
+    with pytest.raises(TypeError, match="Cached mask must be boolean"):
+        model.apply(params, ids, kv_caches=(c.replace(mask=c.mask.to(torch.int32)),))
+    # a populated cache carries the mask: a token-shaped mask no longer fits
+    with pytest.raises(ValueError, match="populated KV cache mask shape"):
+        model.apply(params, ids, attention_mask=torch.ones(1, 1, dtype=torch.bool), kv_caches=(c,))
+    with pytest.raises(ValueError, match="attention_mask is not token-shaped"):
+        model.apply(params, torch.tensor([[-100]], dtype=torch.int32), attention_mask=c.mask, kv_caches=(c,))
+    with pytest.raises(ValueError, match="using populated KV caches"):
+        model.apply(params, torch.tensor([[-100]], dtype=torch.int32), kv_caches=(c,))
+    with pytest.raises(ValueError, match="share input_ids batch size"):
+        model.apply(params, torch.ones(2, 1, dtype=torch.int32), kv_caches=(c,))
+
+
+def test_kv_cache_mask_shapes_must_agree():
+    from jaxml_b200.models import _prepare_model_inputs
+
+    cfg = ModelConfig(head_dim=8, hidden_size=32, num_heads=4, num_layers=2, max_position_embeddings=64,
+                      vocab_size=50)
+    with pytest.raises(ValueError, match="share attention mask shape"):
+        _prepare_model_inputs(cfg, torch.ones(1, 1, dtype=torch.int32), None, (_populated(T=8), _populated(T=9)))
+    from jaxml_b200.decoders import _cached_sequence_length
+
+    with pytest.raises(ValueError, match="share cached sequence length"):
+        _cached_sequence_length((_populated(T=8), _populated(T=9)))
+    assert _cached_sequence_length((None, _populated(T=9))) == 9
+    # populated caches supply the mask: none is built from the ids
+    ids, mask, caches, pos = _prepare_model_inputs(cfg, torch.ones(1, 1, dtype=torch.int32), None,
+                                                   (_populated(), None))
+    assert mask is None and len(caches) == 2 and pos is None
+    # empty caches keep the default mask (ids >= 0)
+    ids, mask, _, _ = _prepare_model_inputs(cfg, torch.tensor([[3, -1]]), None, (None, None))
+    assert mask.tolist() == [[True, False]] and ids.tolist() == [[3, 0]]
 
 
 @pytest.mark.parametrize("fam", ["llama", "neox", "gemma3"])
@@ -98,7 +173,7 @@ def test_stack_model_init_and_input_checks(fam):
         model.apply(params, torch.arange(4, dtype=torch.int32))
     with pytest.raises(ValueError, match="less than vocab_size"):
         model.apply(params, torch.tensor([[0, 50]], dtype=torch.int32))
-    with pytest.raises(NotImplementedError, match="KV caches"):
-        model.apply(params, torch.ones(1, 4, dtype=torch.int32), use_cache=True)
-    with pytest.raises(NotImplementedError, match="hidden states"):
-        model.apply(params, torch.ones(1, 4, dtype=torch.int32), output_hidden_states=True)
+    with pytest.raises(NotImplementedError, match="output_attentions"):
+        model.apply(params, torch.ones(1, 4, dtype=torch.int32), output_attentions=np.bool_(True))
+    with pytest.raises(ValueError, match="one cache per layer"):
+        model.apply(params, torch.ones(1, 4, dtype=torch.int32), kv_caches=(None, None))
