@@ -353,6 +353,85 @@ class Engine:
             raise ValueError("mask must be right padded: valid tokens cannot appear after masked positions.")
         return prompt, mask
 
+    # -- the reference's step-by-step interface ---------------------------------------------------------
+    def init_cache(self, max_seq_len: int) -> tuple:
+        """``engine.py:110-121``: one empty ``KVCache`` of ``max_seq_len`` slots per layer, in the engine's
+        dtype, for driving ``wrapped_apply_fn`` (or the model's ``apply``) step by step."""
+        from .cache import KVCache
+
+        max_seq_len = normalize_count("max_seq_len", max_seq_len)
+        if max_seq_len <= 0:
+            raise ValueError(f"max_seq_len must be positive, got {max_seq_len}.")
+        try:
+            num_layers = self.model.config.num_layers
+        except AttributeError as e:
+            raise TypeError("model must expose config.num_layers to initialize KV caches.") from e
+        num_layers = normalize_count("model.config.num_layers", num_layers)
+        if num_layers <= 0:
+            raise ValueError(f"model.config.num_layers must be positive, got {num_layers}.")
+        return tuple(KVCache.init(max_seq_len, None, None, dtype=self.dtype) for _ in range(num_layers))
+
+    def prepare_input(self, inputs, dtype: Any = None):
+        """``engine.py:320-353``: every leaf of ``inputs`` (an array or a dict / list / tuple of arrays) as a
+        2D tensor on this process's GPU (the reference shards them over its data axis; one process drives
+        one GPU here), cast to ``dtype`` when given.  Leaves must share the batch size, which must divide
+        by ``dp_size``."""
+        dtype = None if dtype is None else normalize_dtype("dtype", dtype)
+        leaves = []
+
+        def prep(x):
+            if isinstance(x, Mapping):
+                return type(x)((k, prep(v)) for k, v in x.items())
+            if isinstance(x, (list, tuple)):
+                return type(x)(prep(v) for v in x)
+            try:
+                t = x if isinstance(x, torch.Tensor) else torch.as_tensor(np.asarray(x))
+            except (TypeError, ValueError, RuntimeError) as e:
+                raise TypeError(f"prepare_input leaves must be array-like, got {type(x)}.") from e
+            if t.ndim != 2:
+                raise ValueError(f"prepare_input leaves must be 2D arrays for data/model sharding, got shape "
+                                 f"{tuple(t.shape)}.")
+            if t.shape[0] == 0:
+                raise ValueError("prepare_input leaves must contain at least one batch row.")
+            if t.shape[1] == 0:
+                raise ValueError("prepare_input leaves must contain at least one token.")
+            if t.shape[0] % self.config.dp_size != 0:
+                raise ValueError(f"prepare_input batch size must be divisible by dp_size={self.config.dp_size}, "
+                                 f"got {t.shape[0]}.")
+            if dtype is not None:
+                t = t.to(dtype)
+            leaves.append(t)
+            return t
+
+        out = prep(inputs)
+        if not leaves:
+            raise ValueError("prepare_input inputs must contain at least one array leaf.")
+        for leaf in leaves[1:]:
+            if leaf.shape[0] != leaves[0].shape[0]:
+                raise ValueError(f"prepare_input leaves must share the same batch size, got {leaves[0].shape[0]} and "
+                                 f"{leaf.shape[0]}.")
+        if not torch.cuda.is_available():
+            return out
+        dev = self._device()
+
+        def move(x):
+            if isinstance(x, Mapping):
+                return type(x)((k, move(v)) for k, v in x.items())
+            if isinstance(x, (list, tuple)):
+                return type(x)(move(v) for v in x)
+            return x.to(dev)
+
+        return move(out)
+
+    def wrapped_apply_fn(self, params, input_token, attention_mask=None, kv_caches=None, use_cache: bool = True):
+        """``engine.py:355-377``: one model call for step-by-step decoding, ``(logits of the last position
+        [B, 1, V], kv_caches)``: a prompt into empty caches from ``init_cache``, then one token per row into
+        the populated caches.  Runs the model's ``apply`` (the decoder blocks on the library's kernels);
+        ``generate`` does the same steps on the fused runtime with one CUDA-graph replay per token."""
+        out = self.model.apply(params, input_token, position_ids=None, attention_mask=attention_mask,
+                               kv_caches=kv_caches, use_cache=use_cache, keep_last_n_logits=1)
+        return out.logits, out.kv_caches
+
     def buffer_length(self, prompt_len: int, max_new_tokens: int) -> int:
         """Cache slots the reference's chunk loop ends with: (P // stride + 1) * stride, grown by stride
         until prompt + new tokens fit (engine.py:543-557)."""

@@ -120,3 +120,67 @@ def test_init_params_validates_weights_before_device_work(engine):
         engine.init_params(use_tpu=1)
     with pytest.raises(TypeError, match="reinit_weight must be a boolean"):
         engine.init_params(reinit_weight="yes")
+
+
+def test_init_cache(engine):
+    """engine.py:110-121: one empty cache per layer in the engine's dtype (the reference's
+    ``tests/test_generation.py:1119-1160`` cases)."""
+    caches = engine.init_cache(max_seq_len=np.int64(8))
+    assert len(caches) == engine.model.config.num_layers
+    assert all(c.max_seq_len == 8 and c.k is None and c.dtype == engine.dtype for c in caches)
+    for bad in (True, 1.5):
+        with pytest.raises(TypeError, match="max_seq_len must be an integer"):
+            engine.init_cache(max_seq_len=bad)
+    for bad in (0, -1):
+        with pytest.raises(ValueError, match="max_seq_len must be positive"):
+            engine.init_cache(max_seq_len=bad)
+
+    class _NoConfig:
+        config = object()
+
+    class _Cfg:
+        def __init__(self, n):
+            self.num_layers = n
+
+    class _Model:
+        def __init__(self, n):
+            self.config = _Cfg(n)
+
+    with pytest.raises(TypeError, match="config.num_layers"):
+        Engine(_NoConfig(), InferenceConfig(), {"params": {}}).init_cache(8)
+    for n, exc, match in ((True, TypeError, "model.config.num_layers must be an integer"),
+                          (1.5, TypeError, "model.config.num_layers must be an integer"),
+                          (0, ValueError, "model.config.num_layers must be positive")):
+        with pytest.raises(exc, match=match):
+            Engine(_Model(n), InferenceConfig(), {"params": {}}).init_cache(8)
+
+
+def test_prepare_input(engine):
+    """engine.py:320-353: 2D leaves of one batch size, cast to ``dtype`` (the reference's
+    ``tests/test_generation.py:297-485`` cases)."""
+    out = engine.prepare_input({"input_ids": np.array([[1, 2, 3]], dtype=np.int32)}, dtype=np.float32)
+    assert set(out) == {"input_ids"} and out["input_ids"].dtype == torch.float32
+    assert out["input_ids"].cpu().tolist() == [[1.0, 2.0, 3.0]]
+    out = engine.prepare_input([np.ones((2, 2), dtype=np.int64), torch.zeros(2, 5, dtype=torch.int32)])
+    assert isinstance(out, list) and out[1].dtype == torch.int32
+    for inputs, exc, match in ((object(), TypeError, "array-like"),
+                               (np.ones(3, dtype=np.int32), ValueError, "2D arrays"),
+                               (np.ones((1, 2, 3), dtype=np.int32), ValueError, "2D arrays"),
+                               ({}, ValueError, "at least one array leaf"),
+                               ({"x": np.ones((0, 2), dtype=np.int32)}, ValueError, "at least one batch row"),
+                               ({"x": np.ones((1, 0), dtype=np.int32)}, ValueError, "at least one token"),
+                               ({"a": np.ones((1, 2)), "b": np.ones((2, 2))}, ValueError, "same batch size")):
+        with pytest.raises(exc, match=match):
+            engine.prepare_input(inputs)
+    with pytest.raises(TypeError, match="valid"):
+        engine.prepare_input(np.ones((1, 2), dtype=np.int32), dtype="not-a-dtype")
+
+
+def test_prepare_input_batch_divisible_by_dp_size(engine, monkeypatch):
+    import jaxml_b200.engine as E
+
+    monkeypatch.setattr(E, "_device_count", lambda: 2)
+    eng = Engine(engine.model, InferenceConfig(dp_size=2), engine.params)
+    assert tuple(eng.prepare_input({"x": np.array([[1, 2], [3, 4]])})["x"].shape) == (2, 2)
+    with pytest.raises(ValueError, match="divisible by dp_size=2"):
+        eng.prepare_input({"x": np.array([[1, 2], [3, 4], [5, 6]])})

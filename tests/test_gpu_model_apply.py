@@ -143,3 +143,27 @@ def test_mlp_blocks_match_oracle(family, dtype, hf_models):
     want = O._mlp(family, lp, x, dtype)
     assert got.dtype == dtype and tuple(got.shape) == (2, 3, cfg.hidden_size)
     _close(got, want, dtype)
+
+
+def test_engine_step_interface_matches_generate(hf_models):
+    """``Engine.init_cache`` + ``Engine.wrapped_apply_fn`` (the reference's step-by-step decoding,
+    engine.py:110-121 and 355-377): last-position logits against the oracle, and greedy steps that give
+    the tokens ``Engine.generate`` (the fused runtime) gives."""
+    from jaxml_b200 import Engine, InferenceConfig
+
+    _, cfg, params = hf_models["llama"]
+    model = CLASSES["llama"](cfg)
+    eng = Engine(model, InferenceConfig(), params)
+    g = torch.Generator().manual_seed(10)
+    ids = torch.randint(0, cfg.vocab_size, (2, 5), generator=g, dtype=torch.int32)
+    logits, caches = eng.wrapped_apply_fn(params, ids, kv_caches=eng.init_cache(16))
+    assert tuple(logits.shape) == (2, 1, cfg.vocab_size) and len(caches) == cfg.num_layers
+    _close(logits[:, 0], O.forward("llama", cfg, params, ids, torch.float32).logits[:, -1], torch.float32)
+    toks = []
+    for _ in range(4):
+        nxt = logits[:, -1].argmax(-1, keepdim=True).to(torch.int32)
+        toks.append(nxt.cpu())
+        logits, caches = eng.wrapped_apply_fn(params, nxt, kv_caches=caches)
+    want = eng.generate(ids, max_new_tokens=4, temperature=0.0, include_prompt=False)
+    assert torch.equal(torch.cat(toks, 1), torch.as_tensor(want).cpu().to(torch.int32))
+    eng.close()
