@@ -12,13 +12,35 @@ from collections.abc import Mapping
 
 import torch
 
-from ._checks import normalize_count, normalize_dtype
+from ._checks import normalize_count
 
 _NORM_KEYS = {"post_attention_layernorm", "pre_feedforward_layernorm", "post_feedforward_layernorm",
               "input_layernorm", "norm", "q_norm", "k_norm"}
 
 
-def _normalize_state_key(key: str) -> list[str]:
+_STATE_DTYPES = {"float16": torch.float16, "bfloat16": torch.bfloat16, "float32": torch.float32,
+                 "float64": torch.float64}
+
+
+def _state_dtype(dtype) -> torch.dtype:
+    """utils.py:57-69: a dtype name or a torch floating dtype among float16 / bfloat16 / float32 / float64."""
+    if isinstance(dtype, torch.dtype):
+        name = str(dtype).replace("torch.", "")
+    elif isinstance(dtype, str):
+        name = dtype
+    else:
+        raise TypeError(f"Expected dtype to be a string or torch.dtype, got {type(dtype)}.")
+    if name not in _STATE_DTYPES:
+        raise ValueError(f"Unsupported dtype {dtype!r}. Supported dtypes are: {', '.join(_STATE_DTYPES)}.")
+    return _STATE_DTYPES[name]
+
+
+def _normalize_state_key(key) -> list[str]:
+    """``layers.3.mlp`` -> ``["layers_3", "mlp"]`` (a numeric segment joins the one before it)."""
+    if not isinstance(key, str):
+        raise TypeError(f"State key must be a string, got {type(key)}.")
+    if not key:
+        raise ValueError("State key must be non-empty.")
     out: list[str] = []
     for seg in key.split("."):
         if not seg:
@@ -30,45 +52,98 @@ def _normalize_state_key(key: str) -> list[str]:
     return out
 
 
+def _state_tensor(value, key: str) -> torch.Tensor:
+    if not isinstance(value, torch.Tensor):
+        raise TypeError(f"State value for key {key!r} must be a torch.Tensor, got {type(value)}.")
+    t = value.detach().cpu()
+    if t.numel() == 0:
+        raise ValueError(f"State value for key {key!r} must not be empty.")
+    if not t.is_floating_point():
+        raise TypeError(f"State value for key {key!r} must contain floating point values, got dtype {t.dtype}.")
+    if not bool(torch.isfinite(t).all()):
+        raise ValueError(f"State value for key {key!r} must contain only finite values.")
+    return t.to(torch.float32) if t.dtype in (torch.bfloat16, torch.float16) else t
+
+
+def _insert_leaf(tree: dict, path: list[str], value, key: str):
+    cursor = tree
+    for seg in path[:-1]:
+        nxt = cursor.setdefault(seg, {})
+        if not isinstance(nxt, dict):
+            raise ValueError(f"State key {key!r} conflicts with existing leaf at destination {'.'.join(path)!r}.")
+        cursor = nxt
+    if path[-1] in cursor:
+        raise ValueError(f"Multiple state keys map to destination {'.'.join(path)!r}.")
+    cursor[path[-1]] = value
+
+
+def _divisible(n: int, by: int, what: str, by_name: str):
+    if n % by:
+        raise ValueError(f"{what} {n} must be divisible by {by_name}.")
+
+
 def torch_to_jax_states(states, dtype=torch.float32, head_dim: int | None = None) -> dict:
-    dtype = normalize_dtype("dtype", dtype)
+    """utils.py:258-371: a torch module or state dict as the reference's parameter tree.  Dense weights
+    become ``kernel`` ``[in, out]``; with ``head_dim`` the q / k / v projections become ``[d, heads,
+    head_dim]`` and a fused ``qkv_proj`` ``[d, 3, heads, head_dim]`` (without it, ``[d, 3, -1]``);
+    embeddings become ``embedding``; norm weights stay as they are.  Leaves are CPU tensors in ``dtype``."""
+    dtype = _state_dtype(dtype)
+    if head_dim is not None:
+        if isinstance(head_dim, bool) or type(head_dim).__name__ == "bool_":
+            raise TypeError(f"head_dim must be an integer when set, got {type(head_dim)}.")
+        try:
+            head_dim = normalize_count("head_dim", head_dim)
+        except TypeError as e:
+            raise TypeError(f"head_dim must be an integer when set, got {type(head_dim)}.") from e
+        if head_dim <= 0:
+            raise ValueError(f"head_dim must be positive when set, got {head_dim}.")
     if isinstance(states, torch.nn.Module):
         states = states.state_dict()
-    if not isinstance(states, Mapping) or not states:
+    elif not isinstance(states, Mapping):
+        raise TypeError(f"Expected input to be either a PyTorch module or a mapping, got {type(states)}.")
+    if not states:
         raise ValueError("PyTorch state dict must contain at least one tensor.")
     tree: dict = {"params": {}}
+    hd = head_dim
     for key, value in states.items():
         path = _normalize_state_key(key)
-        t = value.detach().cpu().to(torch.float32)
         leaf = path[-1]
         if len(path) >= 2 and path[-2] in _NORM_KEYS:
-            pass
-        elif "embed_tokens" in path:
+            _insert_leaf(tree["params"], path, _state_tensor(value, key).contiguous().to(dtype), key)
+            continue
+        t = _state_tensor(value, key)
+        if "embed_tokens" in path:
             if leaf == "weight":
                 path[-1] = "embedding"
         elif any(p in path for p in ("q_proj", "k_proj", "v_proj")):
             if leaf == "weight":
                 path[-1] = "kernel"
-                t = t.T if head_dim is None else t.T.reshape(t.shape[1], -1, head_dim)
-            elif leaf == "bias" and head_dim is not None:
-                t = t.reshape(-1, head_dim)
+                if hd is not None:
+                    _divisible(t.shape[0], hd, "Q/K/V projection output dimension", f"head_dim {hd}")
+                t = t.T if hd is None else t.T.reshape(t.shape[1], -1, hd)
+            elif leaf == "bias" and hd is not None:
+                _divisible(t.shape[0], hd, "Q/K/V projection bias length", f"head_dim {hd}")
+                t = t.reshape(-1, hd)
         elif "qkv_proj" in path:
             if leaf == "weight":
                 path[-1] = "kernel"
-                if head_dim is None:
+                if hd is None:
+                    _divisible(t.shape[0], 3, "Fused QKV projection output dimension", "3")
                     t = t.T.reshape(t.shape[1], 3, -1)
                 else:
-                    t = t.T.reshape(t.shape[1], -1, 3, head_dim).permute(0, 2, 1, 3)
+                    _divisible(t.shape[0], 3 * hd, "Fused QKV projection output dimension", f"3 * head_dim {3 * hd}")
+                    t = t.T.reshape(t.shape[1], -1, 3, hd).permute(0, 2, 1, 3)
             elif leaf == "bias":
-                t = t.reshape(3, -1) if head_dim is None else t.reshape(-1, 3, head_dim).permute(1, 0, 2)
-        else:
-            if leaf == "weight":
-                path[-1] = "kernel"
-                t = t.T
-        cursor = tree["params"]
-        for seg in path[:-1]:
-            cursor = cursor.setdefault(seg, {})
-        cursor[path[-1]] = t.contiguous().to(dtype)
+                if hd is None:
+                    _divisible(t.shape[0], 3, "Fused QKV projection bias length", "3")
+                    t = t.reshape(3, -1)
+                else:
+                    _divisible(t.shape[0], 3 * hd, "Fused QKV projection bias length", f"3 * head_dim {3 * hd}")
+                    t = t.reshape(-1, 3, hd).permute(1, 0, 2)
+        elif leaf == "weight":
+            path[-1] = "kernel"
+            t = t.T
+        _insert_leaf(tree["params"], path, t.contiguous().to(dtype), key)
     return tree
 
 
