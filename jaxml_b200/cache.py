@@ -122,12 +122,21 @@ class KVCache:
             raise ValueError(f"Cached k and v must have the same shape, got {tuple(k.shape)} and {tuple(v.shape)}.")
         if k.ndim != 4:
             raise ValueError(f"Cached k and v must be 4D arrays, got shape {tuple(k.shape)}.")
+        if k.shape[0] <= 0:
+            raise ValueError(f"Cached k/v batch axis must be non-empty, got shape {tuple(k.shape)}.")
         if k.shape[1] != self.max_seq_len:
             raise ValueError(f"Cached k/v sequence axis must match max_seq_len={self.max_seq_len}, got {k.shape[1]}.")
-        if k.dtype != self.dtype:
-            raise TypeError(f"Cached k dtype must match cache dtype {self.dtype}, got {k.dtype}.")
-        if v.dtype != self.dtype:
-            raise TypeError(f"Cached v dtype must match cache dtype {self.dtype}, got {v.dtype}.")
+        if k.shape[2] <= 0:
+            raise ValueError(f"Cached k/v head axis must be non-empty, got shape {tuple(k.shape)}.")
+        if k.shape[3] <= 0:
+            raise ValueError(f"Cached k/v head_dim axis must be non-empty, got shape {tuple(k.shape)}.")
+        for name, x in (("k", k), ("v", v)):
+            if not x.dtype.is_floating_point:
+                raise TypeError(f"Cached {name} must contain floating point values, got dtype {x.dtype}.")
+            if x.dtype != self.dtype:
+                raise TypeError(f"Cached {name} dtype must match cache dtype {self.dtype}, got {x.dtype}.")
+        _check_finite("Cached k", k)
+        _check_finite("Cached v", v)
         if tuple(mask.shape) != tuple(k.shape[:2]):
             raise ValueError(f"Cached mask shape must match cached k/v batch and sequence axes, got {tuple(mask.shape)}.")
         if mask.dtype != torch.bool:

@@ -142,3 +142,54 @@ def test_rollback_and_resize_arguments():
     assert grown.max_seq_len == 10 and grown.k.shape[1] == 10 and torch.equal(grown.k[:, :6], cache.k)
     empty = KVCache.init(4).resize(8)
     assert empty.max_seq_len == 8 and empty.k is None
+
+
+def _state(k_shape=(1, 4, 1, 2), v_shape=None, k_dtype=torch.float32, v_dtype=None, mask=None, pos=None,
+           dtype=torch.float32, T=4):
+    k = torch.zeros(k_shape, dtype=k_dtype)
+    v = torch.zeros(v_shape or k_shape, dtype=v_dtype or k_dtype)
+    B = k_shape[0]
+    mask = torch.ones(B, k_shape[1] if len(k_shape) > 1 else 4, dtype=torch.bool) if mask is None else mask
+    pos = torch.full((B, 1), (mask.shape[1] - 1) if B else 0, dtype=torch.int32) if pos is None else pos
+    return KVCache(k=k, v=v, max_seq_len=T, mask=mask, dtype=dtype, pos_id=pos)
+
+
+def _nonfinite(field, value):
+    c = _state()
+    t = (c.k if field == "k" else c.v).clone()
+    t[0, 0, 0, 0] = value
+    return c.replace(**{field: t})
+
+
+@pytest.mark.parametrize("cache,exc,match", [
+    (_state(v_shape=(1, 3, 1, 2)), ValueError, "same shape"),
+    (_state(k_shape=(1, 4, 2), mask=torch.ones(1, 4, dtype=torch.bool)), ValueError, "4D arrays"),
+    (_state(k_shape=(0, 4, 1, 2), mask=torch.ones(0, 4, dtype=torch.bool)), ValueError, "batch axis must be non-empty"),
+    (_state(k_shape=(1, 3, 1, 2)), ValueError, "sequence axis must match"),
+    (_state(k_shape=(1, 4, 0, 2)), ValueError, "head axis must be non-empty"),
+    (_state(k_shape=(1, 4, 1, 0)), ValueError, "head_dim axis must be non-empty"),
+    (_state(k_dtype=torch.int32, v_dtype=torch.float32), TypeError, "Cached k must contain floating"),
+    (_state(k_dtype=torch.float32, v_dtype=torch.bfloat16, dtype=torch.bfloat16), TypeError,
+     "Cached k dtype must match cache dtype"),
+    (_state(v_dtype=torch.int32), TypeError, "Cached v must contain floating"),
+    (_nonfinite("k", float("nan")), ValueError, "Cached k must contain only finite values"),
+    (_nonfinite("v", float("inf")), ValueError, "Cached v must contain only finite values"),
+    (_state(v_dtype=torch.bfloat16), TypeError, "Cached v dtype must match cache dtype"),
+    (_state(mask=torch.ones(1, 3, dtype=torch.bool)), ValueError, "Cached mask shape"),
+    (_state(mask=torch.ones(1, 4, dtype=torch.int32)), TypeError, "Cached mask must be boolean"),
+    (_state(mask=torch.zeros(1, 4, dtype=torch.bool)), ValueError, "at least one valid token"),
+    (_state(mask=torch.tensor([[True, False, True, False]]), pos=torch.tensor([[2]], dtype=torch.int32)), ValueError,
+     "right padded"),
+    (_state(pos=torch.zeros(1, 2, dtype=torch.int32)), ValueError, "Cached pos_id shape"),
+    (_state(pos=torch.zeros(1, 1)), TypeError, "Cached pos_id must contain integer"),
+    (_state(pos=torch.full((1, 1), 4, dtype=torch.int32)), ValueError, r"within \[0, 4\)"),
+    (_state(pos=torch.zeros(1, 1, dtype=torch.int32)), ValueError, "last valid token position"),
+])
+def test_validate_state_rejects_invalid_populated_state(cache, exc, match):
+    """Each malformed populated cache of the reference's ``tests/test_cache.py:345-590`` table, checked
+    by ``validate_state`` and before any ``update``."""
+    with pytest.raises(exc, match=match):
+        cache.validate_state()
+    k = torch.zeros(cache.k.shape[0], 1, 1, 2) if cache.k.ndim == 4 else torch.zeros(1, 1, 1, 2)
+    with pytest.raises((TypeError, ValueError)):
+        cache.update(k, k.clone())
