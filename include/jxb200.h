@@ -170,6 +170,7 @@ typedef struct jx_attn_args {
   void* out;             /* [B*S, Hq*hd]; K128 when out_rp > 0 */
   long long ldo, out_rp;
   int* status;
+  void* weights;         /* optional [B, Hq, S, T] softmax probabilities in the dtype (output_attentions), or NULL */
 } jx_attn_args;
 
 /* Standalone rotary embedding: q [M, Hq, hd] and k [M, Hk, hd] rows at positions pos[M] (outputs may

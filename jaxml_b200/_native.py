@@ -57,7 +57,7 @@ class JxQkvArgs(ctypes.Structure):
 class JxAttnArgs(ctypes.Structure):
     _fields_ = [("B", I), ("S", I), ("Hq", I), ("Hkv", I), ("hd", I), ("T", I), ("q", P), ("k", P), ("v", P),
                 ("len_ptr", P), ("len_add", I), ("causal", I), ("window", I), ("scale", F), ("out", P),
-                ("ldo", LL), ("out_rp", LL), ("status", P)]
+                ("ldo", LL), ("out_rp", LL), ("status", P), ("weights", P)]
 
 
 class JxRopeArgs(ctypes.Structure):

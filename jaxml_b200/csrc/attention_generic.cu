@@ -2,8 +2,9 @@
 // float32 path and shapes the tensor-core kernels do not cover, and reproduces Attention.mha
 // (nn/attention.py:321-400) exactly: scores = dtype(dtype(q.k) * dtype(attn_scale)); causal, sliding
 // window and prefix-padding masks; a row with no visible key attends uniformly to all T slots;
-// float32 softmax rounded to dtype; dtype(sum p*v) with float32 accumulation.  KV heads are shared
-// by n_rep = Hq / Hkv query heads (repeat_kv, :294-319) by indexing, not copying.
+// float32 softmax rounded to dtype (optionally stored: the attention weights); dtype(sum p*v) with
+// float32 accumulation.  KV heads are shared by n_rep = Hq / Hkv query heads (repeat_kv, :294-319) by
+// indexing, not copying.
 #include "common.cuh"
 
 namespace jxb {
@@ -64,6 +65,11 @@ __global__ void __launch_bounds__(128) attention_generic_kernel(AttnArgs p) {
   __syncthreads();
   l = (red[0] + red[1]) + (red[2] + red[3]);
   for (int j = tid; j < p.T; j += 128) sc[j] = rnd<T>(sc[j] / l);
+  if (p.weights) {
+    // the probabilities themselves (Attention.mha with output_attentions): [B, Hq, S, T]
+    T* w = reinterpret_cast<T*>(p.weights) + (((long long)b * p.Hq + h) * p.S + s) * p.T;
+    for (int j = tid; j < p.T; j += 128) w[j] = from_f<T>(sc[j]);
+  }
   __syncthreads();
   for (int d = tid; d < p.hd; d += 128) {
     float acc = 0.f;

@@ -390,12 +390,13 @@ def _rope_vars(cfg, dtype, base: float, scale: float):
 
 def layered_forward(family: str, cfg, dtype, body: dict, ids: torch.Tensor, attention_mask: Optional[torch.Tensor],
                     position_ids: Optional[torch.Tensor], kv_caches: Optional[tuple], cached_len: Optional[int],
-                    rope_cache: dict):
+                    rope_cache: dict, output_attentions: bool = False):
     """Embedding, the decoder layers and the final norm over ``body`` (the stack's parameters, leaves on
     the device in ``dtype``).  ``ids`` [B, S] with placeholders already mapped to 0; ``attention_mask``
     the prepared boolean mask or None (populated caches); ``cached_len`` the caches' sequence length (the
-    rotary table length the reference checks).  Returns ``(last_hidden_state, next_caches, hidden_states)``
-    with hidden_states the input of every layer followed by the final-norm output."""
+    rotary table length the reference checks).  Returns ``(last_hidden_state, next_caches, hidden_states,
+    attention_weights)``: hidden_states the input of every layer followed by the final-norm output, the
+    weights [B, H, S, T] of every layer when ``output_attentions`` (else Nones)."""
     d = cfg.hidden_size
     scale = 0.0
     if family == "gemma3":
@@ -417,7 +418,7 @@ def layered_forward(family: str, cfg, dtype, body: dict, ids: torch.Tensor, atte
         lrope, lrv = rope_cache["local"]
         cos_sin_local = lrope.apply(lrv, h, seq_len=cached_len)
         stride = cfg.sliding_window_pattern or 1
-    hidden, caches = [], []
+    hidden, caches, weights = [], [], []
     for idx in range(cfg.num_layers):
         hidden.append(h)
         if family == "gemma3":
@@ -428,15 +429,16 @@ def layered_forward(family: str, cfg, dtype, body: dict, ids: torch.Tensor, atte
             cs = cos_sin
         cache = None if kv_caches is None else kv_caches[idx]
         out = dec.apply({"params": body[f"layers_{idx}"]}, h, cos_sin=cs, attention_mask=attention_mask,
-                        position_ids=position_ids, kv_cache=cache)
+                        position_ids=position_ids, kv_cache=cache, output_attentions=output_attentions)
         h = out.hidden_states
         caches.append(out.kv_cache)
+        weights.append(out.attention_weight)
     fw = _weight(body["norm"], "weight", dtype)
     fb = _weight(body["norm"], "bias", dtype)
     kind = {"llama": N.JX_NORM_RMS, "neox": N.JX_NORM_LAYER, "gemma3": N.JX_NORM_GEMMA}[family]
     _, h = _add_norm(h, kind=kind, w=fw, b=fb, eps=cfg.norm_eps)
     hidden.append(h)
-    return h, tuple(caches), tuple(hidden)
+    return h, tuple(caches), tuple(hidden), tuple(weights)
 
 
 def device_tree(tree, dtype: torch.dtype, dev: torch.device):

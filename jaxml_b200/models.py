@@ -66,16 +66,16 @@ class _DecoderWithHead:
         the GPU kernels: logits ``[B, S]`` (or the last ``keep_last_n_logits`` positions) in the model dtype,
         in a ``CausalLMOutputWithCache``.  A cache-free call without position ids or hidden states runs on
         the fused prefill runtime; calls with KV caches (a prompt into empty caches, or one token per row
-        into populated ones), position ids or ``output_hidden_states`` run layer by layer through the
-        decoder blocks.  Masks must be right-padded; attention weights are not produced
-        (``output_attentions=True`` raises ``NotImplementedError``)."""
+        into populated ones), position ids, ``output_hidden_states`` or ``output_attentions`` run layer by
+        layer through the decoder blocks.  Masks must be right-padded."""
         from ._checks import normalize_count
 
         keep = normalize_count("keep_last_n_logits", keep_last_n_logits)
         if keep < 0:
             raise ValueError(f"keep_last_n_logits must be non-negative, got {keep}.")
-        hidden, caches, states, is_logits = self._stack(params, input_ids, attention_mask, position_ids, kv_caches,
-                                                        use_cache, output_attentions, output_hidden_states, keep)
+        hidden, caches, states, weights, is_logits = self._stack(params, input_ids, attention_mask, position_ids,
+                                                                 kv_caches, use_cache, output_attentions,
+                                                                 output_hidden_states, keep)
         if is_logits:
             return CausalLMOutputWithCache(logits=hidden, kv_caches=caches)
         h = hidden if keep == 0 else hidden[:, -keep:]
@@ -85,7 +85,8 @@ class _DecoderWithHead:
 
         logits = _nn._dense(h.reshape(B * n, d), head, None, self.dtype).reshape(B, n, -1)
         _nn._check_status(h.device, "lm_head")
-        return CausalLMOutputWithCache(logits=logits, kv_caches=caches, hidden_states=states)
+        return CausalLMOutputWithCache(logits=logits, kv_caches=caches, hidden_states=states,
+                                       attention_weights=weights)
 
     def _head_kernel(self, params) -> torch.Tensor:
         """The LM head kernel [d, V] on the device in the model dtype (cached with the converted tree)."""
@@ -113,8 +114,9 @@ class _DecoderWithHead:
 
     def _stack(self, params, input_ids, attention_mask, position_ids, kv_caches, use_cache, output_attentions,
                output_hidden_states, keep):
-        """The stack below the head.  Returns ``(last_hidden_state, kv_caches, hidden_states, False)``; on the
-        fused runtime path of a model with a head, ``(logits, kv_caches, None, True)``."""
+        """The stack below the head.  Returns ``(last_hidden_state, kv_caches, hidden_states,
+        attention_weights, False)``; on the fused runtime path of a model with a head, ``(logits, kv_caches,
+        None, None, True)``."""
         from ._checks import normalize_bool
 
         use_cache = normalize_bool("use_cache", use_cache)
@@ -122,28 +124,28 @@ class _DecoderWithHead:
         output_hidden_states = normalize_bool("output_hidden_states", output_hidden_states)
         ids, mask, kv_caches, pos = _prepare_model_inputs(self.config, input_ids, attention_mask, kv_caches,
                                                           position_ids)
-        if output_attentions:
-            raise NotImplementedError("output_attentions: the CUDA attention kernels do not return the weights.")
         L = self.config.num_layers
         if mask is not None and not _right_padded(mask):
             raise NotImplementedError("apply takes right-padded attention masks (the kernels attend to key prefixes).")
-        if kv_caches is None and pos is None and not output_hidden_states:
+        if kv_caches is None and pos is None and not output_hidden_states and not output_attentions:
             B, S = ids.shape
             rt = self._runtime(params, B, S)
             dev = rt.w.device
             caches = (None,) * L if use_cache else None
             if self._has_head:
-                return rt.forward_logits(ids.to(dev), mask.to(dev), keep), caches, None, True
-            return rt.forward_hidden(ids.to(dev), mask.to(dev)), caches, None, False
+                return rt.forward_logits(ids.to(dev), mask.to(dev), keep), caches, None, None, True
+            return rt.forward_hidden(ids.to(dev), mask.to(dev)), caches, None, None, False
         from .decoders import layered_forward, _cached_sequence_length
 
         body = self._body(params)
         dev = body["embed_tokens"]["embedding"].device
         cached_len = _cached_sequence_length(kv_caches)
-        h, caches, states = layered_forward(
+        h, caches, states, weights = layered_forward(
             self.family, self.config, self.dtype, body, ids.to(dev), None if mask is None else mask.to(dev),
-            None if pos is None else pos.to(dev), kv_caches, cached_len, self.__dict__["_layered_cache"]["rope"])
-        return h, (caches if use_cache else None), (states if output_hidden_states else None), False
+            None if pos is None else pos.to(dev), kv_caches, cached_len, self.__dict__["_layered_cache"]["rope"],
+            output_attentions)
+        return (h, caches if use_cache else None, states if output_hidden_states else None,
+                weights if output_attentions else None, False)
 
     _has_head = True
 
@@ -273,8 +275,8 @@ def _prepare_model_inputs(config, input_ids, attention_mask, kv_caches=None, pos
 
 @dataclass
 class CausalLMOutputWithCache:
-    """``outputs.py``: logits, the updated caches and per-layer hidden states when asked for (attention
-    weights are not produced)."""
+    """``outputs.py``: logits, and the updated caches, per-layer hidden states and attention weights when
+    asked for."""
 
     logits: torch.Tensor
     kv_caches: Optional[tuple] = None
@@ -284,8 +286,8 @@ class CausalLMOutputWithCache:
 
 @dataclass
 class BaseModelOutputWithCache:
-    """``outputs.py``: the decoder stack's final hidden states, the updated caches and per-layer hidden
-    states when asked for (attention weights are not produced)."""
+    """``outputs.py``: the decoder stack's final hidden states, and the updated caches, per-layer hidden
+    states and attention weights when asked for."""
 
     last_hidden_state: torch.Tensor
     kv_caches: Optional[tuple] = None
@@ -330,12 +332,13 @@ class _DecoderStack(_DecoderWithHead):
     def apply(self, params, input_ids, attention_mask=None, position_ids=None, kv_caches=None,
               output_attentions=False, output_hidden_states=False, use_cache=False):
         """``*Model.__call__`` (models/llama.py:161-225, gpt_neox.py:158-222, gemma3.py:215-283):
-        ``last_hidden_state`` [B, S, d] after the final norm, the updated caches (``use_cache``) and the
-        per-layer hidden states (``output_hidden_states``) in a ``BaseModelOutputWithCache``.  Same inputs,
-        paths and limits as ``*ModelWithHead.apply``."""
-        h, caches, states, _ = self._stack(params, input_ids, attention_mask, position_ids, kv_caches, use_cache,
-                                           output_attentions, output_hidden_states, 0)
-        return BaseModelOutputWithCache(last_hidden_state=h, kv_caches=caches, hidden_states=states)
+        ``last_hidden_state`` [B, S, d] after the final norm, the updated caches (``use_cache``), the
+        per-layer hidden states (``output_hidden_states``) and attention weights (``output_attentions``) in
+        a ``BaseModelOutputWithCache``.  Same inputs, paths and limits as ``*ModelWithHead.apply``."""
+        h, caches, states, weights, _ = self._stack(params, input_ids, attention_mask, position_ids, kv_caches,
+                                                    use_cache, output_attentions, output_hidden_states, 0)
+        return BaseModelOutputWithCache(last_hidden_state=h, kv_caches=caches, hidden_states=states,
+                                        attention_weights=weights)
 
 
 class LlamaModel(_DecoderStack):

@@ -311,11 +311,19 @@ class _Base:
         self._check_inputs(variables, *args, **kwargs)
         return variables
 
-    def apply(self, variables, *args, **kwargs):
+    def apply(self, variables, *args, method=None, **kwargs):
+        """Runs the module (or, with ``method``, one of its methods: a function of the class such as
+        ``Attention.mha``, or its name) on ``variables``, the Flax way."""
         self._setup()
         if not isinstance(variables, dict):
             raise TypeError(f"variables must be a mapping, got {type(variables)}.")
-        return self._call(variables, *args, **kwargs)
+        if method is None:
+            return self._call(variables, *args, **kwargs)
+        name = method if isinstance(method, str) else getattr(method, "__name__", None)
+        fn = getattr(type(self), name, None) if name else None
+        if name is None or name.startswith("_") or not callable(fn):
+            raise ValueError(f"{type(self).__name__} has no method {method!r} to apply.")
+        return fn(self, variables, *args, **kwargs)
 
 
 def _params(variables: dict) -> dict:
@@ -804,13 +812,15 @@ def _prefix_lengths(mask: torch.Tensor) -> torch.Tensor:
     return m.sum(dim=1).to(torch.int32)
 
 
-def _mha(q, k, v, lengths, len_add: int, causal: bool, window: int, scale: float, dtype) -> torch.Tensor:
-    """q [B, S, Hq, hd], k / v [B, T, Hkv, hd], keys j < lengths[b] + len_add visible -> [B, S, Hq*hd]."""
+def _mha(q, k, v, lengths, len_add: int, causal: bool, window: int, scale: float, dtype, weights: bool = False):
+    """q [B, S, Hq, hd], k / v [B, T, Hkv, hd], keys j < lengths[b] + len_add visible -> [B, S, Hq*hd], and
+    with ``weights`` also the softmax probabilities [B, Hq, S, T] (else None)."""
     dev = q.device
     B, S, Hq, hd = q.shape
     T, Hkv = k.shape[1], k.shape[2]
     qc, kc, vc = q.to(dtype).contiguous(), k.to(dtype).contiguous(), v.to(dtype).contiguous()
     out = torch.empty(B * S, Hq * hd, dtype=dtype, device=dev)
+    w = torch.empty(B, Hq, S, T, dtype=dtype, device=dev) if weights else None
     ln = lengths.to(device=dev, dtype=torch.int32).contiguous()
     a = N.JxAttnArgs()
     a.B, a.S, a.Hq, a.Hkv, a.hd, a.T = B, S, Hq, Hkv, hd, T
@@ -819,8 +829,39 @@ def _mha(q, k, v, lengths, len_add: int, causal: bool, window: int, scale: float
     a.causal, a.window, a.scale = 1 if (causal and S > 1) else 0, window, scale
     a.out, a.ldo, a.out_rp = out.data_ptr(), Hq * hd, 0
     a.status = _state(dev).status.data_ptr()
+    a.weights = None if w is None else w.data_ptr()
     N.check(N.load().jx_attention(a, _jdt(dtype), 0, _stream(dev)), "jx_attention")
-    return out.reshape(B, S, Hq * hd)
+    return out.reshape(B, S, Hq * hd), w
+
+
+def _as_states(x) -> torch.Tensor:
+    return x if isinstance(x, torch.Tensor) else torch.as_tensor(np.asarray(x))
+
+
+def _check_states(name: str, x: torch.Tensor):
+    """A finite float [batch, sequence, head, head_dim] array (nn/attention.py:48-64)."""
+    if x.ndim != 4:
+        raise ValueError(f"{name} must be a 4D array, got shape {tuple(x.shape)}.")
+    for axis, size in zip(("batch", "sequence", "head", "head_dim"), x.shape):
+        if size <= 0:
+            raise ValueError(f"{name} {axis} axis must be non-empty, got shape {tuple(x.shape)}.")
+    if not x.is_floating_point():
+        raise TypeError(f"{name} must contain floating point values, got dtype {x.dtype}.")
+    _finite(name, x)
+
+
+def _optional_positive(name: str, value) -> Optional[int]:
+    if value is None:
+        return None
+    if isinstance(value, (bool, np.bool_)):
+        raise TypeError(f"{name} must be an integer when set, got {type(value)}.")
+    try:
+        value = normalize_count(name, value)
+    except TypeError as e:
+        raise TypeError(f"{name} must be an integer when set, got {type(value)}.") from e
+    if value <= 0:
+        raise ValueError(f"{name} must be positive when set, got {value}.")
+    return value
 
 
 class Attention(Block):
@@ -905,14 +946,92 @@ class Attention(Block):
             k = norms[1].apply({"params": p["k_norm"]}, k)
         return q, k, v
 
+    def repeat_kv(self, variables, key_states, value_states):
+        """nn/attention.py:294-319: key / value states [B, T, Hkv, hd] broadcast to the query heads
+        [B, T, Hkv * n_rep, hd] (head h reads KV head h // n_rep).  The kernels index the shared head
+        instead; this method is for callers that want the repeated arrays."""
+        k, v = _as_states(key_states), _as_states(value_states)
+        for name, x in (("key_states", k), ("value_states", v)):
+            _check_states(name, x)
+        if k.shape != v.shape:
+            raise ValueError(f"key_states and value_states must have the same shape, got {tuple(k.shape)} and "
+                             f"{tuple(v.shape)}.")
+        Hkv, hd = self.config.num_key_value_heads, self.config.head_dim
+        if k.shape[2] != Hkv:
+            raise ValueError(f"key_states and value_states must match config.num_key_value_heads, got {k.shape[2]} "
+                             f"and expected {Hkv}.")
+        if k.shape[-1] != hd:
+            raise ValueError(f"key_states and value_states must match config.head_dim, got {k.shape[-1]} and "
+                             f"expected {hd}.")
+        n_rep = self.config.num_heads // Hkv
+        if n_rep == 1:
+            return k, v
+        B, T = k.shape[:2]
+        return tuple(x[:, :, :, None, :].expand(B, T, Hkv, n_rep, hd).reshape(B, T, Hkv * n_rep, hd) for x in (k, v))
+
+    def mha(self, variables, query_states, key_states, value_states, attention_mask=None, causal=True,
+            sliding_window=None, alibi_slope=None, softmax_fp32=True, output_attentions=False):
+        """nn/attention.py:321-400 on ``jx_attention``: ``(attn_output [B, S, H, hd], weights [B, H, S, T] or
+        None)`` for q [B, S, H, hd] and k / v [B, T, H, hd] (already repeated).  Same checks and
+        messages; the kernel takes prefix (right-padded) masks, a float32 softmax and no ALiBi slope,
+        and anything else raises ``NotImplementedError``."""
+        q, k, v = _as_states(query_states), _as_states(key_states), _as_states(value_states)
+        for name, x in (("query_states", q), ("key_states", k), ("value_states", v)):
+            _check_states(name, x)
+        if k.shape != v.shape:
+            raise ValueError(f"key_states and value_states must have the same shape, got {tuple(k.shape)} and "
+                             f"{tuple(v.shape)}.")
+        if q.shape[0] != k.shape[0] or q.shape[2:] != k.shape[2:]:
+            raise ValueError("query_states and key_states must have matching batch, head count, and head dimension, "
+                             f"got {tuple(q.shape)} and {tuple(k.shape)}.")
+        window = _optional_positive("sliding_window", sliding_window)
+        causal = normalize_bool("causal", causal)
+        softmax_fp32 = normalize_bool("softmax_fp32", softmax_fp32)
+        output_attentions = normalize_bool("output_attentions", output_attentions)
+        if alibi_slope is not None:
+            slope = _as_states(alibi_slope)
+            if slope.ndim != 1:
+                raise ValueError("alibi_slope must be a 1D array with one value per attention head, got shape "
+                                 f"{tuple(slope.shape)}.")
+            if slope.shape[0] != q.shape[2]:
+                raise ValueError(f"alibi_slope must contain {q.shape[2]} values, got {slope.shape[0]}.")
+            if not slope.is_floating_point():
+                raise TypeError(f"alibi_slope must contain floating point values, got dtype {slope.dtype}.")
+            _finite("alibi_slope", slope)
+        B, S, T = q.shape[0], q.shape[1], k.shape[1]
+        lengths = None
+        if attention_mask is not None:
+            m = _as_states(attention_mask)
+            if tuple(m.shape) != (B, T):
+                raise ValueError("attention_mask shape must match attention batch and key length, "
+                                 f"got {tuple(m.shape)} and {(B, T)}.")
+            if m.is_floating_point() or m.is_complex():
+                raise TypeError(f"attention_mask must be boolean or integer, got dtype {m.dtype}.")
+            if m.dtype != torch.bool and bool(((m != 0) & (m != 1)).any()):
+                raise ValueError("attention_mask integer values must be 0 or 1.")
+            lengths = _prefix_lengths(m.to(torch.bool))
+        if alibi_slope is not None:
+            raise NotImplementedError("ALiBi attention is not implemented by the CUDA attention kernels.")
+        if not softmax_fp32:
+            raise NotImplementedError("softmax_fp32=False: the CUDA attention kernels compute the softmax in float32.")
+        if window is not None and S > 1 and not causal:
+            raise NotImplementedError("a sliding window on a non-causal multi-query call is not implemented by the "
+                                      "CUDA attention kernels.")
+        _need_cuda("Attention.mha", q, k, v)
+        if lengths is None:
+            lengths = torch.full((B,), T, dtype=torch.int32)
+        out, w = _mha(q, k, v, lengths, 0, causal, window or 0, float(self.attn_scale), q.dtype,
+                      weights=output_attentions)
+        _check_status(q.device, "Attention.mha")
+        return out.reshape(B, S, q.shape[2], q.shape[3]), w
+
     def post_mha(self, variables, attn_output: torch.Tensor) -> torch.Tensor:
         o = self._projections()["o_proj"]
         return o.apply({"params": _params(variables)["o_proj"]}, attn_output.reshape(attn_output.shape[:2] + (-1,)))
 
     def _attend(self, variables, hidden, q, k, v, attention_mask, kv_cache, sliding_window, output_attentions,
                 use_flash):
-        if normalize_bool("output_attentions", output_attentions):
-            raise NotImplementedError("output_attentions: the CUDA attention kernels do not return the weights.")
+        output_attentions = normalize_bool("output_attentions", output_attentions)
         if normalize_bool("use_flash", use_flash):
             raise NotImplementedError("JAX flash attention is not enabled in jaxml yet.")
         window = 0 if sliding_window is None else normalize_count("sliding_window", sliding_window)
@@ -936,10 +1055,10 @@ class Attention(Block):
                 attention_mask if isinstance(attention_mask, torch.Tensor) else torch.as_tensor(attention_mask))
             lengths, len_add = _prefix_lengths(mask.to(hidden.device)), 0
         _need_cuda("Attention", q, keys, values)
-        out = _mha(q, keys, values, lengths, len_add, True, window, float(self.attn_scale), self.dtype)
+        out, w = _mha(q, keys, values, lengths, len_add, True, window, float(self.attn_scale), self.dtype,
+                      weights=output_attentions)
         _check_status(q.device, "Attention")
-        return AttentionOutput(attention_output=self.post_mha(variables, out), attention_weight=None,
-                               kv_cache=kv_cache)
+        return AttentionOutput(attention_output=self.post_mha(variables, out), attention_weight=w, kv_cache=kv_cache)
 
     def _call(self, variables, hidden_states, attention_mask=None, position_ids=None, kv_cache=None,
               output_attentions=False, use_flash=False, sliding_window=None, **kwargs):

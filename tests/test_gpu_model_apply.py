@@ -167,3 +167,25 @@ def test_engine_step_interface_matches_generate(hf_models):
     want = eng.generate(ids, max_new_tokens=4, temperature=0.0, include_prompt=False)
     assert torch.equal(torch.cat(toks, 1), torch.as_tensor(want).cpu().to(torch.int32))
     eng.close()
+
+
+@pytest.mark.parametrize("family", ["llama", "gemma3"])
+def test_apply_output_attentions(family, hf_models):
+    """``output_attentions``: one [B, H, S, S] probability array per layer (causal, rows summing to one, the
+    sliding window on Gemma's local layers), with logits unchanged against the oracle."""
+    _, cfg, params = hf_models[family]
+    model = CLASSES[family](cfg)
+    g = torch.Generator().manual_seed(11)
+    ids = torch.randint(0, cfg.vocab_size, (2, 7), generator=g, dtype=torch.int32)
+    out = model.apply(params, ids, output_attentions=True)
+    _close(out.logits, O.forward(family, cfg, params, ids, torch.float32).logits, torch.float32)
+    assert len(out.attention_weights) == cfg.num_layers
+    upper = torch.triu(torch.ones(7, 7, dtype=torch.bool), 1)
+    for li, w in enumerate(out.attention_weights):
+        w = w.float().cpu()
+        assert tuple(w.shape) == (2, cfg.num_heads, 7, 7)
+        assert torch.allclose(w.sum(-1), torch.ones(2, cfg.num_heads, 7), atol=1e-5)
+        assert bool((w[..., upper] == 0).all())
+        if family == "gemma3" and (li + 1) % cfg.sliding_window_pattern:
+            lower = torch.tril(torch.ones(7, 7, dtype=torch.bool), -cfg.sliding_window)
+            assert bool((w[..., lower] == 0).all())

@@ -145,3 +145,73 @@ def test_attention_without_cache_and_sliding_window_matches_oracle():
                   cfg.attn_scale)
         ref = O.dense(o.reshape(B, S, -1), p["o_proj"]["kernel"].cpu(), None, torch.float32)
         torch.testing.assert_close(out.attention_output.cpu(), ref, rtol=1e-4, atol=1e-4)
+
+
+def _attn1(**kw):
+    base = dict(head_dim=1, hidden_size=1, num_heads=1, num_layers=1, max_position_embeddings=8, vocab_size=8,
+                attn_scale=1.0, use_rope=False)
+    base.update(kw)
+    return nn.Attention(ModelConfig(**base))
+
+
+def test_mha_known_answers():
+    """``Attention.mha`` with weights (the reference's ``tests/test_attention.py:108-240`` cases): a decode
+    sliding window without and with a padded cache mask, an all-masked row, an integer mask."""
+    attn = _attn1()
+    q = torch.zeros(1, 1, 1, 1, device="cuda")
+    out, w = attn.apply({}, q, torch.zeros(1, 5, 1, 1, device="cuda"),
+                        torch.arange(5.0, device="cuda").reshape(1, 5, 1, 1) * 10, sliding_window=2,
+                        output_attentions=True, method=nn.Attention.mha)
+    assert torch.allclose(out.cpu(), torch.tensor([[[[35.0]]]]))
+    assert torch.allclose(w.cpu(), torch.tensor([[[[0.0, 0.0, 0.0, 0.5, 0.5]]]]))
+    mask = torch.tensor([[True, True, True, True, False, False, False, False]], device="cuda")
+    out, w = attn.apply({}, q, torch.zeros(1, 8, 1, 1, device="cuda"),
+                        torch.arange(8.0, device="cuda").reshape(1, 8, 1, 1) * 10, attention_mask=mask,
+                        sliding_window=2, output_attentions=True, method="mha")
+    assert torch.allclose(out.cpu(), torch.tensor([[[[25.0]]]]))
+    assert torch.allclose(w.cpu(), torch.tensor([[[[0.0, 0.0, 0.5, 0.5, 0.0, 0.0, 0.0, 0.0]]]]))
+    out, w = attn.apply({}, q, torch.zeros(1, 2, 1, 1, device="cuda"),
+                        torch.tensor([[[[2.0]], [[4.0]]]], device="cuda"),
+                        attention_mask=torch.tensor([[False, False]], device="cuda"), output_attentions=True,
+                        method=nn.Attention.mha)
+    assert torch.isfinite(out).all() and torch.allclose(out.cpu(), torch.tensor([[[[3.0]]]]))
+    assert torch.allclose(w.cpu(), torch.tensor([[[[0.5, 0.5]]]]))
+    v = torch.arange(3.0, device="cuda").reshape(1, 3, 1, 1)
+    o1, w1 = attn.apply({}, q, torch.zeros(1, 3, 1, 1, device="cuda"), v,
+                        attention_mask=torch.tensor([[1, 1, 0]], dtype=torch.int32), output_attentions=True,
+                        method=nn.Attention.mha)
+    o2, w2 = attn.apply({}, q, torch.zeros(1, 3, 1, 1, device="cuda"), v,
+                        attention_mask=torch.tensor([[True, True, False]]), output_attentions=True,
+                        method=nn.Attention.mha)
+    assert torch.equal(o1, o2) and torch.equal(w1, w2)
+    o3, w3 = attn.apply({}, q, torch.zeros(1, 3, 1, 1, device="cuda"), v, method=nn.Attention.mha)
+    assert w3 is None and tuple(o3.shape) == (1, 1, 1, 1)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("S,T,causal,window,padded", [(6, 6, True, None, False), (6, 6, True, 3, True),
+                                                      (1, 9, True, None, True), (1, 9, True, 4, True),
+                                                      (1, 9, False, 4, False), (4, 4, False, None, True)])
+def test_mha_matches_oracle(dtype, S, T, causal, window, padded):
+    """``Attention.mha`` output and weights against the oracle's ``mha`` (prefill and decode shapes,
+    causal, sliding window, right-padded masks)."""
+    H, hd = 4, 16
+    attn = _attn1(head_dim=hd, hidden_size=H * hd, num_heads=H, attn_scale=hd ** -0.5)
+    g = torch.Generator().manual_seed(S * 31 + T)
+    q = torch.randn(2, S, H, hd, generator=g).to(dtype)
+    k = torch.randn(2, T, H, hd, generator=g).to(dtype)
+    v = torch.randn(2, T, H, hd, generator=g).to(dtype)
+    mask = None
+    if padded:
+        mask = torch.ones(2, T, dtype=torch.bool)
+        mask[1, T - 2:] = False
+    out, w = attn.apply({}, q.cuda(), k.cuda(), v.cuda(), attention_mask=None if mask is None else mask.cuda(),
+                        causal=causal, sliding_window=window, output_attentions=True, method=nn.Attention.mha)
+    ref, ref_w = O.mha(q, k, v, mask, causal, window, hd ** -0.5, return_weights=True)
+    assert out.dtype == dtype and tuple(w.shape) == (2, H, S, T)
+    if dtype == torch.float32:
+        torch.testing.assert_close(out.cpu(), ref, rtol=1e-5, atol=1e-5)
+        torch.testing.assert_close(w.cpu(), ref_w, rtol=1e-5, atol=1e-6)
+    else:
+        _close_bf16(out, ref)
+        _close_bf16(w, ref_w)

@@ -61,11 +61,9 @@ def test_mask_contents():
         model.apply(params, torch.tensor([[-100, 1]], dtype=torch.int32))
 
 
-def test_unsupported_options_and_flag_types():
+def test_flag_types():
     model, params = MODELS[0]
     ids = torch.ones(1, 3, dtype=torch.int32)
-    with pytest.raises(NotImplementedError, match="output_attentions"):
-        model.apply(params, ids, output_attentions=True)
     for kw, match in (({"use_cache": 1}, "use_cache must be a boolean"),
                       ({"use_cache": None}, "use_cache must be a boolean"),
                       ({"output_attentions": 1}, "output_attentions must be a boolean"),
@@ -173,7 +171,7 @@ def test_stack_model_init_and_input_checks(fam):
         model.apply(params, torch.arange(4, dtype=torch.int32))
     with pytest.raises(ValueError, match="less than vocab_size"):
         model.apply(params, torch.tensor([[0, 50]], dtype=torch.int32))
-    with pytest.raises(NotImplementedError, match="output_attentions"):
-        model.apply(params, torch.ones(1, 4, dtype=torch.int32), output_attentions=np.bool_(True))
+    with pytest.raises(TypeError, match="output_attentions must be a boolean"):
+        model.apply(params, torch.ones(1, 4, dtype=torch.int32), output_attentions=1)
     with pytest.raises(ValueError, match="one cache per layer"):
         model.apply(params, torch.ones(1, 4, dtype=torch.int32), kv_caches=(None, None))

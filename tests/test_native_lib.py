@@ -18,7 +18,7 @@ def test_struct_layouts_match_the_header():
     assert ctypes.sizeof(N.JxEpilogue) == 216
     assert ctypes.sizeof(N.JxNormArgs) == 232
     assert ctypes.sizeof(N.JxQkvArgs) == 128
-    assert ctypes.sizeof(N.JxAttnArgs) == 104
+    assert ctypes.sizeof(N.JxAttnArgs) == 112
     assert ctypes.sizeof(N.JxSampleArgs) == 168
 
 

@@ -176,3 +176,94 @@ def test_apply_refuses_cpu_tensors():
     v = {"params": {k: t.cpu() for k, t in v["params"].items()}}
     with pytest.raises(RuntimeError, match="CUDA tensors only"):
         m.apply(v, torch.ones(1, 4))
+
+
+def _attn1(**kw):
+    from jaxml_b200 import ModelConfig
+    from jaxml_b200.nn import Attention
+
+    base = dict(head_dim=1, hidden_size=1, num_heads=1, num_layers=1, max_position_embeddings=8, vocab_size=8,
+                attn_scale=1.0, use_rope=False)
+    base.update(kw)
+    return Attention(ModelConfig(**base))
+
+
+def test_repeat_kv_on_cpu():
+    """nn/attention.py:294-319 (``tests/test_attention.py:245-340`` cases): the grouped heads repeated."""
+    from jaxml_b200.nn import Attention
+
+    attn = _attn1(head_dim=2, hidden_size=4, num_heads=2, num_kv_heads=1, attn_scale=2 ** -0.5)
+    k = torch.tensor([[[[1.0, 2.0]], [[3.0, 4.0]]]])
+    keys, values = attn.apply({}, k, k + 10, method=Attention.repeat_kv)
+    assert tuple(keys.shape) == (1, 2, 2, 2) and tuple(values.shape) == (1, 2, 2, 2)
+    assert torch.equal(keys[:, :, 1], k[:, :, 0]) and torch.equal(values[:, :, 1], k[:, :, 0] + 10)
+    z = torch.zeros
+    for kw, exc, match in (({"key_states": z(1, 2, 1)}, ValueError, "key_states must be a 4D array"),
+                           ({"key_states": z(0, 2, 1, 2)}, ValueError, "batch axis must be non-empty"),
+                           ({"key_states": z(1, 0, 1, 2)}, ValueError, "sequence axis must be non-empty"),
+                           ({"key_states": z(1, 2, 0, 2)}, ValueError, "head axis must be non-empty"),
+                           ({"key_states": z(1, 2, 1, 0)}, ValueError, "head_dim axis must be non-empty"),
+                           ({"value_states": z(1, 2, 1, 2, dtype=torch.int32)}, TypeError,
+                            "value_states must contain floating"),
+                           ({"value_states": z(1, 3, 1, 2)}, ValueError, "key_states and value_states"),
+                           ({"key_states": z(1, 2, 2, 2), "value_states": z(1, 2, 2, 2)}, ValueError,
+                            "num_key_value_heads"),
+                           ({"key_states": z(1, 2, 1, 3), "value_states": z(1, 2, 1, 3)}, ValueError,
+                            "config.head_dim")):
+        args = {"key_states": z(1, 2, 1, 2), "value_states": z(1, 2, 1, 2)}
+        args.update(kw)
+        with pytest.raises(exc, match=match):
+            attn.apply({}, method="repeat_kv", **args)
+    for field in ("key_states", "value_states"):
+        args = {"key_states": z(1, 2, 1, 2), "value_states": z(1, 2, 1, 2)}
+        args[field][0, 0, 0, 0] = float("nan")
+        with pytest.raises(ValueError, match=f"{field} must contain only finite values"):
+            attn.apply({}, method=Attention.repeat_kv, **args)
+    with pytest.raises(ValueError, match="no method"):
+        attn.apply({}, method="_attend")
+
+
+def test_mha_argument_checks_on_cpu():
+    """nn/attention.py:321-356 (``tests/test_attention.py:340-780`` cases): raised before any device work;
+    the options the kernel does not take raise NotImplementedError."""
+    from jaxml_b200.nn import Attention
+
+    attn = _attn1()
+    z = torch.zeros
+    base = {"query_states": z(1, 1, 1, 1), "key_states": z(1, 3, 1, 1), "value_states": z(1, 3, 1, 1)}
+    cases = [({"query_states": z(1, 1, 1)}, ValueError, "query_states must be a 4D array"),
+             ({"key_states": z(1, 3, 1)}, ValueError, "key_states must be a 4D array"),
+             ({"query_states": z(0, 1, 1, 1)}, ValueError, "batch axis must be non-empty"),
+             ({"query_states": z(1, 1, 1, 0)}, ValueError, "head_dim axis must be non-empty"),
+             ({"value_states": z(1, 0, 1, 1)}, ValueError, "sequence axis must be non-empty"),
+             ({"key_states": z(1, 3, 1, 1, dtype=torch.int32)}, TypeError, "key_states must contain floating"),
+             ({"value_states": z(1, 2, 1, 1)}, ValueError, "key_states and value_states"),
+             ({"query_states": z(2, 1, 1, 1)}, ValueError, "matching batch"),
+             ({"query_states": z(1, 1, 2, 1)}, ValueError, "matching batch"),
+             ({"causal": 1}, TypeError, "causal must be a boolean"),
+             ({"softmax_fp32": "yes"}, TypeError, "softmax_fp32 must be a boolean"),
+             ({"output_attentions": None}, TypeError, "output_attentions must be a boolean"),
+             ({"sliding_window": True}, TypeError, "sliding_window must be an integer when set"),
+             ({"sliding_window": 0}, ValueError, "sliding_window must be positive when set"),
+             ({"attention_mask": torch.ones(1, 2, dtype=torch.bool)}, ValueError, "attention batch and key length"),
+             ({"attention_mask": torch.ones(1, 3)}, TypeError, "attention_mask must be boolean or integer"),
+             ({"attention_mask": torch.tensor([[1, 2, 0]])}, ValueError, "integer values must be 0 or 1"),
+             ({"alibi_slope": z(1, 1)}, ValueError, "alibi_slope must be a 1D array"),
+             ({"alibi_slope": z(2)}, ValueError, "alibi_slope must contain 1 values"),
+             ({"alibi_slope": z(1, dtype=torch.int32)}, TypeError, "alibi_slope must contain floating"),
+             ({"alibi_slope": torch.tensor([float("inf")])}, ValueError, "alibi_slope must contain only finite"),
+             ({"alibi_slope": z(1)}, NotImplementedError, "ALiBi"),
+             ({"softmax_fp32": False}, NotImplementedError, "softmax_fp32"),
+             ({"attention_mask": torch.tensor([[False, True, True]])}, NotImplementedError, "right-padded")]
+    for kw, exc, match in cases:
+        args = dict(base)
+        args.update(kw)
+        with pytest.raises(exc, match=match):
+            attn.apply({}, method=Attention.mha, **args)
+    for field in ("query_states", "key_states", "value_states"):
+        args = {k: v.clone() for k, v in base.items()}
+        args[field][0, 0, 0, 0] = float("inf")
+        with pytest.raises(ValueError, match=f"{field} must contain only finite values"):
+            attn.apply({}, method=Attention.mha, **args)
+    with pytest.raises(RuntimeError, match="CUDA tensors only"):
+        attn.apply({}, method=Attention.mha, **base)
