@@ -18,6 +18,11 @@ from .decoders import (GemmaDecoder, GemmaMLP, GPTNeoXDecoder, GPTNeoXMLP, Llama
                        LlamaMLP)
 from .nn import GemmaRMSNorm  # noqa: F401  (models/gemma3.py:89-106 lives in jaxml.models)
 
+# models/__init__.py of the reference: the architecture entry points, in its order
+__all__ = ["GPTNeoXDecoder", "GPTNeoXMLP", "GPTNeoXModel", "GPTNeoXModelWithHead", "GemmaDecoder", "GemmaMLP",
+           "GemmaModel", "GemmaModelWithHead", "GemmaRMSNorm", "LlamaDecoder", "LlamaMLP", "LlamaModel",
+           "LlamaModelWithHead"]
+
 
 class _DecoderWithHead:
     family = ""

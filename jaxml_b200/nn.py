@@ -35,8 +35,10 @@ from ._checks import normalize_bool, normalize_count, normalize_dtype, normalize
 from .cache import KVCache
 from .config import ModelConfig
 
-__all__ = ["Module", "Block", "Embed", "DenseGeneral", "RMSNorm", "LayerNorm", "RotaryEmbedding", "Attention",
-           "AttentionWithRoPE", "AttentionOutput", "initializers"]
+# nn/__init__.py of the reference, in its order (AttentionOutput, GemmaRMSNorm and initializers are here
+# too, outside the star-import list as there)
+__all__ = ["Attention", "AttentionWithRoPE", "Block", "DenseGeneral", "Embed", "LayerNorm", "Module", "RMSNorm",
+           "RotaryEmbedding"]
 
 _REQ = object()
 
