@@ -19,6 +19,10 @@ from typing import Any, Optional, Sequence
 import numpy as np
 import torch
 
+from ._checks import normalize_dtype
+from .engine import Engine, InferenceConfig
+from .hf_utils import _normalize_hf_architecture, _normalize_hf_model_name, _validate_hf_dtype, load_model_from_hf
+
 
 def _count(name: str, value) -> int:
     if isinstance(value, (bool, np.bool_)):
@@ -177,12 +181,9 @@ class TextGenerationPipeline:
                 inference_config=None, use_tpu: bool = False, cache_stride: int = 256, tokenizer: Any = None,
                 tokenizer_kwargs: Optional[dict] = None, model_kwargs: Optional[dict] = None):
         """Pipeline over a supported HF checkpoint (local path or hub id): the model is converted to the
-        reference's parameter tree and packed for this GPU; the tokenizer defaults to AutoTokenizer."""
-        from ._checks import normalize_dtype
-        from .engine import Engine, InferenceConfig
-        from .hf_utils import _normalize_hf_architecture, _normalize_hf_model_name, _validate_hf_dtype
-        from .hf_utils import load_model_from_hf
-
+        reference's parameter tree in ``model_dtype`` and packed for this GPU; the tokenizer defaults to
+        AutoTokenizer.  The kernels compute in the model's dtype; ``engine_dtype`` is the engine's dtype
+        (the caches ``Engine.init_cache`` makes), as in the reference."""
         name = _normalize_hf_model_name(name)
         architecture = _normalize_hf_architecture(architecture)
         model_dtype = _validate_hf_dtype(model_dtype)
@@ -205,8 +206,6 @@ class TextGenerationPipeline:
             tokenizer = AutoTokenizer.from_pretrained(name, **tokenizer_kwargs)
         tokenizer = _check_tokenizer(tokenizer)
         model, params = load_model_from_hf(name, architecture=architecture, dtype=model_dtype, **model_kwargs)
-        if model.dtype != engine_dtype:
-            model = type(model)(model.config, dtype=engine_dtype)
         engine = Engine(model, inference_config, params, dtype=engine_dtype, cache_stride=cache_stride)
         engine.init_params(use_tpu=use_tpu)
         return cls(engine=engine, tokenizer=tokenizer)

@@ -151,3 +151,119 @@ def test_tokenizer_arrays_are_validated_before_generation(encoded, exc, match):
     with pytest.raises(exc, match=match):
         TextGenerationPipeline(eng, tok).generate_tokens("hello")
     assert tok.calls == 1 and eng.calls == []
+
+
+def _no_loading(monkeypatch):
+    """Tokenizer and model loaders that record and refuse any call."""
+    import transformers
+
+    import jaxml_b200.text_generation as T
+
+    calls = []
+
+    class _AutoTok:
+        @classmethod
+        def from_pretrained(cls, *a, **k):
+            calls.append("tokenizer")
+            raise AssertionError("the tokenizer must not be loaded")
+
+    def _load(*a, **k):
+        calls.append("model")
+        raise AssertionError("the model must not be loaded")
+
+    monkeypatch.setattr(transformers, "AutoTokenizer", _AutoTok)
+    monkeypatch.setattr(T, "load_model_from_hf", _load)
+    return calls
+
+
+def test_from_hf_wires_loader_engine_and_tokenizer(monkeypatch):
+    """text_generation.py:204-262 (the reference's ``tests/test_text_generation.py:577-620``): the loader,
+    the engine and the tokenizer get the arguments as given."""
+    import torch
+
+    import jaxml_b200.text_generation as T
+    from jaxml_b200 import InferenceConfig
+
+    calls = {}
+
+    class _FakeEngine:
+        def __init__(self, model, config, params, dtype, cache_stride):
+            calls["engine"] = (model, config, params, dtype, cache_stride)
+
+        def init_params(self, use_tpu):
+            calls["use_tpu"] = use_tpu
+
+        def generate(self, *a, **k):
+            raise AssertionError("from_hf does not generate")
+
+    def _load(name, architecture, dtype, **kw):
+        calls["load"] = (name, architecture, dtype, kw)
+        return "model", {"params": "params"}
+
+    monkeypatch.setattr(T, "Engine", _FakeEngine)
+    monkeypatch.setattr(T, "load_model_from_hf", _load)
+    tok = _Tok()
+    cfg = InferenceConfig()
+    pipe = TextGenerationPipeline.from_hf("some/model", architecture="llama", model_dtype="bfloat16",
+                                          engine_dtype="float32", inference_config=cfg, use_tpu=np.bool_(True),
+                                          cache_stride=128, tokenizer=tok, model_kwargs={"trust_remote_code": True})
+    assert pipe.tokenizer is tok
+    assert calls["load"] == ("some/model", "llama", "bfloat16", {"trust_remote_code": True})
+    assert calls["engine"] == ("model", cfg, {"params": "params"}, torch.float32, 128)
+    assert calls["use_tpu"] is True
+
+
+@pytest.mark.parametrize("name,exc,match", [("", ValueError, "non-empty"), ("   ", ValueError, "non-empty"),
+                                            (123, TypeError, "string or path-like")])
+def test_from_hf_rejects_invalid_names_before_loading(monkeypatch, name, exc, match):
+    calls = _no_loading(monkeypatch)
+    with pytest.raises(exc, match=match):
+        TextGenerationPipeline.from_hf(name)
+    assert calls == []
+
+
+@pytest.mark.parametrize("kwargs,exc,match", [
+    ({"architecture": None}, TypeError, "architecture must be a string"),
+    ({"architecture": "unknown"}, ValueError, "Unsupported Hugging Face architecture"),
+    ({"model_dtype": np.float32}, TypeError, "Expected dtype"),
+    ({"model_dtype": "bad"}, ValueError, "Unsupported dtype"),
+    ({"engine_dtype": None}, TypeError, "engine_dtype must be a valid"),
+    ({"engine_dtype": "not-a-dtype"}, TypeError, "engine_dtype must be a valid"),
+    ({"use_tpu": 1}, TypeError, "use_tpu must be a boolean"),
+    ({"inference_config": {"tp_size": 1}}, TypeError, "inference_config must be an InferenceConfig"),
+    ({"tokenizer_kwargs": [1]}, TypeError, "tokenizer_kwargs must be a mapping"),
+    ({"model_kwargs": "x"}, TypeError, "model_kwargs must be a mapping"),
+    ({"cache_stride": 0}, ValueError, "cache_stride must be positive"),
+    ({"cache_stride": True}, TypeError, "cache_stride must be an integer"),
+    ({"tokenizer": object()}, TypeError, "tokenizer must be callable"),
+])
+def test_from_hf_rejects_invalid_arguments_before_loading(monkeypatch, kwargs, exc, match):
+    calls = _no_loading(monkeypatch)
+    with pytest.raises(exc, match=match):
+        TextGenerationPipeline.from_hf("some/model", **kwargs)
+    assert calls == []
+
+
+def test_from_hf_pathlike_name(monkeypatch, tmp_path):
+    import jaxml_b200.text_generation as T
+
+    seen = {}
+
+    class _FakeEngine:
+        def __init__(self, *a, **k):
+            pass
+
+        def init_params(self, use_tpu):
+            pass
+
+        def generate(self, *a, **k):
+            raise AssertionError
+
+    def _load(name, architecture, dtype, **kw):
+        seen["name"] = name
+        return "model", {"params": {}}
+
+    monkeypatch.setattr(T, "Engine", _FakeEngine)
+    monkeypatch.setattr(T, "load_model_from_hf", _load)
+    TextGenerationPipeline.from_hf(tmp_path, tokenizer=_Tok())
+    assert seen["name"] == str(tmp_path)
