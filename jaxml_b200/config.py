@@ -7,6 +7,7 @@ from __future__ import annotations
 
 import dataclasses
 import math
+from collections.abc import Mapping
 from dataclasses import dataclass, fields
 from typing import Optional
 
@@ -140,27 +141,21 @@ class ModelConfig:
         num_layers = _hf_count("num_hidden_layers", config.num_hidden_layers)
         max_pos = _hf_count("max_position_embeddings", config.max_position_embeddings)
         vocab = _hf_count("vocab_size", config.vocab_size)
-        rope = _hf_rope_parameters(config, "full_attention" if kind == "gemma3" else None)
-        rope_theta = float(rope.get("rope_theta", getattr(config, "rope_theta", None)
-                                    or getattr(config, "rotary_emb_base", None) or 10000.0))
-        rope_scale = 1.0
-        if kind != "gpt_neox" and rope.get("rope_type") == "linear":
-            rope_scale = float(rope.get("factor", 1.0))
         attn_scale = head_dim ** -0.5
         kw = dict(use_parallel_residual=True, rotary_pct=1.0, use_bias=False, sliding_window=None,
                   sliding_window_pattern=None)
         if kind == "llama":
             norm_eps = config.rms_norm_eps
             num_kv = _hf_count("num_key_value_heads", config.num_key_value_heads)
+            rope_theta = _hf_rope_theta(config)
+            rope_scale = _hf_rope_scale(config)
         elif kind == "gpt_neox":
             norm_eps = config.layer_norm_eps
             num_kv = num_heads
-            rotary_pct = getattr(config, "rotary_pct", None)
-            if rotary_pct is None:
-                rotary_pct = rope.get("partial_rotary_factor", 1.0)
-            kw.update(use_parallel_residual=bool(config.use_parallel_residual), rotary_pct=float(rotary_pct),
+            rope_theta = _hf_rope_theta(config, fallback="rotary_emb_base")
+            rope_scale = 1.0     # GPT-NeoX configs carry no position scaling
+            kw.update(use_parallel_residual=config.use_parallel_residual, rotary_pct=_hf_rotary_pct(config),
                       use_bias=True)
-            rope_scale = 1.0
         else:
             qpas = normalize_float("query_pre_attn_scalar", config.query_pre_attn_scalar)
             if qpas <= 0:
@@ -168,11 +163,17 @@ class ModelConfig:
             attn_scale = qpas ** -0.5
             norm_eps = config.rms_norm_eps
             num_kv = _hf_count("num_key_value_heads", config.num_key_value_heads)
+            rope_theta = _hf_rope_theta(config, kind="full_attention")
+            rope_scale = _hf_rope_scale(config, kind="full_attention")
             kw.update(sliding_window=config.sliding_window, sliding_window_pattern=_gemma_pattern(config))
         pct = kw["rotary_pct"]
-        if (head_dim if pct >= 1.0 else int(head_dim * pct)) <= 0:
+        rd = head_dim if pct >= 1.0 else int(head_dim * pct)
+        if rd <= 0:
             raise ValueError(f"rotary_pct must produce a positive rotary dimension, got rotary_pct={pct} and "
                              f"head_dim={head_dim}.")
+        if rd % 2:
+            raise ValueError(f"rotary_pct must produce an even rotary dimension, got rotary_dim={rd}, "
+                             f"rotary_pct={pct}, and head_dim={head_dim}.")
         return cls(hidden_size=hidden, head_dim=head_dim, num_heads=num_heads,
                    num_layers=num_layers, max_position_embeddings=max_pos,
                    vocab_size=vocab, intermediate_ratio=(inter // factor, hidden // factor),
@@ -187,22 +188,66 @@ def _hf_count(name: str, value) -> int:
     return value
 
 
-def _hf_rope_parameters(config, kind):
-    params = getattr(config, "rope_parameters", None) or {}
-    if kind is not None and isinstance(params, dict) and kind in params:
-        params = params[kind]
-    if not params:
-        params = getattr(config, "rope_scaling", None) or {}
-        params = dict(params)
-        if getattr(config, "rope_theta", None) is not None:
-            params.setdefault("rope_theta", config.rope_theta)
-    return dict(params)
+def _hf_rope_parameters(config, kind=None):
+    """The config's ``rope_parameters`` (for Gemma3, the entry of one attention kind), or {}."""
+    rp = getattr(config, "rope_parameters", None)
+    if rp is None:
+        return {}
+    if not isinstance(rp, Mapping):
+        raise TypeError(f"rope_parameters must be a mapping when set, got {type(rp)}.")
+    if kind is None:
+        return rp
+    sub = rp.get(kind, {})
+    if not isinstance(sub, Mapping):
+        raise TypeError(f"rope_parameters[{kind!r}] must be a mapping when set, got {type(sub)}.")
+    return sub
+
+
+def _hf_rope_theta(config, fallback: str = "rope_theta", kind=None) -> float:
+    rp = _hf_rope_parameters(config, kind)
+    if "rope_theta" in rp:
+        return normalize_float("rope_theta", rp["rope_theta"])
+    if not hasattr(config, fallback):
+        raise ValueError(f"{config.__class__.__name__} must expose rope_theta.")
+    return normalize_float("rope_theta", getattr(config, fallback))
+
+
+def _hf_rope_scale(config, kind=None) -> float:
+    """The position divisor: the ``factor`` of ``rope_scaling`` (or of ``rope_parameters``), else 1."""
+    rs = getattr(config, "rope_scaling", None)
+    if rs is not None and not isinstance(rs, Mapping):
+        raise TypeError(f"rope_scaling must be a mapping when set, got {type(rs)}.")
+    if isinstance(rs, Mapping):
+        sub = rs
+        if kind is not None and kind in rs:
+            sub = rs[kind]
+            if not isinstance(sub, Mapping):
+                raise TypeError(f"rope_scaling[{kind!r}] must be a mapping when set, got {type(sub)}.")
+        if "factor" in sub:
+            return normalize_float("rope_scaling factor", sub["factor"])
+        if sub.get("rope_type") not in (None, "default"):
+            raise ValueError("rope_scaling must include a factor when set.")
+    rp = _hf_rope_parameters(config, kind)
+    if "factor" in rp:
+        return normalize_float("rope_parameters factor", rp["factor"])
+    return 1.0
+
+
+def _hf_rotary_pct(config) -> float:
+    v = getattr(config, "rotary_pct", None)
+    if v is not None:
+        return normalize_float("rotary_pct", v)
+    rp = _hf_rope_parameters(config)
+    if "partial_rotary_factor" in rp:
+        return normalize_float("rotary_pct", rp["partial_rotary_factor"])
+    return 1.0
 
 
 def _gemma_pattern(config):
-    pattern = getattr(config, "sliding_window_pattern", None)
-    if pattern is not None:
-        return pattern
+    """``sliding_window_pattern`` as the config states it; configs without the attribute give it through
+    ``layer_types`` (the first full-attention layer's index + 1)."""
+    if hasattr(config, "sliding_window_pattern"):
+        return config.sliding_window_pattern
     types = getattr(config, "layer_types", None)
     if types:
         for i, t in enumerate(types):
