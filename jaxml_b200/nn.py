@@ -716,7 +716,8 @@ class RotaryEmbedding(_Base):
         if base <= 0:
             raise ValueError(f"base must be positive, got {base}.")
         if scale < 1.0:
-            raise ValueError(f"rope_scale must be >= 1.0 (dividing positions by it), got {scale}.")
+            raise ValueError(f"a rope scale below 1.0 is most likely a mix-up of dividing and multiplying the "
+                             f"positions (they are divided by it), got {scale}.")
         if not 0 < pct <= 1:
             raise ValueError(f"rotary_pct must be in (0, 1], got {pct}.")
         rd = dim if pct >= 1.0 else int(dim * pct)
@@ -760,25 +761,31 @@ class RotaryEmbedding(_Base):
         _finite("x", x)
         return x
 
+    def _seq_len(self, x: torch.Tensor, seq_len, cached_rows: Optional[int]) -> int:
+        seq_len = normalize_count("seq_len", x.shape[1] if seq_len is None else seq_len)
+        if seq_len <= 0:
+            raise ValueError(f"seq_len must be positive, got {seq_len}.")
+        if cached_rows is not None and seq_len > cached_rows:
+            raise ValueError(f"Cached rotary embeddings only cover max_length={cached_rows}, got seq_len={seq_len}. "
+                             "Set disable_cache=True to compute longer embeddings dynamically.")
+        return seq_len
+
     def _check_inputs(self, variables, x=None, seq_len=None, **kwargs):
-        self._x(x)
+        x = self._x(x)
+        cached = None if normalize_bool("disable_cache", self.disable_cache) else self.max_length
+        self._seq_len(x, seq_len, cached)
 
     def _call(self, variables, x, seq_len=None):
         x = self._x(x)
-        seq_len = x.shape[1] if seq_len is None else seq_len
-        seq_len = normalize_count("seq_len", seq_len)
-        if seq_len <= 0:
-            raise ValueError(f"seq_len must be positive, got {seq_len}.")
         cache = variables.get("cache", {})
         if normalize_bool("disable_cache", self.disable_cache):
+            seq_len = self._seq_len(x, seq_len, None)
             emb = self.get_emb(seq_len, cache.get("inv_freq"))
             return torch.cos(emb).to(x.dtype).to(x.device), torch.sin(emb).to(x.dtype).to(x.device)
         if "cos_cached" not in cache:
             raise ValueError("RotaryEmbedding variables have no 'cache' collection: pass the variables init returned.")
         cos, sin = cache["cos_cached"], cache["sin_cached"]
-        if seq_len > cos.shape[0]:
-            raise ValueError(f"Cached rotary embeddings only cover max_length={cos.shape[0]}, got seq_len={seq_len}. "
-                             "Set disable_cache=True to compute longer embeddings dynamically.")
+        self._seq_len(x, seq_len, cos.shape[0])
         return cos.to(device=x.device, dtype=x.dtype), sin.to(device=x.device, dtype=x.dtype)
 
 
