@@ -118,7 +118,7 @@ def test_rotary_tables_match_the_oracle_restatement():
     (dict(dim=0), "dim must be positive"),
     (dict(dim=8, max_length=0), "max_length must be positive"),
     (dict(dim=8, base=0.0), "base must be positive"),
-    (dict(dim=8, rope_scale=0.5), "rope_scale"),
+    (dict(dim=8, rope_scale=0.5), "rope scale"),
     (dict(dim=8, rotary_pct=1.5), "rotary_pct"),
     (dict(dim=6, rotary_pct=0.5), "odd"),
     (dict(dim=2, rotary_pct=0.1), "less than or equal to 0"),
