@@ -468,6 +468,11 @@ class GemmaRMSNorm(_NormBase):
     _name = "GemmaRMSNorm"
     _kind = N.JX_NORM_GEMMA
 
+    def _setup(self):
+        super()._setup()
+        if not normalize_bool("upcast", self.upcast):
+            raise ValueError("GemmaRMSNorm requires upcast=True.")
+
     def _init_vars(self, gen, *args, **kwargs):
         return {"params": {"weight": torch.zeros(self.hidden_size, dtype=self.dtype, device=_device())}}
 

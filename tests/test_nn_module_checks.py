@@ -1,0 +1,88 @@
+"""Field and input checks of ``jaxml_b200.nn``'s norms, ``Embed`` and ``DenseGeneral`` at ``init`` (no
+device work), case by case as the reference's ``tests/test_modules.py:120-680`` states them."""
+import numpy as np
+import pytest
+import torch
+
+from jaxml_b200.nn import DenseGeneral, Embed, GemmaRMSNorm, LayerNorm, RMSNorm
+
+X = torch.ones(1, 2, 4)
+
+
+def test_gemma_rms_norm_requires_upcast():
+    with pytest.raises(ValueError, match="upcast=True"):
+        GemmaRMSNorm(hidden_size=4, upcast=False).init(0, X)
+
+
+@pytest.mark.parametrize("cls", [RMSNorm, LayerNorm, GemmaRMSNorm])
+def test_norm_input_checks(cls):
+    with pytest.raises(ValueError, match="hidden dimension mismatch"):
+        cls(hidden_size=4).init(0, torch.ones(1, 2, 3))
+    with pytest.raises(ValueError, match="at least one dimension"):
+        cls(hidden_size=4).init(0, torch.tensor(1.0))
+    for x in (torch.ones(0, 2, 4), torch.ones(1, 0, 4), torch.ones(1, 2, 0)):
+        with pytest.raises(ValueError, match="empty axes"):
+            cls(hidden_size=4).init(0, x)
+    with pytest.raises(TypeError, match="floating point"):
+        cls(hidden_size=4).init(0, torch.ones(1, 2, 4, dtype=torch.int32))
+    for v in (float("nan"), float("inf"), -float("inf")):
+        x = X.clone()
+        x[0, 0, 0] = v
+        with pytest.raises(ValueError, match="input must contain only finite values"):
+            cls(hidden_size=4).init(0, x)
+
+
+@pytest.mark.parametrize("cls", [RMSNorm, LayerNorm])
+@pytest.mark.parametrize("kwargs,exc,match", [
+    ({"hidden_size": True}, TypeError, "hidden_size must be an integer"),
+    ({"hidden_size": np.bool_(True)}, TypeError, "hidden_size must be an integer"),
+    ({"hidden_size": 1.5}, TypeError, "hidden_size must be an integer"),
+    ({"hidden_size": 0}, ValueError, "hidden_size must be positive"),
+    ({"eps": True}, TypeError, "eps must be a real number"),
+    ({"eps": "1e-6"}, TypeError, "eps must be a real number"),
+    ({"eps": float("nan")}, ValueError, "eps must be finite"),
+    ({"eps": 0.0}, ValueError, "eps must be positive"),
+    ({"upcast": 1}, TypeError, "upcast must be a boolean"),
+    ({"dtype": None}, TypeError, "dtype must be a valid"),
+    ({"dtype": "not-a-dtype"}, TypeError, "dtype must be a valid"),
+])
+def test_norm_field_checks(cls, kwargs, exc, match):
+    with pytest.raises(exc, match=match):
+        cls(**({"hidden_size": 4} | kwargs)).init(0, X)
+
+
+def test_norm_numpy_fields_and_layer_norm_bias_flag():
+    for cls in (RMSNorm, LayerNorm):
+        v = cls(hidden_size=np.int64(4), eps=np.float64(1e-6), upcast=np.bool_(True), dtype=np.float32).init(0, X)
+        assert v["params"]["weight"].dtype == torch.float32
+    with pytest.raises(TypeError, match="use_bias must be a boolean"):
+        LayerNorm(hidden_size=4, use_bias=1).init(0, X)
+    assert set(LayerNorm(hidden_size=4, use_bias=False).init(0, X)["params"]) == {"weight"}
+
+
+@pytest.mark.parametrize("kwargs,exc,match", [
+    ({"num_embeddings": True, "features": 4}, TypeError, "num_embeddings must be an integer"),
+    ({"num_embeddings": np.bool_(True), "features": 4}, TypeError, "num_embeddings must be an integer"),
+    ({"num_embeddings": 1.5, "features": 4}, TypeError, "num_embeddings must be an integer"),
+    ({"num_embeddings": 0, "features": 4}, ValueError, "num_embeddings must be positive"),
+    ({"num_embeddings": 8, "features": True}, TypeError, "features must be an integer"),
+    ({"num_embeddings": 8, "features": 1.5}, TypeError, "features must be an integer"),
+    ({"num_embeddings": 8, "features": 0}, ValueError, "features must be positive"),
+    ({"num_embeddings": 8, "features": 4, "one_hot": 1}, TypeError, "one_hot must be a boolean"),
+    ({"num_embeddings": 8, "features": 4, "dtype": None}, TypeError, "dtype must be a valid"),
+    ({"num_embeddings": 8, "features": 4, "dtype": "not-a-dtype"}, TypeError, "dtype must be a valid"),
+])
+def test_embed_field_checks(kwargs, exc, match):
+    with pytest.raises(exc, match=match):
+        Embed(**kwargs).init(0, torch.tensor([0, 1], dtype=torch.int32))
+
+
+def test_embed_inputs():
+    v = Embed(num_embeddings=np.int64(8), features=np.int64(4), one_hot=np.bool_(True)).init(0, [0, 1])
+    assert tuple(v["params"]["embedding"].shape) == (8, 4)
+    for x in (torch.zeros(0, dtype=torch.int32), torch.zeros(1, 0, dtype=torch.int32)):
+        with pytest.raises(ValueError, match="at least one token id"):
+            Embed(num_embeddings=8, features=4).init(0, x)
+    for x, match in ((torch.tensor([0, 8]), "less than num_embeddings=8"), (torch.tensor([-1, 0]), "non-negative")):
+        with pytest.raises(ValueError, match=match):
+            Embed(num_embeddings=8, features=4).init(0, x)
