@@ -23,6 +23,7 @@ multi-token call.  Anything else raises ``NotImplementedError`` naming the missi
 from __future__ import annotations
 
 import math
+import operator
 from collections import OrderedDict
 from dataclasses import dataclass
 from typing import Any, Callable, Optional
@@ -547,10 +548,19 @@ def _tuple(x):
     return tuple(x) if isinstance(x, (tuple, list)) else (x,)
 
 
+def _int_value(name: str, v) -> int:
+    if isinstance(v, (bool, np.bool_)):
+        raise TypeError(f"{name} values must be integers, got {type(v)}.")
+    try:
+        return operator.index(v)
+    except TypeError as e:
+        raise TypeError(f"{name} values must be integers, got {type(v)}.") from e
+
+
 def _shape_dims(name: str, values) -> tuple:
     out = []
     for v in values:
-        v = normalize_count(f"{name} values", v)
+        v = _int_value(name, v)
         if v <= 0:
             raise ValueError(f"{name} values must be positive, got {v}.")
         out.append(v)
@@ -560,9 +570,7 @@ def _shape_dims(name: str, values) -> tuple:
 def _norm_axes(axes, ndim: int) -> tuple:
     out = []
     for ax in axes:
-        if isinstance(ax, (bool, np.bool_)):
-            raise TypeError(f"axis values must be integers, got {type(ax)}.")
-        ax = normalize_count("axis", ax)
+        ax = _int_value("axis", ax)
         ax = ax if ax >= 0 else ndim + ax
         if ax < 0 or ax >= ndim:
             raise ValueError(f"axis {ax} is out of bounds for input rank {ndim}.")

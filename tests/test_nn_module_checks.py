@@ -86,3 +86,64 @@ def test_embed_inputs():
     for x, match in ((torch.tensor([0, 8]), "less than num_embeddings=8"), (torch.tensor([-1, 0]), "non-negative")):
         with pytest.raises(ValueError, match=match):
             Embed(num_embeddings=8, features=4).init(0, x)
+
+
+def _dense(**kw):
+    base = dict(features=4, axis=-1, kernel_axes=("embed", "features"))
+    base.update(kw)
+    return DenseGeneral(**base)
+
+
+X3 = torch.ones(1, 2, 3)
+
+
+@pytest.mark.parametrize("kw,exc,match", [
+    ({"axis": (-1, -1)}, ValueError, "unique"),
+    ({"axis": 3}, ValueError, "out of bounds"),
+    ({"axis": 1.5}, TypeError, "integers"),
+    ({"axis": True}, TypeError, "integers"),
+    ({"axis": np.bool_(True)}, TypeError, "integers"),
+    ({"with_logical_partitioning": 1}, TypeError, "with_logical_partitioning must be a boolean"),
+    ({"kernel_axes": ()}, ValueError, "Kernel axes must be specified"),
+    ({"kernel_axes": ("embed",)}, ValueError, "one axis name per kernel dimension"),
+    ({"kernel_axes": "embed"}, TypeError, "kernel_axes must be a tuple"),
+    ({"kernel_axes": ("embed", 1)}, TypeError, "kernel_axes entries"),
+    ({"features": True}, TypeError, "features values must be integers"),
+    ({"features": np.bool_(True)}, TypeError, "features values must be integers"),
+    ({"features": 1.5}, TypeError, "features values must be integers"),
+    ({"features": 0}, ValueError, "features values must be positive"),
+    ({"features": (4, True)}, TypeError, "features values must be integers"),
+    ({"features": (4, 0)}, ValueError, "features values must be positive"),
+    ({"dtype": None}, TypeError, "dtype must be a valid"),
+    ({"dtype": "not-a-dtype"}, TypeError, "dtype must be a valid"),
+    ({"weight_dtype": None}, TypeError, "weight_dtype must be a valid"),
+    ({"weight_dtype": "not-a-dtype"}, TypeError, "weight_dtype must be a valid"),
+    ({"use_bias": 1}, TypeError, "use_bias must be a boolean"),
+])
+def test_dense_general_field_checks(kw, exc, match):
+    with pytest.raises(exc, match=match):
+        _dense(**kw).init(0, X3)
+
+
+def test_dense_general_inputs_and_parameter_shapes():
+    with pytest.raises(TypeError, match="floating point"):
+        _dense().init(0, torch.ones(1, 2, 3, dtype=torch.int32))
+    for v in (float("nan"), float("inf")):
+        x = X3.clone()
+        x[0, 0, 0] = v
+        with pytest.raises(ValueError, match="DenseGeneral inputs must contain only finite values"):
+            _dense().init(0, x)
+    for x in (torch.ones(0, 2, 3), torch.ones(1, 0, 3), torch.ones(1, 2, 0)):
+        with pytest.raises(ValueError, match="empty axes"):
+            _dense().init(0, x)
+    assert tuple(_dense(axis=np.int64(-1)).init(0, X3)["params"]["kernel"].shape) == (3, 4)
+    p = _dense(features=(np.int64(4), np.int64(2)), kernel_axes=("embed", "a", "b")).init(0, X3)["params"]
+    assert tuple(p["kernel"].shape) == (3, 4, 2)
+    p = _dense(use_bias=np.bool_(True), dtype=np.float32, weight_dtype=np.float32).init(0, X3)["params"]
+    assert tuple(p["bias"].shape) == (4,) and p["kernel"].dtype == torch.float32
+    for axes in ("embed", ("embed",), (1,)):
+        p = _dense(kernel_axes=axes, use_bias=True, with_logical_partitioning=False).init(0, X3)["params"]
+        assert tuple(p["bias"].shape) == (4,)
+    p = _dense(features=(4, 2), kernel_axes=("embed", "a", "b"), use_bias=True,
+               with_logical_partitioning=np.bool_(True)).init(0, X3)["params"]
+    assert tuple(p["bias"].shape) == (4, 2)
