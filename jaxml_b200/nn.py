@@ -1051,18 +1051,24 @@ class Attention(Block):
         o = self._projections()["o_proj"]
         return o.apply({"params": _params(variables)["o_proj"]}, attn_output.reshape(attn_output.shape[:2] + (-1,)))
 
-    def _attend(self, variables, hidden, q, k, v, attention_mask, kv_cache, sliding_window, output_attentions,
-                use_flash):
+    @staticmethod
+    def _preflight(output_attentions, use_flash, kv_cache) -> bool:
+        """The call's flags and cache type, checked before any projection (nn/attention.py:139-144, 448-517)."""
         output_attentions = normalize_bool("output_attentions", output_attentions)
         if normalize_bool("use_flash", use_flash):
             raise NotImplementedError("JAX flash attention is not enabled in jaxml yet.")
+        if kv_cache is not None and not isinstance(kv_cache, KVCache):
+            raise TypeError(f"kv_cache must be a KVCache instance or None, got {type(kv_cache)}.")
+        return output_attentions
+
+    def _attend(self, variables, hidden, q, k, v, attention_mask, kv_cache, sliding_window, output_attentions,
+                use_flash):
+        output_attentions = self._preflight(output_attentions, use_flash, kv_cache)
         window = 0 if sliding_window is None else normalize_count("sliding_window", sliding_window)
         if window < 0:
             raise ValueError(f"sliding_window must be positive when set, got {window}.")
         B, S = hidden.shape[:2]
         if kv_cache is not None:
-            if not isinstance(kv_cache, KVCache):
-                raise TypeError(f"kv_cache must be a KVCache or None, got {type(kv_cache)}.")
             if kv_cache.k is not None and S > 1:
                 raise NotImplementedError("a multi-token call on a populated KV cache (chunked prefill) is not "
                                           "implemented by the CUDA attention kernels.")
@@ -1085,6 +1091,7 @@ class Attention(Block):
     def _call(self, variables, hidden_states, attention_mask=None, position_ids=None, kv_cache=None,
               output_attentions=False, use_flash=False, sliding_window=None, **kwargs):
         x = _check_hidden_states(hidden_states)
+        self._preflight(output_attentions, use_flash, kv_cache)
         if self.config.use_alibi:
             raise NotImplementedError("ALiBi attention is not implemented by the CUDA attention kernels.")
         if position_ids is not None:
@@ -1092,6 +1099,21 @@ class Attention(Block):
         q, k, v = self.qkv(variables, x)
         return self._attend(variables, x, q, k, v, attention_mask, kv_cache, sliding_window, output_attentions,
                             use_flash)
+
+
+def _cos_sin_pair(cos_sin):
+    """nn/attention.py:164-175: a (cos, sin) pair of arrays."""
+    if cos_sin is None:
+        raise ValueError("AttentionWithRoPE requires cos_sin.")
+    if isinstance(cos_sin, (torch.Tensor, np.ndarray)):
+        raise TypeError("cos_sin must be a pair of cosine and sine arrays, not a single array.")
+    try:
+        cos, sin = cos_sin
+    except TypeError as e:
+        raise TypeError(f"cos_sin must be a pair of cosine and sine arrays, got {type(cos_sin)}.") from e
+    except ValueError as e:
+        raise ValueError("cos_sin must contain exactly two arrays: cosine and sine.") from e
+    return cos, sin
 
 
 class AttentionWithRoPE(Attention):
@@ -1106,9 +1128,8 @@ class AttentionWithRoPE(Attention):
     def _call(self, variables, hidden_states, cos_sin=None, attention_mask=None, position_ids=None, kv_cache=None,
               output_attentions=False, use_flash=False, sliding_window=None):
         x = _check_hidden_states(hidden_states)
-        if cos_sin is None or len(cos_sin) != 2:
-            raise ValueError("cos_sin must be a (cos, sin) tuple.")
-        cos, sin = cos_sin
+        self._preflight(output_attentions, use_flash, kv_cache)
+        cos, sin = _cos_sin_pair(cos_sin)
         q, k, v = self.qkv(variables, x)
         if attention_mask is None and kv_cache is not None and kv_cache.mask is not None:
             attention_mask = kv_cache.next_mask

@@ -147,3 +147,82 @@ def test_dense_general_inputs_and_parameter_shapes():
     p = _dense(features=(4, 2), kernel_axes=("embed", "a", "b"), use_bias=True,
                with_logical_partitioning=np.bool_(True)).init(0, X3)["params"]
     assert tuple(p["bias"].shape) == (4, 2)
+
+
+def _attn_cfg(use_rope, **kw):
+    from jaxml_b200 import ModelConfig
+
+    base = dict(head_dim=2 if use_rope else 1, hidden_size=2 if use_rope else 1, num_heads=1, num_layers=1,
+                max_position_embeddings=8, vocab_size=8, attn_scale=1.0, use_rope=use_rope)
+    base.update(kw)
+    return ModelConfig(**base)
+
+
+def _cos_sin(n):
+    return torch.ones(n, 2), torch.zeros(n, 2)
+
+
+def test_attention_construction_checks():
+    from jaxml_b200.nn import Attention
+
+    cfg = _attn_cfg(False, head_dim=4, hidden_size=16, num_heads=4, num_kv_heads=2)
+    with pytest.raises(ValueError, match="fused_qkv"):
+        Attention(cfg, fused_qkv=True).init(0, torch.zeros(1, 2, 16))
+    for kw, match in (({"dtype": None}, "dtype must be a valid"), ({"dtype": "not-a-dtype"}, "dtype must be a valid"),
+                      ({"weight_dtype": None}, "weight_dtype must be a valid"),
+                      ({"with_logical_partitioning": 1}, "with_logical_partitioning must be a boolean")):
+        with pytest.raises(TypeError, match=match):
+            Attention(_attn_cfg(False), **kw).init(0, torch.zeros(1, 2, 1))
+    p = Attention(_attn_cfg(False), dtype=np.float32, weight_dtype=torch.bfloat16,
+                  with_logical_partitioning=np.bool_(False)).init(0, torch.zeros(1, 2, 1))["params"]
+    assert all(p[n]["kernel"].dtype == torch.bfloat16 for n in ("q_proj", "k_proj", "v_proj", "o_proj"))
+
+
+@pytest.mark.parametrize("use_rope", [False, True], ids=["Attention", "AttentionWithRoPE"])
+def test_attention_call_checks_before_projections(use_rope):
+    """Flags, the flash request, the cache type, hidden states and (with RoPE) the cos / sin pair are
+    checked before any projection (the reference's ``tests/test_attention.py:455-680`` cases)."""
+    from jaxml_b200.nn import Attention, AttentionWithRoPE
+
+    cfg = _attn_cfg(use_rope)
+    attn = (AttentionWithRoPE if use_rope else Attention)(cfg)
+    h = torch.zeros(1, 2, cfg.hidden_size)
+    kw = {"cos_sin": _cos_sin(8)} if use_rope else {}
+    v = attn.init(0, h, **kw)
+    for extra, match in (({"output_attentions": 1}, "output_attentions must be a boolean"),
+                         ({"use_flash": 1}, "use_flash must be a boolean")):
+        with pytest.raises(TypeError, match=match):
+            attn.apply(v, h, **kw, **extra)
+    with pytest.raises(NotImplementedError, match="flash attention is not enabled"):
+        attn.apply(v, h, use_flash=True, **({} if use_rope else {"kv_cache": object()}))
+    with pytest.raises(TypeError, match="kv_cache must be a KVCache"):
+        attn.apply(v, h, **kw, kv_cache=object())
+    for bad, exc, match in ((torch.zeros(1, 2), ValueError, "hidden_states must be a 3D array"),
+                            (torch.zeros(1, 2, 1, 1), ValueError, "hidden_states must be a 3D array"),
+                            (torch.zeros(0, 2, 1), ValueError, "empty axes"),
+                            (torch.zeros(1, 2, 1, dtype=torch.int32), TypeError, "hidden_states must contain floating")):
+        with pytest.raises(exc, match=match):
+            attn.apply(v, bad, **kw)
+    x = h.clone()
+    x[0, 0, 0] = float("nan")
+    with pytest.raises(ValueError, match="hidden_states must contain only finite values"):
+        attn.apply(v, x, **kw)
+
+
+def test_attention_with_rope_cos_sin_checks():
+    from jaxml_b200.nn import AttentionWithRoPE
+
+    cfg = _attn_cfg(True, attn_scale=2 ** -0.5)
+    attn = AttentionWithRoPE(cfg)
+    h = torch.zeros(1, 2, 2)
+    v = attn.init(0, h, cos_sin=_cos_sin(8))
+    with pytest.raises(ValueError, match="requires cos_sin"):
+        attn.apply(v, h)
+    for cs, exc, match in (((), ValueError, "exactly two arrays"),
+                           ((torch.ones(2, 2),), ValueError, "exactly two arrays"),
+                           ((torch.ones(2, 2), torch.zeros(2, 2), torch.ones(2, 2)), ValueError, "exactly two arrays"),
+                           (torch.ones(2, 2), TypeError, "not a single array"),
+                           (np.ones((2, 2), dtype=np.float32), TypeError, "not a single array"),
+                           (object(), TypeError, "cos_sin must be a pair")):
+        with pytest.raises(exc, match=match):
+            attn.apply(v, h, cos_sin=cs)
