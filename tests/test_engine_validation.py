@@ -184,3 +184,49 @@ def test_prepare_input_batch_divisible_by_dp_size(engine, monkeypatch):
     assert tuple(eng.prepare_input({"x": np.array([[1, 2], [3, 4]])})["x"].shape) == (2, 2)
     with pytest.raises(ValueError, match="divisible by dp_size=2"):
         eng.prepare_input({"x": np.array([[1, 2], [3, 4], [5, 6]])})
+
+
+def test_inference_config_checks():
+    """engine.py:59-82 (the reference's ``tests/test_generation.py:1206-1240`` cases)."""
+    for kw in ({"tp_size": 0}, {"tp_size": -1}, {"dp_size": 0}, {"dp_size": -1}):
+        with pytest.raises(ValueError, match=next(iter(kw))):
+            InferenceConfig(**kw)
+    for kw, match in (({"tp_size": True}, "tp_size must be an integer"), ({"tp_size": 1.5}, "tp_size must be an integer"),
+                      ({"dp_size": True}, "dp_size must be an integer"), ({"dp_size": 1.5}, "dp_size must be an integer")):
+        with pytest.raises(TypeError, match=match):
+            InferenceConfig(**kw)
+    c = InferenceConfig(tp_size=np.int64(1), dp_size=np.int64(1))
+    assert c.tp_size == 1 and c.dp_size == 1 and type(c.tp_size) is int
+
+
+def test_engine_dtype_and_config_arguments(engine):
+    for bad in (None, "not-a-dtype", object()):
+        with pytest.raises(TypeError, match="dtype must be a valid"):
+            Engine(engine.model, InferenceConfig(), engine.params, dtype=bad)
+    for dt, want in ((torch.float32, torch.float32), (np.float32, torch.float32), ("bfloat16", torch.bfloat16)):
+        assert Engine(engine.model, InferenceConfig(), engine.params, dtype=dt).dtype == want
+    for bad in (None, {"tp_size": 1}, object()):
+        with pytest.raises(TypeError, match="config must be an InferenceConfig"):
+            Engine(engine.model, bad, engine.params)
+
+
+def test_init_params_checks_explicit_weights_before_touching_the_model():
+    """engine.py:225-240: malformed weights are rejected before the model is asked for anything."""
+    from types import MappingProxyType
+
+    class _Untouchable:
+        def __getattr__(self, name):
+            raise AssertionError(f"the model was used ({name}) before the weights were checked")
+
+    eng = Engine(_Untouchable(), InferenceConfig(), {"params": {}})
+    for weights, exc, match in ((("params", {}), TypeError, "weights must be a mapping"),
+                                ({}, ValueError, "'params'"),
+                                ({"cache": {}}, ValueError, "'params'"),
+                                (MappingProxyType({"cache": {}}), ValueError, "'params'"),
+                                ({"params": []}, TypeError, r"weights\['params'\] must be a mapping"),
+                                (MappingProxyType({"params": []}), TypeError, r"weights\['params'\] must be a mapping")):
+        with pytest.raises(exc, match=match):
+            eng.init_params(weights=weights, use_tpu=False)
+    for kw, match in (({"use_tpu": 1}, "use_tpu must be a boolean"), ({"reinit_weight": 1}, "reinit_weight must be a boolean")):
+        with pytest.raises(TypeError, match=match):
+            eng.init_params(**kw)
