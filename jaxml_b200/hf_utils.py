@@ -166,11 +166,16 @@ def _head_dim(config) -> int:
     return hidden // heads
 
 
-def _model_states(model, what: str):
-    """(config, state dict) of an HF-like model, checked before any conversion."""
+def _model_config(model, what: str):
     config = getattr(model, "config", None)
     if config is None:
         raise ValueError(f"Expected the {what} model to expose a config.")
+    return config
+
+
+def _model_states(model, what: str):
+    """(config, state dict) of an HF-like model, checked before any conversion."""
+    config = _model_config(model, what)
     sd = getattr(model, "state_dict", None)
     if not callable(sd):
         raise TypeError(f"Expected the {what} model to provide a callable state_dict.")
@@ -269,32 +274,89 @@ def _check_model_type(config, expected: tuple, what: str):
         raise ValueError(f"Expected Hugging Face {what} model_type to be one of {expected}, got {mt!r}.")
 
 
-def load_model_from_hf(name, architecture: str = "auto", dtype: str = "float32", **from_pretrained_kwargs):
-    """(model class instance, reference parameter tree) from a supported HF causal LM.  The model class
-    computes in `dtype`; leaves are CPU torch tensors in that dtype."""
-    from .config import ModelConfig
-    from .models import GemmaModelWithHead, GPTNeoXModelWithHead, LlamaModelWithHead
+def _infer_hf_architecture(name: str, **config_kwargs) -> str:
+    """The architecture of a checkpoint from its config's ``model_type`` (hf_utils.py:139-157)."""
+    try:
+        from transformers import AutoConfig
+    except ImportError as e:
+        raise ImportError("Please install transformers library.") from e
+    mt = getattr(AutoConfig.from_pretrained(name, **config_kwargs), "model_type", None)
+    arch = {"llama": "llama", "gpt_neox": "neox", "gemma3": "gemma", "gemma3_text": "gemma"}.get(mt)
+    if arch is None:
+        raise ValueError(f"Unsupported Hugging Face model type {mt!r}.")
+    return arch
 
+
+def load_model_from_hf(name, architecture: str = "auto", dtype: str = "float32", **from_pretrained_kwargs):
+    """(model class instance, reference parameter tree) from a supported HF causal LM (hf_utils.py:160-181):
+    the name, dtype and architecture are checked before anything is loaded, ``auto`` reads the
+    checkpoint's config, and the per-architecture loader does the rest."""
     name = _normalize_hf_model_name(name)
     dtype = _validate_hf_dtype(dtype)
     arch = _normalize_hf_architecture(architecture)
+    if arch == "auto":
+        arch = _infer_hf_architecture(name, **from_pretrained_kwargs)
+    loader = {"llama": load_llama_from_hf, "neox": load_neox_from_hf, "gemma": load_gemma_from_hf}[arch]
+    return loader(name, dtype=dtype, **from_pretrained_kwargs)
+
+
+def _auto_model(name: str, **kw):
     try:
-        from transformers import AutoConfig, AutoModelForCausalLM
+        from transformers import AutoModelForCausalLM
     except ImportError as e:
         raise ImportError("Please install transformers library.") from e
-    if arch == "auto":
-        mt = getattr(AutoConfig.from_pretrained(name, **from_pretrained_kwargs), "model_type", None)
-        arch = {"llama": "llama", "gpt_neox": "neox", "gemma3": "gemma", "gemma3_text": "gemma"}.get(mt)
-        if arch is None:
-            raise ValueError(f"Unsupported Hugging Face model type {mt!r}.")
-    tdt = _HF_DTYPES[dtype.lower()]
-    hf = AutoModelForCausalLM.from_pretrained(name, **from_pretrained_kwargs)
-    if arch == "llama":
-        _check_model_type(hf.config, ("llama",), "Llama")
-        return LlamaModelWithHead(ModelConfig.from_hf(hf.config), dtype=tdt), to_llama_jax_params(hf, dtype=tdt)
-    if arch == "neox":
-        _check_model_type(hf.config, ("gpt_neox",), "GPT-NeoX")
-        return GPTNeoXModelWithHead(ModelConfig.from_hf(hf.config), dtype=tdt), to_neox_jax_params(hf, dtype=tdt)
-    lm = getattr(hf, "language_model", hf)
-    _check_model_type(lm.config, ("gemma3_text", "gemma3"), "Gemma")
-    return GemmaModelWithHead(ModelConfig.from_hf(lm.config), dtype=tdt), to_gemma_jax_params(lm, dtype=tdt)
+    return AutoModelForCausalLM.from_pretrained(name, **kw)
+
+
+def load_llama_from_hf(name, dtype: str = "float32", **from_pretrained_kwargs):
+    """A Llama checkpoint (local path or hub id) as ``(LlamaModelWithHead, params)`` with parameters in
+    ``dtype``; the model class keeps the default compute dtype, as in the reference (hf_utils.py:184-202)."""
+    from .config import ModelConfig
+    from .models import LlamaModelWithHead
+
+    name = _normalize_hf_model_name(name)
+    tdt = _HF_DTYPES[_validate_hf_dtype(dtype).lower()]
+    hf = _auto_model(name, **from_pretrained_kwargs)
+    cfg = _model_config(hf, "Llama")
+    _check_model_type(cfg, ("llama",), "Llama")
+    params = to_llama_jax_params(hf, dtype=tdt)
+    return LlamaModelWithHead(ModelConfig.from_hf(cfg)), params
+
+
+def load_neox_from_hf(name, dtype: str = "float32", **from_pretrained_kwargs):
+    """A GPT-NeoX checkpoint as ``(GPTNeoXModelWithHead, params)`` (hf_utils.py:205-223)."""
+    from .config import ModelConfig
+    from .models import GPTNeoXModelWithHead
+
+    name = _normalize_hf_model_name(name)
+    tdt = _HF_DTYPES[_validate_hf_dtype(dtype).lower()]
+    hf = _auto_model(name, **from_pretrained_kwargs)
+    cfg = _model_config(hf, "GPT-NeoX")
+    _check_model_type(cfg, ("gpt_neox",), "GPT-NeoX")
+    params = to_neox_jax_params(hf, dtype=tdt)
+    return GPTNeoXModelWithHead(ModelConfig.from_hf(cfg)), params
+
+
+def load_gemma_from_hf(name, dtype: str = "float32", **from_pretrained_kwargs):
+    """A Gemma3 checkpoint as ``(GemmaModelWithHead, params)`` (hf_utils.py:226-250): the multimodal
+    wrapper (``model_type`` gemma3) is checked, then its ``language_model`` (gemma3_text) is converted.
+    A text-only checkpoint, whose causal LM is the text model itself, is taken as it is."""
+    from .config import ModelConfig
+    from .models import GemmaModelWithHead
+
+    name = _normalize_hf_model_name(name)
+    tdt = _HF_DTYPES[_validate_hf_dtype(dtype).lower()]
+    hf = _auto_model(name, **from_pretrained_kwargs)
+    wrapper_cfg = _model_config(hf, "Gemma")
+    if getattr(wrapper_cfg, "model_type", None) == "gemma3_text":
+        lm = hf
+    else:
+        _check_model_type(wrapper_cfg, ("gemma3",), "Gemma")
+        try:
+            lm = hf.language_model
+        except AttributeError as e:
+            raise ValueError("Expected Hugging Face Gemma model to expose a language_model module.") from e
+    cfg = _model_config(lm, "Gemma text")
+    _check_model_type(cfg, ("gemma3_text",), "Gemma text")
+    params = to_gemma_jax_params(lm, dtype=tdt)
+    return GemmaModelWithHead(ModelConfig.from_hf(cfg)), params

@@ -103,3 +103,129 @@ def test_load_model_from_hf_architecture_argument():
         load_model_from_hf("some/model", architecture="mamba")
     with pytest.raises(TypeError, match="architecture must be a string"):
         load_model_from_hf("some/model", architecture=3)
+
+
+def _fake_auto_model(monkeypatch, make):
+    import transformers
+
+    class _Auto:
+        @classmethod
+        def from_pretrained(cls, *a, **k):
+            return make()
+
+    monkeypatch.setattr(transformers, "AutoModelForCausalLM", _Auto)
+
+
+def _refuse(monkeypatch, *names):
+    import jaxml_b200.hf_utils as H
+
+    calls = []
+
+    def _no(*a, **k):
+        calls.append(a)
+        raise AssertionError("must not be reached")
+
+    for n in names:
+        monkeypatch.setattr(H, n, _no)
+    return calls
+
+
+def test_direct_loaders_check_arguments_before_loading(monkeypatch):
+    """hf_utils.py:184-250 (the reference's ``tests/test_hf_utils.py:222-270`` cases)."""
+    from jaxml_b200.hf_utils import load_llama_from_hf
+
+    _fake_auto_model(monkeypatch, lambda: (_ for _ in ()).throw(AssertionError("loaded")))
+    with pytest.raises(TypeError, match="Expected dtype"):
+        load_llama_from_hf("some/model", dtype=np.float32)
+    for name, exc, match in (("", ValueError, "non-empty"), ("   ", ValueError, "non-empty"),
+                             (123, TypeError, "string or path-like")):
+        with pytest.raises(exc, match=match):
+            load_llama_from_hf(name)
+
+
+@pytest.mark.parametrize("loader,model_type,match", [("load_llama_from_hf", "gpt_neox", "Llama model_type"),
+                                                     ("load_neox_from_hf", "llama", "GPT-NeoX model_type")])
+def test_direct_loaders_check_the_model_type_before_converting(monkeypatch, loader, model_type, match):
+    import jaxml_b200.hf_utils as H
+
+    _fake_auto_model(monkeypatch, lambda: SimpleNamespace(config=SimpleNamespace(model_type=model_type),
+                                                          state_dict=lambda: {}))
+    calls = _refuse(monkeypatch, "to_llama_jax_params", "to_neox_jax_params")
+    with pytest.raises(ValueError, match=match):
+        getattr(H, loader)("some/model")
+    assert calls == []
+
+
+@pytest.mark.parametrize("loader,match", [("load_llama_from_hf", "Llama model to expose a config"),
+                                          ("load_neox_from_hf", "GPT-NeoX model to expose a config")])
+def test_direct_loaders_need_a_config(monkeypatch, loader, match):
+    import jaxml_b200.hf_utils as H
+
+    _fake_auto_model(monkeypatch, lambda: SimpleNamespace(state_dict=lambda: {}))
+    calls = _refuse(monkeypatch, "to_llama_jax_params", "to_neox_jax_params")
+    with pytest.raises(ValueError, match=match):
+        getattr(H, loader)("some/model")
+    assert calls == []
+
+
+def test_gemma_loader_checks(monkeypatch):
+    """The wrapper's model type and config, its language model, and the text model's type and config are
+    checked before any conversion (the reference's ``tests/test_hf_utils.py:329-422`` cases)."""
+    from jaxml_b200.hf_utils import load_gemma_from_hf
+
+    calls = _refuse(monkeypatch, "to_gemma_jax_params")
+    _fake_auto_model(monkeypatch, lambda: SimpleNamespace(config=SimpleNamespace(model_type="llama")))
+    with pytest.raises(ValueError, match="Gemma model_type"):
+        load_gemma_from_hf("some/model")
+    _fake_auto_model(monkeypatch, lambda: SimpleNamespace(config=SimpleNamespace(model_type="gemma3")))
+    with pytest.raises(ValueError, match="language_model"):
+        load_gemma_from_hf("some/model")
+
+    class _Exploding:
+        @property
+        def language_model(self):
+            raise AssertionError("language_model read before the wrapper config was checked")
+
+    _fake_auto_model(monkeypatch, _Exploding)
+    with pytest.raises(ValueError, match="Gemma model to expose a config"):
+        load_gemma_from_hf("some/model")
+    _fake_auto_model(monkeypatch, lambda: SimpleNamespace(
+        config=SimpleNamespace(model_type="gemma3"),
+        language_model=SimpleNamespace(config=SimpleNamespace(model_type="llama"), state_dict=lambda: {})))
+    with pytest.raises(ValueError, match="Gemma text model_type"):
+        load_gemma_from_hf("some/model")
+    _fake_auto_model(monkeypatch, lambda: SimpleNamespace(config=SimpleNamespace(model_type="gemma3"),
+                                                          language_model=SimpleNamespace(state_dict=lambda: {})))
+    with pytest.raises(ValueError, match="Gemma text model to expose a config"):
+        load_gemma_from_hf("some/model")
+    assert calls == []
+
+
+def test_load_model_from_hf_dispatch(monkeypatch):
+    """``auto`` reads the config's model type (gemma3_text included) and forwards the loader kwargs; a bad
+    dtype is refused before the config is read."""
+    import transformers
+
+    import jaxml_b200.hf_utils as H
+
+    seen = []
+
+    class _AutoConfig:
+        @classmethod
+        def from_pretrained(cls, *a, **k):
+            return SimpleNamespace(model_type="gemma3_text")
+
+    def _gemma(name, dtype, **kw):
+        seen.append((name, dtype, kw))
+        return "model", {"params": {}}
+
+    monkeypatch.setattr(transformers, "AutoConfig", _AutoConfig)
+    monkeypatch.setattr(H, "load_gemma_from_hf", _gemma)
+    assert H.load_model_from_hf("some/model", dtype="float32", local_files_only=True) == ("model", {"params": {}})
+    assert seen == [("some/model", "float32", {"local_files_only": True})]
+    calls = _refuse(monkeypatch, "_infer_hf_architecture")
+    for dtype, exc, match in ((np.float32, TypeError, "Expected dtype"), ("bad", ValueError, "Unsupported dtype"),
+                              (torch.int32, ValueError, "Unsupported dtype")):
+        with pytest.raises(exc, match=match):
+            H.load_model_from_hf("some/model", dtype=dtype)
+    assert calls == []
