@@ -267,3 +267,94 @@ def test_from_hf_pathlike_name(monkeypatch, tmp_path):
     monkeypatch.setattr(T, "load_model_from_hf", _load)
     TextGenerationPipeline.from_hf(tmp_path, tokenizer=_Tok())
     assert seen["name"] == str(tmp_path)
+
+
+class _Fixed:
+    """An engine returning a fixed token array."""
+
+    def __init__(self, out):
+        self.out = out
+
+    def generate(self, *a, **k):
+        return self.out
+
+
+def test_pipeline_construction_checks_and_default_copies():
+    """text_generation.py:194-230 (the reference's ``tests/test_text_generation.py:157-200`` cases)."""
+    for kw, match in (({"default_tokenize_kwargs": ["padding"]}, "default_tokenize_kwargs must be a mapping"),
+                      ({"default_decode_kwargs": ["x"]}, "default_decode_kwargs must be a mapping")):
+        with pytest.raises(TypeError, match=match):
+            TextGenerationPipeline(engine=_Engine(), tokenizer=_Tok(), **kw)
+
+    class _NoDecode:
+        def __call__(self, *a, **k):
+            return {}
+
+    for eng, tok, match in ((object(), _Tok(), "engine must provide a callable generate method"),
+                            (_Engine(), object(), "tokenizer must be callable"),
+                            (_Engine(), _NoDecode(), "batch_decode")):
+        with pytest.raises(TypeError, match=match):
+            TextGenerationPipeline(engine=eng, tokenizer=tok)
+    tk, dk = {"padding": True}, {"skip_special_tokens": True}
+    pipe = TextGenerationPipeline(engine=_Engine(), tokenizer=_Tok(), default_tokenize_kwargs=tk,
+                                  default_decode_kwargs=dk)
+    tk["padding"] = "longest"
+    dk["skip_special_tokens"] = False
+    assert pipe.default_tokenize_kwargs == {"padding": True}
+    assert pipe.default_decode_kwargs == {"skip_special_tokens": True}
+
+
+@pytest.mark.parametrize("ids,mask,exc,match", [
+    (np.ones(2, dtype=np.int32), None, ValueError, "input_ids must be a 2D array"),
+    (np.ones((1, 2), dtype=np.float32), None, TypeError, "integer token ids"),
+    (np.ones((0, 2), dtype=np.int32), None, ValueError, "at least one batch row"),
+    (np.ones((1, 0), dtype=np.int32), None, ValueError, "at least one token"),
+    (np.array([[1, -1]], dtype=np.int32), None, ValueError, "token ids must be non-negative"),
+    (np.ones((1, 2), dtype=np.int32), np.ones(2, dtype=np.int32), ValueError, "attention_mask must be a 2D array"),
+    (np.ones((1, 2), dtype=np.int32), np.ones((1, 2), dtype=np.float32), TypeError, "boolean or integer"),
+    (np.ones((1, 2), dtype=np.int32), np.ones((1, 3), dtype=np.int32), ValueError, "attention_mask shape must match"),
+    (np.ones((1, 2), dtype=np.int32), np.array([[1, 2]]), ValueError, "integer values must be 0 or 1"),
+    (np.ones((1, 2), dtype=np.int32), np.zeros((1, 2), dtype=bool), ValueError, "at least one valid token"),
+])
+def test_token_arrays_checked_before_the_engine(ids, mask, exc, match):
+    eng = _Engine()
+    with pytest.raises(exc, match=match):
+        TextGenerationPipeline(eng, _Tok())._generate_tokens_from_arrays(ids, mask)
+    assert eng.calls == []
+
+
+def test_integer_mask_reaches_the_engine_as_booleans():
+    eng = _Engine()
+    TextGenerationPipeline(eng, _Tok())._generate_tokens_from_arrays(np.ones((1, 2), dtype=np.int32),
+                                                                     np.array([[1, 0]], dtype=np.int32),
+                                                                     max_new_tokens=1)
+    mask = eng.calls[0][1]
+    assert np.asarray(mask).dtype == np.bool_ and np.asarray(mask).tolist() == [[True, False]]
+
+
+def test_engine_output_checked_before_decoding():
+    ids = "ab"
+    for out, exc, match in ((np.ones(3, dtype=np.int32), ValueError, "2D token array"),
+                            (np.ones((1, 2), dtype=np.float32), TypeError, "integer token ids"),
+                            (np.array([[-1]], dtype=np.int32), ValueError, "token ids must be non-negative"),
+                            (np.ones((2, 3), dtype=np.int32), ValueError, "token batch size must match input batch size")):
+        with pytest.raises(exc, match=match):
+            TextGenerationPipeline(_Fixed(out), _Tok()).generate_text(ids, max_new_tokens=1, include_prompt=False)
+    for include, out, expected in ((False, np.ones((1, 0), dtype=np.int32), 1),
+                                   (False, np.ones((1, 2), dtype=np.int32), 1),
+                                   (True, np.ones((1, 1), dtype=np.int32), 3),
+                                   (True, np.ones((1, 4), dtype=np.int32), 3)):
+        with pytest.raises(ValueError, match=f"got {out.shape[1]} and expected {expected}"):
+            TextGenerationPipeline(_Fixed(out), _Tok()).generate_text(ids, max_new_tokens=1, include_prompt=include)
+
+
+@pytest.mark.parametrize("decoded,exc,match", [("decoded", TypeError, "sequence of strings"),
+                                               (["first", "second"], ValueError, "output batch size must match"),
+                                               ([1], TypeError, "sequence of strings")])
+def test_decoded_output_checks(decoded, exc, match):
+    class _Tok2(_Tok):
+        def batch_decode(self, tokens, **kw):
+            return decoded
+
+    with pytest.raises(exc, match=match):
+        TextGenerationPipeline(_Engine(), _Tok2()).generate_text("ab", max_new_tokens=1)
