@@ -26,7 +26,7 @@ import math
 import operator
 from collections import OrderedDict
 from dataclasses import dataclass
-from typing import Any, Callable, Optional
+from typing import Optional
 
 import numpy as np
 import torch

@@ -15,7 +15,6 @@ and positions are shared by all layers.
 """
 from __future__ import annotations
 
-import math
 from dataclasses import dataclass, field
 from typing import Optional
 

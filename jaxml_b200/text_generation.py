@@ -14,7 +14,7 @@ import operator
 from collections.abc import Mapping
 from collections.abc import Sequence as SequenceABC
 from dataclasses import dataclass, field
-from typing import Any, Optional, Sequence
+from typing import Any, Optional
 
 import numpy as np
 import torch
