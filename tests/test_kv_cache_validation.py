@@ -193,3 +193,38 @@ def test_validate_state_rejects_invalid_populated_state(cache, exc, match):
     k = torch.zeros(cache.k.shape[0], 1, 1, 2) if cache.k.ndim == 4 else torch.zeros(1, 1, 1, 2)
     with pytest.raises((TypeError, ValueError)):
         cache.update(k, k.clone())
+
+
+def test_static_fields_and_initial_state():
+    """The reference's ``tests/test_cache.py:16-140`` cases: static fields checked by ``validate_state``
+    and before any update, a complete initial state padded and positioned, partial ones refused."""
+    for cache, exc, match in ((KVCache(k=None, v=None, max_seq_len=0, mask=None), ValueError,
+                               "max_seq_len must be positive"),
+                              (KVCache(k=None, v=None, max_seq_len=True, mask=None), TypeError,
+                               "max_seq_len must be an integer"),
+                              (KVCache(k=None, v=None, max_seq_len=4, mask=None, dtype=None), TypeError,
+                               "dtype must be a valid"),
+                              (KVCache(k=None, v=None, max_seq_len=4, mask=None, dtype="not-a-dtype"), TypeError,
+                               "dtype must be a valid")):
+        with pytest.raises(exc, match=match):
+            cache.validate_state()
+        k, v = _kv(batch=1)
+        with pytest.raises(exc, match=match):
+            cache.update(k, v, mask=None)
+    k, v = _kv(seq_len=2)
+    c = KVCache.init(4, k=k, v=v, mask=torch.tensor([[1, 1], [1, 0]], dtype=torch.int32))
+    assert tuple(c.k.shape) == (2, 4, 1, 2) and c.mask.dtype == torch.bool
+    assert c.mask.tolist() == [[True, True, False, False], [True, False, False, False]]
+    assert c.pos_id.tolist() == [[1], [0]]
+    c = KVCache.init(4, k=k, v=v, mask=None, dtype=torch.bfloat16)
+    assert c.k.dtype == torch.bfloat16 and c.v.dtype == torch.bfloat16 and c.dtype == torch.bfloat16
+    c = KVCache.init(4).update(k, v, mask=None)
+    assert c.mask.tolist() == [[True, True, False, False]] * 2 and c.pos_id.tolist() == [[1], [1]]
+    one_k, one_v = _kv(seq_len=1)
+    for kw in ({"k": one_k}, {"v": one_v}, {"mask": torch.ones(2, 1, dtype=torch.bool)},
+               {"k": one_k, "mask": torch.ones(2, 1, dtype=torch.bool)}):
+        with pytest.raises(ValueError, match="requires both k and v"):
+            KVCache.init(4, **kw)
+    partial = KVCache(k=None, v=None, max_seq_len=4, mask=None, pos_id=torch.zeros(1, 1, dtype=torch.int32))
+    with pytest.raises(ValueError, match="k is empty"):
+        partial.update(*_kv(batch=1), mask=None)
