@@ -61,9 +61,13 @@ class _DecoderWithHead:
     def num_heads(self) -> int:
         return self.config.num_heads
 
-    def init(self, seed: int = 0, *_, std: float = 0.02) -> dict:
-        """Random N(0, std) kernels, unit norm weights, in the reference's parameter layout."""
-        return random_params(self.family, self.config, seed=seed, std=std)
+    def init(self, key=0, input_ids=None, *_, std: float = 0.02, **__) -> dict:
+        """Random N(0, std) kernels, unit norm weights, in the reference's parameter layout.  ``key`` is an
+        int seed or a PRNG key (two uint32 words); example ``input_ids``, when given, are checked as
+        ``apply`` checks them (the reference's ``init`` runs the model on them)."""
+        if input_ids is not None:
+            _prepare_model_inputs(self.config, input_ids, None)
+        return random_params(self.family, self.config, seed=_seed_of(key), std=std)
 
     def apply(self, params, input_ids, attention_mask=None, position_ids=None, kv_caches=None, use_cache=False,
               output_attentions=False, output_hidden_states=False, keep_last_n_logits: int = 0):
@@ -178,6 +182,22 @@ class _DecoderWithHead:
 
     def __repr__(self) -> str:
         return f"{type(self).__name__}(config={self.config!r}, dtype={self.dtype})"
+
+
+def _seed_of(key) -> int:
+    """An int seed, or the seed a PRNG key stands for: ``PRNGKey(s)`` is the words ``(s >> 32, s & mask)``,
+    so the key's words read back as ``(hi << 32) | lo`` (``init(PRNGKey(7))`` draws as ``init(7)``)."""
+    import numpy as np
+
+    if key is None:
+        return 0
+    if isinstance(key, (int, np.integer)) and not isinstance(key, (bool, np.bool_)):
+        return int(key) & ((1 << 63) - 1)
+    words = np.asarray(key.cpu() if isinstance(key, torch.Tensor) else key).reshape(-1).astype(np.int64)
+    seed = 0
+    for w in words.tolist():
+        seed = (seed << 32) | (int(w) & 0xFFFFFFFF)
+    return seed & ((1 << 63) - 1)
 
 
 def _right_padded(mask: torch.Tensor) -> bool:
@@ -322,8 +342,11 @@ class _DecoderStack(_DecoderWithHead):
     def _body_key(self) -> str:
         return "gpt_neox" if self.family == "neox" else "model"
 
-    def init(self, seed: int = 0, *_, std: float = 0.02) -> dict:
-        return {"params": random_params(self.family, self.config, seed=seed, std=std)["params"][self._body_key]}
+    def init(self, key=0, input_ids=None, *_, std: float = 0.02, **__) -> dict:
+        if input_ids is not None:
+            _prepare_model_inputs(self.config, input_ids, None)
+        return {"params": random_params(self.family, self.config, seed=_seed_of(key),
+                                        std=std)["params"][self._body_key]}
 
     def _full_tree(self, params):
         if not isinstance(params, dict) or "params" not in params:

@@ -103,8 +103,11 @@ def _generator(key) -> torch.Generator:
     elif isinstance(key, (int, np.integer)) and not isinstance(key, (bool, np.bool_)):
         seed = int(key)
     else:
-        k = torch.as_tensor(key).reshape(-1).to("cpu", torch.int64) & 0xFFFFFFFF
-        seed = int(sum(int(v) << (32 * i) for i, v in enumerate(k.tolist())))
+        # PRNGKey(s) holds the words (s >> 32, s & 0xFFFFFFFF): read them back as that seed, so that
+        # keys made from different small seeds draw differently
+        seed = 0
+        for v in (torch.as_tensor(key).reshape(-1).to("cpu", torch.int64) & 0xFFFFFFFF).tolist():
+            seed = (seed << 32) | int(v)
     g.manual_seed(seed & ((1 << 63) - 1))
     return g
 

@@ -175,3 +175,18 @@ def test_stack_model_init_and_input_checks(fam):
         model.apply(params, torch.ones(1, 4, dtype=torch.int32), output_attentions=1)
     with pytest.raises(ValueError, match="one cache per layer"):
         model.apply(params, torch.ones(1, 4, dtype=torch.int32), kv_caches=(None, None))
+
+
+def test_model_init_takes_a_seed_or_a_key_and_checks_example_ids():
+    model, _ = MODELS[0]
+    a = model.init(0)
+    b = model.init(np.array([0, 0], dtype=np.uint32))
+    c = model.init(np.array([0, 7], dtype=np.uint32), torch.ones(1, 4, dtype=torch.int32))
+    d = model.init(7)
+    k = "model"
+    emb = [t["params"][k]["embed_tokens"]["embedding"] for t in (a, b, c, d)]
+    assert torch.equal(emb[0], emb[1]) and torch.equal(emb[2], emb[3]) and not torch.equal(emb[0], emb[2])
+    with pytest.raises(ValueError, match="input_ids must be a 2D array"):
+        model.init(0, torch.arange(4, dtype=torch.int32))
+    with pytest.raises(ValueError, match="less than vocab_size"):
+        model.init(0, torch.tensor([[0, 50]], dtype=torch.int32))

@@ -267,3 +267,10 @@ def test_mha_argument_checks_on_cpu():
             attn.apply({}, method=Attention.mha, **args)
     with pytest.raises(RuntimeError, match="CUDA tensors only"):
         attn.apply({}, method=Attention.mha, **base)
+
+
+def test_init_keys_made_from_different_seeds_draw_differently():
+    e = nn.Embed(num_embeddings=8, features=4)
+    t = [e.init(k, [0])["params"]["embedding"] for k in (np.array([0, 1], dtype=np.uint32),
+                                                        np.array([0, 2], dtype=np.uint32), 1)]
+    assert not torch.equal(t[0], t[1]) and torch.equal(t[0], t[2])
