@@ -67,7 +67,30 @@ class _DecoderWithHead:
         ``apply`` checks them (the reference's ``init`` runs the model on them)."""
         if input_ids is not None:
             _prepare_model_inputs(self.config, input_ids, None)
-        return random_params(self.family, self.config, seed=_seed_of(key), std=std)
+        tree = random_params(self.family, self.config, seed=_seed_of(key), std=std)
+        tree["cache"] = {self._body_key: self._rope_cache()}
+        return tree
+
+    @property
+    def _body_key(self) -> str:
+        return "gpt_neox" if self.family == "neox" else "model"
+
+    def _rope_cache(self) -> dict:
+        """The rotary tables in the model dtype, as the stack's ``cache`` collection holds them
+        (``rotary_emb``, and ``rotary_emb_local`` for Gemma3).  ``apply`` does not read them: the kernels
+        take their own copy of the same tables."""
+        from .nn import RotaryEmbedding
+
+        cfg = self.config
+        specs = {"rotary_emb": (cfg.rope_theta, cfg.rope_scale)}
+        if self.family == "gemma3":
+            specs["rotary_emb_local"] = (10000.0, 1.0)
+        out = {}
+        for name, (base, scale) in specs.items():
+            rope = RotaryEmbedding(dim=cfg.head_dim, max_length=cfg.max_position_embeddings, base=base,
+                                   dtype=self.dtype, rotary_pct=cfg.rotary_pct, rope_scale=scale)
+            out[name] = rope.init(0, torch.zeros(1, 1, 1))["cache"]
+        return out
 
     def apply(self, params, input_ids, attention_mask=None, position_ids=None, kv_caches=None, use_cache=False,
               output_attentions=False, output_hidden_states=False, keep_last_n_logits: int = 0):
@@ -338,15 +361,12 @@ class _DecoderStack(_DecoderWithHead):
 
     _has_head = False
 
-    @property
-    def _body_key(self) -> str:
-        return "gpt_neox" if self.family == "neox" else "model"
-
     def init(self, key=0, input_ids=None, *_, std: float = 0.02, **__) -> dict:
         if input_ids is not None:
             _prepare_model_inputs(self.config, input_ids, None)
         return {"params": random_params(self.family, self.config, seed=_seed_of(key),
-                                        std=std)["params"][self._body_key]}
+                                        std=std)["params"][self._body_key],
+                "cache": self._rope_cache()}
 
     def _full_tree(self, params):
         if not isinstance(params, dict) or "params" not in params:

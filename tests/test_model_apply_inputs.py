@@ -190,3 +190,24 @@ def test_model_init_takes_a_seed_or_a_key_and_checks_example_ids():
         model.init(0, torch.arange(4, dtype=torch.int32))
     with pytest.raises(ValueError, match="less than vocab_size"):
         model.init(0, torch.tensor([[0, 50]], dtype=torch.int32))
+
+
+@pytest.mark.parametrize("fam", ["llama", "neox", "gemma3"])
+def test_init_holds_the_rotary_tables_in_the_model_dtype(fam):
+    """The reference's ``tests/test_model_inputs.py:294-320`` case: the ``cache`` collection of ``init``
+    holds the rotary tables (and Gemma's local ones) in the model dtype."""
+    from jaxml_b200.models import GemmaModel, GPTNeoXModel, LlamaModel
+
+    cfg = ModelConfig(head_dim=8, hidden_size=32, num_heads=4, num_kv_heads=4, num_layers=2,
+                      max_position_embeddings=64, vocab_size=50, **({"sliding_window": 4, "sliding_window_pattern": 2}
+                                                                     if fam == "gemma3" else {}))
+    cls = {"llama": LlamaModel, "neox": GPTNeoXModel, "gemma3": GemmaModel}[fam]
+    v = cls(cfg, dtype=torch.bfloat16).init(0, torch.tensor([[0, 1]], dtype=torch.int32))
+    names = ["rotary_emb"] + (["rotary_emb_local"] if fam == "gemma3" else [])
+    assert sorted(v["cache"]) == names
+    for n in names:
+        assert v["cache"][n]["cos_cached"].dtype == torch.bfloat16 and v["cache"][n]["sin_cached"].dtype == torch.bfloat16
+        assert tuple(v["cache"][n]["cos_cached"].shape) == (64, 8)
+    head = {"llama": LlamaModelWithHead, "neox": GPTNeoXModelWithHead, "gemma3": GemmaModelWithHead}[fam]
+    w = head(cfg).init(0)
+    assert set(w) == {"params", "cache"} and set(w["cache"]) == {"gpt_neox" if fam == "neox" else "model"}
