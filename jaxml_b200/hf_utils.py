@@ -187,12 +187,12 @@ def _model_states(model, what: str):
     return config, states
 
 
-def to_llama_jax_params(model, dtype=torch.float32) -> dict:
+def to_llama_jax_params(model, dtype="float16") -> dict:
     config, states = _model_states(model, "Llama")
     return torch_to_jax_states(states, dtype=dtype, head_dim=_head_dim(config))
 
 
-def to_gemma_jax_params(model, dtype=torch.float32) -> dict:
+def to_gemma_jax_params(model, dtype="bfloat16") -> dict:
     config, states = _model_states(model, "Gemma")
     return torch_to_jax_states(states, dtype=dtype, head_dim=_head_dim(config))
 
@@ -209,7 +209,7 @@ _NEOX_SUB = (
 )
 
 
-def to_neox_jax_params(model, dtype=torch.float32) -> dict:
+def to_neox_jax_params(model, dtype="float16") -> dict:
     config, states = _model_states(model, "GPT-NeoX")
     renamed, origin = {}, {}
     for key, value in states.items():

@@ -229,3 +229,12 @@ def test_load_model_from_hf_dispatch(monkeypatch):
         with pytest.raises(exc, match=match):
             H.load_model_from_hf("some/model", dtype=dtype)
     assert calls == []
+
+
+def test_converter_default_dtypes_follow_the_reference():
+    """hf_utils.py:57-70: float16 for Llama and GPT-NeoX, bfloat16 for Gemma, unless asked otherwise."""
+    cfg = SimpleNamespace(hidden_size=8, num_attention_heads=2, head_dim=None)
+    assert to_llama_jax_params(_Fake(cfg))["params"]["q_proj"]["kernel"].dtype == torch.float16
+    assert to_neox_jax_params(_Fake(cfg))["params"]["q_proj"]["kernel"].dtype == torch.float16
+    assert to_gemma_jax_params(_Fake(cfg))["params"]["q_proj"]["kernel"].dtype == torch.bfloat16
+    assert to_llama_jax_params(_Fake(cfg), dtype=torch.float32)["params"]["q_proj"]["kernel"].dtype == torch.float32
