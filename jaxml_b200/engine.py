@@ -319,8 +319,11 @@ class Engine:
             t = torch.as_tensor(np.asarray(x))
         return t
 
-    def _prepare_generation_inputs(self, prompt_tokens, attention_mask):
-        prompt = self._as_int_tensor(prompt_tokens, "prompt_tokens")
+    @staticmethod
+    def _prepare_generation_inputs(prompt_tokens, attention_mask):
+        """engine.py:379-417: 1D inputs become one row; the prompt and mask checks of ``generate``; integer
+        masks become boolean.  Masks must also be right-padded (the kernels attend to key prefixes)."""
+        prompt = Engine._as_int_tensor(prompt_tokens, "prompt_tokens")
         if prompt.ndim == 1:
             prompt = prompt[None]
         elif prompt.ndim != 2:
@@ -333,7 +336,7 @@ class Engine:
             raise ValueError("prompt_tokens must contain at least one token.")
         if attention_mask is None:
             return prompt, None
-        mask = self._as_int_tensor(attention_mask, "attention_mask")
+        mask = Engine._as_int_tensor(attention_mask, "attention_mask")
         if mask.ndim == 1:
             mask = mask[None]
         elif mask.ndim != 2:

@@ -230,3 +230,13 @@ def test_init_params_checks_explicit_weights_before_touching_the_model():
     for kw, match in (({"use_tpu": 1}, "use_tpu must be a boolean"), ({"reinit_weight": 1}, "reinit_weight must be a boolean")):
         with pytest.raises(TypeError, match=match):
             eng.init_params(**kw)
+
+
+def test_prepare_generation_inputs_is_static_and_canonicalises():
+    ids, mask = Engine._prepare_generation_inputs(np.arange(4, dtype=np.int32), np.array([1, 1, 0, 0], dtype=np.int32))
+    assert tuple(ids.shape) == (1, 4) and mask.dtype == torch.bool and mask.tolist() == [[True, True, False, False]]
+    for bad in ([[1, 2, 0, 0]], [[1, -1, 0, 0]]):
+        with pytest.raises(ValueError, match="integer values must be 0 or 1"):
+            Engine._prepare_generation_inputs(np.ones((1, 4), dtype=np.int32), np.array(bad, dtype=np.int32))
+    ids, mask = Engine._prepare_generation_inputs(torch.ones(2, 3, dtype=torch.int64), None)
+    assert mask is None and tuple(ids.shape) == (2, 3)
