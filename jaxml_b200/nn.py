@@ -1050,6 +1050,16 @@ class Attention(Block):
         _check_status(q.device, "Attention.mha")
         return out.reshape(B, S, q.shape[2], q.shape[3]), w
 
+    def apply_kv_cache(self, variables, key_states, value_states, attention_mask, kv_cache):
+        """nn/attention.py:280-292: ``(keys, values, mask, cache)`` after writing this call's key / value
+        states into ``kv_cache`` (or the states themselves and None without a cache)."""
+        if kv_cache is not None and not isinstance(kv_cache, KVCache):
+            raise TypeError(f"kv_cache must be a KVCache instance or None, got {type(kv_cache)}.")
+        if kv_cache is None:
+            return key_states, value_states, attention_mask, None
+        kv_cache = kv_cache.update(key_states, value_states, attention_mask)
+        return kv_cache.k, kv_cache.v, kv_cache.mask, kv_cache
+
     def post_mha(self, variables, attn_output: torch.Tensor) -> torch.Tensor:
         o = self._projections()["o_proj"]
         return o.apply({"params": _params(variables)["o_proj"]}, attn_output.reshape(attn_output.shape[:2] + (-1,)))

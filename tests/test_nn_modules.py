@@ -6,6 +6,7 @@ import pytest
 import torch
 
 from jaxml_b200 import nn
+from jaxml_b200.cache import KVCache
 from jaxml_b200.config import ModelConfig
 from oracle import jaxml_oracle as O
 
@@ -274,3 +275,19 @@ def test_init_keys_made_from_different_seeds_draw_differently():
     t = [e.init(k, [0])["params"]["embedding"] for k in (np.array([0, 1], dtype=np.uint32),
                                                         np.array([0, 2], dtype=np.uint32), 1)]
     assert not torch.equal(t[0], t[1]) and torch.equal(t[0], t[2])
+
+
+def test_apply_kv_cache_method():
+    from jaxml_b200 import ModelConfig
+
+    cfg = ModelConfig(head_dim=2, hidden_size=4, num_heads=2, num_kv_heads=1, num_layers=1,
+                      max_position_embeddings=8, vocab_size=8, use_rope=False)
+    attn = nn.Attention(cfg)
+    k = torch.ones(1, 3, 1, 2)
+    keys, values, mask, cache = attn.apply({}, k, k + 1, None, KVCache.init(6), method=nn.Attention.apply_kv_cache)
+    assert tuple(keys.shape) == (1, 6, 1, 2) and mask.tolist() == [[True] * 3 + [False] * 3]
+    assert cache.pos_id.tolist() == [[2]]
+    same = attn.apply({}, k, k, None, None, method="apply_kv_cache")
+    assert same[0] is k and same[3] is None
+    with pytest.raises(TypeError, match="kv_cache must be a KVCache"):
+        attn.apply({}, k, k, None, object(), method="apply_kv_cache")
