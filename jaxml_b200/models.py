@@ -61,6 +61,11 @@ class _DecoderWithHead:
     def num_heads(self) -> int:
         return self.config.num_heads
 
+    intermediate_size = property(lambda self: self.config.intermediate_size)
+    norm_eps = property(lambda self: self.config.norm_eps)
+    use_bias = property(lambda self: self.config.use_bias)
+    attn_scale = property(lambda self: self.config.attn_scale)
+
     def init(self, key=0, input_ids=None, *_, std: float = 0.02, **__) -> dict:
         """Random N(0, std) kernels, unit norm weights, in the reference's parameter layout.  ``key`` is an
         int seed or a PRNG key (two uint32 words); example ``input_ids``, when given, are checked as

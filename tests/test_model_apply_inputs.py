@@ -211,3 +211,12 @@ def test_init_holds_the_rotary_tables_in_the_model_dtype(fam):
     head = {"llama": LlamaModelWithHead, "neox": GPTNeoXModelWithHead, "gemma3": GemmaModelWithHead}[fam]
     w = head(cfg).init(0)
     assert set(w) == {"params", "cache"} and set(w["cache"]) == {"gpt_neox" if fam == "neox" else "model"}
+
+
+def test_block_properties():
+    model, _ = MODELS[0]
+    cfg = model.config
+    assert (model.num_layers, model.head_dim, model.hidden_size, model.num_heads) == (
+        cfg.num_layers, cfg.head_dim, cfg.hidden_size, cfg.num_heads)
+    assert (model.intermediate_size, model.norm_eps, model.use_bias, model.attn_scale) == (
+        cfg.intermediate_size, cfg.norm_eps, cfg.use_bias, cfg.attn_scale)
