@@ -72,3 +72,12 @@ def test_importing_the_package_leaves_root_logging_alone():
         sys.modules.update(saved)
         root.handlers[:] = handlers
         root.setLevel(level)
+
+
+def test_inference_engine_submodules():
+    from jaxml_b200.engine import Engine as E
+    from jaxml_b200.inference_engine.engine import Engine, InferenceConfig
+    from jaxml_b200.inference_engine.sampling import SamplingMethod, top_k_filtering
+    from jaxml_b200.sampling import SamplingMethod as S
+
+    assert Engine is E and SamplingMethod is S and callable(top_k_filtering) and InferenceConfig is not None
