@@ -4,16 +4,17 @@
 Workload (the headline configuration): 32 layers, d 4096, 32 query / 8 KV heads x 128, SwiGLU FFN
 14336, vocab 128256, RoPE theta 5e5, RMSNorm eps 1e-5, random N(0, 0.02) weights (seed 0), batch 16,
 512 uniform-random prompt ids per row (seed 0), greedy decoding.  One step = one decode step of the
-whole batch (16 tokens).  With the defaults (--warmup 3 --steps 252) the warm-up plus timed steps are
-exactly the 255 decode steps of a 256-token generation.  Weights (15 GB) are far larger than L2, so
-no flush is needed between steps.
+whole batch (16 tokens).  The device-timed steps are steps warmup+1 .. warmup+steps of a generation
+(the line states the contexts they ran at); the e2e leg always generates the workload's 256 new tokens
+through Engine.generate.  Weights (15 GB) are far larger than L2, so no flush is needed between steps.
 
 --gpus N > 1 (launched with torchrun) runs tensor parallelism over N GPUs (NCCL): heads, FFN columns and
 the vocabulary are split N ways; the batch and total work stay fixed (strong scaling).
 
 --impl reference times the CPU restatement of jaxml's math (the oracle; JAX itself is not installed) on
-the host cores for the same metric: a bounded sample (one decoder layer + 1/32 of the LM head per step,
-at context 512) scaled to the 32-layer model.
+the host cores for the same metric.  Each of its steps is a bounded sample of one decode step: one
+decoder layer of the batch at context 512 plus 1/32 of the LM head; the metric scales the sample time
+by 32 (the line says so in "extrapolated").
 """
 from __future__ import annotations
 
@@ -56,6 +57,8 @@ def parse():
     ap.add_argument("--layers", type=int, default=32)
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-temp", action="store_true", help="skip the temperature-0.8 decode timing")
+    ap.add_argument("--e2e-tokens", type=int, default=256, help="new tokens per row of the e2e generation")
     ap.add_argument("--tp-pull", action="store_true",
                     help="tensor-parallel decode: separate pull all-reduce kernels instead of the push-fused projections")
     ap.add_argument("--micro", choices=["gemv", "attn", "gemm", "allreduce", "tpx"], default=None,
@@ -140,84 +143,137 @@ def step_bytes(cfg, B, ctx_mean, tp=1):
     return weights + kv, weights, kv
 
 
-def measure_gemv(rt, reps_layers=8):
-    """Average duration of the decode projection kernel on the gate/up weights of distinct layers
-    (235 MB each, larger than L2): back-to-back launches replayed from a CUDA graph, CUDA events on the
-    replay stream."""
-    import torch
+# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from single-kernel ncu captures
+# of the bench's micro shapes, where one was taken (profiles/ names the capture); None otherwise.
+NCU_TRAFFIC = {
+    "gate/up projection": (GEMV_TC_GATEUP_TRAFFIC, "ncu --set full of `bench.py --micro gemv --shape 28672,4096` "
+                           "(profiles/gemv_tc_gateup_ncu.md)"),
+    "o_proj projection": (33720000, "ncu --set full of `bench.py --micro gemv --shape 4096,4096 --gemv-impl 1` "
+                          "(profiles/gemv_k128_o_proj_ncu.md)"),
+}
 
+
+def kernel_table(rt, cfg, ctx, step_ms, n_layers=8):
+    """Per-kernel device time of the decode step's kernels, each launched back to back over `n_layers`
+    distinct layers (weights larger than L2 in total) from a CUDA graph and timed with CUDA events on the
+    replay stream.  bytes = algorithmic bytes per launch (weights as stored, activations in and out, K/V
+    of `ctx` keys); share = time per launch x launches per step / the measured step time."""
     from jaxml_b200 import _native as N
 
-    w = rt.w
-    acts = rt.dec
-    layers = w.layers[:reps_layers]
+    w, acts = rt.w, rt.dec
+    B, d = rt.B, w.d
+    layers = w.layers[:n_layers]
+    L = cfg.num_layers
+    rows = []
 
-    def launch_all(_stream):   # the runtime launches on torch's current stream (the capture stream)
-        for lw in layers:
-            rt._linear(acts, lw.wgu, w.Np_gu, w.Kp_d, "xn", N.JX_EPI_GLU_SILU, N_valid=w.F, out=acts["act"],
-                       ldo=w.F32, out_rp=acts["Mp"])
-    ms = _graph_ms(launch_all, len(layers))
-    nbytes = 2 * w.Np_gu * w.Kp_d + 2 * acts["Mp"] * w.Kp_d + 2 * rt.B * w.F
-    return ms, nbytes
+    def add(kernel, per_step, fns, nbytes):
+        us = _graph_ms(lambda _s: [f() for f in fns], len(fns)) * 1e3
+        tr = NCU_TRAFFIC.get(kernel)
+        rows.append({"kernel": kernel, "launches_per_step": per_step, "us": us, "bytes": nbytes,
+                     "gbs": nbytes / us / 1e3, "share": us * per_step / (step_ms * 1e3),
+                     "traffic": tr[0] if tr else None, "traffic_note": tr[1] if tr else "no ncu capture"})
+
+    if rt.fused_step is not None:
+        # the persistent decode-step kernel: one launch runs every layer
+        us = rt.time_fused_layers()
+        nbytes = rt.fused_step.algorithmic_bytes(ctx)
+        rows.append({"kernel": "decode layers (persistent kernel, all %d layers)" % L, "launches_per_step": 1,
+                     "us": us, "bytes": nbytes, "gbs": nbytes / us / 1e3, "share": us / (step_ms * 1e3),
+                     "traffic": rt.fused_step.ncu_traffic(ctx), "traffic_note": rt.fused_step.ncu_note})
+    else:
+        x_b = 2 * B * d
+        add("qkv projection", L, [lambda lw=lw: rt._linear(acts, lw.wqkv, w.Np_qkv, w.Kp_d, "xn", N.JX_EPI_STORE,
+                                                          N_valid=w.nqkv, out=acts["qkv"], ldo=w.nqkv)
+                                  for lw in layers], 2 * w.nqkv * d + x_b + 2 * B * w.nqkv)
+        add("attention (scores + pv)", L, [lambda li=li, lw=lw: rt._decode_attention(acts, li, lw, True)
+                                           for li, lw in enumerate(layers)],
+            B * ctx * 2 * w.Hkv * w.hd * 2 + 2 * B * w.nqkv + 2 * B * w.Hq * w.hd)
+        add("o_proj projection", L, [lambda lw=lw: rt._linear(acts, lw.wo, w.Np_d, w.Kp_o, "attn", N.JX_EPI_RESID,
+                                                             N_valid=d, out=acts["h"], ldo=d, res=acts["h"], ldr=d)
+                                     for lw in layers], 2 * d * w.Hq * w.hd + 2 * B * w.Hq * w.hd + 2 * x_b)
+        add("norm", 2 * L + 1, [lambda lw=lw: rt._norm(acts, w=lw.norms["post_attention_layernorm"][0])
+                                for lw in layers], 2 * x_b)
+        add("gate/up projection", L, [lambda lw=lw: rt._linear(acts, lw.wgu, w.Np_gu, w.Kp_d, "xn", N.JX_EPI_GLU_SILU,
+                                                              N_valid=w.F, out=acts["act"], ldo=w.F32,
+                                                              out_rp=acts["Mp"]) for lw in layers],
+            2 * 2 * w.F * d + x_b + 2 * B * w.F)
+        add("down projection", L, [lambda lw=lw: rt._linear(acts, lw.wd, w.Np_d, w.Kp_f, "act", N.JX_EPI_RESID,
+                                                           N_valid=d, out=acts["h"], ldo=d, res=acts["h"], ldr=d)
+                                   for lw in layers], 2 * d * w.F + 2 * B * w.F + 2 * x_b)
+    add("LM head projection", 1, [lambda: rt._linear(acts, w.lm_head, w.Np_v, w.Kp_d, "xn", N.JX_EPI_STORE,
+                                                     N_valid=w.V, out=rt.logits_buf(), ldo=w.V)] * 4,
+        2 * w.V * d + 2 * B * d + 2 * B * w.V)
+    return rows
 
 
 # ------------------------------------------------------------------------------------------------
 # CPU baseline: the oracle restatement on the host cores (bounded sample)
 # ------------------------------------------------------------------------------------------------
-def cpu_decode_sample(B=16, ctx=512, layers=1, seed=0):
-    """Seconds per 32-layer decode step of the L8 shape from a sample of `layers` layers + the LM head
-    (scaled by 1/32 per step so the sample is one layer-equivalent of work)."""
+CPU_SCALE = 32   # one sample = one of the 32 decoder layers + 1/32 of the LM head
+
+
+def cpu_decode_samples(B=16, ctx=512, n_warm=1, n_timed=3, budget_s=60.0, seed=0):
+    """Seconds per sample of one Llama-3-8B-shape decode step on the host cores (the oracle): one decoder
+    layer of the batch at context `ctx` plus 1/32 of the LM head's columns, so 32 samples are one full
+    step's work.  Times up to `n_timed` samples after `n_warm` untimed ones, stopping early once
+    `budget_s` seconds of timed work have run.  Returns (list of sample seconds, threads)."""
     import torch
 
     from oracle import jaxml_oracle as O
 
     threads = len(os.sched_getaffinity(0))
     torch.set_num_threads(threads)
-    full = l8_config(32)
-    cfg = l8_config(layers)
+    cfg = l8_config(1)
     params = O.init_params("llama", cfg, seed=seed, dtype=torch.bfloat16)
+    head = params["params"]["lm_head"]["kernel"][:, : cfg.vocab_size // CPU_SCALE].contiguous()
     T = (ctx // 256 + 1) * 256
     g = torch.Generator().manual_seed(seed)
-    caches = []
-    for _ in range(layers):
-        c = O.OracleKVCache(T, torch.bfloat16)
-        k = (torch.randn(B, ctx, cfg.num_key_value_heads, cfg.head_dim, generator=g)).to(torch.bfloat16)
-        caches.append(c.update(k, k.clone(), None))
+    c = O.OracleKVCache(T, torch.bfloat16)
+    k = (torch.randn(B, ctx, cfg.num_key_value_heads, cfg.head_dim, generator=g)).to(torch.bfloat16)
+    caches = (c.update(k, k.clone(), None),)
     tok = torch.randint(0, cfg.vocab_size, (B, 1), generator=g, dtype=torch.int32)
-    # one untimed pass (page in), then the timed one
-    O.forward("llama", cfg, params, tok, torch.bfloat16, kv_caches=tuple(caches), keep_last_n_logits=1)
-    t0 = time.perf_counter()
-    out = O.forward("llama", cfg, params, tok, torch.bfloat16, kv_caches=tuple(caches), keep_last_n_logits=1,
-                    with_head=False)
-    t_layers = time.perf_counter() - t0
-    h = out.last_hidden_state
-    t0 = time.perf_counter()
-    O.dense(h, params["params"]["lm_head"]["kernel"], None, torch.bfloat16)
-    t_head = time.perf_counter() - t0
-    per_step = t_layers / layers * full.num_layers + t_head
-    return per_step, threads
+
+    def one():
+        out = O.forward("llama", cfg, params, tok, torch.bfloat16, kv_caches=caches, with_head=False)
+        O.dense(out.last_hidden_state, head, None, torch.bfloat16)
+    for _ in range(n_warm):
+        one()
+    times = []
+    for _ in range(n_timed):
+        t0 = time.perf_counter()
+        one()
+        times.append(time.perf_counter() - t0)
+        if sum(times) > budget_s:
+            break
+    return times, threads
+
+
+CPU_SAMPLE_NOTE = ("torch-CPU restatement of jaxml's math (JAX is not installed): each sample is one decoder layer "
+                   "of a batch-16 decode step at context 512 plus 1/32 of the LM head; tok/s = 16 / (32 x sample time)")
 
 
 def reference_arm(args):
-    """--impl reference: the oracle timed on the host cores, the same metric and config."""
+    """--impl reference: the oracle timed on the host cores, the same metric and config.  Rank 0 only."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    per_step, threads = cpu_decode_sample(B=args.batch, ctx=args.prompt)
-    budget = 120.0
-    steps = max(1, min(args.steps, int(budget / max(per_step, 1e-3))))
-    # per_step above is one measured sample; report it as the steady-state step time
-    value = args.batch / per_step
+    times, threads = cpu_decode_samples(B=args.batch, ctx=args.prompt, n_warm=max(1, min(args.warmup, 2)),
+                                        n_timed=max(1, args.steps), budget_s=60.0)
+    sample_s = sum(times) / len(times)
+    value = args.batch / (CPU_SCALE * sample_s)
     line = {
-        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus, "steps": steps,
-        "warmup": args.warmup, "ms_per_step": per_step * 1e3, "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (uniform-random ids, N(0,0.02) weights, seed 0)",
-        "config": {"workload": "llama3-8b-shape bf16 decode, batch 16, prompt 512", "global_batch": args.batch,
-                   "seq_len": args.prompt, "parallelism": "cpu"},
+        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus, "steps": len(times),
+        "warmup": max(1, min(args.warmup, 2)), "ms_per_step": sample_s * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (uniform-random ids, N(0,0.02) weights, seed 0)",
+        "config": {"workload": "llama3-8b-shape bf16 decode, batch %d, context %d (one layer + 1/32 LM head per "
+                               "step, scaled by 32)" % (args.batch, args.prompt),
+                   "global_batch": args.batch, "seq_len": args.prompt, "parallelism": "cpu"},
+        "extrapolated": {"timed": "one decoder layer + 1/32 of the LM head per step (a 1/32 sample of a decode step)",
+                         "scale": CPU_SCALE, "full_step_ms": CPU_SCALE * sample_s * 1e3},
         "impl": "reference",
         "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port",
-                         "sample": "torch-CPU restatement of jaxml's math (JAX not installed): one decode step "
-                                   "of 1 of 32 layers + the LM head at context 512, batch 16, scaled to 32 layers"},
+                         "sample": CPU_SAMPLE_NOTE},
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -307,70 +363,110 @@ def gpu_arm(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         total_ms = float(t.item())
     rt.check_status()
-    ctx_first = P + args.warmup + 1
-    ctx_mean = ctx_first + (args.steps - 1) / 2.0 + 1
+    ctx_first = P + args.warmup + 1          # valid keys (after the append) at the first timed step
+    ctx_last = ctx_first + args.steps - 1
+    ctx_mean = (ctx_first + ctx_last) / 2.0
     value = B * args.steps / (total_ms / 1e3)
     sbytes, wbytes, kvbytes = step_bytes(cfg, B, ctx_mean, tp)
+    step_ms_mean = total_ms / args.steps
 
-    # ---- dominant kernel: the decode projection, timed alone ----
-    gemv_ms, gemv_bytes = measure_gemv(rt)
+    # ---- temperature 0.8 with a fixed seed (the workload's sampled variant), same steps ----
+    temp_line = None
+    if not args.no_temp:
+        rt.reset(torch.ones(B, P, dtype=torch.bool, device=dev), key, sub, n_new)
+        rt.prefill(ids_d, False, 0.8)
+        rt.decode_step(False, 0.8)
+        graph_t = rt.capture_decode(False, 0.8)
+        for _ in range(args.warmup - 1):
+            graph_t.replay()
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+        t0e, t1e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0e.record()
+        for _ in range(args.steps):
+            graph_t.replay()
+        t1e.record()
+        torch.cuda.synchronize()
+        tms = t0e.elapsed_time(t1e)
+        if dist is not None:
+            t = torch.tensor([tms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            tms = float(t.item())
+        rt.check_status()
+        temp_line = {"value": B * args.steps / (tms / 1e3), "unit": "tok/s", "ms_per_step": tms / args.steps,
+                     "seed": 0, "temperature": 0.8}
+        del graph_t
 
-    # ---- end to end through Engine.generate with host buffers ----
+    # ---- per-kernel durations (graph replays, CUDA events) and the dominant kernel ----
+    table = kernel_table(rt, cfg, ctx_last, step_ms_mean) if tp == 1 else None
+
+    # ---- end to end through Engine.generate with host buffers: the workload's 256 new tokens ----
     e2e = None
     if not args.no_e2e:
-        engine.generate(prompt, max_new_tokens=n_new, temperature=0.0)   # warm (graph capture)
+        n_e2e = args.e2e_tokens
+        engine.generate(prompt, max_new_tokens=n_e2e, temperature=0.0)   # warm (graph capture)
         torch.cuda.synchronize()
         if dist is not None:
             dist.barrier()
         t0 = time.perf_counter()
-        out = engine.generate(prompt, max_new_tokens=n_new, temperature=0.0, include_prompt=False)
+        out = engine.generate(prompt, max_new_tokens=n_e2e, temperature=0.0, include_prompt=False)
         el = time.perf_counter() - t0
         if dist is not None:
             t = torch.tensor([el], device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             el = float(t.item())
-        e2e = {"value": B * n_new / el, "unit": "tok/s", "h2d_bytes_per_step": round(prompt.numel() * 4 / n_new, 1),
-               "d2h_bytes_per_step": int(out.numel() * 4 // n_new),
-               "note": "Engine.generate(host prompt) incl. H2D copy, prefill, 255 decode steps, D2H of tokens"}
+        e2e = {"value": B * n_e2e / el, "unit": "tok/s", "h2d_bytes_per_step": round(prompt.numel() * 4 / n_e2e, 1),
+               "d2h_bytes_per_step": int(out.numel() * 4 // n_e2e),
+               "note": "Engine.generate(host prompt [%d, %d]) incl. H2D copy, prefill, %d decode steps, D2H of "
+                       "the [%d, %d] tokens; %d new tokens per row" % (B, P, n_e2e - 1, B, n_e2e, n_e2e)}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        per_step, threads = cpu_decode_sample(B=B, ctx=P)
-        cpu = {"value": B / per_step, "unit": "tok/s", "cores": threads, "kind": "port",
-               "sample": "torch-CPU restatement of jaxml's math: one decode step of 1 of 32 layers + LM head, "
-                         "batch 16, context 512, scaled to 32 layers"}
+        times, threads = cpu_decode_samples(B=B, ctx=P, n_warm=1, n_timed=3, budget_s=30.0)
+        sample_s = sum(times) / len(times)
+        cpu = {"value": B / (CPU_SCALE * sample_s), "unit": "tok/s", "cores": threads, "kind": "port",
+               "sample": CPU_SAMPLE_NOTE + "; %d samples timed" % len(times)}
 
-    import json as _json
     peaks = {}
     try:
-        peaks = _json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
     except OSError:
         pass
     hbm_peak = peaks.get("hbm_gbs", 6650.0)
-    achieved = gemv_bytes / (gemv_ms * 1e-3) / 1e9
+    peak_src = "MEASURED_PEAKS.json hbm_gbs (burst copy)" if "hbm_gbs" in peaks else "fallback 6650 GB/s"
+    roofline = None
+    if table is not None:
+        dom = max(table, key=lambda r: r["share"])
+        roofline = {"bound": "hbm", "achieved": dom["gbs"], "peak": hbm_peak, "unit": "GB/s",
+                    "frac": dom["gbs"] / hbm_peak, "traffic": dom["traffic"],
+                    "traffic_note": dom["traffic_note"], "kernel": dom["kernel"], "share_of_step": dom["share"],
+                    "algorithmic_bytes_per_launch": dom["bytes"], "us_per_launch": dom["us"],
+                    "peak_source": peak_src}
+        for r in table:
+            r["frac"] = r["gbs"] / hbm_peak
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
+            "warmup": args.warmup, "ms_per_step": step_ms_mean,
             "p50_step_ms": statistics.median(step_ms), "prefill_ms": prefill_ms,
             "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (uniform-random prompt ids, N(0,0.02) random-init weights, seed 0)",
-            "config": {"workload": "llama3-8b-shape bf16 greedy decode, batch 16, prompt 512, 256 new tokens",
+            "config": {"workload": "llama3-8b-shape bf16 greedy decode, batch %d, prompt %d: %d timed decode steps "
+                                   "at contexts %d..%d (e2e: %s new tokens)"
+                                   % (B, P, args.steps, ctx_first, ctx_last, args.e2e_tokens if e2e else "no"),
                        "global_batch": B, "seq_len": P, "parallelism": f"tp{tp}",
                        "tp_exchange": None if tp == 1 else ("pull all-reduce" if args.tp_pull else "push-fused"),
+                       "decode_path": rt.decode_path_name(),
                        "decode_attention": ["by shape", "split", "cluster", "column pv", "cluster-split"][args.attn_impl],
                        "l2": "inputs larger than L2 (15 GB of weights per step)"},
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-                         "frac": achieved / hbm_peak, "traffic": GEMV_TC_GATEUP_TRAFFIC,
-                         "traffic_note": "dram__bytes_read.sum + dram__bytes_write.sum of one launch of this "
-                                         "kernel on the gate/up shape (ncu --set full, cold cache); "
-                                         "algorithmic bytes per launch: %d" % gemv_bytes,
-                         "kernel": "gemv_tc_kernel (tcgen05 decode projection, gate/up: 235 MB weights per launch)",
-                         "peak_source": "MEASURED_PEAKS.json hbm_gbs" if "hbm_gbs" in peaks else "fallback"},
+            "roofline": roofline,
+            "kernels": table,
             "step_roofline": {"bytes_per_step": sbytes, "weight_bytes": wbytes, "kv_bytes": kvbytes,
-                              "achieved_gbs": sbytes / (total_ms / args.steps * 1e-3) / 1e9,
-                              "frac": sbytes / (total_ms / args.steps * 1e-3) / 1e9 / hbm_peak},
+                              "achieved_gbs": sbytes / (step_ms_mean * 1e-3) / 1e9,
+                              "frac": sbytes / (step_ms_mean * 1e-3) / 1e9 / hbm_peak, "peak_source": peak_src},
+            "temperature_0.8": temp_line,
             "clocks": clocks.summary(),
             "gpu_launches": launches_per_step * args.steps,
             "e2e": e2e,

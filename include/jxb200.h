@@ -1,8 +1,9 @@
 /*
  * libjxb200 -- C ABI of the B200 (sm_100a) decode/prefill path that stands in for jaxml's
  * JAX/XLA compute.  Every entry point takes plain device pointers, sizes and a cudaStream_t passed as
- * void*, launches asynchronously on that stream and returns a status code (0 = JX_OK).  Nothing here
- * allocates device memory: scratch buffers are passed in by the caller.  Device-side failures (index
+ * void*, launches asynchronously on that stream and returns a status code (0 = JX_OK).  The compute
+ * entry points allocate no device memory (scratch buffers are passed in by the caller); only the
+ * tensor-parallel set-up call jx_comm_alloc allocates (its peer region).  Device-side failures (index
  * out of range, a bounded wait that ran out) are reported through an int status word in device
  * memory that the caller reads after synchronising.
  *
@@ -299,9 +300,11 @@ int jx_linear_decode(const void* W, const void* X, long long Np, long long Kp, i
  * for example a handler running inside a host framework's custom-call / FFI hook, which may only use
  * the buffers it is handed, or a plugin that must not call cudaMalloc.  The split-K scratch is a
  * fixed array compiled into this library (2.3 MiB of every GPU that loads it, until exit), so the
- * sizes are capped: M <= 16 token rows, Np <= 262080 weight rows, at most 148 CTAs; larger requests fail
- * with JX_ERR_SHAPE.  The first call on a device looks the array's address up (make it before any
- * stream capture).  All calls share the array: calls that overlap on the GPU race and must not. */
+ * sizes are capped: M <= 16 token rows, Np <= 262080 weight rows, grid <= 148 CTAs (grid <= 0 means 148);
+ * larger requests fail with JX_ERR_SHAPE.  The first call on a device looks the array's address up (make
+ * it before any stream capture).  Every call clears the array's arrival counters with a stream operation
+ * ahead of the kernel, so pdl gives no overlap with the preceding kernel here.  All calls share the
+ * array: calls that overlap on the GPU race and must not. */
 int jx_linear_decode_noalloc(const void* W, const void* X, long long Np, long long Kp, int M, const jx_epilogue* epi,
                              int* status, int grid, int pdl, void* stream);
 

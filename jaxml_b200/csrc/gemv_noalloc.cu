@@ -62,7 +62,9 @@ extern "C" int jx_linear_decode_noalloc(const void* W, const void* X, long long 
     return fail(JX_ERR_SHAPE, "jx_linear_decode_noalloc: M must be in [1, 16] (fixed scratch size)");
   if (Np <= 0 || Np % 64 || Np / 64 + 1 > kNoAllocMaxCounters)
     return fail(JX_ERR_SHAPE, "jx_linear_decode_noalloc: Np must be a positive multiple of 64 and <= 262080");
-  if (grid <= 0 || grid > kNoAllocMaxGrid) grid = kNoAllocMaxGrid;
+  if (grid > kNoAllocMaxGrid)
+    return fail(JX_ERR_SHAPE, "jx_linear_decode_noalloc: grid must be at most 148 CTAs (fixed scratch size)");
+  if (grid <= 0) grid = kNoAllocMaxGrid;
   if ((long long)gemv_workspace_floats(grid, 1) > kNoAllocPartials)
     return fail(JX_ERR_SHAPE, "jx_linear_decode_noalloc: grid exceeds the fixed scratch size");
   float* scratch = nullptr;
@@ -70,6 +72,8 @@ extern "C" int jx_linear_decode_noalloc(const void* W, const void* X, long long 
   if (rc != JX_OK) return rc;
   int* counters = reinterpret_cast<int*>(scratch + kNoAllocPartials);
   // The counters must start at zero; the array keeps whatever the previous call (or an aborted one) left.
+  // This clear is a stream operation of its own ahead of the kernel, so pdl = 1 cannot overlap the
+  // kernel's start with the kernel before it on this entry point.
   if (cudaMemsetAsync(counters, 0, (size_t)(Np / 64 + 1) * sizeof(int), (cudaStream_t)stream) != cudaSuccess)
     return note_cuda("jx_linear_decode_noalloc: clearing counters");
   rc = run_gemv((const bf16*)W, (const bf16*)X, Np, Kp, M, *epi, scratch, kNoAllocPartials, counters, status, grid,

@@ -317,6 +317,8 @@ class DecoderRuntime:
             self.attn_ws = torch.zeros((nb.value + 3) // 4, dtype=torch.float32, device=dev)
             self.attn_counters = torch.zeros(B * w.Hkv, dtype=torch.int32, device=dev)
         self.graph = None
+        # the persistent decode-step kernel's plan when it runs this runtime's layers (else None)
+        self.fused_step = None
         self._launches = 0
         self.launches_last_step = 0
         self._push_pending = False
@@ -837,6 +839,11 @@ class DecoderRuntime:
         self._head(acts, self.row_map)
         self._sample(greedy, temp, update_pos=True)
         self.launches_last_step = self._launches
+
+    def decode_path_name(self) -> str:
+        if self.fused_step is not None:
+            return "persistent decode-step kernel"
+        return "one launch per op (norm, qkv, attention scores and pv, o_proj, norm, gate/up, down per layer)"
 
     def count_launches_per_decode_step(self) -> int:
         """libjxb200 kernel launches in one decode step (counted while the step was issued)."""

@@ -8,9 +8,6 @@ engine generates int32 tokens on the GPU, and ``batch_decode`` turns them back i
 """
 from __future__ import annotations
 
-import math
-import numbers
-import operator
 from collections.abc import Mapping
 from collections.abc import Sequence as SequenceABC
 from dataclasses import dataclass, field
@@ -19,33 +16,12 @@ from typing import Any, Optional
 import numpy as np
 import torch
 
+from ._checks import normalize_bool as _flag
+from ._checks import normalize_count as _count
 from ._checks import normalize_dtype
+from ._checks import normalize_float as _real
 from .engine import Engine, InferenceConfig
 from .hf_utils import _normalize_hf_architecture, _normalize_hf_model_name, _validate_hf_dtype, load_model_from_hf
-
-
-def _count(name: str, value) -> int:
-    if isinstance(value, (bool, np.bool_)):
-        raise TypeError(f"{name} must be an integer, got {type(value)}.")
-    try:
-        return operator.index(value)
-    except TypeError as e:
-        raise TypeError(f"{name} must be an integer, got {type(value)}.") from e
-
-
-def _real(name: str, value) -> float:
-    if isinstance(value, (bool, np.bool_)) or not isinstance(value, numbers.Real):
-        raise TypeError(f"{name} must be a real number, got {type(value)}.")
-    v = float(value)
-    if not math.isfinite(v):
-        raise ValueError(f"{name} must be finite, got {v}.")
-    return v
-
-
-def _flag(name: str, value) -> bool:
-    if not isinstance(value, (bool, np.bool_)):
-        raise TypeError(f"{name} must be a boolean, got {type(value)}.")
-    return bool(value)
 
 
 def _kwargs(name: str, value) -> dict:

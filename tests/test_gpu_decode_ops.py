@@ -286,3 +286,33 @@ def test_linear_decode_norm_prologue(impl, kind, M):
         assert err <= 2e-2 * max(1.0, out_ref.float().abs().max().item()), err
         if bool((diff == 0).all()):
             assert torch.equal(out, out_ref)
+
+
+@pytest.mark.parametrize("form", [0, 3], ids=["split", "column"])
+@pytest.mark.parametrize("T,lens", [(4096, [4096, 2085, 129]), (32768, [32768, 16421])])
+def test_decode_attention_long_context_matches_oracle(form, T, lens):
+    """Decode attention at 4k and 32k-key caches (Llama-3-8B heads): the key-split count grows with the
+    buffer length (32 and 256 splits of 128 keys), and rows of one batch have different lengths."""
+    from oracle import jaxml_oracle as O
+
+    N = _n()
+    N.call("jx_set_decode_attention_impl", form)
+    try:
+        torch.manual_seed(13)
+        B, Hq, Hkv, hd, L, layer = len(lens), 32, 8, 128, 1, 0
+        lens_t = torch.tensor(lens, dtype=torch.int32)
+        kc = torch.randn(L, B, T, Hkv, hd).to(torch.bfloat16)
+        vc = torch.randn(L, B, T, Hkv, hd).to(torch.bfloat16)
+        q = torch.randn(B, Hq, hd).to(torch.bfloat16)
+        got = _dattn_call(N, B, Hq, Hkv, hd, T, L, layer, q.reshape(B, -1).cuda(), kc.cuda(), vc.cuda(),
+                          (lens_t - 2).cuda()).float().cpu().reshape(B, Hq, hd)
+        for b in range(B):   # one row at a time keeps the oracle's repeated K/V small
+            mask = torch.arange(T)[None, :] < lens_t[b:b + 1, None]
+            want = O.mha(q[b:b + 1, None], O.repeat_kv(kc[layer, b:b + 1], Hq // Hkv),
+                         O.repeat_kv(vc[layer, b:b + 1], Hq // Hkv), mask, True, None, hd ** -0.5)[0, 0].float()
+            ulp = torch.exp2(torch.floor(torch.log2(want.abs().clamp_min(1e-30))) - 7)
+            err = (got[b] - want).abs()
+            assert err.max().item() <= 2e-3, (b, err.max().item())
+            assert (err <= ulp + 1e-6).float().mean().item() >= 0.99
+    finally:
+        N.call("jx_set_decode_attention_impl", 0)
