@@ -27,6 +27,7 @@ installed on either machine).
 """
 from __future__ import annotations
 
+import contextlib
 import math
 from dataclasses import dataclass
 from typing import Optional
@@ -51,10 +52,28 @@ def _scalar(value: float, dtype) -> torch.Tensor:
 # ----------------------------------------------------------------------------------------------
 # Layers
 # ----------------------------------------------------------------------------------------------
+_ACC = [F32]
+
+
+@contextlib.contextmanager
+def accumulation(acc_dtype):
+    """Runs every float32 step (projection and attention sums, softmax, norm statistics) in ``acc_dtype``
+    (float64) instead: a variant of the restatement, not the restatement, used by tests to measure how far
+    the bfloat16 results of the same math move when only the precision / order of those sums changes.
+    The model-dtype rounding points are the same."""
+    old = _ACC[0]
+    _ACC[0] = acc_dtype
+    try:
+        yield
+    finally:
+        _ACC[0] = old
+
+
 def dense(x: torch.Tensor, kernel: torch.Tensor, bias: Optional[torch.Tensor], dtype, n_in: int = 1) -> torch.Tensor:
     """``DenseGeneral`` contracting the last ``n_in`` axes of ``x`` with the first ``n_in`` of ``kernel``."""
-    xin = _f32(x.to(dtype))
-    w = _f32(kernel.to(dtype))
+    acc = _ACC[0]
+    xin = x.to(dtype).to(acc)
+    w = kernel.to(dtype).to(acc)
     kdim = int(np.prod(kernel.shape[:n_in]))
     out_shape = tuple(x.shape[: x.ndim - n_in]) + tuple(kernel.shape[n_in:])
     y = (xin.reshape(-1, kdim) @ w.reshape(kdim, -1)).reshape(out_shape).to(dtype)
@@ -65,29 +84,30 @@ def dense(x: torch.Tensor, kernel: torch.Tensor, bias: Optional[torch.Tensor], d
 
 def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
     in_dtype = x.dtype
-    x32 = _f32(x)
+    x32 = x.to(_ACC[0])
     ms = (x32 * x32).mean(-1, keepdim=True)
-    y = (x32 / torch.sqrt(ms + torch.tensor(eps, dtype=F32))).to(in_dtype)
+    y = (x32 / torch.sqrt(ms + torch.tensor(eps, dtype=_ACC[0]))).to(in_dtype)
     out_dtype = torch.promote_types(weight.dtype, in_dtype)
     return (_f32(weight) * _f32(y)).to(out_dtype)
 
 
 def gemma_rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
     in_dtype = x.dtype
-    x32 = _f32(x)
+    x32 = x.to(_ACC[0])
     ms = (x32 * x32).mean(-1, keepdim=True)
-    y = x32 * (1.0 / torch.sqrt(ms + torch.tensor(eps, dtype=F32)))
-    return ((_f32(weight) + 1.0) * y).to(in_dtype)
+    y = x32 * (1.0 / torch.sqrt(ms + torch.tensor(eps, dtype=_ACC[0])))
+    return ((weight.to(_ACC[0]) + 1.0) * y).to(in_dtype)
 
 
 def layernorm(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor], eps: float) -> torch.Tensor:
     in_dtype = x.dtype
-    x32 = _f32(x)
+    acc = _ACC[0]
+    x32 = x.to(acc)
     mean = x32.mean(-1, keepdim=True)
     var = ((x32 - mean) ** 2).mean(-1, keepdim=True)
-    out = (x32 - mean) / torch.sqrt(var + torch.tensor(eps, dtype=F32)) * _f32(weight)
+    out = (x32 - mean) / torch.sqrt(var + torch.tensor(eps, dtype=acc)) * weight.to(acc)
     if bias is not None:
-        out = out + _f32(bias)
+        out = out + bias.to(acc)
     return out.to(in_dtype)
 
 
@@ -137,7 +157,8 @@ def repeat_kv(x: torch.Tensor, n_rep: int) -> torch.Tensor:
 def mha(q, k, v, attention_mask, causal: bool, sliding_window: Optional[int], attn_scale: float, return_weights=False):
     """``Attention.mha``: q ``[B,S,H,hd]``, k/v ``[B,T,H,hd]`` (already repeated), mask ``[B,T]`` bool."""
     dtype = q.dtype
-    x = torch.einsum("bshn,bthn->bhst", _f32(q), _f32(k)).to(dtype)
+    acc = _ACC[0]
+    x = torch.einsum("bshn,bthn->bhst", q.to(acc), k.to(acc)).to(dtype)
     x = _f32((_f32(x) * _scalar(attn_scale, dtype)).to(dtype))
     _, _, q_len, k_len = x.shape
     neg = torch.zeros_like(x, dtype=torch.bool)
@@ -160,9 +181,10 @@ def mha(q, k, v, attention_mask, causal: bool, sliding_window: Optional[int], at
     x = torch.where(all_masked, torch.zeros_like(x), x)
     # jax.nn.softmax: exp(x - max) / sum(exp(x - max)) with a true division (torch's CPU softmax
     # multiplies by the reciprocal, which rounds differently)
+    x = x.to(acc)
     e = torch.exp(x - x.max(-1, keepdim=True).values)
     p = (e / e.sum(-1, keepdim=True)).to(dtype)
-    out = torch.einsum("bhst,bthn->bshn", _f32(p), _f32(v)).to(dtype)
+    out = torch.einsum("bhst,bthn->bshn", p.to(acc), v.to(acc)).to(dtype)
     return (out, p) if return_weights else out
 
 
