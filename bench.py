@@ -58,6 +58,8 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-temp", action="store_true", help="skip the temperature-0.8 decode timing")
+    ap.add_argument("--per-op", action="store_true",
+                    help="decode with one kernel launch per op instead of the persistent decode-step kernel")
     ap.add_argument("--e2e-tokens", type=int, default=256, help="new tokens per row of the e2e generation")
     ap.add_argument("--tp-pull", action="store_true",
                     help="tensor-parallel decode: separate pull all-reduce kernels instead of the push-fused projections")
@@ -158,6 +160,8 @@ def kernel_table(rt, cfg, ctx, step_ms, n_layers=8):
     distinct layers (weights larger than L2 in total) from a CUDA graph and timed with CUDA events on the
     replay stream.  bytes = algorithmic bytes per launch (weights as stored, activations in and out, K/V
     of `ctx` keys); share = time per launch x launches per step / the measured step time."""
+    import torch
+
     from jaxml_b200 import _native as N
 
     w, acts = rt.w, rt.dec
@@ -174,12 +178,11 @@ def kernel_table(rt, cfg, ctx, step_ms, n_layers=8):
                      "traffic": tr[0] if tr else None, "traffic_note": tr[1] if tr else "no ncu capture"})
 
     if rt.fused_step is not None:
-        # the persistent decode-step kernel: one launch runs every layer
-        us = rt.time_fused_layers()
-        nbytes = rt.fused_step.algorithmic_bytes(ctx)
-        rows.append({"kernel": "decode layers (persistent kernel, all %d layers)" % L, "launches_per_step": 1,
-                     "us": us, "bytes": nbytes, "gbs": nbytes / us / 1e3, "share": us / (step_ms * 1e3),
-                     "traffic": rt.fused_step.ncu_traffic(ctx), "traffic_note": rt.fused_step.ncu_note})
+        # the persistent decode-step kernel: one launch runs every layer, the final norm and the LM head
+        nbytes, _, _ = step_bytes(cfg, B, ctx)
+        add("decode_step_kernel (persistent: %d layers + final norm + LM head)" % L, 1,
+            [lambda: rt.fused_step.launch(torch.cuda.current_stream().cuda_stream)] * 4, nbytes)
+        return rows
     else:
         x_b = 2 * B * d
         add("qkv projection", L, [lambda lw=lw: rt._linear(acts, lw.wqkv, w.Np_qkv, w.Kp_d, "xn", N.JX_EPI_STORE,
@@ -305,10 +308,13 @@ def gpu_arm(args):
         from jaxml_b200 import _native as N
 
         N.call("jx_set_decode_attention_impl", args.attn_impl)
-    if args.tp_pull:
+    if args.tp_pull or args.per_op:
         from jaxml_b200.runtime import DecoderRuntime
 
-        DecoderRuntime.peer_push = False
+        if args.tp_pull:
+            DecoderRuntime.peer_push = False
+        if args.per_op:
+            DecoderRuntime.persistent_decode = False
     cfg = l8_config(args.layers)
     B, P = args.batch, args.prompt
     n_new = 1 + args.warmup + args.steps

@@ -365,6 +365,51 @@ int jx_sample_finalize(const jx_sample_args* args, const unsigned long long* gat
 /* Clear the split-K counters after an error (they are self-resetting otherwise). */
 int jx_memset_async(void* ptr, int value, long long bytes, void* stream);
 
+/* ---- one decode step of a Llama-family stack in one persistent kernel ----
+ * Replaces, for one token per row, the whole of LlamaModelWithHead.__call__ with a populated cache
+ * (models/llama.py:112-143 per layer: input RMSNorm, q/k/v projections, RoPE (nn/position.py:78-141),
+ * cache append (cache.py:183-243), Attention.mha decode branch (nn/attention.py:321-400), o_proj +
+ * residual, post-attention RMSNorm, SwiGLU MLP (models/llama.py:82-88) + residual; then the final norm
+ * and lm_head, models/llama.py:245-273), with the reference's bf16 rounding points.  One cooperative
+ * launch of one CTA per SM runs every layer: the weights of the next phase stream into shared memory
+ * while the current phase finishes, and the phases are separated by grid-wide barriers (bounded waits:
+ * JX_ERR_TIMEOUT in *status).  Embedding rows are gathered from ids[M]; logits [M, V] bf16 are left for
+ * jx_sample.  Requirements: bf16, head_dim 128, M <= 16, Hq / Hkv <= 16, no sliding window, rd % 16 == 0,
+ * weights in the K128 layout (the gate/up rows interleaved in groups of 32, as for JX_EPI_GLU_SILU),
+ * activations h [M, d] row-major and xn / attn / act in the K128 layout with 16 padded rows. */
+typedef struct jx_step_args {
+  int M, L;                  /* token rows (<= 16), layers */
+  int d, Hq, Hkv, hd;        /* hidden size, heads, head size (128) */
+  int F, V, vocab;           /* intermediate size, lm_head columns, embedding rows */
+  int T, rd, max_pos;        /* cache slots per row, rotary dims, rows of the cos / sin tables */
+  long long Np_qkv, Np_d, Np_gu, Np_v, Kp_d, Kp_o, Kp_f;   /* padded K128 extents */
+  float eps, scale;          /* RMSNorm epsilon, attention scale */
+  const void* layers;        /* device array of L x 6 pointers: wqkv, wo, wgu, wd, input / post-attention norm weights */
+  const void* embed;         /* [vocab, d] */
+  const int* ids;            /* [M] this step's token ids */
+  const void* final_norm;    /* [d] */
+  const void* lm_head;       /* K128 [Np_v, Kp_d] */
+  void* h;                   /* residual stream [M, d] (rows 0..M-1) */
+  void* xn;                  /* normalised activations, K128 [16, Kp_d] */
+  void* qkv;                 /* fused projection output [M, (Hq + 2 Hkv) hd] */
+  void* attn;                /* attention output, K128 [16, Kp_o] */
+  void* act;                 /* GLU product, K128 [16, Kp_f] */
+  void* logits;              /* [M, V] */
+  void* k_cache, *v_cache;   /* [L, M, T, Hkv, hd] */
+  const void* cos, *sin;     /* [max_pos, rd] */
+  const int* pos_id;         /* [M]: this step writes position pos_id + 1 */
+  float* ws;                 /* split-K partial tiles, >= grid x 2 x 16 x 128 floats */
+  long long ws_floats;
+  int* counters;             /* >= Np_v / 128 + 1 ints, zero (left zero) */
+  void* attn_ws;             /* jx_decode_attention_workspace(M, Hq, 128, T, 0) bytes */
+  long long attn_ws_bytes;
+  int* attn_counters;        /* [M x Hkv] ints, zero (left zero) */
+  int* sync;                 /* 6 ints: grid barrier counter, abort flag, where a bounded wait gave up (cleared by the call) */
+  int* status;
+  int grid;                  /* CTAs (<= 0: one per SM) */
+} jx_step_args;
+int jx_decode_step(const jx_step_args* args, void* stream);
+
 /* ---- tensor parallelism over NVLink peer memory ----
  * The reference all-reduces the row-parallel o_proj / down_proj outputs through XLA's GSPMD collectives
  * (inference_engine/engine.py:258-267 sharding rules, models/llama.py:133-137 residual adds); these

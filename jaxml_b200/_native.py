@@ -86,6 +86,16 @@ class JxSampleArgs(ctypes.Structure):
                 ("advance_rng", I), ("_pad0", I), ("status", P)]
 
 
+class JxStepArgs(ctypes.Structure):
+    _fields_ = [("M", I), ("L", I), ("d", I), ("Hq", I), ("Hkv", I), ("hd", I), ("F", I), ("V", I), ("vocab", I),
+                ("T", I), ("rd", I), ("max_pos", I), ("Np_qkv", LL), ("Np_d", LL), ("Np_gu", LL), ("Np_v", LL),
+                ("Kp_d", LL), ("Kp_o", LL), ("Kp_f", LL), ("eps", F), ("scale", F), ("layers", P), ("embed", P),
+                ("ids", P), ("final_norm", P), ("lm_head", P), ("h", P), ("xn", P), ("qkv", P), ("attn", P),
+                ("act", P), ("logits", P), ("k_cache", P), ("v_cache", P), ("cos", P), ("sin", P), ("pos_id", P),
+                ("ws", P), ("ws_floats", LL), ("counters", P), ("attn_ws", P), ("attn_ws_bytes", LL),
+                ("attn_counters", P), ("sync", P), ("status", P), ("grid", I)]
+
+
 _PROTOS = {
     "jx_version": (ctypes.c_char_p, []),
     "jx_last_error": (ctypes.c_char_p, []),
@@ -111,6 +121,7 @@ _PROTOS = {
     "jx_set_decode_attention_impl": (I, [I]),
     "jx_prefill_attention": (I, [ctypes.POINTER(JxPAttnArgs), I, P]),
     "jx_sample": (I, [ctypes.POINTER(JxSampleArgs), I, P]),
+    "jx_decode_step": (I, [ctypes.POINTER(JxStepArgs), P]),
     "jx_sample_finalize": (I, [ctypes.POINTER(JxSampleArgs), P, I, P]),
     "jx_comm_alloc": (I, [LL, ctypes.POINTER(P)]),
     "jx_comm_free": (I, [P]),

@@ -262,10 +262,63 @@ class ModelWeights:
 
 
 # ------------------------------------------------------------------------------------------------
+# Persistent decode step
+# ------------------------------------------------------------------------------------------------
+class PersistentDecode:
+    """Arguments of the persistent decode-step kernel (``jx_decode_step``) for one runtime: every layer,
+    the final norm and the LM head of a Llama-family bf16 decode step in one cooperative launch, on the
+    runtime's own buffers.  ``eligible`` says when the kernel covers the runtime's model and batch."""
+
+    @staticmethod
+    def eligible(rt) -> bool:
+        w, cfg = rt.w, rt.w.cfg
+        biases = any(x is not None for lw in w.layers for x in (lw.bqkv, lw.bo, lw.bgu, lw.bd))
+        norm_bias = any(v[1] is not None for lw in w.layers for v in lw.norms.values()) or w.final_norm[1] is not None
+        return (w.bf16 and w.family == "llama" and rt.comm is None and w.hd == 128 and rt.dec["Mp"] == 16
+                and rt.fast_attn and (w.Hq // w.Hkv) <= 16 and w.rd % 16 == 0 and w.rd <= 128
+                and cfg.sliding_window is None and not biases and not norm_bias and w.d % 8 == 0 and w.d <= 8192
+                and w.Np_gu >= 2 * w.F32)
+
+    def __init__(self, rt):
+        w, cfg, dev = rt.w, rt.w.cfg, rt.w.device
+        ptrs = []
+        for lw in w.layers:
+            ptrs += [lw.wqkv.data_ptr(), lw.wo.data_ptr(), lw.wgu.data_ptr(), lw.wd.data_ptr(),
+                     lw.norms["input_layernorm"][0].data_ptr(), lw.norms["post_attention_layernorm"][0].data_ptr()]
+        self.layer_ptrs = torch.tensor(ptrs, dtype=torch.int64, device=dev)
+        self.sync = torch.zeros(6, dtype=torch.int32, device=dev)
+        a = N.JxStepArgs()
+        a.M, a.L, a.d, a.Hq, a.Hkv, a.hd = rt.B, cfg.num_layers, w.d, w.Hq, w.Hkv, w.hd
+        a.F, a.V, a.vocab = w.F, w.V, cfg.vocab_size
+        a.T, a.rd, a.max_pos = rt.T, w.rd, cfg.max_position_embeddings
+        a.Np_qkv, a.Np_d, a.Np_gu, a.Np_v = w.Np_qkv, w.Np_d, w.Np_gu, w.Np_v
+        a.Kp_d, a.Kp_o, a.Kp_f = w.Kp_d, w.Kp_o, w.Kp_f
+        a.eps, a.scale = cfg.norm_eps, cfg.attn_scale
+        a.layers, a.embed, a.ids = ptr(self.layer_ptrs), ptr(w.embed), ptr(rt.next_ids)
+        a.final_norm, a.lm_head = ptr(w.final_norm[0]), ptr(w.lm_head)
+        d = rt.dec
+        a.h, a.xn, a.qkv, a.attn, a.act = ptr(d["h"]), ptr(d["xn"]), ptr(d["qkv"]), ptr(d["attn"]), ptr(d["act"])
+        a.logits = ptr(rt.logits_buf())
+        a.k_cache, a.v_cache, a.cos, a.sin = ptr(rt.k_cache), ptr(rt.v_cache), ptr(w.cos), ptr(w.sin)
+        a.pos_id = ptr(rt.pos_id)
+        a.ws, a.ws_floats, a.counters = ptr(rt.gemv_ws), rt.gemv_ws.numel(), ptr(rt.gemv_counters)
+        a.attn_ws, a.attn_ws_bytes, a.attn_counters = ptr(rt.attn_ws), rt.attn_ws.numel() * 4, ptr(rt.attn_counters)
+        a.sync, a.status, a.grid = ptr(self.sync), ptr(rt.status), rt.grid
+        self.args = a
+
+    def launch(self, stream):
+        N.check(N.load().jx_decode_step(self.args, stream), "jx_decode_step")
+
+
+# ------------------------------------------------------------------------------------------------
 # Runtime
 # ------------------------------------------------------------------------------------------------
 class DecoderRuntime:
     """Buffers + the prefill / decode call sequences for a batch of ``B`` rows and ``T`` cache slots."""
+
+    # Decode steps of the models it covers run as one persistent kernel (PersistentDecode) plus the
+    # sampling kernel; False keeps the one-launch-per-op path (8 kernels per layer).
+    persistent_decode = True
 
     def __init__(self, weights: ModelWeights, B: int, T: int, comm=None):
         self.w = weights
@@ -325,6 +378,8 @@ class DecoderRuntime:
         # normalisation prologue of the decode projections (jx_epilogue.pn_*): epoch, arrivals, row flags
         self.pn_sync = torch.zeros(2 + 16, dtype=torch.int32, device=dev)
         self._pending_norm = None
+        if self.persistent_decode and PersistentDecode.eligible(self):
+            self.fused_step = PersistentDecode(self)
 
     # -- buffers ------------------------------------------------------------------------------------
     def _alloc_acts(self, M: int, Mp: int) -> dict:
@@ -833,10 +888,14 @@ class DecoderRuntime:
 
     def decode_step(self, greedy: bool, temp: float):
         self._launches = 0
-        acts = self.dec
-        self._input_norm(acts, self.w.layers[0], ids=self.next_ids)
-        self._layers(acts, 1, decode=True)
-        self._head(acts, self.row_map)
+        if self.fused_step is not None:
+            self._launches += 1
+            self.fused_step.launch(self.stream_ptr())
+        else:
+            acts = self.dec
+            self._input_norm(acts, self.w.layers[0], ids=self.next_ids)
+            self._layers(acts, 1, decode=True)
+            self._head(acts, self.row_map)
         self._sample(greedy, temp, update_pos=True)
         self.launches_last_step = self._launches
 
@@ -893,4 +952,6 @@ class DecoderRuntime:
             self.status.zero_()
             self.gemv_counters.zero_()
             self.sample_counters.zero_()
+            if self.fast_attn:
+                self.attn_counters.zero_()
             raise N.NativeError(f"device status {st} ({N.STATUS_NAMES.get(st, st)}) during generation")
