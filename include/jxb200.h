@@ -409,6 +409,12 @@ typedef struct jx_step_args {
   int grid;                  /* CTAs (<= 0: one per SM) */
 } jx_step_args;
 int jx_decode_step(const jx_step_args* args, void* stream);
+/* L2 lookahead of jx_decode_step (process-wide): each CTA prefetches into L2 the weight tiles of its next
+ * `stages` projection stages (32 KB each) beyond those in shared memory, across phase boundaries, so HBM
+ * keeps streaming while the step waits at grid barriers and in the attention phase.  0 (the default)
+ * disables it: on the Llama-3-8B decode step every depth tried made the step slower.  A
+ * cache hint only: results are unchanged.  No counterpart in the reference. */
+int jx_set_decode_step_lookahead(int stages);
 
 /* ---- tensor parallelism over NVLink peer memory ----
  * The reference all-reduces the row-parallel o_proj / down_proj outputs through XLA's GSPMD collectives

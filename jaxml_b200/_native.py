@@ -122,6 +122,7 @@ _PROTOS = {
     "jx_prefill_attention": (I, [ctypes.POINTER(JxPAttnArgs), I, P]),
     "jx_sample": (I, [ctypes.POINTER(JxSampleArgs), I, P]),
     "jx_decode_step": (I, [ctypes.POINTER(JxStepArgs), P]),
+    "jx_set_decode_step_lookahead": (I, [I]),
     "jx_sample_finalize": (I, [ctypes.POINTER(JxSampleArgs), P, I, P]),
     "jx_comm_alloc": (I, [LL, ctypes.POINTER(P)]),
     "jx_comm_free": (I, [P]),

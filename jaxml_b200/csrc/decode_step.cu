@@ -56,13 +56,15 @@ constexpr int kOffTile = kStages * kStageBytes;
 constexpr int kOffQ = kOffTile + kTileBytes;    // [2 x (16 rows x 64 dims)] swizzled q
 constexpr int kOffP = kOffQ + 4096;             // [16][kPLd] bf16 probabilities
 constexpr int kOffRed = kOffP + 16 * kPLd * 2;  // 64 floats of reductions, 16 + 16 softmax statistics
-constexpr int kOffBar = kOffRed + 96 * 4;       // mbarriers
+constexpr int kOffS = kOffRed + 96 * 4;         // bf16 scores of the single-pass attention
+constexpr int kSBufBytes = 28 * 1024;           // n_rep x keys <= 14336
+constexpr int kOffBar = kOffS + kSBufBytes;     // mbarriers
 constexpr int kNumBars = 2 * kStages + 6;
 constexpr int kOffMisc = kOffBar + kNumBars * 8;
 constexpr int kSmem = 1024 + kOffMisc + 256;
 static_assert(kOffBar % 8 == 0, "mbarrier alignment");
 static_assert(kSmem <= 227 * 1024, "shared memory");
-enum Kind { NORM = 0, PROJ = 1, SCORES = 2, PV = 3 };
+enum Kind { NORM = 0, PROJ = 1, SCORES = 2, PV = 3, ATTN = 4 };
 enum Epi { E_QKV = 0, E_RESID = 1, E_GLU = 2, E_LOGITS = 3 };
 }  // namespace ds
 
@@ -94,17 +96,26 @@ struct DsParams {
   int* acnt;       // [M * Hkv] split arrivals
   int* sync;       // [0] arrivals, [1] abort, [2..5] where a wait gave up (site, phase, counter, CTA)
   int* status;
+  int l2_ahead;    // projection weight tiles per CTA prefetched into L2 ahead of the ring
 };
 
 // ---------------------------------------------------------------------------------------------------
 // phases
 // ---------------------------------------------------------------------------------------------------
-__device__ __forceinline__ int ds_kind(const DsParams& p, int q) {
-  if (q >= 8 * p.L) return q == 8 * p.L ? ds::NORM : ds::PROJ;
-  switch (q & 7) {
+// Phases per layer: 8 with the two-phase attention (scores items, a grid barrier, then P.V items), 7 with
+// the single-pass attention.  ds_lj gives the phase's index in the 8-phase numbering: 0 input norm,
+// 1 QKV, 2 attention (scores), 3 P.V, 4 o_proj, 5 post-attention norm, 6 gate/up, 7 down.
+__device__ __forceinline__ int ds_lj(int q, int ppl) {
+  const int j = q % ppl;
+  return (ppl == 8 || j < 3) ? j : j + 1;
+}
+
+__device__ __forceinline__ int ds_kind(const DsParams& p, int q, int ppl) {
+  if (q >= ppl * p.L) return q == ppl * p.L ? ds::NORM : ds::PROJ;
+  switch (ds_lj(q, ppl)) {
     case 0:
     case 5: return ds::NORM;
-    case 2: return ds::SCORES;
+    case 2: return ppl == 8 ? ds::SCORES : ds::ATTN;
     case 3: return ds::PV;
     default: return ds::PROJ;
   }
@@ -117,14 +128,14 @@ struct DsProj {
   int epi;
 };
 
-__device__ __forceinline__ DsProj ds_proj(const DsParams& p, int q) {
+__device__ __forceinline__ DsProj ds_proj(const DsParams& p, int q, int ppl) {
   DsProj r;
-  if (q >= 8 * p.L) {
+  if (q >= ppl * p.L) {
     r.W = p.lm_head, r.X = p.xn, r.Np = p.Np_v, r.Kp = p.Kp_d, r.epi = ds::E_LOGITS;
     return r;
   }
-  const bf16* const* lw = p.layers + (q >> 3) * 6;
-  switch (q & 7) {
+  const bf16* const* lw = p.layers + (q / ppl) * 6;
+  switch (ds_lj(q, ppl)) {
     case 1: r.W = lw[0], r.X = p.xn, r.Np = p.Np_qkv, r.Kp = p.Kp_d, r.epi = ds::E_QKV; break;
     case 4: r.W = lw[1], r.X = p.attn, r.Np = p.Np_d, r.Kp = p.Kp_o, r.epi = ds::E_RESID; break;
     case 6: r.W = lw[2], r.X = p.xn, r.Np = p.Np_gu, r.Kp = p.Kp_d, r.epi = ds::E_GLU; break;
@@ -223,12 +234,27 @@ __device__ __noinline__ bool ds_mbar_wait(uint64_t* bar, uint32_t parity, const 
 // see the slot's full barrier two phases behind (an earlier use of the slot still in flight reads as the
 // phase it waits for).  The producer tags a slot with the stage index only after the slot's previous
 // occupant was released, so once the tag reads g the barrier is at most one phase behind and its parity
-// is exact.
-__device__ __noinline__ bool ds_stage_wait(const volatile int* tag, uint64_t* full, int s, long long g,
-                                           const DsParams& p, int site, int q) {
-  if (tag[s] != (int)g) {
+// is exact.  (The tag is a plain shared-memory store: the producer writes it after its wait on the empty
+// barrier saw the previous occupant released, which the consumer did after seeing that occupant land; the
+// consumer reads it with an acquire load before its wait on the full barrier.)  A consumer whose previous
+// stage in the slot was its own can skip the tag: it saw that use complete.
+// Bounded wait with the common case (already complete) inline: the slow path is a call.
+__device__ __forceinline__ bool ds_wait(uint64_t* bar, uint32_t parity, const DsParams& p, int site, int q,
+                                        long long g) {
+  return mbar_try_wait(bar, parity) || ds_mbar_wait(bar, parity, p, site, q, g);
+}
+
+__device__ __forceinline__ int ld_acquire_cta_shared(const volatile int* p) {
+  int v;
+  asm volatile("ld.acquire.cta.shared::cta.b32 %0, [%1];" : "=r"(v) : "r"(smem_u32((const void*)p)) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ bool ds_stage_wait(const volatile int* tag, uint64_t* full, int s, long long g,
+                                              const DsParams& p, int site, int q) {
+  if (ld_acquire_cta_shared(tag + s) != (int)g) {
     const uint64_t t0 = globaltimer_ns();
-    for (int spin = 0; tag[s] != (int)g; ++spin) {
+    for (int spin = 0; ld_acquire_cta_shared(tag + s) != (int)g; ++spin) {
       if ((spin & 255) == 255) {
         if (ds_aborted(p)) return false;
         if (globaltimer_ns() - t0 > kWaitLimitNs) {
@@ -238,7 +264,7 @@ __device__ __noinline__ bool ds_stage_wait(const volatile int* tag, uint64_t* fu
       }
     }
   }
-  __threadfence_block();
+  if (mbar_try_wait(full + s, (uint32_t)((g / ds::kStages) & 1))) return true;
   return ds_mbar_wait(full + s, (uint32_t)((g / ds::kStages) & 1), p, site, q, g);
 }
 
@@ -298,7 +324,7 @@ __device__ __forceinline__ void st_shared_v4(uint32_t a, const uint4& v) {
 // RMSNorm of row m (norms.py:110-117) into the K128 activations xn: from the residual stream h, or for
 // the first layer from the embedding row of ids[m] (written to h first; ids < 0 read row 0,
 // models/llama.py:188).
-__device__ void ds_norm_row(const DsParams& p, int m, const bf16* w, bool embed, int wtid, float* red) {
+__device__ __noinline__ void ds_norm_row(const DsParams& p, int m, const bf16* w, bool embed, int wtid, float* red) {
   const int d = p.d;
   const bf16* src;
   if (embed) {
@@ -312,17 +338,28 @@ __device__ void ds_norm_row(const DsParams& p, int m, const bf16* w, bool embed,
   } else {
     src = p.h + (long long)m * d;
   }
-  float x[64];
+  // this thread's 8 x 8 elements of the row and of the weights, kept packed between the two passes; every
+  // load is issued before any store (the stores could alias them as far as the compiler knows)
+  uint4 raw[8], wraw[8];
   float ss = 0.f;
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
     const int j = (wtid + k * 128) * 8;
+    raw[k] = wraw[k] = make_uint4(0, 0, 0, 0);
     if (j < d) {
-      const uint4 u = embed ? *reinterpret_cast<const uint4*>(src + j) : __ldcg(reinterpret_cast<const uint4*>(src + j));
-      if (embed) *reinterpret_cast<uint4*>(p.h + (long long)m * d + j) = u;
-      unpack8(u, x + k * 8);
+      raw[k] = embed ? *reinterpret_cast<const uint4*>(src + j) : __ldcg(reinterpret_cast<const uint4*>(src + j));
+      wraw[k] = *reinterpret_cast<const uint4*>(w + j);
+    }
+  }
 #pragma unroll
-      for (int i = 0; i < 8; ++i) ss += x[k * 8 + i] * x[k * 8 + i];
+  for (int k = 0; k < 8; ++k) {
+    const int j = (wtid + k * 128) * 8;
+    if (j < d) {
+      if (embed) *reinterpret_cast<uint4*>(p.h + (long long)m * d + j) = raw[k];
+      float x[8];
+      unpack8(raw[k], x);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss += x[i] * x[i];
     }
   }
   for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
@@ -335,56 +372,90 @@ __device__ void ds_norm_row(const DsParams& p, int m, const bf16* w, bool embed,
   for (int k = 0; k < 8; ++k) {
     const int j = (wtid + k * 128) * 8;
     if (j < d) {
-      float wv[8], y[8];
-      unpack8(*reinterpret_cast<const uint4*>(w + j), wv);
+      float wv[8], x[8], y[8];
+      unpack8(wraw[k], wv);
+      unpack8(raw[k], x);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) y[i] = rnd<bf16>(wv[i] * rnd<bf16>(x[k * 8 + i] / den));
+      for (int i = 0; i < 8; ++i) y[i] = rnd<bf16>(wv[i] * rnd<bf16>(x[i] / den));
       *reinterpret_cast<uint4*>(p.xn + k128_offset(m, j, 16)) = pack8(y);
     }
   }
 }
 
-// Fused projection epilogue of one finished 128-row block (tile[m][j], m < 16 token rows).
-__device__ void ds_epilogue(const DsParams& p, int epi, long long n0, const float* tile, int wtid) {
+// Fused projection epilogue of one finished 128-row block (tile[m][j], m < 16 token rows).  Thread t
+// owns token row t / 8 and 16 consecutive weight rows (t % 8) * 16: its tile values come as four
+// float4 reads, a residual row is read with two 16-byte loads before anything is stored, and results
+// leave as 16-byte stores (scalar only at a ragged edge).
+__device__ __noinline__ void ds_epilogue(const DsParams& p, int epi, long long n0, const float* tile, int wtid) {
   using namespace ds;
-  const int M = p.M;
+  const int m = wtid >> 3, j0 = (wtid & 7) * 16;
+  float v[16];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float4 f = *reinterpret_cast<const float4*>(tile + m * kTileLd + j0 + 4 * i);
+    v[4 * i] = f.x, v[4 * i + 1] = f.y, v[4 * i + 2] = f.z, v[4 * i + 3] = f.w;
+  }
   if (epi == E_GLU) {
-    // packed rows come in groups of 64: 32 gate rows, then the 32 up rows of the same columns
-    for (int idx = wtid; idx < M * 64; idx += 128) {
-      const int m = idx >> 6, jj = idx & 63, grp = jj >> 5, j = jj & 31;
-      const long long col = ((n0 >> 6) + grp) * 32 + j;
-      if (col >= p.F) continue;
-      const float g = rnd<bf16>(tile[m * kTileLd + grp * 64 + j]);
-      const float u = rnd<bf16>(tile[m * kTileLd + grp * 64 + 32 + j]);
-      const float a = rnd<bf16>(silu_f(g));
-      p.act[k128_offset(m, col, 16)] = __float2bfloat16_rn(a * u);
+    // packed rows come in groups of 64: 32 gate rows, then the 32 up rows of the same columns; this
+    // thread's 16 rows are gate (j0 % 64 < 32) or up: pair them through the lane that holds the other half
+    float o[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) o[i] = __shfl_xor_sync(0xffffffffu, v[i], 2);   // lane ^ 2: the row 32 away
+    if (m >= p.M || ((j0 & 63) >> 5) != 0) return;                                // up-row threads are done
+    const int grp = j0 >> 6, jj = j0 & 31;
+    const long long col = ((n0 >> 6) + grp) * 32 + jj;
+    float y[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float g = rnd<bf16>(v[i]), u = rnd<bf16>(o[i]);
+      y[i] = rnd<bf16>(silu_f(g)) * u;
+    }
+    if (col + 16 <= p.F) {
+      *reinterpret_cast<uint4*>(p.act + k128_offset(m, col, 16)) = pack8(y);
+      *reinterpret_cast<uint4*>(p.act + k128_offset(m, col + 8, 16)) = pack8(y + 8);
+    } else {
+      #pragma unroll
+      for (int i = 0; i < 16; ++i)
+        if (col + i < p.F) p.act[k128_offset(m, col + i, 16)] = __float2bfloat16_rn(y[i]);
     }
     return;
   }
+  if (m >= p.M) return;
+  const long long n = n0 + j0;
   if (epi == E_RESID) {
-    for (int idx = wtid; idx < M * 128; idx += 128) {
-      const int m = idx >> 7, j = idx & 127;
-      const long long n = n0 + j;
-      if (n >= p.d) continue;
-      bf16* hp = p.h + (long long)m * p.d + n;
-      const float r = __bfloat162float(__ldcg(hp));
-      *hp = __float2bfloat16_rn(rnd<bf16>(tile[m * kTileLd + j]) + r);
+    bf16* hp = p.h + (long long)m * p.d + n;
+    if (n + 16 <= p.d) {
+      const uint4 r0 = __ldcg(reinterpret_cast<const uint4*>(hp)), r1 = __ldcg(reinterpret_cast<const uint4*>(hp + 8));
+      float r[16], y[16];
+      unpack8(r0, r);
+      unpack8(r1, r + 8);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) y[i] = rnd<bf16>(v[i]) + r[i];
+      *reinterpret_cast<uint4*>(hp) = pack8(y);
+      *reinterpret_cast<uint4*>(hp + 8) = pack8(y + 8);
+    } else {
+      #pragma unroll
+      for (int i = 0; i < 16; ++i)
+        if (n + i < p.d) hp[i] = __float2bfloat16_rn(rnd<bf16>(v[i]) + __bfloat162float(__ldcg(hp + i)));
     }
     return;
   }
   bf16* out = epi == E_QKV ? p.qkv : p.logits;
   const long long ld = epi == E_QKV ? p.nqkv : p.V;
-  for (int idx = wtid; idx < M * 128; idx += 128) {
-    const int m = idx >> 7, j = idx & 127;
-    const long long n = n0 + j;
-    if (n >= ld) continue;
-    out[m * ld + n] = __float2bfloat16_rn(tile[m * kTileLd + j]);
+  bf16* op = out + m * ld + n;
+  if (n + 16 <= ld && (ld & 7) == 0) {
+    *reinterpret_cast<uint4*>(op) = pack8(v);
+    *reinterpret_cast<uint4*>(op + 8) = pack8(v + 8);
+  } else {
+    #pragma unroll
+      for (int i = 0; i < 16; ++i)
+      if (n + i < ld) op[i] = __float2bfloat16_rn(v[i]);
   }
 }
 
 // One attention scores item: keys [t0, t1) of KV head kvh of row b, K tile staged in `kt` (two 64-key
 // halves of two [64 x 64] swizzled blocks).  Returns false if the tile wait failed.
-__device__ bool ds_scores_item(const DsParams& p, int layer, int b, int kvh, int split, int valid, uint8_t* kt,
+__device__ __noinline__ bool ds_scores_item(const DsParams& p, int layer, int b, int kvh, int split, int valid, uint8_t* kt,
                                const volatile int* tag, uint64_t* full, int slot, long long g, uint64_t* empty,
                                uint8_t* qs, float* red, volatile int* flag, int wtid, int w4, int lane) {
   using namespace ds;
@@ -522,7 +593,7 @@ __device__ bool ds_scores_item(const DsParams& p, int layer, int b, int kvh, int
 // One attention P.V item (V tile staged in `vt`): exact probabilities from every split's statistics,
 // P.V, the split partial to the workspace; the last split of a (row, KV head) to arrive sums the
 // partials in split order into the bf16 output (K128 layout).
-__device__ bool ds_pv_item(const DsParams& p, int layer, int b, int kvh, int split, int valid, uint8_t* vt,
+__device__ __noinline__ bool ds_pv_item(const DsParams& p, int layer, int b, int kvh, int split, int valid, uint8_t* vt,
                            const volatile int* tag, uint64_t* full, int slot, long long g, uint64_t* empty,
                            bf16* ptile, float* Ms, float* Ls, volatile int* flag, volatile int* last, int wtid, int w4,
                            int lane) {
@@ -624,11 +695,239 @@ __device__ bool ds_pv_item(const DsParams& p, int layer, int b, int kvh, int spl
   return true;
 }
 
+// Single-pass attention for all keys [0, valid) of KV head kvh of row b: the K tiles, then the V tiles,
+// of this item arrive as stages g0 .. g0 + 2 nk - 1.  The rounded scores of the n_rep query rows stay in
+// shared memory (bf16: they are bf16 values), so the exact normaliser comes from the whole row without a
+// second phase: row max and sum of exp(s - max) over every key, then bf16 probabilities per 128-key tile,
+// P.V accumulated in float32 over all tiles and rounded once into the output (K128 layout).  `cap` is the
+// row stride of the score buffer (keys).  Returns false if a stage wait failed.
+__device__ __noinline__ bool ds_attn_item(const DsParams& p, int layer, int b, int kvh, int valid, int cap, uint8_t* ring,
+                             const volatile int* tag, uint64_t* full, uint64_t* empty, long long g0, uint8_t* qs,
+                             float* red, bf16* sbuf, bf16* ptile, float* Ms, float* Ls, volatile int* flag, int wtid,
+                             int w4, int lane) {
+  using namespace ds;
+  constexpr int WCOLS = kHD / 4, NT = WCOLS / 8;
+  const int nk = (valid + kKeys - 1) / kKeys;
+  const int mi = lane >> 3, r8 = lane & 7;
+  int pos = valid - 1;
+  if (pos >= p.max_pos) {
+    if (wtid == 0) set_status(p.status, JX_ERR_RANGE);
+    pos = 0;
+  }
+  const bf16* qkv_row = p.qkv + (long long)b * p.nqkv;
+  for (int idx = wtid; idx < 16 * 16; idx += 128) {
+    const int r = idx >> 4, cg = idx & 15;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (r < p.n_rep) v = ds_rope8(qkv_row + (long long)(kvh * p.n_rep + r) * kHD, cg * 8, p.rd, p.cos, p.sin, pos);
+    st_shared_v4(ds_swz(smem_u32(qs + (cg >> 3) * 2048), r, cg & 7), v);
+  }
+  float mrow[2] = {-INFINITY, -INFINITY};   // query rows lane / 4 and lane / 4 + 8
+  // ---- scores: q . k over every K tile ----
+  for (int j = 0; j < nk; ++j) {
+    const long long g = g0 + j;
+    const int slot = (int)(g % kStages);
+    uint8_t* kt = ring + slot * kStageBytes;
+    const int t0 = j * kKeys, t1 = min(t0 + kKeys, valid);
+    const bool landed = ds_stage_wait(tag, full, slot, g, p, S_WORK_SCORES, -1);
+    if (!landed) *flag = 1;
+    if (valid - 1 >= t0 && valid - 1 < t1) {
+      // this step's key: rotate, append k and v to the cache, patch k into the staged tile
+      const int kpos = valid - 1, half = (kpos - t0) >> 6, trow = (kpos - t0) & 63;
+      const long long crow =
+          (((long long)layer * p.M + b) * p.T + kpos) * ((long long)p.Hkv * kHD) + (long long)kvh * kHD;
+      const int j0 = wtid * 8;
+      if (j0 < kHD) {
+        const uint4 k8 = ds_rope8(qkv_row + (long long)(p.Hq + kvh) * kHD, j0, p.rd, p.cos, p.sin, pos);
+        const uint4 v8 = __ldcg(reinterpret_cast<const uint4*>(qkv_row + (long long)(p.Hq + p.Hkv + kvh) * kHD + j0));
+        *reinterpret_cast<uint4*>(p.k_cache + crow + j0) = k8;
+        *reinterpret_cast<uint4*>(p.v_cache + crow + j0) = v8;
+        if (landed) st_shared_v4(ds_swz(smem_u32(kt + half * 16384 + (j0 >> 6) * 8192), trow, (j0 & 63) >> 3), k8);
+      }
+    }
+    ds_wsync();
+    const bool ok = *flag == 0;
+    const int n_half = (t1 - t0 + 63) / 64;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      if (i >= n_half || !ok) continue;
+      float acc[2][4] = {};
+      const uint32_t kb = smem_u32(kt + i * 16384);
+#pragma unroll
+      for (int ks = 0; ks < kHD / 16; ++ks) {
+        uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
+        {
+          const int row = (mi & 1) * 8 + r8, ch = ks * 2 + (mi >> 1);
+          ldsm_x4(ds_swz(smem_u32(qs + (ch >> 3) * 2048), row, ch & 7), a0, a1, a2, a3);
+        }
+        {
+          const int row = w4 * 16 + (mi >> 1) * 8 + r8, ch = ks * 2 + (mi & 1);
+          ldsm_x4(ds_swz(kb + (ch >> 3) * 8192, row, ch & 7), b0, b1, b2, b3);
+        }
+        mma_bf16(acc[0], a0, a1, a2, a3, b0, b1);
+        mma_bf16(acc[1], a0, a1, a2, a3, b2, b3);
+      }
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int row = (lane >> 2) + (e >> 1) * 8;
+          const int t = t0 + i * 64 + w4 * 16 + nt * 8 + (lane & 3) * 2 + (e & 1);
+          if (t < t1 && row < p.n_rep) {
+            const float v = rnd<bf16>(rnd<bf16>(acc[nt][e]) * p.scale_bf16);
+            sbuf[row * cap + t] = __float2bfloat16_rn(v);
+            mrow[e >> 1] = fmaxf(mrow[e >> 1], v);
+          }
+        }
+    }
+    // every warp is done with the staged tile: hand the stage back to the producer
+    ds_wsync();
+    if (wtid == 0) mbar_arrive(&empty[slot]);
+    if (!ok) return false;
+  }
+  // ---- exact softmax statistics over the whole row ----
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    mrow[h] = fmaxf(mrow[h], __shfl_xor_sync(0xffffffffu, mrow[h], 1));
+    mrow[h] = fmaxf(mrow[h], __shfl_xor_sync(0xffffffffu, mrow[h], 2));
+  }
+  if ((lane & 3) == 0) {
+    red[w4 * 16 + (lane >> 2)] = mrow[0];
+    red[w4 * 16 + (lane >> 2) + 8] = mrow[1];
+  }
+  ds_wsync();
+  if (wtid < 16) Ms[wtid] = fmaxf(fmaxf(red[wtid], red[16 + wtid]), fmaxf(red[32 + wtid], red[48 + wtid]));
+  ds_wsync();
+  // sum of exp(s - max): warp w4 takes rows w4, w4 + 4, ... (lanes stride over the keys, in order)
+  for (int row = w4; row < p.n_rep; row += 4) {
+    float l = 0.f;
+    const float mx = Ms[row];
+    for (int t = lane; t < valid; t += 32) l += expf(__bfloat162float(sbuf[row * cap + t]) - mx);
+    for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+    if (lane == 0) Ls[row] = l;
+  }
+  ds_wsync();
+  // ---- P.V over every V tile ----
+  float acc[NT][4] = {};
+  for (int j = 0; j < nk; ++j) {
+    const long long g = g0 + nk + j;
+    const int slot = (int)(g % kStages);
+    uint8_t* vt = ring + slot * kStageBytes;
+    const int t0 = j * kKeys, t1 = min(t0 + kKeys, valid);
+    for (int idx = wtid; idx < 16 * kKeys; idx += 128) {
+      const int row = idx / kKeys, k = idx % kKeys, t = t0 + k;
+      float pv = 0.f;
+      if (row < p.n_rep && t < t1) pv = rnd<bf16>(expf(__bfloat162float(sbuf[row * cap + t]) - Ms[row]) / Ls[row]);
+      ptile[row * kPLd + k] = __float2bfloat16_rn(pv);
+    }
+    const bool landed = ds_stage_wait(tag, full, slot, g, p, S_WORK_PV, -1);
+    if (!landed) *flag = 1;
+    if (landed && valid - 1 >= t0 && valid - 1 < t1) {
+      // this step's value (appended above, possibly after the tile was staged)
+      const int kpos = valid - 1, half = (kpos - t0) >> 6, trow = (kpos - t0) & 63;
+      const int j0 = wtid * 8;
+      if (j0 < kHD)
+        st_shared_v4(ds_swz(smem_u32(vt + half * 16384 + (j0 >> 6) * 8192), trow, (j0 & 63) >> 3),
+                     __ldcg(reinterpret_cast<const uint4*>(qkv_row + (long long)(p.Hq + p.Hkv + kvh) * kHD + j0)));
+    }
+    ds_wsync();
+    const bool ok = *flag == 0;
+    const int n_half = (t1 - t0 + 63) / 64;
+    for (int i = 0; i < n_half && ok; ++i) {
+      const uint32_t vb = smem_u32(vt + i * 16384);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        uint32_t a0, a1, a2, a3;
+        {
+          const int row = (mi & 1) * 8 + r8, col = i * 64 + kk * 16 + (mi >> 1) * 8;
+          ldsm_x4(smem_u32(ptile + row * kPLd + col), a0, a1, a2, a3);
+        }
+#pragma unroll
+        for (int n16 = 0; n16 < NT / 2; ++n16) {
+          uint32_t b0, b1, b2, b3;
+          const int row = kk * 16 + (mi & 1) * 8 + r8;
+          const int ch = (w4 * WCOLS) / 8 + n16 * 2 + (mi >> 1);
+          ldsm_x4_t(ds_swz(vb + (ch >> 3) * 8192, row, ch & 7), b0, b1, b2, b3);
+          mma_bf16(acc[n16 * 2], a0, a1, a2, a3, b0, b1);
+          mma_bf16(acc[n16 * 2 + 1], a0, a1, a2, a3, b2, b3);
+        }
+      }
+    }
+    ds_wsync();
+    if (wtid == 0) mbar_arrive(&empty[slot]);
+    if (!ok) return false;
+  }
+  const int r_lo = lane >> 2, r_hi = r_lo + 8;
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int row = (e >> 1) ? r_hi : r_lo;
+      const int col = w4 * WCOLS + nt * 8 + (lane & 3) * 2 + (e & 1);
+      if (row < p.n_rep)
+        p.attn[k128_offset(b, (long long)(kvh * p.n_rep + row) * kHD + col, 16)] = __float2bfloat16_rn(acc[nt][e]);
+    }
+  ds_wsync();
+  return true;
+}
+
+// Split-K fix-up of block nb by its last arriver: the partial tiles of CTAs c_first .. c_last summed in CTA
+// order into the staging tile (own = this CTA when its own partial is still in the tile, else -1).  Each
+// thread owns 4 float4 of the [16 x 128] tile; the loads of up to 8 contributors are issued before any is
+// added, so the L2 round trips of a block's contributors overlap.
+__device__ __noinline__ void ds_splitk_sum(const DsParams& p, long long nb, int c_first, int c_last, int own,
+                                           long long total, int kc, int Gp, float* tile, int wtid) {
+  using namespace ds;
+  float4 acc4[4];
+  for (int cc0 = c_first; cc0 <= c_last; cc0 += 8) {
+    float4 vv[8][4];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int cc = cc0 + u;
+      if (cc > c_last) break;
+      if (cc == own) {
+#pragma unroll
+        for (int qq = 0; qq < 4; ++qq) {
+          const int e0 = (wtid + qq * 128) * 4;
+          vv[u][qq] = *reinterpret_cast<const float4*>(tile + (e0 >> 7) * kTileLd + (e0 & 127));
+        }
+      } else {
+        const long long nbf = ds_begin(total, Gp, cc) / kc;
+        const int slot = cc * 2 + (nb == nbf ? 0 : 1);
+        const float4* src = reinterpret_cast<const float4*>(p.ws + (long long)slot * 16 * 128);
+#pragma unroll
+        for (int qq = 0; qq < 4; ++qq) vv[u][qq] = __ldcg(src + wtid + qq * 128);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      if (cc0 + u > c_last) break;
+#pragma unroll
+      for (int qq = 0; qq < 4; ++qq) {
+        if (cc0 + u == c_first) {
+          acc4[qq] = vv[u][qq];
+        } else {
+          acc4[qq].x += vv[u][qq].x;
+          acc4[qq].y += vv[u][qq].y;
+          acc4[qq].z += vv[u][qq].z;
+          acc4[qq].w += vv[u][qq].w;
+        }
+      }
+    }
+  }
+  ds_wsync();   // every thread's reads of its own tile values are done
+#pragma unroll
+  for (int qq = 0; qq < 4; ++qq) {
+    const int e0 = (wtid + qq * 128) * 4;
+    *reinterpret_cast<float4*>(tile + (e0 >> 7) * kTileLd + (e0 & 127)) = acc4[qq];
+  }
+}
+
 // ---------------------------------------------------------------------------------------------------
 // the kernel
 // ---------------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(ds::kThreads, 1)
-    decode_step_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, DsParams p) {
+    decode_step_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
+                       const __grid_constant__ DsParams p) {
   using namespace ds;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -639,6 +938,7 @@ __global__ void __launch_bounds__(ds::kThreads, 1)
   float* red = reinterpret_cast<float*>(smem + kOffRed);
   float* Ms = red + 64;
   float* Ls = Ms + 16;
+  bf16* sbuf = reinterpret_cast<bf16*>(smem + kOffS);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + kOffBar);
   uint64_t* empty = full + kStages;
   uint64_t* accf = empty + kStages;   // [2]
@@ -646,13 +946,13 @@ __global__ void __launch_bounds__(ds::kThreads, 1)
   uint64_t* done = acce + 2;          // workers finished with TMEM
   uint64_t* mmadone = done + 1;       // every MMA issued has completed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kOffMisc);
-  volatile int* sh = reinterpret_cast<volatile int*>(smem + kOffMisc + 16);   // [0] S, [1] flag, [2] last, [3] wait ok
+  // [0] S, [1] flag, [2] last, [3] wait ok, [4] phases per layer
+  volatile int* sh = reinterpret_cast<volatile int*>(smem + kOffMisc + 16);
   volatile int* valid = sh + 8;                                                  // [16]
   volatile int* tag = sh + 24;                                                   // [kStages] stage in each slot
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = gridDim.x, c = blockIdx.x;
-  const int NP = 8 * p.L + 2;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -677,6 +977,10 @@ __global__ void __launch_bounds__(ds::kThreads, 1)
     }
     sh[0] = S;
     sh[1] = 0;
+    // single-pass attention when one item per (row, KV head) keeps at least half the CTAs busy and the
+    // rounded scores of a row fit the shared buffer; otherwise split items over 128-key ranges
+    const bool single = 2 * p.M * p.Hkv >= (int)gridDim.x && p.n_rep * S * kKeys * 2 <= kSBufBytes;
+    sh[4] = single ? 7 : 8;
     for (int s = 0; s < kStages; ++s) tag[s] = -1;
     fence_barrier_init();
   }
@@ -689,7 +993,10 @@ __global__ void __launch_bounds__(ds::kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const int S = sh[0];
-  const int n_items = p.M * p.Hkv * S;
+  const int ppl = sh[4];
+  const int NP = ppl * p.L + 2;
+  const int n_items = p.M * p.Hkv * S;        // split items (two-phase attention)
+  const int n_pairs = p.M * p.Hkv;            // single-pass items
 
   if (warp == 0) {
     // ------------------------------ TMA producer ------------------------------
@@ -697,12 +1004,45 @@ __global__ void __launch_bounds__(ds::kThreads, 1)
       prefetch_tmap(&kmap);
       prefetch_tmap(&vmap);
       const uint64_t pol = l2_policy_evict_first();   // weights and K/V are read once per step
+      const uint64_t pol_keep = l2_policy_evict_last();
       long long g = 0;                                 // stages issued
       bool dead = false;
+      // L2 lookahead: before every wait, the weight tiles of this CTA's next l2_ahead projection stages
+      // (across phase boundaries) are prefetched into L2, so HBM keeps streaming through phase tails,
+      // grid barriers and the attention phase, and those stages then load from L2.
+      long long proj_issued = 0;                       // projection stages issued to the ring
+      long long pf_n = 0, pf_it = 0, pf_it1 = 0;       // cursor: stages passed, range in its phase
+      int pf_q = 0, pf_kc = 1;
+      long long pf_np = 0;
+      const bf16* pf_w = nullptr;
+      auto lookahead = [&]() {
+        while (pf_n < proj_issued + p.l2_ahead) {
+          if (pf_it >= pf_it1) {   // the cursor moves on to the next projection phase this CTA has a share of
+            bool found = false;
+            while (!found && pf_q < NP) {
+              const int qq = pf_q++;
+              if (ds_kind(p, qq, ppl) != PROJ) continue;
+              const DsProj pp = ds_proj(p, qq, ppl);
+              pf_kc = (int)(pp.Kp >> 7);
+              ds_range((pp.Np >> 7) * pf_kc, G, c, pf_it, pf_it1);
+              pf_w = pp.W;
+              pf_np = pp.Np;
+              found = pf_it < pf_it1;
+            }
+            if (!found) return;
+          }
+          if (pf_n >= proj_issued) {
+            const long long nb = pf_it / pf_kc, kk = pf_it - nb * pf_kc;
+            bulk_prefetch_l2(pf_w + ((kk * (pf_np >> 3) + nb * 16) << 10), kWBytes, pol_keep);
+          }
+          ++pf_it;
+          ++pf_n;
+        }
+      };
       for (int q = 0; q < NP && !dead; ++q) {
-        const int kind = ds_kind(p, q);
+        const int kind = ds_kind(p, q, ppl);
         if (kind == PROJ) {
-          const DsProj pr = ds_proj(p, q);
+          const DsProj pr = ds_proj(p, q, ppl);
           const int kc = (int)(pr.Kp >> 7);
           const long long total = (pr.Np >> 7) * kc;
           long long it0, it1;
@@ -720,15 +1060,17 @@ __global__ void __launch_bounds__(ds::kThreads, 1)
           for (; nw < pre; ++nw) {
             const long long gg = g + nw;
             const int s = (int)(gg % kStages);
-            if (gg >= kStages && !ds_mbar_wait(&empty[s], (uint32_t)(((gg / kStages) - 1) & 1), p, S_PROD_EMPTY_PRE, q, gg)) {
+            lookahead();
+            if (gg >= kStages && !ds_wait(&empty[s], (uint32_t)(((gg / kStages) - 1) & 1), p, S_PROD_EMPTY_PRE, q, gg)) {
               dead = true;
               break;
             }
-            __threadfence_block();
             tag[s] = (int)gg;
             mbar_arrive_expect_tx(&full[s], kStageBytes);
             bulk_g2s_hint(ring + s * kStageBytes, wsrc(it0 + nw), kWBytes, &full[s], pol);
+            ++proj_issued;
           }
+          lookahead();
           // the activations exist once every CTA has finished the phases before this one
           const bool ok = !dead && ds_grid_wait(p, q * G, S_PROD_GRID, q);
           if (ok) {
@@ -748,30 +1090,56 @@ __global__ void __launch_bounds__(ds::kThreads, 1)
           for (int i = pre; i < n; ++i) {
             const long long gg = g + i;
             const int s = (int)(gg % kStages);
-            if (!ds_mbar_wait(&empty[s], (uint32_t)(((gg / kStages) - 1) & 1), p, S_PROD_EMPTY, q, gg)) {
+            lookahead();
+            if (!ds_wait(&empty[s], (uint32_t)(((gg / kStages) - 1) & 1), p, S_PROD_EMPTY, q, gg)) {
               dead = true;
               g += i;
               break;
             }
-            __threadfence_block();
             tag[s] = (int)gg;
             mbar_arrive_expect_tx(&full[s], kStageBytes);
             bulk_g2s_hint(ring + s * kStageBytes, wsrc(it0 + i), kWBytes, &full[s], pol);
             bulk_g2s(ring + s * kStageBytes + kWBytes, xsrc(it0 + i), kXBytes, &full[s]);
+            ++proj_issued;
           }
           if (!dead) g += n;
+        } else if (kind == ATTN) {
+          const long long row0 = (long long)(q / ppl) * p.M * p.T;
+          for (int i = c; i < n_pairs && !dead; i += G) {
+            const int b = i / p.Hkv, kvh = i % p.Hkv;
+            const int nk = (valid[b] + kKeys - 1) / kKeys;
+            for (int j = 0; j < 2 * nk; ++j) {
+              const int s = (int)(g % kStages);
+              lookahead();
+              if (g >= kStages && !ds_wait(&empty[s], (uint32_t)(((g / kStages) - 1) & 1), p, S_PROD_EMPTY_ATTN, q, g)) {
+                dead = true;
+                break;
+              }
+              tag[s] = (int)g;
+              mbar_arrive_expect_tx(&full[s], kWBytes);
+              const CUtensorMap* map = j < nk ? &kmap : &vmap;
+              const int y0 = (int)(row0 + (long long)b * p.T + (j < nk ? j : j - nk) * kKeys);
+#pragma unroll
+              for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+                for (int cb = 0; cb < 2; ++cb)
+                  tma_load_2d(ring + s * kStageBytes + hh * 16384 + cb * 8192, map, kvh * kHD + cb * 64, y0 + hh * 64,
+                              &full[s]);
+              ++g;
+            }
+          }
         } else if (kind == SCORES || kind == PV) {
           const CUtensorMap* map = kind == SCORES ? &kmap : &vmap;
-          const long long row0 = (long long)(q >> 3) * p.M * p.T;
+          const long long row0 = (long long)(q / ppl) * p.M * p.T;
           for (int i = c; i < n_items; i += G) {
             int b, kvh, split;
             if (!ds_item(i, S, p.Hkv, valid, b, kvh, split)) continue;
             const int s = (int)(g % kStages);
-            if (g >= kStages && !ds_mbar_wait(&empty[s], (uint32_t)(((g / kStages) - 1) & 1), p, S_PROD_EMPTY_ATTN, q, g)) {
+            lookahead();
+            if (g >= kStages && !ds_wait(&empty[s], (uint32_t)(((g / kStages) - 1) & 1), p, S_PROD_EMPTY_ATTN, q, g)) {
               dead = true;
               break;
             }
-            __threadfence_block();
             tag[s] = (int)g;
             mbar_arrive_expect_tx(&full[s], kWBytes);
             const int y0 = (int)(row0 + (long long)b * p.T + split * kKeys);
@@ -795,12 +1163,13 @@ __global__ void __launch_bounds__(ds::kThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc = umma_idesc_bf16_f32(128, 16);
       long long g = 0;
+      long long g_foreign_end = 0;   // first stage after the last attention stages (which the workers consume)
       int blk = -1;
       bool dead = false;
       for (int q = 0; q < NP && !dead; ++q) {
-        const int kind = ds_kind(p, q);
+        const int kind = ds_kind(p, q, ppl);
         if (kind == PROJ) {
-          const DsProj pr = ds_proj(p, q);
+          const DsProj pr = ds_proj(p, q, ppl);
           const int kc = (int)(pr.Kp >> 7);
           const long long total = (pr.Np >> 7) * kc;
           long long it0, it1;
@@ -814,7 +1183,7 @@ __global__ void __launch_bounds__(ds::kThreads, 1)
               cur_nb = nb;
               ++blk;
               const int buf = blk & 1;
-              if (blk >= 2 && !ds_mbar_wait(&acce[buf], (uint32_t)(((blk >> 1) - 1) & 1), p, S_MMA_ACCE, q, blk)) {
+              if (blk >= 2 && !ds_wait(&acce[buf], (uint32_t)(((blk >> 1) - 1) & 1), p, S_MMA_ACCE, q, blk)) {
                 dead = true;
                 break;
               }
@@ -823,7 +1192,10 @@ __global__ void __launch_bounds__(ds::kThreads, 1)
               first = true;
             }
             const int s = (int)(g % kStages);
-            if (!ds_stage_wait(tag, full, s, g, p, S_MMA_FULL, q)) {
+            const bool ok_full = (g - kStages >= g_foreign_end)
+                                     ? ds_wait(&full[s], (uint32_t)((g / kStages) & 1), p, S_MMA_FULL, q, g)
+                                     : ds_stage_wait(tag, full, s, g, p, S_MMA_FULL, q);
+            if (!ok_full) {
               dead = true;
               break;
             }
@@ -840,11 +1212,15 @@ __global__ void __launch_bounds__(ds::kThreads, 1)
             umma_commit(&empty[s]);
             if (kk == kc - 1 || it == it1 - 1) umma_commit(&accf[blk & 1]);
           }
+        } else if (kind == ATTN) {
+          for (int i = c; i < n_pairs; i += G) g += 2 * ((valid[i / p.Hkv] + kKeys - 1) / kKeys);
+          g_foreign_end = g;
         } else if (kind == SCORES || kind == PV) {
           for (int i = c; i < n_items; i += G) {
             int b, kvh, split;
             if (ds_item(i, S, p.Hkv, valid, b, kvh, split)) ++g;
           }
+          g_foreign_end = g;
         }
       }
       // every MMA issued has completed before TMEM is freed
@@ -860,7 +1236,7 @@ __global__ void __launch_bounds__(ds::kThreads, 1)
     int blk = -1;
     bool dead = false;
     for (int q = 0; q < NP && !dead; ++q) {
-      const int kind = ds_kind(p, q);
+      const int kind = ds_kind(p, q, ppl);
       // Every phase starts once every CTA has arrived for the phases before it (count >= q * G).  No CTA
       // arrives for phase q before that, so the count reaches q * G only when each CTA has arrived once
       // for each earlier phase.  (A projection's epilogue needs its activations anyway; the wait matters
@@ -872,7 +1248,7 @@ __global__ void __launch_bounds__(ds::kThreads, 1)
         break;
       }
       if (kind == PROJ) {
-        const DsProj pr = ds_proj(p, q);
+        const DsProj pr = ds_proj(p, q, ppl);
         const int kc = (int)(pr.Kp >> 7);
         const long long total = (pr.Np >> 7) * kc;
         long long it0, it1;
@@ -890,7 +1266,7 @@ __global__ void __launch_bounds__(ds::kThreads, 1)
           const bool block_end = (kk == kc - 1) || (it == it1 - 1);
           if (!block_end) continue;
           const int buf = blk & 1;
-          bool ok = ds_mbar_wait(&accf[buf], (uint32_t)((blk >> 1) & 1), p, S_WORK_ACCF, q, blk);
+          bool ok = ds_wait(&accf[buf], (uint32_t)((blk >> 1) & 1), p, S_WORK_ACCF, q, blk);
           ok = __all_sync(0xffffffffu, ok);   // tcgen05.ld is warp-wide
           tc_fence_after();
           if (ok) {
@@ -928,8 +1304,12 @@ __global__ void __launch_bounds__(ds::kThreads, 1)
             if (fast) {
               do_epi = true;
             } else {
-              float* my = p.ws + (long long)slot_of(c) * 16 * 128;
-              for (int idx = wtid; idx < 16 * 128; idx += 128) my[idx] = tile[(idx >> 7) * kTileLd + (idx & 127)];
+              float4* my = reinterpret_cast<float4*>(p.ws + (long long)slot_of(c) * 16 * 128);
+#pragma unroll
+              for (int qq = 0; qq < 4; ++qq) {
+                const int e0 = (wtid + qq * 128) * 4;
+                my[wtid + qq * 128] = *reinterpret_cast<const float4*>(tile + (e0 >> 7) * kTileLd + (e0 & 127));
+              }
               __threadfence();
               ds_wsync();
               if (wtid == 0) {
@@ -941,47 +1321,7 @@ __global__ void __launch_bounds__(ds::kThreads, 1)
             }
             if (do_epi) {
               __threadfence();
-              // every contribution (this CTA's too) summed in CTA order; each thread owns 4 float4
-              float4 acc4[4];
-              for (int cc0 = c_first; cc0 <= c_last; cc0 += 4) {
-                float4 vv[4][4];
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                  if (cc0 + u > c_last) break;
-                  if (fast && cc0 + u == c) {
-#pragma unroll
-                    for (int qq = 0; qq < 4; ++qq) {
-                      const int e0 = (wtid + qq * 128) * 4;
-                      vv[u][qq] = *reinterpret_cast<const float4*>(tile + (e0 >> 7) * kTileLd + (e0 & 127));
-                    }
-                  } else {
-                    const float4* src = reinterpret_cast<const float4*>(p.ws + (long long)slot_of(cc0 + u) * 16 * 128);
-#pragma unroll
-                    for (int qq = 0; qq < 4; ++qq) vv[u][qq] = __ldcg(src + wtid + qq * 128);
-                  }
-                }
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                  if (cc0 + u > c_last) break;
-#pragma unroll
-                  for (int qq = 0; qq < 4; ++qq) {
-                    if (cc0 + u == c_first) {
-                      acc4[qq] = vv[u][qq];
-                    } else {
-                      acc4[qq].x += vv[u][qq].x;
-                      acc4[qq].y += vv[u][qq].y;
-                      acc4[qq].z += vv[u][qq].z;
-                      acc4[qq].w += vv[u][qq].w;
-                    }
-                  }
-                }
-              }
-              ds_wsync();   // every thread's reads of its own tile values are done
-#pragma unroll
-              for (int qq = 0; qq < 4; ++qq) {
-                const int e0 = (wtid + qq * 128) * 4;
-                *reinterpret_cast<float4*>(tile + (e0 >> 7) * kTileLd + (e0 & 127)) = acc4[qq];
-              }
+              ds_splitk_sum(p, nb, c_first, c_last, fast ? c : -1, total, kc, Gp, tile, wtid);
               if (wtid == 0) p.counters[nb] = 0;
               ds_wsync();
             }
@@ -992,10 +1332,23 @@ __global__ void __launch_bounds__(ds::kThreads, 1)
       } else {
         if (kind == NORM) {
           if (c < p.M) {
-            const bool fin = q == 8 * p.L;
-            const bf16* w = fin ? p.final_norm : p.layers[(q >> 3) * 6 + ((q & 7) == 0 ? 4 : 5)];
+            const bool fin = q == ppl * p.L;
+            const bf16* w = fin ? p.final_norm : p.layers[(q / ppl) * 6 + (ds_lj(q, ppl) == 0 ? 4 : 5)];
             ds_norm_row(p, c, w, q == 0, wtid, red);
           }
+        } else if (kind == ATTN) {
+          for (int i = c; i < n_pairs; i += G) {
+            const int b = i / p.Hkv, kvh = i % p.Hkv;
+            const int nk = (valid[b] + kKeys - 1) / kKeys;
+            const bool ok = ds_attn_item(p, q / ppl, b, kvh, valid[b], S * kKeys, ring, tag, full, empty, g, qs, red,
+                                         sbuf, ptile, Ms, Ls, &sh[1], wtid, w4, lane);
+            g += 2 * nk;
+            if (!ok) {
+              dead = true;
+              break;
+            }
+          }
+          if (dead) break;
         } else {
           for (int i = c; i < n_items; i += G) {
             int b, kvh, split;
@@ -1003,9 +1356,9 @@ __global__ void __launch_bounds__(ds::kThreads, 1)
             const int s = (int)(g % kStages);
             const long long gi = g++;
             const bool ok = kind == SCORES
-                                ? ds_scores_item(p, q >> 3, b, kvh, split, valid[b], ring + s * kStageBytes, tag, full,
+                                ? ds_scores_item(p, q / ppl, b, kvh, split, valid[b], ring + s * kStageBytes, tag, full,
                                                  s, gi, &empty[s], qs, red, &sh[1], wtid, w4, lane)
-                                : ds_pv_item(p, q >> 3, b, kvh, split, valid[b], ring + s * kStageBytes, tag, full, s,
+                                : ds_pv_item(p, q / ppl, b, kvh, split, valid[b], ring + s * kStageBytes, tag, full, s,
                                              gi, &empty[s], ptile, Ms, Ls, &sh[1], &sh[2], wtid, w4, lane);
             if (!ok) {
               dead = true;
@@ -1036,6 +1389,13 @@ __global__ void __launch_bounds__(ds::kThreads, 1)
 }  // namespace jxb
 
 using namespace jxb;
+
+static int g_l2_ahead = 0;
+extern "C" int jx_set_decode_step_lookahead(int stages) {
+  if (stages < 0 || stages > 64) return fail(JX_ERR_ARG, "jx_set_decode_step_lookahead: stages must be in [0, 64]");
+  g_l2_ahead = stages;
+  return JX_OK;
+}
 
 extern "C" int jx_decode_step(const jx_step_args* a, void* stream) {
   using namespace ds;
@@ -1112,6 +1472,7 @@ extern "C" int jx_decode_step(const jx_step_args* a, void* stream) {
   p.opart = p.stats + (long long)a->M * a->Hq * n_splits * 2;
   p.acnt = a->attn_counters;
   p.sync = a->sync, p.status = a->status;
+  p.l2_ahead = g_l2_ahead;
 
   cudaStream_t s = (cudaStream_t)stream;
   if (cudaMemsetAsync(a->sync, 0, 6 * sizeof(int), s) != cudaSuccess) return note_cuda("jx_decode_step: clearing sync");

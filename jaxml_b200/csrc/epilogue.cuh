@@ -6,6 +6,8 @@
 // (nn/linear.py:161-182 for the bias, models/llama.py:133-137 for the residual adds,
 // models/llama.py:82-88 / gemma3.py:80-86 / gpt_neox.py:75-80 for the activations).
 #pragma once
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace jxb {
@@ -244,6 +246,76 @@ __device__ __forceinline__ void run_epilogue(const EpiParams& e, long long m0, i
         out[row * e.ldo + n] += v;
     }
     return;
+  }
+  if constexpr (std::is_same<T, bf16>::value) {
+    // bfloat16 STORE / RESID / RESID2 in chunks of 8 columns: every residual load of a thread's (up to 4)
+    // chunks is issued before any store.  The output may alias the residual, so a per-element loop would
+    // wait for one L2 round trip per element.
+    const bool al = !((reinterpret_cast<uintptr_t>(e.out) | reinterpret_cast<uintptr_t>(e.res) |
+                       reinterpret_cast<uintptr_t>(e.res2)) & 15);
+    const bool kind_ok = e.kind == JX_EPI_STORE || e.kind == JX_EPI_RESID || e.kind == JX_EPI_RESID2;
+    if (kind_ok && al && cols % 8 == 0 && n0 % 8 == 0 && e.ldo % 8 == 0 && e.ldr % 8 == 0 && e.ldr2 % 8 == 0) {
+      const T* res = reinterpret_cast<const T*>(e.res);
+      const T* res2 = reinterpret_cast<const T*>(e.res2);
+      T* out = reinterpret_cast<T*>(e.out);
+      const int cpr = cols >> 3, nchunks = rows * cpr;
+      for (int base = tid; base < nchunks; base += 4 * nthreads) {
+        uint4 r[4], r2[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int idx = base + u * nthreads;
+          r[u] = r2[u] = make_uint4(0, 0, 0, 0);
+          if (idx >= nchunks) continue;
+          const int m = idx / cpr, j = (idx - m * cpr) * 8;
+          const long long row = m0 + m, n = n0 + j;
+          if (row >= e.M || n + 8 > e.N) continue;
+          if (e.kind != JX_EPI_STORE) r[u] = *reinterpret_cast<const uint4*>(res + row * e.ldr + n);
+          if (e.kind == JX_EPI_RESID2) r2[u] = *reinterpret_cast<const uint4*>(res2 + row * e.ldr2 + n);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int idx = base + u * nthreads;
+          if (idx >= nchunks) continue;
+          const int m = idx / cpr, j = (idx - m * cpr) * 8;
+          const long long row = m0 + m, n = n0 + j;
+          if (row >= e.M || n >= e.N) continue;
+          if (n + 8 > e.N) {   // ragged edge of the output: element by element
+            for (int i = 0; i < 8 && n + i < e.N; ++i) {
+              float v = rnd<T>(tile(m, j + i));
+              if (e.bias) v = rnd<T>(v + bias_at<T>(e, n + i));
+              if (e.kind == JX_EPI_RESID) v = v + to_f(res[row * e.ldr + n + i]);
+              if (e.kind == JX_EPI_RESID2) v = rnd<T>(v + to_f(res2[row * e.ldr2 + n + i])) + to_f(res[row * e.ldr + n + i]);
+              out[row * e.ldo + n + i] = from_f<T>(v);
+            }
+            continue;
+          }
+          const __nv_bfloat162* rh = reinterpret_cast<const __nv_bfloat162*>(&r[u]);
+          const __nv_bfloat162* rh2 = reinterpret_cast<const __nv_bfloat162*>(&r2[u]);
+          float y[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            float v = rnd<T>(tile(m, j + i));
+            if (e.bias) v = rnd<T>(v + bias_at<T>(e, n + i));
+            const float2 rr = __bfloat1622float2(rh[i >> 1]);
+            const float rv = (i & 1) ? rr.y : rr.x;
+            if (e.kind == JX_EPI_RESID) {
+              v = v + rv;
+            } else if (e.kind == JX_EPI_RESID2) {
+              const float2 qq = __bfloat1622float2(rh2[i >> 1]);
+              v = rnd<T>(v + ((i & 1) ? qq.y : qq.x)) + rv;
+            }
+            y[i] = v;
+          }
+          uint4 o;
+          o.x = pack_bf16x2(y[0], y[1]);
+          o.y = pack_bf16x2(y[2], y[3]);
+          o.z = pack_bf16x2(y[4], y[5]);
+          o.w = pack_bf16x2(y[6], y[7]);
+          *reinterpret_cast<uint4*>(out + row * e.ldo + n) = o;
+        }
+      }
+      return;
+    }
   }
   for (int idx = tid; idx < rows * cols; idx += nthreads) {
     const int m = idx / cols, j = idx - m * cols;

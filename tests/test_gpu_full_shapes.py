@@ -2,8 +2,9 @@
 
 * Llama-3-8B shape (d 4096, 32 query / 8 KV heads x 128, SwiGLU FFN 14336, vocabulary 128256, RoPE
   theta 5e5), bfloat16, with 2 of its 32 layers so the CPU oracle stays fast: batch 16, a 512-token
-  prompt, then decode steps replayed from the captured CUDA graph (the tcgen05 projections for gate/up
-  and the LM head, the RoPE-fused split attention, on-device sampling).
+  prompt, then decode steps replayed from the captured CUDA graph, through both decode paths: one launch
+  per op (the tcgen05 projections for gate/up and the LM head, the RoPE-fused split attention) and the
+  persistent decode-step kernel; on-device sampling.
 
   The bf16 tolerance is set by the reference's own arithmetic.  With every op rounded to bf16 and logits
   of magnitude 4-8 (one bf16 ulp = 0.03), moving only the summation order of the projections already
@@ -105,13 +106,22 @@ def _check_cache(rt, two, B):
             _check_bf16(got[:B], want, want64, f"cache layer {li}", floor_max=one_ulp, floor_mean=1e-4, mean_factor=2.0)
 
 
-def test_llama8b_shape_graph_replay_logits_match_oracle(l8):
+@pytest.mark.parametrize("path", ["per-op", "persistent"])
+def test_llama8b_shape_graph_replay_logits_match_oracle(l8, path):
+    from jaxml_b200.runtime import DecoderRuntime
+
     cfg, params = l8
     B, P, n_steps = 16, 512, 8
     T = (P // 256 + 1) * 256
     g = torch.Generator().manual_seed(0)
     ids = torch.randint(0, cfg.vocab_size, (B, P), generator=g, dtype=torch.int32)
-    rt = _runtime("llama", cfg, params, torch.bfloat16, B, T)
+    old = DecoderRuntime.persistent_decode
+    DecoderRuntime.persistent_decode = path == "persistent"
+    try:
+        rt = _runtime("llama", cfg, params, torch.bfloat16, B, T)
+    finally:
+        DecoderRuntime.persistent_decode = old
+    assert (rt.fused_step is not None) == (path == "persistent")
     key, sub = TF.split(TF.prng_key(0))
     rt.reset(torch.ones(B, P, dtype=torch.bool, device="cuda"), key, sub, n_steps + 1)
     rt.prefill(ids.cuda(), True, 1.0)

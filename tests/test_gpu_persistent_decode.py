@@ -3,7 +3,8 @@
 Small Llama-shaped bf16 models with head size 128 (the kernel's) so the oracle stays fast; they
 exercise projections with fewer iterations than CTAs (most CTAs have no share of a phase), rows of
 different lengths (right-padded prompts: different key-split counts per row), several 128-key splits,
-one and sixteen batch rows, and repeated replays of the captured step (the grid barrier counter, the
+both attention forms (split items over 128-key ranges with a grid barrier between scores and P.V, and
+single-pass items per (row, KV head) when those fill half the grid), one and sixteen batch rows, and repeated replays of the captured step (the grid barrier counter, the
 split-K and attention arrival counters must reset every step).  Norm weights are random so their loads
 count.  Logits within max(2e-2, 4 bf16 ulps of the largest logit) of the oracle with a mean error below
 half an ulp of the largest logit (measured: a quarter; a wrong index or rounding point shows as errors
@@ -47,6 +48,8 @@ CASES = [
     (16, 300, [300 - 7 * i for i in range(16)], 4, dict()),
     (1, 130, [130], 5, dict(H=8, Hkv=1)),
     (5, 200, [200, 199, 129, 128, 127], 4, dict(d=1024, H=16, Hkv=4, L=3, V=3000)),
+    # 16 rows x 8 KV heads: one single-pass attention item per (row, KV head), ragged key counts
+    (16, 260, [260 - 17 * i for i in range(16)], 4, dict(d=512, H=32, Hkv=8)),
 ]
 
 
