@@ -30,7 +30,6 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-METRIC = "decode tok/s (box) & p50 step latency, Llama-3-8B-shape bf16, TP=1/2/4/8"
 
 # DRAM bytes (read 235079424 + write 4493056) of one launch of the tcgen05 decode projection on the
 # gate/up shape (M=16, N=28672, K=4096), from an ncu --set full capture of
@@ -46,21 +45,98 @@ def l8_config(num_layers=32):
                        norm_eps=1e-5, rope_theta=500000.0)
 
 
+def nx_config():
+    from jaxml_b200.config import ModelConfig
+
+    return ModelConfig(hidden_size=512, head_dim=64, num_heads=8, num_layers=6, max_position_embeddings=2048,
+                       vocab_size=50304, intermediate_ratio=(4, 1), norm_eps=1e-5, rotary_pct=0.25,
+                       use_parallel_residual=True, use_bias=True)
+
+
+def g12_config(num_layers=48):
+    from jaxml_b200.config import ModelConfig
+
+    return ModelConfig(hidden_size=3840, head_dim=256, num_heads=16, num_kv_heads=8, num_layers=num_layers,
+                       intermediate_ratio=(4, 1), max_position_embeddings=8704, vocab_size=262144, norm_eps=1e-6,
+                       sliding_window=1024, sliding_window_pattern=6, rope_theta=1000000.0, attn_scale=256 ** -0.5)
+
+
+def l70_config(num_layers=80):
+    from jaxml_b200.config import ModelConfig
+
+    return ModelConfig(hidden_size=8192, head_dim=128, num_heads=64, num_kv_heads=8, num_layers=num_layers,
+                       intermediate_ratio=(7, 2), max_position_embeddings=131072, vocab_size=128256,
+                       norm_eps=1e-5, rope_theta=500000.0)
+
+
+# The configurations (model shape, batch, prompt, new tokens, compute dtype).  l8 is the headline.
+CONFIGS = {
+    "l8": dict(family="llama", make=l8_config, B=16, P=512, new=256, dtype="bf16",
+               name="Llama-3-8B-shape bf16"),
+    "nx": dict(family="neox", make=nx_config, B=1, P=32, new=64, dtype="f32",
+               name="GPT-NeoX pythia-70m-shape fp32"),
+    "g12": dict(family="gemma3", make=g12_config, B=8, P=8192, new=128, dtype="bf16",
+                name="Gemma3-12B-shape bf16"),
+    "l70": dict(family="llama", make=l70_config, B=64, P=2048, new=128, dtype="bf16",
+                name="Llama-3-70B-shape bf16"),
+}
+
+
+class LazyLayers(dict):
+    """The per-layer parameter subtrees of a random-init model, made when first read and not kept: packing
+    a rank's shard of a 70B-shaped model then never holds more than one full layer on the device."""
+
+    def __init__(self, family, cfg, seed, dtype, device, body):
+        super().__init__(body)
+        self.family, self.cfg, self.seed, self.dtype, self.device = family, cfg, seed, dtype, device
+
+    def __getitem__(self, key):
+        if isinstance(key, str) and key.startswith("layers_") and not dict.__contains__(self, key):
+            from jaxml_b200.models import random_params
+
+            i = int(key.split("_")[1])
+            one = random_params(self.family, self.cfg.replace(num_layers=1), seed=self.seed * 100003 + i + 1,
+                                dtype=self.dtype, device=self.device)
+            body = one["params"]["gpt_neox" if self.family == "neox" else "model"]
+            return body["layers_0"]
+        return dict.__getitem__(self, key)
+
+    def __contains__(self, key):
+        if isinstance(key, str) and key.startswith("layers_"):
+            return int(key.split("_")[1]) < self.cfg.num_layers
+        return dict.__contains__(self, key)
+
+
+def lazy_random_params(family, cfg, seed, dtype, device):
+    """random_params' tree (N(0, 0.02) kernels) with layers made on demand (LazyLayers)."""
+    from jaxml_b200.models import random_params
+
+    top = random_params(family, cfg.replace(num_layers=1), seed=seed, dtype=dtype, device=device)
+    root = "gpt_neox" if family == "neox" else "model"
+    body = {k: v for k, v in top["params"][root].items() if not k.startswith("layers_")}
+    top["params"][root] = LazyLayers(family, cfg, seed, dtype, device, body)
+    return top
+
+
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="l8",
+                    help="model / workload: l8 Llama-3-8B shape (headline), nx pythia-70m shape fp32, g12 Gemma3-12B "
+                         "shape, l70 Llama-3-70B shape (tensor parallel only)")
     ap.add_argument("--steps", type=int, default=252)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--batch", type=int, default=16)
-    ap.add_argument("--prompt", type=int, default=512)
-    ap.add_argument("--layers", type=int, default=32)
+    ap.add_argument("--batch", type=int, default=None, help="batch rows (default: the config's)")
+    ap.add_argument("--prompt", type=int, default=None, help="prompt length (default: the config's)")
+    ap.add_argument("--layers", type=int, default=None, help="decoder layers (default: the config's)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-temp", action="store_true", help="skip the temperature-0.8 decode timing")
     ap.add_argument("--per-op", action="store_true",
                     help="decode with one kernel launch per op instead of the persistent decode-step kernel")
-    ap.add_argument("--e2e-tokens", type=int, default=256, help="new tokens per row of the e2e generation")
+    ap.add_argument("--e2e-tokens", type=int, default=None,
+                    help="new tokens per row of the e2e generation (default: the config's, 256 for l8)")
     ap.add_argument("--tp-pull", action="store_true",
                     help="tensor-parallel decode: separate pull all-reduce kernels instead of the push-fused projections")
     ap.add_argument("--micro", choices=["gemv", "attn", "gemm", "allreduce", "tpx"], default=None,
@@ -135,13 +211,20 @@ class ClockSampler:
 # ------------------------------------------------------------------------------------------------
 # algorithmic bytes
 # ------------------------------------------------------------------------------------------------
-def step_bytes(cfg, B, ctx_mean, tp=1):
-    """Weight + KV bytes one decode step must move per GPU (bf16)."""
+def step_bytes(cfg, B, ctx_mean, tp=1, family="llama", elem=2):
+    """Weight + KV bytes one decode step must move per GPU: every layer's projection weights (and norms),
+    the final norm, the LM head (vocabulary-parallel under tensor parallelism), the B embedding rows, and
+    the K / V of the keys each layer attends to (Gemma3's sliding-window layers only their window)."""
     d, H, Hkv, hd, F, V = (cfg.hidden_size, cfg.num_heads, cfg.num_key_value_heads, cfg.head_dim,
                            cfg.intermediate_size, cfg.vocab_size)
-    per_layer = (d * (H + 2 * Hkv) * hd + H * hd * d + 3 * d * F) / tp + 2 * d
-    weights = 2 * (cfg.num_layers * per_layer + d + d * V / tp + B * d)
-    kv = B * cfg.num_layers * ctx_mean * 2 * (Hkv / tp) * hd * 2
+    mlp = 2 * d * F if family == "neox" else 3 * d * F
+    per_layer = (d * (H + 2 * Hkv) * hd + H * hd * d + mlp) / tp + 2 * d
+    weights = elem * (cfg.num_layers * per_layer + d + d * V / tp + B * d)
+    kv = 0.0
+    for i in range(cfg.num_layers):
+        local = family == "gemma3" and cfg.sliding_window and (i + 1) % (cfg.sliding_window_pattern or 1)
+        keys = min(ctx_mean, cfg.sliding_window) if local else ctx_mean
+        kv += B * keys * 2 * (Hkv / tp) * hd * elem
     return weights + kv, weights, kv
 
 
@@ -212,33 +295,34 @@ def kernel_table(rt, cfg, ctx, step_ms, n_layers=8):
 # ------------------------------------------------------------------------------------------------
 # CPU baseline: the oracle restatement on the host cores (bounded sample)
 # ------------------------------------------------------------------------------------------------
-CPU_SCALE = 32   # one sample = one of the 32 decoder layers + 1/32 of the LM head
-
-
-def cpu_decode_samples(B=16, ctx=512, n_warm=1, n_timed=3, budget_s=60.0, seed=0):
-    """Seconds per sample of one Llama-3-8B-shape decode step on the host cores (the oracle): one decoder
-    layer of the batch at context `ctx` plus 1/32 of the LM head's columns, so 32 samples are one full
-    step's work.  Times up to `n_timed` samples after `n_warm` untimed ones, stopping early once
-    `budget_s` seconds of timed work have run.  Returns (list of sample seconds, threads)."""
+def cpu_decode_samples(conf, B, ctx, n_warm=1, n_timed=3, budget_s=60.0, seed=0):
+    """Seconds per sample of one decode step of configuration `conf` on the host cores (the oracle): one
+    decoder layer of the batch at context `ctx` plus 1/L of the LM head's columns, so L samples (L = the
+    model's layers) are one full step's work.  Times up to `n_timed` samples after `n_warm` untimed ones,
+    stopping early once `budget_s` seconds of timed work have run.  Returns (sample seconds, threads, L)."""
     import torch
 
     from oracle import jaxml_oracle as O
 
     threads = len(os.sched_getaffinity(0))
     torch.set_num_threads(threads)
-    cfg = l8_config(1)
-    params = O.init_params("llama", cfg, seed=seed, dtype=torch.bfloat16)
-    head = params["params"]["lm_head"]["kernel"][:, : cfg.vocab_size // CPU_SCALE].contiguous()
+    full = conf["make"]()
+    L = full.num_layers
+    cfg = full.replace(num_layers=1)
+    dt = torch.bfloat16 if conf["dtype"] == "bf16" else torch.float32
+    family = conf["family"]
+    params = O.init_params(family, cfg, seed=seed, dtype=dt)
+    head = params["params"]["lm_head"]["kernel"][:, : max(1, cfg.vocab_size // L)].contiguous()
     T = (ctx // 256 + 1) * 256
     g = torch.Generator().manual_seed(seed)
-    c = O.OracleKVCache(T, torch.bfloat16)
-    k = (torch.randn(B, ctx, cfg.num_key_value_heads, cfg.head_dim, generator=g)).to(torch.bfloat16)
+    c = O.OracleKVCache(T, dt)
+    k = (torch.randn(B, ctx, cfg.num_key_value_heads, cfg.head_dim, generator=g)).to(dt)
     caches = (c.update(k, k.clone(), None),)
     tok = torch.randint(0, cfg.vocab_size, (B, 1), generator=g, dtype=torch.int32)
 
     def one():
-        out = O.forward("llama", cfg, params, tok, torch.bfloat16, kv_caches=caches, with_head=False)
-        O.dense(out.last_hidden_state, head, None, torch.bfloat16)
+        out = O.forward(family, cfg, params, tok, dt, kv_caches=caches, with_head=False)
+        O.dense(out.last_hidden_state, head, None, dt)
     for _ in range(n_warm):
         one()
     times = []
@@ -248,11 +332,17 @@ def cpu_decode_samples(B=16, ctx=512, n_warm=1, n_timed=3, budget_s=60.0, seed=0
         times.append(time.perf_counter() - t0)
         if sum(times) > budget_s:
             break
-    return times, threads
+    return times, threads, L
 
 
-CPU_SAMPLE_NOTE = ("torch-CPU restatement of jaxml's math (JAX is not installed): each sample is one decoder layer "
-                   "of a batch-16 decode step at context 512 plus 1/32 of the LM head; tok/s = 16 / (32 x sample time)")
+def cpu_sample_note(B, ctx, L):
+    return ("torch-CPU restatement of jaxml's math (JAX is not installed): each sample is one decoder layer of a "
+            "batch-%d decode step at context %d plus 1/%d of the LM head; tok/s = %d / (%d x sample time)"
+            % (B, ctx, L, B, L))
+
+
+def metric_of(conf):
+    return "decode tok/s (box) & p50 step latency, %s, TP=1/2/4/8" % conf["name"]
 
 
 def reference_arm(args):
@@ -260,23 +350,24 @@ def reference_arm(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    times, threads = cpu_decode_samples(B=args.batch, ctx=args.prompt, n_warm=max(1, min(args.warmup, 2)),
-                                        n_timed=max(1, args.steps), budget_s=60.0)
+    conf = CONFIGS[args.config]
+    times, threads, L = cpu_decode_samples(conf, B=args.batch, ctx=args.prompt, n_warm=max(1, min(args.warmup, 2)),
+                                           n_timed=max(1, args.steps), budget_s=60.0)
     sample_s = sum(times) / len(times)
-    value = args.batch / (CPU_SCALE * sample_s)
+    value = args.batch / (L * sample_s)
     line = {
-        "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": args.gpus, "steps": len(times),
+        "metric": metric_of(conf), "value": value, "unit": "tok/s", "n_gpus": args.gpus, "steps": len(times),
         "warmup": max(1, min(args.warmup, 2)), "ms_per_step": sample_s * 1e3, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "scaling": "strong", "vs_baseline": None, "dtype": conf["dtype"],
         "data": "synthetic (uniform-random ids, N(0,0.02) weights, seed 0)",
-        "config": {"workload": "llama3-8b-shape bf16 decode, batch %d, context %d (one layer + 1/32 LM head per "
-                               "step, scaled by 32)" % (args.batch, args.prompt),
+        "config": {"workload": "%s decode, batch %d, context %d (one layer + 1/%d LM head per step, scaled by %d)"
+                               % (conf["name"], args.batch, args.prompt, L, L),
                    "global_batch": args.batch, "seq_len": args.prompt, "parallelism": "cpu"},
-        "extrapolated": {"timed": "one decoder layer + 1/32 of the LM head per step (a 1/32 sample of a decode step)",
-                         "scale": CPU_SCALE, "full_step_ms": CPU_SCALE * sample_s * 1e3},
+        "extrapolated": {"timed": "one decoder layer + 1/%d of the LM head per step (a 1/%d sample of a decode step)"
+                                  % (L, L), "scale": L, "full_step_ms": L * sample_s * 1e3},
         "impl": "reference",
         "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port",
-                         "sample": CPU_SAMPLE_NOTE},
+                         "sample": cpu_sample_note(args.batch, args.prompt, L)},
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -300,8 +391,7 @@ def gpu_arm(args):
         import torch.distributed as dist
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
-    from jaxml_b200 import Engine, InferenceConfig, LlamaModelWithHead
-    from jaxml_b200.models import random_params
+    from jaxml_b200 import Engine, GemmaModelWithHead, GPTNeoXModelWithHead, InferenceConfig, LlamaModelWithHead
 
     tp = world
     if args.attn_impl:
@@ -315,13 +405,18 @@ def gpu_arm(args):
             DecoderRuntime.peer_push = False
         if args.per_op:
             DecoderRuntime.persistent_decode = False
-    cfg = l8_config(args.layers)
+    conf = CONFIGS[args.config]
+    family = conf["family"]
+    cfg = conf["make"]().replace(num_layers=args.layers)
+    dt = torch.bfloat16 if conf["dtype"] == "bf16" else torch.float32
+    elem = 2 if conf["dtype"] == "bf16" else 4
     B, P = args.batch, args.prompt
     n_new = 1 + args.warmup + args.steps
     dev = torch.device("cuda", local)
-    params = random_params("llama", cfg, seed=0, dtype=torch.bfloat16, device=dev)
-    model = LlamaModelWithHead(cfg, dtype=torch.bfloat16)
-    engine = Engine(model, InferenceConfig(tp_size=tp), params, dtype=torch.bfloat16)
+    params = lazy_random_params(family, cfg, seed=0, dtype=dt, device=dev)
+    cls = {"llama": LlamaModelWithHead, "neox": GPTNeoXModelWithHead, "gemma3": GemmaModelWithHead}[family]
+    model = cls(cfg, dtype=dt)
+    engine = Engine(model, InferenceConfig(tp_size=tp), params, dtype=dt)
     engine.init_params(params)
     del params
     torch.cuda.empty_cache()
@@ -373,7 +468,7 @@ def gpu_arm(args):
     ctx_last = ctx_first + args.steps - 1
     ctx_mean = (ctx_first + ctx_last) / 2.0
     value = B * args.steps / (total_ms / 1e3)
-    sbytes, wbytes, kvbytes = step_bytes(cfg, B, ctx_mean, tp)
+    sbytes, wbytes, kvbytes = step_bytes(cfg, B, ctx_mean, tp, family, elem)
     step_ms_mean = total_ms / args.steps
 
     # ---- temperature 0.8 with a fixed seed (the workload's sampled variant), same steps ----
@@ -405,7 +500,7 @@ def gpu_arm(args):
         del graph_t
 
     # ---- per-kernel durations (graph replays, CUDA events) and the dominant kernel ----
-    table = kernel_table(rt, cfg, ctx_last, step_ms_mean) if tp == 1 else None
+    table = kernel_table(rt, cfg, ctx_last, step_ms_mean) if tp == 1 and args.config == "l8" else None
 
     # ---- end to end through Engine.generate with host buffers: the workload's 256 new tokens ----
     e2e = None
@@ -429,10 +524,10 @@ def gpu_arm(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        times, threads = cpu_decode_samples(B=B, ctx=P, n_warm=1, n_timed=3, budget_s=30.0)
+        times, threads, L = cpu_decode_samples(conf, B=B, ctx=P, n_warm=1, n_timed=3, budget_s=30.0)
         sample_s = sum(times) / len(times)
-        cpu = {"value": B / (CPU_SCALE * sample_s), "unit": "tok/s", "cores": threads, "kind": "port",
-               "sample": CPU_SAMPLE_NOTE + "; %d samples timed" % len(times)}
+        cpu = {"value": B / (L * sample_s), "unit": "tok/s", "cores": threads, "kind": "port",
+               "sample": cpu_sample_note(B, P, L) + "; %d samples timed" % len(times)}
 
     peaks = {}
     try:
@@ -453,20 +548,22 @@ def gpu_arm(args):
             r["frac"] = r["gbs"] / hbm_peak
     if rank == 0:
         line = {
-            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "metric": metric_of(conf), "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": step_ms_mean,
             "p50_step_ms": statistics.median(step_ms), "prefill_ms": prefill_ms,
             "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "bf16",
+            "vs_baseline": None, "dtype": conf["dtype"],
             "data": "synthetic (uniform-random prompt ids, N(0,0.02) random-init weights, seed 0)",
-            "config": {"workload": "llama3-8b-shape bf16 greedy decode, batch %d, prompt %d: %d timed decode steps "
+            "config": {"workload": "%s greedy decode, batch %d, prompt %d: %d timed decode steps "
                                    "at contexts %d..%d (e2e: %s new tokens)"
-                                   % (B, P, args.steps, ctx_first, ctx_last, args.e2e_tokens if e2e else "no"),
+                                   % (conf["name"], B, P, args.steps, ctx_first, ctx_last,
+                                      args.e2e_tokens if e2e else "no"),
+                       "config": args.config, "layers": cfg.num_layers,
                        "global_batch": B, "seq_len": P, "parallelism": f"tp{tp}",
                        "tp_exchange": None if tp == 1 else ("pull all-reduce" if args.tp_pull else "push-fused"),
                        "decode_path": rt.decode_path_name(),
                        "decode_attention": ["by shape", "split", "cluster", "column pv", "cluster-split"][args.attn_impl],
-                       "l2": "inputs larger than L2 (15 GB of weights per step)"},
+                       "l2": "inputs larger than L2 (%.2f GB of weights per step)" % (wbytes / 1e9)},
             "roofline": roofline,
             "kernels": table,
             "step_roofline": {"bytes_per_step": sbytes, "weight_bytes": wbytes, "kv_bytes": kvbytes,
@@ -740,11 +837,11 @@ def micro(args):
         grids = [int(g) for g in args.grids.split(",")]
         for grid in grids[:-1]:
             ms = _graph_ms(lambda st: [run(w, st, grid) for w in ws], copies)
-            print(json.dumps({"micro": "gemv", "impl": ["by-shape", "mma.sync", "tcgen05"][args.gemv_impl],
+            print(json.dumps({"micro": "gemv", "impl": ["by-shape", "mma.sync", "tcgen05", "row-split"][args.gemv_impl],
                               "shape": f"M={B} N={Nn} K={K}", "grid": grid, "us": ms * 1e3,
                               "gbs": nbytes / ms / 1e6}), flush=True)
         ms = _graph_ms(lambda st: [run(w, st, grids[-1]) for w in ws], copies)
-        line = {"micro": "gemv", "impl": ["by-shape", "mma.sync", "tcgen05"][args.gemv_impl], "shape": f"M={B} N={Nn} K={K}",
+        line = {"micro": "gemv", "impl": ["by-shape", "mma.sync", "tcgen05", "row-split"][args.gemv_impl], "shape": f"M={B} N={Nn} K={K}",
                 "grid": grids[-1], "us": ms * 1e3, "gbs": nbytes / ms / 1e6}
     else:
         ctx, L = args.ctx, 8
@@ -780,6 +877,15 @@ def micro(args):
 
 def main():
     args = parse()
+    conf = CONFIGS[args.config]
+    if args.batch is None:
+        args.batch = conf["B"]
+    if args.prompt is None:
+        args.prompt = conf["P"]
+    if args.layers is None:
+        args.layers = conf["make"]().num_layers
+    if args.e2e_tokens is None:
+        args.e2e_tokens = conf["new"]
     if args.micro == "allreduce":
         micro_allreduce(args)
         return

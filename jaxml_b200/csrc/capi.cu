@@ -143,7 +143,8 @@ int jx_norm(const jx_norm_args* args, int dtype, int pdl, void* stream) {
 }
 
 int jx_set_decode_linear_impl(int impl) {
-  if (impl < 0 || impl > 2) return fail(JX_ERR_ARG, "jx_set_decode_linear_impl: 0 (by shape), 1 (mma.sync), 2 (tcgen05)");
+  if (impl < 0 || impl > 3)
+    return fail(JX_ERR_ARG, "jx_set_decode_linear_impl: 0 (by shape), 1 (mma.sync), 2 (tcgen05), 3 (row split)");
   set_gemv_impl(impl);
   return JX_OK;
 }

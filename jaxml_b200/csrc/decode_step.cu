@@ -872,16 +872,16 @@ __device__ __noinline__ bool ds_attn_item(const DsParams& p, int layer, int b, i
 
 // Split-K fix-up of block nb by its last arriver: the partial tiles of CTAs c_first .. c_last summed in CTA
 // order into the staging tile (own = this CTA when its own partial is still in the tile, else -1).  Each
-// thread owns 4 float4 of the [16 x 128] tile; the loads of up to 8 contributors are issued before any is
-// added, so the L2 round trips of a block's contributors overlap.
-__device__ __noinline__ void ds_splitk_sum(const DsParams& p, long long nb, int c_first, int c_last, int own,
+// thread owns 4 float4 of the [16 x 128] tile; the loads of up to 4 contributors are issued before any is
+// added, so their L2 round trips overlap.  (Inlined, 4 at a time: a call, or 8 at a time, measured slower.)
+__device__ __forceinline__ void ds_splitk_sum(const DsParams& p, long long nb, int c_first, int c_last, int own,
                                            long long total, int kc, int Gp, float* tile, int wtid) {
   using namespace ds;
   float4 acc4[4];
-  for (int cc0 = c_first; cc0 <= c_last; cc0 += 8) {
-    float4 vv[8][4];
+  for (int cc0 = c_first; cc0 <= c_last; cc0 += 4) {
+    float4 vv[4][4];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
+    for (int u = 0; u < 4; ++u) {
       const int cc = cc0 + u;
       if (cc > c_last) break;
       if (cc == own) {
@@ -899,7 +899,7 @@ __device__ __noinline__ void ds_splitk_sum(const DsParams& p, long long nb, int 
       }
     }
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
+    for (int u = 0; u < 4; ++u) {
       if (cc0 + u > c_last) break;
 #pragma unroll
       for (int qq = 0; qq < 4; ++qq) {

@@ -1,0 +1,216 @@
+// Decode projection split by output rows: Y[M, N] = X[M, K] . W[N, K]^T for M <= 16 token rows, bfloat16
+// operands in the K128 tiled layout, float32 accumulation on mma.sync.
+//
+// The stream-K kernels (gemv.cu, gemv_tc.cu) give every SM the same number of bytes by splitting K
+// across CTAs, and pay for it at the end: the CTAs sharing a weight block publish float32 partial tiles
+// and the last to arrive sums them (two L2 round trips and an atomic before the epilogue can run), while
+// the kernel's last CTAs finish.  For the projections with fewer 128-row blocks than SMs (the decode
+// qkv, o_proj and down projections of a Llama-3-8B-shaped layer) this kernel instead gives CTA c the
+// output rows [c * ROWS, (c + 1) * ROWS) over the whole K: no partial tiles, no arrival counters, and a
+// CTA's epilogue follows its own last MMA.  ROWS (32 or 48) is chosen so that the grid is at most one
+// CTA per SM; at the shapes above that is 128 CTAs, each streaming ROWS x K weights through a ring of
+// TMA bulk copies (every ROWS-row run of one 128-wide K chunk is one contiguous block of the layout).
+//
+// Warp roles: warp 0 = TMA producer; consumer warp w (RG row groups x 4 K slices) owns weight rows
+// [(w % RG) * 16, + 16) and K steps [(w / RG) * 2, + 2) of every 128-wide chunk.  The 4 K-slice partials
+// are summed in slice order through shared memory (deterministic), then the shared fused epilogue runs.
+#include "common.cuh"
+#include "epilogue.cuh"
+
+namespace jxb {
+
+template <int RG>
+struct RowsCfg {
+  static constexpr int ROWS = 16 * RG;
+  static constexpr int kConsumers = RG * 4;                 // warps
+  static constexpr int kThreads = 32 * (1 + kConsumers);
+  static constexpr int kWBytes = ROWS * 128 * 2;            // 8 / 12 KB
+  static constexpr int kXBytes = 16 * 128 * 2;              // 4 KB
+  static constexpr int kStageBytes = kWBytes + kXBytes;
+  // 10 stages (120 / 160 KB in flight): 16 / 12 stages measured slower on every decode shape (e.g. o_proj
+  // 8.8 -> 9.4 us): the next kernel's CTAs start later behind a larger one.
+  static constexpr int kStages = 10;
+  static constexpr int kLd = ROWS + 4;                      // float32 row stride of the staging tiles
+  static constexpr int kPartBytes = 4 * 16 * kLd * 4;       // [4 K slices][16 tokens][ROWS]
+  static constexpr int kSmem = kStages * kStageBytes + kPartBytes + 2 * kStages * 8 + 16;
+};
+
+template <int RG>
+__global__ void __launch_bounds__(RowsCfg<RG>::kThreads, 1)
+    gemv_rows_kernel(const bf16* __restrict__ W, const bf16* __restrict__ X, long long Np, long long Kp, EpiParams e,
+                     int* status) {
+  using C = RowsCfg<RG>;
+  extern __shared__ __align__(128) uint8_t smem[];
+  float* part = reinterpret_cast<float*>(smem + C::kStages * C::kStageBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kStages * C::kStageBytes + C::kPartBytes);
+  uint64_t* empty = full + C::kStages;
+  volatile int* dead = reinterpret_cast<volatile int*>(empty + C::kStages);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long r0 = (long long)blockIdx.x * C::ROWS;
+  const int kc = (int)(Kp >> 7);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], C::kConsumers);
+    }
+    *dead = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  if (warp == 0) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      auto wsrc = [&](int kk) { return W + (((long long)kk * (Np >> 3) + (r0 >> 3)) << 10); };
+      auto xsrc = [&](int kk) { return X + ((long long)kk << 11); };   // 16 rows x 128 k per chunk
+      const uint64_t pol_w = l2_policy_evict_first();   // weights are read once per step
+      const int pre = kc < C::kStages ? kc : C::kStages;
+      // Weights do not depend on the previous kernel: start streaming them before waiting on it.
+      for (int i = 0; i < pre; ++i) {
+        mbar_arrive_expect_tx(&full[i], C::kStageBytes);
+        bulk_g2s_hint(smem + i * C::kStageBytes, wsrc(i), C::kWBytes, &full[i], pol_w);
+      }
+      pdl_wait();
+      pdl_trigger();
+      for (int i = 0; i < pre; ++i) bulk_g2s(smem + i * C::kStageBytes + C::kWBytes, xsrc(i), C::kXBytes, &full[i]);
+      int issued = pre;
+      for (int i = pre; i < kc; ++i) {
+        const int s = i % C::kStages;
+        if (!mbar_wait_bounded(&empty[s], ((i / C::kStages) - 1) & 1)) {
+          set_status(status, JX_ERR_TIMEOUT);
+          *dead = 1;
+          break;
+        }
+        mbar_arrive_expect_tx(&full[s], C::kStageBytes);
+        bulk_g2s_hint(smem + s * C::kStageBytes, wsrc(i), C::kWBytes, &full[s], pol_w);
+        bulk_g2s(smem + s * C::kStageBytes + C::kWBytes, xsrc(i), C::kXBytes, &full[s]);
+        issued = i + 1;
+      }
+      // every issued copy lands before this CTA's shared memory is released
+      for (int i = (issued > C::kStages ? issued - C::kStages : 0); i < issued; ++i)
+        if (!mbar_wait_bounded(&full[i % C::kStages], (i / C::kStages) & 1)) break;
+    }
+    return;
+  }
+
+  // ---------------- consumers ----------------
+  pdl_wait();
+  pdl_trigger();
+  const int cw = (warp - 1) % RG;     // weight rows [cw * 16, + 16)
+  const int ksl = (warp - 1) / RG;    // K steps [ksl * 2, + 2) of every chunk
+  const int tid = threadIdx.x - 32;
+  // The tensor-core accumulator is folded into an IEEE float32 sum every 4 chunks (8 MMAs): one chain over
+  // the whole K rounds noticeably worse than float32 sums (bf16 results flip more often).
+  float acc[2][4] = {}, sum[2][4] = {};
+  bool ok = true;
+  const int mi = lane >> 3, r8 = lane & 7;
+  for (int i = 0; i < kc; ++i) {
+    const int s = i % C::kStages;
+    if (ok && (*dead || !mbar_wait_bounded(&full[s], (i / C::kStages) & 1))) {
+      ok = false;
+      *dead = 1;
+      set_status(status, JX_ERR_TIMEOUT);
+    }
+    if (ok) {
+      const uint32_t sW = smem_u32(smem + s * C::kStageBytes);
+      const uint32_t sX = sW + C::kWBytes;
+#pragma unroll
+      for (int kq = 0; kq < 2; ++kq) {
+        const int ks = ksl * 2 + kq;
+        uint32_t b0, b1, b2, b3, a0, a1, a2, a3;
+        {
+          const int rg = cw * 2 + (mi >> 1), kcore = ks * 2 + (mi & 1);
+          ldsm_x4(sW + (uint32_t)((rg * 1024 + kcore * 64 + r8 * 8) * 2), b0, b1, b2, b3);
+        }
+        {
+          const int rg = mi & 1, kcore = ks * 2 + (mi >> 1);
+          ldsm_x4(sX + (uint32_t)((rg * 1024 + kcore * 64 + r8 * 8) * 2), a0, a1, a2, a3);
+        }
+        mma_bf16(acc[0], a0, a1, a2, a3, b0, b1);
+        mma_bf16(acc[1], a0, a1, a2, a3, b2, b3);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+    if ((i & 3) == 3 || i == kc - 1) {
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          sum[nt][q] += acc[nt][q];
+          acc[nt][q] = 0.f;
+        }
+    }
+  }
+  // this warp's partial: tokens lane / 4 (+ 8) x weight rows cw * 16 + nt * 8 + (lane % 4) * 2 (+ 1)
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt) {
+    const int t = lane >> 2, col = cw * 16 + nt * 8 + (lane & 3) * 2;
+    float* p0 = part + (ksl * 16 + t) * C::kLd + col;
+    float* p1 = part + (ksl * 16 + t + 8) * C::kLd + col;
+    p0[0] = sum[nt][0];
+    p0[1] = sum[nt][1];
+    p1[0] = sum[nt][2];
+    p1[1] = sum[nt][3];
+  }
+  named_bar_sync(1, C::kConsumers * 32);
+  // the K slices summed in slice order into slice 0
+  for (int idx = tid; idx < 16 * C::ROWS; idx += C::kConsumers * 32) {
+    const int m = idx / C::ROWS, j = idx - m * C::ROWS;
+    float v = part[m * C::kLd + j];
+#pragma unroll
+    for (int q = 1; q < 4; ++q) v += part[(q * 16 + m) * C::kLd + j];
+    part[m * C::kLd + j] = v;
+  }
+  named_bar_sync(1, C::kConsumers * 32);
+  if (ok && !*dead)
+    run_epilogue<bf16>(e, 0, 16, r0, C::ROWS, [&](int m, int j) { return part[m * C::kLd + j]; }, tid,
+                       C::kConsumers * 32);
+}
+
+template <int RG>
+static int launch_rows(const bf16* W, const bf16* X, long long Np, long long Kp, const EpiParams& e, int* status,
+                       bool pdl, cudaStream_t stream) {
+  using C = RowsCfg<RG>;
+  static bool configured = false;
+  if (!configured) {
+    if (cudaFuncSetAttribute(gemv_rows_kernel<RG>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) !=
+        cudaSuccess)
+      return JX_ERR_CUDA;
+    configured = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(Np / C::ROWS));
+  cfg.blockDim = dim3(C::kThreads);
+  cfg.dynamicSmemBytes = C::kSmem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return launch_ex(&cfg, gemv_rows_kernel<RG>, W, X, Np, Kp, e, status) == cudaSuccess ? JX_OK : JX_ERR_CUDA;
+}
+
+// Row-group count (2 -> 32 rows, 3 -> 48 rows per CTA) for an Np-row projection on `sms` SMs: the
+// smallest whose grid fits one CTA per SM and divides Np; 0 when none does.
+int gemv_rows_groups(long long Np, int sms) {
+  for (int rg = 2; rg <= 3; ++rg)
+    if (Np % (16 * rg) == 0 && Np / (16 * rg) <= sms) return rg;
+  return 0;
+}
+
+int run_gemv_rows(const bf16* W, const bf16* X, long long Np, long long Kp, int M, const EpiParams& e, int* status,
+                  int sms, bool pdl, cudaStream_t stream) {
+  if (M <= 0 || M > 16 || Kp % 128 || Kp <= 0) return JX_ERR_SHAPE;
+  if ((reinterpret_cast<uintptr_t>(W) | reinterpret_cast<uintptr_t>(X)) & 15) return JX_ERR_ARG;
+  switch (gemv_rows_groups(Np, sms)) {
+    case 2: return launch_rows<2>(W, X, Np, Kp, e, status, pdl, stream);
+    case 3: return launch_rows<3>(W, X, Np, Kp, e, status, pdl, stream);
+    default: return JX_ERR_SHAPE;
+  }
+}
+
+}  // namespace jxb

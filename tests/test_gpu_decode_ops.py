@@ -316,3 +316,46 @@ def test_decode_attention_long_context_matches_oracle(form, T, lens):
             assert (err <= ulp + 1e-6).float().mean().item() >= 0.99
     finally:
         N.call("jx_set_decode_attention_impl", 0)
+
+
+@pytest.mark.parametrize("M,Nn,K", [(1, 6144, 4096), (16, 6144, 4096), (16, 4096, 14336), (16, 4096, 4096),
+                                    (7, 512, 1024), (16, 4608, 384)])
+def test_linear_decode_row_split(M, Nn, K):
+    """The row-split decode projection (jx_set_decode_linear_impl(3)): each CTA takes 32 or 48 output rows
+    over the whole K; plain store, then a residual epilogue with bias, against a float64 dot."""
+    N = _n()
+    N.call("jx_set_decode_linear_impl", 3)
+    try:
+        torch.manual_seed(2)
+        x = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+        w = (torch.randn(Nn, K, device="cuda") * 0.02).to(torch.bfloat16)
+        Kp = _rup(K, 128)
+        xp, wp = _pack(N, x, 16, Kp), _pack(N, w, Nn, Kp)
+        out = torch.zeros(M, Nn, dtype=torch.bfloat16, device="cuda")
+        ws, cnt = _ws(N, Nn)
+        status = torch.zeros(1, dtype=torch.int32, device="cuda")
+        e = _epi(N, N.JX_EPI_STORE, M, Nn, out, Nn)
+        for _ in range(2):
+            out.zero_()
+            N.call("jx_linear_decode", wp.data_ptr(), xp.data_ptr(), Nn, Kp, M, e, ws.data_ptr(), ws.numel(),
+                   cnt.data_ptr(), status.data_ptr(), 148, 1, _stream())
+            torch.cuda.synchronize()
+            assert int(status.item()) == 0
+            _assert_rounded_dot(out, x, w)
+        bias = (torch.randn(Nn, device="cuda") * 0.1).to(torch.bfloat16)
+        h = torch.randn(M, Nn, device="cuda").to(torch.bfloat16)
+        h0 = h.clone()
+        e2 = _epi(N, N.JX_EPI_RESID, M, Nn, h, Nn, res=h, ldr=Nn, bias=bias)
+        N.call("jx_linear_decode", wp.data_ptr(), xp.data_ptr(), Nn, Kp, M, e2, ws.data_ptr(), ws.numel(),
+               cnt.data_ptr(), status.data_ptr(), 148, 1, _stream())
+        torch.cuda.synchronize()
+        y = (x.double() @ w.double().T).to(torch.bfloat16).double()
+        y = (y + bias.double()).to(torch.bfloat16).double()
+        ref = (y + h0.double()).to(torch.bfloat16).double()
+        assert (h.double() - ref).abs().max().item() <= 0.05 * ref.abs().max().item()
+        # a grid below the row count's needs is refused, not run
+        with pytest.raises(RuntimeError):
+            N.call("jx_linear_decode", wp.data_ptr(), xp.data_ptr(), Nn, Kp, M, e, ws.data_ptr(), ws.numel(),
+                   cnt.data_ptr(), status.data_ptr(), 4, 1, _stream())
+    finally:
+        N.call("jx_set_decode_linear_impl", 0)
