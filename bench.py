@@ -146,7 +146,7 @@ def parse():
     ap.add_argument("--gemv-impl", type=int, default=0, help="--micro gemv kernel: 0 by shape, 1 mma.sync, 2 tcgen05")
     ap.add_argument("--grids", default="148", help="--micro gemv: comma-separated CTA counts to time (one line each)")
     ap.add_argument("--tile-groups", default="", help="--micro gemm: comma-separated tile-group sizes to time")
-    ap.add_argument("--attn-impl", type=int, default=0, help="decode attention form: 0 by shape, 1 split, 2 cluster, 3 column pv, 4 cluster-split")
+    ap.add_argument("--attn-impl", type=int, default=0, help="decode attention form: 0 by shape, 1 split, 2 cluster, 3 column pv, 4 cluster-split, 5 queue")
     ap.add_argument("--tokens", type=int, default=8192, help="token rows of --micro gemm (prefill B x P)")
     ap.add_argument("--gemm-impl", type=int, default=0, help="--micro gemm kernel: 0 by shape, 1 mma.sync, 2 tcgen05")
     return ap.parse_args()
@@ -562,7 +562,7 @@ def gpu_arm(args):
                        "global_batch": B, "seq_len": P, "parallelism": f"tp{tp}",
                        "tp_exchange": None if tp == 1 else ("pull all-reduce" if args.tp_pull else "push-fused"),
                        "decode_path": rt.decode_path_name(),
-                       "decode_attention": ["by shape", "split", "cluster", "column pv", "cluster-split"][args.attn_impl],
+                       "decode_attention": ["by shape", "split", "cluster", "column pv", "cluster-split", "queue"][args.attn_impl],
                        "l2": "inputs larger than L2 (%.2f GB of weights per step)" % (wbytes / 1e9)},
             "roofline": roofline,
             "kernels": table,
@@ -870,7 +870,7 @@ def micro(args):
             N.call("jx_decode_attention", a, 1, st)
         ms = _graph_ms(lambda st: [run(l, st) for l in range(L)], L)
         nbytes = B * ctx * 2 * Hkv * hd * 2
-        line = {"micro": "attn", "impl": ["by-shape", "split", "cluster", "column", "cluster-split"][args.attn_impl], "shape": f"B={B} ctx={ctx} Hq={Hq} Hkv={Hkv} hd={hd}", "us": ms * 1e3,
+        line = {"micro": "attn", "impl": ["by-shape", "split", "cluster", "column", "cluster-split", "queue"][args.attn_impl], "shape": f"B={B} ctx={ctx} Hq={Hq} Hkv={Hkv} hd={hd}", "us": ms * 1e3,
                 "gbs": nbytes / ms / 1e6}
     print(json.dumps(line), flush=True)
 

@@ -268,6 +268,18 @@ typedef struct jx_sample_args {
   int* status;
 } jx_sample_args;
 
+typedef struct jx_filter_args {
+  int B, V;              /* rows, vocabulary columns (V <= 393216) */
+  const void* logits;    /* [B, ld_in] */
+  long long ld_in;
+  void* out;             /* [B, ld_out]; may alias logits */
+  long long ld_out;
+  int dtype;             /* JX_F32 or JX_BF16 */
+  int top_k;             /* <= 0: off */
+  float top_p;           /* >= 1: off */
+  float min_p;           /* <= 0: off */
+} jx_filter_args;
+
 /* ---- library ---- */
 const char* jx_version(void);
 const char* jx_last_error(void);
@@ -353,7 +365,8 @@ int jx_decode_attention(const jx_dattn_args* args, int pdl, void* stream);
  * 2 = the single-pass thread-block-cluster form (key range (T, or the window) up to 8 CTAs x 2048 keys;
  * JX_ERR_SHAPE otherwise), 3 = split scores + column pv, 4 = the cluster-split form (one kernel, the
  * key splits of a head group in one thread-block cluster; up to 16 splits of 128 keys, JX_ERR_SHAPE
- * otherwise). */
+ * otherwise), 5 = the queue form (the split form's score and pv work as one persistent kernel whose CTAs
+ * claim items from a counter in the workspace; outputs bit-identical to the split form). */
 int jx_set_decode_attention_impl(int impl);
 
 /* Attention.mha prefill branch (causal + window + padding masks, nn/attention.py:321-400) for bf16
@@ -363,6 +376,12 @@ int jx_prefill_attention(const jx_pattn_args* args, int pdl, void* stream);
 /* greedy_fn / categorical sampling (inference_engine/sampling.py:75-188) + end-of-step bookkeeping. */
 int jx_sample(const jx_sample_args* args, int pdl, void* stream);
 int jx_sample_finalize(const jx_sample_args* args, const unsigned long long* gathered, int n_shards, void* stream);
+
+/* min_p_filtering, then top_k_filtering, then top_p_filtering (inference_engine/sampling.py:34-75, order
+ * :169-188) of full-vocabulary rows, filtered entries -inf: probabilities in float32 rounded to the logits'
+ * dtype, ties at the top-k cutoff kept, the top-p cutoff from exact (fixed-point) cumulative masses.  One
+ * thread-block cluster per row (see csrc/filter.cu). */
+int jx_filter_logits(const jx_filter_args* args, void* stream);
 
 /* Clear the split-K counters after an error (they are self-resetting otherwise). */
 int jx_memset_async(void* ptr, int value, long long bytes, void* stream);

@@ -86,6 +86,11 @@ class JxSampleArgs(ctypes.Structure):
                 ("advance_rng", I), ("_pad0", I), ("status", P)]
 
 
+class JxFilterArgs(ctypes.Structure):
+    _fields_ = [("B", I), ("V", I), ("logits", P), ("ld_in", LL), ("out", P), ("ld_out", LL), ("dtype", I),
+                ("top_k", I), ("top_p", F), ("min_p", F)]
+
+
 class JxStepArgs(ctypes.Structure):
     _fields_ = [("M", I), ("L", I), ("d", I), ("Hq", I), ("Hkv", I), ("hd", I), ("F", I), ("V", I), ("vocab", I),
                 ("T", I), ("rd", I), ("max_pos", I), ("Np_qkv", LL), ("Np_d", LL), ("Np_gu", LL), ("Np_v", LL),
@@ -121,6 +126,7 @@ _PROTOS = {
     "jx_set_decode_attention_impl": (I, [I]),
     "jx_prefill_attention": (I, [ctypes.POINTER(JxPAttnArgs), I, P]),
     "jx_sample": (I, [ctypes.POINTER(JxSampleArgs), I, P]),
+    "jx_filter_logits": (I, [ctypes.POINTER(JxFilterArgs), P]),
     "jx_decode_step": (I, [ctypes.POINTER(JxStepArgs), P]),
     "jx_set_decode_step_lookahead": (I, [I]),
     "jx_sample_finalize": (I, [ctypes.POINTER(JxSampleArgs), P, I, P]),

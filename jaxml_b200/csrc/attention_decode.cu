@@ -48,6 +48,8 @@ struct DAttnParams {
   int rd, max_pos;
   bf16* k_cache;         // the cache allocations, written at this step's position
   bf16* v_cache;
+  // queue form: [0] item claims, [1] finished CTAs, [2, 2 + B * Hkv) scored splits per head group
+  int* qsync;
 };
 
 // 8 consecutive elements [j0, j0 + 8) of one head of the projection output, rotated on its first rd
@@ -1094,6 +1096,422 @@ __global__ void __launch_bounds__(128) dattn_warp_kernel(const __grid_constant__
   cluster_sync_all();   // no CTA leaves while another may still read its shared memory
 }
 
+
+// ------------------------------------------------------------------------------------------------
+// Queue form: the split form's two kernels as one persistent kernel.  The work is a list of items, the
+// score items of every (head group, key split) and then the pv items of the same; each CTA claims
+// items in list order from a global counter and, while it works on one item, has the TMA tiles of the
+// next one in flight in its second shared-memory slot, so K tiles and then V tiles stream without a
+// kernel boundary between the two phases.  A score item writes its rounded scores and (max, sum) as the
+// scores kernel does and counts itself done for its head group (release); a pv item waits (bounded,
+// acquire) until every split of its head group is scored, then forms the exact bf16 probabilities and
+// P.V as the pv kernel does, and the last pv item of a group sums the split partials in split order.
+// No co-residency is needed: every score item precedes every pv item in the list and a CTA finishes
+// an item before it starts the next, so when a pv item waits, the score items it waits for have all
+// been claimed by CTAs that are running them without waiting on anything.  The sums, roundings and
+// workspace are the split form's, so the outputs are bit-identical to it.
+// ------------------------------------------------------------------------------------------------
+template <int HD>
+struct DqCfg {
+  static constexpr int NB = HD / 64;
+  static constexpr int TILE_BYTES = kDaTile * HD * 2;
+  static constexpr int SLOT_BYTES = 2 * TILE_BYTES;      // one item: 128 keys
+  static constexpr int OFF_QS = 2 * SLOT_BYTES;
+  static constexpr int OFF_PT = OFF_QS + NB * 2048;
+  static constexpr int OFF_BAR = OFF_PT + 16 * kPLd * 2;  // 4 mbarriers: [slot][tile]
+  static constexpr int OFF_RED = OFF_BAR + 4 * 8;         // [4 warps][16 rows]
+  static constexpr int OFF_ML = OFF_RED + 64 * 4;         // M[16], L[16]
+  static constexpr int OFF_IT = OFF_ML + 32 * 4;          // claimed items of the two slots, ok flag
+  static constexpr int BYTES = OFF_IT + 16 + 1024;         // + alignment of the dynamic base to 1 KB
+};
+
+template <int HD>
+__global__ void __launch_bounds__(128) dattn_queue_kernel(const __grid_constant__ CUtensorMap kmap,
+                                                          const __grid_constant__ CUtensorMap vmap, DAttnParams p) {
+  using C = DqCfg<HD>;
+  constexpr int NB = C::NB;
+  constexpr int WCOLS = HD / 4;
+  constexpr int NT = WCOLS / 8;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* qs = smem + C::OFF_QS;
+  bf16* ptile = reinterpret_cast<bf16*>(smem + C::OFF_PT);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  float* red = reinterpret_cast<float*>(smem + C::OFF_RED);
+  float* Ms = reinterpret_cast<float*>(smem + C::OFF_ML);
+  float* Ls = Ms + 16;
+  volatile int* items = reinterpret_cast<volatile int*>(smem + C::OFF_IT);   // [2] items, [2] ok flag
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = p.B * p.Hkv;
+  const int n_score = G * p.n_splits, total = 2 * n_score;
+  int* claim_ctr = p.qsync;
+  int* done_ctas = p.qsync + 1;
+  int* scored = p.qsync + 2;
+  const bool fused = p.qkv != nullptr;
+
+  // Item -> (pv?, batch row, KV head, split, key range).  Items whose split holds no valid key are
+  // skipped at claim time.
+  struct Item {
+    int pv, b, kvh, split, t0, t1, valid, n_tiles, n_active;
+  };
+  auto decode = [&](int it) {
+    Item x;
+    x.pv = it >= n_score;
+    const int r = x.pv ? it - n_score : it;
+    const int g = r / p.n_splits;
+    x.split = r - g * p.n_splits;
+    x.b = g / p.Hkv;
+    x.kvh = g - x.b * p.Hkv;
+    int lo;
+    key_range(p, x.b, lo, x.valid);
+    x.t0 = lo + x.split * kDaKeys;
+    x.t1 = min(x.t0 + kDaKeys, x.valid);
+    x.n_tiles = x.t0 < x.valid ? (x.t1 - x.t0 + kDaTile - 1) / kDaTile : 0;
+    x.n_active = (x.valid - lo + kDaKeys - 1) / kDaKeys;
+    return x;
+  };
+  auto claim = [&]() {
+    for (;;) {
+      const int it = atomicAdd(claim_ctr, 1);
+      if (it >= total) return -1;
+      if (decode(it).n_tiles > 0) return it;
+    }
+  };
+  // tile i of item x holds this step's key (position valid - 1)
+  auto holds_new = [&](const Item& x, int i) {
+    return x.t0 + i * kDaTile <= x.valid - 1 && x.valid - 1 < x.t0 + (i + 1) * kDaTile;
+  };
+  auto issue_tile = [&](const Item& x, int slot, int i) {
+    uint64_t* bb = &bar[slot * 2 + i];
+    mbar_arrive_expect_tx(bb, C::TILE_BYTES);
+    const int y = (int)(p.layer_row0 + (long long)x.b * p.T + x.t0 + i * kDaTile);
+    uint8_t* dst = smem + slot * C::SLOT_BYTES + i * C::TILE_BYTES;
+#pragma unroll
+    for (int c = 0; c < NB; ++c) tma_load_2d(dst + c * 8192, x.pv ? &vmap : &kmap, x.kvh * HD + c * 64, y, bb);
+  };
+  // Thread 0: every barrier of the slot gets one arrival per item (a tile, or a plain arrive for a
+  // tile the item does not have).  Returns the tile left to issue later (-1: none): this step's key or
+  // value when it is not complete yet (before the wait on the previous kernel without the fused
+  // append; the fused append's value, written by a score item of this kernel).
+  auto issue_item = [&](int it, int slot, bool before_wait) {
+    const Item x = decode(it);
+    fence_proxy_async();   // the slot's previous contents were read through the generic proxy
+    int late = -1;
+    for (int i = 0; i < 2; ++i) {
+      if (i >= x.n_tiles) {
+        mbar_arrive(&bar[slot * 2 + i]);
+      } else if (holds_new(x, i) && ((x.pv && fused) || (!fused && before_wait))) {
+        late = i;
+      } else {
+        issue_tile(x, slot, i);
+      }
+    }
+    return late;
+  };
+
+  int late0 = -1, late1 = -1;   // thread 0 only: the tile left to issue later, per slot
+  if (threadIdx.x == 0) {
+    prefetch_tmap(&kmap);
+    prefetch_tmap(&vmap);
+    for (int i = 0; i < 4; ++i) mbar_init(&bar[i], 1);
+    fence_barrier_init();
+    const int first = claim();
+    items[0] = first;
+    if (first >= 0) late0 = issue_item(first, 0, true);
+  }
+  pdl_wait();
+  pdl_trigger();
+  if (threadIdx.x == 0 && items[0] >= 0 && late0 >= 0 && !decode(items[0]).pv) {
+    issue_tile(decode(items[0]), 0, late0);
+    late0 = -1;
+  }
+  if (threadIdx.x == 0) items[2] = 1;
+  __syncthreads();
+
+  const int mi = lane >> 3, r8 = lane & 7;
+  const int r_lo = lane >> 2, r_hi = r_lo + 8;
+  uint32_t phases = 0;   // bit s: parity of slot s's barriers for its next item
+  int slot = 0;
+  for (int cur = items[0]; cur >= 0;) {
+    if (threadIdx.x == 0) {
+      const int nxt = claim();
+      items[slot ^ 1] = nxt;
+      if (nxt >= 0) {
+        const int lt = issue_item(nxt, slot ^ 1, false);
+        if (slot) late0 = lt;
+        else late1 = lt;
+      }
+    }
+    const Item x = decode(cur);
+    const int g = x.b * p.Hkv + x.kvh;
+    uint8_t* tiles = smem + slot * C::SLOT_BYTES;
+    uint64_t* sb = &bar[slot * 2];
+    const uint32_t par = (phases >> slot) & 1u;
+    if (!x.pv) {
+      // ---------------- score item (the scores kernel's work on one split) ----------------
+      int pos = x.valid - 1;
+      if (fused && pos >= p.max_pos) {
+        if (threadIdx.x == 0) set_status(p.status, JX_ERR_RANGE);
+        pos = 0;
+      }
+      const bf16* qkv_row = fused ? p.qkv + (long long)x.b * p.ld_qkv : nullptr;
+      for (int idx = threadIdx.x; idx < 16 * (HD / 8); idx += 128) {
+        const int r = idx / (HD / 8), cg = idx % (HD / 8);
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (r < p.n_rep) {
+          if (fused)
+            v = rope8(qkv_row + (long long)(x.kvh * p.n_rep + r) * HD, cg * 8, HD, p.rd, p.cos, p.sin, pos);
+          else
+            v = *reinterpret_cast<const uint4*>(p.q + ((long long)x.b * p.Hq + x.kvh * p.n_rep + r) * HD + cg * 8);
+        }
+        const uint32_t a = swz(smem_u32(qs + (cg >> 3) * 2048), r, cg & 7);
+        asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w));
+      }
+      if (fused && x.valid - 1 >= x.t0 && x.valid - 1 < x.t1) {
+        // append this step's rotated k and its v to the cache; patch k into the loaded tile
+        const int kpos = x.valid - 1;
+        const int tile = (kpos - x.t0) / kDaTile, trow = (kpos - x.t0) % kDaTile;
+        const long long crow =
+            (p.layer_row0 + (long long)x.b * p.T + kpos) * ((long long)p.Hkv * HD) + (long long)x.kvh * HD;
+        uint4 k8 = make_uint4(0, 0, 0, 0);
+        const int j0 = threadIdx.x * 8;
+        if (j0 < HD) {
+          k8 = rope8(qkv_row + (long long)(p.Hq + x.kvh) * HD, j0, HD, p.rd, p.cos, p.sin, pos);
+          const uint4 v8 = *reinterpret_cast<const uint4*>(qkv_row + (long long)(p.Hq + p.Hkv + x.kvh) * HD + j0);
+          *reinterpret_cast<uint4*>(p.k_cache + crow + j0) = k8;
+          *reinterpret_cast<uint4*>(p.v_cache + crow + j0) = v8;
+        }
+        const bool landed = mbar_wait_bounded(&sb[tile], par);
+        if (!landed) {
+          set_status(p.status, JX_ERR_TIMEOUT);
+          items[2] = 0;
+        }
+        if (landed && j0 < HD) {
+          const uint32_t a = swz(smem_u32(tiles + tile * C::TILE_BYTES + (j0 >> 6) * 8192), trow, (j0 & 63) >> 3);
+          asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(k8.x), "r"(k8.y), "r"(k8.z), "r"(k8.w));
+        }
+      }
+      __syncthreads();
+      float sv[2][2][4];
+      float mrow[2] = {-INFINITY, -INFINITY};
+      bool ok = items[2] != 0;
+#pragma unroll
+      for (int i = 0; i < 2; ++i) {
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) sv[i][nt][e] = -INFINITY;
+        if (i >= x.n_tiles || !ok) continue;
+        if (!mbar_wait_bounded(&sb[i], par)) {
+          set_status(p.status, JX_ERR_TIMEOUT);
+          ok = false;
+          continue;
+        }
+        float acc[2][4] = {};
+        const uint32_t kb = smem_u32(tiles + i * C::TILE_BYTES);
+#pragma unroll
+        for (int ks = 0; ks < HD / 16; ++ks) {
+          uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
+          {
+            const int row = (mi & 1) * 8 + r8, ch = ks * 2 + (mi >> 1);
+            ldsm_x4(swz(smem_u32(qs + (ch >> 3) * 2048), row, ch & 7), a0, a1, a2, a3);
+          }
+          {
+            const int row = warp * 16 + (mi >> 1) * 8 + r8, ch = ks * 2 + (mi & 1);
+            ldsm_x4(swz(kb + (ch >> 3) * 8192, row, ch & 7), b0, b1, b2, b3);
+          }
+          mma_bf16(acc[0], a0, a1, a2, a3, b0, b1);
+          mma_bf16(acc[1], a0, a1, a2, a3, b2, b3);
+        }
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int t = x.t0 + i * kDaTile + warp * 16 + nt * 8 + (lane & 3) * 2 + (e & 1);
+            if (t < x.t1) {
+              const float v = rnd<bf16>(rnd<bf16>(acc[nt][e]) * p.scale_bf16);
+              sv[i][nt][e] = v;
+              mrow[e >> 1] = fmaxf(mrow[e >> 1], v);
+            }
+          }
+      }
+      ok = __syncthreads_and(ok) != 0;
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        mrow[h] = fmaxf(mrow[h], __shfl_xor_sync(0xffffffffu, mrow[h], 1));
+        mrow[h] = fmaxf(mrow[h], __shfl_xor_sync(0xffffffffu, mrow[h], 2));
+      }
+      if ((lane & 3) == 0) {
+        red[warp * 16 + r_lo] = mrow[0];
+        red[warp * 16 + r_hi] = mrow[1];
+      }
+      __syncthreads();
+      float m[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int row = r_lo + h * 8;
+        m[h] = fmaxf(fmaxf(red[row], red[16 + row]), fmaxf(red[32 + row], red[48 + row]));
+      }
+      __syncthreads();
+      float l[2] = {0.f, 0.f};
+      const long long sc_row = ((long long)x.b * p.Hq + x.kvh * p.n_rep) * p.T;
+#pragma unroll
+      for (int i = 0; i < 2; ++i)
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int row = r_lo + (e >> 1) * 8;
+            const int t = x.t0 + i * kDaTile + warp * 16 + nt * 8 + (lane & 3) * 2 + (e & 1);
+            if (t < x.t1 && row < p.n_rep) {
+              const float v = sv[i][nt][e];
+              p.sc[sc_row + (long long)row * p.T + t] = v;
+              l[e >> 1] += expf(v - m[e >> 1]);
+            }
+          }
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        l[h] += __shfl_xor_sync(0xffffffffu, l[h], 1);
+        l[h] += __shfl_xor_sync(0xffffffffu, l[h], 2);
+      }
+      if ((lane & 3) == 0) {
+        red[warp * 16 + r_lo] = l[0];
+        red[warp * 16 + r_hi] = l[1];
+      }
+      __syncthreads();
+      if (warp == 0 && (lane & 3) == 0) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int row = r_lo + h * 8;
+          if (row < p.n_rep) {
+            float* st = p.stats + (((long long)x.b * p.Hq + x.kvh * p.n_rep + row) * p.n_splits + x.split) * 2;
+            st[0] = m[h];
+            st[1] = (red[row] + red[16 + row]) + (red[32 + row] + red[48 + row]);
+          }
+        }
+      }
+      __threadfence();
+      __syncthreads();
+      // counted done even after a timeout (the status is set), so the group's pv items do not wait
+      if (threadIdx.x == 0) atomicAdd(&scored[g], 1);
+    } else {
+      // ---------------- pv item (the pv kernel's work on one split) ----------------
+      if (threadIdx.x == 0) {
+        bool ok = true;
+        if (ld_acquire_gpu(&scored[g]) < x.n_active) {
+          const uint64_t w0 = globaltimer_ns();
+          while (ld_acquire_gpu(&scored[g]) < x.n_active) {
+            if (globaltimer_ns() - w0 > kWaitLimitNs) {
+              set_status(p.status, JX_ERR_TIMEOUT);
+              ok = false;
+              break;
+            }
+          }
+        }
+        const int lt = slot ? late1 : late0;
+        if (lt >= 0) {
+          // this step's value was written by a score item of this kernel: order it before the copy
+          fence_proxy_async_global();
+          issue_tile(x, slot, lt);
+          if (slot) late1 = -1;
+          else late0 = -1;
+        }
+        items[2] = ok ? 1 : 0;
+      }
+      __syncthreads();
+      bool ok = items[2] != 0;
+      if (threadIdx.x < 16) {
+        const int row = threadIdx.x;
+        float M = -INFINITY, L = 0.f;
+        if (row < p.n_rep) {
+          const float* st = p.stats + ((long long)x.b * p.Hq + x.kvh * p.n_rep + row) * p.n_splits * 2;
+          for (int s2 = 0; s2 < x.n_active; ++s2) M = fmaxf(M, __ldcg(st + s2 * 2));
+          for (int s2 = 0; s2 < x.n_active; ++s2) L += __ldcg(st + s2 * 2 + 1) * expf(__ldcg(st + s2 * 2) - M);
+        }
+        Ms[row] = M;
+        Ls[row] = L;
+      }
+      __syncthreads();
+      for (int idx = threadIdx.x; idx < 16 * kDaKeys; idx += 128) {
+        const int row = idx / kDaKeys, k = idx % kDaKeys, t = x.t0 + k;
+        float pv = 0.f;
+        if (row < p.n_rep && t < x.t1) {
+          const float sc = __ldcg(p.sc + ((long long)x.b * p.Hq + x.kvh * p.n_rep + row) * p.T + t);
+          pv = rnd<bf16>(expf(sc - Ms[row]) / Ls[row]);
+        }
+        ptile[row * kPLd + k] = __float2bfloat16_rn(pv);
+      }
+      __syncthreads();
+      float acc[NT][4] = {};
+      for (int i = 0; i < x.n_tiles; ++i) {
+        if (!mbar_wait_bounded(&sb[i], par)) {
+          set_status(p.status, JX_ERR_TIMEOUT);
+          ok = false;
+          break;
+        }
+        if (!ok) continue;
+        const uint32_t vb = smem_u32(tiles + i * C::TILE_BYTES);
+#pragma unroll
+        for (int kk = 0; kk < kDaTile / 16; ++kk) {
+          uint32_t a0, a1, a2, a3;
+          {
+            const int row = (mi & 1) * 8 + r8, col = i * kDaTile + kk * 16 + (mi >> 1) * 8;
+            ldsm_x4(smem_u32(ptile + row * kPLd + col), a0, a1, a2, a3);
+          }
+#pragma unroll
+          for (int n16 = 0; n16 < NT / 2; ++n16) {
+            uint32_t b0, b1, b2, b3;
+            const int row = kk * 16 + (mi & 1) * 8 + r8;
+            const int ch = (warp * WCOLS) / 8 + n16 * 2 + (mi >> 1);
+            ldsm_x4_t(swz(vb + (ch >> 3) * 8192, row, ch & 7), b0, b1, b2, b3);
+            mma_bf16(acc[n16 * 2], a0, a1, a2, a3, b0, b1);
+            mma_bf16(acc[n16 * 2 + 1], a0, a1, a2, a3, b2, b3);
+          }
+        }
+      }
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int row = (e >> 1) ? r_hi : r_lo;
+          const int col = warp * WCOLS + nt * 8 + (lane & 3) * 2 + (e & 1);
+          if (row < p.n_rep)
+            p.opart[(((long long)x.b * p.Hq + x.kvh * p.n_rep + row) * p.n_splits + x.split) * HD + col] = acc[nt][e];
+        }
+      __threadfence();
+      __syncthreads();
+      if (threadIdx.x == 0) items[3] = atomicAdd(&p.counters[g], 1) == x.n_active - 1;
+      __syncthreads();
+      if (items[3]) {
+        __threadfence();
+        for (int idx = threadIdx.x; idx < p.n_rep * HD; idx += 128) {
+          const int row = idx / HD, col = idx % HD;
+          const float* src = p.opart + (((long long)x.b * p.Hq + x.kvh * p.n_rep + row) * p.n_splits) * HD + col;
+          float sum = 0.f;
+          for (int s2 = 0; s2 < x.n_active; ++s2) sum += __ldcg(src + (long long)s2 * HD);
+          const long long ocol = (long long)(x.kvh * p.n_rep + row) * HD + col;
+          p.out[k128_offset(x.b, ocol, p.out_rp)] = __float2bfloat16_rn(sum);
+        }
+        if (threadIdx.x == 0) {
+          p.counters[g] = 0;
+          scored[g] = 0;
+        }
+      }
+    }
+    phases ^= 1u << slot;
+    if (threadIdx.x == 0) items[2] = 1;
+    __syncthreads();   // the slot is free; the next item's claim is visible
+    slot ^= 1;
+    cur = items[slot];
+  }
+  if (threadIdx.x == 0 && atomicAdd(done_ctas, 1) == (int)gridDim.x - 1) {
+    // every CTA has made its last claim: reset the queue for the next call
+    *claim_ctr = 0;
+    *done_ctas = 0;
+  }
+}
+
 // ------------------------------------------------------------------------------------------------
 // host side
 // ------------------------------------------------------------------------------------------------
@@ -1130,11 +1548,13 @@ int make_tmap_2d_bf16(CUtensorMap* map, const void* base, long long rows, long l
   return make_tmap_2d_bf16_box(map, base, rows, cols, row_stride_elems, 64);
 }
 
+// scores [B, Hq, T], split statistics [B, Hq, n_splits, 2], split partials [B, Hq, n_splits, hd] (float32),
+// then the queue form's counters (2 + B * Hkv ints; B * Hq bounds B * Hkv).
 long long dattn_workspace_bytes(int B, int Hq, int T, int hd, int n_splits) {
   const long long sc = (long long)B * Hq * T;
   const long long st = (long long)B * Hq * n_splits * 2;
   const long long op = (long long)B * Hq * n_splits * hd;
-  return (sc + st + op) * 4;
+  return (sc + st + op) * 4 + (2 + (long long)B * Hq) * 4;
 }
 
 int dattn_n_splits(int T, int window) {
@@ -1257,6 +1677,36 @@ static int launch_dattn_csplit(const CUtensorMap& km, const CUtensorMap& vm, con
   return launch_ex(&cfg, dattn_csplit_kernel<HD>, km, vm, p) == cudaSuccess ? JX_OK : JX_ERR_CUDA;
 }
 
+template <int HD>
+static int launch_dattn_queue(const CUtensorMap& km, const CUtensorMap& vm, const DAttnParams& p, bool pdl,
+                              cudaStream_t s) {
+  using C = DqCfg<HD>;
+  static int per_sm = 0, sms = 0;
+  if (!per_sm) {
+    if (cudaFuncSetAttribute(dattn_queue_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::BYTES) !=
+        cudaSuccess)
+      return JX_ERR_CUDA;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, dattn_queue_kernel<HD>, 128, C::BYTES) != cudaSuccess)
+      return JX_ERR_CUDA;
+    if (per_sm < 1) per_sm = 1;
+  }
+  const long long items = 2LL * p.B * p.Hkv * p.n_splits;
+  const long long cap = (long long)per_sm * sms;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(items < cap ? items : cap));
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = C::BYTES;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return launch_ex(&cfg, dattn_queue_kernel<HD>, km, vm, p) == cudaSuccess ? JX_OK : JX_ERR_CUDA;
+}
+
 // 0: by shape (the split form), 1: split form (split pv), 2: single-pass form, 3: split scores + column
 // pv, 4: cluster-split form (key ranges up to 16 splits of 128 keys).  No alternative is chosen by
 // shape: the cluster-split form measured 23.1 / 50.3 us against 17.6 / 43.5 us for the split form at
@@ -1273,8 +1723,8 @@ int run_decode_attention(const jx_dattn_args& a, bool pdl, cudaStream_t stream) 
   if (n_rep > 16) return JX_ERR_SHAPE;
   if (a.hd != 64 && a.hd != 128 && a.hd != 256) return JX_ERR_SHAPE;
   if (a.qkv) {
-    // fused RoPE + append: the split form only; 16-byte rows of the projection output and tables
-    if (g_dattn_impl >= 2) return JX_ERR_UNSUPPORTED;
+    // fused RoPE + append: the split and queue forms; 16-byte rows of the projection output and tables
+    if (g_dattn_impl >= 2 && g_dattn_impl != 5) return JX_ERR_UNSUPPORTED;
     if (!a.cos || !a.sin || a.rd <= 0 || a.rd > a.hd || (a.rd & 1) || a.max_pos <= 0 ||
         a.ld_qkv < (long long)(a.Hq + 2 * a.Hkv) * a.hd || (a.ld_qkv & 7) || (reinterpret_cast<uintptr_t>(a.qkv) & 15))
       return JX_ERR_ARG;
@@ -1349,6 +1799,14 @@ int run_decode_attention(const jx_dattn_args& a, bool pdl, cudaStream_t stream) 
   p.max_pos = a.max_pos;
   p.k_cache = reinterpret_cast<bf16*>(const_cast<void*>(a.k_base));
   p.v_cache = reinterpret_cast<bf16*>(const_cast<void*>(a.v_base));
+  p.qsync = reinterpret_cast<int*>(p.opart + (long long)a.B * a.Hq * n_splits * a.hd);
+  if (g_dattn_impl == 5) {
+    switch (a.hd) {
+      case 64: return launch_dattn_queue<64>(km, vm, p, pdl, stream);
+      case 128: return launch_dattn_queue<128>(km, vm, p, pdl, stream);
+      default: return launch_dattn_queue<256>(km, vm, p, pdl, stream);
+    }
+  }
   if (g_dattn_impl == 4) {
     if (n_splits > 16) return JX_ERR_SHAPE;
     switch (a.hd) {

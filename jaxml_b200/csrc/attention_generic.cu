@@ -32,48 +32,55 @@ __global__ void __launch_bounds__(128) attention_generic_kernel(AttnArgs p) {
   const T* V = reinterpret_cast<const T*>(p.v);
   const float scale_t = rnd<T>(p.scale);
   float* red = sc + p.T;
+  // Keys that can be visible: [j_lo, j_hi).  Every key outside is masked, so the loops below stay on this
+  // range unless the whole row is masked (then every one of the T slots gets the same probability).
+  int j_hi = valid, j_lo = 0;
+  if (p.causal && anchor + 1 < j_hi) j_hi = anchor + 1;
+  if (p.window > 0 && anchor - p.window + 1 > j_lo) j_lo = anchor - p.window + 1;
+  if (j_hi < j_lo) j_hi = j_lo;
+  const int warp = tid >> 5, lane = tid & 31;
 
+  // scores: a warp per key, lanes over the head dimension
   float mx = -INFINITY;
-  for (int j = tid; j < p.T; j += 128) {
-    bool ok = j < valid;
-    if (p.causal && j > anchor) ok = false;
-    if (p.window > 0 && j < anchor - p.window + 1) ok = false;
-    float x = -INFINITY;
-    if (ok) {
-      const T* kr = K + (((long long)b * p.T + j) * p.Hkv + kvh) * p.hd;
-      float dot = 0.f;
-      for (int d = 0; d < p.hd; ++d) dot += to_f(q[d]) * to_f(kr[d]);
-      x = rnd<T>(rnd<T>(dot) * scale_t);
-      mx = fmaxf(mx, x);
-    }
-    sc[j] = x;
+  for (int j = j_lo + warp; j < j_hi; j += 4) {
+    const T* kr = K + (((long long)b * p.T + j) * p.Hkv + kvh) * p.hd;
+    float dot = 0.f;
+    for (int d = lane; d < p.hd; d += 32) dot += to_f(q[d]) * to_f(kr[d]);
+    for (int o = 16; o > 0; o >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+    const float x = rnd<T>(rnd<T>(dot) * scale_t);
+    mx = fmaxf(mx, x);
+    if (lane == 0) sc[j] = x;
   }
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  if ((tid & 31) == 0) red[tid >> 5] = mx;
+  if (lane == 0) red[warp] = mx;
   __syncthreads();
   mx = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
   const bool all_masked = (mx == -INFINITY);
+  if (all_masked) {
+    j_lo = 0;
+    j_hi = p.T;
+  }
   __syncthreads();
   float l = 0.f;
-  for (int j = tid; j < p.T; j += 128) {
-    const float e = all_masked ? 1.0f : (sc[j] == -INFINITY ? 0.f : expf(sc[j] - mx));
+  for (int j = j_lo + tid; j < j_hi; j += 128) {
+    const float e = all_masked ? 1.0f : expf(sc[j] - mx);
     sc[j] = e;
     l += e;
   }
   for (int o = 16; o > 0; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-  if ((tid & 31) == 0) red[tid >> 5] = l;
+  if (lane == 0) red[warp] = l;
   __syncthreads();
   l = (red[0] + red[1]) + (red[2] + red[3]);
-  for (int j = tid; j < p.T; j += 128) sc[j] = rnd<T>(sc[j] / l);
-  if (p.weights) {
-    // the probabilities themselves (Attention.mha with output_attentions): [B, Hq, S, T]
-    T* w = reinterpret_cast<T*>(p.weights) + (((long long)b * p.Hq + h) * p.S + s) * p.T;
-    for (int j = tid; j < p.T; j += 128) w[j] = from_f<T>(sc[j]);
-  }
+  for (int j = j_lo + tid; j < j_hi; j += 128) sc[j] = rnd<T>(sc[j] / l);
   __syncthreads();
+  if (p.weights) {
+    // the probabilities themselves (Attention.mha with output_attentions): [B, Hq, S, T], zero where masked
+    T* w = reinterpret_cast<T*>(p.weights) + (((long long)b * p.Hq + h) * p.S + s) * p.T;
+    for (int j = tid; j < p.T; j += 128) w[j] = from_f<T>(j >= j_lo && j < j_hi ? sc[j] : 0.f);
+  }
   for (int d = tid; d < p.hd; d += 128) {
     float acc = 0.f;
-    for (int j = 0; j < p.T; ++j) {
+    for (int j = j_lo; j < j_hi; ++j) {
       const float pj = sc[j];
       if (pj != 0.f) acc += pj * to_f(V[(((long long)b * p.T + j) * p.Hkv + kvh) * p.hd + d]);
     }

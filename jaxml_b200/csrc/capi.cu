@@ -25,6 +25,7 @@ void set_gemm_tile_group(int gm);
 int run_prefill_attention(const jx_pattn_args& a, bool pdl, cudaStream_t stream);
 long long dattn_workspace_bytes(int B, int Hq, int T, int hd, int n_splits);
 int dattn_n_splits(int T, int window);
+int run_filter_logits(const jx_filter_args& p, cudaStream_t stream);
 int run_sample_finalize(const jx_sample_args& p, const unsigned long long* gathered, int n_shards,
                         cudaStream_t stream);
 
@@ -250,9 +251,9 @@ int jx_set_prefill_linear_impl(int impl) {
 }
 
 int jx_set_decode_attention_impl(int impl) {
-  if (impl < 0 || impl > 4)
-    return fail(JX_ERR_ARG,
-                "jx_set_decode_attention_impl: 0 (by shape), 1 (split), 2 (cluster), 3 (column pv), 4 (cluster-split)");
+  if (impl < 0 || impl > 5)
+    return fail(JX_ERR_ARG, "jx_set_decode_attention_impl: 0 (by shape), 1 (split), 2 (cluster), 3 (column pv), "
+                            "4 (cluster-split), 5 (queue)");
   set_dattn_impl(impl);
   return JX_OK;
 }
@@ -263,6 +264,15 @@ int jx_prefill_attention(const jx_pattn_args* args, int pdl, void* stream) {
   const int rc = run_prefill_attention(*args, pdl != 0, (cudaStream_t)stream);
   if (rc == JX_ERR_CUDA) return note_cuda("jx_prefill_attention");
   if (rc != JX_OK) return fail(rc, "jx_prefill_attention: head_dim must be 64/128/256, Hq % Hkv == 0, S <= T");
+  return JX_OK;
+}
+
+int jx_filter_logits(const jx_filter_args* args, void* stream) {
+  if (!args || !args->logits || !args->out) return fail(JX_ERR_ARG, "jx_filter_logits: null pointer");
+  const int rc = run_filter_logits(*args, (cudaStream_t)stream);
+  if (rc == JX_ERR_CUDA) return note_cuda("jx_filter_logits");
+  if (rc == JX_ERR_DTYPE) return fail(rc, "jx_filter_logits: logits must be float32 or bfloat16");
+  if (rc != JX_OK) return fail(rc, "jx_filter_logits: B <= 8191, 0 < V <= 393216 and V <= each leading dimension");
   return JX_OK;
 }
 

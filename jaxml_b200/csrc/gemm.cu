@@ -232,9 +232,125 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(const float* __restrict__
   run_epilogue<float>(e, m0, kF32BM, n0, kF32BN, [&](int m, int j) { return ct[m][j]; }, tid, 256);
 }
 
+// float32 projection for up to 64 token rows (decode steps, short prompts).  The tiled kernel above gives a decode-sized M only N / 128
+// CTAs, each streaming its whole K x 128 panel with synchronous loads.  Here a CTA owns NC output columns
+// (lane = column, so each W row segment is one coalesced 128-byte load per 32 columns; NC = 64 keeps a
+// GLU epilogue's 32 gate + 32 up columns together) and a K slice; the CS CTAs of one column tile form a
+// thread-block cluster over K.  Sums are deterministic: each warp sums its K range in order, the 8 warps
+// are added in warp order, then rank 0 adds the cluster's CTAs in rank order through distributed shared
+// memory and runs the epilogue.  Rows come in blocks of 16 (grid y), each block reading W again (from
+// L2 at these sizes).  Plain float32 FMA, no TF32.
+constexpr int kF32vWarps = 8;
+
+template <int NC>
+__global__ void __launch_bounds__(kF32vWarps * 32) gemv_f32_kernel(const float* __restrict__ X, long long ldx,
+                                                                   const float* __restrict__ W, int M, int N, int K,
+                                                                   EpiParams e) {
+  constexpr int CPL = NC / 32;   // columns per lane
+  __shared__ float red[kF32vWarps][16][NC + 1];
+  __shared__ float fin[16][NC + 1];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int CS = (int)cluster_nctarank(), rank = (int)cluster_ctarank();
+  const long long n0 = (long long)(blockIdx.x / CS) * NC;
+  const int m0 = blockIdx.y * 16;
+  X += (long long)m0 * ldx;
+  M = M - m0 < 16 ? M - m0 : 16;
+  const int q = rank * kF32vWarps + warp, nq = CS * kF32vWarps;
+  const int k0 = (int)((long long)K * q / nq), k1 = (int)((long long)K * (q + 1) / nq);
+  bool col_ok[CPL];
+#pragma unroll
+  for (int c = 0; c < CPL; ++c) col_ok[c] = n0 + c * 32 + lane < N;
+  // the weights do not depend on the previous kernel: pull this warp's rows towards L2 before waiting on it
+  for (int k = k0 + lane; k < k1; k += 32) prefetch_l2(W + (long long)k * N + n0);
+  pdl_trigger();
+  pdl_wait();
+  float acc[16][CPL];
+#pragma unroll
+  for (int m = 0; m < 16; ++m)
+#pragma unroll
+    for (int c = 0; c < CPL; ++c) acc[m][c] = 0.f;
+#pragma unroll 8
+  for (int k = k0; k < k1; ++k) {
+    float wv[CPL];
+#pragma unroll
+    for (int c = 0; c < CPL; ++c) wv[c] = col_ok[c] ? __ldg(W + (long long)k * N + n0 + c * 32 + lane) : 0.f;
+#pragma unroll
+    for (int m = 0; m < 16; ++m)
+      if (m < M) {
+        const float xv = __ldg(X + m * ldx + k);
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) acc[m][c] = fmaf(xv, wv[c], acc[m][c]);
+      }
+  }
+#pragma unroll
+  for (int m = 0; m < 16; ++m)
+    if (m < M)
+#pragma unroll
+      for (int c = 0; c < CPL; ++c) red[warp][m][c * 32 + lane] = acc[m][c];
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < M * NC; idx += kF32vWarps * 32) {
+    const int m = idx / NC, j = idx - m * NC;
+    float v = red[0][m][j];
+#pragma unroll
+    for (int w = 1; w < kF32vWarps; ++w) v += red[w][m][j];
+    if (CS == 1)
+      fin[m][j] = v;
+    else
+      red[0][m][j] = v;
+  }
+  if (CS > 1) {
+    cluster_sync_all();   // every CTA's warp sums are in its red[0]
+    if (rank == 0) {
+      const uint32_t base = smem_u32(&red[0][0][0]);
+      for (int idx = threadIdx.x; idx < M * NC; idx += kF32vWarps * 32) {
+        const int m = idx / NC, j = idx - m * NC;
+        const uint32_t off = (uint32_t)((m * (NC + 1) + j) * 4);
+        float v = red[0][m][j];
+        for (int r = 1; r < CS; ++r) v += dsmem_ld_f32(dsmem_map(base + off, (uint32_t)r));
+        fin[m][j] = v;
+      }
+    }
+    cluster_sync_all();   // no CTA leaves while rank 0 may still read its shared memory
+    if (rank != 0) return;
+  } else {
+    __syncthreads();
+  }
+  run_epilogue<float>(e, m0, 16, n0, NC, [&](int m, int j) { return fin[m][j]; }, threadIdx.x, kF32vWarps * 32);
+}
+
+template <int NC>
+static int launch_gemv_f32(const float* X, long long ldx, const float* W, int M, int N, int K, const EpiParams& e,
+                           bool pdl, cudaStream_t stream) {
+  const int tiles = (N + NC - 1) / NC;
+  // enough CTAs for two per SM, at most 8 per cluster (portable), at least 8 K steps per warp
+  const int mb = (M + 15) / 16;
+  int cs = (2 * 148 + tiles * mb - 1) / (tiles * mb);
+  cs = cs > 8 ? 8 : cs;
+  while (cs > 1 && K < cs * kF32vWarps * 8) --cs;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(tiles * cs), (unsigned)mb);
+  cfg.blockDim = dim3(kF32vWarps * 32);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cs;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 2 : 1;
+  return launch_ex(&cfg, gemv_f32_kernel<NC>, X, ldx, W, M, N, K, e) == cudaSuccess ? JX_OK : JX_ERR_CUDA;
+}
+
 int run_gemm_f32(const float* X, long long ldx, const float* W, int M, int N, int K, const EpiParams& e, bool pdl,
                  cudaStream_t stream) {
   if (M <= 0 || N <= 0 || K <= 0) return JX_ERR_SHAPE;
+  if (M <= 64) {
+    const bool glu = e.kind == JX_EPI_GLU_SILU || e.kind == JX_EPI_GLU_GELU_TANH;
+    return glu ? launch_gemv_f32<64>(X, ldx, W, M, N, K, e, pdl, stream)
+               : launch_gemv_f32<32>(X, ldx, W, M, N, K, e, pdl, stream);
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((N + kF32BN - 1) / kF32BN, (M + kF32BM - 1) / kF32BM);
   cfg.blockDim = dim3(256);

@@ -475,12 +475,13 @@ class Engine:
                  top_p: float = 1.0, min_p: float = 0.0, temperature: float = 1.0, fuse_decoding: bool = False,
                  include_prompt: bool = True):
         """Greedy / temperature generation on the GPU; returns int32 tokens ``[B, P*include_prompt + N]``
-        on the host.  ``fuse_decoding`` is accepted: every decode step is already one CUDA-graph replay."""
+        on the host.  ``fuse_decoding`` replays the decode loop as CUDA graphs of several steps each (the
+        reference compiles it as one scan) instead of one graph replay per step; the tokens are the same."""
         seed = normalize_count("seed", seed)
         max_new_tokens = normalize_count("max_new_tokens", max_new_tokens)
         if max_new_tokens < 0:
             raise ValueError(f"max_new_tokens must be non-negative, got {max_new_tokens}.")
-        normalize_bool("fuse_decoding", fuse_decoding)
+        fuse_decoding = normalize_bool("fuse_decoding", fuse_decoding)
         include_prompt = normalize_bool("include_prompt", include_prompt)
         prompt, mask = self._prepare_generation_inputs(prompt_tokens, attention_mask)
         vocab = self.model.config.vocab_size
@@ -501,7 +502,7 @@ class Engine:
         pin = prompt.pin_memory() if not prompt.is_cuda else prompt
         ids_d = pin.to(dev, non_blocking=True)
         mask_d = (torch.ones(B, P, dtype=torch.bool) if mask is None else mask).pin_memory().to(dev, non_blocking=True)
-        toks = rt.generate(ids_d, mask_d, max_new_tokens, method.use_greedy, sp.temp, seed)
+        toks = rt.generate(ids_d, mask_d, max_new_tokens, method.use_greedy, sp.temp, seed, fuse=fuse_decoding)
         out = toks.to("cpu")
         rt.check_status()
         self.last_rng = rt.rng_key()

@@ -371,6 +371,8 @@ class DecoderRuntime:
             self.attn_ws = torch.zeros((nb.value + 3) // 4, dtype=torch.float32, device=dev)
             self.attn_counters = torch.zeros(B * w.Hkv, dtype=torch.int32, device=dev)
         self.graph = None
+        # fuse_decoding: a graph of several consecutive decode steps, keyed like self.graph plus the count
+        self.graph_multi = None
         # the persistent decode-step kernel's plan when it runs this runtime's layers (else None)
         self.fused_step = None
         self._launches = 0
@@ -824,6 +826,7 @@ class DecoderRuntime:
         if self.tokens_out is None or self.tokens_out.shape[1] < n_tokens:
             self.tokens_out = torch.zeros(self.B, max(n_tokens, 1), dtype=torch.int32, device=self.w.device)
             self.graph = None
+            self.graph_multi = None
         self.status.zero_()
 
     def prefill(self, ids: torch.Tensor, greedy: bool, temp: float):
@@ -909,27 +912,40 @@ class DecoderRuntime:
         """libjxb200 kernel launches in one decode step (counted while the step was issued)."""
         return self.launches_last_step
 
-    def capture_decode(self, greedy: bool, temp: float):
-        """Captures one decode step in a CUDA graph (run one eager step first to warm up)."""
-        key = (greedy, float(temp), self.filters)
-        if self.graph is not None and self.graph[0] == key:
-            return self.graph[1]
+    # decode steps per graph under fuse_decoding (one replay per 16 tokens)
+    fused_steps = 16
+
+    def capture_decode(self, greedy: bool, temp: float, steps: int = 1):
+        """Captures `steps` consecutive decode steps in one CUDA graph (run one eager step first to warm
+        up).  Every step reads its position, step index and key from device memory, so one graph of n
+        steps replays n steps of the sequence."""
+        key = (greedy, float(temp), self.filters, steps)
+        slot = self.graph if steps == 1 else self.graph_multi
+        if slot is not None and slot[0] == key:
+            return slot[1]
         g = torch.cuda.CUDAGraph()
         s = torch.cuda.Stream(self.w.device)
         s.wait_stream(torch.cuda.current_stream(self.w.device))
         with torch.cuda.stream(s):
             with torch.cuda.graph(g, stream=s):
-                self.decode_step(greedy, temp)
+                for _ in range(steps):
+                    self.decode_step(greedy, temp)
         torch.cuda.current_stream(self.w.device).wait_stream(s)
-        self.graph = (key, g)
+        if steps == 1:
+            self.graph = (key, g)
+        else:
+            self.graph_multi = (key, g)
         return g
 
-    def generate(self, prompt: torch.Tensor, mask: torch.Tensor, n_new: int, greedy: bool, temp: float, seed: int):
+    def generate(self, prompt: torch.Tensor, mask: torch.Tensor, n_new: int, greedy: bool, temp: float, seed: int,
+                 fuse: bool = False):
         """Prefill + (n_new - 1) decode steps on the device; returns device tokens [B, n_new].
 
-        The first decode step runs eagerly (it also warms every kernel up); the rest replay one captured
-        CUDA graph.  Key flow as _generate.py: key = PRNGKey(seed); key, sub = split(key) before the
-        first sample, and one split per decode step on the device.
+        The first decode step runs eagerly (it also warms every kernel up); the rest replay a captured
+        CUDA graph of one step, or with `fuse` (the reference's fuse_decoding: the decode loop compiled
+        as one scan, _generate.py:365-380) a graph of `fused_steps` steps, the remainder on the one-step
+        graph.  Key flow as _generate.py: key = PRNGKey(seed); key, sub = split(key) before the first
+        sample, and one split per decode step on the device.
         """
         from . import prng
 
@@ -938,9 +954,16 @@ class DecoderRuntime:
         self.prefill(prompt, greedy, temp)
         if n_new > 1:
             self.decode_step(greedy, temp)
-        if n_new > 2:
+        rest = max(n_new - 2, 0)
+        if fuse and rest >= 2:
+            k = min(self.fused_steps, rest)
+            g = self.capture_decode(greedy, temp, k)
+            for _ in range(rest // k):
+                g.replay()
+            rest %= k
+        if rest:
             g = self.capture_decode(greedy, temp)
-            for _ in range(n_new - 2):
+            for _ in range(rest):
                 g.replay()
         return self.tokens_out[:, :n_new]
 
@@ -955,4 +978,5 @@ class DecoderRuntime:
             self.sample_counters.zero_()
             if self.fast_attn:
                 self.attn_counters.zero_()
+                self.attn_ws.zero_()   # (the queue form's claim counters live in its tail)
             raise N.NativeError(f"device status {st} ({N.STATUS_NAMES.get(st, st)}) during generation")

@@ -2,11 +2,13 @@
 
 The selection logic (``normalize_sampling_params`` clipping and warnings, ``SamplingMethod.from_values``)
 runs on the host; the selected method runs on the GPU: greedy argmax and temperature sampling in
-``csrc/sample.cu``, preceded for min-p / top-k / top-p by ``filter_logits_`` (``sampling.py:34-72``,
-applied in the reference's order min-p, top-k, top-p) on the device logits.  The reference's public
-functions (``top_k_filtering``, ``top_p_filtering``, ``min_p_filtering``, ``greedy_fn``,
-``SamplingMethod.get_sampling_fn``) are here too, with its checks, on torch tensors; their categorical
-draw is the sampling kernel.
+``csrc/sample.cu``, preceded for min-p / top-k / top-p by ``filter_logits_`` (``sampling.py:34-75``,
+applied in the reference's order min-p, top-k, top-p), which runs CUDA float32 / bfloat16 logits through
+the filter kernel (``csrc/filter.cu``, ``jx_filter_logits``).  The reference's public functions
+(``top_k_filtering``, ``top_p_filtering``, ``min_p_filtering``, ``greedy_fn``,
+``SamplingMethod.get_sampling_fn``) are here too, with its checks, on torch tensors: CUDA float32 /
+bfloat16 logits through the same kernel, host tensors through torch ops; their categorical draw is the
+sampling kernel.
 """
 from __future__ import annotations
 
@@ -153,11 +155,41 @@ def _keep_top_p(x: torch.Tensor, top_p: float) -> torch.Tensor:
     return x.masked_fill(x.float() < torch.gather(srt, -1, idx), float("-inf"))
 
 
+def _on_kernel(x: torch.Tensor) -> bool:
+    return x.device.type == "cuda" and x.dtype in (torch.float32, torch.bfloat16)
+
+
+def _filter_kernel(x: torch.Tensor, out: torch.Tensor | None, top_k: int, top_p: float,
+                   min_p: float) -> torch.Tensor:
+    """``jx_filter_logits`` over the rows of CUDA ``x`` [..., V] into ``out`` (a new tensor when None)."""
+    from . import _native as N
+
+    V = x.shape[-1]
+    rows = x.numel() // V
+    xc = x.reshape(rows, V)
+    if xc.stride(-1) != 1 or (rows > 1 and xc.stride(0) < V):
+        xc = xc.contiguous()
+    o = torch.empty_like(xc) if out is None else out.reshape(rows, V)
+    if o.stride(-1) != 1 or (rows > 1 and o.stride(0) < V):
+        raise ValueError("filter output rows must be contiguous.")
+    a = N.JxFilterArgs()
+    a.B, a.V = rows, V
+    a.logits, a.ld_in = xc.data_ptr(), xc.stride(0) if rows > 1 else V
+    a.out, a.ld_out = o.data_ptr(), o.stride(0) if rows > 1 else V
+    a.dtype = N.JX_BF16 if x.dtype == torch.bfloat16 else N.JX_F32
+    a.top_k = int(min(top_k, 2 ** 31 - 1))
+    a.top_p, a.min_p = float(top_p), float(min_p)
+    N.check(N.load().jx_filter_logits(a, torch.cuda.current_stream(x.device).cuda_stream), "jx_filter_logits")
+    return o.reshape(x.shape) if out is None else out
+
+
 def top_k_filtering(rng, logits, top_k, *args) -> torch.Tensor:
     """Logits below the k-th largest of their row set to -inf (ties kept); ``top_k <= 0`` keeps all."""
     x = _validate_logits(logits)
     k = _normalize_top_k(top_k)
-    return x if k <= 0 else _keep_top_k(x, k)
+    if k <= 0:
+        return x
+    return _filter_kernel(x, None, k, 1.0, 0.0) if _on_kernel(x) else _keep_top_k(x, k)
 
 
 def top_p_filtering(rng, logits, top_k, top_p, min_p, *args) -> torch.Tensor:
@@ -167,6 +199,8 @@ def top_p_filtering(rng, logits, top_k, top_p, min_p, *args) -> torch.Tensor:
     p = _probability("top_p", top_p)
     if p >= 1.0:
         return x
+    if _on_kernel(x):
+        return _filter_kernel(x, None, 0, p, 0.0)
     if p <= 0.0:
         return x.masked_fill(x < x.amax(dim=-1, keepdim=True), float("-inf"))
     return _keep_top_p(x, p)
@@ -175,7 +209,10 @@ def top_p_filtering(rng, logits, top_k, top_p, min_p, *args) -> torch.Tensor:
 def min_p_filtering(rng, logits, top_k, top_p, min_p, *args) -> torch.Tensor:
     """Tokens whose probability is below ``min_p`` set to -inf, unless no token of the row qualifies."""
     x = _validate_logits(logits)
-    return _keep_min_p(x, _probability("min_p", min_p))
+    p = _probability("min_p", min_p)
+    if _on_kernel(x):
+        return x if p <= 0.0 else _filter_kernel(x, None, 0, 1.0, p)
+    return _keep_min_p(x, p)
 
 
 def greedy_fn(rng, logits, *args) -> torch.Tensor:
@@ -240,14 +277,16 @@ def _probs(logits: torch.Tensor) -> torch.Tensor:
 
 
 def filter_logits_(logits: torch.Tensor, out: torch.Tensor, top_k: int, top_p: float, min_p: float) -> torch.Tensor:
-    """min-p, then top-k, then top-p filtering of device logits ``[B, V]`` into ``out`` (filtered entries
-    -inf), inference_engine/sampling.py:34-72.  The reference's own comparisons are kept: min-p keeps
+    """min-p, then top-k, then top-p filtering of logits ``[B, V]`` into ``out`` (filtered entries -inf),
+    inference_engine/sampling.py:34-75.  The reference's own comparisons are kept: min-p keeps
     probabilities >= min_p (unless that keeps nothing in a row), top-k keeps logits >= the k-th largest
     (ties included), top-p keeps logits >= the sorted logit at the count of cumulative probabilities
     below top_p.  Where the reference's JAX arithmetic is not visible from its source: probabilities in
-    float32 rounded to the logits' dtype, the cumulative sum in float32, a cutoff index past the end
-    clamped to the last entry.  Device tensor ops only (capturable in a CUDA graph)."""
-    # (masks with a -inf scalar: no host-to-device copy while a CUDA graph is being captured)
+    float32 rounded to the logits' dtype, a cutoff index past the end clamped to the last entry.  CUDA
+    float32 / bfloat16 logits run through the filter kernel (one launch, capturable in a CUDA graph; its
+    top-p cumulative masses are exact); other tensors through torch ops with a float32 cumulative sum."""
+    if _on_kernel(logits):
+        return _filter_kernel(logits, out, top_k, top_p, min_p)
     x = logits
     if min_p > 0.0:
         x = _keep_min_p(x, min_p)

@@ -94,7 +94,7 @@ def test_linear_decode_glu_resid_bias(impl, M):
     assert (h.double() - ref2).abs().max().item() <= 0.05 * ref2.abs().max().item()
 
 
-@pytest.fixture(params=[2, 1, 3, 4], ids=["cluster", "split", "column", "cluster-split"])
+@pytest.fixture(params=[2, 1, 3, 4, 5], ids=["cluster", "split", "column", "cluster-split", "queue"])
 def attn_form(request):
     N = _n()
     N.call("jx_set_decode_attention_impl", request.param)
@@ -107,7 +107,7 @@ def attn_form(request):
                                                  (128, 32, 8, 0, 20)])
 def test_decode_attention_matches_oracle(attn_form, hd, Hq, Hkv, window, B):
     """Tensor-core decode attention (single-pass cluster form; split scores with the split or the column
-    pv; the cluster-split form) vs the oracle's Attention.mha on a padded cache.
+    pv; the cluster-split form; the queue form) vs the oracle's Attention.mha on a padded cache.
 
     The kernel rounds at the reference's points (scores, scale, probabilities, output), so results agree
     to about one bf16 ulp.  A q.k accumulated in a different order can round to the neighbouring bf16
@@ -150,6 +150,9 @@ def test_decode_attention_matches_oracle(attn_form, hd, Hq, Hkv, window, B):
         N.call("jx_decode_attention", a, 1, _stream())
         torch.cuda.synchronize()
         assert int(status.item()) == 0 and int(cnt.abs().sum().item()) == 0
+        # the queue form's counters (the workspace's last 2 + B * Hq ints) are back at zero
+        tail = ws.view(torch.int32)[(nb.value // 4) - (2 + B * Hq):nb.value // 4]
+        assert int(tail.abs().sum().item()) == 0
         got = torch.empty(B, Hq * hd, dtype=torch.bfloat16, device="cuda")
         N.call("jx_unpack_k128", out.data_ptr(), B, Hq * hd, Mp, got.data_ptr(), N.JX_BF16, Hq * hd, _stream())
         got = got.float().cpu().reshape(B, Hq, hd)
@@ -221,6 +224,17 @@ def test_decode_attention_fused_rope_matches_separate_kernels(hd, Hq, Hkv, rd, B
     out2 = _dattn_call(N, B, Hq, Hkv, hd, T, L, layer, None, k2, v2, pos, fused=(qkv, cos, sin, rd, max_pos))
     assert torch.equal(k1, k2) and torch.equal(v1, v2)
     assert torch.equal(out1, out2)
+    # the queue form: the split form's bits, fused or not, and twice (its claim counters reset themselves)
+    N.call("jx_set_decode_attention_impl", 5)
+    try:
+        for _ in range(2):
+            k3, v3 = kc.clone(), vc.clone()
+            out3 = _dattn_call(N, B, Hq, Hkv, hd, T, L, layer, None, k3, v3, pos, fused=(qkv, cos, sin, rd, max_pos))
+            assert torch.equal(k1, k3) and torch.equal(v1, v3)
+            assert torch.equal(out1, out3)
+            assert torch.equal(out1, _dattn_call(N, B, Hq, Hkv, hd, T, L, layer, q, k1, v1, pos))
+    finally:
+        N.call("jx_set_decode_attention_impl", 0)
     # the other forms do not take the fused inputs
     for form in (2, 3, 4):
         N.call("jx_set_decode_attention_impl", form)
@@ -288,7 +302,7 @@ def test_linear_decode_norm_prologue(impl, kind, M):
             assert torch.equal(out, out_ref)
 
 
-@pytest.mark.parametrize("form", [0, 3], ids=["split", "column"])
+@pytest.mark.parametrize("form", [0, 3, 5], ids=["split", "column", "queue"])
 @pytest.mark.parametrize("T,lens", [(4096, [4096, 2085, 129]), (32768, [32768, 16421])])
 def test_decode_attention_long_context_matches_oracle(form, T, lens):
     """Decode attention at 4k and 32k-key caches (Llama-3-8B heads): the key-split count grows with the

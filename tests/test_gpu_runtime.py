@@ -161,3 +161,32 @@ def test_padded_prompt_matches_oracle(hf_models):
     torch.cuda.synchronize()
     out = O.forward("llama", cfg, params, tok[:, None], torch.float32, kv_caches=out.kv_caches, keep_last_n_logits=1)
     _check_logits(rt.logits_buf()[:B], out.logits[:, 0], torch.float32)
+
+
+@pytest.mark.parametrize("greedy,temp", [(True, 1.0), (False, 0.8)], ids=["greedy", "temp0.8"])
+@pytest.mark.parametrize("n_new", [3, 12, 37])
+def test_fused_decoding_gives_the_same_tokens(n_new, greedy, temp, hf_models):
+    """fuse_decoding (graphs of several decode steps, the remainder on the one-step graph) produces the
+    same tokens and final key as one graph replay per step."""
+    from jaxml_b200.runtime import DecoderRuntime
+
+    _, cfg, params = hf_models["llama"]
+    B, P, T = 3, 9, 256
+    g = torch.Generator().manual_seed(4)
+    ids = torch.randint(0, cfg.vocab_size, (B, P), generator=g, dtype=torch.int32).cuda()
+    mask = torch.ones(B, P, dtype=torch.bool, device="cuda")
+    mask[1, -3:] = False                            # a right-padded row
+    rt = _runtime("llama", cfg, params, torch.float32, B, T)
+    old = DecoderRuntime.fused_steps
+    DecoderRuntime.fused_steps = 16
+    try:
+        runs = []
+        for fuse in (False, True):
+            toks = rt.generate(ids, mask, n_new, greedy, temp, seed=5, fuse=fuse).cpu().clone()
+            torch.cuda.synchronize()
+            rt.check_status()
+            runs.append((toks, rt.rng_key()))
+    finally:
+        DecoderRuntime.fused_steps = old
+    assert torch.equal(runs[0][0], runs[1][0])
+    assert np.array_equal(runs[0][1], runs[1][1])
