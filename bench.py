@@ -139,7 +139,7 @@ def parse():
                     help="new tokens per row of the e2e generation (default: the config's, 256 for l8)")
     ap.add_argument("--tp-pull", action="store_true",
                     help="tensor-parallel decode: separate pull all-reduce kernels instead of the push-fused projections")
-    ap.add_argument("--micro", choices=["gemv", "attn", "gemm", "allreduce", "tpx"], default=None,
+    ap.add_argument("--micro", choices=["gemv", "attn", "gemm", "allreduce", "tpx", "filter", "sweep"], default=None,
                     help="single-kernel microbenchmark on Llama-3-8B layer shapes instead of the decode step")
     ap.add_argument("--ctx", type=int, default=4096, help="context length of --micro attn")
     ap.add_argument("--shape", default="28672,4096", help="N,K of --micro gemv (default: fused gate/up)")
@@ -471,6 +471,47 @@ def gpu_arm(args):
     sbytes, wbytes, kvbytes = step_bytes(cfg, B, ctx_mean, tp, family, elem)
     step_ms_mean = total_ms / args.steps
 
+    # ---- tensor parallelism: the ranks' greedy tokens, a TP=1 run of the same prompt, the exchange cost ----
+    parity, exchange = None, None
+    if dist is not None:
+        toks = rt.tokens_out[:, :n_new].contiguous()
+        gathered = [torch.empty_like(toks) for _ in range(world)]
+        dist.all_gather(gathered, toks)
+        ranks_identical = all(torch.equal(gathered[0], t) for t in gathered)
+        vs1 = None
+        if rank == 0:
+            k = min(n_new, 16)
+            full_w = step_bytes(cfg, B, ctx_first, 1, family, elem)[1]
+            if full_w <= 40e9:
+                params1 = lazy_random_params(family, cfg, seed=0, dtype=dt, device=dev)
+                eng1 = Engine(model, InferenceConfig(tp_size=1), params1, dtype=dt)
+                eng1.init_params(params1)
+                del params1
+                rt1 = eng1._runtime_for(B, engine.buffer_length(P, n_new))
+                t1 = rt1.generate(ids_d, torch.ones(B, P, dtype=torch.bool, device=dev), k, True, 1.0, 0)[:, :k].cpu()
+                rt1.check_status()
+                eq = t1 == gathered[0][:, :k].cpu()
+                first = next((j for j in range(k) if not bool(eq[:, j].all())), None)
+                vs1 = {"tokens": k, "token_match_frac": float(eq.float().mean().item()), "first_divergence_step": first,
+                       "note": "greedy tokens of a TP=1 engine on rank 0's GPU, same weights and prompt; bf16 "
+                               "float32-partial sums in another order can flip a near-tie"}
+                del rt1, eng1
+                torch.cuda.empty_cache()
+            else:
+                vs1 = {"skipped": "the full weights (%.0f GB) are not built beside the shard" % (full_w / 1e9)}
+        dist.barrier()
+        parity = {"ranks_identical": ranks_identical, "tokens": n_new, "vs_tp1": vs1}
+        if family != "neox":
+            # two row-parallel exchanges per layer (o_proj, down), each against its no-exchange floor
+            mode = "pull" if args.tp_pull else "push"
+            costs = tp_exchange_costs(B, cfg.hidden_size, (("o_proj", cfg.num_heads * cfg.head_dim // tp),
+                                                           ("down", cfg.intermediate_size // tp)), world, rank, dev)
+            per_layer = sum(c[mode + "_us"] - c["local_us"] for c in costs.values())
+            exchange = {"mode": mode, "exchange_us_per_step": per_layer * cfg.num_layers,
+                        "share_of_step": per_layer * cfg.num_layers / (step_ms_mean * 1e3), "per_layer": costs,
+                        "how": "tp_exchange_costs: each row-parallel projection + its norm, 32 launches per CUDA "
+                               "graph, with and without the exchange (max over ranks)"}
+
     # ---- temperature 0.8 with a fixed seed (the workload's sampled variant), same steps ----
     temp_line = None
     if not args.no_temp:
@@ -570,6 +611,8 @@ def gpu_arm(args):
                               "achieved_gbs": sbytes / (step_ms_mean * 1e-3) / 1e9,
                               "frac": sbytes / (step_ms_mean * 1e-3) / 1e9 / hbm_peak, "peak_source": peak_src},
             "temperature_0.8": temp_line,
+            "parity": parity,
+            "tp_exchange": exchange,
             "clocks": clocks.summary(),
             "gpu_launches": launches_per_step * args.steps,
             "e2e": e2e,
@@ -678,34 +721,23 @@ def micro_allreduce(args):
     dist.destroy_process_group()
 
 
-def micro_tp_exchange(args):
-    """One row-parallel decode projection of the Llama-3-8B shape and its exchange, at TP = WORLD_SIZE
-    (launch under torchrun): the projection (o_proj: K = 4096 / TP, down: K = 14336 / TP; N = 4096, batch
-    rows) followed by the norm that consumes the sum, three ways, each captured 32 times in a CUDA graph
-    and replayed (max over ranks): `local` = no exchange (the projection's float32 partial fed to the
-    norm as is: the compute-only floor), `pull` = projection, jx_allreduce_f32, norm, `push` = projection
-    with JX_EPI_PUSH_F32 and the push-mode norm.  Prints one JSON line per shape from rank 0."""
-    import datetime
-
+def tp_exchange_costs(M, d, shapes, world, rank, dev):
+    """Row-parallel decode projections and their exchange at TP = world (process group already up): for
+    each (name, K) in `shapes` the projection ([M, K] x [d, K]^T) followed by the norm that consumes the
+    sum, three ways, each captured 32 times in a CUDA graph and replayed (max over ranks): `local` = no
+    exchange (the projection's float32 partial fed to the norm as is: the compute-only floor), `pull` =
+    projection, jx_allreduce_f32, norm, `push` = projection with JX_EPI_PUSH_F32 and the push-mode norm.
+    Returns {name: {"K", "local_us", "pull_us", "push_us", "status"}}."""
     import torch
     import torch.distributed as dist
 
     from jaxml_b200 import _native as N
     from jaxml_b200.engine import TPComm
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world < 2:
-        print(json.dumps({"micro": "tpx", "skipped": "needs WORLD_SIZE >= 2 (torchrun)"}))
-        return
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     lib = N.load()
     comm = TPComm()
     peer = comm.prepare_peer(dev)
-    M, d, Mp = args.batch, 4096, 16 if args.batch <= 16 else 64
+    Mp = 16 if M <= 16 else 64
     status = torch.zeros(1, dtype=torch.int32, device=dev)
     ws_n = N.LL()
     N.check(lib.jx_linear_decode_workspace(148, 64, ws_n), "ws")
@@ -716,8 +748,9 @@ def micro_tp_exchange(args):
     xn = torch.zeros(M, d, dtype=torch.bfloat16, device=dev)
     part = torch.zeros(M, d, dtype=torch.float32, device=dev)
     tmp = torch.zeros(M, d, dtype=torch.float32, device=dev)
-    for name, K in (("o_proj", 4096 // world), ("down", 14336 // world)):
-        copies = 4   # distinct weight copies (4 x 2 x 4096 x K bytes, above L2 for the down shape)
+    res = {}
+    for name, K in shapes:
+        copies = 4   # distinct weight copies (4 x 2 x d x K bytes, above L2 for the down shape)
         ws_list = [(0.02 * torch.randn(d * K, device=dev)).to(torch.bfloat16) for _ in range(copies)]
         xp = torch.randn(Mp * K, device=dev).to(torch.bfloat16)
 
@@ -743,7 +776,7 @@ def micro_tp_exchange(args):
                 a.a, a.a_f32, a.lda = (part if mode == "local" else tmp).data_ptr(), 1, d
             N.check(lib.jx_norm(a, N.JX_BF16, 1, stream), "norm")
 
-        out = {}
+        out = {"K": K}
         for mode in ("local", "pull", "push"):
             def launch_all(stream, mode=mode):
                 for i in range(32):   # the current stream is `stream` here (warm-up and capture)
@@ -752,15 +785,39 @@ def micro_tp_exchange(args):
             ms = _graph_ms(launch_all, 32, reps=5)
             t = torch.tensor([ms * 1e3], device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            out[mode] = float(t.item())
+            out[mode + "_us"] = float(t.item())
+        out["status"] = int(status.item())
+        res[name] = out
         del ws_list
-        if rank == 0:
-            print(json.dumps({"micro": "tpx", "world": world, "shape": name, "M": M, "N": d, "K": K,
-                              "local_us": out["local"], "pull_us": out["pull"], "push_us": out["push"],
-                              "status": int(status.item())}), flush=True)
     torch.cuda.synchronize()
     comm.close()
     dist.barrier()
+    return res
+
+
+def micro_tp_exchange(args):
+    """The Llama-3-8B row-parallel shapes of tp_exchange_costs (o_proj: K = 4096 / TP, down: K = 14336 / TP;
+    N = 4096, batch rows) at TP = WORLD_SIZE (launch under torchrun).  Prints one JSON line per shape from
+    rank 0."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world < 2:
+        print(json.dumps({"micro": "tpx", "skipped": "needs WORLD_SIZE >= 2 (torchrun)"}))
+        return
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    res = tp_exchange_costs(args.batch, 4096, (("o_proj", 4096 // world), ("down", 14336 // world)), world, rank, dev)
+    if rank == 0:
+        for name, r in res.items():
+            print(json.dumps({"micro": "tpx", "world": world, "shape": name, "M": args.batch, "N": 4096, **r}),
+                  flush=True)
     dist.destroy_process_group()
 
 
@@ -777,6 +834,41 @@ def micro(args):
     torch.cuda.set_device(dev)
     B = args.batch
     rup = lambda x, m: (x + m - 1) // m * m
+    if args.micro == "filter":
+        # min-p / top-k / top-p over [B, 128256] bf16 logits (Llama-3's vocabulary): the filter kernel,
+        # and the same filters as torch device ops (sort / top-k) for comparison
+        from jaxml_b200.sampling import _keep_min_p, _keep_top_k, _keep_top_p, filter_logits_
+
+        V, (top_k, top_p, min_p) = 128256, (50, 0.9, 0.02)
+        xs = [(torch.randn(B, V, device=dev) * 2.5).to(torch.bfloat16) for _ in range(8)]
+        outs = [torch.empty_like(x) for x in xs]
+
+        def run_kernel(stream):
+            with torch.cuda.stream(torch.cuda.ExternalStream(stream)):
+                for x, o in zip(xs, outs):
+                    filter_logits_(x, o, top_k, top_p, min_p)
+        ms = _graph_ms(run_kernel, len(xs))
+
+        def torch_ops(x):
+            return _keep_top_p(_keep_top_k(_keep_min_p(x, min_p), top_k), top_p)
+        for x in xs:
+            torch_ops(x)
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(3):
+            for x in xs:
+                torch_ops(x)
+        end.record()
+        torch.cuda.synchronize()
+        # rows whose kept set differs from the torch ops' (their top-p cumulative sum runs in float32,
+        # the kernel's is exact)
+        differ = sum(int((torch.isfinite(o) != torch.isfinite(torch_ops(x))).any(dim=-1).sum().item())
+                     for x, o in zip(xs, outs))
+        print(json.dumps({"micro": "filter", "shape": f"B={B} V={V} bf16", "top_k": top_k, "top_p": top_p,
+                          "min_p": min_p, "us": ms * 1e3, "torch_ops_us": start.elapsed_time(end) / (3 * len(xs)) * 1e3,
+                          "rows_differing_from_torch_ops": differ, "rows": B * len(xs)}), flush=True)
+        return
     if args.micro == "gemm":
         # prefill projection: [tokens, K] x [N, K]^T, bf16 K128 operands, plain store epilogue
         Nn, K = (int(v) for v in args.shape.split(","))
@@ -875,6 +967,120 @@ def micro(args):
     print(json.dumps(line), flush=True)
 
 
+def micro_sweep(args):
+    """The single-layer decode microbenchmark sweep on one GPU (Llama-3-8B layer shapes, bf16), one JSON line
+    per point, each timed as back-to-back launches replayed from a CUDA graph:
+      attn  decode attention (the default form) for B in {1, 4, 16, 64, 256} x context in {1k, 4k, 16k,
+            32k}: K/V bytes read per launch and GB/s (as many distinct layers of cache as fit in ~24 GB);
+      proj  the decode projections of one tensor-parallel rank for TP in {1, 2, 4, 8} (qkv and gate/up
+            split by output rows, o_proj and down by K) at M in {1, 16, 64} token rows (distinct weight
+            copies, more than L2 in total);
+      norm  the vectorised RMSNorm with the residual add over [M, 4096] rows, M in {1, 16, 64, 256}.
+    The exchange of the row-parallel projections needs several GPUs: `--micro tpx` under torchrun."""
+    import torch
+
+    from jaxml_b200 import _native as N
+
+    lib = N.load()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    rup = lambda x, m: (x + m - 1) // m * m
+    Hq, Hkv, hd, d, F = 32, 8, 128, 4096, 14336
+    hbm = 6550.0
+    try:
+        hbm = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))["hbm_gbs"]
+    except (OSError, KeyError):
+        pass
+
+    def emit(kind, **kw):
+        print(json.dumps({"sweep": kind, **kw}), flush=True)
+
+    # ---- decode attention ----
+    for B in (1, 4, 16, 64, 256):
+        for ctx in (1024, 4096, 16384, 32768):
+            T = rup(ctx + 1, 256)
+            per_layer = 2 * B * T * Hkv * hd * 2
+            L = max(1, min(8, int(24e9 // per_layer)))
+            kc = torch.empty(L, B, T, Hkv, hd, dtype=torch.bfloat16, device=dev).normal_()
+            vc = torch.empty_like(kc).normal_()
+            q = torch.randn(rup(B, 16), Hq * hd, device=dev).to(torch.bfloat16)
+            pos = torch.full((B,), ctx - 2, dtype=torch.int32, device=dev)
+            orp = rup(B, 16)
+            out = torch.zeros(orp * Hq * hd, dtype=torch.bfloat16, device=dev)
+            nb = N.LL()
+            N.check(lib.jx_decode_attention_workspace(B, Hq, hd, T, 0, nb), "ws")
+            wsp = torch.zeros(nb.value // 4 + 1, dtype=torch.float32, device=dev)
+            cnt = torch.zeros(B * Hkv, dtype=torch.int32, device=dev)
+            st = torch.zeros(1, dtype=torch.int32, device=dev)
+            a = N.JxDAttnArgs()
+            a.B, a.Hq, a.Hkv, a.hd, a.T, a.window, a.cache_rows = B, Hq, Hkv, hd, T, 0, L * B * T
+            a.q, a.k_base, a.v_base, a.len_ptr, a.len_add, a.scale = (q.data_ptr(), kc.data_ptr(), vc.data_ptr(),
+                                                                      pos.data_ptr(), 2, hd ** -0.5)
+            a.out, a.out_rp, a.ws, a.ws_bytes = out.data_ptr(), orp, wsp.data_ptr(), wsp.numel() * 4
+            a.counters, a.status = cnt.data_ptr(), st.data_ptr()
+
+            def run(layer, stream):
+                a.layer_row0 = layer * B * T
+                N.check(lib.jx_decode_attention(a, 1, stream), "attention")
+            ms = _graph_ms(lambda stream: [run(l, stream) for l in range(L)], L)
+            nbytes = B * ctx * 2 * Hkv * hd * 2
+            emit("attn", B=B, ctx=ctx, layers=L, us=ms * 1e3, bytes=nbytes, gbs=nbytes / ms / 1e6,
+                 frac=nbytes / ms / 1e6 / hbm, status=int(st.item()))
+            del kc, vc, wsp
+            torch.cuda.empty_cache()
+
+    # ---- decode projections of one TP rank ----
+    for tp in (1, 2, 4, 8):
+        shapes = (("qkv", (Hq + 2 * Hkv) * hd // tp, d, False), ("o_proj", d, Hq * hd // tp, False),
+                  ("gate/up", 2 * F // tp, d, True), ("down", d, F // tp, False))
+        for name, Nn, K, glu in shapes:
+            Np, Kp = rup(Nn, 128), rup(K, 128)
+            copies = max(2, min(64, int(2e9 // (Np * Kp * 2))))
+            ws = [torch.empty(Np * Kp, dtype=torch.bfloat16, device=dev).normal_(0, 0.02) for _ in range(copies)]
+            for M in (1, 16, 64):
+                Mp = 16 if M <= 16 else (32 if M <= 32 else 64)
+                x = torch.randn(Mp * Kp, device=dev).to(torch.bfloat16)
+                out = torch.zeros(Mp * Np, dtype=torch.bfloat16, device=dev)
+                nws = N.LL()
+                N.check(lib.jx_linear_decode_workspace(148, M, nws), "ws")
+                wsp = torch.zeros(nws.value, dtype=torch.float32, device=dev)
+                cnt = torch.zeros(Np // 64 + 1, dtype=torch.int32, device=dev)
+                st = torch.zeros(1, dtype=torch.int32, device=dev)
+                e = N.JxEpilogue()
+                if glu:
+                    e.kind, e.M, e.N, e.out, e.out_rp = N.JX_EPI_GLU_SILU, M, Nn // 2, out.data_ptr(), Mp
+                else:
+                    e.kind, e.M, e.N, e.out, e.ldo = N.JX_EPI_STORE, M, Nn, out.data_ptr(), Nn
+
+                def run(w, stream):
+                    N.check(lib.jx_linear_decode(w.data_ptr(), x.data_ptr(), Np, Kp, M, e, wsp.data_ptr(), wsp.numel(),
+                                                 cnt.data_ptr(), st.data_ptr(), 148, 1, stream), "linear")
+                ms = _graph_ms(lambda stream: [run(w, stream) for w in ws], copies)
+                nbytes = 2 * Nn * K + 2 * M * K + 2 * M * (Nn // 2 if glu else Nn)
+                emit("proj", tp=tp, name=name, M=M, N=Nn, K=K, us=ms * 1e3, bytes=nbytes, gbs=nbytes / ms / 1e6,
+                     frac=nbytes / ms / 1e6 / hbm, status=int(st.item()))
+            del ws
+            torch.cuda.empty_cache()
+
+    # ---- norm (residual add + RMSNorm) ----
+    for M in (1, 16, 64, 256):
+        hs = [torch.randn(M, d, device=dev).to(torch.bfloat16) for _ in range(8)]
+        res = torch.randn(M, d, device=dev).to(torch.bfloat16)
+        w = torch.ones(d, dtype=torch.bfloat16, device=dev)
+        xn = torch.zeros(M, d, dtype=torch.bfloat16, device=dev)
+        st = torch.zeros(1, dtype=torch.int32, device=dev)
+
+        def run(h, stream):
+            a = N.JxNormArgs()
+            a.M, a.d, a.eps, a.kind = M, d, 1e-5, N.JX_NORM_RMS
+            a.h, a.ldh, a.w, a.out, a.ldo, a.status = h.data_ptr(), d, w.data_ptr(), xn.data_ptr(), d, st.data_ptr()
+            a.a, a.a_f32, a.lda = res.data_ptr(), 0, d
+            N.check(lib.jx_norm(a, N.JX_BF16, 1, stream), "norm")
+        ms = _graph_ms(lambda stream: [run(h, stream) for h in hs], len(hs))
+        nbytes = 2 * M * d * 4 + 2 * d   # residual in, added input in, sum out, normalised out; weights
+        emit("norm", M=M, d=d, us=ms * 1e3, bytes=nbytes, gbs=nbytes / ms / 1e6, status=int(st.item()))
+
+
 def main():
     args = parse()
     conf = CONFIGS[args.config]
@@ -891,6 +1097,9 @@ def main():
         return
     if args.micro == "tpx":
         micro_tp_exchange(args)
+        return
+    if args.micro == "sweep":
+        micro_sweep(args)
         return
     if args.micro:
         micro(args)

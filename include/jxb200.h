@@ -172,6 +172,8 @@ typedef struct jx_attn_args {
   long long ldo, out_rp;
   int* status;
   void* weights;         /* optional [B, Hq, S, T] softmax probabilities in the dtype (output_attentions), or NULL */
+  int uniform_T;         /* slots a query row with no visible key attends over, uniformly (0 = T) */
+  int _pad1;
 } jx_attn_args;
 
 /* Standalone rotary embedding: q [M, Hq, hd] and k [M, Hk, hd] rows at positions pos[M] (outputs may
@@ -225,7 +227,8 @@ typedef struct jx_pattn_args {
   int B, S, Hq, Hkv, hd;
   int T;                 /* cache slots per row (S <= T) */
   int window;            /* sliding window, 0 = none */
-  int _pad0;
+  int uniform_T;         /* slots a query row with no visible key attends over, uniformly (0 = T): the
+                            reference's cache length when the prompt ran (engine.py:543-557) */
   long long cache_rows;  /* rows of the whole cache allocation viewed as [cache_rows, Hkv*hd] */
   long long layer_row0;  /* first row of this layer (layer * B * T) */
   const void* q;         /* [B*S, Hq, hd] */

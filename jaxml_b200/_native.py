@@ -57,7 +57,7 @@ class JxQkvArgs(ctypes.Structure):
 class JxAttnArgs(ctypes.Structure):
     _fields_ = [("B", I), ("S", I), ("Hq", I), ("Hkv", I), ("hd", I), ("T", I), ("q", P), ("k", P), ("v", P),
                 ("len_ptr", P), ("len_add", I), ("causal", I), ("window", I), ("scale", F), ("out", P),
-                ("ldo", LL), ("out_rp", LL), ("status", P), ("weights", P)]
+                ("ldo", LL), ("out_rp", LL), ("status", P), ("weights", P), ("uniform_T", I), ("_pad1", I)]
 
 
 class JxRopeArgs(ctypes.Structure):
@@ -73,7 +73,7 @@ class JxDAttnArgs(ctypes.Structure):
 
 
 class JxPAttnArgs(ctypes.Structure):
-    _fields_ = [("B", I), ("S", I), ("Hq", I), ("Hkv", I), ("hd", I), ("T", I), ("window", I), ("_pad0", I),
+    _fields_ = [("B", I), ("S", I), ("Hq", I), ("Hkv", I), ("hd", I), ("T", I), ("window", I), ("uniform_T", I),
                 ("cache_rows", LL), ("layer_row0", LL), ("q", P), ("k_base", P), ("v_base", P), ("len_ptr", P),
                 ("len_add", I), ("scale", F), ("out", P), ("out_rp", LL), ("status", P)]
 

@@ -1106,10 +1106,14 @@ __global__ void __launch_bounds__(128) dattn_warp_kernel(const __grid_constant__
 // scores kernel does and counts itself done for its head group (release); a pv item waits (bounded,
 // acquire) until every split of its head group is scored, then forms the exact bf16 probabilities and
 // P.V as the pv kernel does, and the last pv item of a group sums the split partials in split order.
-// No co-residency is needed: every score item precedes every pv item in the list and a CTA finishes
-// an item before it starts the next, so when a pv item waits, the score items it waits for have all
-// been claimed by CTAs that are running them without waiting on anything.  The sums, roundings and
-// workspace are the split form's, so the outputs are bit-identical to it.
+// CTA c starts with score item c (so that its K tiles load before the wait on the previous kernel, as
+// the scores kernel's do); the rest are claimed after that wait.  No deadlock: only score items are
+// assigned up front, every score item precedes every pv item in the list and a CTA finishes an item
+// before it starts the next, so when a pv item waits, the score items it waits for are held by CTAs
+// that run them without waiting on anything, or that become resident as soon as an SM frees up (the
+// grid is sized by occupancy).  After any error status, CTAs stop waiting and claiming, so a failure
+// costs one bounded wait.  The sums, roundings and workspace are the split form's, so the outputs are
+// bit-identical to it.
 // ------------------------------------------------------------------------------------------------
 template <int HD>
 struct DqCfg {
@@ -1171,9 +1175,15 @@ __global__ void __launch_bounds__(128) dattn_queue_kernel(const __grid_constant_
     x.n_active = (x.valid - lo + kDaKeys - 1) / kDaKeys;
     return x;
   };
+  // CTA c starts with score item c (c < S0, no shared state: its tiles load before the wait on the
+  // previous kernel); every later item is claimed from the counter, after that wait.  The counter and the
+  // group counts belong to the previous launch until it has completed (a back-to-back launch of this
+  // kernel on the same workspace starts while the previous one runs), so nothing shared is touched before.
+  const int S0 = (int)gridDim.x < n_score ? (int)gridDim.x : n_score;
   auto claim = [&]() {
     for (;;) {
-      const int it = atomicAdd(claim_ctr, 1);
+      if (p.status && *reinterpret_cast<volatile int*>(p.status) != 0) return -1;   // an error: stop taking work
+      const int it = S0 + atomicAdd(claim_ctr, 1);
       if (it >= total) return -1;
       if (decode(it).n_tiles > 0) return it;
     }
@@ -1216,15 +1226,21 @@ __global__ void __launch_bounds__(128) dattn_queue_kernel(const __grid_constant_
     prefetch_tmap(&vmap);
     for (int i = 0; i < 4; ++i) mbar_init(&bar[i], 1);
     fence_barrier_init();
-    const int first = claim();
+    const int first = (int)blockIdx.x < S0 && decode(blockIdx.x).n_tiles > 0 ? (int)blockIdx.x : -1;
     items[0] = first;
     if (first >= 0) late0 = issue_item(first, 0, true);
   }
   pdl_wait();
   pdl_trigger();
-  if (threadIdx.x == 0 && items[0] >= 0 && late0 >= 0 && !decode(items[0]).pv) {
-    issue_tile(decode(items[0]), 0, late0);
-    late0 = -1;
+  if (threadIdx.x == 0) {
+    if (items[0] < 0) {
+      const int it = claim();
+      items[0] = it;
+      if (it >= 0) late0 = issue_item(it, 0, false);
+    } else if (late0 >= 0) {
+      issue_tile(decode(items[0]), 0, late0);   // (a score item: this step's key after the wait)
+      late0 = -1;
+    }
   }
   if (threadIdx.x == 0) items[2] = 1;
   __syncthreads();
@@ -1402,6 +1418,10 @@ __global__ void __launch_bounds__(128) dattn_queue_kernel(const __grid_constant_
         if (ld_acquire_gpu(&scored[g]) < x.n_active) {
           const uint64_t w0 = globaltimer_ns();
           while (ld_acquire_gpu(&scored[g]) < x.n_active) {
+            if (p.status && *reinterpret_cast<volatile int*>(p.status) != 0) {   // another CTA failed: give up
+              ok = false;
+              break;
+            }
             if (globaltimer_ns() - w0 > kWaitLimitNs) {
               set_status(p.status, JX_ERR_TIMEOUT);
               ok = false;

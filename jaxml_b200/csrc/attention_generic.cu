@@ -1,7 +1,8 @@
 // Attention for any head size and dtype on CUDA cores (one CTA per query row and head).  It serves the
 // float32 path and shapes the tensor-core kernels do not cover, and reproduces Attention.mha
 // (nn/attention.py:321-400) exactly: scores = dtype(dtype(q.k) * dtype(attn_scale)); causal, sliding
-// window and prefix-padding masks; a row with no visible key attends uniformly to all T slots;
+// window and prefix-padding masks; a row with no visible key attends uniformly to the first uniform_T
+// slots (all T by default: the reference's cache length);
 // float32 softmax rounded to dtype (optionally stored: the attention weights); dtype(sum p*v) with
 // float32 accumulation.  KV heads are shared by n_rep = Hq / Hkv query heads (repeat_kv, :294-319) by
 // indexing, not copying.
@@ -58,7 +59,7 @@ __global__ void __launch_bounds__(128) attention_generic_kernel(AttnArgs p) {
   const bool all_masked = (mx == -INFINITY);
   if (all_masked) {
     j_lo = 0;
-    j_hi = p.T;
+    j_hi = p.uniform_T > 0 && p.uniform_T < p.T ? p.uniform_T : p.T;
   }
   __syncthreads();
   float l = 0.f;

@@ -4,7 +4,8 @@
 // Attention.mha for q_len > 1 (nn/attention.py:321-400): scores = bf16(bf16(q.k) * bf16(attn_scale)),
 // key j visible to query i iff j <= i (causal, :366-368), j > i - window (sliding window, :371-372) and
 // j < len (right-padded mask, :382-383); softmax in float32 cast to bf16 (:388-389); o = bf16(p.v).
-// A query row with no visible key attends uniformly to every slot of the buffer (:385-386).
+// A query row with no visible key attends uniformly to every slot of the buffer (:385-386): the first
+// uniform_T slots, the reference's cache length when the prompt ran (the rest are zero then).
 //
 // One CTA per (64 query rows, query head, batch row); each warp owns 16 rows.  To round the normalised
 // probabilities exactly as the reference does, the kernel makes two passes over the key tiles: pass 1
@@ -20,6 +21,7 @@ int make_tmap_2d_bf16_box(CUtensorMap* map, const void* base, long long rows, lo
 
 struct PAttnParams {
   int B, S, Hq, Hkv, n_rep, T;
+  int uniform_T;         // slots of the all-masked rows' uniform attention (<= T)
   long long layer_row0;
   const bf16* q;         // [B*S, Hq, HD]
   const bf16* v_plain;   // cache base of V (row-major [rows, Hkv*HD]) for the all-masked fallback
@@ -236,15 +238,15 @@ __global__ void __launch_bounds__(128) pattn_kernel(const __grid_constant__ CUte
       }
   }
   __syncthreads();
-  // all-masked rows: uniform weights bf16(1/T) over every slot of the buffer
-  const float pu = rnd<bf16>(1.0f / (float)p.T);
+  // all-masked rows: uniform weights bf16(1/Tu) over the first Tu slots of the buffer
+  const float pu = rnd<bf16>(1.0f / (float)p.uniform_T);
   for (int r = 0; r < 64; ++r) {
     if (!dead_rows[r]) continue;
     const long long orow = (long long)b * p.S + s0 + r;
     for (int d = threadIdx.x; d < HD; d += 128) {
       float acc = 0.f;
       const bf16* vcol = p.v_plain + ((p.layer_row0 + (long long)b * p.T) * p.Hkv + kvh) * HD + d;
-      for (int j = 0; j < p.T; ++j) acc += pu * __bfloat162float(vcol[(long long)j * p.Hkv * HD]);
+      for (int j = 0; j < p.uniform_T; ++j) acc += pu * __bfloat162float(vcol[(long long)j * p.Hkv * HD]);
       p.out[k128_offset(orow, (long long)h * HD + d, p.out_rp)] = __float2bfloat16_rn(acc);
     }
   }
@@ -288,6 +290,7 @@ int run_prefill_attention(const jx_pattn_args& a, bool pdl, cudaStream_t stream)
   p.Hkv = a.Hkv;
   p.n_rep = a.Hq / a.Hkv;
   p.T = a.T;
+  p.uniform_T = a.uniform_T > 0 && a.uniform_T < a.T ? a.uniform_T : a.T;
   p.layer_row0 = a.layer_row0;
   p.q = reinterpret_cast<const bf16*>(a.q);
   p.v_plain = reinterpret_cast<const bf16*>(a.v_base);

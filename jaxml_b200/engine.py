@@ -502,7 +502,9 @@ class Engine:
         pin = prompt.pin_memory() if not prompt.is_cuda else prompt
         ids_d = pin.to(dev, non_blocking=True)
         mask_d = (torch.ones(B, P, dtype=torch.bool) if mask is None else mask).pin_memory().to(dev, non_blocking=True)
-        toks = rt.generate(ids_d, mask_d, max_new_tokens, method.use_greedy, sp.temp, seed, fuse=fuse_decoding)
+        first_len = (P // self.cache_stride + 1) * self.cache_stride   # the reference's first chunk's cache
+        toks = rt.generate(ids_d, mask_d, max_new_tokens, method.use_greedy, sp.temp, seed, fuse=fuse_decoding,
+                           first_len=first_len)
         out = toks.to("cpu")
         rt.check_status()
         self.last_rng = rt.rng_key()

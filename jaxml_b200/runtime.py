@@ -373,6 +373,9 @@ class DecoderRuntime:
         self.graph = None
         # fuse_decoding: a graph of several consecutive decode steps, keyed like self.graph plus the count
         self.graph_multi = None
+        # slots that a prompt row with no visible key attends over (0 = the whole buffer): the reference's
+        # cache length when the prompt ran, before its chunk loop grows the cache (engine.py:543-557)
+        self.uniform_T = 0
         # the persistent decode-step kernel's plan when it runs this runtime's layers (else None)
         self.fused_step = None
         self._launches = 0
@@ -608,6 +611,7 @@ class DecoderRuntime:
         at.ldo = W.Hq * W.hd
         at.out_rp = acts["Mp"] if W.bf16 else 0
         at.status = ptr(self.status)
+        at.uniform_T = self.uniform_T
         self._launches += 1
         N.check(N.load().jx_attention(at, W.jdt, 1, self.stream_ptr()), "jx_attention")
 
@@ -647,6 +651,7 @@ class DecoderRuntime:
         a.scale = cfg.attn_scale
         a.out, a.out_rp = ptr(acts["attn"]), acts["Mp"]
         a.status = ptr(self.status)
+        a.uniform_T = self.uniform_T
         self._launches += 1
         N.check(N.load().jx_prefill_attention(a, 1, self.stream_ptr()), "jx_prefill_attention")
 
@@ -938,20 +943,27 @@ class DecoderRuntime:
         return g
 
     def generate(self, prompt: torch.Tensor, mask: torch.Tensor, n_new: int, greedy: bool, temp: float, seed: int,
-                 fuse: bool = False):
+                 fuse: bool = False, first_len: int = 0):
         """Prefill + (n_new - 1) decode steps on the device; returns device tokens [B, n_new].
 
         The first decode step runs eagerly (it also warms every kernel up); the rest replay a captured
         CUDA graph of one step, or with `fuse` (the reference's fuse_decoding: the decode loop compiled
         as one scan, _generate.py:365-380) a graph of `fused_steps` steps, the remainder on the one-step
         graph.  Key flow as _generate.py: key = PRNGKey(seed); key, sub = split(key) before the first
-        sample, and one split per decode step on the device.
+        sample, and one split per decode step on the device.  `first_len` is the cache length the
+        reference's chunk loop starts with (engine.py:543-557); the buffer here is allocated at its final
+        length, which changes nothing but the uniform attention of a prompt row with no visible key, so
+        that attention is confined to the first `first_len` slots.
         """
         from . import prng
 
         key, sub = prng.split(prng.prng_key(seed))
         self.reset(mask, key, sub, n_new)
-        self.prefill(prompt, greedy, temp)
+        self.uniform_T = first_len
+        try:
+            self.prefill(prompt, greedy, temp)
+        finally:
+            self.uniform_T = 0
         if n_new > 1:
             self.decode_step(greedy, temp)
         rest = max(n_new - 2, 0)

@@ -373,3 +373,50 @@ def test_linear_decode_row_split(M, Nn, K):
                    cnt.data_ptr(), status.data_ptr(), 4, 1, _stream())
     finally:
         N.call("jx_set_decode_linear_impl", 0)
+
+
+@pytest.mark.parametrize("form", [1, 5], ids=["split", "queue"])
+def test_decode_attention_back_to_back_launches(form):
+    """Launches on consecutive layers with programmatic dependent launch and no synchronisation between
+    them, sharing one workspace and counter array (as a captured decode step replays them): each output
+    equals a separately synchronised call's, and the counters are zero afterwards.  The queue form's
+    next launch starts while the previous one runs, so its shared counters must not be touched before
+    its wait."""
+    N = _n()
+    torch.manual_seed(17)
+    B, Hq, Hkv, hd, T, L = 16, 32, 8, 128, 768, 4
+    lens = torch.tensor([640 - 9 * i for i in range(B)], dtype=torch.int32)
+    kd = torch.randn(L, B, T, Hkv, hd).to(torch.bfloat16).cuda()
+    vd = torch.randn(L, B, T, Hkv, hd).to(torch.bfloat16).cuda()
+    q = torch.randn(B, Hq * hd).to(torch.bfloat16).cuda()
+    pos = (lens - 2).cuda()
+    Mp, Kp = _rup(B, 16), _rup(Hq * hd, 128)
+    nb = N.LL()
+    N.check(N.load().jx_decode_attention_workspace(B, Hq, hd, T, 0, nb), "ws")
+    ws = torch.zeros(nb.value // 4 + 1, dtype=torch.float32, device="cuda")
+    cnt = torch.zeros(B * Hkv, dtype=torch.int32, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    outs = [torch.zeros(Mp * Kp, dtype=torch.bfloat16, device="cuda") for _ in range(L)]
+    a = N.JxDAttnArgs()
+    a.B, a.Hq, a.Hkv, a.hd, a.T, a.window, a.cache_rows = B, Hq, Hkv, hd, T, 0, L * B * T
+    a.q, a.k_base, a.v_base = q.data_ptr(), kd.data_ptr(), vd.data_ptr()
+    a.len_ptr, a.len_add, a.scale = pos.data_ptr(), 2, hd ** -0.5
+    a.out_rp, a.ws, a.ws_bytes, a.counters, a.status = Mp, ws.data_ptr(), ws.numel() * 4, cnt.data_ptr(), status.data_ptr()
+    N.call("jx_set_decode_attention_impl", form)
+    try:
+        for rep in range(3):
+            for layer in range(L):
+                a.layer_row0, a.out = layer * B * T, outs[layer].data_ptr()
+                N.call("jx_decode_attention", a, 1, _stream())
+            torch.cuda.synchronize()
+            assert int(status.item()) == 0 and int(cnt.abs().sum().item()) == 0
+            tail = ws.view(torch.int32)[(nb.value // 4) - (2 + B * Hq):nb.value // 4]
+            assert int(tail.abs().sum().item()) == 0
+    finally:
+        N.call("jx_set_decode_attention_impl", 0)
+    for layer in range(L):
+        want = _dattn_call(N, B, Hq, Hkv, hd, T, L, layer, q, kd, vd, pos)
+        got = torch.empty(B, Hq * hd, dtype=torch.bfloat16, device="cuda")
+        N.call("jx_unpack_k128", outs[layer].data_ptr(), B, Hq * hd, Mp, got.data_ptr(), N.JX_BF16, Hq * hd, _stream())
+        torch.cuda.synchronize()
+        assert torch.equal(got, want), layer

@@ -190,3 +190,41 @@ def test_fused_decoding_gives_the_same_tokens(n_new, greedy, temp, hf_models):
         DecoderRuntime.fused_steps = old
     assert torch.equal(runs[0][0], runs[1][0])
     assert np.array_equal(runs[0][1], runs[1][1])
+
+
+def test_masked_prompt_row_attends_over_the_first_chunk(hf_models):
+    """A prompt row whose last position sees no key (right padding longer than the sliding window) attends
+    uniformly over the cache the reference's chunk loop holds when the prompt runs ((P // stride + 1) *
+    stride slots), not over the larger buffer allocated here for the whole generation: prefill logits and
+    greedy tokens equal the oracle's chunked generation (cache_stride 16: 48 slots at the prompt, 64 at
+    the end)."""
+    _, cfg, params = hf_models["gemma3"]
+    assert cfg.sliding_window == 32
+    B, P, n, stride = 3, 40, 20, 16
+    g = torch.Generator().manual_seed(6)
+    ids = torch.randint(0, cfg.vocab_size, (B, P), generator=g, dtype=torch.int32)
+    lens = torch.tensor([40, 5, 23])
+    mask = torch.arange(P)[None, :] < lens[:, None]
+    first, T = (P // stride + 1) * stride, 64
+    rt = _runtime("gemma3", cfg, params, torch.float32, B, T)
+    key, sub = TF.split(TF.prng_key(0))
+    logits = {}
+    for ut in (first, 0):
+        rt.reset(mask.cuda(), key, sub, 2)
+        rt.uniform_T = ut
+        rt.prefill(ids.cuda(), greedy=True, temp=1.0)
+        rt.uniform_T = 0
+        torch.cuda.synchronize()
+        rt.check_status()
+        logits[ut] = rt.logits_buf()[:B].float().cpu()
+    for ut, slots in ((first, first), (0, T)):
+        caches = tuple(O.OracleKVCache(slots, torch.float32) for _ in range(cfg.num_layers))
+        want = O.forward("gemma3", cfg, params, ids, torch.float32, attention_mask=mask, kv_caches=caches,
+                         keep_last_n_logits=1).logits[:, -1]
+        _check_logits(logits[ut], want, torch.float32)
+    assert not torch.allclose(logits[first][1], logits[0][1])     # the case is exercised
+    toks = rt.generate(ids.cuda(), mask.cuda(), n, True, 1.0, 0, first_len=first).cpu()
+    rt.check_status()
+    want = O.generate("gemma3", cfg, params, ids, torch.float32, max_new_tokens=n, temperature=0.0,
+                      cache_stride=stride, attention_mask=mask, include_prompt=False)
+    assert torch.equal(toks, want.to(torch.int32))

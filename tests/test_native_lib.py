@@ -18,7 +18,8 @@ def test_struct_layouts_match_the_header():
     assert ctypes.sizeof(N.JxEpilogue) == 216
     assert ctypes.sizeof(N.JxNormArgs) == 232
     assert ctypes.sizeof(N.JxQkvArgs) == 128
-    assert ctypes.sizeof(N.JxAttnArgs) == 112
+    assert ctypes.sizeof(N.JxAttnArgs) == 120
+    assert ctypes.sizeof(N.JxFilterArgs) == 56
     assert ctypes.sizeof(N.JxSampleArgs) == 168
 
 
@@ -34,7 +35,7 @@ def test_struct_field_offsets_match_the_c_compiler(tmp_path):
         pytest.skip("no C compiler")
     pairs = [(N.JxEpilogue, "jx_epilogue"), (N.JxNormArgs, "jx_norm_args"), (N.JxQkvArgs, "jx_qkv_args"),
              (N.JxAttnArgs, "jx_attn_args"), (N.JxDAttnArgs, "jx_dattn_args"), (N.JxPAttnArgs, "jx_pattn_args"),
-             (N.JxSampleArgs, "jx_sample_args"), (N.JxRopeArgs, "jx_rope_args")]
+             (N.JxSampleArgs, "jx_sample_args"), (N.JxRopeArgs, "jx_rope_args"), (N.JxFilterArgs, "jx_filter_args")]
     inc = os.path.join(os.path.dirname(N.__file__), os.pardir, "include")
     lines = ["#include <stdio.h>", "#include <stddef.h>", '#include "jxb200.h"', "int main(void) {"]
     for cls, cname in pairs:
@@ -80,8 +81,8 @@ def test_decode_attention_rejects_an_output_too_small_for_the_batch():
         a.out_rp = rp
         assert lib.jx_decode_attention(a, 0, None) == N.JX_ERR_ARG
         assert b"out_rp" in lib.jx_last_error()
-    for impl in (0, 1, 2, 3, 4, 5):
-        assert lib.jx_set_decode_attention_impl(impl) == (N.JX_OK if impl <= 4 else N.JX_ERR_ARG)
+    for impl in (0, 1, 2, 3, 4, 5, 6):
+        assert lib.jx_set_decode_attention_impl(impl) == (N.JX_OK if impl <= 5 else N.JX_ERR_ARG)
         assert lib.jx_set_prefill_linear_impl(impl) == (N.JX_OK if impl <= 2 else N.JX_ERR_ARG)
     lib.jx_set_decode_attention_impl(0)
     lib.jx_set_prefill_linear_impl(0)
