@@ -97,6 +97,21 @@ typedef struct jx_epilogue {
   int pn_kind, pn_d;
   float pn_eps;
   int _pad1;
+  /* Normalisation tail (the row-split decode projection, jx_set_decode_linear_impl 3 or chosen by shape;
+   * tn_x != NULL, JX_ERR_UNSUPPORTED when another kernel would run): once every CTA has stored its output
+   * columns of the residual stream (kind JX_EPI_STORE or JX_EPI_RESID, bf16, plain [M, ldo] output), the
+   * last CTA to finish normalises the M rows of that output into the next projection's activation
+   * operand tn_x (K128, tn_rp rows) with the arithmetic and summation order of jx_norm (kinds RMS /
+   * GEMMA / LAYER, weights tn_w, bias tn_b, over the N columns; N % 256 == 0, N <= 8192): the RMSNorm
+   * after a residual add of models/llama.py:133-137 without a separate launch.  tn_sync: one int,
+   * zero-initialised once, self-resetting.  No counterpart in the reference. */
+  void* tn_x;
+  long long tn_rp;
+  const void* tn_w;
+  const void* tn_b;
+  int* tn_sync;
+  int tn_kind;
+  float tn_eps;
 } jx_epilogue;
 
 /* Row-wise embedding gather / residual add / normalisation (one launch per call). */

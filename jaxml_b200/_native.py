@@ -36,7 +36,8 @@ class JxEpilogue(ctypes.Structure):
                 ("pf_kp", LL), ("pf_rows", I), ("pf_grid", I), ("peer_bases", P), ("peer_recv_off", LL),
                 ("peer_slot_bytes", LL), ("peer_flag_off", LL), ("peer_seq_off", LL), ("peer_rank", I), ("peer_world", I),
                 ("pn_h", P), ("pn_ldh", LL), ("pn_w", P), ("pn_b", P), ("pn_sync", P), ("pn_kind", I), ("pn_d", I),
-                ("pn_eps", F), ("_pad1", I)]
+                ("pn_eps", F), ("_pad1", I), ("tn_x", P), ("tn_rp", LL), ("tn_w", P), ("tn_b", P), ("tn_sync", P),
+                ("tn_kind", I), ("tn_eps", F)]
 
 
 class JxNormArgs(ctypes.Structure):

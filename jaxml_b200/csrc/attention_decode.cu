@@ -92,18 +92,22 @@ __device__ __forceinline__ void key_range(const DAttnParams& p, int b, int& lo, 
   lo = (p.window > 0 && valid > p.window) ? valid - p.window : 0;
 }
 
-template <int HD>
+// RQ: rows of the query (scores) / probability (pv) tile in shared memory, 16 or, when a head group has
+// at most 8 query heads, 8 (the MMA's rows 8-15 are then zero registers).  The smaller tiles let 6 CTAs
+// share an SM instead of 5, so a 768-slot cache (6 splits x 128 head groups) runs in one wave.
+template <int HD, int RQ>
 __global__ void __launch_bounds__(128) dattn_scores_kernel(const __grid_constant__ CUtensorMap kmap, DAttnParams p) {
   constexpr int NB = HD / 64;                 // 64-column blocks per head
   constexpr int TILE_BYTES = kDaTile * HD * 2;
+  constexpr int QB = RQ * 128;                // bytes of one [RQ x 64] query block
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* ktile = smem;                                   // 2 tiles, each NB blocks of [64 x 64]
-  uint8_t* qs = smem + 2 * TILE_BYTES;                     // NB blocks of [16 x 64]
-  uint64_t* bar = reinterpret_cast<uint64_t*>(qs + NB * 2048);
+  uint8_t* qs = smem + 2 * TILE_BYTES;                     // NB blocks of [RQ x 64]
+  uint64_t* bar = reinterpret_cast<uint64_t*>(qs + NB * QB);
   float* red = reinterpret_cast<float*>(bar + 2);          // [4 warps][16 rows]
 
-  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int kvh = blockIdx.x, b = blockIdx.y, split = blockIdx.z;   // split-major launch order
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // The kernel before this one (RoPE + cache append) releases it only after its own wait, so the
   // positions and the keys of earlier steps are complete here: tiles that end before this step's key
@@ -142,7 +146,7 @@ __global__ void __launch_bounds__(128) dattn_scores_kernel(const __grid_constant
   }
   const bf16* qkv_row = fused ? p.qkv + (long long)b * p.ld_qkv : nullptr;
   // Q rows of this head group (rows >= n_rep are zero) into the swizzled layout.
-  for (int idx = threadIdx.x; idx < 16 * (HD / 8); idx += 128) {
+  for (int idx = threadIdx.x; idx < RQ * (HD / 8); idx += 128) {
     const int r = idx / (HD / 8), cg = idx % (HD / 8);
     uint4 v = make_uint4(0, 0, 0, 0);
     if (r < p.n_rep) {
@@ -151,7 +155,7 @@ __global__ void __launch_bounds__(128) dattn_scores_kernel(const __grid_constant
       else
         v = *reinterpret_cast<const uint4*>(p.q + ((long long)b * p.Hq + kvh * p.n_rep + r) * HD + cg * 8);
     }
-    const uint32_t a = swz(smem_u32(qs + (cg >> 3) * 2048), r, cg & 7);
+    const uint32_t a = swz(smem_u32(qs + (cg >> 3) * QB), r, cg & 7);
     asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w));
   }
   // The CTA holding this step's key appends the rotated k and the v of this KV head to the cache and
@@ -197,10 +201,13 @@ __global__ void __launch_bounds__(128) dattn_scores_kernel(const __grid_constant
     const uint32_t kb = smem_u32(ktile + i * TILE_BYTES);
 #pragma unroll
     for (int ks = 0; ks < HD / 16; ++ks) {
-      uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
-      {
+      uint32_t a0, a1 = 0, a2, a3 = 0, b0, b1, b2, b3;
+      if (RQ == 16) {
         const int row = (mi & 1) * 8 + r8, ch = ks * 2 + (mi >> 1);
-        ldsm_x4(swz(smem_u32(qs + (ch >> 3) * 2048), row, ch & 7), a0, a1, a2, a3);
+        ldsm_x4(swz(smem_u32(qs + (ch >> 3) * QB), row, ch & 7), a0, a1, a2, a3);
+      } else {
+        const int ch = ks * 2 + (mi & 1);   // (lanes 16-31 give no address for .x2)
+        ldsm_x2(swz(smem_u32(qs + (ch >> 3) * QB), r8, ch & 7), a0, a2);
       }
       {
         const int row = warp * 16 + (mi >> 1) * 8 + r8, ch = ks * 2 + (mi & 1);
@@ -280,7 +287,7 @@ __global__ void __launch_bounds__(128) dattn_scores_kernel(const __grid_constant
   }
 }
 
-template <int HD>
+template <int HD, int RQ>
 __global__ void __launch_bounds__(128) dattn_pv_kernel(const __grid_constant__ CUtensorMap vmap, DAttnParams p) {
   constexpr int NB = HD / 64;
   constexpr int TILE_BYTES = kDaTile * HD * 2;
@@ -292,10 +299,10 @@ __global__ void __launch_bounds__(128) dattn_pv_kernel(const __grid_constant__ C
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + 2 * TILE_BYTES);
   float* Ms = reinterpret_cast<float*>(bar + 2);   // [16]
   float* Ls = Ms + 16;                             // [16]
-  bf16* ptile = reinterpret_cast<bf16*>(Ls + 16);  // [16][kPLd]
+  bf16* ptile = reinterpret_cast<bf16*>(Ls + 16);  // [RQ][kPLd]
   __shared__ int last_flag;
 
-  const int split = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int kvh = blockIdx.x, b = blockIdx.y, split = blockIdx.z;   // split-major launch order
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   pdl_trigger();
   // The scores kernel before this one releases it only after its own wait, so every value of the cache
@@ -345,7 +352,7 @@ __global__ void __launch_bounds__(128) dattn_pv_kernel(const __grid_constant__ C
   const int r_lo = lane >> 2, r_hi = r_lo + 8;
   // Probabilities of this CTA's keys, computed once (coalesced score reads) into a padded bf16 tile
   // [16 rows][kDaKeys + 8] that every warp reads with ldmatrix.
-  for (int idx = threadIdx.x; idx < 16 * kDaKeys; idx += 128) {
+  for (int idx = threadIdx.x; idx < RQ * kDaKeys; idx += 128) {
     const int row = idx / kDaKeys, k = idx % kDaKeys, t = t0 + k;
     float pv = 0.f;
     if (row < p.n_rep && t < t1) {
@@ -366,10 +373,12 @@ __global__ void __launch_bounds__(128) dattn_pv_kernel(const __grid_constant__ C
     const uint32_t vb = smem_u32(vtile + i * TILE_BYTES);
 #pragma unroll
     for (int kk = 0; kk < kDaTile / 16; ++kk) {
-      uint32_t a0, a1, a2, a3;
-      {
+      uint32_t a0, a1 = 0, a2, a3 = 0;
+      if (RQ == 16) {
         const int row = (mi & 1) * 8 + r8, col = i * kDaTile + kk * 16 + (mi >> 1) * 8;
         ldsm_x4(smem_u32(ptile + row * kPLd + col), a0, a1, a2, a3);
+      } else {
+        ldsm_x2(smem_u32(ptile + r8 * kPLd + i * kDaTile + kk * 16 + (mi & 1) * 8), a0, a2);
       }
 #pragma unroll
       for (int n16 = 0; n16 < NT / 2; ++n16) {
@@ -1582,22 +1591,26 @@ int dattn_n_splits(int T, int window) {
   return (range + kDaKeys - 1) / kDaKeys;
 }
 
-template <int HD>
-static int launch_dattn(const CUtensorMap& km, const CUtensorMap& vm, const DAttnParams& p, bool column_pv, bool pdl,
-                        cudaStream_t s) {
-  const int smem_a = 1024 + 2 * kDaTile * HD * 2 + (HD / 64) * 2048 + 16 + 4 * 16 * 4;
-  const int smem_b = 1024 + 2 * kDaTile * HD * 2 + 16 + 32 * 4 + 16 * kPLd * 2;
+template <int HD, int RQ>
+static int launch_dattn_rq(const CUtensorMap& km, const CUtensorMap& vm, const DAttnParams& p, bool column_pv,
+                           bool pdl, cudaStream_t s) {
+  const int smem_a = 1024 + 2 * kDaTile * HD * 2 + (HD / 64) * RQ * 128 + 16 + 4 * 16 * 4;
+  const int smem_b = 1024 + 2 * kDaTile * HD * 2 + 16 + 32 * 4 + RQ * kPLd * 2;
   const int smem_c = 1024 + kPcStages * 8192 + 4 * 16 * kPcLd * 2 + kPcStages * 8;
   static bool configured = false;
   if (!configured) {
-    if (cudaFuncSetAttribute(dattn_scores_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_a) != cudaSuccess ||
-        cudaFuncSetAttribute(dattn_pv_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_b) != cudaSuccess ||
+    if (cudaFuncSetAttribute(dattn_scores_kernel<HD, RQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_a) !=
+            cudaSuccess ||
+        cudaFuncSetAttribute(dattn_pv_kernel<HD, RQ>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_b) != cudaSuccess ||
         cudaFuncSetAttribute(dattn_pvcol_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_c) != cudaSuccess)
       return JX_ERR_CUDA;
     configured = true;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(p.n_splits, p.Hkv, p.B);
+  // Splits vary slowest: CTAs are dispatched in linear block order, so the splits past the valid keys
+  // (the grid is sized by the buffer length; they exit at once) come last, and a grid larger than one
+  // wave of resident CTAs leaves only those to the second wave.
+  cfg.gridDim = dim3(p.Hkv, p.B, p.n_splits);
   cfg.blockDim = dim3(128);
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -1606,15 +1619,22 @@ static int launch_dattn(const CUtensorMap& km, const CUtensorMap& vm, const DAtt
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
   cfg.dynamicSmemBytes = smem_a;
-  if (launch_ex(&cfg, dattn_scores_kernel<HD>, km, p) != cudaSuccess) return JX_ERR_CUDA;
+  if (launch_ex(&cfg, dattn_scores_kernel<HD, RQ>, km, p) != cudaSuccess) return JX_ERR_CUDA;
   if (column_pv) {
     cfg.gridDim = dim3(HD / 64, p.Hkv, p.B);
     cfg.dynamicSmemBytes = smem_c;
     return launch_ex(&cfg, dattn_pvcol_kernel<HD>, vm, p) == cudaSuccess ? JX_OK : JX_ERR_CUDA;
   }
   cfg.dynamicSmemBytes = smem_b;
-  if (launch_ex(&cfg, dattn_pv_kernel<HD>, vm, p) != cudaSuccess) return JX_ERR_CUDA;
+  if (launch_ex(&cfg, dattn_pv_kernel<HD, RQ>, vm, p) != cudaSuccess) return JX_ERR_CUDA;
   return JX_OK;
+}
+
+template <int HD>
+static int launch_dattn(const CUtensorMap& km, const CUtensorMap& vm, const DAttnParams& p, bool column_pv, bool pdl,
+                        cudaStream_t s) {
+  return p.n_rep <= 8 ? launch_dattn_rq<HD, 8>(km, vm, p, column_pv, pdl, s)
+                      : launch_dattn_rq<HD, 16>(km, vm, p, column_pv, pdl, s);
 }
 
 // Cluster shape of the single-pass form for B x Hkv head groups over a key range of `range` keys: as

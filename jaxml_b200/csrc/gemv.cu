@@ -412,6 +412,17 @@ int run_gemv(const bf16* W, const bf16* X, long long Np, long long Kp, int M, co
   // prefetch, and a grid of at most one CTA per SM.
   const bool rows_ok = M <= 16 && e.kind != JX_EPI_GLU_SILU && e.kind != JX_EPI_GLU_GELU_TANH &&
                        e.kind != JX_EPI_PUSH_F32 && !e.pn_h && !e.pf_w && gemv_rows_groups(Np, grid > 0 ? grid : 148) > 0;
+  if (e.tn_x) {
+    // the normalisation tail runs in the row-split kernel only
+    const bool rows_taken = rows_ok && (g_gemv_impl == 3 || (g_gemv_impl == 0 && g_rows_by_shape && !gemv_uses_tc(Np, grid)));
+    if (!rows_taken) return JX_ERR_UNSUPPORTED;
+    if ((e.kind != JX_EPI_STORE && e.kind != JX_EPI_RESID) || e.out_rp > 0 || e.N % 256 || e.N > 8192 || e.ldo % 8 ||
+        !e.tn_w || !e.tn_sync || e.tn_rp < M || e.tn_rp % 8 ||
+        (e.tn_kind != JX_NORM_RMS && e.tn_kind != JX_NORM_GEMMA && e.tn_kind != JX_NORM_LAYER) ||
+        ((reinterpret_cast<uintptr_t>(e.out) | reinterpret_cast<uintptr_t>(e.tn_x) |
+          reinterpret_cast<uintptr_t>(e.tn_w) | reinterpret_cast<uintptr_t>(e.tn_b)) & 15))
+      return JX_ERR_ARG;
+  }
   if (g_gemv_impl == 3) {
     if (!rows_ok) return JX_ERR_SHAPE;
     return run_gemv_rows(W, X, Np, Kp, M, e, status, grid > 0 ? grid : 148, pdl, stream);

@@ -19,6 +19,120 @@
 
 namespace jxb {
 
+// ---- normalisation tail (jx_epilogue.tn_*) ----
+// One warp normalises row m of the projection's [M, ldo] bf16 output into the K128 operand tn_x with
+// jx_norm's vectorised arithmetic and summation order: there a block of d / 8 threads holds 8 values
+// each, sums them in order, adds over the lanes of each warp with an xor butterfly, stores each warp's
+// lane-0 value and adds those with a second butterfly, every lane keeping its own result.  Here lane l
+// plays lane l of every one of those d / 256 warps (w), so it holds the same partial sums, takes the
+// same lane-0 values from the butterflies and ends with the same per-lane totals: bit-identical output.
+constexpr int kTnMaxWarps = 32;   // d <= 8192
+
+__device__ __forceinline__ uint4 tn_ld(const bf16* p) {
+  return __ldcg(reinterpret_cast<const uint4*>(p));   // written by other CTAs of this grid
+}
+__device__ __forceinline__ void tn_unpack(const uint4& u, float* v) {
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+// jx_norm's two-stage block sum of per-(virtual warp, lane) partials part[w] (zero for w >= nw).  The
+// 32 butterflies are independent chains (no early exit), so their shuffles overlap.
+__device__ __forceinline__ float tn_block_sum(const float* part, int lane) {
+  float t = 0.f;
+#pragma unroll
+  for (int w = 0; w < kTnMaxWarps; ++w) {
+    float v = part[w];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const float lane0 = __shfl_sync(0xffffffffu, v, 0);
+    if (lane == w) t = lane0;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+  return t;
+}
+
+// Per-(virtual warp, lane) partial sums of row h: sum of x (mode 0), of x^2 (mode 1) or of (x - mean)^2
+// (mode 2).  Loads go out 8 at a time (predicated, no early exit) so that they overlap.
+__device__ __forceinline__ void tn_partials(const bf16* h, int nw, int lane, int mode, float mean, float* part) {
+#pragma unroll
+  for (int c0 = 0; c0 < kTnMaxWarps; c0 += 8) {
+    uint4 u[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      u[j] = c0 + j < nw ? tn_ld(h + ((c0 + j) * 32 + lane) * 8) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float x[8];
+      tn_unpack(u[j], x);
+      float s = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) s += mode == 0 ? x[i] : (mode == 1 ? x[i] * x[i] : (x[i] - mean) * (x[i] - mean));
+      part[c0 + j] = c0 + j < nw ? s : 0.f;
+    }
+  }
+}
+
+__device__ __forceinline__ void tail_norm_row(const EpiParams& e, int m, int lane) {
+  const int d = e.N, nw = d >> 8;
+  const bf16* h = reinterpret_cast<const bf16*>(e.out) + (long long)m * e.ldo;
+  const bf16* w = reinterpret_cast<const bf16*>(e.tn_w);
+  const bf16* b = reinterpret_cast<const bf16*>(e.tn_b);
+  bf16* X = reinterpret_cast<bf16*>(e.tn_x);
+  const bool layer = e.tn_kind == JX_NORM_LAYER;
+  float part[kTnMaxWarps];
+  float mean = 0.f;
+  if (layer) {
+    tn_partials(h, nw, lane, 0, 0.f, part);
+    mean = tn_block_sum(part, lane) / (float)d;
+  }
+  tn_partials(h, nw, lane, layer ? 2 : 1, mean, part);
+  const float den = sqrtf(tn_block_sum(part, lane) / (float)d + e.tn_eps);
+  const float inv = 1.0f / den;
+#pragma unroll
+  for (int c0 = 0; c0 < kTnMaxWarps; c0 += 4) {
+    uint4 uh[4], uw[4], ub[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int j0 = ((c0 + j) * 32 + lane) * 8;
+      const bool on = c0 + j < nw;
+      uh[j] = on ? tn_ld(h + j0) : make_uint4(0, 0, 0, 0);
+      uw[j] = on ? tn_ld(w + j0) : make_uint4(0, 0, 0, 0);
+      ub[j] = on && b ? tn_ld(b + j0) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (c0 + j >= nw) continue;
+      const int j0 = ((c0 + j) * 32 + lane) * 8;
+      float x[8], wv[8], bv[8], y[8];
+      tn_unpack(uh[j], x);
+      tn_unpack(uw[j], wv);
+      tn_unpack(ub[j], bv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (layer)
+          y[i] = rnd<bf16>((x[i] - mean) / den * wv[i] + (b ? bv[i] : 0.f));
+        else if (e.tn_kind == JX_NORM_RMS)
+          y[i] = rnd<bf16>(wv[i] * rnd<bf16>(x[i] / den));
+        else
+          y[i] = rnd<bf16>((wv[i] + 1.0f) * (x[i] * inv));
+      }
+      uint4 o;
+      o.x = pack_bf16x2(y[0], y[1]);
+      o.y = pack_bf16x2(y[2], y[3]);
+      o.z = pack_bf16x2(y[4], y[5]);
+      o.w = pack_bf16x2(y[6], y[7]);
+      *reinterpret_cast<uint4*>(X + k128_offset(m, j0, e.tn_rp)) = o;
+    }
+  }
+}
+
 template <int RG>
 struct RowsCfg {
   static constexpr int ROWS = 16 * RG;
@@ -35,7 +149,9 @@ struct RowsCfg {
   static constexpr int kSmem = kStages * kStageBytes + kPartBytes + 2 * kStages * 8 + 16;
 };
 
-template <int RG>
+// TAIL: the normalisation tail is compiled in (its code roughly doubles the kernel's registers, so the
+// kernel without it is a separate instantiation).
+template <int RG, bool TAIL>
 __global__ void __launch_bounds__(RowsCfg<RG>::kThreads, 1)
     gemv_rows_kernel(const bf16* __restrict__ W, const bf16* __restrict__ X, long long Np, long long Kp, EpiParams e,
                      int* status) {
@@ -169,15 +285,28 @@ __global__ void __launch_bounds__(RowsCfg<RG>::kThreads, 1)
   if (ok && !*dead)
     run_epilogue<bf16>(e, 0, 16, r0, C::ROWS, [&](int m, int j) { return part[m * C::kLd + j]; }, tid,
                        C::kConsumers * 32);
+  if (TAIL && e.tn_x) {
+    // the last CTA to finish its columns normalises the rows (see tail_norm_row)
+    __shared__ int tn_last;
+    __threadfence();
+    named_bar_sync(1, C::kConsumers * 32);
+    if (tid == 0) tn_last = atomicAdd(e.tn_sync, 1) == (int)gridDim.x - 1;
+    named_bar_sync(1, C::kConsumers * 32);
+    if (tn_last) {
+      __threadfence();
+      for (int m = tid >> 5; m < e.M; m += C::kConsumers) tail_norm_row(e, m, lane);
+      if (tid == 0) *e.tn_sync = 0;
+    }
+  }
 }
 
-template <int RG>
-static int launch_rows(const bf16* W, const bf16* X, long long Np, long long Kp, const EpiParams& e, int* status,
+template <int RG, bool TAIL>
+static int launch_rows_t(const bf16* W, const bf16* X, long long Np, long long Kp, const EpiParams& e, int* status,
                        bool pdl, cudaStream_t stream) {
   using C = RowsCfg<RG>;
   static bool configured = false;
   if (!configured) {
-    if (cudaFuncSetAttribute(gemv_rows_kernel<RG>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) !=
+    if (cudaFuncSetAttribute(gemv_rows_kernel<RG, TAIL>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) !=
         cudaSuccess)
       return JX_ERR_CUDA;
     configured = true;
@@ -192,7 +321,14 @@ static int launch_rows(const bf16* W, const bf16* X, long long Np, long long Kp,
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return launch_ex(&cfg, gemv_rows_kernel<RG>, W, X, Np, Kp, e, status) == cudaSuccess ? JX_OK : JX_ERR_CUDA;
+  return launch_ex(&cfg, gemv_rows_kernel<RG, TAIL>, W, X, Np, Kp, e, status) == cudaSuccess ? JX_OK : JX_ERR_CUDA;
+}
+
+template <int RG>
+static int launch_rows(const bf16* W, const bf16* X, long long Np, long long Kp, const EpiParams& e, int* status,
+                       bool pdl, cudaStream_t stream) {
+  return e.tn_x ? launch_rows_t<RG, true>(W, X, Np, Kp, e, status, pdl, stream)
+                : launch_rows_t<RG, false>(W, X, Np, Kp, e, status, pdl, stream);
 }
 
 // Row-group count (2 -> 32 rows, 3 -> 48 rows per CTA) for an Np-row projection on `sms` SMs: the

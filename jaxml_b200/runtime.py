@@ -383,6 +383,8 @@ class DecoderRuntime:
         self._push_pending = False
         # normalisation prologue of the decode projections (jx_epilogue.pn_*): epoch, arrivals, row flags
         self.pn_sync = torch.zeros(2 + 16, dtype=torch.int32, device=dev)
+        # the normalisation tail's arrival counter (self-resetting)
+        self.tn_sync = torch.zeros(1, dtype=torch.int32, device=dev)
         self._pending_norm = None
         if self.persistent_decode and PersistentDecode.eligible(self):
             self.fused_step = PersistentDecode(self)
@@ -495,8 +497,27 @@ class DecoderRuntime:
             self._pending_norm = None
             self._norm(acts, w=w, b=b)
 
+    # The norm that follows a decode projection's residual add can run in that projection's last CTA
+    # (jx_epilogue.tn_*: the row-split kernel's normalisation tail, bit-identical to jx_norm) instead of a
+    # separate launch.  Off: one SM normalising 16 rows x 4096 took 35-50 us per call, and the decode
+    # step went from 3.89-3.94 to 6.48-7.70 ms; the norm kernel spreads the same work over 16 CTAs.
+    tail_norm = False
+
+    def _tail_ok(self, acts, Np) -> bool:
+        """The decode projection of Np packed rows takes the row-split kernel with a normalisation tail."""
+        W = self.w
+        if not (self.tail_norm and self.comm is None and W.bf16 and acts["Mp"] == 16 and W.d % 256 == 0
+                and W.d <= 8192 and W.norm_kind in (N.JX_NORM_RMS, N.JX_NORM_GEMMA, N.JX_NORM_LAYER)):
+            return False
+        g = self.grid if self.grid > 0 else 148
+        if Np // 128 >= g:
+            return False   # the tcgen05 kernel
+        return any(Np % (16 * rg) == 0 and Np // (16 * rg) <= g for rg in (2, 3))
+
     def _linear(self, acts, w_t, Np, Kp, x_key, kind, *, N_valid, bias=None, out=None, ldo=0, out_rp=0, res=None,
-                ldr=0, res2=None, ldr2=0, K_logical=None, N_cols=None, pf=None):
+                ldr=0, res2=None, ldr2=0, K_logical=None, N_cols=None, pf=None, tail=None):
+        """One projection.  `tail` = (w, b): the norm of this call's output (the residual stream h) into
+        acts["xn"], in the projection's last CTA (the caller checked _tail_ok)."""
         W = self.w
         pending = self._pending_norm
         # the prologue needs one CTA per token row: at least M work items whichever decode kernel runs
@@ -525,9 +546,21 @@ class DecoderRuntime:
                                    self.stream_ptr())
             N.check(rc, "jx_linear_f32")
         elif acts["Mp"] <= 64:
+            if tail is not None:
+                e.tn_x, e.tn_rp, e.tn_w, e.tn_b = ptr(acts["xn"]), acts["Mp"], ptr(tail[0]), ptr(tail[1])
+                e.tn_sync, e.tn_kind, e.tn_eps = ptr(self.tn_sync), W.norm_kind, W.cfg.norm_eps
             rc = lib.jx_linear_decode(ptr(w_t), ptr(acts[x_key]), Np, Kp, acts["M"], e, ptr(self.gemv_ws),
                                       self.gemv_ws.numel(), ptr(self.gemv_counters), ptr(self.status), self.grid, 1,
                                       self.stream_ptr())
+            if rc == N.JX_ERR_UNSUPPORTED and tail is not None:
+                # another decode kernel was selected (jx_set_decode_linear_impl): a separate norm then
+                e.tn_x = None
+                rc = lib.jx_linear_decode(ptr(w_t), ptr(acts[x_key]), Np, Kp, acts["M"], e, ptr(self.gemv_ws),
+                                          self.gemv_ws.numel(), ptr(self.gemv_counters), ptr(self.status), self.grid,
+                                          1, self.stream_ptr())
+                N.check(rc, "jx_linear_decode")
+                self._norm(acts, w=tail[0], b=tail[1])
+                return
             N.check(rc, "jx_linear_decode")
         else:
             rc = lib.jx_linear_prefill(ptr(acts[x_key]), ptr(w_t), acts["Mp"], Np, Kp, e, ptr(self.status), 1,
@@ -662,6 +695,7 @@ class DecoderRuntime:
         tp = self.comm is not None
         parallel = fam == "neox" and cfg.use_parallel_residual
         store = N.JX_EPI_STORE_F32 if tp else N.JX_EPI_STORE
+        tail = None   # the post-attention norm in o_proj's tail
         # each decode projection warms L2 with the first weights of the one after it
         pf_gu = self._pf(lw.wgu, W.Np_gu, W.Kp_d)
         pf_d = self._pf(lw.wd, W.Np_d, W.Kp_f)
@@ -679,8 +713,11 @@ class DecoderRuntime:
             if not parallel:
                 self._allreduce(dst, M, acts)
         else:
+            pn = lw.norms["post_attention_layernorm"]
+            tail = (pn[0], pn[1]) if self._tail_ok(acts, W.Np_d) else None
             self._linear(acts, lw.wo, W.Np_d, W.Kp_o, "attn", N.JX_EPI_RESID, N_valid=d, bias=lw.bo,
-                         out=acts["h"], ldo=d, res=acts["h"], ldr=d, K_logical=W.Hq * hd, N_cols=d, pf=pf_gu)
+                         out=acts["h"], ldo=d, res=acts["h"], ldr=d, K_logical=W.Hq * hd, N_cols=d, pf=pf_gu,
+                         tail=tail)
         # ---- MLP input ----
         if fam == "gemma3":
             pa = lw.norms["post_attention_layernorm"]
@@ -693,6 +730,8 @@ class DecoderRuntime:
             pn = lw.norms["post_attention_layernorm"]
             if tp:
                 self._norm(acts, a=acts["tmp"], w=pn[0], b=pn[1])
+            elif tail is not None:
+                pass   # normalised in o_proj's tail
             elif not self._defer_norm(acts, pn[0], pn[1]):
                 self._norm(acts, w=pn[0], b=pn[1])
             mlp_in = "xn"
@@ -722,8 +761,14 @@ class DecoderRuntime:
             self._linear(acts, lw.wd, W.Np_d, W.Kp_f, "act", N.JX_EPI_RESID2, out=acts["h"], ldo=d,
                          res=acts["h"], ldr=d, res2=acts["tmp"], ldr2=d, **down_kw)
         else:
+            down_tail = None
+            if nx is not None and not (fam == "neox" and cfg.use_parallel_residual) and self._tail_ok(acts, W.Np_d):
+                inw = nx.norms["input_layernorm"]
+                down_tail = (inw[0], inw[1])
             self._linear(acts, lw.wd, W.Np_d, W.Kp_f, "act", N.JX_EPI_RESID, out=acts["h"], ldo=d,
-                         res=acts["h"], ldr=d, **down_kw)
+                         res=acts["h"], ldr=d, tail=down_tail, **down_kw)
+            if down_tail is not None:
+                return   # the next layer's input norm ran in down's tail
         # ---- next layer's input norm (the final norm is done by the caller) ----
         if nx is None:
             if fam == "gemma3":
@@ -988,6 +1033,7 @@ class DecoderRuntime:
             self.status.zero_()
             self.gemv_counters.zero_()
             self.sample_counters.zero_()
+            self.tn_sync.zero_()
             if self.fast_attn:
                 self.attn_counters.zero_()
                 self.attn_ws.zero_()   # (the queue form's claim counters live in its tail)

@@ -420,3 +420,57 @@ def test_decode_attention_back_to_back_launches(form):
         N.call("jx_unpack_k128", outs[layer].data_ptr(), B, Hq * hd, Mp, got.data_ptr(), N.JX_BF16, Hq * hd, _stream())
         torch.cuda.synchronize()
         assert torch.equal(got, want), layer
+
+
+@pytest.mark.parametrize("kind", ["rms", "gemma", "layer"])
+@pytest.mark.parametrize("M,d,K", [(16, 4096, 4096), (1, 4096, 14336), (5, 2048, 1024), (16, 512, 384)])
+def test_linear_decode_norm_tail(kind, M, d, K):
+    """Normalisation tail of the row-split projection (jx_epilogue.tn_*): the residual stream it writes and
+    the normalised activations its last CTA writes are bit-identical to the projection without the tail
+    followed by jx_norm, over back-to-back calls (the arrival counter resets itself); a tail on another
+    decode kernel is refused before any launch."""
+    N = _n()
+    torch.manual_seed(19)
+    Mp = 16
+    knd = {"rms": N.JX_NORM_RMS, "gemma": N.JX_NORM_GEMMA, "layer": N.JX_NORM_LAYER}[kind]
+    x = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+    wt = (torch.randn(d, K, device="cuda") * 0.02).to(torch.bfloat16)
+    Kp = _rup(K, 128)
+    xp, wp = _pack(N, x, Mp, Kp), _pack(N, wt, d, Kp)
+    nw = (1 + 0.1 * torch.randn(d, device="cuda")).to(torch.bfloat16)
+    nb = (0.1 * torch.randn(d, device="cuda")).to(torch.bfloat16) if kind == "layer" else None
+    h0 = (2 * torch.randn(M, d, device="cuda")).to(torch.bfloat16)
+    ws, cnt = _ws(N, d)
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    sync = torch.zeros(1, dtype=torch.int32, device="cuda")
+    N.call("jx_set_decode_linear_impl", 3)
+    try:
+        # reference: the projection's residual add, then jx_norm into the K128 activations
+        h_ref = h0.clone()
+        e = _epi(N, N.JX_EPI_RESID, M, d, h_ref, d, res=h_ref, ldr=d)
+        N.call("jx_linear_decode", wp.data_ptr(), xp.data_ptr(), d, Kp, M, e, ws.data_ptr(), ws.numel(),
+               cnt.data_ptr(), status.data_ptr(), 148, 1, _stream())
+        xn_ref = torch.zeros(Mp * d, dtype=torch.bfloat16, device="cuda")
+        a = N.JxNormArgs()
+        a.M, a.d, a.eps, a.kind = M, d, 1e-5, knd
+        a.h, a.ldh, a.w, a.b = h_ref.data_ptr(), d, nw.data_ptr(), None if nb is None else nb.data_ptr()
+        a.out, a.ldo, a.out_rp, a.status = xn_ref.data_ptr(), d, Mp, status.data_ptr()
+        N.call("jx_norm", a, N.JX_BF16, 1, _stream())
+        torch.cuda.synchronize()
+        for rep in range(3):
+            h = h0.clone()
+            xn = torch.zeros(Mp * d, dtype=torch.bfloat16, device="cuda")
+            e2 = _epi(N, N.JX_EPI_RESID, M, d, h, d, res=h, ldr=d)
+            e2.tn_x, e2.tn_rp, e2.tn_w, e2.tn_b = xn.data_ptr(), Mp, nw.data_ptr(), None if nb is None else nb.data_ptr()
+            e2.tn_sync, e2.tn_kind, e2.tn_eps = sync.data_ptr(), knd, 1e-5
+            N.call("jx_linear_decode", wp.data_ptr(), xp.data_ptr(), d, Kp, M, e2, ws.data_ptr(), ws.numel(),
+                   cnt.data_ptr(), status.data_ptr(), 148, 1, _stream())
+            torch.cuda.synchronize()
+            assert int(status.item()) == 0 and int(sync.item()) == 0
+            assert torch.equal(h, h_ref)
+            assert torch.equal(xn, xn_ref), rep
+        N.call("jx_set_decode_linear_impl", 1)
+        assert N.load().jx_linear_decode(wp.data_ptr(), xp.data_ptr(), d, Kp, M, e2, ws.data_ptr(), ws.numel(),
+                                         cnt.data_ptr(), status.data_ptr(), 148, 1, _stream()) == N.JX_ERR_UNSUPPORTED
+    finally:
+        N.call("jx_set_decode_linear_impl", 0)

@@ -123,3 +123,46 @@ def test_persistent_decode_rejects_unsupported_shapes():
     assert N.load().jx_decode_step(a, None) == N.JX_ERR_SHAPE
     a.M, a.hd = 4, 64
     assert N.load().jx_decode_step(a, None) == N.JX_ERR_SHAPE
+
+
+def test_norm_tail_decode_step_is_bit_identical():
+    """The per-op decode step with the norms in the o_proj / down tails (DecoderRuntime.tail_norm) gives
+    the same logits, tokens and caches, bit for bit, as with separate jx_norm launches, and launches two
+    kernels fewer per layer."""
+    from jaxml_b200.runtime import DecoderRuntime, ModelWeights
+
+    cfg = _cfg(d=512, H=4, Hkv=2, L=3, V=1000)
+    params = O.init_params("llama", cfg, seed=4, dtype=torch.bfloat16)
+    gw = torch.Generator().manual_seed(10)
+    body = params["params"]["model"]
+    for lp in [body[f"layers_{i}"][n] for i in range(cfg.num_layers)
+               for n in ("input_layernorm", "post_attention_layernorm")]:
+        lp["weight"] = (1 + 0.1 * torch.randn(cfg.hidden_size, generator=gw)).to(torch.bfloat16)
+    B, P, T, n = 7, 45, 256, 5
+    g = torch.Generator().manual_seed(8)
+    ids = torch.randint(0, cfg.vocab_size, (B, P), generator=g, dtype=torch.int32)
+    mask = torch.arange(P)[None, :] < torch.tensor([45, 40, 33, 45, 12, 30, 44])[:, None]
+    runs = {}
+    old = DecoderRuntime.tail_norm
+    try:
+        for on in (True, False):
+            DecoderRuntime.tail_norm = on
+            rt = DecoderRuntime(ModelWeights("llama", cfg, params, torch.bfloat16, "cuda:0"), B, T)
+            key, sub = TF.split(TF.prng_key(0))
+            rt.reset(mask.cuda(), key, sub, n + 1)
+            rt.prefill(ids.cuda(), True, 1.0)
+            logits = [rt.logits_buf()[:B].clone()]
+            for _ in range(n):
+                rt.decode_step(True, 1.0)
+                logits.append(rt.logits_buf()[:B].clone())
+            torch.cuda.synchronize()
+            rt.check_status()
+            runs[on] = (logits, rt.tokens_out[:, :n + 1].clone(), rt.k_cache.clone(), rt.v_cache.clone(),
+                        rt.count_launches_per_decode_step())
+    finally:
+        DecoderRuntime.tail_norm = old
+    a, b = runs[True], runs[False]
+    for la, lb in zip(a[0], b[0]):
+        assert torch.equal(la, lb)
+    assert torch.equal(a[1], b[1]) and torch.equal(a[2], b[2]) and torch.equal(a[3], b[3])
+    assert a[4] == b[4] - 2 * cfg.num_layers + 1   # no norm after o_proj; none after down except the last
