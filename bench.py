@@ -133,8 +133,8 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-temp", action="store_true", help="skip the temperature-0.8 decode timing")
-    ap.add_argument("--separate-norms", action="store_true",
-                    help="decode step: every norm as its own jx_norm launch (no normalisation tails)")
+    ap.add_argument("--tail-norms", action="store_true",
+                    help="decode step: the norms after o_proj / down in those projections' last CTA")
     ap.add_argument("--per-op", action="store_true",
                     help="decode with one kernel launch per op instead of the persistent decode-step kernel")
     ap.add_argument("--e2e-tokens", type=int, default=None,
@@ -400,11 +400,11 @@ def gpu_arm(args):
         from jaxml_b200 import _native as N
 
         N.call("jx_set_decode_attention_impl", args.attn_impl)
-    if args.tp_pull or args.per_op or args.separate_norms:
+    if args.tp_pull or args.per_op or args.tail_norms:
         from jaxml_b200.runtime import DecoderRuntime
 
-        if args.separate_norms:
-            DecoderRuntime.tail_norm = False
+        if args.tail_norms:
+            DecoderRuntime.tail_norm = True
 
         if args.tp_pull:
             DecoderRuntime.peer_push = False

@@ -92,6 +92,74 @@ __device__ __forceinline__ void key_range(const DAttnParams& p, int b, int& lo, 
   lo = (p.window > 0 && valid > p.window) ? valid - p.window : 0;
 }
 
+// Exact softmax normaliser of each query row of a head group from its split statistics st[row][split]
+// (max, sum): M = max over the splits, L = sum over the splits in split order of sum * exp(max - M).  All
+// 128 threads: 8 lanes per row (rows tid / 8 < 16) load the statistics at once; the ordered sum passes
+// each split's term to the row's lanes by shuffles, so L is added in split order, as a loop over the
+// splits would (bit-identical).  Writes Ms[row], Ls[row] for rows < 16 (rows >= n_rep: -inf, 0).
+__device__ __forceinline__ void split_normaliser(const float* st_group, int n_rep, int n_splits, int n_active,
+                                                 float* Ms, float* Ls) {
+  const int row = threadIdx.x >> 3, j = threadIdx.x & 7, base = (threadIdx.x & 31) & ~7;
+  const bool on = row < n_rep;
+  const float* st = st_group + (long long)row * n_splits * 2;
+  float M = -INFINITY;
+#pragma unroll 4
+  for (int s = j; s < n_active; s += 8)
+    if (on) M = fmaxf(M, __ldcg(st + s * 2));
+  M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 4));
+  M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 2));
+  M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 1));
+  float L = 0.f;
+  for (int s0 = 0; s0 < n_active; s0 += 8) {
+    const int sj = s0 + j;
+    const float term = on && sj < n_active ? __ldcg(st + sj * 2 + 1) * expf(__ldcg(st + sj * 2) - M) : 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float t = __shfl_sync(0xffffffffu, term, base + k);
+      if (s0 + k < n_active) L += t;
+    }
+  }
+  if (j == 0) {
+    Ms[row] = on ? M : -INFINITY;
+    Ls[row] = on ? L : 0.f;
+  }
+}
+
+// The last pv CTA of a head group: out = bf16(sum over the splits, in split order, of the float32
+// partials), four outputs a thread at a time with their partials' loads issued together.
+template <int HD>
+__device__ __forceinline__ void sum_split_partials(const float* opart_group, int n_rep, int n_splits, int n_active,
+                                                   bf16* out, long long out_rp, int b, long long col0) {
+  const int total = n_rep * HD;
+  for (int i0 = threadIdx.x; i0 < total; i0 += 4 * 128) {
+    float sum[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int s0 = 0; s0 < n_active; s0 += 8) {
+      float v[4][8];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int idx = i0 + q * 128;
+        const int row = idx / HD, col = idx % HD;
+        const float* src = opart_group + ((long long)row * n_splits) * HD + col;
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          v[q][k] = idx < total && s0 + k < n_active ? __ldcg(src + (long long)(s0 + k) * HD) : 0.f;
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          if (s0 + k < n_active) sum[q] += v[q][k];
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int idx = i0 + q * 128;
+      if (idx >= total) continue;
+      const int row = idx / HD, col = idx % HD;
+      out[k128_offset(b, col0 + (long long)row * HD + col, out_rp)] = __float2bfloat16_rn(sum[q]);
+    }
+  }
+}
+
 // RQ: rows of the query (scores) / probability (pv) tile in shared memory, 16 or, when a head group has
 // at most 8 query heads, 8 (the MMA's rows 8-15 are then zero registers).  The smaller tiles let 6 CTAs
 // share an SM instead of 5, so a 768-slot cache (6 splits x 128 head groups) runs in one wave.
@@ -334,31 +402,29 @@ __global__ void __launch_bounds__(128) dattn_pv_kernel(const __grid_constant__ C
   pdl_wait();
   if (threadIdx.x == 0)
     for (int i = n_early; i < n_tiles; ++i) issue(i);
-  // exact softmax normaliser of each row from the split statistics
-  if (threadIdx.x < 16) {
-    const int row = threadIdx.x;
-    float M = -INFINITY, L = 0.f;
-    if (row < p.n_rep) {
-      const float* st = p.stats + ((long long)b * p.Hq + kvh * p.n_rep + row) * p.n_splits * 2;
-      for (int s2 = 0; s2 < n_active; ++s2) M = fmaxf(M, st[s2 * 2]);
-      for (int s2 = 0; s2 < n_active; ++s2) L += st[s2 * 2 + 1] * expf(st[s2 * 2] - M);
-    }
-    Ms[row] = M;
-    Ls[row] = L;
+  // this CTA's scores (coalesced reads, issued before the statistics are combined)
+  float sv[RQ];
+#pragma unroll
+  for (int i = 0; i < RQ; ++i) {
+    const int idx = threadIdx.x + i * 128;
+    const int row = idx / kDaKeys, t = t0 + idx % kDaKeys;
+    sv[i] = row < p.n_rep && t < t1 ? __ldcg(p.sc + ((long long)b * p.Hq + kvh * p.n_rep + row) * p.T + t) : 0.f;
   }
+  // exact softmax normaliser of each row from the split statistics
+  split_normaliser(p.stats + ((long long)b * p.Hq + kvh * p.n_rep) * p.n_splits * 2, p.n_rep, p.n_splits, n_active,
+                   Ms, Ls);
   __syncthreads();
 
   const int mi = lane >> 3, r8 = lane & 7;
   const int r_lo = lane >> 2, r_hi = r_lo + 8;
-  // Probabilities of this CTA's keys, computed once (coalesced score reads) into a padded bf16 tile
-  // [16 rows][kDaKeys + 8] that every warp reads with ldmatrix.
-  for (int idx = threadIdx.x; idx < RQ * kDaKeys; idx += 128) {
+  // Probabilities of this CTA's keys, computed once into a padded bf16 tile [RQ rows][kDaKeys + 8] that
+  // every warp reads with ldmatrix.
+#pragma unroll
+  for (int i = 0; i < RQ; ++i) {
+    const int idx = threadIdx.x + i * 128;
     const int row = idx / kDaKeys, k = idx % kDaKeys, t = t0 + k;
     float pv = 0.f;
-    if (row < p.n_rep && t < t1) {
-      const float s = __ldcg(p.sc + ((long long)b * p.Hq + kvh * p.n_rep + row) * p.T + t);
-      pv = rnd<bf16>(expf(s - Ms[row]) / Ls[row]);
-    }
+    if (row < p.n_rep && t < t1) pv = rnd<bf16>(expf(sv[i] - Ms[row]) / Ls[row]);
     ptile[row * kPLd + k] = __float2bfloat16_rn(pv);
   }
   __syncthreads();
@@ -411,14 +477,8 @@ __global__ void __launch_bounds__(128) dattn_pv_kernel(const __grid_constant__ C
   __syncthreads();
   if (!last_flag) return;
   __threadfence();
-  for (int idx = threadIdx.x; idx < p.n_rep * HD; idx += 128) {
-    const int row = idx / HD, col = idx % HD;
-    const float* src = p.opart + (((long long)b * p.Hq + kvh * p.n_rep + row) * p.n_splits) * HD + col;
-    float sum = 0.f;
-    for (int s2 = 0; s2 < n_active; ++s2) sum += __ldcg(src + (long long)s2 * HD);
-    const long long ocol = (long long)(kvh * p.n_rep + row) * HD + col;
-    p.out[k128_offset(b, ocol, p.out_rp)] = __float2bfloat16_rn(sum);
-  }
+  sum_split_partials<HD>(p.opart + (((long long)b * p.Hq + kvh * p.n_rep) * p.n_splits) * HD, p.n_rep, p.n_splits,
+                         n_active, p.out, p.out_rp, b, (long long)kvh * p.n_rep * HD);
   if (threadIdx.x == 0) p.counters[b * p.Hkv + kvh] = 0;
 }
 
