@@ -95,28 +95,48 @@ __device__ __forceinline__ void key_range(const DAttnParams& p, int b, int& lo, 
 // Exact softmax normaliser of each query row of a head group from its split statistics st[row][split]
 // (max, sum): M = max over the splits, L = sum over the splits in split order of sum * exp(max - M).  All
 // 128 threads: 8 lanes per row (rows tid / 8 < 16) load the statistics at once; the ordered sum passes
-// each split's term to the row's lanes by shuffles, so L is added in split order, as a loop over the
-// splits would (bit-identical).  Writes Ms[row], Ls[row] for rows < 16 (rows >= n_rep: -inf, 0).
+// each split's (sum, exp) to the row's lanes by shuffles, so L is accumulated in split order with one
+// fused multiply-add a split, as a loop over the splits compiles (bit-identical).  Writes Ms[row], Ls[row] for rows < 16 (rows >= n_rep: -inf, 0).
 __device__ __forceinline__ void split_normaliser(const float* st_group, int n_rep, int n_splits, int n_active,
                                                  float* Ms, float* Ls) {
   const int row = threadIdx.x >> 3, j = threadIdx.x & 7, base = (threadIdx.x & 31) & ~7;
   const bool on = row < n_rep;
   const float* st = st_group + (long long)row * n_splits * 2;
+  // chunks of 64 splits: lane j holds splits c0 + 8 i + j, i < 8, all loaded before they are used
   float M = -INFINITY;
-#pragma unroll 4
-  for (int s = j; s < n_active; s += 8)
-    if (on) M = fmaxf(M, __ldcg(st + s * 2));
+  for (int c0 = 0; c0 < n_active; c0 += 64) {
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int sj = c0 + 8 * i + j;
+      v[i] = on && sj < n_active ? __ldcg(st + sj * 2) : -INFINITY;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) M = fmaxf(M, v[i]);
+  }
   M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 4));
   M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 2));
   M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, 1));
   float L = 0.f;
-  for (int s0 = 0; s0 < n_active; s0 += 8) {
-    const int sj = s0 + j;
-    const float term = on && sj < n_active ? __ldcg(st + sj * 2 + 1) * expf(__ldcg(st + sj * 2) - M) : 0.f;
+  for (int c0 = 0; c0 < n_active; c0 += 64) {
+    float mx[8], sm[8];
 #pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const float t = __shfl_sync(0xffffffffu, term, base + k);
-      if (s0 + k < n_active) L += t;
+    for (int i = 0; i < 8; ++i) {
+      const int sj = c0 + 8 * i + j;
+      const bool in = on && sj < n_active;
+      mx[i] = in ? __ldcg(st + sj * 2) : 0.f;
+      sm[i] = in ? __ldcg(st + sj * 2 + 1) : 0.f;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float e = expf(mx[i] - M);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        // L += sum * e as one fused multiply-add, as the compiler contracts it in a loop over the splits
+        const float sk = __shfl_sync(0xffffffffu, sm[i], base + k);
+        const float ek = __shfl_sync(0xffffffffu, e, base + k);
+        if (c0 + 8 * i + k < n_active) L = fmaf(sk, ek, L);
+      }
     }
   }
   if (j == 0) {
@@ -402,14 +422,17 @@ __global__ void __launch_bounds__(128) dattn_pv_kernel(const __grid_constant__ C
   pdl_wait();
   if (threadIdx.x == 0)
     for (int i = n_early; i < n_tiles; ++i) issue(i);
-  // this CTA's scores (coalesced reads, issued before the statistics are combined)
-  float sv[RQ];
-#pragma unroll
-  for (int i = 0; i < RQ; ++i) {
+  // this CTA's scores (coalesced reads, issued before the statistics are combined; with 16-row tiles they
+  // are read afterwards, which keeps the kernel at 5 CTAs per SM)
+  constexpr bool kEarly = RQ == 8;
+  auto score = [&](int i) {
     const int idx = threadIdx.x + i * 128;
     const int row = idx / kDaKeys, t = t0 + idx % kDaKeys;
-    sv[i] = row < p.n_rep && t < t1 ? __ldcg(p.sc + ((long long)b * p.Hq + kvh * p.n_rep + row) * p.T + t) : 0.f;
-  }
+    return row < p.n_rep && t < t1 ? __ldcg(p.sc + ((long long)b * p.Hq + kvh * p.n_rep + row) * p.T + t) : 0.f;
+  };
+  float sv[kEarly ? RQ : 1];
+#pragma unroll
+  for (int i = 0; i < (kEarly ? RQ : 0); ++i) sv[i] = score(i);
   // exact softmax normaliser of each row from the split statistics
   split_normaliser(p.stats + ((long long)b * p.Hq + kvh * p.n_rep) * p.n_splits * 2, p.n_rep, p.n_splits, n_active,
                    Ms, Ls);
@@ -424,7 +447,7 @@ __global__ void __launch_bounds__(128) dattn_pv_kernel(const __grid_constant__ C
     const int idx = threadIdx.x + i * 128;
     const int row = idx / kDaKeys, k = idx % kDaKeys, t = t0 + k;
     float pv = 0.f;
-    if (row < p.n_rep && t < t1) pv = rnd<bf16>(expf(sv[i] - Ms[row]) / Ls[row]);
+    if (row < p.n_rep && t < t1) pv = rnd<bf16>(expf((kEarly ? sv[kEarly ? i : 0] : score(i)) - Ms[row]) / Ls[row]);
     ptile[row * kPLd + k] = __float2bfloat16_rn(pv);
   }
   __syncthreads();
