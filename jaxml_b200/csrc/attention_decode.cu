@@ -218,7 +218,10 @@ __global__ void __launch_bounds__(128) dattn_scores_kernel(const __grid_constant
     mbar_init(&bar[0], 1);
     mbar_init(&bar[1], 1);
     fence_barrier_init();
-    while (n_early < n_tiles && t0 + (n_early + 1) * kDaTile <= valid - 1) issue(n_early++);
+    // with the append fused in, this kernel writes this step's key itself and patches it into the
+    // loaded tile, so that tile loads early too; otherwise the kernel before wrote it
+    const bool fused_append = p.qkv != nullptr;
+    while (n_early < n_tiles && (fused_append || t0 + (n_early + 1) * kDaTile <= valid - 1)) issue(n_early++);
   }
   pdl_wait();
   // the pv kernel after this one loads values before its own wait: release it only now
@@ -491,9 +494,10 @@ __global__ void __launch_bounds__(128) dattn_pv_kernel(const __grid_constant__ C
       if (row < p.n_rep)
         p.opart[(((long long)b * p.Hq + kvh * p.n_rep + row) * p.n_splits + split) * HD + col] = acc[nt][e];
     }
-  __threadfence();
+  // one fence after the barrier releases every thread's partial stores (cumulativity), then the arrival
   __syncthreads();
   if (threadIdx.x == 0) {
+    __threadfence();
     const int prev = atomicAdd(&p.counters[b * p.Hkv + kvh], 1);
     last_flag = (prev == n_active - 1);
   }
