@@ -7,7 +7,9 @@
 // A query row with no visible key attends uniformly to every slot of the buffer (:385-386): the first
 // uniform_T slots, the reference's cache length when the prompt ran (the rest are zero then).
 //
-// One CTA per (64 query rows, query head, batch row); each warp owns 16 rows.  To round the normalised
+// One CTA per (64 query rows, HPC query heads of one KV head, batch row); each warp owns 16 rows of one
+// head, so the HPC heads' warps share every K / V tile the CTA loads (HPC = 4, 2 or 1: the largest that
+// divides the heads per KV head).  To round the normalised
 // probabilities exactly as the reference does, the kernel makes two passes over the key tiles: pass 1
 // finds each row's max and exp-sum, pass 2 recomputes the identical scores, forms bf16(exp(s-m)/l) and
 // accumulates P.V.  K and V tiles arrive by TMA (the cache's 2-D tensor maps, 128-byte swizzle) in a
@@ -37,9 +39,10 @@ __device__ __forceinline__ uint32_t pswz(uint32_t block_base, int r, int c) {
   return block_base + r * 128 + ((c ^ (r & 7)) << 4);
 }
 
-template <int HD, int KT>
-__global__ void __launch_bounds__(128) pattn_kernel(const __grid_constant__ CUtensorMap kmap,
-                                                    const __grid_constant__ CUtensorMap vmap, PAttnParams p) {
+template <int HD, int KT, int HPC>
+__global__ void __launch_bounds__(128 * HPC) pattn_kernel(const __grid_constant__ CUtensorMap kmap,
+                                                          const __grid_constant__ CUtensorMap vmap, PAttnParams p) {
+  constexpr int NT = 128 * HPC;                  // threads
   constexpr int NB = HD / 64;                    // 64-column blocks per head
   constexpr int QBLK = 64 * 128;                 // bytes of one [64 rows x 64 cols] Q block
   constexpr int TBLK = KT * 128;                 // bytes of one [KT rows x 64 cols] K/V block
@@ -48,15 +51,19 @@ __global__ void __launch_bounds__(128) pattn_kernel(const __grid_constant__ CUte
   constexpr int NO = HD / 8;                     // output n8 tiles per warp
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* qs = smem;                            // NB * QBLK
-  uint8_t* ks = qs + NB * QBLK;                  // 2 stages
+  uint8_t* qs_all = smem;                        // HPC heads x NB * QBLK
+  uint8_t* ks = qs_all + HPC * NB * QBLK;        // 2 stages
   uint8_t* vs = ks + 2 * TILE;                   // 2 stages
   uint64_t* bar = reinterpret_cast<uint64_t*>(vs + 2 * TILE);
-  int* dead_rows = reinterpret_cast<int*>(bar + 2);   // [64]
+  int* dead_rows = reinterpret_cast<int*>(bar + 2);   // [HPC][64]
 
-  const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int kvh = h / p.n_rep;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qt = blockIdx.x, b = blockIdx.z;
+  const int h0 = blockIdx.y * HPC;               // first query head of this CTA
+  const int kvh = h0 / p.n_rep;
+  const int hw = (threadIdx.x >> 5) >> 2;        // this warp's head within the CTA
+  const int h = h0 + hw;
+  const int warp = (threadIdx.x >> 5) & 3, lane = threadIdx.x & 31;   // warp within its head's rows
+  uint8_t* qs = qs_all + hw * NB * QBLK;
   const int s0 = qt * 64;
   pdl_trigger();
   pdl_wait();
@@ -90,13 +97,15 @@ __global__ void __launch_bounds__(128) pattn_kernel(const __grid_constant__ CUte
     if (n_loads > 0) issue(0);
     if (n_loads > 1) issue(1);
   }
-  if (threadIdx.x < 64) dead_rows[threadIdx.x] = 0;
-  // Q tile (rows past S are zero)
-  for (int idx = threadIdx.x; idx < 64 * (HD / 8); idx += 128) {
-    const int r = idx / (HD / 8), cg = idx % (HD / 8);
+  if (threadIdx.x < 64 * HPC) dead_rows[threadIdx.x] = 0;
+  // Q tiles of the CTA's heads (rows past S are zero)
+  for (int idx = threadIdx.x; idx < HPC * 64 * (HD / 8); idx += NT) {
+    const int hl = idx / (64 * (HD / 8)), rem = idx % (64 * (HD / 8));
+    const int r = rem / (HD / 8), cg = rem % (HD / 8);
     uint4 v = make_uint4(0, 0, 0, 0);
-    if (s0 + r < p.S) v = *reinterpret_cast<const uint4*>(p.q + (((long long)b * p.S + s0 + r) * p.Hq + h) * HD + cg * 8);
-    const uint32_t a = pswz(smem_u32(qs + (cg >> 3) * QBLK), r, cg & 7);
+    if (s0 + r < p.S)
+      v = *reinterpret_cast<const uint4*>(p.q + (((long long)b * p.S + s0 + r) * p.Hq + h0 + hl) * HD + cg * 8);
+    const uint32_t a = pswz(smem_u32(qs_all + hl * NB * QBLK + (cg >> 3) * QBLK), r, cg & 7);
     asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(a), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w));
   }
   __syncthreads();
@@ -225,7 +234,7 @@ __global__ void __launch_bounds__(128) pattn_kernel(const __grid_constant__ CUte
     const int row = hh ? row_hi : row_lo;
     if (row >= p.S) continue;
     if (m[hh] == -INFINITY) {
-      if ((lane & 3) == 0) dead_rows[row - s0] = 1;
+      if ((lane & 3) == 0) dead_rows[hw * 64 + row - s0] = 1;
       continue;
     }
     const long long orow = (long long)b * p.S + row;
@@ -240,35 +249,36 @@ __global__ void __launch_bounds__(128) pattn_kernel(const __grid_constant__ CUte
   __syncthreads();
   // all-masked rows: uniform weights bf16(1/Tu) over the first Tu slots of the buffer
   const float pu = rnd<bf16>(1.0f / (float)p.uniform_T);
-  for (int r = 0; r < 64; ++r) {
+  for (int r = 0; r < 64 * HPC; ++r) {
     if (!dead_rows[r]) continue;
-    const long long orow = (long long)b * p.S + s0 + r;
-    for (int d = threadIdx.x; d < HD; d += 128) {
+    const long long orow = (long long)b * p.S + s0 + (r & 63);
+    for (int d = threadIdx.x; d < HD; d += NT) {
       float acc = 0.f;
       const bf16* vcol = p.v_plain + ((p.layer_row0 + (long long)b * p.T) * p.Hkv + kvh) * HD + d;
       for (int j = 0; j < p.uniform_T; ++j) acc += pu * __bfloat162float(vcol[(long long)j * p.Hkv * HD]);
-      p.out[k128_offset(orow, (long long)h * HD + d, p.out_rp)] = __float2bfloat16_rn(acc);
+      p.out[k128_offset(orow, (long long)(h0 + (r >> 6)) * HD + d, p.out_rp)] = __float2bfloat16_rn(acc);
     }
   }
 }
 
-template <int HD, int KT>
-static int launch_pattn(const jx_pattn_args& a, const PAttnParams& p, bool pdl, cudaStream_t s) {
+template <int HD, int KT, int HPC>
+static int launch_pattn_h(const jx_pattn_args& a, const PAttnParams& p, bool pdl, cudaStream_t s) {
   CUtensorMap km, vm;
   const long long cols = (long long)a.Hkv * HD;
   int rc = make_tmap_2d_bf16_box(&km, a.k_base, a.cache_rows, cols, cols, KT);
   if (rc == JX_OK) rc = make_tmap_2d_bf16_box(&vm, a.v_base, a.cache_rows, cols, cols, KT);
   if (rc != JX_OK) return rc;
-  const int smem = 1024 + (HD / 64) * 64 * 128 + 4 * KT * HD * 2 + 16 + 64 * 4;
+  const int smem = 1024 + HPC * (HD / 64) * 64 * 128 + 4 * KT * HD * 2 + 16 + HPC * 64 * 4;
   static bool configured = false;
   if (!configured) {
-    if (cudaFuncSetAttribute(pattn_kernel<HD, KT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    if (cudaFuncSetAttribute(pattn_kernel<HD, KT, HPC>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+        cudaSuccess)
       return JX_ERR_CUDA;
     configured = true;
   }
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((a.S + 63) / 64, a.Hq, a.B);
-  cfg.blockDim = dim3(128);
+  cfg.gridDim = dim3((a.S + 63) / 64, a.Hq / HPC, a.B);
+  cfg.blockDim = dim3(128 * HPC);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -276,7 +286,16 @@ static int launch_pattn(const jx_pattn_args& a, const PAttnParams& p, bool pdl, 
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return launch_ex(&cfg, pattn_kernel<HD, KT>, km, vm, p) == cudaSuccess ? JX_OK : JX_ERR_CUDA;
+  return launch_ex(&cfg, pattn_kernel<HD, KT, HPC>, km, vm, p) == cudaSuccess ? JX_OK : JX_ERR_CUDA;
+}
+
+// Heads per CTA: the largest of 4, 2, 1 that divides the heads per KV head (all of a CTA's heads read
+// the same K / V tiles).
+template <int HD, int KT>
+static int launch_pattn(const jx_pattn_args& a, const PAttnParams& p, bool pdl, cudaStream_t s) {
+  if (p.n_rep % 4 == 0) return launch_pattn_h<HD, KT, 4>(a, p, pdl, s);
+  if (p.n_rep % 2 == 0) return launch_pattn_h<HD, KT, 2>(a, p, pdl, s);
+  return launch_pattn_h<HD, KT, 1>(a, p, pdl, s);
 }
 
 int run_prefill_attention(const jx_pattn_args& a, bool pdl, cudaStream_t stream) {

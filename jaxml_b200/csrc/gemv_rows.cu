@@ -217,9 +217,10 @@ __global__ void __launch_bounds__(RowsCfg<RG>::kThreads, 1)
   const int cw = (warp - 1) % RG;     // weight rows [cw * 16, + 16)
   const int ksl = (warp - 1) / RG;    // K steps [ksl * 2, + 2) of every chunk
   const int tid = threadIdx.x - 32;
-  // The tensor-core accumulator is folded into an IEEE float32 sum every 8 chunks (16 MMAs): one chain over
-  // the whole K rounds noticeably worse than float32 sums (bf16 results flip more often); every 4 chunks
-  // cost up to 0.8 us more on the down projection.
+  // The tensor-core accumulator is folded into an IEEE float32 sum every 4 chunks (8 MMAs): one chain over
+  // the whole K rounds noticeably worse than float32 sums (bf16 results flip more often).  Every 8 chunks
+  // saved up to 0.8 us on the down projection but took a small bf16 model's decode logits to 1.5 ulps
+  // (0.0234) from the oracle's, past the 2e-2 bound that every 4 chunks meets.
   float acc[2][4] = {}, sum[2][4] = {};
   bool ok = true;
   const int mi = lane >> 3, r8 = lane & 7;
@@ -251,7 +252,7 @@ __global__ void __launch_bounds__(RowsCfg<RG>::kThreads, 1)
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
-    if ((i & 7) == 7 || i == kc - 1) {
+    if ((i & 3) == 3 || i == kc - 1) {
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
