@@ -483,6 +483,11 @@ def gpu_arm(args):
         gathered = [torch.empty_like(toks) for _ in range(world)]
         dist.all_gather(gathered, toks)
         ranks_identical = all(torch.equal(gathered[0], t) for t in gathered)
+        # the prompt's logits at TP=N, gathered over the vocabulary shards (every rank takes part)
+        rt.reset(torch.ones(B, P, dtype=torch.bool, device=dev), key, sub, n_new)
+        rt.prefill(ids_d, True, 1.0)
+        lgN = rt.comm.all_gather_vocab(rt.logits_buf()[:B]).float().cpu()
+        rt.check_status()
         vs1 = None
         if rank == 0:
             k = min(n_new, 16)
@@ -493,13 +498,31 @@ def gpu_arm(args):
                 eng1.init_params(params1)
                 del params1
                 rt1 = eng1._runtime_for(B, engine.buffer_length(P, n_new))
+                rt1.reset(torch.ones(B, P, dtype=torch.bool, device=dev), key, sub, k)
+                rt1.prefill(ids_d, True, 1.0)
+                lg1 = rt1.logits_buf()[:B].float().cpu()
                 t1 = rt1.generate(ids_d, torch.ones(B, P, dtype=torch.bool, device=dev), k, True, 1.0, 0)[:, :k].cpu()
                 rt1.check_status()
                 eq = t1 == gathered[0][:, :k].cpu()
                 first = next((j for j in range(k) if not bool(eq[:, j].all())), None)
                 vs1 = {"tokens": k, "token_match_frac": float(eq.float().mean().item()), "first_divergence_step": first,
                        "note": "greedy tokens of a TP=1 engine on rank 0's GPU, same weights and prompt; bf16 "
-                               "float32-partial sums in another order can flip a near-tie"}
+                               "float32-partial sums in another order can flip a near-tie, after which the "
+                               "sequences differ"}
+                if lgN.shape == lg1.shape:
+                    dlt = (lgN - lg1).abs()
+                    top2 = lg1.topk(2, dim=-1).values
+                    gap = top2[:, 0] - top2[:, 1]
+                    differ = lgN.argmax(-1) != lg1.argmax(-1)
+                    vs1["prompt_logits"] = {
+                        "max_abs_diff": float(dlt.max().item()), "mean_abs_diff": float(dlt.mean().item()),
+                        "max_abs_logit": float(lg1.abs().max().item()),
+                        "rows_argmax_differ": int(differ.sum().item()),
+                        "rows_argmax_differ_with_top2_gap_above_max_diff":
+                            int((differ & (gap > dlt.max(dim=-1).values * 2)).sum().item()),
+                        "min_top2_gap": float(gap.min().item())}
+                else:
+                    vs1["prompt_logits"] = {"skipped": "gathered %s vs %s" % (tuple(lgN.shape), tuple(lg1.shape))}
                 del rt1, eng1
                 torch.cuda.empty_cache()
             else:

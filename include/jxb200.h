@@ -322,8 +322,8 @@ int jx_norm(const jx_norm_args* args, int dtype, int pdl, void* stream);
 int jx_linear_decode_workspace(int grid, int M, long long* floats_out);
 /* Kernel behind jx_linear_decode: 0 = by shape (default: tcgen05/TMEM when Np/128 >= grid), 1 = mma.sync,
  * 2 = tcgen05/TMEM (needs Np % 128 == 0), 3 = row split (M <= 16: each CTA takes 32 or 48 output rows over
- * the whole K, so no split-K partials; needs a grid of at most `grid` CTAs, an element-wise epilogue and no
- * prologue / prefetch; JX_ERR_SHAPE otherwise). */
+ * the whole K, so no split-K partials; needs a grid of at most `grid` CTAs, an element-wise bf16 epilogue
+ * (not the float32 partial sums of tensor parallelism) and no prologue / prefetch; JX_ERR_SHAPE otherwise). */
 int jx_set_decode_linear_impl(int impl);
 int jx_linear_decode(const void* W, const void* X, long long Np, long long Kp, int M, const jx_epilogue* epi,
                      float* ws, long long ws_floats, int* counters, int* status, int grid, int pdl, void* stream);

@@ -409,9 +409,12 @@ int run_gemv(const bf16* W, const bf16* X, long long Np, long long Kp, int M, co
     e.pf_w = nullptr;
   }
   // Row-split kernel: M <= 16, element-wise epilogues (not the 64-row GLU / push units), no prologue or
-  // prefetch, and a grid of at most one CTA per SM.
+  // prefetch, and a grid of at most one CTA per SM.  The float32 partial sums of a row-parallel
+  // projection (tensor parallelism) stay on the stream-K kernel, which the push epilogue needs, so the
+  // pull and the push exchange sum the same partials (bit-identical results).
   const bool rows_ok = M <= 16 && e.kind != JX_EPI_GLU_SILU && e.kind != JX_EPI_GLU_GELU_TANH &&
-                       e.kind != JX_EPI_PUSH_F32 && !e.pn_h && !e.pf_w && gemv_rows_groups(Np, grid > 0 ? grid : 148) > 0;
+                       e.kind != JX_EPI_PUSH_F32 && e.kind != JX_EPI_STORE_F32 && e.kind != JX_EPI_ACC_F32 &&
+                       !e.pn_h && !e.pf_w && gemv_rows_groups(Np, grid > 0 ? grid : 148) > 0;
   if (e.tn_x) {
     // the normalisation tail runs in the row-split kernel only
     const bool rows_taken = rows_ok && (g_gemv_impl == 3 || (g_gemv_impl == 0 && g_rows_by_shape && !gemv_uses_tc(Np, grid)));

@@ -184,12 +184,11 @@ __device__ __forceinline__ void vstore8(bf16* p, const float* v) {
   *reinterpret_cast<uint4*>(p) = u;
 }
 
-// Normalise the 8 values of this thread (the row is spread over the block).
-__device__ __forceinline__ void vnormalize(const float* x, float* y, int d, int kind, float eps, const bf16* w,
-                                           const bf16* b, int j0, float* red) {
-  float wv[8], bv[8];
-  vload8(w + j0, wv);
-  if (b) vload8(b + j0, bv);
+// Normalise the 8 values of this thread (the row is spread over the block); wv / bv: this thread's 8
+// weights and biases (bv unused without a bias).
+__device__ __forceinline__ void vnormalize_wb(const float* x, float* y, int d, int kind, float eps, const float* wv,
+                                              const float* bv, bool has_b, int j0, float* red) {
+  const bool b = has_b;
   if (kind == JX_NORM_LAYER) {
     float s = 0.f;
 #pragma unroll
@@ -215,6 +214,14 @@ __device__ __forceinline__ void vnormalize(const float* x, float* y, int d, int 
 #pragma unroll
     for (int i = 0; i < 8; ++i) y[i] = rnd<bf16>((wv[i] + 1.0f) * (x[i] * inv));
   }
+}
+
+__device__ __forceinline__ void vnormalize(const float* x, float* y, int d, int kind, float eps, const bf16* w,
+                                           const bf16* b, int j0, float* red) {
+  float wv[8], bv[8];
+  vload8(w + j0, wv);
+  if (b) vload8(b + j0, bv);
+  vnormalize_wb(x, y, d, kind, eps, wv, bv, b != nullptr, j0, red);
 }
 
 // Push mode: wait, bounded, until every 64-column unit carries epoch v from every rank (thread t polls
@@ -257,6 +264,12 @@ __global__ void __launch_bounds__(1024) norm_vec_kernel(NormArgs p) {
   __shared__ unsigned s_epoch;
   const long long m = blockIdx.x;
   const int j0 = threadIdx.x * 8;
+  // the norm weights do not depend on the previous kernel: load them before waiting on it
+  float wv[8], bv[8];
+  if (p.out) {
+    vload8(reinterpret_cast<const bf16*>(p.w) + j0, wv);
+    if (p.b) vload8(reinterpret_cast<const bf16*>(p.b) + j0, bv);
+  }
   pdl_trigger();
   pdl_wait();
   const bool push = p.peer_world > 0;
@@ -313,8 +326,7 @@ __global__ void __launch_bounds__(1024) norm_vec_kernel(NormArgs p) {
     vstore8(h + m * p.ldh + j0, x);
   }
   if (p.out) {
-    vnormalize(x, y, p.d, p.kind, p.eps, reinterpret_cast<const bf16*>(p.w), reinterpret_cast<const bf16*>(p.b), j0,
-               red);
+    vnormalize_wb(x, y, p.d, p.kind, p.eps, wv, bv, p.b != nullptr, j0, red);
     bf16* o = reinterpret_cast<bf16*>(p.out);
     vstore8(o + (p.out_rp > 0 ? k128_offset(m, j0, p.out_rp) : m * p.ldo + j0), y);
   }
