@@ -133,17 +133,21 @@ __device__ __forceinline__ void tail_norm_row(const EpiParams& e, int m, int lan
   }
 }
 
+constexpr int kRowsChunksPerStage = 1;
+
 template <int RG>
 struct RowsCfg {
   static constexpr int ROWS = 16 * RG;
   static constexpr int kConsumers = RG * 4;                 // warps
   static constexpr int kThreads = 32 * (1 + kConsumers);
-  static constexpr int kWBytes = ROWS * 128 * 2;            // 8 / 12 KB
-  static constexpr int kXBytes = 16 * 128 * 2;              // 4 KB
-  static constexpr int kStageBytes = kWBytes + kXBytes;
-  // 10 stages (120 / 160 KB in flight): 16 / 12 stages measured slower on every decode shape (e.g. o_proj
+  static constexpr int kWBytes = ROWS * 128 * 2;            // 8 / 12 KB: one 128-wide K chunk of weights
+  static constexpr int kXBytes = 16 * 128 * 2;              // 4 KB: one chunk of activations
+  static constexpr int kCps = kRowsChunksPerStage;          // K chunks per ring stage
+  // a stage: kCps weight chunks, then their kCps activation chunks (contiguous in the K128 layout)
+  static constexpr int kStageBytes = kCps * (kWBytes + kXBytes);
+  // 10 chunks in flight (120 / 160 KB): 16 / 12 measured slower on every decode shape (e.g. o_proj
   // 8.8 -> 9.4 us): the next kernel's CTAs start later behind a larger one.
-  static constexpr int kStages = 10;
+  static constexpr int kStages = 10 / kCps;
   static constexpr int kLd = ROWS + 4;                      // float32 row stride of the staging tiles
   static constexpr int kPartBytes = 4 * 16 * kLd * 4;       // [4 K slices][16 tokens][ROWS]
   static constexpr int kSmem = kStages * kStageBytes + kPartBytes + 2 * kStages * 8 + 16;
@@ -182,27 +186,35 @@ __global__ void __launch_bounds__(RowsCfg<RG>::kThreads, 1)
       auto wsrc = [&](int kk) { return W + (((long long)kk * (Np >> 3) + (r0 >> 3)) << 10); };
       auto xsrc = [&](int kk) { return X + ((long long)kk << 11); };   // 16 rows x 128 k per chunk
       const uint64_t pol_w = l2_policy_evict_first();   // weights are read once per step
-      const int pre = kc < C::kStages ? kc : C::kStages;
+      const int ns = (kc + C::kCps - 1) / C::kCps;      // stages of the whole K
+      auto nch = [&](int st) { return kc - st * C::kCps < C::kCps ? kc - st * C::kCps : C::kCps; };
+      auto issue_w = [&](int st, int s) {
+        mbar_arrive_expect_tx(&full[s], nch(st) * (C::kWBytes + C::kXBytes));
+        for (int j = 0; j < nch(st); ++j)
+          bulk_g2s_hint(smem + s * C::kStageBytes + j * C::kWBytes, wsrc(st * C::kCps + j), C::kWBytes, &full[s],
+                        pol_w);
+      };
+      auto issue_x = [&](int st, int s) {
+        bulk_g2s(smem + s * C::kStageBytes + C::kCps * C::kWBytes, xsrc(st * C::kCps), nch(st) * C::kXBytes,
+                 &full[s]);
+      };
+      const int pre = ns < C::kStages ? ns : C::kStages;
       // Weights do not depend on the previous kernel: start streaming them before waiting on it.
-      for (int i = 0; i < pre; ++i) {
-        mbar_arrive_expect_tx(&full[i], C::kStageBytes);
-        bulk_g2s_hint(smem + i * C::kStageBytes, wsrc(i), C::kWBytes, &full[i], pol_w);
-      }
+      for (int st = 0; st < pre; ++st) issue_w(st, st);
       pdl_wait();
       pdl_trigger();
-      for (int i = 0; i < pre; ++i) bulk_g2s(smem + i * C::kStageBytes + C::kWBytes, xsrc(i), C::kXBytes, &full[i]);
+      for (int st = 0; st < pre; ++st) issue_x(st, st);
       int issued = pre;
-      for (int i = pre; i < kc; ++i) {
-        const int s = i % C::kStages;
-        if (!mbar_wait_bounded(&empty[s], ((i / C::kStages) - 1) & 1)) {
+      for (int st = pre; st < ns; ++st) {
+        const int s = st % C::kStages;
+        if (!mbar_wait_bounded(&empty[s], ((st / C::kStages) - 1) & 1)) {
           set_status(status, JX_ERR_TIMEOUT);
           *dead = 1;
           break;
         }
-        mbar_arrive_expect_tx(&full[s], C::kStageBytes);
-        bulk_g2s_hint(smem + s * C::kStageBytes, wsrc(i), C::kWBytes, &full[s], pol_w);
-        bulk_g2s(smem + s * C::kStageBytes + C::kWBytes, xsrc(i), C::kXBytes, &full[s]);
-        issued = i + 1;
+        issue_w(st, s);
+        issue_x(st, s);
+        issued = st + 1;
       }
       // every issued copy lands before this CTA's shared memory is released
       for (int i = (issued > C::kStages ? issued - C::kStages : 0); i < issued; ++i)
@@ -224,16 +236,21 @@ __global__ void __launch_bounds__(RowsCfg<RG>::kThreads, 1)
   float acc[2][4] = {}, sum[2][4] = {};
   bool ok = true;
   const int mi = lane >> 3, r8 = lane & 7;
-  for (int i = 0; i < kc; ++i) {
-    const int s = i % C::kStages;
-    if (ok && (*dead || !mbar_wait_bounded(&full[s], (i / C::kStages) & 1))) {
+  const int ns = (kc + C::kCps - 1) / C::kCps;
+  for (int st = 0; st < ns; ++st) {
+    const int s = st % C::kStages;
+    if (ok && (*dead || !mbar_wait_bounded(&full[s], (st / C::kStages) & 1))) {
       ok = false;
       *dead = 1;
       set_status(status, JX_ERR_TIMEOUT);
     }
+#pragma unroll
+    for (int j = 0; j < C::kCps; ++j) {
+    const int i = st * C::kCps + j;
+    if (i >= kc) break;
     if (ok) {
-      const uint32_t sW = smem_u32(smem + s * C::kStageBytes);
-      const uint32_t sX = sW + C::kWBytes;
+      const uint32_t sW = smem_u32(smem + s * C::kStageBytes + j * C::kWBytes);
+      const uint32_t sX = smem_u32(smem + s * C::kStageBytes + C::kCps * C::kWBytes + j * C::kXBytes);
 #pragma unroll
       for (int kq = 0; kq < 2; ++kq) {
         const int ks = ksl * 2 + kq;
@@ -250,8 +267,6 @@ __global__ void __launch_bounds__(RowsCfg<RG>::kThreads, 1)
         mma_bf16(acc[1], a0, a1, a2, a3, b2, b3);
       }
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
     if ((i & 3) == 3 || i == kc - 1) {
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt)
@@ -261,6 +276,9 @@ __global__ void __launch_bounds__(RowsCfg<RG>::kThreads, 1)
           acc[nt][q] = 0.f;
         }
     }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
   }
   // this warp's partial: tokens lane / 4 (+ 8) x weight rows cw * 16 + nt * 8 + (lane % 4) * 2 (+ 1)
 #pragma unroll
