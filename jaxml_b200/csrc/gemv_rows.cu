@@ -133,7 +133,14 @@ __device__ __forceinline__ void tail_norm_row(const EpiParams& e, int m, int lan
   }
 }
 
-constexpr int kRowsChunksPerStage = 1;
+// K chunks per ring stage and in flight.  The consumers' mbarrier wait and arrival per stage, not the
+// bytes in flight, limited this kernel: with one 128-wide chunk a stage (10 in flight) qkv / o_proj / down
+// took 10.6 / 9.5 / 26.2 us and the step 3.72 ms; 2 a stage (10 in flight) 9.6 / 8.0 / 21.6 us, 3.54 ms;
+// 3 a stage (9) 9.7 / 7.9 / 21.4 us; 5 a stage (10) 10.3 / 8.5 / 23.0 us; 2 a stage with 12 in flight
+// 9.6 / 8.2 / 21.7 us; 4 a stage with 12 in flight 9.7 / 7.5 / 19.5 us (down at 0.92 of the measured
+// copy bandwidth) and 3.49 ms (same calls).
+constexpr int kRowsChunksPerStage = 4;
+constexpr int kRowsChunksInFlight = 12;
 
 template <int RG>
 struct RowsCfg {
@@ -145,9 +152,9 @@ struct RowsCfg {
   static constexpr int kCps = kRowsChunksPerStage;          // K chunks per ring stage
   // a stage: kCps weight chunks, then their kCps activation chunks (contiguous in the K128 layout)
   static constexpr int kStageBytes = kCps * (kWBytes + kXBytes);
-  // 10 chunks in flight (120 / 160 KB): 16 / 12 measured slower on every decode shape (e.g. o_proj
-  // 8.8 -> 9.4 us): the next kernel's CTAs start later behind a larger one.
-  static constexpr int kStages = 10 / kCps;
+  // 10 chunks in flight (120 / 160 KB): 16 / 12 measured slower on every decode shape with one chunk a
+  // stage (e.g. o_proj 8.8 -> 9.4 us): the next kernel's CTAs start later behind a larger one.
+  static constexpr int kStages = kRowsChunksInFlight / kCps;
   static constexpr int kLd = ROWS + 4;                      // float32 row stride of the staging tiles
   static constexpr int kPartBytes = 4 * 16 * kLd * 4;       // [4 K slices][16 tokens][ROWS]
   static constexpr int kSmem = kStages * kStageBytes + kPartBytes + 2 * kStages * 8 + 16;
