@@ -109,3 +109,23 @@ def test_comm_layout_regions_do_not_overlap():
     bad = (N.LL * 10)()
     assert lib.jx_comm_layout(0, 2, bad) == N.JX_ERR_ARG
     assert lib.jx_comm_layout(16, 9, bad) == N.JX_ERR_ARG
+
+
+def test_filter_logits_checks_its_arguments_before_any_launch():
+    """jx_filter_logits refuses null pointers, unsupported sizes and dtypes on the host (no GPU needed)."""
+    lib = N.load()
+    a = N.JxFilterArgs()
+    a.B, a.V, a.ld_in, a.ld_out, a.dtype, a.top_k, a.top_p, a.min_p = 4, 1000, 1000, 1000, N.JX_BF16, 5, 0.9, 0.0
+    assert lib.jx_filter_logits(a, None) == N.JX_ERR_ARG            # null logits / out
+    a.logits = a.out = 1 << 20                                        # never dereferenced
+    for field, value, code in (("V", 0, N.JX_ERR_SHAPE), ("V", 8 * 49152 + 1, N.JX_ERR_SHAPE),
+                               ("ld_in", 999, N.JX_ERR_SHAPE), ("ld_out", 10, N.JX_ERR_SHAPE),
+                               ("B", 65535, N.JX_ERR_SHAPE), ("dtype", 7, N.JX_ERR_DTYPE)):
+        b = N.JxFilterArgs.from_buffer_copy(a)
+        setattr(b, field, value)
+        if field == "V" and value > 1000:
+            b.ld_in = b.ld_out = value
+        assert lib.jx_filter_logits(b, None) == code, (field, value)
+    b = N.JxFilterArgs.from_buffer_copy(a)
+    b.B = 0
+    assert lib.jx_filter_logits(b, None) == N.JX_OK                   # nothing to do
