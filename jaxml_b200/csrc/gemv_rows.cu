@@ -138,9 +138,12 @@ __device__ __forceinline__ void tail_norm_row(const EpiParams& e, int m, int lan
 // took 10.6 / 9.5 / 26.2 us and the step 3.72 ms; 2 a stage (10 in flight) 9.6 / 8.0 / 21.6 us, 3.54 ms;
 // 3 a stage (9) 9.7 / 7.9 / 21.4 us; 5 a stage (10) 10.3 / 8.5 / 23.0 us; 2 a stage with 12 in flight
 // 9.6 / 8.2 / 21.7 us; 4 a stage with 12 in flight 9.7 / 7.5 / 19.5 us (down at 0.92 of the measured
-// copy bandwidth) and 3.49 ms (same calls).
+// copy bandwidth) and 3.49 ms; 4 a stage with 16 in flight for the 32-row CTAs (o_proj, down; the 48-row
+// ones keep 12, the shared memory holds no more) 9.7 / 7.5 / 19.0 us and 3.42 ms; 8 a stage (16 / 8 in
+// flight) 13.0 / 8.0 / 20.2 us, 3.56-3.60 ms (same calls).
 constexpr int kRowsChunksPerStage = 4;
 constexpr int kRowsChunksInFlight = 12;
+constexpr int kRowsChunksInFlight32 = 16;   // 32-row CTAs
 
 template <int RG>
 struct RowsCfg {
@@ -154,7 +157,7 @@ struct RowsCfg {
   static constexpr int kStageBytes = kCps * (kWBytes + kXBytes);
   // 10 chunks in flight (120 / 160 KB): 16 / 12 measured slower on every decode shape with one chunk a
   // stage (e.g. o_proj 8.8 -> 9.4 us): the next kernel's CTAs start later behind a larger one.
-  static constexpr int kStages = kRowsChunksInFlight / kCps;
+  static constexpr int kStages = (RG == 2 ? kRowsChunksInFlight32 : kRowsChunksInFlight) / kCps;
   static constexpr int kLd = ROWS + 4;                      // float32 row stride of the staging tiles
   static constexpr int kPartBytes = 4 * 16 * kLd * 4;       // [4 K slices][16 tokens][ROWS]
   static constexpr int kSmem = kStages * kStageBytes + kPartBytes + 2 * kStages * 8 + 16;
