@@ -430,7 +430,12 @@ int run_gemv(const bf16* W, const bf16* X, long long Np, long long Kp, int M, co
     if (!rows_ok) return JX_ERR_SHAPE;
     return run_gemv_rows(W, X, Np, Kp, M, e, status, grid > 0 ? grid : 148, pdl, stream);
   }
-  if (gemv_uses_tc(Np, grid)) return run_gemv_tc(W, X, Np, Kp, M, e, ws, ws_floats, counters, status, grid, pdl, stream);
+  // By shape, more than 16 token rows over a long K also take the tcgen05 kernel: at M = 64 the down
+  // projection (4096 x 14336) took 37.8 us against 45.2 us on mma.sync, while o_proj (K = 4096) took
+  // 25.4 against 19.4 us and qkv 24.6 against 24.2 us.
+  const bool tc_by_k = g_gemv_impl == 0 && M > 16 && Kp >= 8192 && Np % 128 == 0 && !e.pn_h;
+  if (gemv_uses_tc(Np, grid) || tc_by_k)
+    return run_gemv_tc(W, X, Np, Kp, M, e, ws, ws_floats, counters, status, grid, pdl, stream);
   if (g_gemv_impl == 0 && g_rows_by_shape && rows_ok)
     return run_gemv_rows(W, X, Np, Kp, M, e, status, grid > 0 ? grid : 148, pdl, stream);
   if (M <= 0 || M > 64) return JX_ERR_SHAPE;

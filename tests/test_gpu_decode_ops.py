@@ -47,6 +47,30 @@ def test_linear_decode_store(impl, M, Nn, K):
         _assert_rounded_dot(out, x, w)
 
 
+@pytest.mark.parametrize("M,Nn,K", [(33, 512, 8192), (64, 640, 14336)])
+def test_linear_decode_long_k_by_shape(M, Nn, K):
+    """By shape, more than 16 token rows over K >= 8192 take the tcgen05 kernel: its results equal the
+    float64 dot rounded once, over the full grid and a partial one."""
+    N = _n()
+    torch.manual_seed(3)
+    x = torch.randn(M, K, device="cuda").to(torch.bfloat16)
+    w = (torch.randn(Nn, K, device="cuda") * 0.02).to(torch.bfloat16)
+    Mp = 64 if M > 32 else 32
+    Np, Kp = _rup(Nn, 128), _rup(K, 128)
+    xp, wp = _pack(N, x, Mp, Kp), _pack(N, w, Np, Kp)
+    out = torch.zeros(M, Nn, dtype=torch.bfloat16, device="cuda")
+    ws, cnt = _ws(N, Np)
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    e = _epi(N, N.JX_EPI_STORE, M, Nn, out, Nn)
+    for grid in (148, 13):
+        out.zero_()
+        N.call("jx_linear_decode", wp.data_ptr(), xp.data_ptr(), Np, Kp, M, e, ws.data_ptr(), ws.numel(),
+               cnt.data_ptr(), status.data_ptr(), grid, 1, _stream())
+        torch.cuda.synchronize()
+        assert int(status.item()) == 0 and int(cnt.abs().sum().item()) == 0
+        _assert_rounded_dot(out, x, w)
+
+
 @pytest.mark.parametrize("M", [3, 16, 40])
 def test_linear_decode_glu_resid_bias(impl, M):
     """GLU (SiLU) into a K128 output, then a residual projection with bias, both fused."""
