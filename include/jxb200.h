@@ -320,7 +320,8 @@ int jx_norm(const jx_norm_args* args, int dtype, int pdl, void* stream);
 /* Decode projection (M <= 64): DenseGeneral (nn/linear.py:119-182) with fused epilogue.  W and X are
  * bfloat16 K128 ([Np, Kp] and [16*ceil(M/16) (or 64), Kp]); workspace from jx_linear_decode_workspace. */
 int jx_linear_decode_workspace(int grid, int M, long long* floats_out);
-/* Kernel behind jx_linear_decode: 0 = by shape (default: tcgen05/TMEM when Np/128 >= grid), 1 = mma.sync,
+/* Kernel behind jx_linear_decode: 0 = by shape (default: tcgen05/TMEM when Np/128 >= grid or when M > 16
+ * and Kp >= 8192; else the row split where it applies; else mma.sync stream-K), 1 = mma.sync,
  * 2 = tcgen05/TMEM (needs Np % 128 == 0), 3 = row split (M <= 16: each CTA takes 32 or 48 output rows over
  * the whole K, so no split-K partials; needs a grid of at most `grid` CTAs, an element-wise bf16 epilogue
  * (not the float32 partial sums of tensor parallelism) and no prologue / prefetch; JX_ERR_SHAPE otherwise). */
