@@ -8,14 +8,19 @@
 //   o   = bf16(sum_t p_t v_t)                                          (float32 accumulation)
 // Only the valid (or in-window) keys are read, not the whole padded buffer.
 //
-// Two forms.  The single-pass form (dattn_warp_kernel, below; key ranges up to 8 CTAs x 2048 keys per
-// (row, KV head)) is selected explicitly.  The default split form runs two kernels per layer, each a grid
-// of (key split, KV head, batch row) CTAs of 128 keys:
+// The default split form runs two kernels per layer, each a grid of (KV head, batch row, key split) CTAs
+// of 128 keys (the split varying slowest, so the splits past the valid keys are dispatched last):
 //   scores: K tiles arrive by TMA (2-D tensor map over the [L*B*T, Hkv*hd] cache, 128-byte swizzle);
 //           Q.K^T on mma.sync; the rounded scores go to a float32 workspace with per-split (max, sum).
 //   pv:     combines the split statistics into the exact softmax normaliser, forms the bf16
 //           probabilities, P.V on mma.sync with V tiles by TMA, and the last CTA of a head group sums
 //           the split partials in split order (deterministic) into the bf16 output (K128 layout).
+// Selectable alternatives (jx_set_decode_attention_impl; all tested, none faster at the decode shapes):
+// the column pv (one CTA per 64 output columns over all keys), the single-pass cluster form
+// (dattn_warp_kernel: a thread-block cluster per (row, KV head), key ranges up to 8 CTAs x 2048 keys), the
+// cluster-split form (the split form's CTAs of a head group as one cluster exchanging statistics and
+// partials through distributed shared memory) and the queue form (the split form's work as one
+// persistent kernel whose CTAs claim score and pv items from a counter).
 #include <cudaTypedefs.h>
 
 #include "common.cuh"
