@@ -294,6 +294,59 @@ def kernel_table(rt, cfg, ctx, step_ms, n_layers=8):
     return rows
 
 
+def prefill_table(rt, cfg, prefill_ms, n_layers=8):
+    """Per-op device time of the prefill's kernels (sequential-residual Llama layers), each launched back
+    to back over `n_layers` distinct layers from a CUDA graph and timed with CUDA events on the replay
+    stream, on the prefill's own buffers (the timing does not depend on their values).  flop / bytes =
+    algorithmic work per launch (causal attention: the visible half of the score matrix); share = time
+    per launch x launches per prefill / the measured prefill time.  The RoPE + append rows rewrite the
+    K/V cache of the first layers: run it after everything that reads the runtime's cache."""
+    from jaxml_b200 import _native as N
+
+    w, acts = rt.w, rt.pre
+    M, Mp, d = acts["M"], acts["Mp"], w.d
+    S = M // rt.B
+    layers = w.layers[:n_layers]
+    L = cfg.num_layers
+    Fk = w.F32 if (w.glu and not w.bf16) else w.F
+    rows = []
+
+    def add(op, per, fns, flop=None, nbytes=None):
+        us = _graph_ms(lambda _s: [f() for f in fns], len(fns)) * 1e3
+        r = {"op": op, "launches_per_prefill": per, "us": us, "share": us * per / (prefill_ms * 1e3)}
+        if flop is not None:
+            r.update(flop=flop, tflops=flop / us / 1e6)
+        if nbytes is not None:
+            r.update(bytes=nbytes, gbs=nbytes / us / 1e3)
+        rows.append(r)
+
+    add("qkv projection (tcgen05 GEMM)", L,
+        [lambda lw=lw: rt._linear(acts, lw.wqkv, w.Np_qkv, w.Kp_d, "xn", N.JX_EPI_STORE, N_valid=w.nqkv, bias=lw.bqkv,
+                                  out=acts["qkv"], ldo=w.nqkv, K_logical=d, N_cols=w.nqkv) for lw in layers],
+        flop=2.0 * M * w.nqkv * d)
+    add("RoPE + KV append", L, [lambda li=li, lw=lw: rt._qkv_rope_append(acts, li, lw, S, False)
+                                for li, lw in enumerate(layers)], nbytes=4.0 * M * w.nqkv)
+    add("attention (causal)", L, [lambda li=li, lw=lw: rt._prefill_attention(acts, li, lw, S)
+                                  for li, lw in enumerate(layers)], flop=2.0 * rt.B * w.Hq * w.hd * S * S)
+    add("o_proj projection (tcgen05 GEMM, residual add)", L,
+        [lambda lw=lw: rt._linear(acts, lw.wo, w.Np_d, w.Kp_o, "attn", N.JX_EPI_RESID, N_valid=d, bias=lw.bo,
+                                  out=acts["h"], ldo=d, res=acts["h"], ldr=d, K_logical=w.Hq * w.hd, N_cols=d)
+         for lw in layers], flop=2.0 * M * d * w.Hq * w.hd)
+    add("norm", 2 * L - 1, [lambda lw=lw: rt._norm(acts, w=lw.norms["post_attention_layernorm"][0],
+                                                   b=lw.norms["post_attention_layernorm"][1]) for lw in layers],
+        nbytes=4.0 * M * d)
+    add("gate/up projection (tcgen05 GEMM, SwiGLU)", L,
+        [lambda lw=lw: rt._linear(acts, lw.wgu, w.Np_gu, w.Kp_d, "xn", N.JX_EPI_GLU_SILU, N_valid=w.F, bias=lw.bgu,
+                                  out=acts["act"], ldo=w.F32, out_rp=Mp, K_logical=d, N_cols=2 * w.F32)
+         for lw in layers], flop=2.0 * M * 2 * w.F * d)
+    add("down projection (tcgen05 GEMM, residual add)", L,
+        [lambda lw=lw: rt._linear(acts, lw.wd, w.Np_d, w.Kp_f, "act", N.JX_EPI_RESID, out=acts["h"], ldo=d,
+                                  res=acts["h"], ldr=d, N_valid=d, bias=lw.bd, K_logical=Fk, N_cols=d)
+         for lw in layers], flop=2.0 * M * d * w.F)
+    rt.check_status()
+    return rows
+
+
 # ------------------------------------------------------------------------------------------------
 # CPU baseline: the oracle restatement on the host cores (bounded sample)
 # ------------------------------------------------------------------------------------------------
@@ -570,6 +623,12 @@ def gpu_arm(args):
 
     # ---- per-kernel durations (graph replays, CUDA events) and the dominant kernel ----
     table = kernel_table(rt, cfg, ctx_last, step_ms_mean) if tp == 1 and args.config == "l8" else None
+    ptable = None
+    if tp == 1 and args.config == "l8":
+        try:
+            ptable = prefill_table(rt, cfg, prefill_ms)
+        except Exception as exc:   # a measurement aid: report, do not lose the bench line
+            ptable = {"error": str(exc)[:300]}
 
     # ---- end to end through Engine.generate with host buffers: the workload's 256 new tokens ----
     e2e = None
@@ -635,6 +694,7 @@ def gpu_arm(args):
                        "l2": "inputs larger than L2 (%.2f GB of weights per step)" % (wbytes / 1e9)},
             "roofline": roofline,
             "kernels": table,
+            "prefill_kernels": ptable,
             "step_roofline": {"bytes_per_step": sbytes, "weight_bytes": wbytes, "kv_bytes": kvbytes,
                               "achieved_gbs": sbytes / (step_ms_mean * 1e-3) / 1e9,
                               "frac": sbytes / (step_ms_mean * 1e-3) / 1e9 / hbm_peak, "peak_source": peak_src},

@@ -273,16 +273,6 @@ __device__ __forceinline__ bool ds_stage_wait(const volatile int* tag, uint64_t*
 // ---------------------------------------------------------------------------------------------------
 __device__ __forceinline__ void ds_wsync() { named_bar_sync(1, 128); }
 
-__device__ __forceinline__ void unpack8(const uint4& u, float* v) {
-  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 f = __bfloat1622float2(h[i]);
-    v[2 * i] = f.x;
-    v[2 * i + 1] = f.y;
-  }
-}
-
 __device__ __forceinline__ uint4 pack8(const float* y) {
   return make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]), pack_bf16x2(y[4], y[5]),
                     pack_bf16x2(y[6], y[7]));

@@ -1,4 +1,5 @@
-// Fused embedding / residual-add / normalisation kernel (one CTA per token row).
+// Fused embedding / residual-add / normalisation kernels (one CTA per token row; prefill-sized calls
+// that only normalise take one warp per row, norm_rows_kernel).
 //
 // Per row m it can, in order:
 //   1. gather the embedding row of ids[m] (ids < 0 read row 0, models/llama.py:188) and scale it by the
@@ -350,6 +351,116 @@ __global__ void __launch_bounds__(1024) norm_vec_kernel(NormArgs p) {
   }
 }
 
+// ------------------------------------------------------------------------------------------------
+// Prefill-sized calls (M >= kNormRowsMin rows) that only normalise h into one output: one warp per row.
+// One CTA per row (norm_vec_kernel) keeps a single 16-byte load per thread in flight and left most of
+// the HBM bandwidth unused at 8192 rows; here a warp copies its whole row into shared memory with
+// 16-byte cp.async copies, all in flight at once, then works from there.  Lane l takes vectors l, l + 32,
+// l + 64, ... (16-byte vector v = elements 8v .. 8v + 7), the vectors that threads l, l + 32, ... of
+// norm_vec_kernel hold, and forms the same per-vector partial sums, the same xor-shuffle tree over each
+// group of 32 vectors (a warp there) and the same tree over the group totals as vblock_sum: the outputs
+// are bit-identical to norm_vec_kernel's.
+// ------------------------------------------------------------------------------------------------
+constexpr int kNormRowsMin = 256;
+constexpr int kNormRowsWarps = 4;          // rows per CTA
+constexpr int kNormRowsMaxGroups = 16;     // d / 256 (groups of 32 vectors) <= 16
+
+__device__ __forceinline__ float warp_tree_sum(float v) {
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n cp.async.wait_group 0;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(32 * kNormRowsWarps) norm_rows_kernel(NormArgs p) {
+  extern __shared__ uint4 rows_sm[];   // [kNormRowsWarps][d / 8] vectors
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long m = (long long)blockIdx.x * kNormRowsWarps + warp;
+  pdl_trigger();
+  pdl_wait();
+  if (m >= p.M) return;
+  const int ng = p.d >> 8;
+  uint4* row = rows_sm + warp * (p.d >> 3);
+  const uint4* hr = reinterpret_cast<const uint4*>(reinterpret_cast<const bf16*>(p.h) + m * p.ldh);
+  for (int g = 0; g < ng; ++g) cp_async16(row + g * 32 + lane, hr + g * 32 + lane);
+  cp_async_wait_all();
+  __syncwarp();
+  // Each group's xor-tree total is the same in every lane; lane g keeps group g's, and the xor tree over
+  // the lanes (zero above the group count) is vblock_sum's second stage.
+  float t = 0.f, mean = 0.f, den;
+  if (p.kind == JX_NORM_LAYER) {
+    for (int g = 0; g < ng; ++g) {
+      float x[8];
+      unpack8(row[g * 32 + lane], x);
+      float s = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) s += x[i];
+      const float sg = warp_tree_sum(s);
+      if (g == lane) t = sg;
+    }
+    mean = warp_tree_sum(t) / (float)p.d;
+    t = 0.f;
+    for (int g = 0; g < ng; ++g) {
+      float x[8];
+      unpack8(row[g * 32 + lane], x);
+      float v = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v += (x[i] - mean) * (x[i] - mean);
+      const float sg = warp_tree_sum(v);
+      if (g == lane) t = sg;
+    }
+    den = sqrtf(warp_tree_sum(t) / (float)p.d + p.eps);
+  } else {
+    for (int g = 0; g < ng; ++g) {
+      float x[8];
+      unpack8(row[g * 32 + lane], x);
+      float s = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) s += x[i] * x[i];
+      const float sg = warp_tree_sum(s);
+      if (g == lane) t = sg;
+    }
+    den = sqrtf(warp_tree_sum(t) / (float)p.d + p.eps);
+  }
+  const bf16* w = reinterpret_cast<const bf16*>(p.w);
+  const bf16* bias = reinterpret_cast<const bf16*>(p.b);
+  bf16* o = reinterpret_cast<bf16*>(p.out);
+  for (int g = 0; g < ng; ++g) {
+    const int j0 = g * 256 + lane * 8;
+    float x[8], wv[8], bv[8], y[8];
+    unpack8(row[g * 32 + lane], x);
+    vload8(w + j0, wv);
+    if (p.kind == JX_NORM_LAYER) {
+      const bool b = bias != nullptr;
+      if (b) vload8(bias + j0, bv);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) y[i] = rnd<bf16>((x[i] - mean) / den * wv[i] + (b ? bv[i] : 0.f));
+    } else if (p.kind == JX_NORM_RMS) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) y[i] = rnd<bf16>(wv[i] * rnd<bf16>(x[i] / den));
+    } else {
+      const float inv = 1.0f / den;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) y[i] = rnd<bf16>((wv[i] + 1.0f) * (x[i] * inv));
+    }
+    vstore8(o + (p.out_rp > 0 ? k128_offset(m, j0, p.out_rp) : m * p.ldo + j0), y);
+  }
+}
+
+static bool norm_rows_ok(const NormArgs& p) {
+  const uintptr_t ptrs = reinterpret_cast<uintptr_t>(p.h) | reinterpret_cast<uintptr_t>(p.out) |
+                         reinterpret_cast<uintptr_t>(p.w) | reinterpret_cast<uintptr_t>(p.b);
+  return p.M >= kNormRowsMin && p.peer_world == 0 && !p.ids && !p.row_map && !p.a && !p.out2 && p.out && p.w &&
+         p.kind_pre == JX_NORM_NONE &&
+         (p.kind == JX_NORM_RMS || p.kind == JX_NORM_GEMMA || p.kind == JX_NORM_LAYER) && p.d % 256 == 0 &&
+         p.d <= 256 * kNormRowsMaxGroups && (ptrs & 15) == 0 && p.ldh % 8 == 0 && (p.out_rp > 0 || p.ldo % 8 == 0);
+}
+
 int run_norm(int dtype, const NormArgs& p, bool pdl, cudaStream_t stream) {
   if (p.M <= 0 || p.d <= 0) return JX_ERR_SHAPE;
   const bool aligned = ((p.ldh | p.lda | p.ldo | p.ldo2) & 7) == 0;
@@ -361,6 +472,19 @@ int run_norm(int dtype, const NormArgs& p, bool pdl, cudaStream_t stream) {
     if ((p.lda & 3) || (p.peer_stride & 3) || ((uintptr_t)p.peer_recv & 15) || ((uintptr_t)p.peer_seq & 7) ||
         (long long)p.M * p.lda > p.peer_stride)
       return JX_ERR_ARG;
+  }
+  if (vec && norm_rows_ok(p)) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)((p.M + kNormRowsWarps - 1) / kNormRowsWarps));
+    cfg.blockDim = dim3(32 * kNormRowsWarps);
+    cfg.dynamicSmemBytes = (size_t)kNormRowsWarps * p.d * 2;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return launch_ex(&cfg, norm_rows_kernel, p) == cudaSuccess ? JX_OK : JX_ERR_CUDA;
   }
   if (vec) {
     cudaLaunchConfig_t cfg = {};

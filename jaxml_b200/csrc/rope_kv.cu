@@ -77,9 +77,92 @@ __global__ void __launch_bounds__(256) qkv_rope_append_kernel(QkvArgs p) {
   }
 }
 
+// Prefill-sized calls (M >= kRopeRowsMin token rows, decode == 0) of bfloat16 models without QK norm,
+// hd % 8 == 0 and rd % 16 == 0: one CTA per token row in 16-byte vectors.  The kernel above keeps one
+// head (256 bytes) per warp in flight and left most of the HBM bandwidth unused at 8192 rows.  Here the
+// CTA first loads every vector of the row into shared memory (the rotate-half partner of a vector is
+// the vector rd / 16 places away in the same head), then each thread rotates and stores its vectors.
+// The per-element arithmetic is the kernel's above, so q, k and v are bit-identical to it.
+constexpr int kRopeRowsMin = 256;
+constexpr int kRopeRowsMaxBytes = 48 * 1024;   // one token row of q, k and v in shared memory
+
+__global__ void __launch_bounds__(256) qkv_rope_rows_kernel(QkvArgs p) {
+  extern __shared__ uint4 rowv[];   // [(Hq + 2 Hkv) * hd / 8] vectors of 8 bf16
+  const long long m = blockIdx.x;
+  pdl_wait();
+  pdl_trigger();
+  const int b = (int)(m / p.S), pos = (int)(m % p.S);
+  if (pos >= p.max_pos || pos >= p.T) {
+    if (threadIdx.x == 0) set_status(p.status, JX_ERR_RANGE);
+    return;
+  }
+  const int vph = p.hd >> 3;                    // vectors per head
+  const int nv = (p.Hq + 2 * p.Hkv) * vph;
+  const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const bf16*>(p.qkv) + m * p.ld_qkv);
+  for (int v = threadIdx.x; v < nv; v += blockDim.x) rowv[v] = src[v];
+  __syncthreads();
+  const int rv = p.rd >> 3, hv = p.rd >> 4;     // rotated vectors of a head, half of them
+  const bf16* cos = reinterpret_cast<const bf16*>(p.cos) + (long long)pos * p.rd;
+  const bf16* sin = reinterpret_cast<const bf16*>(p.sin) + (long long)pos * p.rd;
+  for (int v = threadIdx.x; v < nv; v += blockDim.x) {
+    const int head = v / vph, jv = v - head * vph;
+    const bool is_q = head < p.Hq, is_k = !is_q && head < p.Hq + p.Hkv;
+    uint4 o = rowv[v];
+    if ((is_q || is_k) && jv < rv) {
+      const bool lo = jv < hv;
+      float x[8], r[8], c[8], sn[8], y[8];
+      unpack8(o, x);
+      unpack8(rowv[lo ? v + hv : v - hv], r);
+      unpack8(*reinterpret_cast<const uint4*>(cos + jv * 8), c);
+      unpack8(*reinterpret_cast<const uint4*>(sin + jv * 8), sn);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float rot = lo ? -r[i] : r[i];
+        const float a = rnd<bf16>(x[i] * c[i]);
+        const float cc = rnd<bf16>(rot * sn[i]);
+        y[i] = rnd<bf16>(a + cc);
+      }
+      o.x = pack_bf16x2(y[0], y[1]);
+      o.y = pack_bf16x2(y[2], y[3]);
+      o.z = pack_bf16x2(y[4], y[5]);
+      o.w = pack_bf16x2(y[6], y[7]);
+    }
+    bf16* dst;
+    if (is_q) {
+      dst = reinterpret_cast<bf16*>(p.q_out) + (m * p.Hq + head) * p.hd;
+    } else {
+      const int kvh = is_k ? head - p.Hq : head - p.Hq - p.Hkv;
+      dst = reinterpret_cast<bf16*>(is_k ? p.k_cache : p.v_cache) + (((long long)b * p.T + pos) * p.Hkv + kvh) * p.hd;
+    }
+    *reinterpret_cast<uint4*>(dst + jv * 8) = o;
+  }
+}
+
+static bool qkv_rope_rows_ok(int dtype, const QkvArgs& p) {
+  const uintptr_t ptrs = reinterpret_cast<uintptr_t>(p.qkv) | reinterpret_cast<uintptr_t>(p.cos) |
+                         reinterpret_cast<uintptr_t>(p.sin) | reinterpret_cast<uintptr_t>(p.q_out) |
+                         reinterpret_cast<uintptr_t>(p.k_cache) | reinterpret_cast<uintptr_t>(p.v_cache);
+  return dtype == JX_BF16 && !p.decode && p.M >= kRopeRowsMin && !p.qn_w && !p.kn_w && p.hd % 8 == 0 &&
+         p.rd % 16 == 0 && p.ld_qkv % 8 == 0 && (ptrs & 15) == 0 &&
+         (long long)(p.Hq + 2 * p.Hkv) * p.hd * 2 <= kRopeRowsMaxBytes;
+}
+
 int run_qkv_rope_append(int dtype, const QkvArgs& p, bool pdl, cudaStream_t stream) {
   if (p.M <= 0 || p.S <= 0 || p.hd <= 0 || p.hd > 256 || p.rd < 0 || p.rd > p.hd || (p.rd & 1)) return JX_ERR_SHAPE;
   if (p.decode && p.S != 1) return JX_ERR_SHAPE;
+  if (qkv_rope_rows_ok(dtype, p)) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.M);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = (size_t)(p.Hq + 2 * p.Hkv) * p.hd * 2;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return launch_ex(&cfg, qkv_rope_rows_kernel, p) == cudaSuccess ? JX_OK : JX_ERR_CUDA;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.M, (p.Hq + 2 * p.Hkv + 7) / 8);
   cfg.blockDim = dim3(256);

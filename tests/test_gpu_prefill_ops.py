@@ -104,3 +104,88 @@ def test_model_with_tensor_core_attention_matches_oracle(family):
         err = (rt.logits_buf()[:B].float().cpu() - out.logits[:, 0].float()).abs().max().item()
         assert err <= 2e-2, err
         tok = rt.next_ids.cpu()
+
+
+@pytest.mark.parametrize("kind", ["rms", "gemma", "layer"])
+@pytest.mark.parametrize("d,ldh,k128", [(4096, 4096, True), (3840, 3840, False), (2048, 2112, True), (256, 256, False)])
+def test_prefill_norm_rows_match_the_per_row_kernel(kind, d, ldh, k128):
+    """jx_norm at prefill row counts (one warp per row) writes the bits of the same rows normalised in
+    calls of fewer rows (one CTA per row), into row-major and K128 outputs, with a row stride above d."""
+    N = _n()
+    torch.manual_seed(23)
+    M, chunk = 600, 100
+    knd = {"rms": N.JX_NORM_RMS, "gemma": N.JX_NORM_GEMMA, "layer": N.JX_NORM_LAYER}[kind]
+    h = (2 * torch.randn(M, ldh, device="cuda") + 0.3).to(torch.bfloat16)
+    w = (1 + 0.1 * torch.randn(d, device="cuda")).to(torch.bfloat16)
+    b = (0.1 * torch.randn(d, device="cuda")).to(torch.bfloat16) if kind == "layer" else None
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+
+    def call(r0, rows, out, ldo, out_rp):
+        a = N.JxNormArgs()
+        a.M, a.d, a.eps, a.kind = rows, d, 1e-5, knd
+        a.h, a.ldh = h[r0:].data_ptr(), ldh
+        a.w, a.b = w.data_ptr(), None if b is None else b.data_ptr()
+        a.out, a.ldo, a.out_rp, a.status = out, ldo, out_rp, status.data_ptr()
+        N.call("jx_norm", a, N.JX_BF16, 1, _stream())
+
+    ref = torch.empty(M, d, dtype=torch.bfloat16, device="cuda")
+    for r0 in range(0, M, chunk):
+        call(r0, min(chunk, M - r0), ref[r0:].data_ptr(), d, 0)
+    got = torch.empty(M, d, dtype=torch.bfloat16, device="cuda")
+    if k128:
+        Mp = _rup(M, 128)
+        xk = torch.zeros(Mp * d, dtype=torch.bfloat16, device="cuda")
+        call(0, M, xk.data_ptr(), d, Mp)
+        N.call("jx_unpack_k128", xk.data_ptr(), M, d, Mp, got.data_ptr(), N.JX_BF16, d, _stream())
+    else:
+        call(0, M, got.data_ptr(), d, 0)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    assert torch.equal(got, ref)
+    # against the oracle's norm (float32 statistics in another summation order: within two bf16 ulps)
+    x, wc = h[:, :d].cpu(), w.cpu()
+    want = {"rms": lambda: O.rmsnorm(x, wc, 1e-5), "gemma": lambda: O.gemma_rmsnorm(x, wc, 1e-5),
+            "layer": lambda: O.layernorm(x, wc, b.cpu(), 1e-5)}[kind]().float()
+    diff = (got.float().cpu() - want).abs()
+    assert bool((diff <= 2.0 ** -6 * want.abs() + 1e-3).all()), diff.max().item()
+
+
+@pytest.mark.parametrize("hd,Hq,Hkv,rd", [(128, 32, 8, 128), (64, 8, 8, 16), (128, 16, 2, 64), (256, 8, 4, 256)])
+def test_prefill_rope_append_rows_match_the_per_head_kernel(hd, Hq, Hkv, rd):
+    """jx_qkv_rope_append at prefill row counts (one CTA per token row, 16-byte vectors) writes the bits
+    that the same prompts appended one sequence at a time (fewer rows: one warp per head) write: q and
+    the K / V cache."""
+    N = _n()
+    torch.manual_seed(29)
+    B, S, T, max_pos = 4, 96, 128, 256
+    M, nq = B * S, (Hq + 2 * Hkv) * hd
+    qkv = torch.randn(M, nq, device="cuda").to(torch.bfloat16)
+    cos, sin = (t.cuda() for t in O.rope_tables(hd, rd / hd, 10000.0, 1.0, max_pos, torch.bfloat16))
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+
+    def run(m0, rows, q, kc, vc):
+        qa = N.JxQkvArgs()
+        qa.M, qa.S, qa.Hq, qa.Hkv, qa.hd, qa.rd = rows, S, Hq, Hkv, hd, rd
+        qa.qkv, qa.ld_qkv, qa.qn_w, qa.kn_w, qa.eps = qkv[m0:].data_ptr(), nq, None, None, 1e-6
+        qa.max_pos, qa.cos, qa.sin, qa.pos_id, qa.decode, qa.T = max_pos, cos.data_ptr(), sin.data_ptr(), None, 0, T
+        qa.q_out, qa.k_cache, qa.v_cache, qa.status = q, kc, vc, status.data_ptr()
+        N.call("jx_qkv_rope_append", qa, N.JX_BF16, 1, _stream())
+
+    q1 = torch.zeros(M, Hq * hd, dtype=torch.bfloat16, device="cuda")
+    k1 = torch.zeros(B, T, Hkv, hd, dtype=torch.bfloat16, device="cuda")
+    v1 = torch.zeros_like(k1)
+    run(0, M, q1.data_ptr(), k1.data_ptr(), v1.data_ptr())
+    q2, k2, v2 = torch.zeros_like(q1), torch.zeros_like(k1), torch.zeros_like(v1)
+    for b in range(B):
+        run(b * S, S, q2[b * S:].data_ptr(), k2[b].data_ptr(), v2[b].data_ptr())
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    assert torch.equal(q1, q2) and torch.equal(k1, k2) and torch.equal(v1, v2)
+    # against the oracle's rotation (q and k rotated in the model dtype: the same bits), v copied
+    x = qkv.cpu().view(B, S, Hq + 2 * Hkv, hd)
+    pos = torch.arange(S).expand(B, S)
+    want_q, want_k = O.apply_rope(x[:, :, :Hq], x[:, :, Hq:Hq + Hkv], cos.cpu(), sin.cpu(), pos)
+    assert torch.equal(q1.cpu().view(B, S, Hq, hd), want_q)
+    assert torch.equal(k1[:, :S].cpu(), want_k)
+    assert torch.equal(v1[:, :S].cpu(), x[:, :, Hq + Hkv:])
+    assert not k1[:, S:].any() and not v1[:, S:].any()
