@@ -107,13 +107,15 @@ def test_model_with_tensor_core_attention_matches_oracle(family):
 
 
 @pytest.mark.parametrize("kind", ["rms", "gemma", "layer"])
-@pytest.mark.parametrize("d,ldh,k128", [(4096, 4096, True), (3840, 3840, False), (2048, 2112, True), (256, 256, False)])
-def test_prefill_norm_rows_match_the_per_row_kernel(kind, d, ldh, k128):
+@pytest.mark.parametrize("d,ldh,k128,M", [(4096, 4096, True, 600), (3840, 3840, False, 600), (2048, 2112, True, 600),
+                                          (256, 256, False, 600), (2048, 2048, True, 603)])
+def test_prefill_norm_rows_match_the_per_row_kernel(kind, d, ldh, k128, M):
     """jx_norm at prefill row counts (one warp per row) writes the bits of the same rows normalised in
-    calls of fewer rows (one CTA per row), into row-major and K128 outputs, with a row stride above d."""
+    calls of fewer rows (one CTA per row), into row-major and K128 outputs, with a row stride above d and
+    a row count that is not a multiple of the rows per CTA."""
     N = _n()
     torch.manual_seed(23)
-    M, chunk = 600, 100
+    chunk = 100
     knd = {"rms": N.JX_NORM_RMS, "gemma": N.JX_NORM_GEMMA, "layer": N.JX_NORM_LAYER}[kind]
     h = (2 * torch.randn(M, ldh, device="cuda") + 0.3).to(torch.bfloat16)
     w = (1 + 0.1 * torch.randn(d, device="cuda")).to(torch.bfloat16)
