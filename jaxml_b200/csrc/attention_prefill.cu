@@ -7,9 +7,9 @@
 // A query row with no visible key attends uniformly to every slot of the buffer (:385-386): the first
 // uniform_T slots, the reference's cache length when the prompt ran (the rest are zero then).
 //
-// One CTA per (64 query rows, HPC query heads of one KV head, batch row); each warp owns 16 rows of one
-// head, so the HPC heads' warps share every K / V tile the CTA loads (HPC = 4, 2 or 1: the largest that
-// divides the heads per KV head).  To round the normalised
+// One CTA per (64 query rows, HPC query heads of one KV head, batch row), the last query tiles (the
+// most key tiles) first; each warp owns 16 rows of one head, so the HPC heads' warps share every K / V
+// tile the CTA loads (HPC = 4, 2 or 1: the largest that divides the heads per KV head).  To round the normalised
 // probabilities exactly as the reference does, the kernel makes two passes over the key tiles: pass 1
 // finds each row's max and exp-sum, pass 2 recomputes the identical scores, forms bf16(exp(s-m)/l) and
 // accumulates P.V.  K and V tiles arrive by TMA (the cache's 2-D tensor maps, 128-byte swizzle) in a
@@ -57,8 +57,13 @@ __global__ void __launch_bounds__(128 * HPC) pattn_kernel(const __grid_constant_
   uint64_t* bar = reinterpret_cast<uint64_t*>(vs + 2 * TILE);
   int* dead_rows = reinterpret_cast<int*>(bar + 2);   // [HPC][64]
 
-  const int qt = blockIdx.x, b = blockIdx.z;
-  const int h0 = blockIdx.y * HPC;               // first query head of this CTA
+  // CTAs start in linear grid order; the query tiles with the most key tiles (the last ones, causal) go
+  // first, so that the short ones fill in at the end instead of a long one starting last.
+  const int per_qt = gridDim.y * gridDim.z;
+  const int lin = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+  const int qt = gridDim.x - 1 - lin / per_qt, rest = lin % per_qt;
+  const int b = rest / gridDim.y;
+  const int h0 = (rest % gridDim.y) * HPC;       // first query head of this CTA
   const int kvh = h0 / p.n_rep;
   const int hw = (threadIdx.x >> 5) >> 2;        // this warp's head within the CTA
   const int h = h0 + hw;
