@@ -114,6 +114,7 @@ _PROTOS = {
     "jx_set_decode_linear_impl": (I, [I]),
     "jx_set_prefill_tile_group": (I, [I]),
     "jx_set_prefill_linear_impl": (I, [I]),
+    "jx_set_prefill_attention_impl": (I, [I]),
     "jx_linear_decode": (I, [P, P, LL, LL, I, ctypes.POINTER(JxEpilogue), P, LL, P, P, I, I, P]),
     "jx_linear_decode_noalloc": (I, [P, P, LL, LL, I, ctypes.POINTER(JxEpilogue), P, I, I, P]),
     "jx_linear_prefill": (I, [P, P, LL, LL, LL, ctypes.POINTER(JxEpilogue), P, I, P]),

@@ -303,7 +303,14 @@ static int launch_pattn(const jx_pattn_args& a, const PAttnParams& p, bool pdl, 
   return launch_pattn_h<HD, KT, 1>(a, p, pdl, s);
 }
 
+int run_prefill_attention_tc(const jx_pattn_args& a, bool pdl, cudaStream_t stream);
+
+// 0 = by shape (this file's kernel), 1 = this file's kernel, 2 = the tcgen05 kernel (attention_prefill_tc.cu)
+static int g_pattn_impl = 0;
+void set_pattn_impl(int impl) { g_pattn_impl = impl; }
+
 int run_prefill_attention(const jx_pattn_args& a, bool pdl, cudaStream_t stream) {
+  if (g_pattn_impl == 2) return run_prefill_attention_tc(a, pdl, stream);
   if (a.B <= 0 || a.S <= 0 || a.Hkv <= 0 || a.Hq % a.Hkv || a.T <= 0 || a.S > a.T) return JX_ERR_SHAPE;
   if (a.B > 65535 || a.Hq > 65535) return JX_ERR_SHAPE;
   if (reinterpret_cast<uintptr_t>(a.q) & 15) return JX_ERR_ARG;

@@ -23,6 +23,7 @@ void set_dattn_impl(int impl);
 void set_gemm_impl(int impl);
 void set_gemm_tile_group(int gm);
 int run_prefill_attention(const jx_pattn_args& a, bool pdl, cudaStream_t stream);
+void set_pattn_impl(int impl);
 long long dattn_workspace_bytes(int B, int Hq, int T, int hd, int n_splits);
 int dattn_n_splits(int T, int window);
 int run_filter_logits(const jx_filter_args& p, cudaStream_t stream);
@@ -255,6 +256,13 @@ int jx_set_decode_attention_impl(int impl) {
     return fail(JX_ERR_ARG, "jx_set_decode_attention_impl: 0 (by shape), 1 (split), 2 (cluster), 3 (column pv), "
                             "4 (cluster-split), 5 (queue)");
   set_dattn_impl(impl);
+  return JX_OK;
+}
+
+int jx_set_prefill_attention_impl(int impl) {
+  if (impl < 0 || impl > 2)
+    return fail(JX_ERR_ARG, "jx_set_prefill_attention_impl: 0 (by shape), 1 (mma.sync), 2 (tcgen05)");
+  set_pattn_impl(impl);
   return JX_OK;
 }
 

@@ -84,8 +84,10 @@ def test_decode_attention_rejects_an_output_too_small_for_the_batch():
     for impl in (0, 1, 2, 3, 4, 5, 6):
         assert lib.jx_set_decode_attention_impl(impl) == (N.JX_OK if impl <= 5 else N.JX_ERR_ARG)
         assert lib.jx_set_prefill_linear_impl(impl) == (N.JX_OK if impl <= 2 else N.JX_ERR_ARG)
+        assert lib.jx_set_prefill_attention_impl(impl) == (N.JX_OK if impl <= 2 else N.JX_ERR_ARG)
     lib.jx_set_decode_attention_impl(0)
     lib.jx_set_prefill_linear_impl(0)
+    lib.jx_set_prefill_attention_impl(0)
 
 
 def test_comm_layout_regions_do_not_overlap():
@@ -129,3 +131,25 @@ def test_filter_logits_checks_its_arguments_before_any_launch():
     b = N.JxFilterArgs.from_buffer_copy(a)
     b.B = 0
     assert lib.jx_filter_logits(b, None) == N.JX_OK                   # nothing to do
+
+
+def test_tensor_core_prefill_attention_refuses_unsupported_shapes_before_any_launch():
+    """With the tcgen05 prefill attention selected, head sizes other than 64 / 128, a row-major output,
+    S > T or Hq % Hkv != 0 fail with JX_ERR_SHAPE before any device work (the pointers are never
+    dereferenced)."""
+    lib = N.load()
+    fake = 1 << 20
+    a = N.JxPAttnArgs()
+    a.B, a.S, a.Hq, a.Hkv, a.hd, a.T, a.window = 2, 64, 8, 2, 128, 128, 0
+    a.cache_rows, a.layer_row0 = 2 * 128, 0
+    a.q = a.k_base = a.v_base = a.out = a.len_ptr = fake
+    a.len_add, a.scale, a.out_rp = 1, 128 ** -0.5, 128
+    assert lib.jx_set_prefill_attention_impl(2) == N.JX_OK
+    try:
+        for field, value in (("hd", 256), ("hd", 96), ("out_rp", 0), ("S", 200), ("Hkv", 3)):
+            saved = getattr(a, field)
+            setattr(a, field, value)
+            assert lib.jx_prefill_attention(a, 0, None) == N.JX_ERR_SHAPE, field
+            setattr(a, field, saved)
+    finally:
+        lib.jx_set_prefill_attention_impl(0)
