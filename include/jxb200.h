@@ -392,8 +392,8 @@ int jx_set_decode_attention_impl(int impl);
  * caches on tensor cores, exact reference rounding (see csrc/attention_prefill.cu). */
 int jx_prefill_attention(const jx_pattn_args* args, int pdl, void* stream);
 /* Kernel behind jx_prefill_attention (process-wide): 0 = by shape (the mma.sync kernel), 1 = mma.sync
- * (csrc/attention_prefill.cu), 2 = tcgen05/TMEM (csrc/attention_prefill_tc.cu: head_dim 64 / 128, a K128
- * output; JX_ERR_SHAPE otherwise; not yet the by-shape choice). */
+ * (csrc/attention_prefill.cu), 2 = tcgen05/TMEM (csrc/attention_prefill_tc.cu: head_dim 64 / 128 / 256, a
+ * K128 output; JX_ERR_SHAPE otherwise; not yet the by-shape choice). */
 int jx_set_prefill_attention_impl(int impl);
 
 /* greedy_fn / categorical sampling (inference_engine/sampling.py:75-188) + end-of-step bookkeeping. */

@@ -1,4 +1,4 @@
-// Prefill attention on the 5th-generation tensor cores (tcgen05 + TMEM), head_dim 64 / 128: the masks
+// Prefill attention on the 5th-generation tensor cores (tcgen05 + TMEM), head_dim 64 / 128 / 256: the masks
 // and rounding points of attention_prefill.cu (Attention.mha for q_len > 1, nn/attention.py:321-400):
 // scores = bf16(bf16(q.k) * bf16(attn_scale)) over the visible keys (causal, sliding window, right
 // padding), probabilities bf16(exp(s - m) / l) with the row's final max m and exp-sum l (a first pass
@@ -13,8 +13,9 @@
 // 9 the MMA issuer (and TMEM owner).  Shared memory holds every operand as 64-column blocks of
 // [rows][128 bytes] with the 128-byte swizzle (16-byte chunk c of row r at chunk c ^ (r % 8)), the
 // layout the K / V tensor maps produce: Q and P (written by threads) and K are K-major operands, V is
-// the MN-major B operand of P.V.  TMEM: two 128-column score buffers (the MMA of the next tile
-// overlaps the softmax of this one) and the HD-column output accumulator.
+// the MN-major B operand of P.V.  TMEM: two KT-column score buffers (the MMA of the next tile overlaps
+// the softmax of this one) and the HD-column output accumulator; KT = 128 keys per tile for head_dim
+// 64 / 128, 64 for 256 (shared memory).
 //
 // The query tiles with the most key tiles start first (the CTA order is reversed over query blocks).
 // Every wait is bounded; on a timeout the kernel records JX_ERR_TIMEOUT and returns.
@@ -42,19 +43,19 @@ struct PTcParams {
   int* status;
 };
 
-constexpr int kPtKT = 128;                         // keys per tile (MMA N of the scores)
 constexpr int kPtRows = 128;                       // query rows per CTA (MMA M)
 constexpr int kPtSoftWarps = 8;
 constexpr int kPtThreads = 32 * (kPtSoftWarps + 2);
-constexpr uint32_t kPtTmemCols = 512;              // scores 2 x 128 columns, output at column 256
+constexpr uint32_t kPtTmemCols = 512;              // scores 2 x KT columns, output at column 2 KT
 constexpr int kPtBlk = kPtRows * 128;              // bytes of one [128 rows][128 B] block
 
-template <int HD>
+// KT keys per tile (MMA N of the scores): 128 for head_dim 64 / 128, 64 for 256 (shared memory).
+template <int HD, int KT>
 struct PtCfg {
   static constexpr int kCB = HD / 64;                    // 64-column blocks of a head
   static constexpr int kQBytes = kCB * kPtBlk;           // Q: [kCB][128 rows][128 B]
-  static constexpr int kTileBytes = kCB * kPtKT * 128;   // one K or V tile: [kCB][128 keys][128 B]
-  static constexpr int kPBytes = 2 * kPtBlk;             // P: [2 key blocks][128 rows][128 B]
+  static constexpr int kTileBytes = kCB * KT * 128;      // one K or V tile: [kCB][KT keys][128 B]
+  static constexpr int kPBytes = (KT / 64) * kPtBlk;     // P: [KT / 64 key blocks][128 rows][128 B]
   static constexpr int kOffK = kQBytes;                  // 2 stages
   static constexpr int kOffV = kOffK + 2 * kTileBytes;   // 2 stages
   static constexpr int kOffP = kOffV + 2 * kTileBytes;
@@ -83,10 +84,10 @@ __device__ __forceinline__ uint64_t umma_desc_mnmajor_sw128(uint32_t smem_addr, 
 // Byte offset of 16-byte chunk c of row r in a swizzled [rows][128 B] block.
 __device__ __forceinline__ uint32_t sw128_off(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
 
-template <int HD>
+template <int HD, int KT>
 __global__ void __launch_bounds__(kPtThreads, 1)
     pattn_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap, PTcParams p) {
-  using C = PtCfg<HD>;
+  using C = PtCfg<HD, KT>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* qs = smem;
@@ -153,7 +154,7 @@ __global__ void __launch_bounds__(kPtThreads, 1)
   const int s_max = min(q0 + p.rph - 1, p.S - 1);
   const int j_hi = min(s_max, valid - 1);
   const int j_lo = p.window > 0 ? max(0, q0 - p.window + 1) : 0;
-  const int n = j_hi >= j_lo ? (j_hi - j_lo + kPtKT) / kPtKT : 0;   // key tiles per pass
+  const int n = j_hi >= j_lo ? (j_hi - j_lo + KT) / KT : 0;   // key tiles per pass
 
   // Q rows [head][position] (positions past S are zero) in 64-column swizzled blocks
   for (int idx = threadIdx.x; idx < kPtRows * (HD / 8); idx += kPtThreads) {
@@ -177,7 +178,7 @@ __global__ void __launch_bounds__(kPtThreads, 1)
       int issued = 0, v_issued = 0;
       for (int i = 0; i < 2 * n && !*dead; ++i) {
         const int st = i & 1, t = i < n ? i : i - n;
-        const int y = (int)(p.layer_row0 + (long long)b * p.T + j_lo + t * kPtKT);
+        const int y = (int)(p.layer_row0 + (long long)b * p.T + j_lo + t * KT);
         if (i >= 2 && !mbar_wait_bounded(&kempty[st], ((i >> 1) - 1) & 1)) {
           set_status(p.status, JX_ERR_TIMEOUT);
           *dead = 1;
@@ -186,7 +187,7 @@ __global__ void __launch_bounds__(kPtThreads, 1)
         mbar_arrive_expect_tx(&kfull[st], C::kTileBytes);
 #pragma unroll
         for (int c = 0; c < C::kCB; ++c)
-          tma_load_2d(ks + st * C::kTileBytes + c * kPtKT * 128, &kmap, kvh * HD + c * 64, y, &kfull[st]);
+          tma_load_2d(ks + st * C::kTileBytes + c * KT * 128, &kmap, kvh * HD + c * 64, y, &kfull[st]);
         issued = i + 1;
         if (i >= n) {
           const int vst = t & 1;
@@ -198,7 +199,7 @@ __global__ void __launch_bounds__(kPtThreads, 1)
           mbar_arrive_expect_tx(&vfull[vst], C::kTileBytes);
 #pragma unroll
           for (int c = 0; c < C::kCB; ++c)
-            tma_load_2d(vs + vst * C::kTileBytes + c * kPtKT * 128, &vmap, kvh * HD + c * 64, y, &vfull[vst]);
+            tma_load_2d(vs + vst * C::kTileBytes + c * KT * 128, &vmap, kvh * HD + c * 64, y, &vfull[vst]);
           v_issued = t + 1;
         }
       }
@@ -211,7 +212,7 @@ __global__ void __launch_bounds__(kPtThreads, 1)
   } else if (warp == kPtSoftWarps + 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0 && n > 0) {
-      const uint32_t idesc_s = umma_idesc_bf16_f32(kPtRows, kPtKT);
+      const uint32_t idesc_s = umma_idesc_bf16_f32(kPtRows, KT);
       const uint32_t idesc_o = umma_idesc_bf16_f32(kPtRows, HD) | (1u << 16);   // B (V) MN-major
       const uint32_t qa = smem_u32(qs);
       bool ok = true;
@@ -225,8 +226,8 @@ __global__ void __launch_bounds__(kPtThreads, 1)
 #pragma unroll
         for (int k = 0; k < HD / 16; ++k) {
           const uint32_t off = (uint32_t)((k >> 2) * kPtBlk + (k & 3) * 32);
-          const uint32_t koff = (uint32_t)((k >> 2) * kPtKT * 128 + (k & 3) * 32);
-          umma_bf16(tmem + (uint32_t)(buf * kPtKT), umma_desc_kmajor_sw128(qa + off), umma_desc_kmajor_sw128(kb + koff),
+          const uint32_t koff = (uint32_t)((k >> 2) * KT * 128 + (k & 3) * 32);
+          umma_bf16(tmem + (uint32_t)(buf * KT), umma_desc_kmajor_sw128(qa + off), umma_desc_kmajor_sw128(kb + koff),
                     idesc_s, k > 0 ? 1u : 0u);
         }
         umma_commit(&sfull[buf]);
@@ -243,10 +244,10 @@ __global__ void __launch_bounds__(kPtThreads, 1)
         tc_fence_after();
         const uint32_t pa = smem_u32(ps), vb = smem_u32(vs + vst * C::kTileBytes);
 #pragma unroll
-        for (int k = 0; k < kPtKT / 16; ++k) {
+        for (int k = 0; k < KT / 16; ++k) {
           const uint32_t aoff = (uint32_t)((k >> 2) * kPtBlk + (k & 3) * 32);
-          umma_bf16(tmem + 256u, umma_desc_kmajor_sw128(pa + aoff),
-                    umma_desc_mnmajor_sw128(vb + (uint32_t)(k * 16 * 128), (uint32_t)(kPtKT * 128)), idesc_o,
+          umma_bf16(tmem + (uint32_t)(2 * KT), umma_desc_kmajor_sw128(pa + aoff),
+                    umma_desc_mnmajor_sw128(vb + (uint32_t)(k * 16 * 128), (uint32_t)(KT * 128)), idesc_o,
                     (t > 0 || k > 0) ? 1u : 0u);
         }
         umma_commit(pempty);
@@ -267,7 +268,8 @@ __global__ void __launch_bounds__(kPtThreads, 1)
     const int hl = r / p.rph, pos = q0 + r % p.rph;
     const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16);
     bool ok = true;
-    float x[64];
+    constexpr int kCols = KT / 2;   // this thread's columns of a tile
+    float x[kCols];
     // scores of tile t (score buffer `buf`) for this thread's 64 columns, masked and rounded
     auto load_scores = [&](int i, int t) -> bool {
       const int buf = i & 1;
@@ -276,14 +278,14 @@ __global__ void __launch_bounds__(kPtThreads, 1)
       if (w) {
         tc_fence_after();
 #pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_ld16(trow + (uint32_t)(buf * kPtKT + hf * 64 + c * 16), x + c * 16);
+        for (int c = 0; c < kCols / 16; ++c) tmem_ld16(trow + (uint32_t)(buf * KT + hf * kCols + c * 16), x + c * 16);
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sempty[buf]);
-      const int jb = j_lo + t * kPtKT + hf * 64;
+      const int jb = j_lo + t * KT + hf * kCols;
 #pragma unroll
-      for (int e = 0; e < 64; ++e) {
+      for (int e = 0; e < kCols; ++e) {
         const int j = jb + e;
         bool vis = j <= pos && j < valid && j <= j_hi;
         if (p.window > 0 && j <= pos - p.window) vis = false;
@@ -298,12 +300,12 @@ __global__ void __launch_bounds__(kPtThreads, 1)
       if (!ok) break;
       float tm = -INFINITY;
 #pragma unroll
-      for (int e = 0; e < 64; ++e) tm = fmaxf(tm, x[e]);
+      for (int e = 0; e < kCols; ++e) tm = fmaxf(tm, x[e]);
       const float mn = fmaxf(m, tm);
       if (mn != -INFINITY) {
         float ts = 0.f;
 #pragma unroll
-        for (int e = 0; e < 64; ++e)
+        for (int e = 0; e < kCols; ++e)
           if (x[e] != -INFINITY) ts += expf(x[e] - mn);
         l = (m == -INFINITY ? 0.f : l * expf(m - mn)) + ts;
         m = mn;
@@ -322,9 +324,9 @@ __global__ void __launch_bounds__(kPtThreads, 1)
     for (int t = 0; t < n && ok; ++t) {
       ok = load_scores(n + t, t);
       if (!ok) break;
-      uint32_t pk[32];
+      uint32_t pk[kCols / 2];
 #pragma unroll
-      for (int e = 0; e < 64; e += 2) {
+      for (int e = 0; e < kCols; e += 2) {
         const float a = x[e] == -INFINITY ? 0.f : rnd<bf16>(expf(x[e] - m) / l);
         const float c = x[e + 1] == -INFINITY ? 0.f : rnd<bf16>(expf(x[e + 1] - m) / l);
         pk[e >> 1] = pack_bf16x2(a, c);
@@ -336,27 +338,42 @@ __global__ void __launch_bounds__(kPtThreads, 1)
           break;
         }
       }
-      uint8_t* prow = ps + hf * kPtBlk;
 #pragma unroll
-      for (int c = 0; c < 8; ++c)
-        *reinterpret_cast<uint4*>(prow + sw128_off(r, c)) =
+      for (int c = 0; c < kCols / 8; ++c) {
+        const int kk = hf * kCols + 8 * c;   // first key of the chunk within the tile
+        *reinterpret_cast<uint4*>(ps + (kk >> 6) * kPtBlk + sw128_off(r, (kk & 63) >> 3)) =
             make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+      }
       fence_proxy_async();   // generic-proxy writes of P, read by the tensor core
       __syncwarp();
       if (lane == 0) mbar_arrive(pfull);
     }
-    // output accumulator: this thread's row, columns hf * HD / 2 .. + HD / 2
+    // output accumulator: this thread's row, columns hf * HD / 2 .. + HD / 2, read and stored 16 at a time
     constexpr int kHalf = HD / 2;
-    float o[kHalf];
-    bool have_o = false;
     if (ok && n > 0) {
       bool w = mbar_wait_bounded(ofull, 0);
       w = __all_sync(0xffffffffu, w);
       if (w) {
         tc_fence_after();
+        const bool store = pos < p.S && m != -INFINITY;
+        const long long orow = (long long)b * p.S + pos;
+        const long long col0 = (long long)(h0 + hl) * HD + hf * kHalf;
 #pragma unroll
-        for (int c = 0; c < kHalf / 16; ++c) tmem_ld16(trow + (uint32_t)(256 + hf * kHalf + c * 16), o + c * 16);
-        have_o = true;
+        for (int c = 0; c < kHalf / 16; ++c) {
+          float o[16];
+          tmem_ld16(trow + (uint32_t)(2 * KT + hf * kHalf + c * 16), o);   // warp-wide: every lane loads
+          if (store) {
+#pragma unroll
+            for (int h2 = 0; h2 < 2; ++h2) {
+              uint4 v;
+              v.x = pack_bf16x2(o[8 * h2], o[8 * h2 + 1]);
+              v.y = pack_bf16x2(o[8 * h2 + 2], o[8 * h2 + 3]);
+              v.z = pack_bf16x2(o[8 * h2 + 4], o[8 * h2 + 5]);
+              v.w = pack_bf16x2(o[8 * h2 + 6], o[8 * h2 + 7]);
+              *reinterpret_cast<uint4*>(p.out + k128_offset(orow, col0 + 16 * c + 8 * h2, p.out_rp)) = v;
+            }
+          }
+        }
       } else {
         ok = false;
       }
@@ -368,23 +385,7 @@ __global__ void __launch_bounds__(kPtThreads, 1)
       set_status(p.status, JX_ERR_TIMEOUT);
       *dead = 1;
     }
-    if (pos < p.S) {
-      if (m == -INFINITY) {
-        if (hf == 0) dead_rows[r] = 1;
-      } else if (have_o) {
-        const long long orow = (long long)b * p.S + pos;
-        const long long col0 = (long long)(h0 + hl) * HD + hf * kHalf;
-#pragma unroll
-        for (int c = 0; c < kHalf / 8; ++c) {
-          uint4 v;
-          v.x = pack_bf16x2(o[8 * c], o[8 * c + 1]);
-          v.y = pack_bf16x2(o[8 * c + 2], o[8 * c + 3]);
-          v.z = pack_bf16x2(o[8 * c + 4], o[8 * c + 5]);
-          v.w = pack_bf16x2(o[8 * c + 6], o[8 * c + 7]);
-          *reinterpret_cast<uint4*>(p.out + k128_offset(orow, col0 + 8 * c, p.out_rp)) = v;
-        }
-      }
-    }
+    if (pos < p.S && m == -INFINITY && hf == 0) dead_rows[r] = 1;
     // rows with no visible key: uniform weights bf16(1/Tu) over the first Tu slots of the buffer
     named_bar_sync(1, 32 * kPtSoftWarps);
     if (ok) {
@@ -418,35 +419,35 @@ __global__ void __launch_bounds__(kPtThreads, 1)
 // ------------------------------------------------------------------------------------------------
 // host side
 // ------------------------------------------------------------------------------------------------
-template <int HD>
+template <int HD, int KT>
 static int launch_pattn_tc(const jx_pattn_args& a, const PTcParams& p, bool pdl, cudaStream_t s) {
   CUtensorMap km, vm;
   const long long cols = (long long)a.Hkv * HD;
-  int rc = make_tmap_2d_bf16_box(&km, a.k_base, a.cache_rows, cols, cols, kPtKT);
-  if (rc == JX_OK) rc = make_tmap_2d_bf16_box(&vm, a.v_base, a.cache_rows, cols, cols, kPtKT);
+  int rc = make_tmap_2d_bf16_box(&km, a.k_base, a.cache_rows, cols, cols, KT);
+  if (rc == JX_OK) rc = make_tmap_2d_bf16_box(&vm, a.v_base, a.cache_rows, cols, cols, KT);
   if (rc != JX_OK) return rc;
   static bool configured = false;
   if (!configured) {
-    if (cudaFuncSetAttribute(pattn_tc_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, PtCfg<HD>::kSmem) !=
-        cudaSuccess)
+    if (cudaFuncSetAttribute(pattn_tc_kernel<HD, KT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             PtCfg<HD, KT>::kSmem) != cudaSuccess)
       return JX_ERR_CUDA;
     configured = true;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((a.S + p.rph - 1) / p.rph, a.Hq / p.hpt, a.B);
   cfg.blockDim = dim3(kPtThreads);
-  cfg.dynamicSmemBytes = PtCfg<HD>::kSmem;
+  cfg.dynamicSmemBytes = PtCfg<HD, KT>::kSmem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return launch_ex(&cfg, pattn_tc_kernel<HD>, km, vm, p) == cudaSuccess ? JX_OK : JX_ERR_CUDA;
+  return launch_ex(&cfg, pattn_tc_kernel<HD, KT>, km, vm, p) == cudaSuccess ? JX_OK : JX_ERR_CUDA;
 }
 
 bool prefill_attention_tc_supported(const jx_pattn_args& a) {
-  return (a.hd == 64 || a.hd == 128) && a.Hkv > 0 && a.Hq % a.Hkv == 0 && a.S > 0 && a.S <= a.T && a.B > 0 &&
+  return (a.hd == 64 || a.hd == 128 || a.hd == 256) && a.Hkv > 0 && a.Hq % a.Hkv == 0 && a.S > 0 && a.S <= a.T && a.B > 0 &&
          a.B <= 65535 && a.Hq <= 65535 && (reinterpret_cast<uintptr_t>(a.q) & 15) == 0 && a.out_rp > 0;
 }
 
@@ -472,7 +473,9 @@ int run_prefill_attention_tc(const jx_pattn_args& a, bool pdl, cudaStream_t stre
   p.out = reinterpret_cast<bf16*>(a.out);
   p.out_rp = a.out_rp;
   p.status = a.status;
-  return a.hd == 64 ? launch_pattn_tc<64>(a, p, pdl, stream) : launch_pattn_tc<128>(a, p, pdl, stream);
+  if (a.hd == 64) return launch_pattn_tc<64, 128>(a, p, pdl, stream);
+  if (a.hd == 128) return launch_pattn_tc<128, 128>(a, p, pdl, stream);
+  return launch_pattn_tc<256, 64>(a, p, pdl, stream);
 }
 
 }  // namespace jxb

@@ -134,7 +134,7 @@ def test_filter_logits_checks_its_arguments_before_any_launch():
 
 
 def test_tensor_core_prefill_attention_refuses_unsupported_shapes_before_any_launch():
-    """With the tcgen05 prefill attention selected, head sizes other than 64 / 128, a row-major output,
+    """With the tcgen05 prefill attention selected, head sizes other than 64 / 128 / 256, a row-major output,
     S > T or Hq % Hkv != 0 fail with JX_ERR_SHAPE before any device work (the pointers are never
     dereferenced)."""
     lib = N.load()
@@ -146,7 +146,7 @@ def test_tensor_core_prefill_attention_refuses_unsupported_shapes_before_any_lau
     a.len_add, a.scale, a.out_rp = 1, 128 ** -0.5, 128
     assert lib.jx_set_prefill_attention_impl(2) == N.JX_OK
     try:
-        for field, value in (("hd", 256), ("hd", 96), ("out_rp", 0), ("S", 200), ("Hkv", 3)):
+        for field, value in (("hd", 32), ("hd", 96), ("out_rp", 0), ("S", 200), ("Hkv", 3)):
             saved = getattr(a, field)
             setattr(a, field, value)
             assert lib.jx_prefill_attention(a, 0, None) == N.JX_ERR_SHAPE, field
