@@ -1,6 +1,6 @@
 """CPU tests of bench.py's host side: the algorithmic bytes of a decode step, the clock-record summary
-and the reference arm's JSON line (the oracle timed on the host cores), which the round-end driver
-parses."""
+and the reference arm's JSON line (the oracle timed on the host cores), whose keys are the bench
+contract."""
 import json
 import os
 import subprocess
