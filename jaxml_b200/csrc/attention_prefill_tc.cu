@@ -64,6 +64,12 @@ struct PtCfg {
   static constexpr int kNBar = 17;
   static constexpr int kOffMisc = kOffBar + kNBar * 8;   // tmem slot, dead flag, dead rows [128]
   static constexpr int kSmem = 1024 + kOffMisc + 16 + kPtRows * 4;
+  static_assert(HD % 64 == 0 && KT % 64 == 0 && KT <= 256, "64-column blocks, at most a 256-row TMA box");
+  static_assert(kOffK % 1024 == 0 && kOffV % 1024 == 0 && kOffP % 1024 == 0 && kTileBytes % 1024 == 0,
+                "swizzled operand blocks start on 1024-byte boundaries");
+  static_assert(2 * KT + HD <= (int)kPtTmemCols, "two score buffers and the output fit the TMEM allocation");
+  static_assert(kSmem <= 227 * 1024, "shared memory per CTA");
+  static_assert(HD <= 256 && KT <= 256, "MMA N <= 256");
 };
 
 // Shared-memory descriptor of a K-major operand in 128-byte-swizzled [rows][128 B] blocks: 8-row groups
