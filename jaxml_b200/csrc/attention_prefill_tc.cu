@@ -8,9 +8,9 @@
 //
 // One CTA per (query block, head set, batch row): its 128 query rows are HPT heads x RPH positions
 // (rows [head][position]; HPT = 4, 2 or 1, the largest that divides the heads per KV head, RPH =
-// 128 / HPT), so the HPT heads share every K / V tile.  Warps: 0..7 softmax (warp w reads TMEM lane
-// quadrant w % 4, i.e. rows 32 (w % 4) .. +31, and columns half w / 4 of each tile), 8 the TMA producer,
-// 9 the MMA issuer (and TMEM owner).  Shared memory holds every operand as 64-column blocks of
+// 128 / HPT), so the HPT heads share every K / V tile.  Warps: 0..15 softmax (warp w reads TMEM lane
+// quadrant w % 4, i.e. rows 32 (w % 4) .. +31, and column group w / 4, a quarter of each tile), 16 the
+// TMA producer, 17 the MMA issuer (and TMEM owner).  Shared memory holds every operand as 64-column blocks of
 // [rows][128 bytes] with the 128-byte swizzle (16-byte chunk c of row r at chunk c ^ (r % 8)), the
 // layout the K / V tensor maps produce: Q and P (written by threads) and K are K-major operands, V is
 // the MN-major B operand of P.V.  TMEM: two KT-column score buffers (the MMA of the next tile overlaps
@@ -44,7 +44,8 @@ struct PTcParams {
 };
 
 constexpr int kPtRows = 128;                       // query rows per CTA (MMA M)
-constexpr int kPtSoftWarps = 8;
+constexpr int kPtSoftWarps = 16;                   // 4 per TMEM lane quadrant
+constexpr int kPtGroups = kPtSoftWarps / 4;        // column groups of a row (one warp of each quadrant)
 constexpr int kPtThreads = 32 * (kPtSoftWarps + 2);
 constexpr uint32_t kPtTmemCols = 512;              // scores 2 x KT columns, output at column 2 KT
 constexpr int kPtBlk = kPtRows * 128;              // bytes of one [128 rows][128 B] block
@@ -59,8 +60,8 @@ struct PtCfg {
   static constexpr int kOffK = kQBytes;                  // 2 stages
   static constexpr int kOffV = kOffK + 2 * kTileBytes;   // 2 stages
   static constexpr int kOffP = kOffV + 2 * kTileBytes;
-  static constexpr int kOffStat = kOffP + kPBytes;       // float m[2][128], l[2][128]
-  static constexpr int kOffBar = kOffStat + 4 * kPtRows * 4;
+  static constexpr int kOffStat = kOffP + kPBytes;       // float m[kPtGroups][128], l[kPtGroups][128]
+  static constexpr int kOffBar = kOffStat + 2 * kPtGroups * kPtRows * 4;
   static constexpr int kNBar = 17;
   static constexpr int kOffMisc = kOffBar + kNBar * 8;   // tmem slot, dead flag, dead rows [128]
   static constexpr int kSmem = 1024 + kOffMisc + 16 + kPtRows * 4;
@@ -70,6 +71,7 @@ struct PtCfg {
   static_assert(2 * KT + HD <= (int)kPtTmemCols, "two score buffers and the output fit the TMEM allocation");
   static_assert(kSmem <= 227 * 1024, "shared memory per CTA");
   static_assert(HD <= 256 && KT <= 256, "MMA N <= 256");
+  static_assert((KT / kPtGroups) % 16 == 0 && (HD / kPtGroups) % 16 == 0, "16-column TMEM loads per group");
 };
 
 // Shared-memory descriptor of a K-major operand in 128-byte-swizzled [rows][128 B] blocks: 8-row groups
@@ -100,7 +102,7 @@ __global__ void __launch_bounds__(kPtThreads, 1)
   uint8_t* ks = smem + C::kOffK;
   uint8_t* vs = smem + C::kOffV;
   uint8_t* ps = smem + C::kOffP;
-  float* stat = reinterpret_cast<float*>(smem + C::kOffStat);   // m[2][128], l[2][128]
+  float* stat = reinterpret_cast<float*>(smem + C::kOffStat);   // m[kPtGroups][128], l[kPtGroups][128]
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem + C::kOffBar);
   uint64_t* kfull = bar;
   uint64_t* kempty = bar + 2;
@@ -268,13 +270,13 @@ __global__ void __launch_bounds__(kPtThreads, 1)
       umma_commit(fin);
     }
   } else {
-    // ---------------- softmax warps: row r = 32 (warp % 4) + lane, columns half hf ----------------
-    const int quad = warp & 3, hf = warp >> 2;
+    // ------------- softmax warps: row r = 32 (warp % 4) + lane, column group cg = warp / 4 -------------
+    const int quad = warp & 3, cg = warp >> 2;
     const int r = quad * 32 + lane;
     const int hl = r / p.rph, pos = q0 + r % p.rph;
     const uint32_t trow = tmem + ((uint32_t)(quad * 32) << 16);
     bool ok = true;
-    constexpr int kCols = KT / 2;   // this thread's columns of a tile
+    constexpr int kCols = KT / kPtGroups;   // this thread's columns of a tile
     float x[kCols];
     // scores of tile t (score buffer `buf`) for this thread's 64 columns, masked and rounded
     auto load_scores = [&](int i, int t) -> bool {
@@ -284,12 +286,12 @@ __global__ void __launch_bounds__(kPtThreads, 1)
       if (w) {
         tc_fence_after();
 #pragma unroll
-        for (int c = 0; c < kCols / 16; ++c) tmem_ld16(trow + (uint32_t)(buf * KT + hf * kCols + c * 16), x + c * 16);
+        for (int c = 0; c < kCols / 16; ++c) tmem_ld16(trow + (uint32_t)(buf * KT + cg * kCols + c * 16), x + c * 16);
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&sempty[buf]);
-      const int jb = j_lo + t * KT + hf * kCols;
+      const int jb = j_lo + t * KT + cg * kCols;
 #pragma unroll
       for (int e = 0; e < kCols; ++e) {
         const int j = jb + e;
@@ -299,7 +301,7 @@ __global__ void __launch_bounds__(kPtThreads, 1)
       }
       return w;
     };
-    // pass 1: online max / exp-sum of this half of the row
+    // pass 1: online max / exp-sum of this column group of the row
     float m = -INFINITY, l = 0.f;
     for (int t = 0; t < n && ok; ++t) {
       ok = load_scores(t, t);
@@ -317,14 +319,19 @@ __global__ void __launch_bounds__(kPtThreads, 1)
         m = mn;
       }
     }
-    // the two halves of the row: final max and exp-sum (every half-pair computes the same values)
-    stat[hf * kPtRows + r] = m;
-    stat[2 * kPtRows + hf * kPtRows + r] = l;
+    // the column groups of the row: final max and exp-sum, combined in group order (every group of the
+    // row computes the same values)
+    stat[cg * kPtRows + r] = m;
+    stat[(kPtGroups + cg) * kPtRows + r] = l;
     named_bar_sync(1, 32 * kPtSoftWarps);
-    {
-      const float m0 = stat[r], m1 = stat[kPtRows + r], l0 = stat[2 * kPtRows + r], l1 = stat[3 * kPtRows + r];
-      m = fmaxf(m0, m1);
-      l = (m0 == -INFINITY ? 0.f : l0 * expf(m0 - m)) + (m1 == -INFINITY ? 0.f : l1 * expf(m1 - m));
+    m = -INFINITY;
+#pragma unroll
+    for (int g = 0; g < kPtGroups; ++g) m = fmaxf(m, stat[g * kPtRows + r]);
+    l = 0.f;
+#pragma unroll
+    for (int g = 0; g < kPtGroups; ++g) {
+      const float mg = stat[g * kPtRows + r];
+      l += mg == -INFINITY ? 0.f : stat[(kPtGroups + g) * kPtRows + r] * expf(mg - m);
     }
     // pass 2: probabilities rounded as the reference does, into P for the P.V MMA
     for (int t = 0; t < n && ok; ++t) {
@@ -346,7 +353,7 @@ __global__ void __launch_bounds__(kPtThreads, 1)
       }
 #pragma unroll
       for (int c = 0; c < kCols / 8; ++c) {
-        const int kk = hf * kCols + 8 * c;   // first key of the chunk within the tile
+        const int kk = cg * kCols + 8 * c;   // first key of the chunk within the tile
         *reinterpret_cast<uint4*>(ps + (kk >> 6) * kPtBlk + sw128_off(r, (kk & 63) >> 3)) =
             make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
       }
@@ -354,8 +361,8 @@ __global__ void __launch_bounds__(kPtThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(pfull);
     }
-    // output accumulator: this thread's row, columns hf * HD / 2 .. + HD / 2, read and stored 16 at a time
-    constexpr int kHalf = HD / 2;
+    // output accumulator: this thread's row, columns cg * HD / kPtGroups .., read and stored 16 at a time
+    constexpr int kHalf = HD / kPtGroups;
     if (ok && n > 0) {
       bool w = mbar_wait_bounded(ofull, 0);
       w = __all_sync(0xffffffffu, w);
@@ -363,11 +370,11 @@ __global__ void __launch_bounds__(kPtThreads, 1)
         tc_fence_after();
         const bool store = pos < p.S && m != -INFINITY;
         const long long orow = (long long)b * p.S + pos;
-        const long long col0 = (long long)(h0 + hl) * HD + hf * kHalf;
+        const long long col0 = (long long)(h0 + hl) * HD + cg * kHalf;
 #pragma unroll
         for (int c = 0; c < kHalf / 16; ++c) {
           float o[16];
-          tmem_ld16(trow + (uint32_t)(2 * KT + hf * kHalf + c * 16), o);   // warp-wide: every lane loads
+          tmem_ld16(trow + (uint32_t)(2 * KT + cg * kHalf + c * 16), o);   // warp-wide: every lane loads
           if (store) {
 #pragma unroll
             for (int h2 = 0; h2 < 2; ++h2) {
@@ -391,7 +398,7 @@ __global__ void __launch_bounds__(kPtThreads, 1)
       set_status(p.status, JX_ERR_TIMEOUT);
       *dead = 1;
     }
-    if (pos < p.S && m == -INFINITY && hf == 0) dead_rows[r] = 1;
+    if (pos < p.S && m == -INFINITY && cg == 0) dead_rows[r] = 1;
     // rows with no visible key: uniform weights bf16(1/Tu) over the first Tu slots of the buffer
     named_bar_sync(1, 32 * kPtSoftWarps);
     if (ok) {
